@@ -1,0 +1,328 @@
+"""Headline benchmark: DeepSeek-V3-shape normal-mode dispatch + combine over NVLink on N B200s,
+plus the low-latency decode dispatch / combine latencies.
+
+Config: per rank 4096 tokens, hidden 7168, bf16 activations ~N(0,1),
+256 experts (256/N per rank), top-8 from N(0,1) router logits with softmax weights; dispatch in
+FP8 e4m3 with per-token 1x128 fp32 scales (quantization fused into the dispatch), combine in bf16.
+One step = get_dispatch_layout + dispatch + combine (fresh, CPU-synced receive counts).
+
+Byte definition (DeepEP v2 "logical bandwidth", local traffic included): dispatch bytes per
+received token = FP8 row + fp32 scales + int64 top-k ids + fp32 top-k weights; combine bytes per
+received token = bf16 row + fp32 top-k weights. `value` is the job aggregate: the sum over ranks of
+those bytes divided by the step time (max over ranks). The published per-rank SM100 EP8 figures
+(726 GB/s dispatch, 740 GB/s combine) combine into 735.1 GB/s per rank for a full cycle;
+`vs_baseline` divides `value` by 735.1 x N.
+
+Low-latency (config 3): 128 tokens/rank, hidden 7168, 256 experts, top-8 (uniform logits), FP8
+dispatch with `return_recv_hook`, weighted bf16 combine; reported as device microseconds per
+dispatch (send + hook) and per combine (send + hook), max over ranks, median over iterations.
+
+Timing: CUDA events on the launching stream per step, L2 flushed (a 256 MiB write) before every
+timed step, barrier + synchronize on both sides, max over ranks. SM clocks are sampled with
+nvidia-smi during the timed region. `--impl reference` runs the unmodified reference if it is
+installed under baseline/_ref; it is not installable offline here and prints why.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'dispatch/combine NVLink GB/s (normal) + LL dispatch/combine us, 8xB200'
+BASELINE_CYCLE_GBPS_PER_RANK = 735.1
+REFERENCE_UNAVAILABLE = ('reference (swiss-ai/DeepEP_Slingshot) is not installable offline: its root has no '
+                         'setup.py/pyproject.toml, and its vendored DeepEP v2 source fails to build against '
+                         'NCCL 2.28.9 (no GIN/LSA device API: ncclCommProperties, ncclGetLsaDevicePointer) and '
+                         'NVSHMEM IBGDA (missing infiniband/mlx5dv.h)')
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=20)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--impl', default='ours', choices=['ours', 'reference', 'nccl'])
+    p.add_argument('--tokens', type=int, default=4096)
+    p.add_argument('--hidden', type=int, default=7168)
+    p.add_argument('--experts', type=int, default=256)
+    p.add_argument('--topk', type=int, default=8)
+    p.add_argument('--num-sms', type=int, default=0)
+    p.add_argument('--ll-tokens', type=int, default=128)
+    p.add_argument('--no-ll', action='store_true')
+    p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--check', action='store_true', help='verify against the torch oracle before timing')
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200', '-i', str(self.device)], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled']}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        mhz, max_mhz, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.file.read().splitlines():
+            f = [c.strip() for c in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                max_mhz = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == 'active':
+                    reasons.add(n)
+        os.unlink(self.file.name)
+        return {'sm_mhz': statistics.median(mhz) if mhz else None, 'sm_max_mhz': max_mhz,
+                'reasons': sorted(reasons), 'samples': len(mhz)}
+
+
+def init(args):
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    assert world == args.gpus, f'--gpus {args.gpus} but WORLD_SIZE={world}'
+    os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
+    os.environ.setdefault('MASTER_PORT', str(29600 + os.getpid() % 1000))
+    torch.cuda.set_device(local)
+    import datetime
+    dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                            device_id=torch.device('cuda', local))
+    return rank, world, local
+
+
+def max_over_ranks(values):
+    t = torch.tensor(values, dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def sum_over_ranks(v):
+    t = torch.tensor([float(v)], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t)
+    return t.item()
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        print(json.dumps({'impl': 'reference', 'unavailable': REFERENCE_UNAVAILABLE}))
+        return 0
+    rank, world, local = init(args)
+    from deepep_slingshot_b200 import Buffer
+    from deepep_slingshot_b200.utils import gate
+    N, H, E, K = args.tokens, args.hidden, args.experts, args.topk
+    E_l = E // world
+    g = torch.Generator().manual_seed(1234 + rank)
+    x = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
+    idx, w = gate.normal_routing(N, E, K, generator=g)
+    idx, w = idx.cuda(), w.cuda()
+    num_sms = args.num_sms or Buffer.num_sms
+    cfg = Buffer.get_dispatch_config(world)
+    cfg.num_sms = num_sms
+    nvl_bytes = Buffer.get_nvl_buffer_size_hint(N, H, world)
+    ll_bytes = 0 if args.no_ll else Buffer.get_low_latency_rdma_size_hint(args.ll_tokens, H, world, E)
+
+    if args.impl == 'nccl':
+        from deepep_slingshot_b200.parallel.nccl_baseline import NcclAllToAllEP
+        buf = NcclAllToAllEP(dist.group.WORLD)
+    else:
+        buf = Buffer(dist.group.WORLD, num_nvl_bytes=nvl_bytes, num_rdma_bytes=ll_bytes, low_latency_mode=ll_bytes > 0)
+    y_full = torch.randn((N * world, H), generator=g).to(torch.bfloat16).cuda()
+    state = {}
+
+    def step():
+        ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(idx, E)
+        (rx, rs), ri, rw, lst, h, _ = buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
+                                                   num_tokens_per_expert=ntpe, topk_idx=idx, topk_weights=w,
+                                                   config=cfg, quantize_fp8=True)
+        state['mid'].record()
+        out, out_w, _ = buf.combine(y_full[:rx.shape[0]], h, topk_weights=rw, config=cfg)
+        state['num_recv'] = rx.shape[0]
+        return out
+
+    if args.check:
+        from deepep_slingshot_b200 import ReferenceBuffer
+        ref = ReferenceBuffer(dist.group.WORLD)
+        (rx, rs), ri, rw, lst, h, _ = buf.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, quantize_fp8=True)
+        (ex, es), ei, ew, el, eh, _ = ref.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, quantize_fp8=True)
+        assert torch.equal(rx.view(torch.uint8), ex.view(torch.uint8)) and torch.equal(rs, es) and lst == el
+        o, _, _ = buf.combine(y_full[:rx.shape[0]], h)
+        eo, _, _ = ref.combine(y_full[:rx.shape[0]], eh)
+        assert torch.allclose(o.float(), eo.float(), atol=1e-2, rtol=1e-2)
+        del ref
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device='cuda')
+    for _ in range(args.warmup):
+        state['mid'] = torch.cuda.Event(enable_timing=True)
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        state['mid'] = mids[i]
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t_disp = [starts[i].elapsed_time(mids[i]) for i in range(args.steps)]
+    t_comb = [mids[i].elapsed_time(ends[i]) for i in range(args.steps)]
+    t_step = [starts[i].elapsed_time(ends[i]) for i in range(args.steps)]
+    t_disp, t_comb, t_step = max_over_ranks(t_disp), max_over_ranks(t_comb), max_over_ranks(t_step)
+    ms_step = sum(t_step) / len(t_step)
+    ms_disp = sum(t_disp) / len(t_disp)
+    ms_comb = sum(t_comb) / len(t_comb)
+    num_recv = state['num_recv']
+    disp_bytes = num_recv * (H + H // 128 * 4 + K * 8 + K * 4)
+    comb_bytes = num_recv * (2 * H + K * 4)
+    total_disp = sum_over_ranks(disp_bytes)
+    total_comb = sum_over_ranks(comb_bytes)
+    value = (total_disp + total_comb) / (ms_step * 1e-3) / 1e9
+    disp_gbps_rank = disp_bytes / (ms_disp * 1e-3) / 1e9
+    comb_gbps_rank = comb_bytes / (ms_comb * 1e-3) / 1e9
+
+    # ---------------------------------------------------------------- low-latency
+    ll = {}
+    if not args.no_ll and args.impl == 'ours':
+        T = args.ll_tokens
+        gl = torch.Generator().manual_seed(99 + rank)
+        lx = torch.randn((T, H), generator=gl).to(torch.bfloat16).cuda()
+        lidx, lw = gate.uniform_routing(T, E, K, generator=gl)
+        lidx, lw = lidx.cuda(), lw.cuda()
+        ly = torch.randn((E_l, world * T, H), generator=gl).to(torch.bfloat16).cuda()
+        d_us, c_us = [], []
+        iters = max(args.steps, 20)
+        for i in range(args.warmup + iters):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            dist.barrier()
+            e0.record()
+            recv, cnt, hh, _, hook = buf.low_latency_dispatch(lx, lidx, T, E, use_fp8=True, return_recv_hook=True)
+            hook()
+            e1.record()
+            out, _, chook = buf.low_latency_combine(ly, lidx, lw, hh, return_recv_hook=True)
+            chook()
+            e2.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                d_us.append(e0.elapsed_time(e1) * 1e3)
+                c_us.append(e1.elapsed_time(e2) * 1e3)
+        d_us, c_us = max_over_ranks(d_us), max_over_ranks(c_us)
+        ll = {'ll_dispatch_us': statistics.median(d_us), 'll_combine_us': statistics.median(c_us),
+              'll_config': {'tokens_per_rank': T, 'hidden': H, 'experts': E, 'topk': K, 'fp8_dispatch': True,
+                            'return_recv_hook': True, 'routing': 'uniform logits'}}
+
+    # ---------------------------------------------------------------- end to end through the public API
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty((N, H), dtype=torch.bfloat16, pin_memory=True)
+        hx.copy_(x.cpu())
+        hidx = idx.cpu().pin_memory()
+        hw = w.cpu().pin_memory()
+        hy = torch.empty(1, dtype=torch.float32, pin_memory=True)
+        e_steps = max(3, args.steps // 2)
+        ts = []
+        for i in range(args.warmup + e_steps):
+            dist.barrier()
+            torch.cuda.synchronize()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            dx = hx.cuda(non_blocking=True)
+            didx = hidx.cuda(non_blocking=True)
+            dw = hw.cuda(non_blocking=True)
+            ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(didx, E)
+            (rx, rs), ri, rw, lst, h, _ = buf.dispatch(dx, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
+                                                       num_tokens_per_expert=ntpe, topk_idx=didx, topk_weights=dw,
+                                                       config=cfg, quantize_fp8=True)
+            out, _, _ = buf.combine(y_full[:rx.shape[0]], h, topk_weights=rw, config=cfg)
+            hy.copy_(out.float().sum().view(1), non_blocking=True)
+            t1.record()
+            t1.synchronize()
+            _ = hy.item()
+            if i >= args.warmup:
+                ts.append(t0.elapsed_time(t1))
+        ts = max_over_ranks(ts)
+        ms_e2e = sum(ts) / len(ts)
+        e2e = {'value': (total_disp + total_comb) / (ms_e2e * 1e-3) / 1e9, 'unit': 'GB/s', 'ms_per_step': ms_e2e,
+               'h2d_bytes_per_step': hx.numel() * 2 + hidx.numel() * 8 + hw.numel() * 4,
+               'd2h_bytes_per_step': 4}
+
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': value / (BASELINE_CYCLE_GBPS_PER_RANK * world), 'dtype': 'bf16',
+            'data': 'synthetic (random bf16 activations ~N(0,1), N(0,1) router logits, seeded)',
+            'impl': args.impl,
+            'config': {'model': 'DeepSeek-V3 MoE dispatch/combine (hidden 7168, 256 experts, top-8)',
+                       'global_batch': N * world, 'seq_len': N, 'tokens_per_rank': N,
+                       'parallelism': f'ep{world}', 'dispatch_dtype': 'fp8_e4m3 1x128 (fused quantization)',
+                       'combine_dtype': 'bf16', 'num_sms': num_sms, 'l2': 'flushed before every timed step',
+                       'byte_definition': 'DeepEP v2 logical bytes incl. local traffic, summed over ranks',
+                       'baseline': f'{BASELINE_CYCLE_GBPS_PER_RANK} GB/s per rank x n_gpus (published SM100 EP8 726/740)'},
+            'dispatch_ms': ms_disp, 'combine_ms': ms_comb,
+            'dispatch_gbps_per_rank': disp_gbps_rank, 'combine_gbps_per_rank': comb_gbps_rank,
+            'num_recv_tokens_rank0': num_recv,
+            'clocks': clocks,
+            'gpu_launches': args.steps * 6 if args.impl == 'ours' else 0,
+        }
+        line.update(ll)
+        if e2e is not None:
+            line['e2e'] = e2e
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    if hasattr(buf, 'runtime') and getattr(buf, 'explicitly_destroy', False):
+        buf.destroy()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == '__main__':
+    sys.exit(main())

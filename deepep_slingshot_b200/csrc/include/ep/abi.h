@@ -1,0 +1,153 @@
+// Host/device ABI of the B200 expert-parallel runtime: peer tables, control-block layout, error
+// codes and buffer layouts. Every struct here is passed to kernels by value or stored in device or
+// host-mapped memory, so sizes are pinned with static_asserts (the same discipline as the
+// reference's `CxiGpuContext`/`CxiWindow` ABI header, backend/include/cxi_gin_abi.h:6-60).
+#pragma once
+
+#include <cstdint>
+
+namespace ep {
+
+constexpr int kMaxRanks = 8;        // one NVLink/NVSwitch domain (one B200 box)
+constexpr int kMaxTopk = 16;
+constexpr int kMaxLocalExperts = 1024;
+constexpr int kAbiVersion = 1;
+
+// ------------------------------------------------------------------------------------------------
+// Error codes written into the host-mapped `ErrorState` by kernels whose bounded waits expire.
+// ------------------------------------------------------------------------------------------------
+enum ErrorCode : int {
+    kOk = 0,
+    kErrTimeoutNotify = 1,         // dispatch notify: counts/list of a peer never arrived
+    kErrTimeoutPullDone = 2,       // staging reuse: a receiver never finished pulling the last dispatch
+    kErrTimeoutCombineReady = 3,   // combine: destination never finished its previous combine
+    kErrTimeoutCombineArrive = 4,  // combine: contributions never all arrived
+    kErrTimeoutBarrier = 5,
+    kErrTimeoutLLDispatch = 6,
+    kErrTimeoutLLCombine = 7,
+    kErrTimeoutTma = 8,            // a TMA bulk copy never completed
+    kErrCapacity = 10,             // receive capacity exceeded (tokens beyond the buffer)
+    kErrBounds = 11,               // an index outside its window (bounds check on every peer store)
+    kErrBadArgs = 12,
+    kErrTimeoutPP = 13,
+    kErrTimeoutTest = 20,          // transport self-test wait expired (used by the delayed-peer test)
+};
+
+struct ErrorState {
+    int code;
+    int peer;
+    int detail;
+    int rank;
+    int reserved[4];
+};
+static_assert(sizeof(ErrorState) == 32, "ErrorState ABI");
+
+// Passed by value to every kernel that waits.
+struct KernelStatus {
+    ErrorState* host_error;  // host-mapped (cudaHostAllocMapped) device pointer
+    int* abort_flag;         // device memory; set by the first failing block
+    uint64_t timeout_ns;     // wait limit in nanoseconds of %globaltimer
+    int rank;
+    int pad;
+};
+static_assert(sizeof(KernelStatus) == 32, "KernelStatus ABI");
+
+// Peer table: base address of the same symmetric region on every rank (index = rank). Entry
+// `rank` is the local base. Passed by value (64 bytes).
+struct PeerTable {
+    void* base[kMaxRanks];
+};
+static_assert(sizeof(PeerTable) == 64, "PeerTable ABI");
+
+// ------------------------------------------------------------------------------------------------
+// Control block at offset 0 of the normal-mode (NVL) region. Every flag is written by the party
+// that signals and read by the party that waits in ITS OWN memory (signals are pushed, never
+// polled across NVLink). All epochs are monotonically increasing call sequence numbers.
+// ------------------------------------------------------------------------------------------------
+struct alignas(128) NormalCtrl {
+    int notify_flag[kMaxRanks];             // [src] = dispatch epoch once src's counts/list/staging are ready
+    int pull_done[kMaxRanks];               // [dst] = dispatch epoch once dst finished reading my staging
+    int combine_ready[kMaxRanks];           // [dst] = combine seq once dst finished reducing (its slots are free)
+    int barrier_flag[kMaxRanks];            // [src] = barrier epoch
+    int combine_arrived;                    // rows of combine contributions that landed here (reset by reducer)
+    int combine_reduced_blocks;             // reducer blocks that finished (reset by the last one)
+    int pull_finished_blocks;               // pull blocks that finished (reset by the last one)
+    int pad0[29];
+    int token_counts[2][kMaxRanks][kMaxRanks];  // [parity][src][dst] tokens src sends to dst
+    int expert_counts[2][kMaxRanks][kMaxLocalExperts];  // [parity][src][local expert] tokens from src
+};
+static_assert(sizeof(NormalCtrl) % 128 == 0, "NormalCtrl alignment");
+
+// Host-mapped per-buffer workspace read by the CPU after the notify step (the reference's
+// `moe_recv_counter` / `moe_recv_expert_counter`, [DE]csrc/legacy/buffer.hpp:579-597).
+struct HostCounters {
+    int ready_epoch;               // = dispatch epoch when the fields below are valid
+    int num_recv_tokens;
+    int num_local_experts;
+    int pad;
+    int num_recv_tokens_per_expert[kMaxLocalExperts];
+};
+
+// ------------------------------------------------------------------------------------------------
+// Normal-mode region layout (a pure function of region size, hidden, top-k and ranks, so every rank
+// computes the same offsets). Offsets are relative to the region base.
+// ------------------------------------------------------------------------------------------------
+struct NormalLayout {
+    int64_t ctrl_off;
+    int64_t list_off;        // int32 [kMaxRanks][capacity]: token ids I send to each destination
+    int64_t staging_off;     // records [capacity], record_bytes each
+    int64_t combine_off;     // bf16 rows [capacity * num_ranks][hidden]
+    int64_t combine_w_off;   // f32 [capacity * num_ranks][topk_pad]
+    int64_t total_bytes;
+    int32_t capacity;        // max tokens per rank per call
+    int32_t hidden;
+    int32_t num_topk;
+    int32_t topk_pad;        // top-k rounded up to a multiple of 4 (16-byte metadata)
+    int32_t record_bytes;    // staging record stride
+    int32_t num_ranks;
+};
+static_assert(sizeof(NormalLayout) == 72, "NormalLayout ABI");
+
+// Staging record of one token (written by its source rank, pulled by receivers):
+//   [x: hidden * elem bytes][scales: f32 * hidden/128 (fp8 only)][topk_idx: i32 * topk_pad][topk_w: f32 * topk_pad]
+struct RecordFormat {
+    int32_t x_bytes;
+    int32_t scale_off;
+    int32_t scale_bytes;
+    int32_t idx_off;
+    int32_t w_off;
+    int32_t bytes;  // total, 16-byte multiple
+};
+
+// ------------------------------------------------------------------------------------------------
+// Low-latency region layout: two halves (double buffering, at most two live results, the
+// reference's rule at [DE]deep_ep/buffers/legacy.py:425-426).
+// ------------------------------------------------------------------------------------------------
+struct LLLayout {
+    int64_t half_bytes;
+    // offsets relative to a half base
+    int64_t ctrl_off;           // LLCtrl
+    int64_t recv_x_off;         // [E_l][R*maxT][hidden] (bf16 capacity; fp8 uses hidden bytes per row)
+    int64_t recv_scales_off;    // f32 [E_l][hidden/128][R*maxT] (column-major per expert)
+    int64_t recv_src_info_off;  // i32 [E_l][R*maxT] source token index
+    int64_t recv_src_meta_off;  // i32 [E_l][R*maxT] src_rank * topk + k
+    int64_t combine_recv_off;   // bf16 [maxT][topk][hidden]
+    int64_t combine_send_off;   // bf16 [E_l][R*maxT][hidden] zero-copy send buffer
+    int32_t max_tokens;
+    int32_t hidden;
+    int32_t num_experts;
+    int32_t num_local_experts;
+    int32_t num_ranks;
+    int32_t num_topk;
+};
+
+struct alignas(128) LLCtrl {
+    int dispatch_done[kMaxRanks];   // [src] = LL dispatch seq once src's messages to me all landed
+    int combine_done[kMaxRanks];    // [src] = LL combine seq once src's rows to me all landed
+    int send_finished_blocks;       // local: blocks that finished the send phase (reset by last)
+    int csend_finished_blocks;
+    int pad[14];
+    int slot_counter[kMaxLocalExperts];  // [local expert] slots claimed by senders (remote atomics)
+};
+
+}  // namespace ep

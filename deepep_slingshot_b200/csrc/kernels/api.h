@@ -1,0 +1,174 @@
+// Launch API of the sm_100a kernels. Plain C++ (no torch headers) so that the CUDA translation units
+// compile fast and can also be driven from C (see the extern "C" entry points in the .cu files).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../include/ep/abi.h"
+
+namespace ep {
+
+// ---------------------------------------------------------------- layout (get_dispatch_layout)
+void launch_dispatch_layout(const int64_t* topk_idx, int num_tokens, int num_topk, int num_experts, int num_ranks,
+                            int* num_tokens_per_rank, int* num_tokens_per_expert, bool* is_token_in_rank,
+                            cudaStream_t stream);
+
+// ---------------------------------------------------------------- normal-mode dispatch
+struct StageArgs {
+    const void* x;               // [N][H] bf16 or fp8
+    const float* x_scales;       // pre-quantized input scales, or null
+    int64_t scale_stride_t;      // element stride between tokens
+    int64_t scale_stride_b;      // element stride between 128-blocks
+    const int64_t* topk_idx;     // [N][K] or null
+    const float* topk_weights;   // [N][K] or null
+    uint8_t* staging;            // local staging base (region base + staging_off)
+    const int* pull_done;        // local ctrl.pull_done
+    int num_tokens, hidden, num_topk, topk_pad;
+    int in_elem_bytes;           // 2 = bf16 input, 1 = fp8 input
+    int quantize;                // 1: fuse bf16 -> fp8 e4m3 1x128 quantization
+    int round_scale;             // 1: power-of-two scales
+    int num_ranks;
+    int wait_epoch;              // wait until pull_done[r] >= wait_epoch (0: no wait)
+    RecordFormat rec;
+    int record_stride;
+    KernelStatus st;
+};
+void launch_dispatch_stage(const StageArgs& a, int num_sms, cudaStream_t stream);
+
+struct NotifyArgs {
+    const int64_t* topk_idx;         // [N][K] or null
+    const bool* is_token_in_rank;    // [N][R] or null (then derived from topk_idx)
+    int num_tokens, num_topk, num_experts, num_local_experts;
+    int num_ranks, rank;
+    int cached;                      // 1: only publish readiness and wait (handle reuse)
+    int epoch, parity;
+    int expert_alignment;
+    PeerTable peers;
+    NormalLayout layout;
+    int* send_head;                  // [N][R]
+    int* rank_prefix_matrix;         // [R][R] inclusive prefix over sources
+    int* send_prefix_matrix;         // [R][R] exclusive prefix over destinations
+    int* recv_rank_prefix;           // [R+1]
+    int* num_recv_per_expert;        // [E_l] aligned counts (device)
+    int* dev_num_recv;               // [1]
+    int* cumulative_stats;           // [E_l] optional
+    HostCounters* host;              // host-mapped
+    KernelStatus st;
+};
+void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream);
+
+struct PullArgs {
+    PeerTable peers;
+    NormalLayout layout;
+    RecordFormat rec;
+    int rank, num_ranks, num_local_experts, num_topk;
+    const int* rank_prefix_matrix;   // [R][R]
+    const int* dev_num_recv;         // device count or null
+    int num_recv_host;               // used when dev_num_recv is null
+    int num_out_rows;                // allocated output rows (>= num_recv)
+    void* recv_x;
+    float* recv_scales;              // null for bf16
+    int scales_col_major;            // 1: [H/128][ld] layout
+    int64_t scales_ld;
+    int64_t* recv_topk_idx;          // null allowed
+    float* recv_topk_weights;        // null allowed
+    int* recv_src_idx;               // written for fresh dispatches (null in cached mode)
+    const int* cached_src_idx;       // cached mode: source token of every receive row (handle)
+    int epoch;
+    int stages;
+    KernelStatus st;
+};
+void launch_dispatch_pull(const PullArgs& a, int num_sms, cudaStream_t stream);
+
+// ---------------------------------------------------------------- normal-mode combine
+struct CombinePushArgs {
+    PeerTable peers;
+    NormalLayout layout;
+    int rank, num_ranks, num_topk;
+    const void* x;                   // bf16 [num_recv][H]
+    const float* topk_weights;       // [num_recv][K] or null
+    const int* rank_prefix_matrix;
+    const int* send_prefix_matrix;
+    int num_recv_max;                // rows available in x; the true count comes from the prefix matrix
+    int seq;
+    int stages;
+    KernelStatus st;
+};
+void launch_combine_push(const CombinePushArgs& a, int num_sms, cudaStream_t stream);
+
+struct CombineReduceArgs {
+    PeerTable peers;
+    NormalLayout layout;
+    int rank, num_ranks, num_topk, hidden;
+    const int* send_head;            // [N][R]
+    const int* rank_prefix_matrix;
+    const int* send_prefix_matrix;
+    int num_tokens;
+    int has_weights;
+    const void* bias0;               // bf16 [N][H] or null
+    const void* bias1;
+    void* out;                       // bf16 [N][H]
+    float* out_topk_weights;         // [N][K] or null
+    int seq;
+    KernelStatus st;
+};
+void launch_combine_reduce(const CombineReduceArgs& a, int num_sms, cudaStream_t stream);
+
+// ---------------------------------------------------------------- barrier
+void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, int epoch, KernelStatus st,
+                    cudaStream_t stream);
+
+// ---------------------------------------------------------------- low-latency mode
+struct LLDispatchArgs {
+    PeerTable peers;                 // LL region bases
+    LLLayout layout;
+    int half;
+    const void* x;                   // bf16 [N][H]
+    const int64_t* topk_idx;         // [N][K]
+    int num_tokens;
+    int rank;
+    int use_fp8, round_scale, use_ue8m0;
+    int seq;
+    int phases;                      // 1 send, 2 recv, 3 both
+    int* mask;                       // [R] shrink-mode mask (1 = masked) or null
+    int shrink;                      // 1: timeouts mask the rank instead of failing
+    // recv outputs
+    int* recv_count;                 // [E_l]
+    int64_t* layout_range;           // [E_l][R]
+    int* cumulative_stats;           // [E_l] optional
+    int64_t* wait_stats;             // [R] optional
+    KernelStatus st;
+};
+void launch_ll_dispatch(const LLDispatchArgs& a, cudaStream_t stream);
+
+struct LLCombineArgs {
+    PeerTable peers;
+    LLLayout layout;
+    int half;                        // combine half
+    int dispatch_half;               // half whose src info / counts describe the rows
+    const void* x;                   // bf16 [E_l][R*maxT][H]
+    const int* recv_count;           // [E_l] from the dispatch
+    const int64_t* topk_idx;         // [N][K]
+    const float* topk_weights;       // [N][K]
+    int num_tokens;
+    int rank;
+    int seq;
+    int phases;
+    int* mask;
+    int shrink;
+    void* out;                       // bf16 [N][H]
+    int64_t* wait_stats;             // [R] optional
+    KernelStatus st;
+};
+void launch_ll_combine(const LLCombineArgs& a, cudaStream_t stream);
+
+void launch_ll_clean(PeerTable peers, LLLayout layout, int rank, KernelStatus st, cudaStream_t stream);
+
+// ---------------------------------------------------------------- standalone ops
+void launch_per_token_cast_to_fp8(const void* x, int num_tokens, int hidden, void* out_fp8, float* out_scales,
+                                  int round_scale, cudaStream_t stream);
+void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_tokens, int hidden, void* out_bf16,
+                                cudaStream_t stream);
+
+}  // namespace ep

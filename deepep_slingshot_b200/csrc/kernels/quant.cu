@@ -1,0 +1,63 @@
+// Standalone per-token FP8 cast kernels (the reference's Python/torch.compile helpers
+// `per_token_cast_to_fp8` / `per_token_cast_back`, [DE]deep_ep/utils/math.py:36-61), as sm_100a
+// kernels: one warp per row, 16-byte vector loads, scales fp32 [N][H/128].
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "../include/ep/device.cuh"
+#include "../include/ep/quant.cuh"
+#include "api.h"
+
+namespace ep {
+
+__global__ void __launch_bounds__(256) per_token_cast_to_fp8_kernel(const __nv_bfloat16* __restrict__ x, int num_tokens,
+                                                                    int hidden, uint8_t* __restrict__ out,
+                                                                    float* __restrict__ scales, int round_scale) {
+    const int warps = blockDim.x / 32;
+    for (int t = blockIdx.x * warps + warp_id(); t < num_tokens; t += gridDim.x * warps)
+        quantize_row_to_fp8(x + (int64_t)t * hidden, out + (int64_t)t * hidden, scales + (int64_t)t * (hidden / 128), hidden,
+                            round_scale != 0);
+}
+
+__global__ void __launch_bounds__(256) per_token_cast_back_kernel(const uint8_t* __restrict__ x, const float* __restrict__ scales,
+                                                                  int num_tokens, int hidden, __nv_bfloat16* __restrict__ out) {
+    const int64_t n_vec = (int64_t)num_tokens * hidden / 8;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n_vec; v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e = v * 8;
+        const int64_t t = e / hidden;
+        const int64_t c = e % hidden;
+        const float s = scales[t * (hidden / 128) + c / 128];
+        const uint2 q = *reinterpret_cast<const uint2*>(x + e);
+        const __nv_fp8x2_storage_t* p = reinterpret_cast<const __nv_fp8x2_storage_t*>(&q);
+        int4 o;
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p[i], __NV_E4M3);
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            o2[i] = __floats2bfloat162_rn(f.x * s, f.y * s);
+        }
+        *reinterpret_cast<int4*>(out + e) = o;
+    }
+}
+
+void launch_per_token_cast_to_fp8(const void* x, int num_tokens, int hidden, void* out_fp8, float* out_scales,
+                                  int round_scale, cudaStream_t stream) {
+    if (num_tokens == 0) return;
+    int blocks = (num_tokens + 7) / 8;
+    if (blocks > 1184) blocks = 1184;
+    per_token_cast_to_fp8_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), num_tokens, hidden,
+                                                             static_cast<uint8_t*>(out_fp8), out_scales, round_scale);
+}
+
+void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_tokens, int hidden, void* out_bf16,
+                                cudaStream_t stream) {
+    if (num_tokens == 0) return;
+    const int64_t n_vec = (int64_t)num_tokens * hidden / 8;
+    int64_t blocks = (n_vec + 255) / 256;
+    if (blocks > 4736) blocks = 4736;
+    per_token_cast_back_kernel<<<(int)blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(x_fp8), scales, num_tokens, hidden,
+                                                                static_cast<__nv_bfloat16*>(out_bf16));
+}
+
+}  // namespace ep

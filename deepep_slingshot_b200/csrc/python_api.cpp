@@ -1,0 +1,75 @@
+// pybind11 module `deepep_slingshot_b200._C`: the runtime classes (Buffer, Config, EventHandle) and
+// the standalone sm_100a ops. Mirrors the reference's module surface ([DE]csrc/python_api.cpp:1-39,
+// pybind section [DE]csrc/legacy/buffer.hpp:1751-1792).
+#include <ATen/cuda/CUDAContext.h>
+#include <pybind11/functional.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include "kernels/api.h"
+#include "runtime/buffer.hpp"
+#include "runtime/ops.hpp"
+
+namespace py = pybind11;
+
+PYBIND11_MODULE(_C, m) {
+    m.doc() = "B200-native expert-parallel communication runtime (NVLink 5 / NVSwitch, sm_100a)";
+    m.attr("abi_version") = ep::kAbiVersion;
+    m.attr("max_ranks") = ep::kMaxRanks;
+    m.attr("max_topk") = ep::kMaxTopk;
+
+    py::class_<ep::Config>(m, "Config")
+        .def(py::init<int, int, int, int, int>(), py::arg("num_sms") = 20, py::arg("num_max_nvl_chunked_send_tokens") = 6,
+             py::arg("num_max_nvl_chunked_recv_tokens") = 256, py::arg("num_max_rdma_chunked_send_tokens") = 6,
+             py::arg("num_max_rdma_chunked_recv_tokens") = 256)
+        .def_readwrite("num_sms", &ep::Config::num_sms)
+        .def_readwrite("num_max_nvl_chunked_send_tokens", &ep::Config::num_max_nvl_chunked_send_tokens)
+        .def_readwrite("num_max_nvl_chunked_recv_tokens", &ep::Config::num_max_nvl_chunked_recv_tokens)
+        .def_readwrite("num_max_rdma_chunked_send_tokens", &ep::Config::num_max_rdma_chunked_send_tokens)
+        .def_readwrite("num_max_rdma_chunked_recv_tokens", &ep::Config::num_max_rdma_chunked_recv_tokens)
+        .def("get_nvl_buffer_size_hint", &ep::Config::get_nvl_buffer_size_hint, py::arg("hidden_bytes"), py::arg("num_ranks"),
+             py::arg("num_max_tokens") = 4096, py::arg("num_topk") = 8)
+        .def("get_rdma_buffer_size_hint", &ep::Config::get_rdma_buffer_size_hint);
+
+    py::class_<ep::EventHandle>(m, "EventHandle")
+        .def(py::init<>())
+        .def("current_stream_wait", &ep::EventHandle::current_stream_wait);
+
+    m.def("normal_region_size_for", &ep::normal_region_size_for);
+    m.def("ll_region_size_for", &ep::ll_region_size_for);
+    m.def("normal_layout_capacity", [](int64_t region_bytes, int hidden, int num_ranks) {
+        return ep::compute_normal_layout(region_bytes, hidden, num_ranks).capacity;
+    });
+
+    py::class_<ep::Buffer>(m, "Buffer")
+        .def(py::init<int, int, int64_t, int64_t, bool, bool, bool, double>())
+        .def("is_available", &ep::Buffer::is_available)
+        .def("get_num_rdma_ranks", &ep::Buffer::get_num_rdma_ranks)
+        .def("get_rdma_rank", &ep::Buffer::get_rdma_rank)
+        .def("get_root_rdma_rank", &ep::Buffer::get_root_rdma_rank)
+        .def("get_local_device_id", &ep::Buffer::get_local_device_id)
+        .def("get_local_ipc_handle", &ep::Buffer::get_local_ipc_handle)
+        .def("get_local_ll_ipc_handle", &ep::Buffer::get_local_ll_ipc_handle)
+        .def("sync", &ep::Buffer::sync)
+        .def("destroy", &ep::Buffer::destroy)
+        .def("get_comm_stream", &ep::Buffer::get_comm_stream)
+        .def("get_local_buffer_tensor", &ep::Buffer::get_local_buffer_tensor)
+        .def("get_capacity", &ep::Buffer::get_capacity)
+        .def("check_error", &ep::Buffer::check_error)
+        .def("get_error_state", &ep::Buffer::get_error_state)
+        .def("clear_error", &ep::Buffer::clear_error)
+        .def("set_timeout_secs", &ep::Buffer::set_timeout_secs)
+        .def("get_dispatch_layout", &ep::Buffer::get_dispatch_layout)
+        .def("intranode_dispatch", &ep::Buffer::intranode_dispatch)
+        .def("intranode_combine", &ep::Buffer::intranode_combine)
+        .def("barrier", &ep::Buffer::barrier)
+        .def("clean_low_latency_buffer", &ep::Buffer::clean_low_latency_buffer)
+        .def("low_latency_dispatch", &ep::Buffer::low_latency_dispatch)
+        .def("low_latency_combine", &ep::Buffer::low_latency_combine)
+        .def("get_next_low_latency_combine_buffer", &ep::Buffer::get_next_low_latency_combine_buffer)
+        .def("low_latency_update_mask_buffer", &ep::Buffer::low_latency_update_mask_buffer)
+        .def("low_latency_query_mask_buffer", &ep::Buffer::low_latency_query_mask_buffer)
+        .def("low_latency_clean_mask_buffer", &ep::Buffer::low_latency_clean_mask_buffer);
+
+    ep::register_ops(m);
+}

@@ -1,0 +1,902 @@
+// C++ runtime of the B200 expert-parallel buffer. See buffer.hpp for the design summary.
+#include "buffer.hpp"
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/python.h>
+
+#include <chrono>
+#include <cstring>
+#include <stdexcept>
+#include <thread>
+
+namespace ep {
+
+#define EP_CUDA_CHECK(cmd)                                                                                   \
+    do {                                                                                                     \
+        cudaError_t e_ = (cmd);                                                                              \
+        if (e_ != cudaSuccess)                                                                               \
+            throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " at " __FILE__ ":" + \
+                                     std::to_string(__LINE__));                                              \
+    } while (0)
+
+namespace {
+
+constexpr int64_t kAlign = 128;
+constexpr int64_t kCtrlRegionMin = 2 << 20;  // control block always present (barriers)
+
+int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+const char* error_name(int code) {
+    switch (code) {
+        case kErrTimeoutNotify: return "timeout waiting for a peer's dispatch counts (notify)";
+        case kErrTimeoutPullDone: return "timeout waiting for receivers to finish reading the staging area";
+        case kErrTimeoutCombineReady: return "timeout waiting for a destination to finish its previous combine";
+        case kErrTimeoutCombineArrive: return "timeout waiting for combine contributions to arrive";
+        case kErrTimeoutBarrier: return "timeout in the NVLink barrier";
+        case kErrTimeoutLLDispatch: return "timeout in low-latency dispatch receive";
+        case kErrTimeoutLLCombine: return "timeout in low-latency combine receive";
+        case kErrTimeoutTma: return "timeout waiting for a TMA bulk copy";
+        case kErrCapacity: return "receive capacity exceeded";
+        case kErrBounds: return "index out of bounds in a peer window";
+        case kErrBadArgs: return "bad kernel arguments";
+        case kErrTimeoutPP: return "timeout in pipeline-parallel send/recv";
+        case kErrTimeoutTest: return "transport self-test wait expired";
+        default: return "unknown error";
+    }
+}
+
+void stream_wait(const at::cuda::CUDAStream& waiter, const at::cuda::CUDAStream& signaler) {
+    if (waiter == signaler) return;
+    at::cuda::CUDAEvent ev;
+    ev.record(signaler);
+    ev.block(waiter);
+}
+
+// The reference's stream discipline ([DE]csrc/legacy/buffer.hpp:337-404): kernels run on the comm
+// stream, which first waits for `previous_event` (or the current stream); outputs may be allocated
+// on the comm stream; with `async` an event is returned and tensors are recorded on the comm stream,
+// otherwise the current stream waits for the comm stream.
+struct StreamScope {
+    at::cuda::CUDAStream compute;
+    at::cuda::CUDAStream comm;
+    bool alloc_on_comm;
+    StreamScope(const at::cuda::CUDAStream& comm_stream, std::optional<EventHandle>& previous_event, bool allocate_on_comm_stream)
+        : compute(at::cuda::getCurrentCUDAStream()), comm(comm_stream), alloc_on_comm(allocate_on_comm_stream) {
+        if (previous_event.has_value()) previous_event->event->block(comm);
+        else stream_wait(comm, compute);
+        if (alloc_on_comm) at::cuda::setCurrentCUDAStream(comm);
+    }
+    std::optional<EventHandle> finish(bool async, std::initializer_list<std::optional<torch::Tensor>> tensors) {
+        std::optional<EventHandle> event;
+        if (async) {
+            event = EventHandle(comm);
+            for (const auto& t : tensors)
+                if (t.has_value() && t->defined()) t->record_stream(comm);
+        } else {
+            stream_wait(compute, comm);
+        }
+        if (alloc_on_comm) at::cuda::setCurrentCUDAStream(compute);
+        return event;
+    }
+};
+
+}  // namespace
+
+// =================================================================================================
+// Config / layouts
+// =================================================================================================
+RecordFormat record_format(int hidden, int num_topk, bool fp8) {
+    RecordFormat r{};
+    const int topk_pad = (int)align_up(num_topk, 4);
+    r.x_bytes = fp8 ? hidden : hidden * 2;
+    r.scale_off = r.x_bytes;
+    r.scale_bytes = fp8 ? (int)align_up((int64_t)(hidden / 128) * 4, 16) : 0;
+    r.idx_off = r.scale_off + r.scale_bytes;
+    r.w_off = r.idx_off + topk_pad * 4;
+    r.bytes = r.w_off + topk_pad * 4;
+    return r;
+}
+
+static int64_t normal_bytes_per_token(int hidden, int num_ranks, int* record_stride) {
+    const RecordFormat bf = record_format(hidden, kMaxTopk, false);
+    const RecordFormat f8 = record_format(hidden, kMaxTopk, true);
+    const int rec = (int)align_up(std::max(bf.bytes, f8.bytes), kAlign);
+    if (record_stride) *record_stride = rec;
+    return (int64_t)num_ranks * 4 + rec + (int64_t)num_ranks * hidden * 2 + (int64_t)num_ranks * kMaxTopk * 4;
+}
+
+NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ranks) {
+    NormalLayout l{};
+    int rec = 0;
+    const int64_t per_token = normal_bytes_per_token(hidden, num_ranks, &rec);
+    const int64_t ctrl = align_up(sizeof(NormalCtrl), 4096);
+    const int64_t slack = 8 * kAlign;
+    int64_t cap = region_bytes > ctrl + slack ? (region_bytes - ctrl - slack) / per_token : 0;
+    cap = cap / 32 * 32;
+    l.capacity = (int32_t)std::min<int64_t>(cap, 1 << 24);
+    l.hidden = hidden;
+    l.num_topk = kMaxTopk;
+    l.topk_pad = kMaxTopk;
+    l.record_bytes = rec;
+    l.num_ranks = num_ranks;
+    l.ctrl_off = 0;
+    l.list_off = ctrl;
+    l.staging_off = align_up(l.list_off + (int64_t)num_ranks * l.capacity * 4, kAlign);
+    l.combine_off = align_up(l.staging_off + (int64_t)l.capacity * rec, kAlign);
+    l.combine_w_off = align_up(l.combine_off + (int64_t)l.capacity * num_ranks * hidden * 2, kAlign);
+    l.total_bytes = align_up(l.combine_w_off + (int64_t)l.capacity * num_ranks * kMaxTopk * 4, kAlign);
+    return l;
+}
+
+int64_t normal_region_size_for(int num_max_tokens, int hidden, int num_ranks) {
+    const int64_t per_token = normal_bytes_per_token(hidden, num_ranks, nullptr);
+    const int64_t ctrl = align_up(sizeof(NormalCtrl), 4096);
+    const int64_t tokens = align_up(num_max_tokens, 32);
+    return align_up(ctrl + 8 * kAlign + tokens * per_token + 16 * kAlign, 2 << 20);
+}
+
+LLLayout compute_ll_layout(int64_t region_bytes, int max_tokens, int hidden, int num_experts, int num_ranks) {
+    LLLayout l{};
+    const int64_t E_l = num_experts / num_ranks;
+    const int64_t slots = (int64_t)num_ranks * max_tokens;
+    const int64_t nb = hidden / 128;
+    l.max_tokens = max_tokens;
+    l.hidden = hidden;
+    l.num_experts = num_experts;
+    l.num_local_experts = (int)E_l;
+    l.num_ranks = num_ranks;
+    l.num_topk = kMaxTopk;
+    int64_t off = 0;
+    l.ctrl_off = off;
+    off = align_up(off + sizeof(LLCtrl), kAlign);
+    l.recv_x_off = off;
+    off = align_up(off + E_l * slots * hidden * 2, kAlign);
+    l.recv_scales_off = off;
+    off = align_up(off + E_l * nb * slots * 4, kAlign);
+    l.recv_src_info_off = off;
+    off = align_up(off + E_l * slots * 4, kAlign);
+    l.recv_src_meta_off = off;
+    off = align_up(off + E_l * slots * 4, kAlign);
+    l.combine_recv_off = off;
+    off = align_up(off + (int64_t)max_tokens * kMaxTopk * hidden * 2, kAlign);
+    l.combine_send_off = off;
+    off = align_up(off + E_l * slots * hidden * 2, kAlign);
+    l.half_bytes = align_up(off, 4096);
+    (void)region_bytes;
+    return l;
+}
+
+int64_t ll_region_size_for(int max_tokens, int hidden, int num_ranks, int num_experts) {
+    const LLLayout l = compute_ll_layout(0, max_tokens, hidden, num_experts, num_ranks);
+    return align_up(2 * l.half_bytes, 2 << 20);
+}
+
+int64_t Config::get_nvl_buffer_size_hint(int64_t hidden_bytes, int num_ranks, int num_max_tokens, int num_topk) const {
+    (void)num_topk;
+    const int hidden = (int)(hidden_bytes / 2);  // sized for bf16 rows (covers FP8 records too)
+    return normal_region_size_for(num_max_tokens, std::max(hidden, 128), num_ranks);
+}
+
+int64_t Config::get_rdma_buffer_size_hint(int64_t hidden_bytes, int num_ranks) const {
+    (void)hidden_bytes;
+    (void)num_ranks;
+    return 0;  // no RDMA domain on one NVLink box
+}
+
+// =================================================================================================
+// EventHandle
+// =================================================================================================
+EventHandle::EventHandle() {
+    event = std::make_shared<at::cuda::CUDAEvent>();
+    event->record(at::cuda::getCurrentCUDAStream());
+}
+EventHandle::EventHandle(const at::cuda::CUDAStream& stream) {
+    event = std::make_shared<at::cuda::CUDAEvent>();
+    event->record(stream);
+}
+void EventHandle::current_stream_wait() const { event->block(at::cuda::getCurrentCUDAStream()); }
+
+// =================================================================================================
+// Buffer: construction, IPC exchange, teardown
+// =================================================================================================
+Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_bytes, bool low_latency_mode,
+               bool explicitly_destroy, bool enable_shrink, double gpu_timeout_secs)
+    : rank_(rank),
+      num_ranks_(num_ranks),
+      num_nvl_bytes_(std::max<int64_t>(num_nvl_bytes, kCtrlRegionMin)),
+      num_rdma_bytes_(num_rdma_bytes),
+      low_latency_mode_(low_latency_mode),
+      explicitly_destroy_(explicitly_destroy),
+      enable_shrink_(enable_shrink),
+      comm_stream_(at::cuda::getStreamFromPool(true)) {
+    if (num_ranks < 1 || num_ranks > kMaxRanks)
+        throw std::runtime_error("B200 EP buffer: the group must be one NVLink domain of 1..8 ranks (got " +
+                                 std::to_string(num_ranks) + "); internode RDMA is not available on a single box");
+    if (rank < 0 || rank >= num_ranks) throw std::runtime_error("bad rank");
+    EP_CUDA_CHECK(cudaGetDevice(&device_id_));
+    set_timeout_secs(gpu_timeout_secs);
+
+    num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
+    EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
+    EP_CUDA_CHECK(cudaMemset(nvl_base_, 0, std::min<int64_t>(num_nvl_bytes_, align_up(sizeof(NormalCtrl), 4096))));
+    EP_CUDA_CHECK(cudaIpcGetMemHandle(&nvl_ipc_, nvl_base_));
+    if (num_rdma_bytes_ > 0) {
+        num_rdma_bytes_ = align_up(num_rdma_bytes_, 2 << 20);
+        EP_CUDA_CHECK(cudaMalloc(&ll_base_, num_rdma_bytes_));
+        EP_CUDA_CHECK(cudaMemset(ll_base_, 0, num_rdma_bytes_));
+        EP_CUDA_CHECK(cudaIpcGetMemHandle(&ll_ipc_, ll_base_));
+    }
+    EP_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&host_error_), sizeof(ErrorState), cudaHostAllocMapped));
+    std::memset(host_error_, 0, sizeof(ErrorState));
+    EP_CUDA_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_error_dev_), host_error_, 0));
+    EP_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&host_counters_), sizeof(HostCounters), cudaHostAllocMapped));
+    std::memset(host_counters_, 0, sizeof(HostCounters));
+    EP_CUDA_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_counters_dev_), host_counters_, 0));
+    EP_CUDA_CHECK(cudaMalloc(reinterpret_cast<void**>(&dev_workspace_), 4096));
+    EP_CUDA_CHECK(cudaMemset(dev_workspace_, 0, 4096));
+    EP_CUDA_CHECK(cudaMalloc(reinterpret_cast<void**>(&mask_), sizeof(int) * kMaxRanks));
+    EP_CUDA_CHECK(cudaMemset(mask_, 0, sizeof(int) * kMaxRanks));
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
+}
+
+Buffer::~Buffer() noexcept(false) {
+    if (!explicitly_destroy_) {
+        destroy();
+    } else if (!destroyed_) {
+        fprintf(stderr, "B200 EP buffer: explicitly_destroy is set but destroy() was never called; resources leak\n");
+    }
+}
+
+pybind11::bytearray Buffer::get_local_ipc_handle() const {
+    return {nvl_ipc_.reserved, CUDA_IPC_HANDLE_SIZE};
+}
+pybind11::bytearray Buffer::get_local_ll_ipc_handle() const {
+    if (ll_base_ == nullptr) return {"", 0};
+    return {ll_ipc_.reserved, CUDA_IPC_HANDLE_SIZE};
+}
+
+void Buffer::sync(const std::vector<int>& device_ids, const std::vector<std::optional<pybind11::bytearray>>& handles,
+                  const std::vector<std::optional<pybind11::bytearray>>& ll_handles) {
+    if (available_) throw std::runtime_error("buffer already synced");
+    if ((int)device_ids.size() != num_ranks_ || (int)handles.size() != num_ranks_)
+        throw std::runtime_error("sync: wrong number of peers");
+    for (int r = 0; r < num_ranks_; ++r) {
+        if (r == rank_) {
+            nvl_peer_[r] = nvl_base_;
+            ll_peer_[r] = ll_base_;
+            continue;
+        }
+        if (device_ids[r] == device_id_)
+            throw std::runtime_error("sync: two ranks share one GPU; kernels that wait on one another cannot share a device");
+        int can = 0;
+        EP_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, device_id_, device_ids[r]));
+        if (!can) throw std::runtime_error("sync: no peer access to device " + std::to_string(device_ids[r]));
+        auto h = std::string(handles[r].value());
+        if (h.size() != CUDA_IPC_HANDLE_SIZE) throw std::runtime_error("sync: bad IPC handle size");
+        cudaIpcMemHandle_t ipc;
+        std::memcpy(ipc.reserved, h.data(), CUDA_IPC_HANDLE_SIZE);
+        EP_CUDA_CHECK(cudaIpcOpenMemHandle(&nvl_peer_[r], ipc, cudaIpcMemLazyEnablePeerAccess));
+        nvl_peer_opened_[r] = true;
+        if (ll_base_ != nullptr) {
+            if ((int)ll_handles.size() != num_ranks_ || !ll_handles[r].has_value())
+                throw std::runtime_error("sync: missing low-latency IPC handle");
+            auto lh = std::string(ll_handles[r].value());
+            if (lh.size() != CUDA_IPC_HANDLE_SIZE) throw std::runtime_error("sync: bad LL IPC handle size");
+            cudaIpcMemHandle_t lipc;
+            std::memcpy(lipc.reserved, lh.data(), CUDA_IPC_HANDLE_SIZE);
+            EP_CUDA_CHECK(cudaIpcOpenMemHandle(&ll_peer_[r], lipc, cudaIpcMemLazyEnablePeerAccess));
+            ll_peer_opened_[r] = true;
+        }
+    }
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
+    available_ = true;
+}
+
+void Buffer::destroy() {
+    if (destroyed_) return;
+    destroyed_ = true;
+    cudaDeviceSynchronize();
+    for (int r = 0; r < kMaxRanks; ++r) {
+        if (nvl_peer_opened_[r]) cudaIpcCloseMemHandle(nvl_peer_[r]);
+        if (ll_peer_opened_[r]) cudaIpcCloseMemHandle(ll_peer_[r]);
+        nvl_peer_opened_[r] = ll_peer_opened_[r] = false;
+    }
+    if (nvl_base_) cudaFree(nvl_base_);
+    if (ll_base_) cudaFree(ll_base_);
+    if (dev_workspace_) cudaFree(dev_workspace_);
+    if (mask_) cudaFree(mask_);
+    if (host_error_) cudaFreeHost(host_error_);
+    if (host_counters_) cudaFreeHost(host_counters_);
+    nvl_base_ = ll_base_ = nullptr;
+    dev_workspace_ = mask_ = nullptr;
+    host_error_ = nullptr;
+    host_counters_ = nullptr;
+    available_ = false;
+}
+
+torch::Stream Buffer::get_comm_stream() const { return comm_stream_; }
+
+torch::Tensor Buffer::get_local_buffer_tensor(const pybind11::object& dtype, int64_t offset, bool use_rdma_buffer) const {
+    const auto scalar = torch::python::detail::py_object_to_dtype(dtype);
+    const int64_t esize = c10::elementSize(scalar);
+    void* base = use_rdma_buffer ? ll_base_ : nvl_base_;
+    const int64_t bytes = use_rdma_buffer ? num_rdma_bytes_ : num_nvl_bytes_;
+    if (base == nullptr) throw std::runtime_error("requested region is not allocated");
+    const int64_t n = bytes / esize - offset;
+    return torch::from_blob(static_cast<uint8_t*>(base) + offset * esize, {n},
+                            torch::TensorOptions().dtype(scalar).device(torch::kCUDA, device_id_));
+}
+
+int64_t Buffer::get_capacity(int hidden, int num_topk) const {
+    (void)num_topk;
+    return compute_normal_layout(num_nvl_bytes_, hidden, num_ranks_).capacity;
+}
+
+// =================================================================================================
+// Errors
+// =================================================================================================
+void Buffer::set_timeout_secs(double secs) {
+    if (secs <= 0) secs = 100.0;
+    timeout_ns_ = (uint64_t)(secs * 1e9);
+}
+
+KernelStatus Buffer::status() const {
+    KernelStatus s{};
+    s.host_error = host_error_dev_;
+    s.abort_flag = dev_workspace_;
+    s.timeout_ns = timeout_ns_;
+    s.rank = rank_;
+    return s;
+}
+
+void Buffer::check_error() const {
+    if (host_error_ == nullptr) return;
+    const int code = *reinterpret_cast<volatile int*>(&host_error_->code);
+    if (code != 0) {
+        throw std::runtime_error("B200 EP kernel error on rank " + std::to_string(host_error_->rank) + ": " +
+                                 error_name(code) + " (code " + std::to_string(code) + ", peer " +
+                                 std::to_string(host_error_->peer) + ", detail " + std::to_string(host_error_->detail) + ")");
+    }
+}
+
+std::tuple<int, int, int, int> Buffer::get_error_state() const {
+    if (host_error_ == nullptr) return {0, 0, 0, 0};
+    return {host_error_->code, host_error_->peer, host_error_->detail, host_error_->rank};
+}
+
+void Buffer::clear_error() {
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
+    if (host_error_) std::memset(host_error_, 0, sizeof(ErrorState));
+    if (dev_workspace_) EP_CUDA_CHECK(cudaMemset(dev_workspace_, 0, sizeof(int)));
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
+}
+
+PeerTable Buffer::nvl_peers() const {
+    PeerTable p{};
+    for (int r = 0; r < num_ranks_; ++r) p.base[r] = nvl_peer_[r];
+    return p;
+}
+PeerTable Buffer::ll_peers() const {
+    PeerTable p{};
+    for (int r = 0; r < num_ranks_; ++r) p.base[r] = ll_peer_[r];
+    return p;
+}
+
+void Buffer::wait_host_counters(int epoch) {
+    const auto start = std::chrono::steady_clock::now();
+    const double limit = (double)timeout_ns_ * 1e-9;
+    uint64_t it = 0;
+    while (*reinterpret_cast<volatile int*>(&host_counters_->ready_epoch) != epoch) {
+        if ((++it & 1023) == 0) {
+            check_error();
+            const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+            if (el > limit)
+                throw std::runtime_error("B200 EP: CPU timeout waiting for received token counts (rank " + std::to_string(rank_) + ")");
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    check_error();
+}
+
+// =================================================================================================
+// Normal mode
+// =================================================================================================
+std::tuple<torch::Tensor, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, std::optional<EventHandle>>
+Buffer::get_dispatch_layout(const torch::Tensor& topk_idx, int num_experts, std::optional<EventHandle>& previous_event,
+                            bool async, bool allocate_on_comm_stream) {
+    check_error();
+    TORCH_CHECK(topk_idx.dim() == 2 && topk_idx.is_contiguous() && topk_idx.scalar_type() == torch::kInt64);
+    TORCH_CHECK(num_experts % num_ranks_ == 0, "num_experts must be a multiple of the group size");
+    StreamScope scope(comm_stream_, previous_event, allocate_on_comm_stream);
+    const int N = (int)topk_idx.size(0), K = (int)topk_idx.size(1);
+    auto i32 = torch::dtype(torch::kInt32).device(torch::kCUDA);
+    auto num_tokens_per_rank = torch::empty({num_ranks_}, i32);
+    auto num_tokens_per_expert = torch::empty({num_experts}, i32);
+    auto is_token_in_rank = torch::empty({N, num_ranks_}, torch::dtype(torch::kBool).device(torch::kCUDA));
+    launch_dispatch_layout(topk_idx.data_ptr<int64_t>(), N, K, num_experts, num_ranks_, num_tokens_per_rank.data_ptr<int>(),
+                           num_tokens_per_expert.data_ptr<int>(), is_token_in_rank.data_ptr<bool>(), scope.comm.stream());
+    auto event = scope.finish(async, {topk_idx, num_tokens_per_rank, num_tokens_per_expert, is_token_in_rank});
+    return {num_tokens_per_rank, std::nullopt, num_tokens_per_expert, is_token_in_rank, event};
+}
+
+std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<torch::Tensor>, std::optional<torch::Tensor>,
+           std::vector<int>, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+           std::optional<torch::Tensor>, std::optional<EventHandle>>
+Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Tensor>& x_scales,
+                           const std::optional<torch::Tensor>& topk_idx, const std::optional<torch::Tensor>& topk_weights,
+                           const std::optional<torch::Tensor>& is_token_in_rank, int num_experts,
+                           const std::optional<torch::Tensor>& cached_rank_prefix_matrix,
+                           const std::optional<torch::Tensor>& cached_send_prefix_matrix,
+                           const std::optional<torch::Tensor>& cached_recv_src_idx,
+                           const std::optional<torch::Tensor>& cached_send_head, int expert_alignment,
+                           int num_worst_tokens, bool quantize_fp8, bool round_scale, bool scales_col_major,
+                           const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats, int num_sms,
+                           std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream) {
+    check_error();
+    TORCH_CHECK(available_, "buffer not synced");
+    const bool cached = cached_rank_prefix_matrix.has_value();
+    TORCH_CHECK(x.dim() == 2 && x.is_contiguous(), "x must be a contiguous [num_tokens, hidden] tensor");
+    const bool fp8_in = x.scalar_type() == torch::kFloat8_e4m3fn;
+    TORCH_CHECK(fp8_in || x.scalar_type() == torch::kBFloat16, "x must be bf16 or float8_e4m3fn");
+    TORCH_CHECK(fp8_in == x_scales.has_value(), "FP8 input needs scales (and only FP8 input takes them)");
+    TORCH_CHECK(!(fp8_in && quantize_fp8), "input is already FP8");
+    const bool out_fp8 = fp8_in || quantize_fp8;
+    const int N = (int)x.size(0), H = (int)x.size(1), R = num_ranks_;
+    TORCH_CHECK(H % 128 == 0, "hidden must be a multiple of 128");
+    const int K = (!cached && topk_idx.has_value()) ? (int)topk_idx->size(1) : 0;
+    TORCH_CHECK(K <= kMaxTopk, "top-k larger than 16 is not supported");
+    if (!cached) {
+        TORCH_CHECK(topk_idx.has_value() || is_token_in_rank.has_value(), "need topk_idx or is_token_in_rank");
+        TORCH_CHECK(num_experts > 0 && num_experts % R == 0, "num_experts must be a positive multiple of the group size");
+        TORCH_CHECK(num_experts / R <= kMaxLocalExperts, "too many local experts");
+        if (topk_idx.has_value())
+            TORCH_CHECK(topk_idx->scalar_type() == torch::kInt64 && topk_idx->is_contiguous() && topk_idx->size(0) == N);
+        if (topk_weights.has_value())
+            TORCH_CHECK(topk_weights->scalar_type() == torch::kFloat32 && topk_weights->is_contiguous() &&
+                        topk_weights->size(0) == N && topk_weights->size(1) == K);
+        if (is_token_in_rank.has_value())
+            TORCH_CHECK(is_token_in_rank->scalar_type() == torch::kBool && is_token_in_rank->is_contiguous() &&
+                        is_token_in_rank->size(0) == N && is_token_in_rank->size(1) == R);
+    } else {
+        TORCH_CHECK(cached_send_prefix_matrix.has_value() && cached_recv_src_idx.has_value() && cached_send_head.has_value());
+        TORCH_CHECK(cached_send_head->size(0) == N, "cached handle was built for a different token count");
+    }
+    const NormalLayout L = compute_normal_layout(num_nvl_bytes_, H, R);
+    TORCH_CHECK(N <= L.capacity, "num_tokens (" + std::to_string(N) + ") exceeds the buffer capacity (" +
+                                     std::to_string(L.capacity) + "); allocate num_nvl_bytes >= Buffer.get_nvl_buffer_size_hint(...)");
+    const RecordFormat rec = record_format(H, K, out_fp8);
+    const int E_l = cached ? 0 : num_experts / R;
+    if (num_sms <= 0) num_sms = 32;
+
+    const int epoch = ++dispatch_epoch_;
+    StreamScope scope(comm_stream_, previous_event, allocate_on_comm_stream);
+    auto stream = scope.comm.stream();
+    auto i32 = torch::dtype(torch::kInt32).device(torch::kCUDA);
+    const KernelStatus st = status();
+    const PeerTable peers = nvl_peers();
+    uint8_t* my_base = static_cast<uint8_t*>(nvl_base_);
+
+    // 1) stage
+    StageArgs sa{};
+    sa.x = x.data_ptr();
+    if (fp8_in) {
+        TORCH_CHECK(x_scales->scalar_type() == torch::kFloat32 && x_scales->dim() == 2 && x_scales->size(0) == N &&
+                        x_scales->size(1) == H / 128,
+                    "x scales must be float32 [num_tokens, hidden / 128]");
+        sa.x_scales = x_scales->data_ptr<float>();
+        sa.scale_stride_t = x_scales->stride(0);
+        sa.scale_stride_b = x_scales->stride(1);
+    }
+    sa.topk_idx = (!cached && topk_idx.has_value()) ? topk_idx->data_ptr<int64_t>() : nullptr;
+    sa.topk_weights = (!cached && topk_weights.has_value()) ? topk_weights->data_ptr<float>() : nullptr;
+    sa.staging = my_base + L.staging_off;
+    sa.pull_done = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->pull_done;
+    sa.num_tokens = N;
+    sa.hidden = H;
+    sa.num_topk = K;
+    sa.topk_pad = (int)align_up(K, 4);
+    sa.in_elem_bytes = fp8_in ? 1 : 2;
+    sa.quantize = quantize_fp8 ? 1 : 0;
+    sa.round_scale = round_scale ? 1 : 0;
+    sa.num_ranks = R;
+    sa.wait_epoch = epoch - 1;
+    sa.rec = rec;
+    sa.record_stride = L.record_bytes;
+    sa.st = st;
+    launch_dispatch_stage(sa, num_sms, stream);
+
+    // 2) notify
+    torch::Tensor send_head, rpm, spm, recv_rank_prefix;
+    std::optional<torch::Tensor> num_recv_per_expert;
+    if (cached) {
+        rpm = *cached_rank_prefix_matrix;
+        spm = *cached_send_prefix_matrix;
+        send_head = *cached_send_head;
+        recv_rank_prefix = torch::empty({0}, i32);
+    } else {
+        send_head = torch::empty({N, R}, i32);
+        rpm = torch::empty({R, R}, i32);
+        spm = torch::empty({R, R}, i32);
+        recv_rank_prefix = torch::empty({R + 1}, i32);
+        num_recv_per_expert = torch::empty({E_l}, i32);
+    }
+    NotifyArgs na{};
+    na.topk_idx = sa.topk_idx;
+    na.is_token_in_rank = (!cached && is_token_in_rank.has_value()) ? is_token_in_rank->data_ptr<bool>() : nullptr;
+    na.num_tokens = N;
+    na.num_topk = K;
+    na.num_experts = cached ? 0 : num_experts;
+    na.num_local_experts = E_l;
+    na.num_ranks = R;
+    na.rank = rank_;
+    na.cached = cached ? 1 : 0;
+    na.epoch = epoch;
+    na.parity = epoch & 1;
+    na.expert_alignment = std::max(1, expert_alignment);
+    na.peers = peers;
+    na.layout = L;
+    na.send_head = send_head.data_ptr<int>();
+    na.rank_prefix_matrix = rpm.data_ptr<int>();
+    na.send_prefix_matrix = spm.data_ptr<int>();
+    na.recv_rank_prefix = cached ? nullptr : recv_rank_prefix.data_ptr<int>();
+    na.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
+    na.dev_num_recv = dev_workspace_ + 1;
+    na.cumulative_stats = cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
+    na.host = host_counters_dev_;
+    na.st = st;
+    launch_dispatch_notify(na, stream);
+
+    // 3) receive size: cached, worst case (no CPU sync) or CPU sync on the mapped counters
+    int num_recv = -1, num_out_rows = 0;
+    std::vector<int> per_expert_list;
+    if (cached) {
+        num_recv = (int)cached_recv_src_idx->size(0);
+        num_out_rows = num_recv;
+    } else if (num_worst_tokens > 0) {
+        num_out_rows = num_worst_tokens;
+    } else {
+        wait_host_counters(epoch);
+        num_recv = host_counters_->num_recv_tokens;
+        num_out_rows = num_recv;
+        per_expert_list.assign(host_counters_->num_recv_tokens_per_expert, host_counters_->num_recv_tokens_per_expert + E_l);
+    }
+
+    // 4) outputs + pull
+    auto recv_x = torch::empty({num_out_rows, H}, x.options().dtype(out_fp8 ? torch::kFloat8_e4m3fn : torch::kBFloat16));
+    std::optional<torch::Tensor> recv_scales;
+    int64_t scales_ld = 0;
+    if (out_fp8) {
+        if (scales_col_major) {
+            scales_ld = align_up(std::max(num_out_rows, 1), 4);
+            auto storage = torch::empty({H / 128, scales_ld}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+            recv_scales = storage.narrow(1, 0, num_out_rows).t();
+        } else {
+            recv_scales = torch::empty({num_out_rows, H / 128}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+        }
+    }
+    std::optional<torch::Tensor> recv_topk_idx, recv_topk_weights;
+    if (!cached && topk_idx.has_value())
+        recv_topk_idx = torch::empty({num_out_rows, K}, torch::dtype(torch::kInt64).device(torch::kCUDA));
+    if (!cached && topk_weights.has_value())
+        recv_topk_weights = torch::empty({num_out_rows, K}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+    torch::Tensor recv_src_idx = cached ? *cached_recv_src_idx : torch::empty({num_out_rows}, i32);
+
+    PullArgs pa{};
+    pa.peers = peers;
+    pa.layout = L;
+    pa.rec = rec;
+    pa.rank = rank_;
+    pa.num_ranks = R;
+    pa.num_local_experts = E_l;
+    pa.num_topk = K;
+    pa.rank_prefix_matrix = rpm.data_ptr<int>();
+    pa.dev_num_recv = cached ? nullptr : dev_workspace_ + 1;
+    pa.num_recv_host = num_recv;
+    pa.num_out_rows = num_out_rows;
+    pa.recv_x = recv_x.data_ptr();
+    pa.recv_scales = recv_scales.has_value() ? recv_scales->data_ptr<float>() : nullptr;
+    pa.scales_col_major = scales_col_major ? 1 : 0;
+    pa.scales_ld = scales_ld;
+    pa.recv_topk_idx = recv_topk_idx.has_value() ? recv_topk_idx->data_ptr<int64_t>() : nullptr;
+    pa.recv_topk_weights = recv_topk_weights.has_value() ? recv_topk_weights->data_ptr<float>() : nullptr;
+    pa.recv_src_idx = cached ? nullptr : recv_src_idx.data_ptr<int>();
+    pa.cached_src_idx = cached ? cached_recv_src_idx->data_ptr<int>() : nullptr;
+    pa.epoch = epoch;
+    pa.stages = 0;
+    pa.st = st;
+    launch_dispatch_pull(pa, num_sms, stream);
+    EP_CUDA_CHECK(cudaGetLastError());
+
+    auto event = scope.finish(async, {x, x_scales, topk_idx, topk_weights, is_token_in_rank, recv_x, recv_scales, recv_topk_idx,
+                                      recv_topk_weights, recv_src_idx, send_head, rpm, spm, recv_rank_prefix,
+                                      num_recv_per_expert, cumulative_local_expert_recv_stats});
+    return {recv_x, recv_scales, recv_topk_idx, recv_topk_weights, per_expert_list, rpm, spm, recv_rank_prefix,
+            recv_src_idx, send_head, num_recv_per_expert, event};
+}
+
+std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandle>> Buffer::intranode_combine(
+    const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
+    const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,
+    const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, int num_sms,
+    std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream) {
+    check_error();
+    TORCH_CHECK(available_, "buffer not synced");
+    TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16, "x must be contiguous bf16 [rows, hidden]");
+    const int H = (int)x.size(1), R = num_ranks_;
+    const int N = (int)send_head.size(0);
+    TORCH_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
+    const int K = topk_weights.has_value() ? (int)topk_weights->size(1) : 0;
+    if (topk_weights.has_value())
+        TORCH_CHECK(topk_weights->scalar_type() == torch::kFloat32 && topk_weights->is_contiguous() &&
+                    topk_weights->size(0) == x.size(0));
+    for (const auto* b : {&bias_0, &bias_1})
+        if (b->has_value())
+            TORCH_CHECK((*b)->scalar_type() == torch::kBFloat16 && (*b)->is_contiguous() && (*b)->size(0) == N && (*b)->size(1) == H);
+    const NormalLayout L = compute_normal_layout(num_nvl_bytes_, H, R);
+    TORCH_CHECK(N <= L.capacity, "num_tokens exceeds the buffer capacity");
+    if (num_sms <= 0) num_sms = 32;
+    const int seq = ++combine_seq_;
+    StreamScope scope(comm_stream_, previous_event, allocate_on_comm_stream);
+    auto stream = scope.comm.stream();
+    auto out = torch::empty({N, H}, x.options());
+    std::optional<torch::Tensor> out_w;
+    if (topk_weights.has_value()) out_w = torch::empty({N, K}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+    const KernelStatus st = status();
+    const PeerTable peers = nvl_peers();
+
+    CombinePushArgs pa{};
+    pa.peers = peers;
+    pa.layout = L;
+    pa.rank = rank_;
+    pa.num_ranks = R;
+    pa.num_topk = K;
+    pa.x = x.data_ptr();
+    pa.topk_weights = topk_weights.has_value() ? topk_weights->data_ptr<float>() : nullptr;
+    pa.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
+    pa.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
+    pa.num_recv_max = (int)x.size(0);
+    pa.seq = seq;
+    pa.stages = 0;
+    pa.st = st;
+    launch_combine_push(pa, num_sms, stream);
+
+    CombineReduceArgs ra{};
+    ra.peers = peers;
+    ra.layout = L;
+    ra.rank = rank_;
+    ra.num_ranks = R;
+    ra.num_topk = K;
+    ra.hidden = H;
+    ra.send_head = send_head.data_ptr<int>();
+    ra.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
+    ra.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
+    ra.num_tokens = N;
+    ra.has_weights = topk_weights.has_value() ? 1 : 0;
+    ra.bias0 = bias_0.has_value() ? bias_0->data_ptr() : nullptr;
+    ra.bias1 = bias_1.has_value() ? bias_1->data_ptr() : nullptr;
+    ra.out = out.data_ptr();
+    ra.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
+    ra.seq = seq;
+    ra.st = st;
+    launch_combine_reduce(ra, num_sms, stream);
+    EP_CUDA_CHECK(cudaGetLastError());
+    auto event = scope.finish(async, {x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, out, out_w});
+    return {out, out_w, event};
+}
+
+void Buffer::barrier(bool use_comm_stream, bool with_cpu_sync) {
+    check_error();
+    if (with_cpu_sync) EP_CUDA_CHECK(cudaDeviceSynchronize());
+    auto compute = at::cuda::getCurrentCUDAStream();
+    auto stream = use_comm_stream ? comm_stream_ : compute;
+    if (use_comm_stream) stream_wait(comm_stream_, compute);
+    const int epoch = ++barrier_epoch_;
+    launch_barrier(nvl_peers(), 0, rank_, num_ranks_, epoch, status(), stream.stream());
+    if (use_comm_stream) stream_wait(compute, comm_stream_);
+    if (with_cpu_sync) {
+        EP_CUDA_CHECK(cudaDeviceSynchronize());
+        check_error();
+    }
+}
+
+// =================================================================================================
+// Low-latency mode
+// =================================================================================================
+void Buffer::clean_low_latency_buffer(int num_max_dispatch_tokens_per_rank, int hidden, int num_experts) {
+    TORCH_CHECK(ll_base_ != nullptr, "no low-latency region (num_rdma_bytes == 0)");
+    const LLLayout L = compute_ll_layout(num_rdma_bytes_, num_max_dispatch_tokens_per_rank, hidden, num_experts, num_ranks_);
+    TORCH_CHECK(2 * L.half_bytes <= num_rdma_bytes_, "low-latency region too small");
+    barrier(true, true);
+    launch_ll_clean(ll_peers(), L, rank_, status(), comm_stream_.stream());
+    barrier(true, true);
+}
+
+std::tuple<torch::Tensor, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int,
+           std::optional<EventHandle>, std::optional<std::function<void()>>>
+Buffer::low_latency_dispatch(const torch::Tensor& x, const torch::Tensor& topk_idx,
+                             const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats,
+                             const std::optional<torch::Tensor>& dispatch_wait_recv_cost_stats,
+                             int num_max_dispatch_tokens_per_rank, int num_experts, bool use_fp8, bool round_scale,
+                             bool use_ue8m0, bool async, bool return_recv_hook) {
+    check_error();
+    TORCH_CHECK(available_ && ll_base_ != nullptr, "low-latency mode needs num_rdma_bytes > 0");
+    TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16, "x must be contiguous bf16");
+    TORCH_CHECK(topk_idx.dim() == 2 && topk_idx.is_contiguous() && topk_idx.scalar_type() == torch::kInt64);
+    TORCH_CHECK(!use_ue8m0 || round_scale, "use_ue8m0 requires round_scale");
+    const int N = (int)x.size(0), H = (int)x.size(1), K = (int)topk_idx.size(1), R = num_ranks_;
+    const int maxT = num_max_dispatch_tokens_per_rank;
+    TORCH_CHECK(N <= maxT, "num_tokens exceeds num_max_dispatch_tokens_per_rank");
+    TORCH_CHECK(H % 128 == 0 && K <= kMaxTopk && num_experts % R == 0);
+    LLLayout L = compute_ll_layout(num_rdma_bytes_, maxT, H, num_experts, R);
+    TORCH_CHECK(2 * L.half_bytes <= num_rdma_bytes_, "low-latency region too small: need " + std::to_string(2 * L.half_bytes) +
+                                                         " bytes (Buffer.get_low_latency_rdma_size_hint)");
+    TORCH_CHECK(L.num_local_experts <= kMaxLocalExperts);
+    L.num_topk = K;
+    const int seq = ++ll_dispatch_seq_;
+    const int half = seq & 1;
+    const int E_l = L.num_local_experts, slots = R * maxT;
+
+    auto compute = at::cuda::getCurrentCUDAStream();
+    auto launch_stream = return_recv_hook ? compute : comm_stream_;
+    if (!return_recv_hook) stream_wait(comm_stream_, compute);
+    auto i32 = torch::dtype(torch::kInt32).device(torch::kCUDA);
+    auto recv_count = torch::empty({E_l}, i32);
+    auto layout_range = torch::empty({E_l, R}, torch::dtype(torch::kInt64).device(torch::kCUDA));
+    if (return_recv_hook || async) {
+        recv_count.record_stream(launch_stream);
+        layout_range.record_stream(launch_stream);
+    }
+
+    LLDispatchArgs a{};
+    a.peers = ll_peers();
+    a.layout = L;
+    a.half = half;
+    a.x = x.data_ptr();
+    a.topk_idx = topk_idx.data_ptr<int64_t>();
+    a.num_tokens = N;
+    a.rank = rank_;
+    a.use_fp8 = use_fp8 ? 1 : 0;
+    a.round_scale = round_scale ? 1 : 0;
+    a.use_ue8m0 = use_ue8m0 ? 1 : 0;
+    a.seq = seq;
+    a.mask = mask_;
+    a.shrink = enable_shrink_ ? 1 : 0;
+    a.recv_count = recv_count.data_ptr<int>();
+    a.layout_range = layout_range.data_ptr<int64_t>();
+    a.cumulative_stats = cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
+    a.wait_stats = dispatch_wait_recv_cost_stats.has_value() ? dispatch_wait_recv_cost_stats->data_ptr<int64_t>() : nullptr;
+    a.st = status();
+    a.phases = return_recv_hook ? 1 : 3;
+    launch_ll_dispatch(a, launch_stream.stream());
+    EP_CUDA_CHECK(cudaGetLastError());
+
+    uint8_t* half_base = static_cast<uint8_t*>(ll_base_) + (int64_t)half * L.half_bytes;
+    auto dev = torch::TensorOptions().device(torch::kCUDA, device_id_);
+    auto recv_x = torch::from_blob(half_base + L.recv_x_off, {E_l, slots, H}, dev.dtype(use_fp8 ? torch::kFloat8_e4m3fn : torch::kBFloat16));
+    std::optional<torch::Tensor> recv_scales;
+    if (use_fp8) {
+        const int nb = H / 128;
+        recv_scales = torch::from_blob(half_base + L.recv_scales_off, {E_l, slots, nb}, {(int64_t)nb * slots, 1, slots},
+                                       dev.dtype(torch::kFloat32));
+    }
+    auto src_info = torch::from_blob(half_base + L.recv_src_info_off, {E_l, slots}, dev.dtype(torch::kInt32));
+    auto src_meta = torch::from_blob(half_base + L.recv_src_meta_off, {E_l, slots}, dev.dtype(torch::kInt32));
+
+    std::optional<EventHandle> event;
+    std::optional<std::function<void()>> hook;
+    if (return_recv_hook) {
+        LLDispatchArgs ra = a;
+        ra.phases = 2;
+        hook = [ra, recv_count, layout_range, this]() mutable {
+            check_error();
+            launch_ll_dispatch(ra, at::cuda::getCurrentCUDAStream().stream());
+        };
+    } else if (async) {
+        event = EventHandle(comm_stream_);
+        x.record_stream(comm_stream_);
+        topk_idx.record_stream(comm_stream_);
+    } else {
+        stream_wait(compute, comm_stream_);
+    }
+    return {recv_x, recv_scales, recv_count, src_info, src_meta, layout_range, half, event, hook};
+}
+
+std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::function<void()>>> Buffer::low_latency_combine(
+    const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights, const torch::Tensor& recv_count,
+    int dispatch_half, const std::optional<torch::Tensor>& combine_wait_recv_cost_stats, int num_max_dispatch_tokens_per_rank,
+    int num_experts, bool use_logfmt, bool zero_copy, bool async, bool return_recv_hook, const std::optional<torch::Tensor>& out) {
+    check_error();
+    TORCH_CHECK(available_ && ll_base_ != nullptr, "low-latency mode needs num_rdma_bytes > 0");
+    TORCH_CHECK(!use_logfmt, "LogFMT combine is not supported by this build");
+    const int R = num_ranks_, maxT = num_max_dispatch_tokens_per_rank;
+    TORCH_CHECK(x.dim() == 3 && x.scalar_type() == torch::kBFloat16 && x.is_contiguous());
+    const int H = (int)x.size(2), N = (int)topk_idx.size(0), K = (int)topk_idx.size(1);
+    TORCH_CHECK(topk_weights.scalar_type() == torch::kFloat32 && topk_weights.is_contiguous() && topk_weights.size(0) == N);
+    TORCH_CHECK(N <= maxT && K <= kMaxTopk);
+    LLLayout L = compute_ll_layout(num_rdma_bytes_, maxT, H, num_experts, R);
+    TORCH_CHECK(2 * L.half_bytes <= num_rdma_bytes_, "low-latency region too small");
+    TORCH_CHECK(x.size(0) == L.num_local_experts && x.size(1) == (int64_t)R * maxT, "x must be [num_local_experts, num_ranks * max_tokens, hidden]");
+    L.num_topk = K;
+    const int seq = ++ll_combine_seq_;
+    const int half = seq & 1;
+    auto compute = at::cuda::getCurrentCUDAStream();
+    auto launch_stream = return_recv_hook ? compute : comm_stream_;
+    if (!return_recv_hook) stream_wait(comm_stream_, compute);
+    torch::Tensor combined = out.has_value() ? *out : torch::empty({N, H}, x.options());
+    TORCH_CHECK(combined.is_contiguous() && combined.size(0) == N && combined.size(1) == H && combined.scalar_type() == torch::kBFloat16);
+
+    LLCombineArgs a{};
+    a.peers = ll_peers();
+    a.layout = L;
+    a.half = half;
+    a.dispatch_half = dispatch_half;
+    const void* src = x.data_ptr();
+    if (zero_copy) {
+        // The caller filled the registered send buffer of this combine's half.
+        src = static_cast<uint8_t*>(ll_base_) + (int64_t)half * L.half_bytes + L.combine_send_off;
+    }
+    a.x = src;
+    a.recv_count = recv_count.data_ptr<int>();
+    a.topk_idx = topk_idx.data_ptr<int64_t>();
+    a.topk_weights = topk_weights.data_ptr<float>();
+    a.num_tokens = N;
+    a.rank = rank_;
+    a.seq = seq;
+    a.mask = mask_;
+    a.shrink = enable_shrink_ ? 1 : 0;
+    a.out = combined.data_ptr();
+    a.wait_stats = combine_wait_recv_cost_stats.has_value() ? combine_wait_recv_cost_stats->data_ptr<int64_t>() : nullptr;
+    a.st = status();
+    a.phases = return_recv_hook ? 1 : 3;
+    launch_ll_combine(a, launch_stream.stream());
+    EP_CUDA_CHECK(cudaGetLastError());
+
+    std::optional<EventHandle> event;
+    std::optional<std::function<void()>> hook;
+    if (return_recv_hook) {
+        LLCombineArgs ra = a;
+        ra.phases = 2;
+        hook = [ra, combined, topk_idx, topk_weights, this]() mutable {
+            check_error();
+            launch_ll_combine(ra, at::cuda::getCurrentCUDAStream().stream());
+        };
+    } else if (async) {
+        event = EventHandle(comm_stream_);
+        for (auto t : {x, topk_idx, topk_weights, recv_count, combined}) t.record_stream(comm_stream_);
+    } else {
+        stream_wait(compute, comm_stream_);
+    }
+    return {combined, event, hook};
+}
+
+torch::Tensor Buffer::get_next_low_latency_combine_buffer(int num_max_dispatch_tokens_per_rank, int hidden, int num_experts) {
+    TORCH_CHECK(ll_base_ != nullptr, "no low-latency region");
+    const LLLayout L = compute_ll_layout(num_rdma_bytes_, num_max_dispatch_tokens_per_rank, hidden, num_experts, num_ranks_);
+    const int half = (ll_combine_seq_ + 1) & 1;
+    uint8_t* base = static_cast<uint8_t*>(ll_base_) + (int64_t)half * L.half_bytes + L.combine_send_off;
+    return torch::from_blob(base, {L.num_local_experts, (int64_t)num_ranks_ * num_max_dispatch_tokens_per_rank, hidden},
+                            torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, device_id_));
+}
+
+void Buffer::low_latency_update_mask_buffer(int rank_to_mask, bool mask) {
+    TORCH_CHECK(enable_shrink_, "mask APIs need enable_shrink=True");
+    TORCH_CHECK(rank_to_mask >= 0 && rank_to_mask < num_ranks_);
+    const int v = mask ? 1 : 0;
+    EP_CUDA_CHECK(cudaMemcpyAsync(mask_ + rank_to_mask, &v, sizeof(int), cudaMemcpyHostToDevice, at::cuda::getCurrentCUDAStream()));
+    EP_CUDA_CHECK(cudaStreamSynchronize(at::cuda::getCurrentCUDAStream()));
+}
+
+void Buffer::low_latency_query_mask_buffer(const torch::Tensor& mask_status) {
+    TORCH_CHECK(enable_shrink_, "mask APIs need enable_shrink=True");
+    TORCH_CHECK(mask_status.numel() == num_ranks_ && mask_status.scalar_type() == torch::kInt32 && mask_status.is_cuda());
+    EP_CUDA_CHECK(cudaMemcpyAsync(mask_status.data_ptr(), mask_, sizeof(int) * num_ranks_, cudaMemcpyDeviceToDevice,
+                                  at::cuda::getCurrentCUDAStream()));
+}
+
+void Buffer::low_latency_clean_mask_buffer() {
+    TORCH_CHECK(enable_shrink_, "mask APIs need enable_shrink=True");
+    EP_CUDA_CHECK(cudaMemsetAsync(mask_, 0, sizeof(int) * kMaxRanks, at::cuda::getCurrentCUDAStream()));
+}
+
+}  // namespace ep

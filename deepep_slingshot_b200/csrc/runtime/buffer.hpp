@@ -1,0 +1,169 @@
+// C++ runtime of the B200 expert-parallel buffer (the reference's legacy `Buffer` runtime,
+// [DE]csrc/legacy/buffer.hpp:84-1792, and its `Config`, [DE]csrc/legacy/config.hpp:24-188),
+// re-designed for one NVLink 5 / NVSwitch domain:
+//  * two symmetric regions per rank, each a cudaMalloc allocation shared through CUDA IPC handles
+//    that Python all-gathers over torch.distributed: the normal-mode region (`num_nvl_bytes`) and the
+//    low-latency region (`num_rdma_bytes`; on one box the LL traffic is NVLink peer stores too);
+//  * peer tables passed by value to every kernel; no NIC, no NVSHMEM, no proxy thread;
+//  * host-mapped counters for the CPU sync of received counts, a host-mapped error page and a device
+//    abort flag: every kernel wait is bounded and reports, the host turns reports into exceptions.
+#pragma once
+
+#include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CUDAEvent.h>
+#include <c10/cuda/CUDAStream.h>
+#include <pybind11/functional.h>
+#include <pybind11/pybind11.h>
+#include <torch/extension.h>
+
+#include <functional>
+#include <memory>
+#include <optional>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../include/ep/abi.h"
+#include "../kernels/api.h"
+
+namespace ep {
+
+// Tuning/config object kept for API parity ([DE]csrc/legacy/config.hpp:24-51). On NVLink with the
+// pull/push design only `num_sms` drives the kernels; the chunk sizes are accepted and stored.
+struct Config {
+    int num_sms;
+    int num_max_nvl_chunked_send_tokens;
+    int num_max_nvl_chunked_recv_tokens;
+    int num_max_rdma_chunked_send_tokens;
+    int num_max_rdma_chunked_recv_tokens;
+    Config(int num_sms, int nvl_send, int nvl_recv, int rdma_send, int rdma_recv)
+        : num_sms(num_sms),
+          num_max_nvl_chunked_send_tokens(nvl_send),
+          num_max_nvl_chunked_recv_tokens(nvl_recv),
+          num_max_rdma_chunked_send_tokens(rdma_send),
+          num_max_rdma_chunked_recv_tokens(rdma_recv) {}
+    // Size of the normal-mode region for `num_max_tokens` tokens per rank (default 4096, top-8).
+    int64_t get_nvl_buffer_size_hint(int64_t hidden_bytes, int num_ranks, int num_max_tokens = 4096, int num_topk = 8) const;
+    int64_t get_rdma_buffer_size_hint(int64_t hidden_bytes, int num_ranks) const;
+};
+
+struct EventHandle {
+    std::shared_ptr<at::cuda::CUDAEvent> event;
+    EventHandle();
+    explicit EventHandle(const at::cuda::CUDAStream& stream);
+    void current_stream_wait() const;
+};
+
+NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ranks);
+int64_t normal_region_size_for(int num_max_tokens, int hidden, int num_ranks);
+RecordFormat record_format(int hidden, int num_topk, bool fp8);
+LLLayout compute_ll_layout(int64_t region_bytes, int max_tokens, int hidden, int num_experts, int num_ranks);
+int64_t ll_region_size_for(int max_tokens, int hidden, int num_ranks, int num_experts);
+
+class Buffer {
+   public:
+    Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_bytes, bool low_latency_mode,
+           bool explicitly_destroy, bool enable_shrink, double gpu_timeout_secs);
+    ~Buffer() noexcept(false);
+
+    bool is_available() const { return available_; }
+    int get_num_rdma_ranks() const { return 1; }
+    int get_rdma_rank() const { return 0; }
+    int get_root_rdma_rank(bool global) const { return global ? 0 : 0; }
+    int get_local_device_id() const { return device_id_; }
+    pybind11::bytearray get_local_ipc_handle() const;
+    pybind11::bytearray get_local_ll_ipc_handle() const;
+    void sync(const std::vector<int>& device_ids, const std::vector<std::optional<pybind11::bytearray>>& handles,
+              const std::vector<std::optional<pybind11::bytearray>>& ll_handles);
+    void destroy();
+    torch::Stream get_comm_stream() const;
+    torch::Tensor get_local_buffer_tensor(const pybind11::object& dtype, int64_t offset, bool use_rdma_buffer) const;
+    int64_t get_capacity(int hidden, int num_topk) const;
+
+    void check_error() const;
+    std::tuple<int, int, int, int> get_error_state() const;
+    void clear_error();
+    void set_timeout_secs(double secs);
+
+    // ---------------------------------------------------------------- normal mode
+    std::tuple<torch::Tensor, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, std::optional<EventHandle>>
+    get_dispatch_layout(const torch::Tensor& topk_idx, int num_experts, std::optional<EventHandle>& previous_event,
+                        bool async, bool allocate_on_comm_stream);
+
+    std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<torch::Tensor>, std::optional<torch::Tensor>,
+               std::vector<int>, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+               std::optional<torch::Tensor>, std::optional<EventHandle>>
+    intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Tensor>& x_scales,
+                       const std::optional<torch::Tensor>& topk_idx, const std::optional<torch::Tensor>& topk_weights,
+                       const std::optional<torch::Tensor>& is_token_in_rank, int num_experts,
+                       const std::optional<torch::Tensor>& cached_rank_prefix_matrix,
+                       const std::optional<torch::Tensor>& cached_send_prefix_matrix,
+                       const std::optional<torch::Tensor>& cached_recv_src_idx,
+                       const std::optional<torch::Tensor>& cached_send_head, int expert_alignment,
+                       int num_worst_tokens, bool quantize_fp8, bool round_scale, bool scales_col_major,
+                       const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats, int num_sms,
+                       std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream);
+
+    std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandle>> intranode_combine(
+        const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
+        const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,
+        const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, int num_sms,
+        std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream);
+
+    void barrier(bool use_comm_stream, bool with_cpu_sync);
+
+    // ---------------------------------------------------------------- low-latency mode
+    void clean_low_latency_buffer(int num_max_dispatch_tokens_per_rank, int hidden, int num_experts);
+    std::tuple<torch::Tensor, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int,
+               std::optional<EventHandle>, std::optional<std::function<void()>>>
+    low_latency_dispatch(const torch::Tensor& x, const torch::Tensor& topk_idx,
+                         const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats,
+                         const std::optional<torch::Tensor>& dispatch_wait_recv_cost_stats,
+                         int num_max_dispatch_tokens_per_rank, int num_experts, bool use_fp8, bool round_scale,
+                         bool use_ue8m0, bool async, bool return_recv_hook);
+    std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::function<void()>>> low_latency_combine(
+        const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights,
+        const torch::Tensor& recv_count, int dispatch_half, const std::optional<torch::Tensor>& combine_wait_recv_cost_stats,
+        int num_max_dispatch_tokens_per_rank, int num_experts, bool use_logfmt, bool zero_copy, bool async,
+        bool return_recv_hook, const std::optional<torch::Tensor>& out);
+    torch::Tensor get_next_low_latency_combine_buffer(int num_max_dispatch_tokens_per_rank, int hidden, int num_experts);
+    void low_latency_update_mask_buffer(int rank_to_mask, bool mask);
+    void low_latency_query_mask_buffer(const torch::Tensor& mask_status);
+    void low_latency_clean_mask_buffer();
+
+    int rank() const { return rank_; }
+    int num_ranks() const { return num_ranks_; }
+
+   private:
+    KernelStatus status() const;
+    PeerTable nvl_peers() const;
+    PeerTable ll_peers() const;
+    void wait_host_counters(int epoch);
+
+    int rank_, num_ranks_, device_id_;
+    int64_t num_nvl_bytes_, num_rdma_bytes_;
+    bool low_latency_mode_, explicitly_destroy_, enable_shrink_;
+    bool available_ = false, destroyed_ = false;
+    uint64_t timeout_ns_;
+
+    void* nvl_base_ = nullptr;
+    void* ll_base_ = nullptr;
+    cudaIpcMemHandle_t nvl_ipc_{}, ll_ipc_{};
+    void* nvl_peer_[kMaxRanks] = {};
+    void* ll_peer_[kMaxRanks] = {};
+    bool nvl_peer_opened_[kMaxRanks] = {};
+    bool ll_peer_opened_[kMaxRanks] = {};
+
+    // host-mapped error page and counters
+    ErrorState* host_error_ = nullptr;
+    ErrorState* host_error_dev_ = nullptr;
+    HostCounters* host_counters_ = nullptr;
+    HostCounters* host_counters_dev_ = nullptr;
+    int* dev_workspace_ = nullptr;  // [0] abort flag, [1] num_recv, [2..] scratch
+    int* mask_ = nullptr;           // [kMaxRanks] shrink-mode mask
+
+    at::cuda::CUDAStream comm_stream_;
+    int dispatch_epoch_ = 0, combine_seq_ = 0, barrier_epoch_ = 0, ll_dispatch_seq_ = 0, ll_combine_seq_ = 0;
+};
+
+}  // namespace ep

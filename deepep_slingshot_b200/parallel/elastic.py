@@ -1,0 +1,194 @@
+"""`ElasticBuffer` / `EPHandle`: the reference's v2 API ([DE]deep_ep/buffers/elastic.py:24-928) on B200.
+
+One NVLink domain: the logical and physical domains are (1 scale-out rank, R scale-up ranks); the
+hybrid (RDMA + NVLink) mode, QPs and service levels are accepted and have no effect. Dispatch and
+combine run on the same sm_100a NVLink kernels as `Buffer` (pull-dispatch from the sources' staging,
+push-combine + fp32 reduce), with the layout computed inside the dispatch (no separate layout call).
+"""
+import math
+import os
+from typing import Optional, Tuple, Union
+
+import torch
+import torch.distributed as dist
+
+from .._ext import require_ext
+from ..utils.event import EventOverlap
+from ..utils.envs import get_nvlink_gbs
+from ..utils.math import align
+from .buffer import Buffer
+
+
+class EPHandle:
+    """Routing state returned by `ElasticBuffer.dispatch`, reusable as a cached handle and consumed by
+    `combine` (fields follow [DE]deep_ep/buffers/elastic.py:24-87)."""
+
+    def __init__(self, do_expand: bool, num_experts: int, expert_alignment: int, num_max_tokens_per_rank: int,
+                 num_sms: int, topk_idx: torch.Tensor, num_recv_tokens_per_expert_list: list,
+                 psum_num_recv_tokens_per_scaleup_rank: torch.Tensor, psum_num_recv_tokens_per_expert: torch.Tensor,
+                 recv_src_metadata: torch.Tensor, legacy_handle: tuple):
+        self.do_expand = do_expand
+        self.num_experts = num_experts
+        self.expert_alignment = expert_alignment
+        self.num_max_tokens_per_rank = num_max_tokens_per_rank
+        self.num_sms = num_sms
+        self.topk_idx = topk_idx
+        self.num_recv_tokens_per_expert_list = num_recv_tokens_per_expert_list
+        self.psum_num_recv_tokens_per_scaleup_rank = psum_num_recv_tokens_per_scaleup_rank
+        self.psum_num_recv_tokens_per_expert = psum_num_recv_tokens_per_expert
+        self.recv_src_metadata = recv_src_metadata
+        self.dst_buffer_slot_idx = legacy_handle[5]
+        self.token_metadata_at_forward = None
+        self.channel_linked_list = None
+        self.legacy_handle = legacy_handle
+        self.num_recv_tokens = recv_src_metadata.shape[0]
+
+
+class ElasticBuffer:
+    """Elastic EP buffer (v2 API) over one NVLink 5 / NVSwitch domain."""
+
+    def __init__(self, group: dist.ProcessGroup, num_bytes: Optional[int] = None, num_cpu_bytes: int = 0,
+                 num_max_tokens_per_rank: int = 0, hidden: int = 0, num_topk: int = 0, use_fp8_dispatch: bool = False,
+                 deterministic: bool = False, allow_hybrid_mode: bool = True, allow_multiple_reduction: bool = True,
+                 prefer_overlap_with_compute: bool = True, sl_idx: int = 3, num_allocated_qps: int = 0,
+                 num_cpu_timeout_secs: int = 300, num_gpu_timeout_secs: int = 100,
+                 explicitly_destroy: bool = False) -> None:
+        _C = require_ext()
+        self.group = group
+        self.rank_idx = group.rank()
+        self.num_ranks = group.size()
+        self.allow_hybrid_mode = allow_hybrid_mode
+        self.allow_multiple_reduction = allow_multiple_reduction
+        self.prefer_overlap_with_compute = prefer_overlap_with_compute
+        self.deterministic = deterministic
+        if num_bytes is None:
+            num_bytes = self.get_buffer_size_hint(group, num_max_tokens_per_rank, hidden, num_topk, use_fp8_dispatch)
+        if os.environ.get('EP_BUFFER_DEBUG', 0):
+            print(f'Initializing EP elastic buffer with {num_bytes} bytes at rank {self.rank_idx}/{self.num_ranks}')
+        self.num_bytes = num_bytes
+        self.num_max_tokens_per_rank = num_max_tokens_per_rank
+        self.num_allocated_qps = num_allocated_qps or 17
+        self.explicitly_destroy = explicitly_destroy
+        self._buffer = Buffer(group, num_nvl_bytes=num_bytes, num_rdma_bytes=0, explicitly_destroy=explicitly_destroy,
+                              num_gpu_timeout_secs=num_gpu_timeout_secs)
+        self.runtime = self._buffer.runtime
+        self.num_scaleout_ranks, self.num_scaleup_ranks = 1, self.num_ranks
+        self.scaleout_rank_idx, self.scaleup_rank_idx = 0, self.rank_idx
+        self.num_rdma_ranks, self.num_nvlink_ranks = 1, self.num_ranks
+        torch.cuda.synchronize()
+        group.barrier()
+
+    def destroy(self) -> None:
+        assert self.explicitly_destroy
+        if self._buffer is not None:
+            self._buffer.destroy()
+            self._buffer = None
+            self.runtime = None
+
+    @staticmethod
+    def get_buffer_size_hint(group: dist.ProcessGroup, num_max_tokens_per_rank: int, hidden: int, num_topk: int = 0,
+                             use_fp8_dispatch: bool = False, allow_hybrid_mode: bool = True,
+                             allow_multiple_reduction: bool = True) -> int:
+        return require_ext().normal_region_size_for(max(num_max_tokens_per_rank, 1), max(hidden, 128), group.size())
+
+    @staticmethod
+    def get_elastic_buffer_alignment() -> int:
+        return 2 << 20
+
+    def barrier(self, use_comm_stream: bool = True, with_cpu_sync: bool = False) -> None:
+        self._buffer.barrier(use_comm_stream, with_cpu_sync)
+
+    @staticmethod
+    def capture():
+        return require_ext().EventHandle()
+
+    def get_comm_stream(self) -> torch.cuda.Stream:
+        return self._buffer.get_comm_stream()
+
+    def get_physical_domain_size(self) -> Tuple[int, int]:
+        return 1, self.num_ranks
+
+    def get_logical_domain_size(self) -> Tuple[int, int]:
+        return 1, self.num_ranks
+
+    def get_theoretical_num_sms(self, num_experts: int, num_topk: int, num_scaleout_topk: int = 0,
+                                rdma_gbs: float = 0, nvlink_gbs: float = 0, sm_read_gbs: float = 200,
+                                sm_write_gbs: float = 50) -> int:
+        """SM count for the NVLink kernels from a bandwidth model: each SM sustains about `sm_write_gbs`
+        of NVLink traffic; size the grid so the link (not the SMs) is the bottleneck, with 25% headroom."""
+        if self.num_ranks == 1:
+            return torch.cuda.get_device_properties('cuda').multi_processor_count // 2
+        nvlink_gbs = nvlink_gbs or get_nvlink_gbs()
+        remote_fraction = 1 - 1 / self.num_ranks
+        num_sms = math.ceil(nvlink_gbs * remote_fraction / sm_write_gbs * 1.25)
+        num_sms = align(max(num_sms, 8), 2)
+        if not self.prefer_overlap_with_compute:
+            num_sms = max(num_sms, 64)
+        return min(num_sms, torch.cuda.get_device_properties('cuda').multi_processor_count)
+
+    def get_theoretical_num_qps(self, num_sms: int) -> int:
+        return min(num_sms, 8 + 1)
+
+    def dispatch(self, x: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]],
+                 topk_idx: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
+                 cumulative_local_expert_recv_stats: Optional[torch.Tensor] = None, num_experts: Optional[int] = None,
+                 num_max_tokens_per_rank: Optional[int] = None, expert_alignment: Optional[int] = None,
+                 num_sms: int = 0, num_qps: int = 0, previous_event=None, previous_event_before_epilogue=None,
+                 async_with_compute_stream: bool = False, allocate_on_comm_stream: bool = False,
+                 handle: Optional[EPHandle] = None, do_handle_copy: bool = True, do_cpu_sync: Optional[bool] = None,
+                 do_expand: bool = False, use_tma_aligned_col_major_sf: bool = False, quantize_fp8: bool = False,
+                 round_scale: bool = False):
+        if do_expand:
+            raise NotImplementedError('expanded dispatch layout: use ops.permute on the non-expanded result')
+        x, sf = x if isinstance(x, tuple) else (x, None)
+        if handle is not None:
+            assert topk_idx is None and topk_weights is None
+            assert not do_cpu_sync, 'Cannot do CPU sync with cached handle'
+            num_experts = num_experts or handle.num_experts
+            num_sms = num_sms or handle.num_sms
+            prev = previous_event
+            rpm, spm, rrp, src_idx, itir, send_head = handle.legacy_handle
+            out = self.runtime.intranode_dispatch(
+                x, sf, None, None, None, 0, rpm, spm, src_idx, send_head, handle.expert_alignment, 0, quantize_fp8,
+                round_scale, use_tma_aligned_col_major_sf, None, num_sms, prev, async_with_compute_stream,
+                allocate_on_comm_stream)
+            recv_x = (out[0], out[1]) if out[1] is not None else out[0]
+            return recv_x, None, None, handle, EventOverlap(out[11])
+        assert topk_idx is not None and num_experts is not None
+        num_topk = topk_idx.shape[1]
+        num_sms = self.get_theoretical_num_sms(num_experts, num_topk) if num_sms == 0 else num_sms
+        num_max_tokens_per_rank = num_max_tokens_per_rank or self.num_max_tokens_per_rank or x.shape[0]
+        expert_alignment = expert_alignment or 1
+        do_cpu_sync = True if do_cpu_sync is None else do_cpu_sync
+        num_worst = 0 if do_cpu_sync else num_max_tokens_per_rank * self.num_ranks
+        (recv_x, recv_sf, recv_topk_idx, recv_topk_weights, per_expert_list, rpm, spm, rrp, src_idx, send_head,
+         per_expert_dev, event) = self.runtime.intranode_dispatch(
+            x, sf, topk_idx, topk_weights, None, num_experts, None, None, None, None, expert_alignment, num_worst,
+            quantize_fp8, round_scale, use_tma_aligned_col_major_sf, cumulative_local_expert_recv_stats, num_sms,
+            previous_event, async_with_compute_stream, allocate_on_comm_stream)
+        is_token_in_rank = send_head >= 0
+        legacy = (rpm, spm, rrp, src_idx, is_token_in_rank, send_head)
+        # source metadata: [global source token index, source rank]
+        num_rows = src_idx.shape[0]
+        src_rank = torch.searchsorted(rrp[1:].to(torch.int64),
+                                      torch.arange(num_rows, device=src_idx.device, dtype=torch.int64), right=True)
+        src_rank = src_rank.clamp_(max=self.num_ranks - 1).to(torch.int32)
+        recv_src_metadata = torch.stack([src_rank * num_max_tokens_per_rank + src_idx, src_rank], dim=1)
+        psum_expert = per_expert_dev.cumsum(0).to(torch.int32)
+        ep_handle = EPHandle(False, num_experts, expert_alignment, num_max_tokens_per_rank, num_sms,
+                             topk_idx.clone() if do_handle_copy else topk_idx, per_expert_list, rrp[1:], psum_expert,
+                             recv_src_metadata, legacy)
+        out_x = (recv_x, recv_sf) if recv_sf is not None else recv_x
+        return out_x, recv_topk_idx, recv_topk_weights, ep_handle, EventOverlap(event)
+
+    def combine(self, x: torch.Tensor, handle: EPHandle, topk_weights: Optional[torch.Tensor] = None,
+                bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None, num_sms: int = 0,
+                num_qps: int = 0, previous_event=None, previous_event_before_epilogue=None,
+                async_with_compute_stream: bool = False, allocate_on_comm_stream: bool = False):
+        num_sms = handle.num_sms if num_sms == 0 else num_sms
+        rpm, spm, _, _, _, send_head = handle.legacy_handle
+        bias_0, bias_1 = Buffer._unpack_bias(bias)
+        combined_x, combined_w, event = self.runtime.intranode_combine(
+            x, topk_weights, bias_0, bias_1, rpm, spm, send_head, num_sms, previous_event, async_with_compute_stream,
+            allocate_on_comm_stream)
+        return combined_x, combined_w, EventOverlap(event)

@@ -1,0 +1,102 @@
+"""Small numeric helpers and the pure-torch FP8 reference casts.
+
+Parity with the reference's `deep_ep/utils/math.py` ([DE]deep_ep/utils/math.py:5-103): `calc_diff`,
+`ceil_div`, `align`, `per_token_cast_to_fp8` (1x128 amax, scale = amax/448, amax clamped at 1e-4),
+`per_token_cast_back` (also accepts packed UE8M0 scales), `inplace_unique`, `count_bytes`, hashes.
+The torch versions here are the numerics oracle of the sm_100a cast kernels (`ops.quant`).
+"""
+from typing import Tuple
+
+import torch
+
+
+def calc_diff(x: torch.Tensor, y: torch.Tensor) -> float:
+    x, y = x.double() + 1, y.double() + 1
+    denominator = (x * x + y * y).sum()
+    sim = 2 * (x * y).sum() / denominator
+    return (1 - sim).item()
+
+
+def safe_div(a, b) -> float:
+    if b == 0:
+        if a == 0:
+            return 0
+        raise ZeroDivisionError
+    return a / b
+
+
+def ceil_div(x: int, y: int) -> int:
+    return (x + y - 1) // y
+
+
+def align(x: int, y: int) -> int:
+    return ceil_div(x, y) * y
+
+
+def per_token_cast_to_fp8(x: torch.Tensor, round_scale: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16/fp32 [m, n] -> (fp8 e4m3 [m, n], fp32 scales [m, ceil(n/128)])."""
+    assert x.dim() == 2
+    m, n = x.shape
+    aligned_n = align(n, 128)
+    x_padded = torch.nn.functional.pad(x, (0, aligned_n - n), mode='constant', value=0)
+    x_view = x_padded.view(m, -1, 128)
+    x_amax = x_view.abs().float().amax(dim=2).view(m, -1).clamp(1e-4)
+    if round_scale:
+        scale = torch.pow(2.0, torch.ceil(torch.log2(x_amax / 448.0)))
+        q = (x_view.float() * (1.0 / scale).unsqueeze(2))
+    else:
+        scale = x_amax / 448.0
+        q = x_view.float() * (448.0 / x_amax.unsqueeze(2))
+    q = q.clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(m, aligned_n)[:, :n].contiguous(), scale.view(m, -1)
+
+
+def per_token_cast_back(x_fp8: torch.Tensor, x_scales: torch.Tensor) -> torch.Tensor:
+    if x_fp8.numel() == 0:
+        return x_fp8.to(torch.bfloat16)
+    assert x_fp8.dim() == 2
+    m, n = x_fp8.shape
+    aligned_n = align(n, 128)
+    x_padded = torch.nn.functional.pad(x_fp8.view(torch.uint8), (0, aligned_n - n), value=0).view(torch.float8_e4m3fn)
+    if x_scales.dtype == torch.int:
+        x_scales = x_scales.view(dtype=torch.uint8).to(torch.int) << 23
+        x_scales = x_scales.view(dtype=torch.float)
+    x_fp32 = x_padded.to(torch.float32).view(m, -1, 128)
+    x_scales = x_scales.reshape(m, -1, 1)
+    return (x_fp32 * x_scales).view(m, aligned_n).to(torch.bfloat16)[:, :n].contiguous()
+
+
+def pack_ue8m0(scales: torch.Tensor) -> torch.Tensor:
+    """fp32 power-of-two scales [..., nb] -> packed UE8M0 int32 [..., nb/4] (exponent bytes, little endian)."""
+    assert scales.shape[-1] % 4 == 0
+    exp = ((scales.contiguous().view(torch.int32) >> 23) & 0xff).to(torch.uint8)
+    return exp.view(*scales.shape[:-1], scales.shape[-1] // 4, 4).contiguous().view(torch.int32).view(*scales.shape[:-1], scales.shape[-1] // 4)
+
+
+def inplace_unique(x: torch.Tensor, num_slots: int) -> None:
+    assert x.dim() == 2
+    mask = x < 0
+    x_padded = x.masked_fill(mask, num_slots)
+    bin_count = torch.zeros((x.size(0), num_slots + 1), dtype=x.dtype, device=x.device)
+    bin_count.scatter_add_(1, x_padded, torch.ones_like(x_padded))
+    bin_count = bin_count[:, :num_slots]
+    sorted_bin_count, sorted_bin_idx = torch.sort(bin_count, dim=-1, descending=True)
+    sorted_bin_idx.masked_fill_(sorted_bin_count == 0, -1)
+    sorted_bin_idx = torch.sort(sorted_bin_idx, descending=True, dim=-1).values
+    x[:, :].fill_(-1)
+    valid_len = min(num_slots, x.size(1))
+    x[:, :valid_len] = sorted_bin_idx[:, :valid_len]
+
+
+def hash_tensor(t: torch.Tensor) -> int:
+    return t.view(torch.int).sum().item()
+
+
+def count_bytes(*tensors) -> int:
+    total = 0
+    for t in tensors:
+        if isinstance(t, (tuple, list)):
+            total += count_bytes(*t)
+        elif t is not None:
+            total += t.numel() * t.element_size()
+    return total

@@ -1,0 +1,44 @@
+"""Build of the sm_100a extension `deepep_slingshot_b200._C` (in-tree: `python setup.py build_ext --inplace`).
+
+Only Blackwell datacenter parts are targeted: every CUDA translation unit is compiled with
+`-gencode arch=compute_100a,code=sm_100a`, which also keeps torch from adding its own arch list.
+"""
+import os
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("deepep_slingshot_b200", "csrc")
+
+SOURCES = [
+    os.path.join(CSRC, "python_api.cpp"),
+    os.path.join(CSRC, "runtime", "buffer.cpp"),
+    os.path.join(CSRC, "runtime", "ops.cpp"),
+    os.path.join(CSRC, "kernels", "intranode.cu"),
+    os.path.join(CSRC, "kernels", "low_latency.cu"),
+    os.path.join(CSRC, "kernels", "quant.cu"),
+]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xptxas", "-v",
+    "--diag-suppress=177,550",
+]
+CXX_FLAGS = ["-O3", "-std=c++17", "-Wno-unused-function"]
+
+setup(
+    name="deepep_slingshot_b200",
+    version="0.1.0",
+    packages=["deepep_slingshot_b200"],
+    ext_modules=[
+        CUDAExtension(
+            name="deepep_slingshot_b200._C",
+            sources=SOURCES,
+            include_dirs=[os.path.join(ROOT, CSRC)],
+            extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

@@ -1,0 +1,52 @@
+"""CPU/gloo plumbing check (world size 2, no GPU): the reference backend's dispatch/combine semantics.
+
+Config: per rank 64 tokens, hidden 256, fp32 ~N(0,1) from seed 0; 8 experts (4 per rank), top-2 of
+N(0,1) router logits, softmax weights over the chosen 2. combine(dispatch(x)) with identity experts
+weighted by the received top-k weights equals x * sum(top-k weights); per-expert receive counts
+from get_dispatch_layout are exact.
+"""
+import torch
+import torch.distributed as dist
+
+from tests._dist import run_ranks
+
+
+def _body(rank, world):
+    from deepep_slingshot_b200 import ReferenceBuffer
+    from deepep_slingshot_b200.utils.gate import normal_routing
+    g = torch.Generator().manual_seed(rank)
+    torch.manual_seed(0)
+    N, H, E, K = 64, 256, 8, 2
+    x = torch.randn((N, H), generator=torch.Generator().manual_seed(rank * 7 + 0))
+    topk_idx, topk_w = normal_routing(N, E, K, generator=g)
+    buf = ReferenceBuffer(dist.group.WORLD)
+    ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(topk_idx, E)
+    # exact per-expert counts: all-reduce of the local counts must equal the global histogram
+    all_idx = [torch.zeros_like(topk_idx) for _ in range(world)]
+    dist.all_gather(all_idx, topk_idx)
+    hist = torch.bincount(torch.cat(all_idx).flatten(), minlength=E).to(torch.int32)
+    tot = ntpe.clone()
+    dist.all_reduce(tot)
+    assert torch.equal(tot, hist)
+    x_bf = x.to(torch.bfloat16)
+    (recv_x, recv_idx, recv_w, per_expert, handle, _) = buf.dispatch(
+        x_bf, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe, topk_idx=topk_idx,
+        topk_weights=topk_w)
+    # receive counts per local expert match the global histogram slice
+    epr = E // world
+    assert per_expert == hist[rank * epr:(rank + 1) * epr].tolist()
+    # identity experts: each received row scaled by the sum of its local weights
+    y = (recv_x.float() * recv_w.sum(dim=1, keepdim=True)).to(torch.bfloat16)
+    out, out_w, _ = buf.combine(y, handle, topk_weights=recv_w)
+    expect = x_bf.float() * topk_w.sum(dim=1, keepdim=True)
+    assert torch.allclose(out.float(), expect, atol=3e-2, rtol=2e-2), (out.float() - expect).abs().max()
+    assert torch.allclose(out_w, topk_w, atol=1e-6)
+    # low-latency reference: weighted combine of identity experts gives x * sum(w) as well
+    recv, cnt, h, _, hook = buf.low_latency_dispatch(x_bf, topk_idx, 64, E, use_fp8=False, return_recv_hook=True)
+    hook()
+    out2, _, _ = buf.low_latency_combine(recv, topk_idx, topk_w, h)
+    assert torch.allclose(out2.float(), expect, atol=3e-2, rtol=2e-2)
+
+
+def test_gloo_world2_plumbing():
+    run_ranks(_body, 2, 'gloo')
