@@ -237,24 +237,58 @@ def main():
         lidx, lw = gate.uniform_routing(T, E, K, generator=gl)
         lidx, lw = lidx.cuda(), lw.cuda()
         ly = torch.randn((E_l, world * T, H), generator=gl).to(torch.bfloat16).cuda()
-        d_us, c_us = [], []
         iters = max(args.steps, 20)
-        for i in range(args.warmup + iters):
-            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            dist.barrier()
-            e0.record()
+
+        def ll_dispatch():
             recv, cnt, hh, _, hook = buf.low_latency_dispatch(lx, lidx, T, E, use_fp8=True, return_recv_hook=True)
             hook()
-            e1.record()
+            return hh
+
+        def ll_combine(hh):
             out, _, chook = buf.low_latency_combine(ly, lidx, lw, hh, return_recv_hook=True)
             chook()
-            e2.record()
-            torch.cuda.synchronize()
-            if i >= args.warmup:
+            return out
+
+        def time_ll(run_d, run_c, n):
+            d_us, c_us = [], []
+            for i in range(n):
+                e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                dist.barrier()
+                torch.cuda.synchronize()
+                e0.record()
+                hh = run_d()
+                e1.record()
+                run_c(hh)
+                e2.record()
+                torch.cuda.synchronize()
                 d_us.append(e0.elapsed_time(e1) * 1e3)
                 c_us.append(e1.elapsed_time(e2) * 1e3)
-        d_us, c_us = max_over_ranks(d_us), max_over_ranks(c_us)
+            return max_over_ranks(d_us), max_over_ranks(c_us)
+
+        time_ll(ll_dispatch, ll_combine, args.warmup)
+        eager_d, eager_c = time_ll(ll_dispatch, ll_combine, iters)
+        # CUDA-graph replay (how decode runs): device time without host launch gaps
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            hh = ll_dispatch()
+            ll_combine(hh)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        gd, gc = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gd):
+            ghh = ll_dispatch()
+        with torch.cuda.graph(gc):
+            ll_combine(ghh)
+        torch.cuda.synchronize()
+        dist.barrier()
+        time_ll(lambda: gd.replay(), lambda _: gc.replay(), args.warmup)
+        d_us, c_us = time_ll(lambda: gd.replay(), lambda _: gc.replay(), iters)
+        del gd, gc
         ll = {'ll_dispatch_us': statistics.median(d_us), 'll_combine_us': statistics.median(c_us),
+              'll_timing': 'CUDA-graph replay, device time, max over ranks, median over iterations',
+              'll_eager_dispatch_us': statistics.median(eager_d), 'll_eager_combine_us': statistics.median(eager_c),
               'll_config': {'tokens_per_rank': T, 'hidden': H, 'experts': E, 'topk': K, 'fp8_dispatch': True,
                             'return_recv_hook': True, 'routing': 'uniform logits'}}
 

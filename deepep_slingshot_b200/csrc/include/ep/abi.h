@@ -72,7 +72,12 @@ struct alignas(128) NormalCtrl {
     int combine_arrived;                    // rows of combine contributions that landed here (reset by reducer)
     int combine_reduced_blocks;             // reducer blocks that finished (reset by the last one)
     int pull_finished_blocks;               // pull blocks that finished (reset by the last one)
-    int pad0[29];
+    // Device-resident sequence numbers (local to this rank). Kernels read and advance them, so no
+    // per-call value is baked into a launch and captured CUDA graphs replay correctly.
+    int dispatch_epoch;                     // last dispatch whose notify completed
+    int combine_seq;                        // last combine whose reduce completed
+    int barrier_epoch;                      // last barrier
+    int pad0[26];
     int token_counts[2][kMaxRanks][kMaxRanks];  // [parity][src][dst] tokens src sends to dst
     int expert_counts[2][kMaxRanks][kMaxLocalExperts];  // [parity][src][local expert] tokens from src
 };
@@ -81,7 +86,7 @@ static_assert(sizeof(NormalCtrl) % 128 == 0, "NormalCtrl alignment");
 // Host-mapped per-buffer workspace read by the CPU after the notify step (the reference's
 // `moe_recv_counter` / `moe_recv_expert_counter`, [DE]csrc/legacy/buffer.hpp:579-597).
 struct HostCounters {
-    int ready_epoch;               // = dispatch epoch when the fields below are valid
+    int ready_ticket;              // = host ticket of the dispatch whose fields below are valid
     int num_recv_tokens;
     int num_local_experts;
     int pad;
@@ -141,12 +146,17 @@ struct LLLayout {
     int32_t num_topk;
 };
 
+// LL flags are set to 1 by the sender and reset to 0 by the receiver once every receive block has
+// seen them (no sequence numbers, so captured CUDA graphs replay). A half is reused two calls later,
+// after the alternation of dispatch/combine has ordered the receiver's reset before the next write.
 struct alignas(128) LLCtrl {
-    int dispatch_done[kMaxRanks];   // [src] = LL dispatch seq once src's messages to me all landed
-    int combine_done[kMaxRanks];    // [src] = LL combine seq once src's rows to me all landed
+    int dispatch_done[kMaxRanks];   // [src] = 1 once src's messages to me all landed
+    int combine_done[kMaxRanks];    // [src] = 1 once src's rows to me all landed
     int send_finished_blocks;       // local: blocks that finished the send phase (reset by last)
     int csend_finished_blocks;
-    int pad[14];
+    int recv_finished_blocks;       // local: dispatch receive blocks that saw every flag
+    int crecv_finished_blocks;
+    int pad[12];
     int slot_counter[kMaxLocalExperts];  // [local expert] slots claimed by senders (remote atomics)
 };
 

@@ -29,7 +29,7 @@ struct StageArgs {
     int quantize;                // 1: fuse bf16 -> fp8 e4m3 1x128 quantization
     int round_scale;             // 1: power-of-two scales
     int num_ranks;
-    int wait_epoch;              // wait until pull_done[r] >= wait_epoch (0: no wait)
+    const int* dispatch_epoch;   // local ctrl.dispatch_epoch: wait until pull_done[r] >= it
     RecordFormat rec;
     int record_stride;
     KernelStatus st;
@@ -42,7 +42,7 @@ struct NotifyArgs {
     int num_tokens, num_topk, num_experts, num_local_experts;
     int num_ranks, rank;
     int cached;                      // 1: only publish readiness and wait (handle reuse)
-    int epoch, parity;
+    int host_ticket;                 // written to host->ready_ticket when the counts are valid
     int expert_alignment;
     PeerTable peers;
     NormalLayout layout;
@@ -75,7 +75,6 @@ struct PullArgs {
     float* recv_topk_weights;        // null allowed
     int* recv_src_idx;               // written for fresh dispatches (null in cached mode)
     const int* cached_src_idx;       // cached mode: source token of every receive row (handle)
-    int epoch;
     int stages;
     KernelStatus st;
 };
@@ -91,7 +90,6 @@ struct CombinePushArgs {
     const int* rank_prefix_matrix;
     const int* send_prefix_matrix;
     int num_recv_max;                // rows available in x; the true count comes from the prefix matrix
-    int seq;
     int stages;
     KernelStatus st;
 };
@@ -110,14 +108,12 @@ struct CombineReduceArgs {
     const void* bias1;
     void* out;                       // bf16 [N][H]
     float* out_topk_weights;         // [N][K] or null
-    int seq;
     KernelStatus st;
 };
 void launch_combine_reduce(const CombineReduceArgs& a, int num_sms, cudaStream_t stream);
 
 // ---------------------------------------------------------------- barrier
-void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, int epoch, KernelStatus st,
-                    cudaStream_t stream);
+void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st, cudaStream_t stream);
 
 // ---------------------------------------------------------------- low-latency mode
 struct LLDispatchArgs {
@@ -129,7 +125,6 @@ struct LLDispatchArgs {
     int num_tokens;
     int rank;
     int use_fp8, round_scale, use_ue8m0;
-    int seq;
     int phases;                      // 1 send, 2 recv, 3 both
     int* mask;                       // [R] shrink-mode mask (1 = masked) or null
     int shrink;                      // 1: timeouts mask the rank instead of failing
@@ -153,7 +148,6 @@ struct LLCombineArgs {
     const float* topk_weights;       // [N][K]
     int num_tokens;
     int rank;
-    int seq;
     int phases;
     int* mask;
     int shrink;

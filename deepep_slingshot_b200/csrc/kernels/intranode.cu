@@ -38,26 +38,6 @@ __device__ __forceinline__ NormalCtrl* ctrl_of(const PeerTable& p, const NormalL
     return reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(p.base[r]) + l.ctrl_off);
 }
 
-// Block-wide exclusive scan over all threads of the block (blockDim.x <= 1024). Returns the
-// exclusive prefix of `v`; `*total` receives the block sum. `ws` must hold 33 ints.
-__device__ int block_exclusive_scan(int v, int* total, int* ws) {
-    const int lane = lane_id(), warp = warp_id(), nwarps = (blockDim.x + 31) / 32;
-    int incl = warp_inclusive_scan(v);
-    if (lane == 31) ws[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        int w = lane < nwarps ? ws[lane] : 0;
-        int wincl = warp_inclusive_scan(w);
-        if (lane < nwarps) ws[lane] = wincl - w;
-        if (lane == nwarps - 1) ws[32] = wincl;
-    }
-    __syncthreads();
-    int result = ws[warp] + incl - v;
-    *total = ws[32];
-    __syncthreads();
-    return result;
-}
-
 }  // namespace
 
 // =================================================================================================
@@ -113,8 +93,11 @@ void launch_dispatch_layout(const int64_t* topk_idx, int num_tokens, int num_top
 // stage: one record per token into the local staging area, FP8 quantization fused.
 // =================================================================================================
 __global__ void __launch_bounds__(256) dispatch_stage_kernel(StageArgs a) {
-    if (a.wait_epoch > 0 && (int)threadIdx.x < a.num_ranks)
-        wait_ge(&a.pull_done[threadIdx.x], a.wait_epoch, a.st, kErrTimeoutPullDone, threadIdx.x);
+    if ((int)threadIdx.x < a.num_ranks) {
+        // Receivers must have finished pulling the previous dispatch before the staging is rewritten.
+        const int prev_epoch = ld_volatile(a.dispatch_epoch);
+        if (prev_epoch > 0) wait_ge(&a.pull_done[threadIdx.x], prev_epoch, a.st, kErrTimeoutPullDone, threadIdx.x);
+    }
     __syncthreads();
     if (aborted(a.st)) return;
 
@@ -151,9 +134,8 @@ __global__ void __launch_bounds__(256) dispatch_stage_kernel(StageArgs a) {
 }
 
 void launch_dispatch_stage(const StageArgs& a, int num_sms, cudaStream_t stream) {
+    (void)num_sms;
     int blocks = (a.num_tokens + 7) / 8;
-    const int max_blocks = num_sms * 4;
-    if (blocks > max_blocks) blocks = max_blocks;
     if (blocks < 1) blocks = 1;
     dispatch_stage_kernel<<<blocks, 256, 0, stream>>>(a);
 }
@@ -174,27 +156,82 @@ __device__ __forceinline__ uint32_t token_rank_mask(const NotifyArgs& a, int t) 
     return m;
 }
 
+// Block-wide exclusive scan of eight 16-bit counters packed in two 64-bit words (one scan for all
+// destination ranks; per-rank totals < 65536 by construction: capacity checks bound the tokens).
+__device__ void block_exclusive_scan_u64x2(uint64_t& lo, uint64_t& hi, uint64_t* total_lo, uint64_t* total_hi,
+                                           uint64_t* ws /* 2*33 */) {
+    const int lane = lane_id(), warp = warp_id(), nwarps = (blockDim.x + 31) / 32;
+    uint64_t ilo = lo, ihi = hi;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t nlo = __shfl_up_sync(0xffffffffu, ilo, o), nhi = __shfl_up_sync(0xffffffffu, ihi, o);
+        if (lane >= o) {
+            ilo += nlo;
+            ihi += nhi;
+        }
+    }
+    if (lane == 31) {
+        ws[warp] = ilo;
+        ws[33 + warp] = ihi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint64_t wlo = lane < nwarps ? ws[lane] : 0, whi = lane < nwarps ? ws[33 + lane] : 0;
+        uint64_t slo = wlo, shi = whi;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t nlo = __shfl_up_sync(0xffffffffu, slo, o), nhi = __shfl_up_sync(0xffffffffu, shi, o);
+            if (lane >= o) {
+                slo += nlo;
+                shi += nhi;
+            }
+        }
+        if (lane < nwarps) {
+            ws[lane] = slo - wlo;
+            ws[33 + lane] = shi - whi;
+        }
+        if (lane == nwarps - 1) {
+            ws[32] = slo;
+            ws[65] = shi;
+        }
+    }
+    __syncthreads();
+    lo = ws[warp] + ilo - lo;
+    hi = ws[33 + warp] + ihi - hi;
+    *total_lo = ws[32];
+    *total_hi = ws[65];
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
-    extern __shared__ int s_ecnt[];  // [num_experts]
-    __shared__ int s_ws[33];
+    extern __shared__ __align__(16) int s_dyn[];  // [num_experts] counters, then [num_tokens] uint8 masks
+    __shared__ uint64_t s_ws[66];
     __shared__ int s_total[kMaxRanks];
     __shared__ int s_tc[kMaxRanks][kMaxRanks];
+    __shared__ int s_epoch;
+    int* s_ecnt = s_dyn;
+    uint8_t* s_mask = reinterpret_cast<uint8_t*>(s_dyn + a.num_experts);
     const int tid = threadIdx.x, nt = blockDim.x;
     const int R = a.num_ranks;
     NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
+    if (tid == 0) s_epoch = ld_volatile(&my_ctrl->dispatch_epoch) + 1;
+    __syncthreads();
+    const int epoch = s_epoch, parity = epoch & 1;
 
     if (!a.cached) {
         for (int i = tid; i < a.num_experts; i += nt) s_ecnt[i] = 0;
         __syncthreads();
         const int chunk = (a.num_tokens + nt - 1) / nt;
         const int t0 = min(a.num_tokens, tid * chunk), t1 = min(a.num_tokens, t0 + chunk);
-        int cnt[kMaxRanks];
-#pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) cnt[r] = 0;
+        uint64_t lo = 0, hi = 0;
         for (int t = t0; t < t1; ++t) {
             const uint32_t m = token_rank_mask(a, t);
+            s_mask[t] = (uint8_t)m;
 #pragma unroll
-            for (int r = 0; r < kMaxRanks; ++r) cnt[r] += (m >> r) & 1u;
+            for (int r = 0; r < 4; ++r) {
+                lo += (uint64_t)((m >> r) & 1u) << (16 * r);
+                hi += (uint64_t)((m >> (r + 4)) & 1u) << (16 * r);
+            }
             if (a.topk_idx != nullptr) {
                 for (int k = 0; k < a.num_topk; ++k) {
                     const int64_t e = a.topk_idx[(int64_t)t * a.num_topk + k];
@@ -202,20 +239,19 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
                 }
             }
         }
+        uint64_t tlo, thi;
+        block_exclusive_scan_u64x2(lo, hi, &tlo, &thi, s_ws);
+        if (tid < R) s_total[tid] = (int)(((tid < 4 ? tlo : thi) >> (16 * (tid & 3))) & 0xffffu);
         int base[kMaxRanks];
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) {
-            if (r < R) {
-                int total;
-                base[r] = block_exclusive_scan(cnt[r], &total, s_ws);
-                if (tid == 0) s_total[r] = total;
-            }
-        }
+        for (int r = 0; r < kMaxRanks; ++r) base[r] = (int)(((r < 4 ? lo : hi) >> (16 * (r & 3))) & 0xffffu);
         int* list = reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[a.rank]) + a.layout.list_off);
         const int cap = a.layout.capacity;
         for (int t = t0; t < t1; ++t) {
-            const uint32_t m = token_rank_mask(a, t);
-            for (int r = 0; r < R; ++r) {
+            const uint32_t m = s_mask[t];
+#pragma unroll
+            for (int r = 0; r < kMaxRanks; ++r) {
+                if (r >= R) break;
                 int pos = -1;
                 if ((m >> r) & 1u) {
                     pos = base[r]++;
@@ -228,25 +264,29 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
         // Push my count row and my per-expert counts into every destination's control block.
         for (int i = tid; i < R * R; i += nt) {
             const int dst = i / R, col = i % R;
-            ctrl_of(a.peers, a.layout, dst)->token_counts[a.parity][a.rank][col] = s_total[col];
+            ctrl_of(a.peers, a.layout, dst)->token_counts[parity][a.rank][col] = s_total[col];
         }
         for (int i = tid; i < R * a.num_local_experts; i += nt) {
             const int dst = i / a.num_local_experts, le = i % a.num_local_experts;
-            ctrl_of(a.peers, a.layout, dst)->expert_counts[a.parity][a.rank][le] =
+            ctrl_of(a.peers, a.layout, dst)->expert_counts[parity][a.rank][le] =
                 a.topk_idx != nullptr ? s_ecnt[dst * a.num_local_experts + le] : 0;
         }
     }
     __syncthreads();
     if (tid < R) {
         fence_sys();
-        st_release_sys(&ctrl_of(a.peers, a.layout, tid)->notify_flag[a.rank], a.epoch);
-        wait_ge(&my_ctrl->notify_flag[tid], a.epoch, a.st, kErrTimeoutNotify, tid);
+        st_release_sys(&ctrl_of(a.peers, a.layout, tid)->notify_flag[a.rank], epoch);
+        wait_ge(&my_ctrl->notify_flag[tid], epoch, a.st, kErrTimeoutNotify, tid);
     }
     __syncthreads();
-    if (aborted(a.st) || a.cached) return;
+    if (aborted(a.st)) return;
+    if (a.cached) {
+        if (tid == 0) my_ctrl->dispatch_epoch = epoch;
+        return;
+    }
 
     for (int i = tid; i < R * R; i += nt)
-        s_tc[i / R][i % R] = ld_volatile(&my_ctrl->token_counts[a.parity][i / R][i % R]);
+        s_tc[i / R][i % R] = ld_volatile(&my_ctrl->token_counts[parity][i / R][i % R]);
     __syncthreads();
     if (tid == 0) {
         for (int r = 0; r < R; ++r) {
@@ -274,28 +314,87 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
     }
     for (int le = tid; le < a.num_local_experts; le += nt) {
         int c = 0;
-        for (int s = 0; s < R; ++s) c += ld_volatile(&my_ctrl->expert_counts[a.parity][s][le]);
+        for (int s = 0; s < R; ++s) c += ld_volatile(&my_ctrl->expert_counts[parity][s][le]);
         if (a.cumulative_stats != nullptr) a.cumulative_stats[le] += c;
         const int al = a.expert_alignment > 1 ? (c + a.expert_alignment - 1) / a.expert_alignment * a.expert_alignment : c;
         a.num_recv_per_expert[le] = al;
         if (a.host != nullptr) a.host->num_recv_tokens_per_expert[le] = al;
     }
     __syncthreads();
-    if (tid == 0 && a.host != nullptr) {
-        __threadfence_system();
-        *reinterpret_cast<volatile int*>(&a.host->ready_epoch) = a.epoch;
-        __threadfence_system();
+    if (tid == 0) {
+        my_ctrl->dispatch_epoch = epoch;
+        if (a.host != nullptr) {
+            __threadfence_system();
+            *reinterpret_cast<volatile int*>(&a.host->ready_ticket) = a.host_ticket;
+            __threadfence_system();
+        }
     }
 }
 
 void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream) {
-    const size_t smem = sizeof(int) * (a.num_experts > 0 ? a.num_experts : 1);
+    const size_t smem = sizeof(int) * (a.num_experts > 0 ? a.num_experts : 1) + (size_t)(a.cached ? 0 : a.num_tokens) + 16;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(dispatch_notify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dispatch_notify_kernel<<<1, 1024, smem, stream>>>(a);
 }
 
 // =================================================================================================
-// pull: receivers TMA-load records from the sources' staging (peer memory) and TMA-store rows into
-// their own outputs. Each warp runs an independent S-stage pipeline over chunks of 32 rows.
+// Row pipeline shared by pull (dispatch) and push (combine): each CTA runs kPairs independent
+// (producer warp, consumer warp) pairs over an S-slot shared-memory ring. The producer's lane 0
+// TMA-loads rows (from a peer's staging, or from local expert outputs) as soon as a slot is free;
+// the consumer's lane 0 TMA-stores each landed row to its destination (local output, or a peer's
+// combine slots) and frees the slot once the store has read it. Loads never wait on store
+// completion, so both directions stay in flight.
+// =================================================================================================
+constexpr int kPairs = 2;
+constexpr int kStoreLag = 2;  // stores allowed to still be reading shared memory
+
+struct PipeSmem {
+    uint8_t* slots;
+    uint64_t* full;
+    uint64_t* empty;
+    int* side;  // per-slot side information written by the producer (source token / destination)
+    int S, slot_bytes;
+};
+
+// Bytes of one pair's region, rounded to 128 so every pair's slots (TMA targets, 16-byte rule) and
+// mbarriers (8-byte rule) stay aligned whatever the stage count.
+__host__ __device__ __forceinline__ size_t pipe_pair_bytes(int S, int slot_bytes) {
+    return ((size_t)S * slot_bytes + (size_t)S * 20 + 16 + 127) / 128 * 128;
+}
+
+__device__ __forceinline__ PipeSmem pipe_smem(uint8_t* smem, int pair, int S, int slot_bytes) {
+    uint8_t* base = smem + (size_t)pair * pipe_pair_bytes(S, slot_bytes);
+    PipeSmem p;
+    p.slots = base;
+    p.full = reinterpret_cast<uint64_t*>(base + (size_t)S * slot_bytes);
+    p.empty = p.full + S;
+    p.side = reinterpret_cast<int*>(p.empty + S);
+    p.S = S;
+    p.slot_bytes = slot_bytes;
+    return p;
+}
+
+static size_t pipe_smem_bytes(int S, int slot_bytes) { return (size_t)kPairs * pipe_pair_bytes(S, slot_bytes); }
+
+__device__ __forceinline__ void pipe_init(const PipeSmem& p) {
+    if (lane_id() == 0) {
+        for (int s = 0; s < p.S; ++s) {
+            mbar_init(&p.full[s], 1);
+            mbar_init(&p.empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+}
+
+// Contiguous row range of pair `g` out of `total_pairs` for `n` rows.
+__device__ __forceinline__ void pair_range(int n, int g, int total_pairs, int& r0, int& r1) {
+    const int per = (n + total_pairs - 1) / total_pairs;
+    r0 = min(n, g * per);
+    r1 = min(n, r0 + per);
+}
+
+// =================================================================================================
+// pull (dispatch receive): rows of my receive block are pulled from the sources' staging.
 // =================================================================================================
 __device__ __forceinline__ int find_source(const int* prefix, int R, int j) {
     int s = 0;
@@ -303,29 +402,24 @@ __device__ __forceinline__ int find_source(const int* prefix, int R, int j) {
     return s;
 }
 
-__global__ void __launch_bounds__(128) dispatch_pull_kernel(PullArgs a) {
+__global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_prefix[kMaxRanks + 1];
-    const int lane = lane_id(), warp = warp_id(), W = blockDim.x / 32;
-    const int R = a.num_ranks, S = a.stages;
-    const int stage_bytes = (a.rec.bytes + 127) / 128 * 128;
-    uint8_t* wbuf = smem + (size_t)warp * S * stage_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * stage_bytes) + warp * S;
-
-    if (lane == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-        fence_mbar_init();
-    }
+    const int lane = lane_id(), warp = warp_id();
+    const int pair = warp >> 1;
+    const bool producer = (warp & 1) == 0;
+    const int R = a.num_ranks;
+    const int slot_bytes = (a.rec.bytes + 127) / 128 * 128;
+    const PipeSmem p = pipe_smem(smem, pair, a.stages, slot_bytes);
+    pipe_init(p);
     if (threadIdx.x == 0) {
         s_prefix[0] = 0;
-        for (int s = 0; s < R; ++s)
-            s_prefix[s + 1] = a.rank_prefix_matrix[s * R + a.rank];  // inclusive prefix over sources
+        for (int s = 0; s < R; ++s) s_prefix[s + 1] = a.rank_prefix_matrix[s * R + a.rank];
     }
     __syncthreads();
 
     const int num_recv = a.dev_num_recv != nullptr ? ld_volatile(a.dev_num_recv) : a.num_recv_host;
     const int K = a.num_topk;
-    // Padding rows of a worst-case allocation: mark as empty.
     for (int j = num_recv + blockIdx.x * blockDim.x + threadIdx.x; j < a.num_out_rows; j += gridDim.x * blockDim.x) {
         if (a.recv_topk_idx != nullptr)
             for (int k = 0; k < K; ++k) a.recv_topk_idx[(int64_t)j * K + k] = -1;
@@ -337,97 +431,82 @@ __global__ void __launch_bounds__(128) dispatch_pull_kernel(PullArgs a) {
         if (threadIdx.x == 0 && blockIdx.x == 0) report_error(a.st, kErrCapacity, -1, num_recv);
         return;
     }
+    int r0, r1;
+    pair_range(num_recv, blockIdx.x * kPairs + pair, gridDim.x * kPairs, r0, r1);
+    const int S = p.S;
 
-    const int x_bytes = a.rec.x_bytes;
-    const int nb = a.rec.scale_bytes > 0 ? a.layout.hidden / 128 : 0;
-    const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
-    const int E_l = a.num_local_experts;
-    const int lo_e = a.rank * E_l;
-    uint32_t phase = 0;  // per-stage parity bits (lane 0)
-    const int num_chunks = (num_recv + 31) / 32;
-    const int gw = blockIdx.x * W + warp, total_warps = gridDim.x * W;
-    bool ok = true;
-
-    for (int c = gw; c < num_chunks && ok; c += total_warps) {
-        const int j = c * 32 + lane;
-        const bool valid = j < num_recv;
-        int src = 0, t = 0;
-        if (valid) {
-            src = find_source(s_prefix, R, j);
-            const int pos = j - s_prefix[src];
-            if (a.cached_src_idx != nullptr) {
-                t = a.cached_src_idx[j];
-            } else {
-                const int* list = reinterpret_cast<const int*>(static_cast<const uint8_t*>(a.peers.base[src]) + a.layout.list_off) +
-                                  (int64_t)a.rank * a.layout.capacity;
-                t = ld_relaxed_sys(list + pos);
+    if (producer) {
+        for (int base = r0; base < r1; base += 32) {
+            const int j = base + lane;
+            int src = 0, t = 0;
+            if (j < r1) {
+                src = find_source(s_prefix, R, j);
+                if (a.cached_src_idx != nullptr) {
+                    t = a.cached_src_idx[j];
+                } else {
+                    const int* list = reinterpret_cast<const int*>(static_cast<const uint8_t*>(a.peers.base[src]) + a.layout.list_off) +
+                                      (int64_t)a.rank * a.layout.capacity;
+                    t = ld_relaxed_sys(list + (j - s_prefix[src]));
+                }
             }
-        }
-        const int n_rows = min(32, num_recv - c * 32);
-        // Stages may still be read by stores of the previous chunk.
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();
-        // Prefetch the first S-1 rows.
-        for (int i = 0; i < S - 1 && i < n_rows; ++i) {
-            const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
-            if (lane == 0) {
-                const uint8_t* g = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
-                                   (int64_t)pt * a.layout.record_bytes;
-                mbar_arrive_expect_tx(&bars[i], a.rec.bytes);
-                tma_load_1d(wbuf + (size_t)i * stage_bytes, g, a.rec.bytes, &bars[i]);
+            const int n = min(32, r1 - base);
+            for (int i = 0; i < n; ++i) {
+                const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
+                if (lane == 0) {
+                    const int k = base + i - r0, slot = k % S;
+                    bool ok = true;
+                    if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
+                    if (ok) {
+                        p.side[slot] = pt;
+                        const uint8_t* g = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
+                                           (int64_t)pt * a.layout.record_bytes;
+                        mbar_arrive_expect_tx(&p.full[slot], a.rec.bytes);
+                        tma_load_1d(p.slots + (size_t)slot * slot_bytes, g, a.rec.bytes, &p.full[slot]);
+                    }
+                }
+                if (aborted(a.st)) break;
             }
+            if (aborted(a.st)) break;
         }
-        for (int i = 0; i < n_rows; ++i) {
-            const int stage = i % S;
-            const int jj = c * 32 + i;
-            const int st_t = __shfl_sync(0xffffffffu, t, i);
-            // rows i + S - 1 for the next load
-            const int nxt = i + S - 1;
-            const int ns = __shfl_sync(0xffffffffu, src, nxt & 31), ntk = __shfl_sync(0xffffffffu, t, nxt & 31);
+    } else {
+        const int x_bytes = a.rec.x_bytes;
+        const int nb = a.rec.scale_bytes > 0 ? a.layout.hidden / 128 : 0;
+        const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
+        const int E_l = a.num_local_experts, lo_e = a.rank * E_l;
+        for (int j = r0; j < r1; ++j) {
+            const int k = j - r0, slot = k % S;
             int good = 1;
+            if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
+            if (!__shfl_sync(0xffffffffu, good, 0)) break;
+            const uint8_t* buf = p.slots + (size_t)slot * slot_bytes;
             if (lane == 0) {
-                good = mbar_wait(&bars[stage], (phase >> stage) & 1u, a.st, kErrTimeoutTma) ? 1 : 0;
-                phase ^= 1u << stage;
-            }
-            good = __shfl_sync(0xffffffffu, good, 0);
-            if (!good) {
-                ok = false;
-                break;
-            }
-            const uint8_t* buf = wbuf + (size_t)stage * stage_bytes;
-            if (lane == 0) {
-                tma_store_1d(static_cast<uint8_t*>(a.recv_x) + (int64_t)jj * x_bytes, buf, x_bytes);
-                if (scales_bulk) tma_store_1d(a.recv_scales + (int64_t)jj * nb, buf + a.rec.scale_off, nb * 4);
+                tma_store_1d(static_cast<uint8_t*>(a.recv_x) + (int64_t)j * x_bytes, buf, x_bytes);
+                if (scales_bulk) tma_store_1d(a.recv_scales + (int64_t)j * nb, buf + a.rec.scale_off, nb * 4);
                 bulk_commit();
             }
             if (a.recv_scales != nullptr && !scales_bulk) {
                 const float* sc = reinterpret_cast<const float*>(buf + a.rec.scale_off);
                 for (int b = lane; b < nb; b += 32) {
-                    if (a.scales_col_major) a.recv_scales[(int64_t)b * a.scales_ld + jj] = sc[b];
-                    else a.recv_scales[(int64_t)jj * nb + b] = sc[b];
+                    if (a.scales_col_major) a.recv_scales[(int64_t)b * a.scales_ld + j] = sc[b];
+                    else a.recv_scales[(int64_t)j * nb + b] = sc[b];
                 }
             }
             if (lane < K) {
                 const int e = reinterpret_cast<const int*>(buf + a.rec.idx_off)[lane];
                 const float w = reinterpret_cast<const float*>(buf + a.rec.w_off)[lane];
                 const bool mine = e >= lo_e && e < lo_e + E_l;
-                if (a.recv_topk_idx != nullptr) a.recv_topk_idx[(int64_t)jj * K + lane] = mine ? (e - lo_e) : -1;
-                if (a.recv_topk_weights != nullptr) a.recv_topk_weights[(int64_t)jj * K + lane] = mine ? w : 0.f;
+                if (a.recv_topk_idx != nullptr) a.recv_topk_idx[(int64_t)j * K + lane] = mine ? (e - lo_e) : -1;
+                if (a.recv_topk_weights != nullptr) a.recv_topk_weights[(int64_t)j * K + lane] = mine ? w : 0.f;
             }
-            if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[jj] = st_t;
+            if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[slot];
             __syncwarp();
-            if (nxt < n_rows && lane == 0) {
-                bulk_wait_read<1>();  // the store of row i-1 is done reading stage nxt % S
-                const int nstage = nxt % S;
-                const uint8_t* g = static_cast<const uint8_t*>(a.peers.base[ns]) + a.layout.staging_off +
-                                   (int64_t)ntk * a.layout.record_bytes;
-                mbar_arrive_expect_tx(&bars[nstage], a.rec.bytes);
-                tma_load_1d(wbuf + (size_t)nstage * stage_bytes, g, a.rec.bytes, &bars[nstage]);
+            if (lane == 0) {
+                bulk_wait_read<kStoreLag>();
+                if (k >= kStoreLag) mbar_arrive(&p.empty[(k - kStoreLag) % S]);
             }
-            __syncwarp();
         }
+        if (lane == 0) bulk_wait<0>();
     }
-    if (lane == 0) bulk_wait<0>();
     __syncthreads();
     // The last block tells every source that its staging may be reused.
     if (threadIdx.x == 0) {
@@ -436,53 +515,51 @@ __global__ void __launch_bounds__(128) dispatch_pull_kernel(PullArgs a) {
         const int old = atom_add_acq_rel_gpu(&my_ctrl->pull_finished_blocks, 1);
         if (old == (int)gridDim.x - 1) {
             my_ctrl->pull_finished_blocks = 0;
+            const int epoch = ld_volatile(&my_ctrl->dispatch_epoch);
             fence_sys();
-            for (int s = 0; s < R; ++s) st_release_sys(&ctrl_of(a.peers, a.layout, s)->pull_done[a.rank], a.epoch);
+            for (int s = 0; s < R; ++s) st_release_sys(&ctrl_of(a.peers, a.layout, s)->pull_done[a.rank], epoch);
         }
     }
 }
 
-static int smem_stages(int record_bytes, int warps, int max_stages) {
-    const int stage_bytes = (record_bytes + 127) / 128 * 128;
+static int pipe_stages(int slot_bytes, int max_stages) {
     const int budget = 200 * 1024;
-    int s = budget / (warps * (stage_bytes + 8));
+    int s = (int)(budget / ((size_t)kPairs * (slot_bytes + 20) + 256));
     if (s > max_stages) s = max_stages;
     return s;
 }
 
 void launch_dispatch_pull(const PullArgs& a_in, int num_sms, cudaStream_t stream) {
     PullArgs a = a_in;
-    const int warps = 4;
-    if (a.stages <= 0) a.stages = smem_stages(a.rec.bytes, warps, 6);
-    if (a.stages < 2) a.stages = 2;
-    const int stage_bytes = (a.rec.bytes + 127) / 128 * 128;
-    const size_t smem = (size_t)warps * a.stages * stage_bytes + (size_t)warps * a.stages * sizeof(uint64_t);
+    const int slot_bytes = (a.rec.bytes + 127) / 128 * 128;
+    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 8);
+    if (a.stages < kStoreLag + 2) a.stages = kStoreLag + 2;
+    const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
     cudaFuncSetAttribute(dispatch_pull_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dispatch_pull_kernel<<<num_sms, warps * 32, smem, stream>>>(a);
+    dispatch_pull_kernel<<<num_sms, 64 * kPairs, smem, stream>>>(a);
 }
 
 // =================================================================================================
 // combine push: expert-output rows -> the source rank's combine slots (peer memory).
 // =================================================================================================
-__global__ void __launch_bounds__(128) combine_push_kernel(CombinePushArgs a) {
+__global__ void __launch_bounds__(64 * kPairs) combine_push_kernel(CombinePushArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_prefix[kMaxRanks + 1];
     __shared__ int s_dst_base[kMaxRanks];
-    const int lane = lane_id(), warp = warp_id(), W = blockDim.x / 32;
-    const int R = a.num_ranks, S = a.stages, K = a.num_topk;
-    const int H = a.layout.hidden;
-    const int row_bytes = H * 2;
-    const int stage_bytes = (row_bytes + 127) / 128 * 128;
-    uint8_t* wbuf = smem + (size_t)warp * S * stage_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * stage_bytes) + warp * S;
+    const int lane = lane_id(), warp = warp_id();
+    const int pair = warp >> 1;
+    const bool producer = (warp & 1) == 0;
+    const int R = a.num_ranks, K = a.num_topk;
+    const int row_bytes = a.layout.hidden * 2;
+    const int slot_bytes = (row_bytes + 127) / 128 * 128;
+    const PipeSmem p = pipe_smem(smem, pair, a.stages, slot_bytes);
     NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
 
     // Destination `tid` must have finished reducing the previous combine before its slots are reused.
-    if ((int)threadIdx.x < R) wait_ge(&my_ctrl->combine_ready[threadIdx.x], a.seq - 1, a.st, kErrTimeoutCombineReady, threadIdx.x);
-    if (lane == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-        fence_mbar_init();
-    }
+    if ((int)threadIdx.x < R)
+        wait_ge(&my_ctrl->combine_ready[threadIdx.x], ld_volatile(&my_ctrl->combine_seq), a.st, kErrTimeoutCombineReady,
+                threadIdx.x);
+    pipe_init(p);
     if (threadIdx.x == 0) {
         s_prefix[0] = 0;
         for (int s = 0; s < R; ++s) {
@@ -494,104 +571,142 @@ __global__ void __launch_bounds__(128) combine_push_kernel(CombinePushArgs a) {
     if (aborted(a.st)) return;
 
     const int num_recv = min(s_prefix[R], a.num_recv_max);
-    const int num_chunks = (num_recv + 31) / 32;
-    const int gw = blockIdx.x * W + warp, total_warps = gridDim.x * W;
-    const int64_t combine_rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int c = gw; c < num_chunks && ok; c += total_warps) {
-        const int j = c * 32 + lane;
-        const bool valid = j < num_recv;
-        int dst = 0, drow = 0;
-        if (valid) {
-            dst = find_source(s_prefix, R, j);
-            drow = s_dst_base[dst] + (j - s_prefix[dst]);
-            if (drow < 0 || drow >= combine_rows_cap) {
-                report_error(a.st, kErrBounds, dst, drow);
-                dst = -1;
-            }
-        }
-        const int n_rows = min(32, num_recv - c * 32);
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();
-        for (int i = 0; i < S - 1 && i < n_rows; ++i) {
+    int r0, r1;
+    pair_range(num_recv, blockIdx.x * kPairs + pair, gridDim.x * kPairs, r0, r1);
+    const int S = p.S;
+    const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
+
+    if (producer) {
+        for (int j = r0; j < r1; ++j) {
             if (lane == 0) {
-                mbar_arrive_expect_tx(&bars[i], row_bytes);
-                tma_load_1d(wbuf + (size_t)i * stage_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)(c * 32 + i) * row_bytes,
-                            row_bytes, &bars[i]);
+                const int k = j - r0, slot = k % S;
+                bool ok = true;
+                if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
+                if (ok) {
+                    mbar_arrive_expect_tx(&p.full[slot], row_bytes);
+                    tma_load_1d(p.slots + (size_t)slot * slot_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)j * row_bytes,
+                                row_bytes, &p.full[slot]);
+                }
             }
+            if (aborted(a.st)) break;
         }
-        for (int i = 0; i < n_rows; ++i) {
-            const int stage = i % S;
-            const int jj = c * 32 + i;
-            const int d = __shfl_sync(0xffffffffu, dst, i), dr = __shfl_sync(0xffffffffu, drow, i);
+    } else {
+        int sent = 0;  // lane d: rows sent to destination d
+        for (int j = r0; j < r1; ++j) {
+            const int k = j - r0, slot = k % S;
+            const int d = find_source(s_prefix, R, j);
+            const int64_t drow = s_dst_base[d] + (j - s_prefix[d]);
             int good = 1;
-            if (lane == 0) {
-                good = mbar_wait(&bars[stage], (phase >> stage) & 1u, a.st, kErrTimeoutTma) ? 1 : 0;
-                phase ^= 1u << stage;
-            }
-            good = __shfl_sync(0xffffffffu, good, 0);
-            if (!good) {
-                ok = false;
+            if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
+            if (!__shfl_sync(0xffffffffu, good, 0)) break;
+            if (drow < 0 || drow >= rows_cap) {
+                if (lane == 0) report_error(a.st, kErrBounds, d, (int)drow);
                 break;
             }
-            if (d >= 0) {
-                uint8_t* peer = static_cast<uint8_t*>(a.peers.base[d]);
-                if (lane == 0) {
-                    tma_store_1d(peer + a.layout.combine_off + (int64_t)dr * row_bytes, wbuf + (size_t)stage * stage_bytes, row_bytes);
-                }
-                if (a.topk_weights != nullptr && lane < a.layout.topk_pad) {
-                    float* wdst = reinterpret_cast<float*>(peer + a.layout.combine_w_off) + (int64_t)dr * a.layout.topk_pad;
-                    wdst[lane] = lane < K ? a.topk_weights[(int64_t)jj * K + lane] : 0.f;
-                }
+            uint8_t* peer = static_cast<uint8_t*>(a.peers.base[d]);
+            if (lane == 0) {
+                tma_store_1d(peer + a.layout.combine_off + drow * row_bytes, p.slots + (size_t)slot * slot_bytes, row_bytes);
+                bulk_commit();
             }
-            if (lane == 0) bulk_commit();
-            __syncwarp();
-            const int nxt = i + S - 1;
-            if (nxt < n_rows && lane == 0) {
-                bulk_wait_read<1>();
-                const int nstage = nxt % S;
-                mbar_arrive_expect_tx(&bars[nstage], row_bytes);
-                tma_load_1d(wbuf + (size_t)nstage * stage_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)(c * 32 + nxt) * row_bytes,
-                            row_bytes, &bars[nstage]);
+            if (a.topk_weights != nullptr && lane < a.layout.topk_pad) {
+                float* wdst = reinterpret_cast<float*>(peer + a.layout.combine_w_off) + drow * a.layout.topk_pad;
+                wdst[lane] = lane < K ? a.topk_weights[(int64_t)j * K + lane] : 0.f;
             }
+            if (lane == d) ++sent;
             __syncwarp();
+            if (lane == 0) {
+                bulk_wait_read<kStoreLag>();
+                if (k >= kStoreLag) mbar_arrive(&p.empty[(k - kStoreLag) % S]);
+            }
         }
-        // Rows of this chunk are complete in the destinations' memory: publish the counts.
+        // All rows of this pair are complete in the destinations' memory: publish the counts.
         if (lane == 0) {
             bulk_wait<0>();
             fence_proxy_async_global();
         }
         __syncwarp();
-        for (int d = 0; d < R; ++d) {
-            const int cnt = __popc(__ballot_sync(0xffffffffu, valid && dst == d));
-            if (cnt > 0 && lane == 0) {
-                fence_sys();
-                red_add_release_sys(&ctrl_of(a.peers, a.layout, d)->combine_arrived, cnt);
-            }
+        if (lane < R && sent > 0) {
+            fence_sys();
+            red_add_release_sys(&ctrl_of(a.peers, a.layout, lane)->combine_arrived, sent);
         }
     }
 }
 
 void launch_combine_push(const CombinePushArgs& a_in, int num_sms, cudaStream_t stream) {
     CombinePushArgs a = a_in;
-    const int warps = 4;
-    if (a.stages <= 0) a.stages = smem_stages(a.layout.hidden * 2, warps, 4);
-    if (a.stages < 2) a.stages = 2;
-    const int stage_bytes = (a.layout.hidden * 2 + 127) / 128 * 128;
-    const size_t smem = (size_t)warps * a.stages * stage_bytes + (size_t)warps * a.stages * sizeof(uint64_t);
+    const int slot_bytes = (a.layout.hidden * 2 + 127) / 128 * 128;
+    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 8);
+    if (a.stages < kStoreLag + 2) a.stages = kStoreLag + 2;
+    const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
     cudaFuncSetAttribute(combine_push_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    combine_push_kernel<<<num_sms, warps * 32, smem, stream>>>(a);
+    combine_push_kernel<<<num_sms, 64 * kPairs, smem, stream>>>(a);
 }
 
 // =================================================================================================
 // combine reduce: fp32 sum of the <= R contributions per token (+ bias) -> bf16; top-k weight sum.
+// One warp per token; all contributions of a 256-element slice are loaded before they are summed.
 // =================================================================================================
+template <int kU>
+__device__ __forceinline__ void reduce_rows(const __nv_bfloat16* rows, const int* src_rows, int n, int H, int t,
+                                            const void* bias0, const void* bias1, void* out, int e_start) {
+    const int lane = lane_id();
+    int4 v[kU][kMaxRanks];
+    for (int e0 = e_start + lane * 8; e0 - lane * 8 < H; e0 += 256 * kU) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int e = e0 + u * 256;
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < n && e < H) v[u][q] = *reinterpret_cast<const int4*>(rows + (int64_t)src_rows[q] * H + e);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int e = e0 + u * 256;
+            if (e >= H) break;
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q) {
+                if (q >= n) break;
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[u][q]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __bfloat1622float2(h2[i]);
+                    acc[2 * i] += f.x;
+                    acc[2 * i + 1] += f.y;
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const void* bias = b == 0 ? bias0 : bias1;
+                if (bias != nullptr) {
+                    const int4 bv = *reinterpret_cast<const int4*>(static_cast<const __nv_bfloat16*>(bias) + (int64_t)t * H + e);
+                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&bv);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = __bfloat1622float2(h2[i]);
+                        acc[2 * i] += f.x;
+                        acc[2 * i + 1] += f.y;
+                    }
+                }
+            }
+            int4 o;
+            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+            *reinterpret_cast<int4*>(static_cast<__nv_bfloat16*>(out) + (int64_t)t * H + e) = o;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) combine_reduce_kernel(CombineReduceArgs a) {
     __shared__ int s_base[kMaxRanks];
+    __shared__ int s_seq;
     const int R = a.num_ranks, K = a.num_topk, H = a.hidden;
     NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
     if (threadIdx.x == 0) {
+        s_seq = ld_volatile(&my_ctrl->combine_seq) + 1;
         int expected = 0;
         for (int r = 0; r < R; ++r) {
             const int prev = a.rank > 0 ? a.rank_prefix_matrix[(a.rank - 1) * R + r] : 0;
@@ -604,7 +719,8 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(CombineReduceArgs a
     if (!aborted(a.st)) {
         const int lane = lane_id();
         const int warps = blockDim.x / 32;
-        const __nv_bfloat16* rows = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_off);
+        const __nv_bfloat16* rows =
+            reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_off);
         const float* wrows = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_w_off);
         for (int t = blockIdx.x * warps + warp_id(); t < a.num_tokens; t += gridDim.x * warps) {
             int my_row = -1;
@@ -619,39 +735,8 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(CombineReduceArgs a
                 const int v = __shfl_sync(0xffffffffu, my_row, r);
                 if (r < R && v >= 0) src_rows[n++] = v;
             }
-            for (int e0 = lane * 8; e0 < H; e0 += 256) {
-                float acc[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-                for (int q = 0; q < n; ++q) {
-                    const int4 v = *reinterpret_cast<const int4*>(rows + (int64_t)src_rows[q] * H + e0);
-                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 f = __bfloat1622float2(h2[i]);
-                        acc[2 * i] += f.x;
-                        acc[2 * i + 1] += f.y;
-                    }
-                }
-                for (int b = 0; b < 2; ++b) {
-                    const void* bias = b == 0 ? a.bias0 : a.bias1;
-                    if (bias != nullptr) {
-                        const int4 v = *reinterpret_cast<const int4*>(static_cast<const __nv_bfloat16*>(bias) + (int64_t)t * H + e0);
-                        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float2 f = __bfloat1622float2(h2[i]);
-                            acc[2 * i] += f.x;
-                            acc[2 * i + 1] += f.y;
-                        }
-                    }
-                }
-                int4 o;
-                __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-                *reinterpret_cast<int4*>(static_cast<__nv_bfloat16*>(a.out) + (int64_t)t * H + e0) = o;
-            }
+            if (n <= 2) reduce_rows<4>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+            else reduce_rows<1>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
             if (a.out_topk_weights != nullptr && lane < K) {
                 float w = 0.f;
                 if (a.has_weights)
@@ -666,16 +751,16 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(CombineReduceArgs a
         if (old == (int)gridDim.x - 1) {
             my_ctrl->combine_reduced_blocks = 0;
             my_ctrl->combine_arrived = 0;
+            my_ctrl->combine_seq = s_seq;
             fence_sys();
-            for (int r = 0; r < R; ++r) st_release_sys(&ctrl_of(a.peers, a.layout, r)->combine_ready[a.rank], a.seq);
+            for (int r = 0; r < R; ++r) st_release_sys(&ctrl_of(a.peers, a.layout, r)->combine_ready[a.rank], s_seq);
         }
     }
 }
 
 void launch_combine_reduce(const CombineReduceArgs& a, int num_sms, cudaStream_t stream) {
+    (void)num_sms;
     int blocks = (a.num_tokens + 7) / 8;
-    const int max_blocks = num_sms * 2;
-    if (blocks > max_blocks) blocks = max_blocks;
     if (blocks < 1) blocks = 1;
     combine_reduce_kernel<<<blocks, 256, 0, stream>>>(a);
 }
@@ -683,20 +768,22 @@ void launch_combine_reduce(const CombineReduceArgs& a, int num_sms, cudaStream_t
 // =================================================================================================
 // barrier across the NVLink domain (bounded).
 // =================================================================================================
-__global__ void barrier_kernel(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, int epoch, KernelStatus st) {
+__global__ void barrier_kernel(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st) {
     const int r = threadIdx.x;
+    NormalCtrl* mine = reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(peers.base[rank]) + ctrl_off);
+    const int epoch = ld_volatile(&mine->barrier_epoch) + 1;
     if (r < num_ranks) {
         NormalCtrl* peer = reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(peers.base[r]) + ctrl_off);
-        NormalCtrl* mine = reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(peers.base[rank]) + ctrl_off);
         fence_sys();
         st_release_sys(&peer->barrier_flag[rank], epoch);
         wait_ge(&mine->barrier_flag[r], epoch, st, kErrTimeoutBarrier, r);
     }
+    __syncwarp();
+    if (r == 0) mine->barrier_epoch = epoch;
 }
 
-void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, int epoch, KernelStatus st,
-                    cudaStream_t stream) {
-    barrier_kernel<<<1, 32, 0, stream>>>(peers, ctrl_off, rank, num_ranks, epoch, st);
+void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st, cudaStream_t stream) {
+    barrier_kernel<<<1, 32, 0, stream>>>(peers, ctrl_off, rank, num_ranks, st);
 }
 
 }  // namespace ep

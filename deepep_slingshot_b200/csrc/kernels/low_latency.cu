@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
                 fence_sys();
                 for (int d = 0; d < R; ++d) {
                     if (is_masked(a.mask, d)) continue;
-                    st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->dispatch_done[a.rank], a.seq);
+                    st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->dispatch_done[a.rank], 1);
                 }
             }
         }
@@ -160,9 +160,17 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
     if (a.phases & 2) {
         LLHalf mine = half_of(a.peers, L, a.rank, a.half);
         if ((int)threadIdx.x < R && !is_masked(a.mask, threadIdx.x))
-            ll_wait(&mine.ctrl()->dispatch_done[threadIdx.x], a.seq, a.st, kErrTimeoutLLDispatch, threadIdx.x, a.mask,
+            ll_wait(&mine.ctrl()->dispatch_done[threadIdx.x], 1, a.st, kErrTimeoutLLDispatch, threadIdx.x, a.mask,
                     a.shrink != 0, blockIdx.x == 0 ? a.wait_stats : nullptr);
         __syncthreads();
+        // The last block that has seen every flag resets them for the next use of this half.
+        if (threadIdx.x == 0) {
+            const int old = atom_add_acq_rel_gpu(&mine.ctrl()->recv_finished_blocks, 1);
+            if (old == (int)gridDim.x - 1) {
+                mine.ctrl()->recv_finished_blocks = 0;
+                for (int s = 0; s < R; ++s) mine.ctrl()->dispatch_done[s] = 0;
+            }
+        }
         for (int le = blockIdx.x; le < E_l; le += gridDim.x) {
             if (threadIdx.x < kMaxRanks) s_src_count[threadIdx.x] = 0;
             __syncthreads();
@@ -264,7 +272,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 fence_sys();
                 for (int d = 0; d < R; ++d) {
                     if (is_masked(a.mask, d)) continue;
-                    st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->combine_done[a.rank], a.seq);
+                    st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->combine_done[a.rank], 1);
                 }
             }
         }
@@ -273,9 +281,16 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
     if (a.phases & 2) {
         LLHalf mine = half_of(a.peers, L, a.rank, a.half);
         if ((int)threadIdx.x < R && !is_masked(a.mask, threadIdx.x))
-            ll_wait(&mine.ctrl()->combine_done[threadIdx.x], a.seq, a.st, kErrTimeoutLLCombine, threadIdx.x, a.mask,
+            ll_wait(&mine.ctrl()->combine_done[threadIdx.x], 1, a.st, kErrTimeoutLLCombine, threadIdx.x, a.mask,
                     a.shrink != 0, blockIdx.x == 0 ? a.wait_stats : nullptr);
         __syncthreads();
+        if (threadIdx.x == 0) {
+            const int old = atom_add_acq_rel_gpu(&mine.ctrl()->crecv_finished_blocks, 1);
+            if (old == (int)gridDim.x - 1) {
+                mine.ctrl()->crecv_finished_blocks = 0;
+                for (int s = 0; s < R; ++s) mine.ctrl()->combine_done[s] = 0;
+            }
+        }
         if (aborted(a.st) && !a.shrink) return;
         const __nv_bfloat16* recv = mine.combine_recv();
         for (int t = blockIdx.x * W + warp; t < a.num_tokens; t += gridDim.x * W) {
@@ -289,20 +304,36 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 }
             }
             const uint32_t use_mask = __ballot_sync(0xffffffffu, use);
+            // Gather the (token, k) rows that contribute, then load all of a slice before summing.
+            int ks[kMaxTopk];
+            float ws[kMaxTopk];
+            int n = 0;
+            for (int k = 0; k < K; ++k) {
+                const float wv = __shfl_sync(0xffffffffu, wk, k);
+                if ((use_mask >> k) & 1u) {
+                    ks[n] = k;
+                    ws[n] = wv;
+                    ++n;
+                }
+            }
+            const __nv_bfloat16* trow = recv + (int64_t)t * K * H;
             for (int e0 = lane * 8; e0 < H; e0 += 256) {
+                int4 v[kMaxTopk];
+#pragma unroll
+                for (int q = 0; q < kMaxTopk; ++q)
+                    if (q < n) v[q] = *reinterpret_cast<const int4*>(trow + (int64_t)ks[q] * H + e0);
                 float acc[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-                for (int k = 0; k < K; ++k) {
-                    const float w = __shfl_sync(0xffffffffu, wk, k);
-                    if (!((use_mask >> k) & 1u)) continue;
-                    const int4 v = *reinterpret_cast<const int4*>(recv + ((int64_t)t * K + k) * H + e0);
-                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+                for (int q = 0; q < kMaxTopk; ++q) {
+                    if (q >= n) break;
+                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[q]);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const float2 f = __bfloat1622float2(h2[i]);
-                        acc[2 * i] = fmaf(w, f.x, acc[2 * i]);
-                        acc[2 * i + 1] = fmaf(w, f.y, acc[2 * i + 1]);
+                        acc[2 * i] = fmaf(ws[q], f.x, acc[2 * i]);
+                        acc[2 * i + 1] = fmaf(ws[q], f.y, acc[2 * i + 1]);
                     }
                 }
                 int4 o;
@@ -342,6 +373,12 @@ __global__ void ll_clean_kernel(PeerTable peers, LLLayout layout, int rank) {
         if (threadIdx.x == 0) {
             mine.ctrl()->send_finished_blocks = 0;
             mine.ctrl()->csend_finished_blocks = 0;
+            mine.ctrl()->recv_finished_blocks = 0;
+            mine.ctrl()->crecv_finished_blocks = 0;
+        }
+        if (threadIdx.x < kMaxRanks) {
+            mine.ctrl()->dispatch_done[threadIdx.x] = 0;
+            mine.ctrl()->combine_done[threadIdx.x] = 0;
         }
     }
 }

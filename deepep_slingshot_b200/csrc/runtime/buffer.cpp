@@ -256,8 +256,8 @@ pybind11::bytearray Buffer::get_local_ll_ipc_handle() const {
     return {ll_ipc_.reserved, CUDA_IPC_HANDLE_SIZE};
 }
 
-void Buffer::sync(const std::vector<int>& device_ids, const std::vector<std::optional<pybind11::bytearray>>& handles,
-                  const std::vector<std::optional<pybind11::bytearray>>& ll_handles) {
+void Buffer::sync(const std::vector<int>& device_ids, const std::vector<std::optional<pybind11::bytes>>& handles,
+                  const std::vector<std::optional<pybind11::bytes>>& ll_handles) {
     if (available_) throw std::runtime_error("buffer already synced");
     if ((int)device_ids.size() != num_ranks_ || (int)handles.size() != num_ranks_)
         throw std::runtime_error("sync: wrong number of peers");
@@ -383,13 +383,18 @@ PeerTable Buffer::ll_peers() const {
     return p;
 }
 
-void Buffer::wait_host_counters(int epoch) {
+void Buffer::wait_host_counters(int ticket) {
     const auto start = std::chrono::steady_clock::now();
     const double limit = (double)timeout_ns_ * 1e-9;
     uint64_t it = 0;
-    while (*reinterpret_cast<volatile int*>(&host_counters_->ready_epoch) != epoch) {
+    while (*reinterpret_cast<volatile int*>(&host_counters_->ready_ticket) != ticket) {
         if ((++it & 1023) == 0) {
             check_error();
+            // A faulted context never completes the notify kernel: surface the CUDA error at once.
+            const cudaError_t q = cudaStreamQuery(comm_stream_.stream());
+            if (q != cudaSuccess && q != cudaErrorNotReady)
+                throw std::runtime_error(std::string("B200 EP: CUDA error while waiting for received token counts: ") +
+                                         cudaGetErrorString(q));
             const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
             if (el > limit)
                 throw std::runtime_error("B200 EP: CPU timeout waiting for received token counts (rank " + std::to_string(rank_) + ")");
@@ -469,7 +474,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     const int E_l = cached ? 0 : num_experts / R;
     if (num_sms <= 0) num_sms = 32;
 
-    const int epoch = ++dispatch_epoch_;
+    const int ticket = ++dispatch_epoch_;
     StreamScope scope(comm_stream_, previous_event, allocate_on_comm_stream);
     auto stream = scope.comm.stream();
     auto i32 = torch::dtype(torch::kInt32).device(torch::kCUDA);
@@ -500,7 +505,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     sa.quantize = quantize_fp8 ? 1 : 0;
     sa.round_scale = round_scale ? 1 : 0;
     sa.num_ranks = R;
-    sa.wait_epoch = epoch - 1;
+    sa.dispatch_epoch = &reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->dispatch_epoch;
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
     sa.st = st;
@@ -531,8 +536,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     na.num_ranks = R;
     na.rank = rank_;
     na.cached = cached ? 1 : 0;
-    na.epoch = epoch;
-    na.parity = epoch & 1;
+    na.host_ticket = ticket;
     na.expert_alignment = std::max(1, expert_alignment);
     na.peers = peers;
     na.layout = L;
@@ -556,7 +560,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     } else if (num_worst_tokens > 0) {
         num_out_rows = num_worst_tokens;
     } else {
-        wait_host_counters(epoch);
+        wait_host_counters(ticket);
         num_recv = host_counters_->num_recv_tokens;
         num_out_rows = num_recv;
         per_expert_list.assign(host_counters_->num_recv_tokens_per_expert, host_counters_->num_recv_tokens_per_expert + E_l);
@@ -602,7 +606,6 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.recv_topk_weights = recv_topk_weights.has_value() ? recv_topk_weights->data_ptr<float>() : nullptr;
     pa.recv_src_idx = cached ? nullptr : recv_src_idx.data_ptr<int>();
     pa.cached_src_idx = cached ? cached_recv_src_idx->data_ptr<int>() : nullptr;
-    pa.epoch = epoch;
     pa.stages = 0;
     pa.st = st;
     launch_dispatch_pull(pa, num_sms, stream);
@@ -636,7 +639,6 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     const NormalLayout L = compute_normal_layout(num_nvl_bytes_, H, R);
     TORCH_CHECK(N <= L.capacity, "num_tokens exceeds the buffer capacity");
     if (num_sms <= 0) num_sms = 32;
-    const int seq = ++combine_seq_;
     StreamScope scope(comm_stream_, previous_event, allocate_on_comm_stream);
     auto stream = scope.comm.stream();
     auto out = torch::empty({N, H}, x.options());
@@ -656,7 +658,6 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     pa.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
     pa.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
     pa.num_recv_max = (int)x.size(0);
-    pa.seq = seq;
     pa.stages = 0;
     pa.st = st;
     launch_combine_push(pa, num_sms, stream);
@@ -677,7 +678,6 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     ra.bias1 = bias_1.has_value() ? bias_1->data_ptr() : nullptr;
     ra.out = out.data_ptr();
     ra.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
-    ra.seq = seq;
     ra.st = st;
     launch_combine_reduce(ra, num_sms, stream);
     EP_CUDA_CHECK(cudaGetLastError());
@@ -691,8 +691,7 @@ void Buffer::barrier(bool use_comm_stream, bool with_cpu_sync) {
     auto compute = at::cuda::getCurrentCUDAStream();
     auto stream = use_comm_stream ? comm_stream_ : compute;
     if (use_comm_stream) stream_wait(comm_stream_, compute);
-    const int epoch = ++barrier_epoch_;
-    launch_barrier(nvl_peers(), 0, rank_, num_ranks_, epoch, status(), stream.stream());
+    launch_barrier(nvl_peers(), 0, rank_, num_ranks_, status(), stream.stream());
     if (use_comm_stream) stream_wait(compute, comm_stream_);
     if (with_cpu_sync) {
         EP_CUDA_CHECK(cudaDeviceSynchronize());
@@ -733,8 +732,7 @@ Buffer::low_latency_dispatch(const torch::Tensor& x, const torch::Tensor& topk_i
                                                          " bytes (Buffer.get_low_latency_rdma_size_hint)");
     TORCH_CHECK(L.num_local_experts <= kMaxLocalExperts);
     L.num_topk = K;
-    const int seq = ++ll_dispatch_seq_;
-    const int half = seq & 1;
+    const int half = (++ll_dispatch_seq_) & 1;
     const int E_l = L.num_local_experts, slots = R * maxT;
 
     auto compute = at::cuda::getCurrentCUDAStream();
@@ -759,7 +757,6 @@ Buffer::low_latency_dispatch(const torch::Tensor& x, const torch::Tensor& topk_i
     a.use_fp8 = use_fp8 ? 1 : 0;
     a.round_scale = round_scale ? 1 : 0;
     a.use_ue8m0 = use_ue8m0 ? 1 : 0;
-    a.seq = seq;
     a.mask = mask_;
     a.shrink = enable_shrink_ ? 1 : 0;
     a.recv_count = recv_count.data_ptr<int>();
@@ -818,8 +815,7 @@ std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::functio
     TORCH_CHECK(2 * L.half_bytes <= num_rdma_bytes_, "low-latency region too small");
     TORCH_CHECK(x.size(0) == L.num_local_experts && x.size(1) == (int64_t)R * maxT, "x must be [num_local_experts, num_ranks * max_tokens, hidden]");
     L.num_topk = K;
-    const int seq = ++ll_combine_seq_;
-    const int half = seq & 1;
+    const int half = (++ll_combine_seq_) & 1;
     auto compute = at::cuda::getCurrentCUDAStream();
     auto launch_stream = return_recv_hook ? compute : comm_stream_;
     if (!return_recv_hook) stream_wait(comm_stream_, compute);
@@ -842,7 +838,6 @@ std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::functio
     a.topk_weights = topk_weights.data_ptr<float>();
     a.num_tokens = N;
     a.rank = rank_;
-    a.seq = seq;
     a.mask = mask_;
     a.shrink = enable_shrink_ ? 1 : 0;
     a.out = combined.data_ptr();

@@ -73,8 +73,8 @@ class Buffer {
     int get_local_device_id() const { return device_id_; }
     pybind11::bytearray get_local_ipc_handle() const;
     pybind11::bytearray get_local_ll_ipc_handle() const;
-    void sync(const std::vector<int>& device_ids, const std::vector<std::optional<pybind11::bytearray>>& handles,
-              const std::vector<std::optional<pybind11::bytearray>>& ll_handles);
+    void sync(const std::vector<int>& device_ids, const std::vector<std::optional<pybind11::bytes>>& handles,
+              const std::vector<std::optional<pybind11::bytes>>& ll_handles);
     void destroy();
     torch::Stream get_comm_stream() const;
     torch::Tensor get_local_buffer_tensor(const pybind11::object& dtype, int64_t offset, bool use_rdma_buffer) const;
@@ -138,7 +138,7 @@ class Buffer {
     KernelStatus status() const;
     PeerTable nvl_peers() const;
     PeerTable ll_peers() const;
-    void wait_host_counters(int epoch);
+    void wait_host_counters(int ticket);
 
     int rank_, num_ranks_, device_id_;
     int64_t num_nvl_bytes_, num_rdma_bytes_;

@@ -28,7 +28,10 @@ class _Evt:
 
 
 def _as_bytes(t: torch.Tensor) -> torch.Tensor:
-    return t.contiguous().view(torch.uint8).reshape(t.shape[0], -1)
+    cols = t.element_size()
+    for d in t.shape[1:]:
+        cols *= d
+    return t.contiguous().view(torch.uint8).reshape(t.shape[0], cols)
 
 
 def _from_bytes(b: torch.Tensor, dtype: torch.dtype, cols: int) -> torch.Tensor:

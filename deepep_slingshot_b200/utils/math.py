@@ -41,12 +41,16 @@ def per_token_cast_to_fp8(x: torch.Tensor, round_scale: bool = False) -> Tuple[t
     x_padded = torch.nn.functional.pad(x, (0, aligned_n - n), mode='constant', value=0)
     x_view = x_padded.view(m, -1, 128)
     x_amax = x_view.abs().float().amax(dim=2).view(m, -1).clamp(1e-4)
+    # Tensor/tensor divisions: one IEEE rounding, as in the kernels (a Python-scalar divisor would
+    # make torch multiply by a rounded reciprocal instead).
+    c448 = torch.full_like(x_amax, 448.0)
+    scale = x_amax / c448
     if round_scale:
-        scale = torch.pow(2.0, torch.ceil(torch.log2(x_amax / 448.0)))
-        q = (x_view.float() * (1.0 / scale).unsqueeze(2))
+        scale = torch.pow(2.0, torch.ceil(torch.log2(scale)))
+        mult = 1.0 / scale
     else:
-        scale = x_amax / 448.0
-        q = x_view.float() * (448.0 / x_amax.unsqueeze(2))
+        mult = c448 / x_amax
+    q = x_view.float() * mult.unsqueeze(2)
     q = q.clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
     return q.view(m, aligned_n)[:, :n].contiguous(), scale.view(m, -1)
 
