@@ -154,7 +154,9 @@ def main():
     x = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
     idx, w = gate.normal_routing(N, E, K, generator=g)
     idx, w = idx.cuda(), w.cuda()
-    num_sms = args.num_sms or Buffer.num_sms
+    # One rank: every byte is a local HBM copy, use every SM. Several ranks: NVLink-bound, 64 SMs
+    # (measured: 32-64 CTAs of the pull pipeline already reach ~745 GB/s from a peer).
+    num_sms = args.num_sms or (torch.cuda.get_device_properties(local).multi_processor_count if world == 1 else Buffer.num_sms)
     cfg = Buffer.get_dispatch_config(world)
     cfg.num_sms = num_sms
     nvl_bytes = Buffer.get_nvl_buffer_size_hint(N, H, world)

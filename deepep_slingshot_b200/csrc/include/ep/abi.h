@@ -103,6 +103,7 @@ struct NormalLayout {
     int64_t staging_off;     // records [capacity], record_bytes each
     int64_t combine_off;     // bf16 rows [capacity * num_ranks][hidden]
     int64_t combine_w_off;   // f32 [capacity * num_ranks][topk_pad]
+    int64_t scratch_off;     // local only: uint8 rank mask per token [capacity], then int expert counters
     int64_t total_bytes;
     int32_t capacity;        // max tokens per rank per call
     int32_t hidden;
@@ -111,7 +112,8 @@ struct NormalLayout {
     int32_t record_bytes;    // staging record stride
     int32_t num_ranks;
 };
-static_assert(sizeof(NormalLayout) == 72, "NormalLayout ABI");
+static_assert(sizeof(NormalLayout) == 80, "NormalLayout ABI");
+constexpr int kMaxExperts = kMaxRanks * kMaxLocalExperts;
 
 // Staging record of one token (written by its source rank, pulled by receivers):
 //   [x: hidden * elem bytes][scales: f32 * hidden/128 (fp8 only)][topk_idx: i32 * topk_pad][topk_w: f32 * topk_pad]

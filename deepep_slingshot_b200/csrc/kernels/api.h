@@ -30,6 +30,10 @@ struct StageArgs {
     int round_scale;             // 1: power-of-two scales
     int num_ranks;
     const int* dispatch_epoch;   // local ctrl.dispatch_epoch: wait until pull_done[r] >= it
+    const bool* is_token_in_rank;  // [N][R] or null
+    uint8_t* token_mask;         // scratch [N]: destination-rank bit mask per token (null: skip)
+    int* expert_counts;          // scratch [E]: tokens per expert (atomics; zeroed by notify after use)
+    int num_experts, num_local_experts;
     RecordFormat rec;
     int record_stride;
     KernelStatus st;
@@ -43,6 +47,8 @@ struct NotifyArgs {
     int num_ranks, rank;
     int cached;                      // 1: only publish readiness and wait (handle reuse)
     int host_ticket;                 // written to host->ready_ticket when the counts are valid
+    const uint8_t* token_mask;       // per-token destination masks computed by the stage kernel
+    int* expert_counts;              // per-expert token counts computed by the stage kernel
     int expert_alignment;
     PeerTable peers;
     NormalLayout layout;

@@ -120,15 +120,27 @@ __global__ void __launch_bounds__(256) dispatch_stage_kernel(StageArgs a) {
                 for (int b = lane; b < nb; b += 32) dst[b] = a.x_scales[t * a.scale_stride_t + b * a.scale_stride_b];
             }
         }
+        int idx = -1;
+        float w = 0.f;
+        if (lane < a.num_topk) {
+            if (a.topk_idx != nullptr) idx = (int)a.topk_idx[(int64_t)t * a.num_topk + lane];
+            if (a.topk_weights != nullptr) w = a.topk_weights[(int64_t)t * a.num_topk + lane];
+        }
         if (lane < a.topk_pad) {
-            int idx = -1;
-            float w = 0.f;
-            if (lane < a.num_topk) {
-                if (a.topk_idx != nullptr) idx = (int)a.topk_idx[(int64_t)t * a.num_topk + lane];
-                if (a.topk_weights != nullptr) w = a.topk_weights[(int64_t)t * a.num_topk + lane];
-            }
             reinterpret_cast<int*>(rec + a.rec.idx_off)[lane] = idx;
             reinterpret_cast<float*>(rec + a.rec.w_off)[lane] = w;
+        }
+        // Per-token destination-rank mask and per-expert counts for the notify step.
+        if (a.token_mask != nullptr) {
+            uint32_t bit = 0;
+            if (a.is_token_in_rank != nullptr) {
+                if (lane < a.num_ranks && a.is_token_in_rank[(int64_t)t * a.num_ranks + lane]) bit = 1u << lane;
+            } else if (idx >= 0 && idx < a.num_experts) {
+                bit = 1u << (idx / a.num_local_experts);
+            }
+            const uint32_t m = __reduce_or_sync(0xffffffffu, bit);
+            if (lane == 0) a.token_mask[t] = (uint8_t)m;
+            if (idx >= 0 && idx < a.num_experts) atomicAdd(&a.expert_counts[idx], 1);
         }
     }
 }
@@ -219,24 +231,20 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
     const int epoch = s_epoch, parity = epoch & 1;
 
     if (!a.cached) {
-        for (int i = tid; i < a.num_experts; i += nt) s_ecnt[i] = 0;
-        __syncthreads();
+        for (int i = tid; i < a.num_experts; i += nt) {
+            s_ecnt[i] = a.expert_counts[i];
+            a.expert_counts[i] = 0;  // ready for the next dispatch
+        }
         const int chunk = (a.num_tokens + nt - 1) / nt;
         const int t0 = min(a.num_tokens, tid * chunk), t1 = min(a.num_tokens, t0 + chunk);
         uint64_t lo = 0, hi = 0;
         for (int t = t0; t < t1; ++t) {
-            const uint32_t m = token_rank_mask(a, t);
+            const uint32_t m = a.token_mask[t];
             s_mask[t] = (uint8_t)m;
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 lo += (uint64_t)((m >> r) & 1u) << (16 * r);
                 hi += (uint64_t)((m >> (r + 4)) & 1u) << (16 * r);
-            }
-            if (a.topk_idx != nullptr) {
-                for (int k = 0; k < a.num_topk; ++k) {
-                    const int64_t e = a.topk_idx[(int64_t)t * a.num_topk + k];
-                    if (e >= 0 && e < a.num_experts) atomicAdd(&s_ecnt[e], 1);
-                }
             }
         }
         uint64_t tlo, thi;
@@ -342,11 +350,15 @@ void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream) {
 // (producer warp, consumer warp) pairs over an S-slot shared-memory ring. The producer's lane 0
 // TMA-loads rows (from a peer's staging, or from local expert outputs) as soon as a slot is free;
 // the consumer's lane 0 TMA-stores each landed row to its destination (local output, or a peer's
-// combine slots) and frees the slot once the store has read it. Loads never wait on store
-// completion, so both directions stay in flight.
+// combine slots) and returns the slot once the store has read it, keeping up to S/2 stores in
+// flight (a store's read of shared memory completes only as its writes drain, ~2 us over NVLink, so
+// a shallow store window starves the pipeline). Measured on B200: 32-64 CTAs of this pipeline pull
+// ~745 GB/s from one peer.
 // =================================================================================================
 constexpr int kPairs = 2;
-constexpr int kStoreLag = 2;  // stores allowed to still be reading shared memory
+
+struct PipeSmem;
+__device__ __forceinline__ void release_slots(const PipeSmem& p, int k, int lag);
 
 struct PipeSmem {
     uint8_t* slots;
@@ -375,6 +387,22 @@ __device__ __forceinline__ PipeSmem pipe_smem(uint8_t* smem, int pair, int S, in
 }
 
 static size_t pipe_smem_bytes(int S, int slot_bytes) { return (size_t)kPairs * pipe_pair_bytes(S, slot_bytes); }
+
+// Consumer lane 0, after committing the TMA store of pipeline row k: keep at most `lag` stores
+// reading shared memory and hand the slot of row k - lag back to the producer.
+__device__ __forceinline__ void release_slots(const PipeSmem& p, int k, int lag) {
+    switch (lag) {
+        case 1: bulk_wait_read<1>(); break;
+        case 2: bulk_wait_read<2>(); break;
+        case 3: bulk_wait_read<3>(); break;
+        case 4: bulk_wait_read<4>(); break;
+        case 5: bulk_wait_read<5>(); break;
+        case 6: bulk_wait_read<6>(); break;
+        case 7: bulk_wait_read<7>(); break;
+        default: bulk_wait_read<8>(); lag = 8; break;
+    }
+    if (k >= lag) mbar_arrive(&p.empty[(k - lag) % p.S]);
+}
 
 __device__ __forceinline__ void pipe_init(const PipeSmem& p) {
     if (lane_id() == 0) {
@@ -464,15 +492,14 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
                         tma_load_1d(p.slots + (size_t)slot * slot_bytes, g, a.rec.bytes, &p.full[slot]);
                     }
                 }
-                if (aborted(a.st)) break;
             }
-            if (aborted(a.st)) break;
         }
     } else {
         const int x_bytes = a.rec.x_bytes;
         const int nb = a.rec.scale_bytes > 0 ? a.layout.hidden / 128 : 0;
         const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
         const int E_l = a.num_local_experts, lo_e = a.rank * E_l;
+        const int lag = S / 2 < 4 ? S / 2 : 4;  // peer loads are the slow leg: favour loads in flight
         for (int j = r0; j < r1; ++j) {
             const int k = j - r0, slot = k % S;
             int good = 1;
@@ -500,10 +527,7 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
             }
             if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[slot];
             __syncwarp();
-            if (lane == 0) {
-                bulk_wait_read<kStoreLag>();
-                if (k >= kStoreLag) mbar_arrive(&p.empty[(k - kStoreLag) % S]);
-            }
+            if (lane == 0) release_slots(p, k, lag);
         }
         if (lane == 0) bulk_wait<0>();
     }
@@ -532,8 +556,8 @@ static int pipe_stages(int slot_bytes, int max_stages) {
 void launch_dispatch_pull(const PullArgs& a_in, int num_sms, cudaStream_t stream) {
     PullArgs a = a_in;
     const int slot_bytes = (a.rec.bytes + 127) / 128 * 128;
-    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 8);
-    if (a.stages < kStoreLag + 2) a.stages = kStoreLag + 2;
+    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 16);
+    if (a.stages < 4) a.stages = 4;
     const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
     cudaFuncSetAttribute(dispatch_pull_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dispatch_pull_kernel<<<num_sms, 64 * kPairs, smem, stream>>>(a);
@@ -588,7 +612,6 @@ __global__ void __launch_bounds__(64 * kPairs) combine_push_kernel(CombinePushAr
                                 row_bytes, &p.full[slot]);
                 }
             }
-            if (aborted(a.st)) break;
         }
     } else {
         int sent = 0;  // lane d: rows sent to destination d
@@ -614,29 +637,25 @@ __global__ void __launch_bounds__(64 * kPairs) combine_push_kernel(CombinePushAr
             }
             if (lane == d) ++sent;
             __syncwarp();
-            if (lane == 0) {
-                bulk_wait_read<kStoreLag>();
-                if (k >= kStoreLag) mbar_arrive(&p.empty[(k - kStoreLag) % S]);
-            }
+            if (lane == 0) release_slots(p, k, S / 2);
         }
-        // All rows of this pair are complete in the destinations' memory: publish the counts.
+        // The bulk stores of this pair are complete (and every lane's weight stores performed
+        // system-wide) before the counts are published.
         if (lane == 0) {
             bulk_wait<0>();
             fence_proxy_async_global();
         }
+        fence_sys();
         __syncwarp();
-        if (lane < R && sent > 0) {
-            fence_sys();
-            red_add_release_sys(&ctrl_of(a.peers, a.layout, lane)->combine_arrived, sent);
-        }
+        if (lane < R && sent > 0) red_add_release_sys(&ctrl_of(a.peers, a.layout, lane)->combine_arrived, sent);
     }
 }
 
 void launch_combine_push(const CombinePushArgs& a_in, int num_sms, cudaStream_t stream) {
     CombinePushArgs a = a_in;
     const int slot_bytes = (a.layout.hidden * 2 + 127) / 128 * 128;
-    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 8);
-    if (a.stages < kStoreLag + 2) a.stages = kStoreLag + 2;
+    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 16);
+    if (a.stages < 4) a.stages = 4;
     const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
     cudaFuncSetAttribute(combine_push_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     combine_push_kernel<<<num_sms, 64 * kPairs, smem, stream>>>(a);
@@ -646,17 +665,17 @@ void launch_combine_push(const CombinePushArgs& a_in, int num_sms, cudaStream_t 
 // combine reduce: fp32 sum of the <= R contributions per token (+ bias) -> bf16; top-k weight sum.
 // One warp per token; all contributions of a 256-element slice are loaded before they are summed.
 // =================================================================================================
-template <int kU>
+template <int kU, int kN>
 __device__ __forceinline__ void reduce_rows(const __nv_bfloat16* rows, const int* src_rows, int n, int H, int t,
                                             const void* bias0, const void* bias1, void* out, int e_start) {
     const int lane = lane_id();
-    int4 v[kU][kMaxRanks];
+    int4 v[kU][kN];
     for (int e0 = e_start + lane * 8; e0 - lane * 8 < H; e0 += 256 * kU) {
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int e = e0 + u * 256;
 #pragma unroll
-            for (int q = 0; q < kMaxRanks; ++q)
+            for (int q = 0; q < kN; ++q)
                 if (q < n && e < H) v[u][q] = *reinterpret_cast<const int4*>(rows + (int64_t)src_rows[q] * H + e);
         }
 #pragma unroll
@@ -667,7 +686,7 @@ __device__ __forceinline__ void reduce_rows(const __nv_bfloat16* rows, const int
 #pragma unroll
             for (int i = 0; i < 8; ++i) acc[i] = 0.f;
 #pragma unroll
-            for (int q = 0; q < kMaxRanks; ++q) {
+            for (int q = 0; q < kN; ++q) {
                 if (q >= n) break;
                 const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[u][q]);
 #pragma unroll
@@ -700,7 +719,7 @@ __device__ __forceinline__ void reduce_rows(const __nv_bfloat16* rows, const int
     }
 }
 
-__global__ void __launch_bounds__(256) combine_reduce_kernel(CombineReduceArgs a) {
+__global__ void __launch_bounds__(256, 2) combine_reduce_kernel(CombineReduceArgs a) {
     __shared__ int s_base[kMaxRanks];
     __shared__ int s_seq;
     const int R = a.num_ranks, K = a.num_topk, H = a.hidden;
@@ -735,8 +754,8 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(CombineReduceArgs a
                 const int v = __shfl_sync(0xffffffffu, my_row, r);
                 if (r < R && v >= 0) src_rows[n++] = v;
             }
-            if (n <= 2) reduce_rows<4>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
-            else reduce_rows<1>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+            if (n <= 2) reduce_rows<4, 2>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+            else reduce_rows<1, kMaxRanks>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
             if (a.out_topk_weights != nullptr && lane < K) {
                 float w = 0.f;
                 if (a.has_weights)

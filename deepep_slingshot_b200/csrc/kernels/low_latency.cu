@@ -44,7 +44,14 @@ __device__ __forceinline__ LLHalf half_of(const PeerTable& p, const LLLayout& l,
     return LLHalf{static_cast<uint8_t*>(p.base[rank]) + (int64_t)half * l.half_bytes, &l};
 }
 
-__device__ __forceinline__ bool is_masked(const int* mask, int r) { return mask != nullptr && ld_volatile(mask + r) != 0; }
+// Shrink-mode mask, snapshotted into shared memory once per block (a volatile global load per
+// (token, k) would put a round trip to L2 on every message).
+__device__ __forceinline__ uint32_t load_mask_bits(const int* mask, int R) {
+    uint32_t m = 0;
+    if (mask != nullptr)
+        for (int r = 0; r < R; ++r) m |= (ld_volatile(mask + r) != 0 ? 1u : 0u) << r;
+    return m;
+}
 
 // Bounded wait used by LL receivers. In shrink mode an expired wait masks `peer` and succeeds.
 __device__ bool ll_wait(const int* flag, int target, const KernelStatus& st, int code, int peer, int* mask, bool shrink,
@@ -81,6 +88,10 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
     const int nb = H / 128;
     const int row_bytes = a.use_fp8 ? H : 2 * H;
     const int warp_buf_bytes = (row_bytes + nb * 4 + 127) / 128 * 128;
+    __shared__ uint32_t s_masked;
+    if (threadIdx.x == 0) s_masked = load_mask_bits(a.mask, R);
+    __syncthreads();
+    uint32_t masked = s_masked;
 
     if (a.phases & 1) {
         uint8_t* buf = smem + (size_t)warp * warp_buf_bytes;
@@ -105,7 +116,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
                 if (e >= 0 && e < L.num_experts) {
                     dst_rank = (int)(e / E_l);
                     le = (int)(e % E_l);
-                    if (is_masked(a.mask, dst_rank)) {
+                    if (((masked >> (dst_rank))) & 1u) {
                         dst_rank = -1;
                     } else {
                         LLHalf h = half_of(a.peers, L, dst_rank, a.half);
@@ -150,7 +161,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
                 mine.ctrl()->send_finished_blocks = 0;
                 fence_sys();
                 for (int d = 0; d < R; ++d) {
-                    if (is_masked(a.mask, d)) continue;
+                    if (((masked >> (d))) & 1u) continue;
                     st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->dispatch_done[a.rank], 1);
                 }
             }
@@ -159,7 +170,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
 
     if (a.phases & 2) {
         LLHalf mine = half_of(a.peers, L, a.rank, a.half);
-        if ((int)threadIdx.x < R && !is_masked(a.mask, threadIdx.x))
+        if ((int)threadIdx.x < R && !((masked >> threadIdx.x) & 1u))
             ll_wait(&mine.ctrl()->dispatch_done[threadIdx.x], 1, a.st, kErrTimeoutLLDispatch, threadIdx.x, a.mask,
                     a.shrink != 0, blockIdx.x == 0 ? a.wait_stats : nullptr);
         __syncthreads();
@@ -222,6 +233,10 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
     const int H = L.hidden, K = L.num_topk, R = L.num_ranks, E_l = L.num_local_experts;
     const int slots = R * L.max_tokens;
     const int row_bytes = 2 * H;
+    __shared__ uint32_t s_masked;
+    if (threadIdx.x == 0) s_masked = load_mask_bits(a.mask, R);
+    __syncthreads();
+    uint32_t masked = s_masked;
 
     if (a.phases & 1) {
         uint8_t* buf = smem + (size_t)warp * ((row_bytes + 127) / 128 * 128);
@@ -243,7 +258,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 if (lane == 0) report_error(a.st, kErrBounds, src, t);
                 continue;
             }
-            if (is_masked(a.mask, src)) continue;
+            if (((masked >> (src))) & 1u) continue;
             if (lane == 0) {
                 bulk_wait_read<0>();
                 mbar_arrive_expect_tx(&s_bar[warp], row_bytes);
@@ -271,7 +286,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 mine.ctrl()->csend_finished_blocks = 0;
                 fence_sys();
                 for (int d = 0; d < R; ++d) {
-                    if (is_masked(a.mask, d)) continue;
+                    if (((masked >> (d))) & 1u) continue;
                     st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->combine_done[a.rank], 1);
                 }
             }
@@ -280,7 +295,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
 
     if (a.phases & 2) {
         LLHalf mine = half_of(a.peers, L, a.rank, a.half);
-        if ((int)threadIdx.x < R && !is_masked(a.mask, threadIdx.x))
+        if ((int)threadIdx.x < R && !((masked >> threadIdx.x) & 1u))
             ll_wait(&mine.ctrl()->combine_done[threadIdx.x], 1, a.st, kErrTimeoutLLCombine, threadIdx.x, a.mask,
                     a.shrink != 0, blockIdx.x == 0 ? a.wait_stats : nullptr);
         __syncthreads();
@@ -292,13 +307,14 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
             }
         }
         if (aborted(a.st) && !a.shrink) return;
+        masked = load_mask_bits(a.mask, R);  // ranks masked by an expired wait above
         const __nv_bfloat16* recv = mine.combine_recv();
         for (int t = blockIdx.x * W + warp; t < a.num_tokens; t += gridDim.x * W) {
             float wk = 0.f;
             int use = 0;
             if (lane < K) {
                 const int64_t e = a.topk_idx[(int64_t)t * K + lane];
-                if (e >= 0 && e < L.num_experts && !is_masked(a.mask, (int)(e / E_l))) {
+                if (e >= 0 && e < L.num_experts && !((masked >> (int)(e / E_l)) & 1u)) {
                     use = 1;
                     wk = a.topk_weights[(int64_t)t * K + lane];
                 }

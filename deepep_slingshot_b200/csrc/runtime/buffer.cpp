@@ -103,7 +103,7 @@ static int64_t normal_bytes_per_token(int hidden, int num_ranks, int* record_str
     const RecordFormat f8 = record_format(hidden, kMaxTopk, true);
     const int rec = (int)align_up(std::max(bf.bytes, f8.bytes), kAlign);
     if (record_stride) *record_stride = rec;
-    return (int64_t)num_ranks * 4 + rec + (int64_t)num_ranks * hidden * 2 + (int64_t)num_ranks * kMaxTopk * 4;
+    return (int64_t)num_ranks * 4 + rec + (int64_t)num_ranks * hidden * 2 + (int64_t)num_ranks * kMaxTopk * 4 + 1;
 }
 
 NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ranks) {
@@ -111,7 +111,7 @@ NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ran
     int rec = 0;
     const int64_t per_token = normal_bytes_per_token(hidden, num_ranks, &rec);
     const int64_t ctrl = align_up(sizeof(NormalCtrl), 4096);
-    const int64_t slack = 8 * kAlign;
+    const int64_t slack = 8 * kAlign + (int64_t)kMaxExperts * 4;
     int64_t cap = region_bytes > ctrl + slack ? (region_bytes - ctrl - slack) / per_token : 0;
     cap = cap / 32 * 32;
     l.capacity = (int32_t)std::min<int64_t>(cap, 1 << 24);
@@ -125,7 +125,8 @@ NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ran
     l.staging_off = align_up(l.list_off + (int64_t)num_ranks * l.capacity * 4, kAlign);
     l.combine_off = align_up(l.staging_off + (int64_t)l.capacity * rec, kAlign);
     l.combine_w_off = align_up(l.combine_off + (int64_t)l.capacity * num_ranks * hidden * 2, kAlign);
-    l.total_bytes = align_up(l.combine_w_off + (int64_t)l.capacity * num_ranks * kMaxTopk * 4, kAlign);
+    l.scratch_off = align_up(l.combine_w_off + (int64_t)l.capacity * num_ranks * kMaxTopk * 4, kAlign);
+    l.total_bytes = align_up(l.scratch_off + align_up(l.capacity, kAlign) + (int64_t)kMaxExperts * 4, kAlign);
     return l;
 }
 
@@ -133,7 +134,7 @@ int64_t normal_region_size_for(int num_max_tokens, int hidden, int num_ranks) {
     const int64_t per_token = normal_bytes_per_token(hidden, num_ranks, nullptr);
     const int64_t ctrl = align_up(sizeof(NormalCtrl), 4096);
     const int64_t tokens = align_up(num_max_tokens, 32);
-    return align_up(ctrl + 8 * kAlign + tokens * per_token + 16 * kAlign, 2 << 20);
+    return align_up(ctrl + 8 * kAlign + tokens * per_token + 16 * kAlign + (int64_t)kMaxExperts * 4, 2 << 20);
 }
 
 LLLayout compute_ll_layout(int64_t region_bytes, int max_tokens, int hidden, int num_experts, int num_ranks) {
@@ -219,7 +220,7 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
-    EP_CUDA_CHECK(cudaMemset(nvl_base_, 0, std::min<int64_t>(num_nvl_bytes_, align_up(sizeof(NormalCtrl), 4096))));
+    EP_CUDA_CHECK(cudaMemset(nvl_base_, 0, num_nvl_bytes_));
     EP_CUDA_CHECK(cudaIpcGetMemHandle(&nvl_ipc_, nvl_base_));
     if (num_rdma_bytes_ > 0) {
         num_rdma_bytes_ = align_up(num_rdma_bytes_, 2 << 20);
@@ -506,6 +507,11 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     sa.round_scale = round_scale ? 1 : 0;
     sa.num_ranks = R;
     sa.dispatch_epoch = &reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->dispatch_epoch;
+    sa.token_mask = cached ? nullptr : my_base + L.scratch_off;
+    sa.expert_counts = cached ? nullptr : reinterpret_cast<int*>(my_base + L.scratch_off + align_up(L.capacity, kAlign));
+    sa.is_token_in_rank = (!cached && is_token_in_rank.has_value()) ? is_token_in_rank->data_ptr<bool>() : nullptr;
+    sa.num_experts = cached ? 0 : num_experts;
+    sa.num_local_experts = E_l;
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
     sa.st = st;
@@ -537,6 +543,8 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     na.rank = rank_;
     na.cached = cached ? 1 : 0;
     na.host_ticket = ticket;
+    na.token_mask = sa.token_mask;
+    na.expert_counts = sa.expert_counts;
     na.expert_alignment = std::max(1, expert_alignment);
     na.peers = peers;
     na.layout = L;
