@@ -1,0 +1,50 @@
+"""Permute dispatched tokens into the expert-grouped layout of the grouped GEMMs, and back.
+
+`permute` groups the rows of every (token, k) selection by local expert (deterministic order),
+padding each expert's block to `alignment` rows, and returns the map needed by `unpermute`.
+`unpermute` is the top-k weighted fp32 gather-sum back to one row per token (bf16).
+The torch functions `permute_reference` / `unpermute_reference` are the numerics oracle.
+"""
+from typing import NamedTuple, Optional
+
+import torch
+
+from .._ext import require_ext
+
+
+class Permuted(NamedTuple):
+    x: torch.Tensor                 # [rows, H] grouped by expert (rows past offsets[E] unused)
+    scales: Optional[torch.Tensor]  # [rows, H/128] FP8 block scales
+    probs: Optional[torch.Tensor]   # [rows] top-k weight of each grouped row
+    row_map: torch.Tensor           # [N, K] int32 grouped row of (t, k), -1 if none
+    expert_offsets: torch.Tensor    # [E+1] int32, aligned exclusive prefix
+    expert_counts: torch.Tensor     # [E] int32, unpadded counts
+
+
+def permute(x: torch.Tensor, topk_idx: torch.Tensor, num_experts: int, alignment: int = 1,
+            probs: Optional[torch.Tensor] = None, x_scales: Optional[torch.Tensor] = None,
+            num_out_rows: int = 0) -> Permuted:
+    out = require_ext().permute(x, x_scales, topk_idx, probs, num_experts, alignment, num_out_rows)
+    return Permuted(*out)
+
+
+def unpermute(y: torch.Tensor, row_map: torch.Tensor, weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return require_ext().unpermute(y, row_map, weights)
+
+
+def permute_reference(topk_idx: torch.Tensor, num_experts: int, alignment: int = 1):
+    """(counts, aligned offsets) of the grouped layout, computed with torch."""
+    valid = topk_idx[topk_idx >= 0]
+    counts = torch.bincount(valid, minlength=num_experts)[:num_experts].to(torch.int32)
+    aligned = (counts + alignment - 1) // alignment * alignment
+    offsets = torch.zeros(num_experts + 1, dtype=torch.int32, device=topk_idx.device)
+    offsets[1:] = aligned.cumsum(0)
+    return counts, offsets
+
+
+def unpermute_reference(y: torch.Tensor, row_map: torch.Tensor, weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    N, K = row_map.shape
+    w = weights if weights is not None else torch.ones((N, K), device=y.device)
+    valid = row_map >= 0
+    g = y[row_map.clamp(min=0).long()].float() * (w * valid).unsqueeze(-1)
+    return g.sum(1).to(torch.bfloat16)

@@ -17,6 +17,7 @@ SOURCES = [
     os.path.join(CSRC, "kernels", "intranode.cu"),
     os.path.join(CSRC, "kernels", "low_latency.cu"),
     os.path.join(CSRC, "kernels", "quant.cu"),
+    os.path.join(CSRC, "kernels", "permute.cu"),
 ]
 
 NVCC_FLAGS = [

@@ -1,0 +1,43 @@
+"""GPU tests of the standalone sm_100a ops against torch oracles: permute / unpermute."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize('N,H,E,K,align,fp8', [(1000, 1024, 32, 8, 128, True), (4096, 7168, 32, 8, 128, True),
+                                                (77, 256, 8, 2, 1, False), (513, 2048, 256, 8, 64, False)])
+def test_permute_unpermute(N, H, E, K, align, fp8):
+    from deepep_slingshot_b200.ops.permute import permute, permute_reference, unpermute, unpermute_reference
+    from deepep_slingshot_b200.utils.math import per_token_cast_to_fp8
+    g = torch.Generator().manual_seed(N)
+    x = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)]).cuda()
+    idx[torch.rand((N, K), generator=g).cuda() < 0.1] = -1
+    w = torch.rand((N, K), generator=g).cuda()
+    xs = None
+    if fp8:
+        x, xs = per_token_cast_to_fp8(x)
+    p = permute(x, idx, E, alignment=align, probs=w, x_scales=xs)
+    p2 = permute(x, idx, E, alignment=align, probs=w, x_scales=xs)
+    torch.cuda.synchronize()
+    counts, offsets = permute_reference(idx, E, align)
+    assert torch.equal(p.expert_counts, counts) and torch.equal(p.expert_offsets, offsets)
+    assert torch.equal(p.row_map, p2.row_map)  # deterministic order
+    rm = p.row_map
+    valid = rm >= 0
+    assert torch.equal(valid, idx >= 0)
+    rows = rm[valid].long()
+    assert rows.unique().numel() == rows.numel()
+    t_of = torch.arange(N, device='cuda').unsqueeze(1).expand(N, K)[valid]
+    e_of = idx[valid]
+    assert ((rows >= offsets[e_of].long()) & (rows < (offsets[e_of] + counts[e_of]).long())).all()
+    assert torch.equal(p.x[rows].view(torch.uint8), x[t_of].view(torch.uint8))
+    assert torch.equal(p.probs[rows], w[valid])
+    if fp8:
+        assert torch.equal(p.scales[rows], xs[t_of])
+    # unpermute (bf16 expert outputs)
+    y = torch.randn((p.x.shape[0], H), generator=g).to(torch.bfloat16).cuda()
+    out = unpermute(y, rm, w)
+    ref = unpermute_reference(y, rm, w)
+    assert torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=1e-2)
