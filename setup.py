@@ -18,6 +18,7 @@ SOURCES = [
     os.path.join(CSRC, "kernels", "low_latency.cu"),
     os.path.join(CSRC, "kernels", "quant.cu"),
     os.path.join(CSRC, "kernels", "permute.cu"),
+    os.path.join(CSRC, "kernels", "permute_noalloc.cu"),
 ]
 
 NVCC_FLAGS = [
