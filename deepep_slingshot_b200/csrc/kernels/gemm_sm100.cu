@@ -1,0 +1,316 @@
+// Grouped block-scaled FP8 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+//   D[m, n] = sum_kb  sa[m, kb] * sb[e, n/128, kb] * sum_{k in block kb} A[m, k] * B_e[n, k]
+//
+// A: [rows, K] e4m3, rows grouped by expert e at [offsets[e], offsets[e+1]) (128-aligned blocks, the
+//    layout `permute(..., alignment=128)` produces); sa: [rows, K/128] fp32 (1x128 activation scales).
+// B: [E, N, K] e4m3 (K-major expert weights); sb: [E, N/128, K/128] fp32 (128x128 weight scales).
+// D: [rows, N] bf16.
+//
+// The reference has no GEMM (its expert compute comes from DeepGEMM via SGLang,
+// backend/tests/sglang_dispatcher_smoke.py:107-124); this kernel is new. Structure:
+//  * one persistent CTA per SM walks tiles (expert, m-tile, n-tile) with n innermost, so a 128-row A
+//    tile and an expert's weights stay in L2 while neighbouring CTAs use them;
+//  * warp 0, one thread: TMA 2D loads (128B swizzle, no multicast) of the A and B tiles of every
+//    128-wide K block into an S-stage shared-memory ring;
+//  * warp 1, one thread: four `tcgen05.mma.cta_group::1.kind::f8f6f4` (M=128, N=128, K=32) per K
+//    block into one of two TMEM accumulators (K blocks alternate), then `tcgen05.commit` frees the
+//    shared-memory stage and publishes the TMEM buffer;
+//  * warps 2..9: read the K-block partial with `tcgen05.ld`, release the TMEM buffer at once, and
+//    accumulate sa*sb*partial in fp32 registers (the per-block scale promotion that fp32 scales need);
+//    after the last K block they write bf16 rows.
+// Every mbarrier wait is bounded (a status is reported, the kernel returns).
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "../include/ep/device.cuh"
+#include "gemm.h"
+
+namespace ep {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 128;  // tile; BK = 128 fp8 = one 128-byte swizzle row
+constexpr int kStageBytes = (kBM + kBN) * kBK;  // 32 KiB
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 2 * kBN;        // two fp32 accumulators of 128 columns
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major tile, 128-byte swizzle, 8-row core groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3fffu);          // start address
+    d |= (uint64_t)1 << 16;                           // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;                 // stride byte offset: next 8-row group
+    d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                           // layout: 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor, kind::f8f6f4: E4M3 x E4M3 -> F32, both K-major, M = 128, N = kBN.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%"
+        "22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Bounded wait; on expiry reports and returns false (the caller abandons the tile loop).
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const KernelStatus& st) {
+    return mbar_wait(bar, parity, st, kErrTimeoutTma);
+}
+
+struct TileInfo {
+    int e, m0, n0;
+};
+
+// Map a linear tile index to (expert, m0, n0) using the per-expert m-tile prefix in shared memory.
+__device__ __forceinline__ bool tile_of(int t, const int* s_mt_prefix, int E, int n_tiles, const int* offsets, TileInfo& ti) {
+    const int total = s_mt_prefix[E] * n_tiles;
+    if (t >= total) return false;
+    const int mt = t / n_tiles, nt = t % n_tiles;
+    int lo = 0, hi = E - 1;  // expert with s_mt_prefix[e] <= mt < s_mt_prefix[e+1]
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_mt_prefix[mid] <= mt) lo = mid;
+        else hi = mid - 1;
+    }
+    ti.e = lo;
+    ti.m0 = offsets[lo] + (mt - s_mt_prefix[lo]) * kBM;
+    ti.n0 = nt * kBN;
+    return true;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                     const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
+    __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_mt_prefix[kMaxGemmExperts + 1];
+
+    const int warp = warp_id(), lane = lane_id();
+    const int S = a.stages;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int KB = a.k / kBK;
+    const int n_tiles = a.n / kBN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_tfull[b], 1);
+            mbar_init(&s_tempty[b], kEpiWarps);
+        }
+        fence_mbar_init();
+        int acc = 0;
+        s_mt_prefix[0] = 0;
+        for (int e = 0; e < a.num_experts; ++e) {
+            const int rows = a.expert_counts != nullptr ? a.expert_counts[e] : a.offsets[e + 1] - a.offsets[e];
+            acc += (rows + kBM - 1) / kBM;
+            s_mt_prefix[e + 1] = acc;
+        }
+    }
+    if (warp == 1) {  // TMEM allocation: one warp, power-of-two columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            TileInfo ti;
+            for (int t = blockIdx.x; ok && tile_of(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int s = g % S;
+                    ok = wait_bar(&s_empty[s], ((g / S) & 1) ^ 1, a.st);
+                    if (!ok) break;
+                    uint8_t* sa_tile = smem + (size_t)s * kStageBytes;
+                    uint8_t* sb_tile = sa_tile + kBM * kBK;
+                    mbar_arrive_expect_tx(&s_full[s], kStageBytes);
+                    tma_load_2d(sa_tile, &map_a, kb * kBK, ti.m0, &s_full[s]);
+                    tma_load_2d(sb_tile, &map_b, kb * kBK, ti.e * a.n + ti.n0, &s_full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_e4m3_f32(kBM, kBN);
+            uint32_t g = 0;
+            bool ok = true;
+            TileInfo ti;
+            for (int t = blockIdx.x; ok && tile_of(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int s = g % S, b = g & 1;
+                    ok = wait_bar(&s_tempty[b], ((g >> 1) & 1) ^ 1, a.st) && wait_bar(&s_full[s], (g / S) & 1, a.st);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t sa_addr = smem_u32(smem + (size_t)s * kStageBytes);
+                    const uint32_t sb_addr = sa_addr + kBM * kBK;
+                    const uint64_t da = smem_desc_sw128(sa_addr), db = smem_desc_sw128(sb_addr);
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(b * kBN);
+#pragma unroll
+                    for (int k = 0; k < kBK / 32; ++k)  // K = 32 per instruction = 32 bytes: +2 in 16-byte units
+                        mma_f8(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, k > 0 ? 1u : 0u);
+                    mma_commit(&s_empty[s]);
+                    mma_commit(&s_tfull[b]);
+                }
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue / scale promotion
+        const int ew = warp - 2;
+        const int q = warp & 3;      // TMEM lane quarter this warp may access
+        const int h = ew >> 2;       // column half: [64h, 64h + 64)
+        const int row = 32 * q + lane;
+        uint32_t g = 0;
+        bool ok = true;
+        TileInfo ti;
+        for (int t = blockIdx.x; ok && tile_of(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+            float acc[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            const int m = ti.m0 + row;
+            const float* sa_row = a.sa + (int64_t)m * KB;
+            const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + ti.n0 / 128) * KB;
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int b = g & 1;
+                const float scale = sa_row[kb] * sb_blk[kb];
+                int good = 1;
+                if (lane == 0) good = wait_bar(&s_tfull[b], (g >> 1) & 1, a.st) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, good, 0)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                float v[64];
+                const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + 64 * h);
+                tmem_ld_32(taddr, v);
+                tmem_ld_32(taddr + 32, v + 32);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_tempty[b]);
+#pragma unroll
+                for (int i = 0; i < 64; ++i) acc[i] = fmaf(scale, v[i], acc[i]);
+            }
+            if (!ok) break;
+            __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + 64 * h;
+#pragma unroll
+            for (int c = 0; c < 64; c += 8) {
+                int4 o;
+                __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[c + 2 * i], acc[c + 2 * i + 1]);
+                *reinterpret_cast<int4*>(d + c) = o;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Host side: tensor maps through the driver entry point (no libcuda link), launch.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D uint8 map over [rows][cols] (row-major), box 128 x 128 bytes, 128-byte swizzle.
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {128, 128};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
+    GemmArgs a = args_in;
+    if (a.k % kBK != 0 || a.n % kBN != 0 || a.num_experts > kMaxGemmExperts || a.rows <= 0) return 1;
+    CUtensorMap map_a, map_b;
+    if (!make_map_u8(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
+    if (!make_map_u8(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k)) return 2;
+    if (a.stages <= 0) a.stages = 6;
+    if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
+    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
+    cudaFuncSetAttribute(grouped_gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    grouped_gemm_fp8_kernel<<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace ep

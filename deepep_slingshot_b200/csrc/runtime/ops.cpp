@@ -2,15 +2,83 @@
 #include "ops.hpp"
 
 #include <ATen/cuda/CUDAContext.h>
+#include <cstring>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include "../kernels/api.h"
 #include "../kernels/permute.h"
+#include "../kernels/gemm.h"
 
 namespace ep {
 
 namespace {
+
+// Host-mapped error page shared by the standalone ops (timeouts of bounded waits land here).
+ErrorState* op_error_page(ErrorState** dev_ptr) {
+    static ErrorState* host = nullptr;
+    static ErrorState* dev = nullptr;
+    if (host == nullptr) {
+        TORCH_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(ErrorState), cudaHostAllocMapped) == cudaSuccess);
+        std::memset(host, 0, sizeof(ErrorState));
+        TORCH_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev), host, 0) == cudaSuccess);
+    }
+    *dev_ptr = dev;
+    return host;
+}
+
+std::tuple<int, int, int, int> op_error_state(bool clear) {
+    ErrorState* dev;
+    ErrorState* h = op_error_page(&dev);
+    auto r = std::make_tuple(h->code, h->peer, h->detail, h->rank);
+    if (clear) std::memset(h, 0, sizeof(ErrorState));
+    return r;
+}
+
+KernelStatus op_status(double timeout_s) {
+    KernelStatus s{};
+    op_error_page(&s.host_error);
+    s.abort_flag = nullptr;
+    s.timeout_ns = (uint64_t)(timeout_s * 1e9);
+    return s;
+}
+
+// Grouped block-scaled FP8 GEMM (tcgen05): d[rows, n] = per-expert A x B_e^T with 1x128 / 128x128 scales.
+torch::Tensor grouped_gemm_fp8(const torch::Tensor& a, const torch::Tensor& sa, const torch::Tensor& b, const torch::Tensor& sb,
+                               const torch::Tensor& offsets, const std::optional<torch::Tensor>& counts, int num_sms,
+                               double timeout_s) {
+    TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.is_contiguous() && a.scalar_type() == torch::kFloat8_e4m3fn);
+    TORCH_CHECK(b.dim() == 3 && b.is_contiguous() && b.scalar_type() == torch::kFloat8_e4m3fn);
+    const int rows = (int)a.size(0), k = (int)a.size(1), E = (int)b.size(0), n = (int)b.size(1);
+    TORCH_CHECK(b.size(2) == k && k % 128 == 0 && n % 128 == 0, "k and n must be multiples of 128");
+    TORCH_CHECK(sa.scalar_type() == torch::kFloat32 && sa.is_contiguous() && sa.size(0) == rows && sa.size(1) == k / 128);
+    TORCH_CHECK(sb.scalar_type() == torch::kFloat32 && sb.is_contiguous() && sb.size(0) == E && sb.size(1) == n / 128 &&
+                sb.size(2) == k / 128);
+    TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() == E + 1);
+    if (counts.has_value()) TORCH_CHECK(counts->scalar_type() == torch::kInt32 && counts->numel() == E);
+    auto d = torch::empty({rows, n}, a.options().dtype(torch::kBFloat16));
+    if (num_sms <= 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    GemmArgs g{};
+    g.a = a.data_ptr();
+    g.sa = sa.data_ptr<float>();
+    g.b = b.data_ptr();
+    g.sb = sb.data_ptr<float>();
+    g.offsets = offsets.data_ptr<int>();
+    g.expert_counts = counts.has_value() ? counts->data_ptr<int>() : nullptr;
+    g.d = d.data_ptr();
+    g.rows = rows;
+    g.n = n;
+    g.k = k;
+    g.num_experts = E;
+    g.st = op_status(timeout_s);
+    const int rc = launch_grouped_gemm_fp8(g, num_sms, at::cuda::getCurrentCUDAStream());
+    TORCH_CHECK(rc == 0, "grouped_gemm_fp8 launch failed (code " + std::to_string(rc) + ")");
+    return d;
+}
 
 std::tuple<torch::Tensor, torch::Tensor> per_token_cast_to_fp8(const torch::Tensor& x, bool round_scale) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16,
@@ -105,6 +173,10 @@ void register_ops(pybind11::module_& m) {
     m.def("permute", &permute, pybind11::arg("x"), pybind11::arg("x_scales"), pybind11::arg("topk_idx"), pybind11::arg("probs"),
           pybind11::arg("num_experts"), pybind11::arg("alignment") = 1, pybind11::arg("num_out_rows") = 0);
     m.def("unpermute", &unpermute);
+    m.def("grouped_gemm_fp8", &grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"), pybind11::arg("b"), pybind11::arg("sb"),
+          pybind11::arg("offsets"), pybind11::arg("counts") = pybind11::none(), pybind11::arg("num_sms") = 0,
+          pybind11::arg("timeout_s") = 10.0);
+    m.def("op_error_state", &op_error_state, pybind11::arg("clear") = false);
     m.def("per_token_cast_to_fp8", &per_token_cast_to_fp8, pybind11::arg("x"), pybind11::arg("round_scale") = false);
     m.def("per_token_cast_back", &per_token_cast_back);
 }

@@ -1,0 +1,57 @@
+"""Grouped GEMMs on the B200 tensor cores (tcgen05 + TMEM, hand-written sm_100a kernels).
+
+`grouped_gemm_fp8`: rows of A grouped by expert (128-aligned blocks from `permute(..., alignment=128)`),
+per-token 1x128 activation scales, 128x128 weight scales, fp32 promotion per 128-wide K block, bf16 out.
+`grouped_gemm_fp8_reference` is the fp32 torch oracle.
+"""
+from typing import Optional
+
+import torch
+
+from .._ext import require_ext
+
+
+def grouped_gemm_fp8(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, offsets: torch.Tensor,
+                     counts: Optional[torch.Tensor] = None, num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
+    return require_ext().grouped_gemm_fp8(a, sa, b, sb, offsets, counts, num_sms, timeout_s)
+
+
+def op_error_state(clear: bool = False):
+    """(code, peer, detail, rank) of the last bounded wait that expired in a standalone op."""
+    return require_ext().op_error_state(clear)
+
+
+def dequant_rows(x: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """fp8 [m, k] with 1x128 scales [m, k/128] -> fp32."""
+    m, k = x.shape
+    return (x.float().view(m, k // 128, 128) * s.view(m, k // 128, 1)).view(m, k)
+
+
+def dequant_blocks(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """fp8 [E, n, k] with 128x128 scales [E, n/128, k/128] -> fp32."""
+    E, n, k = w.shape
+    return (w.float().view(E, n // 128, 128, k // 128, 128) * s.view(E, n // 128, 1, k // 128, 1)).view(E, n, k)
+
+
+def quantize_weights_fp8(w: torch.Tensor):
+    """bf16/fp32 [E, n, k] -> (fp8 [E, n, k], fp32 128x128 block scales [E, n/128, k/128])."""
+    E, n, k = w.shape
+    v = w.float().view(E, n // 128, 128, k // 128, 128)
+    amax = v.abs().amax(dim=(2, 4)).clamp(min=1e-4)
+    scale = amax / torch.full_like(amax, 448.0)
+    q = (v / scale.view(E, n // 128, 1, k // 128, 1)).clamp(-448, 448).to(torch.float8_e4m3fn)
+    return q.view(E, n, k), scale
+
+
+def grouped_gemm_fp8_reference(a, sa, b, sb, offsets, counts=None) -> torch.Tensor:
+    af = dequant_rows(a, sa)
+    bf = dequant_blocks(b, sb)
+    out = torch.zeros((a.shape[0], b.shape[1]), dtype=torch.float32, device=a.device)
+    E = b.shape[0]
+    off = offsets.tolist()
+    cnt = counts.tolist() if counts is not None else [off[e + 1] - off[e] for e in range(E)]
+    for e in range(E):
+        r0, r1 = off[e], off[e] + cnt[e]
+        if r1 > r0:
+            out[r0:r1] = af[r0:r1] @ bf[e].t()
+    return out

@@ -19,6 +19,7 @@ SOURCES = [
     os.path.join(CSRC, "kernels", "quant.cu"),
     os.path.join(CSRC, "kernels", "permute.cu"),
     os.path.join(CSRC, "kernels", "permute_noalloc.cu"),
+    os.path.join(CSRC, "kernels", "gemm_sm100.cu"),
 ]
 
 NVCC_FLAGS = [
