@@ -168,6 +168,8 @@ void launch_ll_clean(PeerTable peers, LLLayout layout, int rank, KernelStatus st
 // ---------------------------------------------------------------- standalone ops
 void launch_per_token_cast_to_fp8(const void* x, int num_tokens, int hidden, void* out_fp8, float* out_scales,
                                   int round_scale, cudaStream_t stream);
+void launch_swiglu_quant(const void* h, int rows, int inter, void* a, void* a_q, float* a_s, int round_scale,
+                         cudaStream_t stream);
 void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_tokens, int hidden, void* out_bf16,
                                 cudaStream_t stream);
 

@@ -41,6 +41,54 @@ __global__ void __launch_bounds__(256) per_token_cast_back_kernel(const uint8_t*
     }
 }
 
+// SwiGLU + per-token FP8 requantization, one warp per row:
+//   a = silu(h[:, :I]) * h[:, I:]  (fp32 math, rounded to bf16 and stored for the backward pass),
+//   (a_q, a_s) = 1x128 FP8 quantization of the bf16 `a` (the input of the down projection).
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ h, int rows, int inter,
+                                                           __nv_bfloat16* __restrict__ a, uint8_t* __restrict__ a_q,
+                                                           float* __restrict__ a_s, int round_scale) {
+    const int lane = lane_id();
+    const int warps = blockDim.x / 32;
+    for (int r = blockIdx.x * warps + warp_id(); r < rows; r += gridDim.x * warps) {
+        const __nv_bfloat16* gate = h + (int64_t)r * 2 * inter;
+        const __nv_bfloat16* up = gate + inter;
+        for (int base = 0; base < inter; base += 256) {
+            const int e = base + lane * 8;
+            const bool valid = e < inter;
+            int4 gv = make_int4(0, 0, 0, 0), uv = make_int4(0, 0, 0, 0);
+            if (valid) {
+                gv = ld_nc_v4(reinterpret_cast<const int4*>(gate + e));
+                uv = ld_nc_v4(reinterpret_cast<const int4*>(up + e));
+            }
+            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+            const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
+            int4 ov;
+            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 gf = __bfloat1622float2(g2[i]), uf = __bfloat1622float2(u2[i]);
+                const float s0 = gf.x / (1.0f + __expf(-gf.x)), s1 = gf.y / (1.0f + __expf(-gf.y));
+                o2[i] = __floats2bfloat162_rn(s0 * uf.x, s1 * uf.y);
+            }
+            float scale;
+            const uint2 qv = quantize_8(ov, round_scale != 0, &scale);
+            if (valid) {
+                *reinterpret_cast<int4*>(a + (int64_t)r * inter + e) = ov;
+                *reinterpret_cast<uint2*>(a_q + (int64_t)r * inter + e) = qv;
+                if ((lane & 15) == 0) a_s[(int64_t)r * (inter / 128) + e / 128] = scale;
+            }
+        }
+    }
+}
+
+void launch_swiglu_quant(const void* h, int rows, int inter, void* a, void* a_q, float* a_s, int round_scale, cudaStream_t stream) {
+    if (rows == 0) return;
+    int blocks = (rows + 7) / 8;
+    if (blocks > 4736) blocks = 4736;
+    swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(h), rows, inter,
+                                                    static_cast<__nv_bfloat16*>(a), static_cast<uint8_t*>(a_q), a_s, round_scale);
+}
+
 void launch_per_token_cast_to_fp8(const void* x, int num_tokens, int hidden, void* out_fp8, float* out_scales,
                                   int round_scale, cudaStream_t stream) {
     if (num_tokens == 0) return;

@@ -102,6 +102,19 @@ torch::Tensor per_token_cast_back(const torch::Tensor& x, const torch::Tensor& s
     return out;
 }
 
+// a = silu(h[:, :I]) * h[:, I:] (bf16) and its 1x128 FP8 quantization.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> swiglu_quant(const torch::Tensor& h, bool round_scale) {
+    TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.is_contiguous() && h.scalar_type() == torch::kBFloat16);
+    const int rows = (int)h.size(0), inter = (int)h.size(1) / 2;
+    TORCH_CHECK(h.size(1) % 256 == 0, "2*intermediate must be a multiple of 256");
+    auto a = torch::empty({rows, inter}, h.options());
+    auto aq = torch::empty({rows, inter}, h.options().dtype(torch::kFloat8_e4m3fn));
+    auto as = torch::empty({rows, inter / 128}, h.options().dtype(torch::kFloat32));
+    launch_swiglu_quant(h.data_ptr(), rows, inter, a.data_ptr(), aq.data_ptr(), as.data_ptr<float>(), round_scale ? 1 : 0,
+                        at::cuda::getCurrentCUDAStream());
+    return {a, aq, as};
+}
+
 // Grouped-by-expert permutation of dispatched tokens. Output rows are allocated for the worst case
 // (`num_out_rows`, default N*K + E*(alignment-1)); rows past expert_offsets[E] are unused.
 std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor>
@@ -173,6 +186,7 @@ void register_ops(pybind11::module_& m) {
     m.def("permute", &permute, pybind11::arg("x"), pybind11::arg("x_scales"), pybind11::arg("topk_idx"), pybind11::arg("probs"),
           pybind11::arg("num_experts"), pybind11::arg("alignment") = 1, pybind11::arg("num_out_rows") = 0);
     m.def("unpermute", &unpermute);
+    m.def("swiglu_quant", &swiglu_quant, pybind11::arg("h"), pybind11::arg("round_scale") = false);
     m.def("grouped_gemm_fp8", &grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"), pybind11::arg("b"), pybind11::arg("sb"),
           pybind11::arg("offsets"), pybind11::arg("counts") = pybind11::none(), pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 10.0);

@@ -1,0 +1,138 @@
+"""Expert-parallel SwiGLU MoE FFN layer (forward + backward) on the B200 kernels.
+
+Forward per rank (every step on hand-written sm_100a kernels):
+  dispatch (FP8 1x128 quantization fused) -> permute (expert-grouped, 128-aligned) ->
+  grouped FP8 GEMM gate/up (tcgen05, 1x128 x 128x128 block scales) -> fused SwiGLU + FP8 requant ->
+  grouped FP8 GEMM down -> top-k weighted unpermute -> combine (sum over ranks).
+Backward: combine^T = cached dispatch of the output gradient; dispatch^T = combine; the expert
+GEMM gradients run in bf16 (straight-through through the FP8 quantization). In this version the
+backward grouped GEMMs are per-expert torch matmuls (cuBLAS), a stand-in for tcgen05 kernels.
+
+The reference library has no model layer (its expert compute is SGLang + DeepGEMM,
+backend/tests/sglang_dispatcher_smoke.py:107-124); this is the flagship workload of the benchmark
+config "full MoE layer forward+backward".
+"""
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops.gemm import grouped_gemm_fp8, quantize_weights_fp8
+from ..ops.permute import permute, unpermute
+from .._ext import require_ext
+
+
+def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
+    off = offsets.tolist()
+    cnt = counts.tolist()
+    return [(off[e], off[e] + cnt[e]) for e in range(len(cnt))]
+
+
+class _MoEFunction(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, x, topk_idx, topk_weights, w1, w2, buffer, num_experts, config):
+        E_l = w1.shape[0]
+        inter = w1.shape[1] // 2
+        (rxq, rxs), ridx, rw, _, handle, _ = buffer.dispatch(x, topk_idx=topk_idx, topk_weights=topk_weights,
+                                                             num_experts=num_experts, quantize_fp8=True, config=config)
+        p = permute(rxq, ridx, E_l, alignment=128, probs=rw, x_scales=rxs)
+        w1q, w1s = quantize_weights_fp8(w1.detach())
+        h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts)
+        a, aq, as_ = require_ext().swiglu_quant(h, False)
+        w2q, w2s = quantize_weights_fp8(w2.detach())
+        y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts)
+        y_tok = unpermute(y, p.row_map, rw)
+        out, _, _ = buffer.combine(y_tok, handle, config=config)
+        ctx.buffer, ctx.config, ctx.inter = buffer, config, inter
+        ctx.handle = handle
+        ctx.save_for_backward(p.x, p.scales, p.row_map, p.expert_offsets, p.expert_counts, rw, h, a, y, w1, w2)
+        return out
+
+    @staticmethod
+    def backward(ctx, g_out):
+        xp, xs, row_map, offsets, counts, rw, h, a, y, w1, w2 = ctx.saved_tensors
+        buffer, config, inter = ctx.buffer, ctx.config, ctx.inter
+        g_out = g_out.contiguous().to(torch.bfloat16)
+        # combine^T: send the output gradient to the ranks that computed each token (cached layout)
+        g_tok, *_ = buffer.dispatch(g_out, handle=ctx.handle, config=config)
+        valid = row_map >= 0
+        rows = row_map[valid].long()
+        t_of = torch.arange(row_map.shape[0], device=g_out.device).unsqueeze(1).expand_as(row_map)[valid]
+        # unpermute^T: grouped output gradient (scaled by the routing weight) and the weight gradient
+        g_y = torch.zeros_like(y)
+        g_y[rows] = (g_tok[t_of].float() * rw[valid].unsqueeze(1)).to(torch.bfloat16)
+        g_rw = torch.zeros_like(rw)
+        g_rw[valid] = (g_tok[t_of].float() * y[rows].float()).sum(-1)
+        xf = (xp.float().view(xp.shape[0], -1, 128) * xs.unsqueeze(-1)).view(xp.shape).to(torch.bfloat16)
+        g_xp = torch.zeros_like(xf)
+        g_w1 = torch.zeros_like(w1)
+        g_w2 = torch.zeros_like(w2)
+        gate, up = h[:, :inter].float(), h[:, inter:].float()
+        sig = torch.sigmoid(gate)
+        for e, (r0, r1) in enumerate(_expert_rows(offsets, counts)):
+            if r1 <= r0:
+                continue
+            gy = g_y[r0:r1]
+            g_a = gy @ w2[e]                                   # [m, H] x [H, I]
+            g_w2[e] = gy.t() @ a[r0:r1]                        # [H, m] x [m, I]
+            s, gt, u = sig[r0:r1], gate[r0:r1], up[r0:r1]
+            gaf = g_a.float()
+            g_h = torch.cat([gaf * u * s * (1 + gt * (1 - s)), gaf * gt * s], dim=1).to(torch.bfloat16)
+            g_xp[r0:r1] = g_h @ w1[e]                          # [m, 2I] x [2I, H]
+            g_w1[e] = g_h.t() @ xf[r0:r1]                      # [2I, m] x [m, H]
+        # permute^T: sum the k copies of each received token; dispatch^T = combine (sum over ranks)
+        g_recv = unpermute(g_xp, row_map, None)
+        g_x, g_topk_w, _ = buffer.combine(g_recv, ctx.handle, topk_weights=g_rw, config=config)
+        return g_x, None, g_topk_w, g_w1, g_w2, None, None, None
+
+
+class MoEFFN(torch.nn.Module):
+    """SwiGLU MoE FFN with `num_experts / group_size` local experts per rank.
+
+    Weights: w1 [E_local, 2*inter, hidden] (gate rows then up rows), w2 [E_local, hidden, inter],
+    bf16 master copies, quantized to FP8 with 128x128 block scales inside every forward.
+    """
+
+    def __init__(self, buffer, hidden: int, inter: int, num_experts: int, num_topk: int,
+                 config=None, init_std: float = 0.02, generator: Optional[torch.Generator] = None):
+        super().__init__()
+        world = buffer.group_size
+        assert num_experts % world == 0
+        self.buffer, self.config = buffer, config
+        self.hidden, self.inter, self.num_experts, self.num_topk = hidden, inter, num_experts, num_topk
+        e_l = num_experts // world
+        g = generator
+        self.w1 = torch.nn.Parameter((torch.randn((e_l, 2 * inter, hidden), generator=g) * init_std)
+                                     .to(torch.bfloat16).cuda())
+        self.w2 = torch.nn.Parameter((torch.randn((e_l, hidden, inter), generator=g) * init_std)
+                                     .to(torch.bfloat16).cuda())
+
+    def forward(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
+        return _MoEFunction.apply(x, topk_idx, topk_weights, self.w1, self.w2, self.buffer, self.num_experts,
+                                  self.config)
+
+
+def moe_reference(x, topk_idx, topk_weights, w1_all, w2_all):
+    """Single-process fp32 oracle with the layer's quantization points (FP8 x, FP8 weights, bf16 h,
+    FP8 a, bf16 y); w*_all hold every expert of the group: [E, 2I, H] and [E, H, I]."""
+    from ..ops.gemm import dequant_blocks
+    from ..utils.math import per_token_cast_back, per_token_cast_to_fp8
+    inter = w1_all.shape[1] // 2
+    xq, xs = per_token_cast_to_fp8(x)
+    xf = per_token_cast_back(xq, xs).float()
+    w1q, w1s = quantize_weights_fp8(w1_all)
+    w2q, w2s = quantize_weights_fp8(w2_all)
+    w1f, w2f = dequant_blocks(w1q, w1s), dequant_blocks(w2q, w2s)
+    out = torch.zeros_like(x, dtype=torch.float32)
+    for k in range(topk_idx.shape[1]):
+        for e in topk_idx[:, k].unique().tolist():
+            if e < 0:
+                continue
+            sel = topk_idx[:, k] == e
+            h = (xf[sel] @ w1f[e].t()).to(torch.bfloat16).float()
+            a = (torch.nn.functional.silu(h[:, :inter]) * h[:, inter:]).to(torch.bfloat16)
+            aq, as_ = per_token_cast_to_fp8(a)
+            y = (per_token_cast_back(aq, as_).float() @ w2f[e].t()).to(torch.bfloat16).float()
+            out[sel] += topk_weights[sel, k].unsqueeze(1) * y
+    return out.to(torch.bfloat16)
