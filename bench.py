@@ -59,6 +59,8 @@ def parse():
     p.add_argument('--ll-tokens', type=int, default=128)
     p.add_argument('--no-ll', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--no-moe', action='store_true')
+    p.add_argument('--moe-steps', type=int, default=3)
     p.add_argument('--check', action='store_true', help='verify against the torch oracle before timing')
     return p.parse_args()
 
@@ -294,6 +296,55 @@ def main():
               'll_config': {'tokens_per_rank': T, 'hidden': H, 'experts': E, 'topk': K, 'fp8_dispatch': True,
                             'return_recv_hook': True, 'routing': 'uniform logits'}}
 
+    # ---------------------------------------------------------------- MoE layer forward + backward (config 4)
+    moe = {}
+    if not args.no_moe and args.impl == 'ours':
+        from deepep_slingshot_b200.models import MoEFFN
+        inter = 2048
+        gm = torch.Generator().manual_seed(4321)
+        layer = MoEFFN(buf, H, inter, E, K, config=cfg, init_std=0.02, generator=gm)
+        mx = torch.randn((N, H), generator=gm).to(torch.bfloat16).cuda().requires_grad_(True)
+        midx, mw = gate.zipf_routing(N, E, K, s=1.1, generator=torch.Generator().manual_seed(77 + rank))
+        midx, mw = midx.cuda(), mw.cuda().requires_grad_(True)
+        gout = torch.randn((N, H), generator=gm).to(torch.bfloat16).cuda()
+
+        def moe_step():
+            out = layer(mx, midx, mw)
+            out.backward(gout)
+            return out
+
+        for _ in range(2):
+            moe_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        mts = []
+        for _ in range(args.moe_steps):
+            flush.zero_()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            moe_step()
+            a1.record()
+            torch.cuda.synchronize()
+            mts.append(a0.elapsed_time(a1))
+        mts = max_over_ranks(mts)
+        ms_moe = sum(mts) / len(mts)
+        rows = sum_over_ranks(int((midx >= 0).sum())) / world  # expert rows per rank (average)
+        fwd_flops = 6.0 * rows * H * inter
+        bwd_flops = 12.0 * rows * H * inter
+        peak = 1650.1e12  # measured cuBLAS bf16 burst (MEASURED_PEAKS.json); FP8 counted at 2x
+        t_compute = fwd_flops / (2 * peak) + bwd_flops / peak
+        remote = (world - 1) / world
+        nv_bytes = 2 * remote * num_recv * ((H + H // 128 * 4) + 2 * H)  # fwd dispatch+combine, bwd mirror
+        t_comm = nv_bytes / 770e9
+        moe = {'moe_tokens_per_s': N * world / (ms_moe * 1e-3), 'moe_ms_per_step': ms_moe,
+               'moe_roofline_fraction': max(t_compute, t_comm) / (ms_moe * 1e-3),
+               'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
+                              'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs',
+                              'backward': 'bf16 per-expert torch matmuls (stand-in)',
+                              'roofline': 'max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes at 770 GB/s)'}}
+        del layer
+        torch.cuda.empty_cache()
+
     # ---------------------------------------------------------------- end to end through the public API
     e2e = None
     if not args.no_e2e:
@@ -350,6 +401,7 @@ def main():
             'gpu_launches': args.steps * 6 if args.impl == 'ours' else 0,
         }
         line.update(ll)
+        line.update(moe)
         if e2e is not None:
             line['e2e'] = e2e
         print(json.dumps(line), flush=True)

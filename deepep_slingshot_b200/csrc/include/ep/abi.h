@@ -77,7 +77,8 @@ struct alignas(128) NormalCtrl {
     int dispatch_epoch;                     // last dispatch whose notify completed
     int combine_seq;                        // last combine whose reduce completed
     int barrier_epoch;                      // last barrier
-    int pad0[26];
+    int combine_token_cursor;               // next token for the combine reducers (reset by the last block)
+    int pad0[25];
     int token_counts[2][kMaxRanks][kMaxRanks];  // [parity][src][dst] tokens src sends to dst
     int expert_counts[2][kMaxRanks][kMaxLocalExperts];  // [parity][src][local expert] tokens from src
 };
@@ -104,6 +105,7 @@ struct NormalLayout {
     int64_t combine_off;     // bf16 rows [capacity * num_ranks][hidden]
     int64_t combine_w_off;   // f32 [capacity * num_ranks][topk_pad]
     int64_t scratch_off;     // local only: uint8 rank mask per token [capacity], then int expert counters
+    int64_t arrival_off;     // int32 [capacity]: combine contributions landed per token (peers add, reducer resets)
     int64_t total_bytes;
     int32_t capacity;        // max tokens per rank per call
     int32_t hidden;
@@ -112,7 +114,7 @@ struct NormalLayout {
     int32_t record_bytes;    // staging record stride
     int32_t num_ranks;
 };
-static_assert(sizeof(NormalLayout) == 80, "NormalLayout ABI");
+static_assert(sizeof(NormalLayout) == 88, "NormalLayout ABI");
 constexpr int kMaxExperts = kMaxRanks * kMaxLocalExperts;
 
 // Staging record of one token (written by its source rank, pulled by receivers):

@@ -87,36 +87,28 @@ struct PullArgs {
 void launch_dispatch_pull(const PullArgs& a, int num_sms, cudaStream_t stream);
 
 // ---------------------------------------------------------------- normal-mode combine
-struct CombinePushArgs {
+struct CombineArgs {
     PeerTable peers;
     NormalLayout layout;
     int rank, num_ranks, num_topk;
-    const void* x;                   // bf16 [num_recv][H]
+    const void* x;                   // bf16 [num_recv][H] expert outputs (one row per received token)
     const float* topk_weights;       // [num_recv][K] or null
-    const int* rank_prefix_matrix;
-    const int* send_prefix_matrix;
     int num_recv_max;                // rows available in x; the true count comes from the prefix matrix
-    int stages;
-    KernelStatus st;
-};
-void launch_combine_push(const CombinePushArgs& a, int num_sms, cudaStream_t stream);
-
-struct CombineReduceArgs {
-    PeerTable peers;
-    NormalLayout layout;
-    int rank, num_ranks, num_topk, hidden;
-    const int* send_head;            // [N][R]
     const int* rank_prefix_matrix;
     const int* send_prefix_matrix;
+    const int* recv_src_idx;         // [num_recv] source token index of every received row (handle)
+    const int* send_head;            // [N][R] position of my token t in rank r's block, -1 if not sent
     int num_tokens;
     int has_weights;
     const void* bias0;               // bf16 [N][H] or null
     const void* bias1;
     void* out;                       // bf16 [N][H]
     float* out_topk_weights;         // [N][K] or null
+    int push_blocks;                 // set by the launcher
+    int stages;
     KernelStatus st;
 };
-void launch_combine_reduce(const CombineReduceArgs& a, int num_sms, cudaStream_t stream);
+void launch_combine(const CombineArgs& a, int num_sms, cudaStream_t stream);
 
 // ---------------------------------------------------------------- barrier
 void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st, cudaStream_t stream);

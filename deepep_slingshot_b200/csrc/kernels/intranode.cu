@@ -356,6 +356,7 @@ void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream) {
 // ~745 GB/s from one peer.
 // =================================================================================================
 constexpr int kPairs = 2;
+constexpr int kCombineThreads = 256;  // combine blocks: 2 push pairs (4 warps) + 4 reducer warps
 
 struct PipeSmem;
 __device__ __forceinline__ void release_slots(const PipeSmem& p, int k, int lag);
@@ -364,14 +365,14 @@ struct PipeSmem {
     uint8_t* slots;
     uint64_t* full;
     uint64_t* empty;
-    int* side;  // per-slot side information written by the producer (source token / destination)
+    int* side;  // two ints per slot of side information (source token / destination rank, token)
     int S, slot_bytes;
 };
 
 // Bytes of one pair's region, rounded to 128 so every pair's slots (TMA targets, 16-byte rule) and
 // mbarriers (8-byte rule) stay aligned whatever the stage count.
 __host__ __device__ __forceinline__ size_t pipe_pair_bytes(int S, int slot_bytes) {
-    return ((size_t)S * slot_bytes + (size_t)S * 20 + 16 + 127) / 128 * 128;
+    return ((size_t)S * slot_bytes + (size_t)S * 24 + 16 + 127) / 128 * 128;
 }
 
 __device__ __forceinline__ PipeSmem pipe_smem(uint8_t* smem, int pair, int S, int slot_bytes) {
@@ -548,7 +549,7 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
 
 static int pipe_stages(int slot_bytes, int max_stages) {
     const int budget = 200 * 1024;
-    int s = (int)(budget / ((size_t)kPairs * (slot_bytes + 20) + 256));
+    int s = (int)(budget / ((size_t)kPairs * (slot_bytes + 24) + 256));
     if (s > max_stages) s = max_stages;
     return s;
 }
@@ -564,106 +565,15 @@ void launch_dispatch_pull(const PullArgs& a_in, int num_sms, cudaStream_t stream
 }
 
 // =================================================================================================
-// combine push: expert-output rows -> the source rank's combine slots (peer memory).
-// =================================================================================================
-__global__ void __launch_bounds__(64 * kPairs) combine_push_kernel(CombinePushArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_prefix[kMaxRanks + 1];
-    __shared__ int s_dst_base[kMaxRanks];
-    const int lane = lane_id(), warp = warp_id();
-    const int pair = warp >> 1;
-    const bool producer = (warp & 1) == 0;
-    const int R = a.num_ranks, K = a.num_topk;
-    const int row_bytes = a.layout.hidden * 2;
-    const int slot_bytes = (row_bytes + 127) / 128 * 128;
-    const PipeSmem p = pipe_smem(smem, pair, a.stages, slot_bytes);
-    NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
-
-    // Destination `tid` must have finished reducing the previous combine before its slots are reused.
-    if ((int)threadIdx.x < R)
-        wait_ge(&my_ctrl->combine_ready[threadIdx.x], ld_volatile(&my_ctrl->combine_seq), a.st, kErrTimeoutCombineReady,
-                threadIdx.x);
-    pipe_init(p);
-    if (threadIdx.x == 0) {
-        s_prefix[0] = 0;
-        for (int s = 0; s < R; ++s) {
-            s_prefix[s + 1] = a.rank_prefix_matrix[s * R + a.rank];
-            s_dst_base[s] = a.send_prefix_matrix[s * R + a.rank];
-        }
-    }
-    __syncthreads();
-    if (aborted(a.st)) return;
-
-    const int num_recv = min(s_prefix[R], a.num_recv_max);
-    int r0, r1;
-    pair_range(num_recv, blockIdx.x * kPairs + pair, gridDim.x * kPairs, r0, r1);
-    const int S = p.S;
-    const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
-
-    if (producer) {
-        for (int j = r0; j < r1; ++j) {
-            if (lane == 0) {
-                const int k = j - r0, slot = k % S;
-                bool ok = true;
-                if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
-                if (ok) {
-                    mbar_arrive_expect_tx(&p.full[slot], row_bytes);
-                    tma_load_1d(p.slots + (size_t)slot * slot_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)j * row_bytes,
-                                row_bytes, &p.full[slot]);
-                }
-            }
-        }
-    } else {
-        int sent = 0;  // lane d: rows sent to destination d
-        for (int j = r0; j < r1; ++j) {
-            const int k = j - r0, slot = k % S;
-            const int d = find_source(s_prefix, R, j);
-            const int64_t drow = s_dst_base[d] + (j - s_prefix[d]);
-            int good = 1;
-            if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
-            if (!__shfl_sync(0xffffffffu, good, 0)) break;
-            if (drow < 0 || drow >= rows_cap) {
-                if (lane == 0) report_error(a.st, kErrBounds, d, (int)drow);
-                break;
-            }
-            uint8_t* peer = static_cast<uint8_t*>(a.peers.base[d]);
-            if (lane == 0) {
-                tma_store_1d(peer + a.layout.combine_off + drow * row_bytes, p.slots + (size_t)slot * slot_bytes, row_bytes);
-                bulk_commit();
-            }
-            if (a.topk_weights != nullptr && lane < a.layout.topk_pad) {
-                float* wdst = reinterpret_cast<float*>(peer + a.layout.combine_w_off) + drow * a.layout.topk_pad;
-                wdst[lane] = lane < K ? a.topk_weights[(int64_t)j * K + lane] : 0.f;
-            }
-            if (lane == d) ++sent;
-            __syncwarp();
-            if (lane == 0) release_slots(p, k, S / 2);
-        }
-        // The bulk stores of this pair are complete (and every lane's weight stores performed
-        // system-wide) before the counts are published.
-        if (lane == 0) {
-            bulk_wait<0>();
-            fence_proxy_async_global();
-        }
-        fence_sys();
-        __syncwarp();
-        if (lane < R && sent > 0) red_add_release_sys(&ctrl_of(a.peers, a.layout, lane)->combine_arrived, sent);
-    }
-}
-
-void launch_combine_push(const CombinePushArgs& a_in, int num_sms, cudaStream_t stream) {
-    CombinePushArgs a = a_in;
-    const int slot_bytes = (a.layout.hidden * 2 + 127) / 128 * 128;
-    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 16);
-    if (a.stages < 4) a.stages = 4;
-    const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
-    cudaFuncSetAttribute(combine_push_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    combine_push_kernel<<<num_sms, 64 * kPairs, smem, stream>>>(a);
-}
-
-// =================================================================================================
-// combine reduce: fp32 sum of the <= R contributions per token (+ bias) -> bf16; top-k weight sum.
-// One warp per token; all contributions of a 256-element slice are loaded before they are summed.
+// combine: one launch, two roles.
+//  * push blocks (first `push_blocks`): producer/consumer pairs move each expert-output row to its
+//    source rank's combine slot with TMA (load local, store to the peer). Once a row's store has
+//    completed (bulk wait_group, not .read) the consumer adds 1 to the destination's arrival counter
+//    of that token with a sys-scope release.
+//  * reduce blocks (the rest): one warp per token of this rank, in token order; it waits until the
+//    token's arrival counter equals its number of contributing ranks, sums the rows in fp32 (+ bias),
+//    writes bf16, sums the top-k weights and resets the counter. Reduction overlaps the transfer.
+// All blocks are co-resident (grid <= SM count, one block per SM by shared memory).
 // =================================================================================================
 template <int kU, int kN>
 __device__ __forceinline__ void reduce_rows(const __nv_bfloat16* rows, const int* src_rows, int n, int H, int t,
@@ -719,69 +629,194 @@ __device__ __forceinline__ void reduce_rows(const __nv_bfloat16* rows, const int
     }
 }
 
-__global__ void __launch_bounds__(256, 2) combine_reduce_kernel(CombineReduceArgs a) {
-    __shared__ int s_base[kMaxRanks];
-    __shared__ int s_seq;
-    const int R = a.num_ranks, K = a.num_topk, H = a.hidden;
-    NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
-    if (threadIdx.x == 0) {
-        s_seq = ld_volatile(&my_ctrl->combine_seq) + 1;
-        int expected = 0;
-        for (int r = 0; r < R; ++r) {
-            const int prev = a.rank > 0 ? a.rank_prefix_matrix[(a.rank - 1) * R + r] : 0;
-            expected += a.rank_prefix_matrix[a.rank * R + r] - prev;
-            s_base[r] = a.send_prefix_matrix[a.rank * R + r];
-        }
-        wait_eq(&my_ctrl->combine_arrived, expected, a.st, kErrTimeoutCombineArrive, -1);
+// Reduce one token t (all its contributions must have arrived): fp32 sum (+ bias) -> bf16, weight sum.
+__device__ __forceinline__ bool combine_reduce_token(const CombineArgs& a, int t, const int* s_base, const __nv_bfloat16* rows,
+                                                     const float* wrows, int* arrival) {
+    const int lane = lane_id();
+    const int R = a.num_ranks, K = a.num_topk, H = a.layout.hidden;
+    int my_row = -1;
+    if (lane < R) {
+        const int p = a.send_head[(int64_t)t * R + lane];
+        my_row = p >= 0 ? s_base[lane] + p : -1;
     }
-    __syncthreads();
-    if (!aborted(a.st)) {
-        const int lane = lane_id();
-        const int warps = blockDim.x / 32;
-        const __nv_bfloat16* rows =
-            reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_off);
-        const float* wrows = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_w_off);
-        for (int t = blockIdx.x * warps + warp_id(); t < a.num_tokens; t += gridDim.x * warps) {
-            int my_row = -1;
-            if (lane < R) {
-                const int p = a.send_head[(int64_t)t * R + lane];
-                my_row = p >= 0 ? s_base[lane] + p : -1;
-            }
-            int src_rows[kMaxRanks];
-            int n = 0;
+    int src_rows[kMaxRanks];
+    int n = 0;
 #pragma unroll
-            for (int r = 0; r < kMaxRanks; ++r) {
-                const int v = __shfl_sync(0xffffffffu, my_row, r);
-                if (r < R && v >= 0) src_rows[n++] = v;
+    for (int r = 0; r < kMaxRanks; ++r) {
+        const int v = __shfl_sync(0xffffffffu, my_row, r);
+        if (r < R && v >= 0) src_rows[n++] = v;
+    }
+    if (n > 0) {
+        int good = 1;
+        if (lane == 0) good = wait_eq(arrival + t, n, a.st, kErrTimeoutCombineArrive, t) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, good, 0)) return false;
+    }
+    if (n <= 1) reduce_rows<8, 1>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+    else if (n == 2) reduce_rows<4, 2>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+    else if (n <= 4) reduce_rows<2, 4>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+    else reduce_rows<1, kMaxRanks>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
+    if (a.out_topk_weights != nullptr && lane < K) {
+        float w = 0.f;
+        if (a.has_weights)
+            for (int q = 0; q < n; ++q) w += wrows[(int64_t)src_rows[q] * a.layout.topk_pad + lane];
+        a.out_topk_weights[(int64_t)t * K + lane] = w;
+    }
+    __syncwarp();
+    if (lane == 0 && n > 0) arrival[t] = 0;
+    return true;
+}
+
+// Reducer loop: grab tokens from the shared cursor until none are left.
+__device__ __forceinline__ void combine_reduce_loop(const CombineArgs& a, NormalCtrl* my_ctrl, const int* s_base) {
+    const int lane = lane_id();
+    const __nv_bfloat16* rows =
+        reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_off);
+    const float* wrows = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers.base[a.rank]) + a.layout.combine_w_off);
+    int* arrival = reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[a.rank]) + a.layout.arrival_off);
+    while (true) {
+        int t = 0;
+        if (lane == 0) t = atomicAdd(&my_ctrl->combine_token_cursor, 1);
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t >= a.num_tokens) break;
+        if (!combine_reduce_token(a, t, s_base, rows, wrows, arrival)) break;
+    }
+}
+
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_prefix[kMaxRanks + 1];
+    __shared__ int s_base[kMaxRanks];      // where my rows start in each destination's combine region
+    __shared__ int s_red_base[kMaxRanks];  // where each rank's rows start in MY combine region
+    const int lane = lane_id(), warp = warp_id();
+    const int R = a.num_ranks, K = a.num_topk, H = a.layout.hidden;
+    NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
+    const bool pusher = (int)blockIdx.x < a.push_blocks;
+    const int row_bytes = H * 2;
+    const int slot_bytes = (row_bytes + 127) / 128 * 128;
+
+    if (pusher && (int)threadIdx.x < R)
+        // Destination `tid` must have finished reducing the previous combine before its slots are reused.
+        wait_ge(&my_ctrl->combine_ready[threadIdx.x], ld_volatile(&my_ctrl->combine_seq), a.st, kErrTimeoutCombineReady,
+                threadIdx.x);
+    if (threadIdx.x == 0) {
+        s_prefix[0] = 0;
+        for (int s = 0; s < R; ++s) {
+            s_prefix[s + 1] = a.rank_prefix_matrix[s * R + a.rank];
+            s_base[s] = a.send_prefix_matrix[s * R + a.rank];
+            s_red_base[s] = a.send_prefix_matrix[a.rank * R + s];
+        }
+    }
+    const PipeSmem p = pipe_smem(smem, warp >> 1, a.stages, slot_bytes);
+    if (pusher && warp < 2 * kPairs) pipe_init(p);
+    __syncthreads();
+
+    if (pusher && warp < 2 * kPairs && !aborted(a.st)) {
+        const int pair = warp >> 1;
+        const bool producer = (warp & 1) == 0;
+        const int num_recv = min(s_prefix[R], a.num_recv_max);
+        int r0, r1;
+        pair_range(num_recv, blockIdx.x * kPairs + pair, a.push_blocks * kPairs, r0, r1);
+        const int S = p.S;
+        const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
+        if (producer) {
+            for (int j = r0; j < r1; ++j) {
+                if (lane == 0) {
+                    const int k = j - r0, slot = k % S;
+                    bool ok = true;
+                    if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
+                    if (ok) {
+                        mbar_arrive_expect_tx(&p.full[slot], row_bytes);
+                        tma_load_1d(p.slots + (size_t)slot * slot_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)j * row_bytes,
+                                    row_bytes, &p.full[slot]);
+                    }
+                }
             }
-            if (n <= 2) reduce_rows<4, 2>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
-            else reduce_rows<1, kMaxRanks>(rows, src_rows, n, H, t, a.bias0, a.bias1, a.out, 0);
-            if (a.out_topk_weights != nullptr && lane < K) {
-                float w = 0.f;
-                if (a.has_weights)
-                    for (int q = 0; q < n; ++q) w += wrows[(int64_t)src_rows[q] * a.layout.topk_pad + lane];
-                a.out_topk_weights[(int64_t)t * K + lane] = w;
+        } else {
+            // Slots recycle on read-completion (as in the pull). Arrivals are announced per batch of
+            // kAnnounce rows: one drain of this thread's bulk stores, one sys-scope fence, then relaxed
+            // reds (a release per row would wait for an NVLink round trip every row).
+            constexpr int kAnnounce = 16;
+            const int lag = S / 2 < 4 ? S / 2 : 4;
+            int* arrivals[kMaxRanks];
+#pragma unroll
+            for (int r = 0; r < kMaxRanks; ++r)
+                arrivals[r] = r < R ? reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[r]) + a.layout.arrival_off) : nullptr;
+            int pend_t = -1, pend_d = 0;  // lane i holds the i-th row of the current announce batch
+            int k = 0;
+            for (int j = r0; j < r1; ++j, ++k) {
+                const int slot = k % S;
+                const int d = find_source(s_prefix, R, j);
+                const int64_t drow = s_base[d] + (j - s_prefix[d]);
+                int good = 1;
+                if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, good, 0)) break;
+                if (drow < 0 || drow >= rows_cap) {
+                    if (lane == 0) report_error(a.st, kErrBounds, d, (int)drow);
+                    break;
+                }
+                uint8_t* peer = static_cast<uint8_t*>(a.peers.base[d]);
+                if (a.topk_weights != nullptr && lane < a.layout.topk_pad) {
+                    float* wdst = reinterpret_cast<float*>(peer + a.layout.combine_w_off) + drow * a.layout.topk_pad;
+                    wdst[lane] = lane < K ? a.topk_weights[(int64_t)j * K + lane] : 0.f;
+                }
+                if (lane == k % kAnnounce) {
+                    pend_t = a.recv_src_idx[j];
+                    pend_d = d;
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_1d(peer + a.layout.combine_off + drow * row_bytes, p.slots + (size_t)slot * slot_bytes, row_bytes);
+                    bulk_commit();
+                    release_slots(p, k, lag);
+                }
+                const bool flush = (k % kAnnounce) == kAnnounce - 1 || j + 1 == r1;
+                if (flush) {
+                    const int cnt = (k % kAnnounce) + 1;
+                    if (lane == 0) {
+                        bulk_wait<0>();
+                        fence_proxy_async_global();
+                        fence_sys();  // weight stores of every lane precede the __syncwarp above
+                    }
+                    for (int i = 0; i < cnt; ++i) {
+                        const int tt = __shfl_sync(0xffffffffu, pend_t, i), dd = __shfl_sync(0xffffffffu, pend_d, i);
+                        if (lane == 0) atomicAdd_system(arrivals[dd] + tt, 1);
+                    }
+                }
+                __syncwarp();
             }
         }
     }
+    // Every warp (push warps once their rows are sent) reduces tokens of this rank.
+    if (!aborted(a.st)) combine_reduce_loop(a, my_ctrl, s_red_base);
     __syncthreads();
     if (threadIdx.x == 0) {
         const int old = atom_add_acq_rel_gpu(&my_ctrl->combine_reduced_blocks, 1);
         if (old == (int)gridDim.x - 1) {
             my_ctrl->combine_reduced_blocks = 0;
-            my_ctrl->combine_arrived = 0;
-            my_ctrl->combine_seq = s_seq;
+            my_ctrl->combine_token_cursor = 0;
+            const int seq = ld_volatile(&my_ctrl->combine_seq) + 1;
+            my_ctrl->combine_seq = seq;
             fence_sys();
-            for (int r = 0; r < R; ++r) st_release_sys(&ctrl_of(a.peers, a.layout, r)->combine_ready[a.rank], s_seq);
+            for (int r = 0; r < R; ++r) st_release_sys(&ctrl_of(a.peers, a.layout, r)->combine_ready[a.rank], seq);
         }
     }
 }
 
-void launch_combine_reduce(const CombineReduceArgs& a, int num_sms, cudaStream_t stream) {
-    (void)num_sms;
-    int blocks = (a.num_tokens + 7) / 8;
-    if (blocks < 1) blocks = 1;
-    combine_reduce_kernel<<<blocks, 256, 0, stream>>>(a);
+void launch_combine(const CombineArgs& a_in, int num_sms, cudaStream_t stream) {
+    CombineArgs a = a_in;
+    int sm_count = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    const int slot_bytes = (a.layout.hidden * 2 + 127) / 128 * 128;
+    if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 16);
+    if (a.stages < 4) a.stages = 4;
+    // All blocks co-resident (one per SM): push blocks carry 2 push pairs + 4 reducer warps, the
+    // remaining SMs reduce only; push warps join the reduction when their rows are out.
+    a.push_blocks = num_sms < sm_count ? num_sms : sm_count;
+    if (a.push_blocks < 1) a.push_blocks = 1;
+    const int reduce_blocks = sm_count - a.push_blocks;
+    const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
+    cudaFuncSetAttribute(combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    combine_kernel<<<a.push_blocks + reduce_blocks, kCombineThreads, smem, stream>>>(a);
 }
 
 // =================================================================================================

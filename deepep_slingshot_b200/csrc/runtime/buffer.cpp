@@ -103,7 +103,7 @@ static int64_t normal_bytes_per_token(int hidden, int num_ranks, int* record_str
     const RecordFormat f8 = record_format(hidden, kMaxTopk, true);
     const int rec = (int)align_up(std::max(bf.bytes, f8.bytes), kAlign);
     if (record_stride) *record_stride = rec;
-    return (int64_t)num_ranks * 4 + rec + (int64_t)num_ranks * hidden * 2 + (int64_t)num_ranks * kMaxTopk * 4 + 1;
+    return (int64_t)num_ranks * 4 + rec + (int64_t)num_ranks * hidden * 2 + (int64_t)num_ranks * kMaxTopk * 4 + 1 + 4;
 }
 
 NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ranks) {
@@ -126,7 +126,8 @@ NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ran
     l.combine_off = align_up(l.staging_off + (int64_t)l.capacity * rec, kAlign);
     l.combine_w_off = align_up(l.combine_off + (int64_t)l.capacity * num_ranks * hidden * 2, kAlign);
     l.scratch_off = align_up(l.combine_w_off + (int64_t)l.capacity * num_ranks * kMaxTopk * 4, kAlign);
-    l.total_bytes = align_up(l.scratch_off + align_up(l.capacity, kAlign) + (int64_t)kMaxExperts * 4, kAlign);
+    l.arrival_off = align_up(l.scratch_off + align_up(l.capacity, kAlign) + (int64_t)kMaxExperts * 4, kAlign);
+    l.total_bytes = align_up(l.arrival_off + (int64_t)l.capacity * 4, kAlign);
     return l;
 }
 
@@ -629,9 +630,11 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
 std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandle>> Buffer::intranode_combine(
     const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
     const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,
-    const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, int num_sms,
+    const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, const torch::Tensor& recv_src_idx, int num_sms,
     std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream) {
     check_error();
+    TORCH_CHECK(recv_src_idx.scalar_type() == torch::kInt32 && recv_src_idx.is_contiguous() && recv_src_idx.size(0) >= x.size(0),
+                "handle's recv_src_idx must cover every row of x");
     TORCH_CHECK(available_, "buffer not synced");
     TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16, "x must be contiguous bf16 [rows, hidden]");
     const int H = (int)x.size(1), R = num_ranks_;
@@ -655,39 +658,28 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     const KernelStatus st = status();
     const PeerTable peers = nvl_peers();
 
-    CombinePushArgs pa{};
-    pa.peers = peers;
-    pa.layout = L;
-    pa.rank = rank_;
-    pa.num_ranks = R;
-    pa.num_topk = K;
-    pa.x = x.data_ptr();
-    pa.topk_weights = topk_weights.has_value() ? topk_weights->data_ptr<float>() : nullptr;
-    pa.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
-    pa.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
-    pa.num_recv_max = (int)x.size(0);
-    pa.stages = 0;
-    pa.st = st;
-    launch_combine_push(pa, num_sms, stream);
-
-    CombineReduceArgs ra{};
-    ra.peers = peers;
-    ra.layout = L;
-    ra.rank = rank_;
-    ra.num_ranks = R;
-    ra.num_topk = K;
-    ra.hidden = H;
-    ra.send_head = send_head.data_ptr<int>();
-    ra.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
-    ra.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
-    ra.num_tokens = N;
-    ra.has_weights = topk_weights.has_value() ? 1 : 0;
-    ra.bias0 = bias_0.has_value() ? bias_0->data_ptr() : nullptr;
-    ra.bias1 = bias_1.has_value() ? bias_1->data_ptr() : nullptr;
-    ra.out = out.data_ptr();
-    ra.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
-    ra.st = st;
-    launch_combine_reduce(ra, num_sms, stream);
+    CombineArgs ca{};
+    ca.peers = peers;
+    ca.layout = L;
+    ca.rank = rank_;
+    ca.num_ranks = R;
+    ca.num_topk = K;
+    ca.x = x.data_ptr();
+    ca.topk_weights = topk_weights.has_value() ? topk_weights->data_ptr<float>() : nullptr;
+    ca.num_recv_max = (int)x.size(0);
+    ca.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
+    ca.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
+    ca.recv_src_idx = recv_src_idx.data_ptr<int>();
+    ca.send_head = send_head.data_ptr<int>();
+    ca.num_tokens = N;
+    ca.has_weights = topk_weights.has_value() ? 1 : 0;
+    ca.bias0 = bias_0.has_value() ? bias_0->data_ptr() : nullptr;
+    ca.bias1 = bias_1.has_value() ? bias_1->data_ptr() : nullptr;
+    ca.out = out.data_ptr();
+    ca.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
+    ca.stages = 0;
+    ca.st = st;
+    launch_combine(ca, num_sms, stream);
     EP_CUDA_CHECK(cudaGetLastError());
     auto event = scope.finish(async, {x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, out, out_w});
     return {out, out_w, event};

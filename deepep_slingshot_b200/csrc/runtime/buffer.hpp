@@ -107,7 +107,7 @@ class Buffer {
     std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandle>> intranode_combine(
         const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
         const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,
-        const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, int num_sms,
+        const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, const torch::Tensor& recv_src_idx, int num_sms,
         std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream);
 
     void barrier(bool use_comm_stream, bool with_cpu_sync);

@@ -242,10 +242,10 @@ class Buffer:
         """Sum (without weights) every rank's row of each token back on its source rank (+ bias);
         also returns the summed top-k weights. Returns `(combined_x, combined_topk_weights, event)`."""
         config = self.get_combine_config(self.group_size) if config is None else config
-        rank_prefix_matrix, send_prefix_matrix, _, _, _, send_head = handle
+        rank_prefix_matrix, send_prefix_matrix, _, recv_src_idx, _, send_head = handle
         bias_0, bias_1 = Buffer._unpack_bias(bias)
         recv_x, recv_topk_weights, event = self.runtime.intranode_combine(
-            x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, config.num_sms,
+            x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, recv_src_idx, config.num_sms,
             getattr(previous_event, 'event', None), async_finish, allocate_on_comm_stream)
         return recv_x, recv_topk_weights, EventOverlap(event)
 

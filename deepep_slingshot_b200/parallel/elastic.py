@@ -186,9 +186,9 @@ class ElasticBuffer:
                 num_qps: int = 0, previous_event=None, previous_event_before_epilogue=None,
                 async_with_compute_stream: bool = False, allocate_on_comm_stream: bool = False):
         num_sms = handle.num_sms if num_sms == 0 else num_sms
-        rpm, spm, _, _, _, send_head = handle.legacy_handle
+        rpm, spm, _, src_idx, _, send_head = handle.legacy_handle
         bias_0, bias_1 = Buffer._unpack_bias(bias)
         combined_x, combined_w, event = self.runtime.intranode_combine(
-            x, topk_weights, bias_0, bias_1, rpm, spm, send_head, num_sms, previous_event, async_with_compute_stream,
+            x, topk_weights, bias_0, bias_1, rpm, spm, send_head, src_idx, num_sms, previous_event, async_with_compute_stream,
             allocate_on_comm_stream)
         return combined_x, combined_w, EventOverlap(event)
