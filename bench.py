@@ -398,8 +398,10 @@ def main():
             'dispatch_gbps_per_rank': disp_gbps_rank, 'combine_gbps_per_rank': comb_gbps_rank,
             'num_recv_tokens_rank0': num_recv,
             'clocks': clocks,
-            'gpu_launches': args.steps * 6 if args.impl == 'ours' else 0,
+            'gpu_launches': args.steps * 5 if args.impl == 'ours' else 0,
         }
+        if os.environ.get('DEEPEP_B200_PROFILE') == '1' and hasattr(buf, 'get_profile'):
+            line['kernel_profile_rank0'] = buf.get_profile()
         line.update(ll)
         line.update(moe)
         if e2e is not None:

@@ -73,6 +73,7 @@ struct PullArgs {
     const int* dev_num_recv;         // device count or null
     int num_recv_host;               // used when dev_num_recv is null
     int num_out_rows;                // allocated output rows (>= num_recv)
+    int fill_padding;                // 1: rows past num_recv get topk -1 / src -1 (worst-case mode)
     void* recv_x;
     float* recv_scales;              // null for bf16
     int scales_col_major;            // 1: [H/128][ld] layout
@@ -82,6 +83,10 @@ struct PullArgs {
     int* recv_src_idx;               // written for fresh dispatches (null in cached mode)
     const int* cached_src_idx;       // cached mode: source token of every receive row (handle)
     int stages;
+    HostCounters* host;              // host-mapped counts for the CPU (null: none)
+    const int* num_recv_per_expert;  // [E_l] aligned counts computed by notify
+    int host_ticket;
+    int chunk;                       // rows dealt to pipeline pairs in chunks of this size (0: contiguous)
     KernelStatus st;
 };
 void launch_dispatch_pull(const PullArgs& a, int num_sms, cudaStream_t stream);
@@ -105,6 +110,7 @@ struct CombineArgs {
     void* out;                       // bf16 [N][H]
     float* out_topk_weights;         // [N][K] or null
     int push_blocks;                 // set by the launcher
+    int chunk;                       // rows dealt to push pairs in chunks of this size (0: contiguous)
     int stages;
     KernelStatus st;
 };

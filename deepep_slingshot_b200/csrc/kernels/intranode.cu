@@ -318,7 +318,6 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
             a.recv_rank_prefix[s + 1] = acc;
         }
         *a.dev_num_recv = acc;
-        if (a.host != nullptr) a.host->num_recv_tokens = acc;
     }
     for (int le = tid; le < a.num_local_experts; le += nt) {
         int c = 0;
@@ -326,17 +325,9 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
         if (a.cumulative_stats != nullptr) a.cumulative_stats[le] += c;
         const int al = a.expert_alignment > 1 ? (c + a.expert_alignment - 1) / a.expert_alignment * a.expert_alignment : c;
         a.num_recv_per_expert[le] = al;
-        if (a.host != nullptr) a.host->num_recv_tokens_per_expert[le] = al;
     }
     __syncthreads();
-    if (tid == 0) {
-        my_ctrl->dispatch_epoch = epoch;
-        if (a.host != nullptr) {
-            __threadfence_system();
-            *reinterpret_cast<volatile int*>(&a.host->ready_ticket) = a.host_ticket;
-            __threadfence_system();
-        }
-    }
+    if (tid == 0) my_ctrl->dispatch_epoch = epoch;
 }
 
 void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream) {
@@ -415,6 +406,26 @@ __device__ __forceinline__ void pipe_init(const PipeSmem& p) {
     }
 }
 
+// Rows are dealt to pairs in chunks of kChunk: pair g owns chunks g, g + P, g + 2P, ... so every pair
+// sees rows of every source/destination rank (receive rows are sorted by rank).
+// chunk == 0 deals contiguous ranges instead (pair g owns rows [g*per, (g+1)*per)).
+__device__ __forceinline__ int pair_row(int g, int P, int k, int chunk, int n) {
+    if (chunk == 0) return g * ((n + P - 1) / P) + k;
+    return ((k / chunk) * P + g) * chunk + (k % chunk);
+}
+__device__ __forceinline__ int pair_num_rows(int g, int P, int n, int chunk) {
+    if (chunk == 0) {
+        const int per = (n + P - 1) / P;
+        const int r0 = min(n, g * per);
+        return min(n, r0 + per) - r0;
+    }
+    const int full_chunks = n / chunk, rem = n % chunk;
+    int c = full_chunks > g ? (full_chunks - g + P - 1) / P : 0;
+    int rows = c * chunk;
+    if (rem > 0 && full_chunks % P == g) rows += rem;  // the trailing partial chunk
+    return rows;
+}
+
 // Contiguous row range of pair `g` out of `total_pairs` for `n` rows.
 __device__ __forceinline__ void pair_range(int n, int g, int total_pairs, int& r0, int& r1) {
     const int per = (n + total_pairs - 1) / total_pairs;
@@ -449,7 +460,8 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
 
     const int num_recv = a.dev_num_recv != nullptr ? ld_volatile(a.dev_num_recv) : a.num_recv_host;
     const int K = a.num_topk;
-    for (int j = num_recv + blockIdx.x * blockDim.x + threadIdx.x; j < a.num_out_rows; j += gridDim.x * blockDim.x) {
+    for (int j = num_recv + blockIdx.x * blockDim.x + threadIdx.x; a.fill_padding && j < a.num_out_rows;
+         j += gridDim.x * blockDim.x) {
         if (a.recv_topk_idx != nullptr)
             for (int k = 0; k < K; ++k) a.recv_topk_idx[(int64_t)j * K + k] = -1;
         if (a.recv_topk_weights != nullptr)
@@ -460,15 +472,28 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
         if (threadIdx.x == 0 && blockIdx.x == 0) report_error(a.st, kErrCapacity, -1, num_recv);
         return;
     }
-    int r0, r1;
-    pair_range(num_recv, blockIdx.x * kPairs + pair, gridDim.x * kPairs, r0, r1);
+    // Host-mapped counts for the CPU (written here rather than by the notify kernel, so PCIe writes
+    // and their fence stay off the path to the first pull).
+    if (blockIdx.x == gridDim.x - 1 && warp == 1 && a.host != nullptr) {
+        for (int le = lane; le < a.num_local_experts; le += 32)
+            a.host->num_recv_tokens_per_expert[le] = a.num_recv_per_expert[le];
+        if (lane == 0) a.host->num_recv_tokens = num_recv;
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_system();
+            *reinterpret_cast<volatile int*>(&a.host->ready_ticket) = a.host_ticket;
+        }
+    }
+    const int g = blockIdx.x * kPairs + pair, P = gridDim.x * kPairs;
+    const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
     const int S = p.S;
 
     if (producer) {
-        for (int base = r0; base < r1; base += 32) {
-            const int j = base + lane;
+        for (int base = 0; base < my_rows; base += 32) {
+            const int kk = base + lane;
             int src = 0, t = 0;
-            if (j < r1) {
+            if (kk < my_rows) {
+                const int j = pair_row(g, P, kk, a.chunk, num_recv);
                 src = find_source(s_prefix, R, j);
                 if (a.cached_src_idx != nullptr) {
                     t = a.cached_src_idx[j];
@@ -478,19 +503,19 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
                     t = ld_relaxed_sys(list + (j - s_prefix[src]));
                 }
             }
-            const int n = min(32, r1 - base);
+            const int n = min(32, my_rows - base);
             for (int i = 0; i < n; ++i) {
                 const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
                 if (lane == 0) {
-                    const int k = base + i - r0, slot = k % S;
+                    const int k = base + i, slot = k % S;
                     bool ok = true;
                     if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
                     if (ok) {
-                        p.side[slot] = pt;
-                        const uint8_t* g = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
-                                           (int64_t)pt * a.layout.record_bytes;
+                        p.side[2 * slot] = pt;
+                        const uint8_t* gsrc = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
+                                              (int64_t)pt * a.layout.record_bytes;
                         mbar_arrive_expect_tx(&p.full[slot], a.rec.bytes);
-                        tma_load_1d(p.slots + (size_t)slot * slot_bytes, g, a.rec.bytes, &p.full[slot]);
+                        tma_load_1d(p.slots + (size_t)slot * slot_bytes, gsrc, a.rec.bytes, &p.full[slot]);
                     }
                 }
             }
@@ -501,8 +526,8 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
         const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
         const int E_l = a.num_local_experts, lo_e = a.rank * E_l;
         const int lag = S / 2 < 4 ? S / 2 : 4;  // peer loads are the slow leg: favour loads in flight
-        for (int j = r0; j < r1; ++j) {
-            const int k = j - r0, slot = k % S;
+        for (int k = 0; k < my_rows; ++k) {
+            const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
             int good = 1;
             if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
             if (!__shfl_sync(0xffffffffu, good, 0)) break;
@@ -526,7 +551,7 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
                 if (a.recv_topk_idx != nullptr) a.recv_topk_idx[(int64_t)j * K + lane] = mine ? (e - lo_e) : -1;
                 if (a.recv_topk_weights != nullptr) a.recv_topk_weights[(int64_t)j * K + lane] = mine ? w : 0.f;
             }
-            if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[slot];
+            if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[2 * slot];
             __syncwarp();
             if (lane == 0) release_slots(p, k, lag);
         }
@@ -714,14 +739,14 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
         const int pair = warp >> 1;
         const bool producer = (warp & 1) == 0;
         const int num_recv = min(s_prefix[R], a.num_recv_max);
-        int r0, r1;
-        pair_range(num_recv, blockIdx.x * kPairs + pair, a.push_blocks * kPairs, r0, r1);
+        const int g = blockIdx.x * kPairs + pair, P = a.push_blocks * kPairs;
+        const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
         const int S = p.S;
         const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
         if (producer) {
-            for (int j = r0; j < r1; ++j) {
+            for (int k = 0; k < my_rows; ++k) {
                 if (lane == 0) {
-                    const int k = j - r0, slot = k % S;
+                    const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
                     bool ok = true;
                     if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
                     if (ok) {
@@ -742,9 +767,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
             for (int r = 0; r < kMaxRanks; ++r)
                 arrivals[r] = r < R ? reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[r]) + a.layout.arrival_off) : nullptr;
             int pend_t = -1, pend_d = 0;  // lane i holds the i-th row of the current announce batch
-            int k = 0;
-            for (int j = r0; j < r1; ++j, ++k) {
-                const int slot = k % S;
+            for (int k = 0; k < my_rows; ++k) {
+                const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
                 const int d = find_source(s_prefix, R, j);
                 const int64_t drow = s_base[d] + (j - s_prefix[d]);
                 int good = 1;
@@ -769,7 +793,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
                     bulk_commit();
                     release_slots(p, k, lag);
                 }
-                const bool flush = (k % kAnnounce) == kAnnounce - 1 || j + 1 == r1;
+                const bool flush = (k % kAnnounce) == kAnnounce - 1 || k + 1 == my_rows;
                 if (flush) {
                     const int cnt = (k % kAnnounce) + 1;
                     if (lane == 0) {

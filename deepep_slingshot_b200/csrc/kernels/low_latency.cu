@@ -87,68 +87,77 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
     const int slots = R * L.max_tokens;
     const int nb = H / 128;
     const int row_bytes = a.use_fp8 ? H : 2 * H;
-    const int warp_buf_bytes = (row_bytes + nb * 4 + 127) / 128 * 128;
     __shared__ uint32_t s_masked;
     if (threadIdx.x == 0) s_masked = load_mask_bits(a.mask, R);
     __syncthreads();
     uint32_t masked = s_masked;
 
     if (a.phases & 1) {
-        uint8_t* buf = smem + (size_t)warp * warp_buf_bytes;
+        // One block per token: the 8 warps quantize the row cooperatively into shared memory, then
+        // warp k claims a slot for top-k choice k (one remote atomic) and TMA-stores the row there.
+        uint8_t* buf = smem;
         float* sbuf = reinterpret_cast<float*>(buf + row_bytes);
-        for (int t = blockIdx.x * W + warp; t < a.num_tokens; t += gridDim.x * W) {
-            // The previous token's stores must be done reading this warp's buffer.
-            if (lane == 0) bulk_wait_read<0>();
-            __syncwarp();
+        for (int t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {
             const __nv_bfloat16* xr = static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * H;
-            if (a.use_fp8) {
-                quantize_row_to_fp8(xr, buf, sbuf, H, a.round_scale != 0);
-            } else {
-                for (int o = lane * 16; o < row_bytes; o += 512)
-                    *reinterpret_cast<int4*>(buf + o) = ld_nc_v4(reinterpret_cast<const int4*>(reinterpret_cast<const uint8_t*>(xr) + o));
+            for (int base = warp * 256; base < H; base += W * 256) {
+                const int e = base + lane * 8;
+                const bool valid = e < H;
+                const int4 v = valid ? ld_nc_v4(reinterpret_cast<const int4*>(xr + e)) : make_int4(0, 0, 0, 0);
+                if (a.use_fp8) {
+                    float scale;
+                    const uint2 q = quantize_8(v, a.round_scale != 0, &scale);
+                    if (valid) {
+                        *reinterpret_cast<uint2*>(buf + e) = q;
+                        if ((lane & 15) == 0) sbuf[e / 128] = scale;
+                    }
+                } else if (valid) {
+                    *reinterpret_cast<int4*>(buf + 2 * e) = v;
+                }
             }
             fence_proxy_async_smem();  // generic smem writes -> visible to the TMA (async proxy)
-            __syncwarp();
-            // Claim one slot per valid top-k destination (lane k), then broadcast.
-            int dst_rank = -1, le = -1, slot = -1;
-            if (lane < K) {
-                const int64_t e = a.topk_idx[(int64_t)t * K + lane];
-                if (e >= 0 && e < L.num_experts) {
-                    dst_rank = (int)(e / E_l);
-                    le = (int)(e % E_l);
-                    if (((masked >> (dst_rank))) & 1u) {
-                        dst_rank = -1;
-                    } else {
-                        LLHalf h = half_of(a.peers, L, dst_rank, a.half);
-                        slot = atom_add_relaxed_sys(&h.ctrl()->slot_counter[le], 1);
-                        if (slot >= slots) {
-                            report_error(a.st, kErrCapacity, dst_rank, slot);
+            __syncthreads();
+            if (warp < K) {
+                const int k = warp;
+                int dst_rank = -1, le = -1, slot = -1;
+                if (lane == 0) {
+                    const int64_t e = a.topk_idx[(int64_t)t * K + k];
+                    if (e >= 0 && e < L.num_experts) {
+                        dst_rank = (int)(e / E_l);
+                        le = (int)(e % E_l);
+                        if ((masked >> dst_rank) & 1u) {
                             dst_rank = -1;
+                        } else {
+                            LLHalf h = half_of(a.peers, L, dst_rank, a.half);
+                            slot = atom_add_relaxed_sys(&h.ctrl()->slot_counter[le], 1);
+                            if (slot >= slots) {
+                                report_error(a.st, kErrCapacity, dst_rank, slot);
+                                dst_rank = -1;
+                            }
                         }
                     }
                 }
-            }
-            for (int k = 0; k < K; ++k) {
-                const int d = __shfl_sync(0xffffffffu, dst_rank, k);
-                const int dle = __shfl_sync(0xffffffffu, le, k);
-                const int ds = __shfl_sync(0xffffffffu, slot, k);
-                if (d < 0) continue;
-                LLHalf h = half_of(a.peers, L, d, a.half);
-                const int64_t row = (int64_t)dle * slots + ds;
-                if (lane == 0) {
-                    tma_store_1d(h.recv_x() + row * row_bytes, buf, row_bytes);
-                    h.src_info()[row] = t;
-                    h.src_meta()[row] = a.rank * K + k;
+                dst_rank = __shfl_sync(0xffffffffu, dst_rank, 0);
+                le = __shfl_sync(0xffffffffu, le, 0);
+                slot = __shfl_sync(0xffffffffu, slot, 0);
+                if (dst_rank >= 0) {
+                    LLHalf h = half_of(a.peers, L, dst_rank, a.half);
+                    const int64_t row = (int64_t)le * slots + slot;
+                    if (lane == 0) {
+                        tma_store_1d(h.recv_x() + row * row_bytes, buf, row_bytes);
+                        bulk_commit();
+                        h.src_info()[row] = t;
+                        h.src_meta()[row] = a.rank * K + k;
+                    }
+                    if (a.use_fp8) {
+                        float* sc = h.recv_scales() + (int64_t)le * nb * slots;
+                        for (int b = lane; b < nb; b += 32) sc[(int64_t)b * slots + slot] = sbuf[b];
+                    }
                 }
-                if (a.use_fp8) {
-                    float* sc = h.recv_scales() + (int64_t)dle * nb * slots;
-                    for (int b = lane; b < nb; b += 32) sc[(int64_t)b * slots + ds] = sbuf[b];
-                }
+                if (lane == 0) bulk_wait_read<0>();  // the row buffer is rewritten for the next token
             }
-            if (lane == 0) bulk_commit();
-            __syncwarp();
+            __syncthreads();
         }
-        if (lane == 0) {
+        if (warp < K && lane == 0) {
             bulk_wait<0>();
             fence_proxy_async_global();
         }
@@ -161,7 +170,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
                 mine.ctrl()->send_finished_blocks = 0;
                 fence_sys();
                 for (int d = 0; d < R; ++d) {
-                    if (((masked >> (d))) & 1u) continue;
+                    if ((masked >> d) & 1u) continue;
                     st_release_sys(&half_of(a.peers, L, d, a.half).ctrl()->dispatch_done[a.rank], 1);
                 }
             }
@@ -208,13 +217,12 @@ void launch_ll_dispatch(const LLDispatchArgs& a, cudaStream_t stream) {
     const int W = 8;
     const int nb = L.hidden / 128;
     const int row_bytes = a.use_fp8 ? L.hidden : 2 * L.hidden;
-    const int warp_buf_bytes = (row_bytes + nb * 4 + 127) / 128 * 128;
-    const size_t smem = (a.phases & 1) ? (size_t)W * warp_buf_bytes : 0;
+    const size_t smem = (a.phases & 1) ? (size_t)((row_bytes + nb * 4 + 127) / 128 * 128) : 0;
     int num_sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     int blocks = 1;
-    if (a.phases & 1) blocks = (a.num_tokens + W - 1) / W;
+    if (a.phases & 1) blocks = a.num_tokens;  // one block per token
     if (a.phases & 2) blocks = blocks > L.num_local_experts ? blocks : L.num_local_experts;
     if (blocks > num_sms) blocks = num_sms;  // all blocks co-resident: the recv phase may wait on the send phase
     if (blocks < 1) blocks = 1;
@@ -309,7 +317,9 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
         if (aborted(a.st) && !a.shrink) return;
         masked = load_mask_bits(a.mask, R);  // ranks masked by an expired wait above
         const __nv_bfloat16* recv = mine.combine_recv();
-        for (int t = blockIdx.x * W + warp; t < a.num_tokens; t += gridDim.x * W) {
+        // Eight warps per token, each summing one eighth of the hidden dimension.
+        const int span = (H / W + 7) / 8 * 8;
+        for (int t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {
             float wk = 0.f;
             int use = 0;
             if (lane < K) {
@@ -320,7 +330,6 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 }
             }
             const uint32_t use_mask = __ballot_sync(0xffffffffu, use);
-            // Gather the (token, k) rows that contribute, then load all of a slice before summing.
             int ks[kMaxTopk];
             float ws[kMaxTopk];
             int n = 0;
@@ -333,7 +342,8 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 }
             }
             const __nv_bfloat16* trow = recv + (int64_t)t * K * H;
-            for (int e0 = lane * 8; e0 < H; e0 += 256) {
+            const int h0 = warp * span, h1 = min(H, h0 + span);
+            for (int e0 = h0 + lane * 8; e0 < h1; e0 += 256) {
                 int4 v[kMaxTopk];
 #pragma unroll
                 for (int q = 0; q < kMaxTopk; ++q)
@@ -371,7 +381,7 @@ void launch_ll_combine(const LLCombineArgs& a, cudaStream_t stream) {
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     int blocks = num_sms;
     if (!(a.phases & 1)) {
-        blocks = (a.num_tokens + W - 1) / W;
+        blocks = a.num_tokens;  // receive: one block (8 warps) per token
         if (blocks > num_sms) blocks = num_sms;
     }
     if (blocks < 1) blocks = 1;

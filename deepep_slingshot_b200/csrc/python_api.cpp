@@ -59,6 +59,7 @@ PYBIND11_MODULE(_C, m) {
         .def("get_error_state", &ep::Buffer::get_error_state)
         .def("clear_error", &ep::Buffer::clear_error)
         .def("set_timeout_secs", &ep::Buffer::set_timeout_secs)
+        .def("get_profile", &ep::Buffer::get_profile)
         .def("get_dispatch_layout", &ep::Buffer::get_dispatch_layout)
         .def("intranode_dispatch", &ep::Buffer::intranode_dispatch)
         .def("intranode_combine", &ep::Buffer::intranode_combine)

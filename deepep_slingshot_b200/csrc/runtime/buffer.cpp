@@ -9,6 +9,7 @@
 #include <cstring>
 #include <stdexcept>
 #include <thread>
+#include <cstdlib>
 
 namespace ep {
 
@@ -218,6 +219,11 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     if (rank < 0 || rank >= num_ranks) throw std::runtime_error("bad rank");
     EP_CUDA_CHECK(cudaGetDevice(&device_id_));
     set_timeout_secs(gpu_timeout_secs);
+    const char* prof = std::getenv("DEEPEP_B200_PROFILE");
+    profile_enabled_ = prof != nullptr && std::string(prof) == "1";
+    // Row dealing of the pull/push pipelines: chunks of N rows round-robin over pairs (0: contiguous).
+    const char* chunk = std::getenv("DEEPEP_B200_ROW_CHUNK");
+    row_chunk_ = chunk != nullptr ? std::max(0, std::atoi(chunk)) : 0;
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
@@ -385,6 +391,37 @@ PeerTable Buffer::ll_peers() const {
     return p;
 }
 
+// Opt-in kernel timing (env DEEPEP_B200_PROFILE=1): events at fixed points of every dispatch /
+// combine; `get_profile()` synchronizes and returns the mean milliseconds between marks.
+// Points: 0 stage, 1 notify, 2 pull, 3 dispatch end, 4 combine, 5 combine end.
+void Buffer::prof_mark(cudaStream_t stream, int point) {
+    if (!profile_enabled_) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, stream);
+    prof_events_.push_back({point, e});
+}
+
+std::map<std::string, double> Buffer::get_profile() {
+    std::map<std::string, double> out;
+    cudaDeviceSynchronize();
+    const char* names[] = {"stage", "notify", "pull", "dispatch_end", "combine", "combine_end"};
+    std::map<std::string, std::pair<double, int>> acc;
+    for (size_t i = 0; i + 1 < prof_events_.size(); ++i) {
+        const int a = prof_events_[i].first, b = prof_events_[i + 1].first;
+        if (b != a + 1 || a == 3) continue;
+        float ms = 0;
+        cudaEventElapsedTime(&ms, prof_events_[i].second, prof_events_[i + 1].second);
+        const std::string key = names[a];
+        acc[key].first += ms;
+        acc[key].second += 1;
+    }
+    for (auto& kv : acc) out[kv.first + "_ms"] = kv.second.first / std::max(1, kv.second.second);
+    for (auto& pe : prof_events_) cudaEventDestroy(pe.second);
+    prof_events_.clear();
+    return out;
+}
+
 void Buffer::wait_host_counters(int ticket) {
     const auto start = std::chrono::steady_clock::now();
     const double limit = (double)timeout_ns_ * 1e-9;
@@ -516,6 +553,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
     sa.st = st;
+    prof_mark(stream, 0);
     launch_dispatch_stage(sa, num_sms, stream);
 
     // 2) notify
@@ -558,32 +596,33 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     na.cumulative_stats = cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
     na.host = host_counters_dev_;
     na.st = st;
+    prof_mark(stream, 1);
     launch_dispatch_notify(na, stream);
 
-    // 3) receive size: cached, worst case (no CPU sync) or CPU sync on the mapped counters
+    // 3) receive size. Cached: known. Worst case (`num_worst_tokens`): no CPU sync at all. Otherwise
+    //    the pull is launched at once into outputs sized for the largest possible receive
+    //    (num_ranks * capacity rows; the kernel reads the true count on the device) and the host
+    //    waits for the mapped counts while the pull runs, then returns exact-size views.
     int num_recv = -1, num_out_rows = 0;
-    std::vector<int> per_expert_list;
+    const bool cpu_sync = !cached && num_worst_tokens <= 0;
     if (cached) {
         num_recv = (int)cached_recv_src_idx->size(0);
         num_out_rows = num_recv;
     } else if (num_worst_tokens > 0) {
         num_out_rows = num_worst_tokens;
     } else {
-        wait_host_counters(ticket);
-        num_recv = host_counters_->num_recv_tokens;
-        num_out_rows = num_recv;
-        per_expert_list.assign(host_counters_->num_recv_tokens_per_expert, host_counters_->num_recv_tokens_per_expert + E_l);
+        num_out_rows = R * L.capacity;
     }
 
     // 4) outputs + pull
     auto recv_x = torch::empty({num_out_rows, H}, x.options().dtype(out_fp8 ? torch::kFloat8_e4m3fn : torch::kBFloat16));
-    std::optional<torch::Tensor> recv_scales;
+    std::optional<torch::Tensor> recv_scales, scales_storage;
     int64_t scales_ld = 0;
     if (out_fp8) {
         if (scales_col_major) {
             scales_ld = align_up(std::max(num_out_rows, 1), 4);
-            auto storage = torch::empty({H / 128, scales_ld}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
-            recv_scales = storage.narrow(1, 0, num_out_rows).t();
+            scales_storage = torch::empty({H / 128, scales_ld}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+            recv_scales = scales_storage->narrow(1, 0, num_out_rows).t();
         } else {
             recv_scales = torch::empty({num_out_rows, H / 128}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
         }
@@ -607,6 +646,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.dev_num_recv = cached ? nullptr : dev_workspace_ + 1;
     pa.num_recv_host = num_recv;
     pa.num_out_rows = num_out_rows;
+    pa.fill_padding = num_worst_tokens > 0 ? 1 : 0;
     pa.recv_x = recv_x.data_ptr();
     pa.recv_scales = recv_scales.has_value() ? recv_scales->data_ptr<float>() : nullptr;
     pa.scales_col_major = scales_col_major ? 1 : 0;
@@ -616,9 +656,28 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.recv_src_idx = cached ? nullptr : recv_src_idx.data_ptr<int>();
     pa.cached_src_idx = cached ? cached_recv_src_idx->data_ptr<int>() : nullptr;
     pa.stages = 0;
+    pa.host = cached ? nullptr : host_counters_dev_;
+    pa.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
+    pa.host_ticket = ticket;
+    pa.chunk = row_chunk_;
     pa.st = st;
+    prof_mark(stream, 2);
     launch_dispatch_pull(pa, num_sms, stream);
+    prof_mark(stream, 3);
     EP_CUDA_CHECK(cudaGetLastError());
+
+    std::vector<int> per_expert_list;
+    if (cpu_sync) {
+        wait_host_counters(ticket);
+        num_recv = host_counters_->num_recv_tokens;
+        per_expert_list.assign(host_counters_->num_recv_tokens_per_expert, host_counters_->num_recv_tokens_per_expert + E_l);
+        recv_x = recv_x.narrow(0, 0, num_recv);
+        if (recv_scales.has_value())
+            recv_scales = scales_col_major ? scales_storage->narrow(1, 0, num_recv).t() : recv_scales->narrow(0, 0, num_recv);
+        if (recv_topk_idx.has_value()) recv_topk_idx = recv_topk_idx->narrow(0, 0, num_recv);
+        if (recv_topk_weights.has_value()) recv_topk_weights = recv_topk_weights->narrow(0, 0, num_recv);
+        recv_src_idx = recv_src_idx.narrow(0, 0, num_recv);
+    }
 
     auto event = scope.finish(async, {x, x_scales, topk_idx, topk_weights, is_token_in_rank, recv_x, recv_scales, recv_topk_idx,
                                       recv_topk_weights, recv_src_idx, send_head, rpm, spm, recv_rank_prefix,
@@ -678,8 +737,11 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     ca.out = out.data_ptr();
     ca.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
     ca.stages = 0;
+    ca.chunk = row_chunk_;
     ca.st = st;
+    prof_mark(stream, 4);
     launch_combine(ca, num_sms, stream);
+    prof_mark(stream, 5);
     EP_CUDA_CHECK(cudaGetLastError());
     auto event = scope.finish(async, {x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, out, out_w});
     return {out, out_w, event};

@@ -17,6 +17,7 @@
 #include <torch/extension.h>
 
 #include <functional>
+#include <map>
 #include <memory>
 #include <optional>
 #include <string>
@@ -84,6 +85,7 @@ class Buffer {
     std::tuple<int, int, int, int> get_error_state() const;
     void clear_error();
     void set_timeout_secs(double secs);
+    std::map<std::string, double> get_profile();
 
     // ---------------------------------------------------------------- normal mode
     std::tuple<torch::Tensor, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, std::optional<EventHandle>>
@@ -139,6 +141,10 @@ class Buffer {
     PeerTable nvl_peers() const;
     PeerTable ll_peers() const;
     void wait_host_counters(int ticket);
+    void prof_mark(cudaStream_t stream, int point);
+    bool profile_enabled_ = false;
+    int row_chunk_ = 0;
+    std::vector<std::pair<int, cudaEvent_t>> prof_events_;
 
     int rank_, num_ranks_, device_id_;
     int64_t num_nvl_bytes_, num_rdma_bytes_;

@@ -154,6 +154,11 @@ class Buffer:
     def clear_error(self) -> None:
         self.runtime.clear_error()
 
+    def get_profile(self) -> dict:
+        """Mean device milliseconds per phase (stage / notify / pull / combine) since the last call,
+        recorded only when the process runs with DEEPEP_B200_PROFILE=1 (diagnostics; adds events)."""
+        return dict(self.runtime.get_profile())
+
     def barrier(self, use_comm_stream: bool = True, with_cpu_sync: bool = False) -> None:
         self.runtime.barrier(use_comm_stream, with_cpu_sync)
 
