@@ -16,6 +16,7 @@ from .._ext import require_ext
 from ..utils.event import EventOverlap
 from ..utils.envs import get_nvlink_gbs
 from ..utils.math import align
+from ..ops.permute import permute, unpermute
 from .buffer import Buffer
 
 
@@ -138,8 +139,6 @@ class ElasticBuffer:
                  handle: Optional[EPHandle] = None, do_handle_copy: bool = True, do_cpu_sync: Optional[bool] = None,
                  do_expand: bool = False, use_tma_aligned_col_major_sf: bool = False, quantize_fp8: bool = False,
                  round_scale: bool = False):
-        if do_expand:
-            raise NotImplementedError('expanded dispatch layout: use ops.permute on the non-expanded result')
         x, sf = x if isinstance(x, tuple) else (x, None)
         if handle is not None:
             assert topk_idx is None and topk_weights is None
@@ -150,9 +149,12 @@ class ElasticBuffer:
             rpm, spm, rrp, src_idx, itir, send_head = handle.legacy_handle
             out = self.runtime.intranode_dispatch(
                 x, sf, None, None, None, 0, rpm, spm, src_idx, send_head, handle.expert_alignment, 0, quantize_fp8,
-                round_scale, use_tma_aligned_col_major_sf, None, num_sms, prev, async_with_compute_stream,
-                allocate_on_comm_stream)
-            recv_x = (out[0], out[1]) if out[1] is not None else out[0]
+                round_scale, use_tma_aligned_col_major_sf and not handle.do_expand, None, num_sms, prev,
+                async_with_compute_stream, allocate_on_comm_stream)
+            rx, rs = out[0], out[1]
+            if handle.do_expand:
+                rx, rs = self._expand_rows(rx, rs, handle)
+            recv_x = (rx, rs) if rs is not None else rx
             return recv_x, None, None, handle, EventOverlap(out[11])
         assert topk_idx is not None and num_experts is not None
         num_topk = topk_idx.shape[1]
@@ -175,17 +177,50 @@ class ElasticBuffer:
         src_rank = src_rank.clamp_(max=self.num_ranks - 1).to(torch.int32)
         recv_src_metadata = torch.stack([src_rank * num_max_tokens_per_rank + src_idx, src_rank], dim=1)
         psum_expert = per_expert_dev.cumsum(0).to(torch.int32)
-        ep_handle = EPHandle(False, num_experts, expert_alignment, num_max_tokens_per_rank, num_sms,
+        ep_handle = EPHandle(do_expand, num_experts, expert_alignment, num_max_tokens_per_rank, num_sms,
                              topk_idx.clone() if do_handle_copy else topk_idx, per_expert_list, rrp[1:], psum_expert,
                              recv_src_metadata, legacy)
+        if do_expand:
+            # Expanded layout: one row per (received token, local expert), grouped by expert with every
+            # group padded to `expert_alignment` (the permute kernels). recv_src_metadata gains the row
+            # of each top-k slot (-1 if not local); psum per expert = aligned start + unpadded count.
+            E_l = num_experts // self.num_ranks
+            ep_handle.recv_topk_idx_local = recv_topk_idx
+            perm = permute(recv_x, recv_topk_idx, E_l, alignment=expert_alignment, probs=recv_topk_weights,
+                           x_scales=recv_sf.contiguous() if recv_sf is not None else None)
+            ep_handle.row_map = perm.row_map
+            ep_handle.expert_offsets = perm.expert_offsets
+            ep_handle.recv_src_metadata = torch.cat([recv_src_metadata, perm.row_map], dim=1)
+            ep_handle.psum_num_recv_tokens_per_expert = (perm.expert_offsets[:-1] + perm.expert_counts).to(torch.int32)
+            ep_handle.num_recv_tokens_per_expert_list = perm.expert_counts.tolist() if do_cpu_sync else []
+            rows = int(perm.expert_offsets[-1].item())
+            recv_x = perm.x[:rows]
+            recv_sf = perm.scales[:rows] if perm.scales is not None else None
+            if recv_sf is not None and use_tma_aligned_col_major_sf:
+                recv_sf = recv_sf.t().contiguous().t()
+            recv_topk_weights = perm.probs[:rows] if perm.probs is not None else None
         out_x = (recv_x, recv_sf) if recv_sf is not None else recv_x
         return out_x, recv_topk_idx, recv_topk_weights, ep_handle, EventOverlap(event)
+
+    @staticmethod
+    def _expand_rows(rx, rs, handle):
+        """Cached-mode expansion with the handle's grouped layout."""
+        E_l = handle.expert_offsets.numel() - 1
+        perm = permute(rx, handle.recv_topk_idx_local, E_l, alignment=handle.expert_alignment,
+                       x_scales=rs.contiguous() if rs is not None else None)
+        rows = int(handle.expert_offsets[-1].item())
+        return perm.x[:rows], (perm.scales[:rows] if perm.scales is not None else None)
 
     def combine(self, x: torch.Tensor, handle: EPHandle, topk_weights: Optional[torch.Tensor] = None,
                 bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None, num_sms: int = 0,
                 num_qps: int = 0, previous_event=None, previous_event_before_epilogue=None,
                 async_with_compute_stream: bool = False, allocate_on_comm_stream: bool = False):
         num_sms = handle.num_sms if num_sms == 0 else num_sms
+        if handle.do_expand:
+            # One row per (token, local expert): sum each token's rows first (weights already applied
+            # by the caller, as in the reference's expanded combine), then combine across ranks.
+            x = unpermute(x.contiguous(), handle.row_map, None)
+            topk_weights = None
         rpm, spm, _, src_idx, _, send_head = handle.legacy_handle
         bias_0, bias_1 = Buffer._unpack_bias(bias)
         combined_x, combined_w, event = self.runtime.intranode_combine(

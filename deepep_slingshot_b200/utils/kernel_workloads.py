@@ -1,0 +1,126 @@
+"""Small single-GPU workloads that launch every sm_100a kernel of the library once.
+
+Used to profile kernels in isolation (for example with Nsight Compute, filtering on the NVTX range
+`profile`): each workload first runs once as a warm-up outside the range, then once inside it.
+
+    python -m deepep_slingshot_b200.utils.kernel_workloads [--only name,name] [--tokens 4096]
+
+Sizes default to inputs larger than L2 for the bandwidth-bound kernels while keeping the whole
+process within a few GB of device memory.
+"""
+import argparse
+import datetime
+import socket
+
+import torch
+import torch.distributed as dist
+
+
+def _init_single_rank():
+    if dist.is_initialized():
+        return
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        port = s.getsockname()[1]
+    torch.cuda.set_device(0)
+    dist.init_process_group('nccl', init_method=f'tcp://127.0.0.1:{port}', rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device('cuda', 0))
+
+
+def build(args):
+    from deepep_slingshot_b200 import Buffer
+    from deepep_slingshot_b200.ops import gemm, permute, quant
+    from deepep_slingshot_b200.utils import gate
+    from deepep_slingshot_b200._ext import require_ext
+    N, H, E, K = args.tokens, args.hidden, args.experts, args.topk
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
+    idx, w = gate.normal_routing(N, E, K, generator=g)
+    idx, w = idx.cuda(), w.cuda()
+    T = args.ll_tokens
+    E_ll = args.ll_experts
+    buf = Buffer(dist.group.WORLD, num_nvl_bytes=Buffer.get_nvl_buffer_size_hint(N, H, 1),
+                 num_rdma_bytes=Buffer.get_low_latency_rdma_size_hint(T, H, 1, E_ll), low_latency_mode=True)
+    lx = x[:T].contiguous()
+    lidx, lw = gate.uniform_routing(T, E_ll, K, generator=g)
+    lidx, lw = lidx.cuda(), lw.cuda()
+    ly = torch.randn((E_ll, T, H), generator=g).to(torch.bfloat16).cuda()
+    y_recv = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()  # world 1: at most N rows arrive
+    state = {}
+
+    def layout():
+        state['layout'] = buf.get_dispatch_layout(idx, E)
+
+    def dispatch():
+        ntpr, _, ntpe, itir, _ = state['layout']
+        state['disp'] = buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe,
+                                     topk_idx=idx, topk_weights=w, quantize_fp8=True)
+
+    def combine():
+        (rx, rs), ri, rw, _, h, _ = state['disp']
+        state['comb'] = buf.combine(y_recv[:rx.shape[0]], h, topk_weights=rw)
+
+    def ll():
+        recv, cnt, hh, _, hook = buf.low_latency_dispatch(lx, lidx, T, E_ll, use_fp8=True, return_recv_hook=True)
+        hook()
+        out, _, chook = buf.low_latency_combine(ly, lidx, lw, hh, return_recv_hook=True)
+        chook()
+
+    def cast():
+        q, s = quant.per_token_cast_to_fp8(x)
+        quant.per_token_cast_back(q, s)
+
+    rows_per, n1, k1, e_g = args.gemm_rows, 2 * args.inter, H, args.gemm_experts
+    ga, gsa = quant.per_token_cast_to_fp8(torch.randn((rows_per * e_g, k1), generator=g).to(torch.bfloat16).cuda())
+    gb, gsb = gemm.quantize_weights_fp8((torch.randn((e_g, n1, k1), generator=g) * 0.02).cuda())
+    gsb = gsb.contiguous()
+    goff = torch.arange(0, e_g + 1, dtype=torch.int32, device='cuda') * rows_per
+    gcnt = torch.full((e_g,), rows_per, dtype=torch.int32, device='cuda')
+
+    def grouped_gemm():
+        state['h'] = gemm.grouped_gemm_fp8(ga, gsa, gb, gsb, goff, gcnt)
+
+    def swiglu():
+        require_ext().swiglu_quant(state['h'], False)
+
+    def perm():
+        p = permute.permute(x, idx[:, :K], E, alignment=128, probs=w)
+        permute.unpermute(p.x, p.row_map, w)
+
+    def barrier():
+        buf.barrier()
+
+    return {'layout': layout, 'dispatch': dispatch, 'combine': combine, 'low_latency': ll, 'cast': cast,
+            'grouped_gemm': grouped_gemm, 'swiglu_quant': swiglu, 'permute': perm, 'barrier': barrier}
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument('--only', default='')
+    p.add_argument('--tokens', type=int, default=4096)
+    p.add_argument('--hidden', type=int, default=7168)
+    p.add_argument('--experts', type=int, default=256)
+    p.add_argument('--topk', type=int, default=8)
+    p.add_argument('--inter', type=int, default=2048)
+    p.add_argument('--ll-tokens', type=int, default=128)
+    p.add_argument('--ll-experts', type=int, default=64)
+    p.add_argument('--gemm-rows', type=int, default=1024)
+    p.add_argument('--gemm-experts', type=int, default=4)
+    args = p.parse_args()
+    _init_single_rank()
+    work = build(args)
+    names = [n for n in work if not args.only or n in args.only.split(',')]
+    for n in names:  # warm-up outside the profiled range
+        work[n]()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push('profile')
+    for n in names:
+        work[n]()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print('kernel workloads done:', ','.join(names))
+    dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()
