@@ -5,12 +5,16 @@
 // The reference has no permute (SGLang/DeepGEMM do it downstream of DeepEP,
 // backend/tests/sglang_dispatcher_smoke.py:107-124); the v2 `do_expand` layout
 // ([DE]deep_ep/buffers/elastic.py:830-855) is the closest. Here it is three sm_100a kernels with a
-// deterministic row order (chunk of 32 tokens, then top-k slot, then lane):
+// deterministic row order (chunk of 32 tokens, then top-k slot, then lane), in four launches:
 //   count   : one warp per 32-token chunk adds its per-expert counts into scratch[chunk][expert];
 //   scan    : one CTA turns the counts into per-(chunk, expert) bases and aligned expert offsets;
-//   scatter : one warp per chunk ranks equal experts with __match_any_sync, writes row_map and
-//             copies rows (and FP8 scales / top-k probabilities) into the grouped layout.
+//   rowmap  : one warp per chunk ranks equal experts with __match_any_sync and writes row_map (and
+//             the permuted top-k probabilities);
+//   copy    : one warp per (token, row segment) reads the segment once and writes its K copies
+//             (and the FP8 scales) into the grouped layout.
 // Scratch: 2 * num_chunks * num_experts int32 (counts, bases), zeroed by the count launch.
+#include <algorithm>
+
 #include <cuda_bf16.h>
 
 #include "../include/ep/device.cuh"
@@ -46,21 +50,38 @@ __global__ void __launch_bounds__(256) permute_count_kernel(const int64_t* __res
 }
 
 // One CTA: bases[c][e] = offset[e] + sum_{c' < c} counts[c'][e]; offsets = aligned exclusive prefix.
+// Experts are processed 1024 at a time; when fewer, the chunk range is split among `1024 / E` thread
+// groups so each thread walks C / groups chunks instead of all of them.
 __global__ void __launch_bounds__(1024) permute_scan_kernel(const int* __restrict__ counts, int num_chunks, int E,
                                                             int alignment, int* __restrict__ bases,
                                                             int* __restrict__ expert_offsets, int* __restrict__ expert_counts) {
+    __shared__ int s_part[1024];  // [group][expert of this pass]: partial sums, then group prefixes
+    __shared__ int s_off[1024];
     __shared__ int s_warp[33];
     const int tid = threadIdx.x;
-    // Pass 1: per-expert totals (thread per expert; E <= 1024 per pass, loop otherwise).
     int carry = 0;
-    for (int e0 = 0; e0 < E; e0 += blockDim.x) {
-        const int e = e0 + tid;
+    for (int e0 = 0; e0 < E; e0 += 1024) {
+        const int eb = min(1024, E - e0);
+        const int ng = 1024 / eb;
+        const int g = tid / eb, el = tid % eb, e = e0 + el;
+        const bool act = g < ng;
+        const int c0 = act ? (int)((int64_t)num_chunks * g / ng) : 0;
+        const int c1 = act ? (int)((int64_t)num_chunks * (g + 1) / ng) : 0;
+        int part = 0;
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) part += counts[(int64_t)c * E + e];
+        if (act) s_part[g * eb + el] = part;
+        __syncthreads();
         int tot = 0;
-        if (e < E)
-            for (int c = 0; c < num_chunks; ++c) tot += counts[(int64_t)c * E + e];
-        if (e < E && expert_counts != nullptr) expert_counts[e] = tot;
-        const int al = e < E ? (alignment > 1 ? (tot + alignment - 1) / alignment * alignment : tot) : 0;
-        // block exclusive scan of `al`
+        if (tid < eb) {
+            for (int gg = 0; gg < ng; ++gg) {
+                const int v = s_part[gg * eb + tid];
+                s_part[gg * eb + tid] = tot;
+                tot += v;
+            }
+            if (expert_counts != nullptr) expert_counts[e0 + tid] = tot;
+        }
+        const int al = tid < eb ? (alignment > 1 ? (tot + alignment - 1) / alignment * alignment : tot) : 0;
         int incl = al;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -70,25 +91,28 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int* __restric
         if (lane_id() == 31) s_warp[warp_id()] = incl;
         __syncthreads();
         if (warp_id() == 0) {
-            const int nw = blockDim.x / 32;
-            int w = lane_id() < nw ? s_warp[lane_id()] : 0;
+            const int w = s_warp[lane_id()];
             int wi = w;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int n = __shfl_up_sync(0xffffffffu, wi, o);
                 if (lane_id() >= o) wi += n;
             }
-            if (lane_id() < nw) s_warp[lane_id()] = wi - w;
-            if (lane_id() == nw - 1) s_warp[32] = wi;
+            s_warp[lane_id()] = wi - w;
+            if (lane_id() == 31) s_warp[32] = wi;
         }
         __syncthreads();
-        const int excl = carry + s_warp[warp_id()] + incl - al;
-        if (e < E) expert_offsets[e] = excl;
+        if (tid < eb) {
+            const int excl = carry + s_warp[warp_id()] + incl - al;
+            expert_offsets[e0 + tid] = excl;
+            s_off[tid] = excl;
+        }
         const int block_total = s_warp[32];
         __syncthreads();
-        if (e < E) {
-            int run = excl;
-            for (int c = 0; c < num_chunks; ++c) {
+        if (act) {
+            int run = s_off[el] + s_part[g * eb + el];
+#pragma unroll 4
+            for (int c = c0; c < c1; ++c) {
                 bases[(int64_t)c * E + e] = run;
                 run += counts[(int64_t)c * E + e];
             }
@@ -99,7 +123,8 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int* __restric
     if (tid == 0) expert_offsets[E] = carry;
 }
 
-__global__ void __launch_bounds__(256) permute_scatter_kernel(PermuteArgs a) {
+// One warp per 32-token chunk: grouped row of every (token, k) and the permuted top-k probability.
+__global__ void __launch_bounds__(256) permute_rowmap_kernel(PermuteArgs a) {
     extern __shared__ int s_cnt[];  // [warps][E] running counts of this chunk
     const int lane = lane_id(), warp = warp_id();
     const int chunk = blockIdx.x * (blockDim.x / 32) + warp;
@@ -108,8 +133,6 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(PermuteArgs a) {
     __syncwarp();
     if (chunk * 32 >= a.num_tokens) return;
     const int t = chunk * 32 + lane;
-    const int row_bytes = a.hidden * a.x_elem_bytes;
-    const int nb = a.hidden / 128;
     for (int k = 0; k < a.num_topk; ++k) {
         int e = -1;
         if (t < a.num_tokens) {
@@ -118,28 +141,59 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(PermuteArgs a) {
         }
         const uint32_t same = __match_any_sync(0xffffffffu, e);
         int pos = -1;
-        if (e >= 0) {
-            const int rank = __popc(same & lanemask_lt());
-            pos = a.bases[(int64_t)chunk * a.num_experts + e] + my[e] + rank;
-        }
+        if (e >= 0) pos = a.bases[(int64_t)chunk * a.num_experts + e] + my[e] + __popc(same & lanemask_lt());
         __syncwarp();
         if (e >= 0 && (same & lanemask_lt()) == 0) my[e] += __popc(same);
         __syncwarp();
         if (t < a.num_tokens) a.row_map[(int64_t)t * a.num_topk + k] = pos;
         if (a.probs != nullptr && pos >= 0) a.probs_perm[pos] = a.probs[(int64_t)t * a.num_topk + k];
-        // Copy the rows of this k-slice: the warp moves one row at a time with 16-byte vectors.
-        uint32_t todo = __ballot_sync(0xffffffffu, pos >= 0);
-        while (todo) {
-            const int src_lane = __ffs(todo) - 1;
-            todo &= todo - 1;
-            const int st = chunk * 32 + src_lane;
-            const int dp = __shfl_sync(0xffffffffu, pos, src_lane);
-            const uint8_t* s = static_cast<const uint8_t*>(a.x) + (int64_t)st * row_bytes;
-            uint8_t* d = static_cast<uint8_t*>(a.x_perm) + (int64_t)dp * row_bytes;
-            for (int o = lane * 16; o < row_bytes; o += 512)
-                *reinterpret_cast<int4*>(d + o) = ld_nc_v4(reinterpret_cast<const int4*>(s + o));
-            if (a.x_scales != nullptr)
-                for (int b = lane; b < nb; b += 32) a.scales_perm[(int64_t)dp * nb + b] = a.x_scales[(int64_t)st * nb + b];
+    }
+}
+
+// Token-major row copy: one warp per (token, 2 KB segment of the row) reads the segment once and
+// writes it to each of the token's grouped rows (K destinations). Segment 0 also copies the scales.
+constexpr int kPermuteCopyUnroll = 4;
+constexpr int kPermuteSegBytes = 32 * 16 * kPermuteCopyUnroll;
+
+__global__ void __launch_bounds__(512) permute_copy_kernel(PermuteArgs a) {
+    const int lane = lane_id();
+    const int warps = blockDim.x / 32;
+    const int row_bytes = a.hidden * a.x_elem_bytes;
+    const int segs = (row_bytes + kPermuteSegBytes - 1) / kPermuteSegBytes;
+    const int nb = a.hidden / 128;
+    const int64_t items = (int64_t)a.num_tokens * segs;
+    for (int64_t it = (int64_t)blockIdx.x * warps + warp_id(); it < items; it += (int64_t)gridDim.x * warps) {
+        const int t = (int)(it / segs), seg = (int)(it % segs);
+        const int pos = lane < a.num_topk ? a.row_map[(int64_t)t * a.num_topk + lane] : -1;
+        const uint32_t valid = __ballot_sync(0xffffffffu, pos >= 0);
+        if (valid == 0) continue;
+        const uint8_t* src = static_cast<const uint8_t*>(a.x) + (int64_t)t * row_bytes;
+        const int o0 = seg * kPermuteSegBytes + lane * 16;
+        int4 v[kPermuteCopyUnroll];
+#pragma unroll
+        for (int u = 0; u < kPermuteCopyUnroll; ++u)
+            if (o0 + u * 512 < row_bytes) v[u] = ld_nc_v4(reinterpret_cast<const int4*>(src + o0 + u * 512));
+        float sv[2];
+        const bool do_scales = a.x_scales != nullptr && seg == 0;
+        if (do_scales) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) sv[j] = lane + 32 * j < nb ? a.x_scales[(int64_t)t * nb + lane + 32 * j] : 0.f;
+        }
+        uint32_t m = valid;
+        while (m) {
+            const int k = __ffs(m) - 1;
+            m &= m - 1;
+            const int dp = __shfl_sync(0xffffffffu, pos, k);
+            uint8_t* dst = static_cast<uint8_t*>(a.x_perm) + (int64_t)dp * row_bytes;
+#pragma unroll
+            for (int u = 0; u < kPermuteCopyUnroll; ++u)
+                if (o0 + u * 512 < row_bytes) *reinterpret_cast<int4*>(dst + o0 + u * 512) = v[u];
+            if (do_scales) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+                    if (lane + 32 * j < nb) a.scales_perm[(int64_t)dp * nb + lane + 32 * j] = sv[j];
+                for (int b = lane + 64; b < nb; b += 32) a.scales_perm[(int64_t)dp * nb + b] = a.x_scales[(int64_t)t * nb + b];
+            }
         }
     }
 }
@@ -154,60 +208,82 @@ void launch_permute(const PermuteArgs& a, cudaStream_t stream) {
                                                 a.expert_offsets, a.expert_counts);
     if (num_chunks > 0) {
         const size_t smem = sizeof(int) * 8 * (size_t)a.num_experts;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        permute_scatter_kernel<<<blocks, 256, smem, stream>>>(a);
+        if (smem > 48 * 1024) cudaFuncSetAttribute(permute_rowmap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        permute_rowmap_kernel<<<blocks, 256, smem, stream>>>(a);
+        const int row_bytes = a.hidden * a.x_elem_bytes;
+        const int64_t items = (int64_t)a.num_tokens * ((row_bytes + kPermuteSegBytes - 1) / kPermuteSegBytes);
+        const int copy_blocks = (int)std::min<int64_t>((items + 15) / 16, 148 * 4);
+        permute_copy_kernel<<<copy_blocks, 512, 0, stream>>>(a);
     }
 }
 
-// out[t] = sum_k w[t][k] * y[row_map[t][k]] (fp32 accumulation, bf16 out). One warp per token.
-__global__ void __launch_bounds__(256) unpermute_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ row_map,
-                                                        const float* __restrict__ w, int N, int H, int K,
-                                                        __nv_bfloat16* __restrict__ out) {
+// out[t] = sum_k w[t][k] * y[row_map[t][k]] (fp32 accumulation in k order, bf16 out).
+// One warp per (token, 512-column segment); lane k holds the row and weight of slot k, the warp
+// walks the slots four at a time so 8 independent 16-byte loads per lane are in flight.
+constexpr int kUnpermuteSeg = 512;
+
+__global__ void __launch_bounds__(256, 3) unpermute_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ row_map,
+                                                           const float* __restrict__ w, int N, int H, int K,
+                                                           __nv_bfloat16* __restrict__ out) {
     const int lane = lane_id();
     const int warps = blockDim.x / 32;
-    for (int t = blockIdx.x * warps + warp_id(); t < N; t += gridDim.x * warps) {
-        int rows[kMaxTopk];
-        float ws[kMaxTopk];
-        int n = 0;
-        for (int k = 0; k < K; ++k) {
-            const int r = row_map[(int64_t)t * K + k];
-            if (r >= 0) {
-                rows[n] = r;
-                ws[n] = w != nullptr ? w[(int64_t)t * K + k] : 1.f;
-                ++n;
-            }
-        }
-        for (int e0 = lane * 8; e0 < H; e0 += 256) {
-            int4 v[kMaxTopk];
+    const int segs = (H + kUnpermuteSeg - 1) / kUnpermuteSeg;
+    const int64_t items = (int64_t)N * segs;
+    for (int64_t it = (int64_t)blockIdx.x * warps + warp_id(); it < items; it += (int64_t)gridDim.x * warps) {
+        const int t = (int)(it / segs), seg = (int)(it % segs);
+        const int my_row = lane < K ? row_map[(int64_t)t * K + lane] : -1;
+        const float my_w = (lane < K && w != nullptr) ? w[(int64_t)t * K + lane] : 1.f;
+        const int c0 = seg * kUnpermuteSeg + lane * 8;
+        const bool in0 = c0 < H, in1 = c0 + 256 < H;
+        float acc[16];
 #pragma unroll
-            for (int q = 0; q < kMaxTopk; ++q)
-                if (q < n) v[q] = *reinterpret_cast<const int4*>(y + (int64_t)rows[q] * H + e0);
-            float acc[8];
+        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        for (int q0 = 0; q0 < K; q0 += 4) {
+            int4 v[4][2];
+            int r[4];
+            float ws[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll
-            for (int q = 0; q < kMaxTopk; ++q) {
-                if (q >= n) break;
-                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[q]);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 f = __bfloat1622float2(h2[i]);
-                    acc[2 * i] = fmaf(ws[q], f.x, acc[2 * i]);
-                    acc[2 * i + 1] = fmaf(ws[q], f.y, acc[2 * i + 1]);
+            for (int j = 0; j < 4; ++j) {
+                r[j] = __shfl_sync(0xffffffffu, my_row, (q0 + j) & 31);
+                ws[j] = __shfl_sync(0xffffffffu, my_w, (q0 + j) & 31);
+                if (q0 + j >= K) r[j] = -1;
+                if (r[j] >= 0) {
+                    const __nv_bfloat16* p = y + (int64_t)r[j] * H + c0;
+                    if (in0) v[j][0] = ld_nc_v4(reinterpret_cast<const int4*>(p));
+                    if (in1) v[j][1] = ld_nc_v4(reinterpret_cast<const int4*>(p + 256));
                 }
             }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (r[j] < 0) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[j][h]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = __bfloat1622float2(h2[i]);
+                        acc[8 * h + 2 * i] = fmaf(ws[j], f.x, acc[8 * h + 2 * i]);
+                        acc[8 * h + 2 * i + 1] = fmaf(ws[j], f.y, acc[8 * h + 2 * i + 1]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (!(h == 0 ? in0 : in1)) continue;
             int4 o;
             __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-            *reinterpret_cast<int4*>(out + (int64_t)t * H + e0) = o;
+            for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[8 * h + 2 * i], acc[8 * h + 2 * i + 1]);
+            *reinterpret_cast<int4*>(out + (int64_t)t * H + c0 + 256 * h) = o;
         }
     }
 }
 
 void launch_unpermute(const void* y, const int* row_map, const float* w, int N, int H, int K, void* out, cudaStream_t stream) {
     if (N == 0) return;
-    const int blocks = (N + 7) / 8;
+    const int64_t items = (int64_t)N * ((H + kUnpermuteSeg - 1) / kUnpermuteSeg);
+    const int blocks = (int)std::min<int64_t>((items + 7) / 8, 148 * 3 * 4);
     unpermute_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(y), row_map, w, N, H, K,
                                                  static_cast<__nv_bfloat16*>(out));
 }

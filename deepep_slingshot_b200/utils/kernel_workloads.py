@@ -3,7 +3,10 @@
 Used to profile kernels in isolation (for example with Nsight Compute, filtering on the NVTX range
 `profile`): each workload first runs once as a warm-up outside the range, then once inside it.
 
-    python -m deepep_slingshot_b200.utils.kernel_workloads [--only name,name] [--tokens 4096]
+    python -m deepep_slingshot_b200.utils.kernel_workloads [--only name,name] [--tokens 4096] [--time 20]
+
+With `--time R` each workload is also timed: R repetitions, each bracketed by CUDA events on the
+current stream after a 256 MB write that evicts L2, median reported in microseconds.
 
 Sizes default to inputs larger than L2 for the bandwidth-bound kernels while keeping the whole
 process within a few GB of device memory.
@@ -106,6 +109,7 @@ def main():
     p.add_argument('--ll-experts', type=int, default=64)
     p.add_argument('--gemm-rows', type=int, default=1024)
     p.add_argument('--gemm-experts', type=int, default=4)
+    p.add_argument('--time', type=int, default=0, help='timed repetitions per workload (0: profile pass only)')
     args = p.parse_args()
     _init_single_rank()
     work = build(args)
@@ -119,6 +123,21 @@ def main():
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     print('kernel workloads done:', ','.join(names))
+    if args.time > 0:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device='cuda')
+        for n in names:
+            ts = []
+            for _ in range(args.time):
+                flush.fill_(1)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                s.record()
+                work[n]()
+                e.record()
+                torch.cuda.synchronize()
+                ts.append(s.elapsed_time(e) * 1e3)
+            ts.sort()
+            print(f'time {n}: median {ts[len(ts) // 2]:.1f} us, min {ts[0]:.1f} us')
     dist.destroy_process_group()
 
 
