@@ -30,6 +30,7 @@ enum ErrorCode : int {
     kErrBounds = 11,               // an index outside its window (bounds check on every peer store)
     kErrBadArgs = 12,
     kErrTimeoutPP = 13,
+    kErrTimeoutAgrs = 14,          // AGRS: a peer never signalled its all-gather copies / session end
     kErrTimeoutTest = 20,          // transport self-test wait expired (used by the delayed-peer test)
 };
 
@@ -163,5 +164,29 @@ struct alignas(128) LLCtrl {
     int pad[12];
     int slot_counter[kMaxLocalExperts];  // [local expert] slots claimed by senders (remote atomics)
 };
+
+// ------------------------------------------------------------------------------------------------
+// Symmetric side region (pipeline send/recv, AGRS sessions, Engram storage): one CUDA-IPC region per
+// feature and rank, [SymCtrl | data]. Every flag here is written by the PEER named in its comment
+// and waited on locally (signals live in the waiter's memory).
+// ------------------------------------------------------------------------------------------------
+constexpr int kMaxAgrsSlots = 64;            // all-gathers per AGRS session
+constexpr int64_t kSymCtrlBytes = 64 * 1024; // data starts here (TMA / vector aligned)
+
+struct alignas(128) SymCtrl {
+    // Pipeline ring. Direction d = 0: the neighbour is my PREV rank (it sends with dst == its next);
+    // d = 1: the neighbour is my NEXT rank. With two ranks both neighbours are one rank and d = 0.
+    int pp_arrival[2];      // written by neighbour d: tensors it has delivered into my slot set d
+    int pp_release[2];      // written by neighbour d: tensors of mine it has consumed
+    int pp_send_count[2];   // local: tensors sent towards neighbour d
+    int pp_recv_count[2];   // local: tensors received from slot set d
+    int pp_send_ticket[2];  // local CTA tickets (last CTA signals)
+    int pp_recv_ticket[2];
+    int pad0[20];
+    int barrier_signal[kMaxRanks];                    // written by peer r: barrier epoch
+    int agrs_session_signal[kMaxRanks];               // written by peer r: AGRS session it finished
+    int agrs_recv_signal[kMaxAgrsSlots][kMaxRanks];   // written by peer r: its copy of slot s arrived (value = session)
+};
+static_assert(sizeof(SymCtrl) <= kSymCtrlBytes, "SymCtrl must fit in the control block");
 
 }  // namespace ep

@@ -9,6 +9,7 @@
 #include "kernels/api.h"
 #include "runtime/buffer.hpp"
 #include "runtime/ops.hpp"
+#include "runtime/symmetric.hpp"
 
 namespace py = pybind11;
 
@@ -71,6 +72,30 @@ PYBIND11_MODULE(_C, m) {
         .def("low_latency_update_mask_buffer", &ep::Buffer::low_latency_update_mask_buffer)
         .def("low_latency_query_mask_buffer", &ep::Buffer::low_latency_query_mask_buffer)
         .def("low_latency_clean_mask_buffer", &ep::Buffer::low_latency_clean_mask_buffer);
+
+    py::class_<ep::SymmetricRegion>(m, "SymmetricRegion")
+        .def(py::init<int, int, int64_t, double>())
+        .def("get_local_ipc_handle", &ep::SymmetricRegion::get_local_ipc_handle)
+        .def("get_local_device_id", &ep::SymmetricRegion::get_local_device_id)
+        .def("sync", &ep::SymmetricRegion::sync)
+        .def("is_available", &ep::SymmetricRegion::is_available)
+        .def("destroy", &ep::SymmetricRegion::destroy)
+        .def("data_bytes", &ep::SymmetricRegion::data_bytes)
+        .def("local_data", &ep::SymmetricRegion::local_data)
+        .def("check_error", &ep::SymmetricRegion::check_error)
+        .def("get_error_state", &ep::SymmetricRegion::get_error_state)
+        .def("clear_error", &ep::SymmetricRegion::clear_error)
+        .def("barrier", &ep::SymmetricRegion::barrier)
+        .def("pp_set_config", &ep::SymmetricRegion::pp_set_config)
+        .def("pp_send", &ep::SymmetricRegion::pp_send)
+        .def("pp_recv", &ep::SymmetricRegion::pp_recv)
+        .def("agrs_set_config", &ep::SymmetricRegion::agrs_set_config)
+        .def("create_agrs_session", &ep::SymmetricRegion::create_agrs_session)
+        .def("destroy_agrs_session", &ep::SymmetricRegion::destroy_agrs_session)
+        .def("agrs_get_inplace_tensor", &ep::SymmetricRegion::agrs_get_inplace_tensor)
+        .def("all_gather", &ep::SymmetricRegion::all_gather)
+        .def("engram_write", &ep::SymmetricRegion::engram_write)
+        .def("engram_fetch", &ep::SymmetricRegion::engram_fetch);
 
     ep::register_ops(m);
 }

@@ -28,25 +28,6 @@ constexpr int64_t kCtrlRegionMin = 2 << 20;  // control block always present (ba
 
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
-const char* error_name(int code) {
-    switch (code) {
-        case kErrTimeoutNotify: return "timeout waiting for a peer's dispatch counts (notify)";
-        case kErrTimeoutPullDone: return "timeout waiting for receivers to finish reading the staging area";
-        case kErrTimeoutCombineReady: return "timeout waiting for a destination to finish its previous combine";
-        case kErrTimeoutCombineArrive: return "timeout waiting for combine contributions to arrive";
-        case kErrTimeoutBarrier: return "timeout in the NVLink barrier";
-        case kErrTimeoutLLDispatch: return "timeout in low-latency dispatch receive";
-        case kErrTimeoutLLCombine: return "timeout in low-latency combine receive";
-        case kErrTimeoutTma: return "timeout waiting for a TMA bulk copy";
-        case kErrCapacity: return "receive capacity exceeded";
-        case kErrBounds: return "index out of bounds in a peer window";
-        case kErrBadArgs: return "bad kernel arguments";
-        case kErrTimeoutPP: return "timeout in pipeline-parallel send/recv";
-        case kErrTimeoutTest: return "transport self-test wait expired";
-        default: return "unknown error";
-    }
-}
-
 void stream_wait(const at::cuda::CUDAStream& waiter, const at::cuda::CUDAStream& signaler) {
     if (waiter == signaler) return;
     at::cuda::CUDAEvent ev;
@@ -83,6 +64,27 @@ struct StreamScope {
 };
 
 }  // namespace
+
+const char* error_name(int code) {
+    switch (code) {
+        case kErrTimeoutNotify: return "timeout waiting for a peer's dispatch counts (notify)";
+        case kErrTimeoutPullDone: return "timeout waiting for receivers to finish reading the staging area";
+        case kErrTimeoutCombineReady: return "timeout waiting for a destination to finish its previous combine";
+        case kErrTimeoutCombineArrive: return "timeout waiting for combine contributions to arrive";
+        case kErrTimeoutBarrier: return "timeout in the NVLink barrier";
+        case kErrTimeoutLLDispatch: return "timeout in low-latency dispatch receive";
+        case kErrTimeoutLLCombine: return "timeout in low-latency combine receive";
+        case kErrTimeoutTma: return "timeout waiting for a TMA bulk copy";
+        case kErrCapacity: return "receive capacity exceeded";
+        case kErrBounds: return "index out of bounds in a peer window";
+        case kErrBadArgs: return "bad kernel arguments";
+        case kErrTimeoutPP: return "timeout in pipeline-parallel send/recv";
+        case kErrTimeoutAgrs: return "timeout waiting for a peer's AGRS signal or region barrier";
+        case kErrTimeoutTest: return "transport self-test wait expired";
+        default: return "unknown error";
+    }
+}
+
 
 // =================================================================================================
 // Config / layouts

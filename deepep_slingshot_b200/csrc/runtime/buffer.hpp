@@ -55,6 +55,9 @@ struct EventHandle {
     void current_stream_wait() const;
 };
 
+// Human-readable name of an ErrorCode (kernel error reports).
+const char* error_name(int code);
+
 NormalLayout compute_normal_layout(int64_t region_bytes, int hidden, int num_ranks);
 int64_t normal_region_size_for(int num_max_tokens, int hidden, int num_ranks);
 RecordFormat record_format(int hidden, int num_topk, bool fp8);

@@ -7,6 +7,7 @@ push-combine + fp32 reduce), with the layout computed inside the dispatch (no se
 """
 import math
 import os
+from contextlib import contextmanager
 from typing import Optional, Tuple, Union
 
 import torch
@@ -81,6 +82,9 @@ class ElasticBuffer:
 
     def destroy(self) -> None:
         assert self.explicitly_destroy
+        for region in self.__dict__.get('_side_regions', {}).values():
+            region.destroy()
+        self.__dict__['_side_regions'] = {}
         if self._buffer is not None:
             self._buffer.destroy()
             self._buffer = None
@@ -227,3 +231,101 @@ class ElasticBuffer:
             x, topk_weights, bias_0, bias_1, rpm, spm, send_head, src_idx, num_sms, previous_event, async_with_compute_stream,
             allocate_on_comm_stream)
         return combined_x, combined_w, EventOverlap(event)
+
+    # ------------------------------------------------------------------ experimental side features
+    # Engram storage, pipeline send/recv and AGRS all-gather sessions ([DE]deep_ep/buffers/elastic.py:
+    # 433-572). Each feature owns a symmetric CUDA-IPC region that its (collective) configuration call
+    # allocates; see `parallel/symmetric.py` and `csrc/runtime/symmetric.cpp`.
+    def _side_region(self, name: str, data_bytes: int):
+        from .symmetric import SymmetricRegion
+        regions = self.__dict__.setdefault('_side_regions', {})
+        sizes = [None] * self.num_ranks
+        dist.all_gather_object(sizes, int(data_bytes), self.group)
+        need = max(sizes)
+        region = regions.get(name)
+        if region is None or region.data_bytes < need:
+            if region is not None:
+                region.destroy()
+            region = SymmetricRegion(self.group, need)
+            regions[name] = region
+        return region.runtime
+
+    def engram_write(self, storage: torch.Tensor) -> None:
+        """(Experimental) Publish this rank's Engram storage `[num_entries, hidden]` bf16 (collective;
+        barriers before and after). Entry `i` of the group lives on rank `i // num_entries`."""
+        assert storage.dtype == torch.bfloat16 and storage.dim() == 2
+        shapes = [None] * self.num_ranks
+        dist.all_gather_object(shapes, tuple(storage.shape), self.group)
+        assert all(s == shapes[0] for s in shapes), 'every rank must hold the same number of Engram entries'
+        self._engram = self._side_region('engram', storage.numel() * storage.element_size())
+        self._engram.engram_write(storage.contiguous())
+
+    def engram_fetch(self, indices: torch.Tensor, num_qps: int = 0):
+        """(Experimental) Fetch rows by global entry index (int32 `[num_tokens]`). The peer reads run on
+        the region's copy stream; the returned hook joins it and returns `[num_tokens, hidden]` bf16."""
+        assert getattr(self, '_engram', None) is not None, 'call engram_write first'
+        return self._engram.engram_fetch(indices.to(torch.int32).contiguous(), 0)
+
+    def pp_set_config(self, num_max_tensor_bytes: int, num_max_inflight_tensors: int) -> None:
+        """(Experimental) Size the pipeline ring: `num_max_inflight_tensors` receive slots of
+        `num_max_tensor_bytes` per neighbour (collective; includes a barrier)."""
+        slot = align(num_max_tensor_bytes, 128)
+        self._pp = self._side_region('pp', 2 * slot * num_max_inflight_tensors)
+        self._pp.pp_set_config(num_max_tensor_bytes, num_max_inflight_tensors)
+
+    def pp_send(self, t: torch.Tensor, dst_rank_idx: int, num_sms: int = 0) -> None:
+        """(Experimental) Send `t` to the previous or next rank of the ring (TMA stores into its slot)."""
+        assert getattr(self, '_pp', None) is not None, 'call pp_set_config first'
+        self._pp.pp_send(t, dst_rank_idx, num_sms)
+
+    def pp_recv(self, t: torch.Tensor, src_rank_idx: int, num_sms: int = 0) -> None:
+        """(Experimental) Receive into `t` from the previous or next rank of the ring."""
+        assert getattr(self, '_pp', None) is not None, 'call pp_set_config first'
+        self._pp.pp_recv(t, src_rank_idx, num_sms)
+
+    def agrs_set_config(self, num_max_session_bytes: int, num_max_all_gathers_per_session: int) -> None:
+        """(Experimental) Size the AGRS session buffer (collective; includes a barrier)."""
+        self._agrs = self._side_region('agrs', align(num_max_session_bytes, 32))
+        self._agrs.agrs_set_config(num_max_session_bytes, num_max_all_gathers_per_session)
+
+    def create_agrs_session(self) -> None:
+        assert getattr(self, '_agrs', None) is not None, 'call agrs_set_config first'
+        self._agrs.create_agrs_session()
+
+    def destroy_agrs_session(self) -> None:
+        """End the session: after this rank's compute stream, signal every peer and wait for theirs
+        (on the copy stream), so the next session may overwrite the buffer."""
+        self._agrs.destroy_agrs_session()
+
+    @contextmanager
+    def agrs_new_session(self, enabled: bool = True):
+        if not enabled:
+            yield
+            return
+        self.create_agrs_session()
+        try:
+            yield
+        finally:
+            self.destroy_agrs_session()
+
+    def agrs_get_inplace_tensor(self, shapes, dtype: torch.dtype):
+        """Tensor(s) in this rank's slot of the next all-gather: filling them in place saves the local
+        copy. One shape, or a sequence of shapes (batched)."""
+        batched = isinstance(shapes[0], (tuple, list, torch.Size))
+        if not batched:
+            shapes = (shapes,)
+        nbytes = [math.prod(s) * dtype.itemsize for s in shapes]
+        raw = self._agrs.agrs_get_inplace_tensor(nbytes)
+        out = tuple(r.view(dtype).view(tuple(s)) for r, s in zip(raw, shapes))
+        return out if batched else out[0]
+
+    def all_gather(self, t):
+        """All-gather inside an AGRS session on the copy engines (one cudaMemcpyAsync per peer and
+        tensor, no SMs). Returns `(gathered, hook)` (or `(*gathered, hook)` for a sequence): each
+        gathered tensor is `[num_ranks, *t.shape]` in the session buffer; `hook()` makes the current
+        stream wait for every peer's copy."""
+        single = isinstance(t, torch.Tensor)
+        tensors = (t,) if single else tuple(t)
+        raw, hook = self._agrs.all_gather([x.contiguous() for x in tensors])
+        out = tuple(r.view(x.dtype).view(self.num_ranks, *x.shape) for r, x in zip(raw, tensors))
+        return (out[0], hook) if single else (*out, hook)

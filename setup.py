@@ -14,12 +14,14 @@ SOURCES = [
     os.path.join(CSRC, "python_api.cpp"),
     os.path.join(CSRC, "runtime", "buffer.cpp"),
     os.path.join(CSRC, "runtime", "ops.cpp"),
+    os.path.join(CSRC, "runtime", "symmetric.cpp"),
     os.path.join(CSRC, "kernels", "intranode.cu"),
     os.path.join(CSRC, "kernels", "low_latency.cu"),
     os.path.join(CSRC, "kernels", "quant.cu"),
     os.path.join(CSRC, "kernels", "permute.cu"),
     os.path.join(CSRC, "kernels", "permute_noalloc.cu"),
     os.path.join(CSRC, "kernels", "gemm_sm100.cu"),
+    os.path.join(CSRC, "kernels", "symmetric_ops.cu"),
 ]
 
 NVCC_FLAGS = [
