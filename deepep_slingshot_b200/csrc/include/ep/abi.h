@@ -43,6 +43,45 @@ struct ErrorState {
 };
 static_assert(sizeof(ErrorState) == 32, "ErrorState ABI");
 
+// ------------------------------------------------------------------------------------------------
+// Device trace ring: kernels append [start, end, event, block, smid, rank, a, b] records read from
+// %globaltimer when `KernelStatus::trace` is non-null (a runtime switch, no rebuild). Records are
+// appended with one atomic; a full ring drops records and the host sees `cursor > capacity`.
+// ------------------------------------------------------------------------------------------------
+enum TraceEvent : int {
+    kTraceStage = 100,          // dispatch stage block (quantize + records), a = tokens
+    kTraceStageWait = 101,      // stage: wait for receivers of the previous dispatch
+    kTraceNotify = 102,         // notify kernel, a = 1 in cached mode
+    kTraceNotifyWait = 103,     // notify: count exchange wait, a = epoch
+    kTracePull = 104,           // pull block, a = received tokens
+    kTraceCombine = 110,        // combine block (push + reduce), a = 1 for push blocks
+    kTraceCombinePush = 111,    // combine push warp finished its rows, a = warp
+    kTraceLLDispatchSend = 120,
+    kTraceLLDispatchRecv = 121,
+    kTraceLLCombineSend = 122,
+    kTraceLLCombineRecv = 123,
+    kTraceBarrier = 130,
+    kTracePP = 140,             // pipeline copy CTA, a = is_send, b = bytes
+};
+
+struct TraceRecord {
+    uint64_t start_ns;
+    uint64_t end_ns;
+    int32_t event;
+    int32_t block;
+    int32_t smid;
+    int32_t rank;
+    int32_t a;
+    int32_t b;
+};
+static_assert(sizeof(TraceRecord) == 40, "TraceRecord ABI");
+
+struct TraceRing {
+    TraceRecord* records;
+    unsigned long long* cursor;
+    uint64_t capacity;
+};
+
 // Passed by value to every kernel that waits.
 struct KernelStatus {
     ErrorState* host_error;  // host-mapped (cudaHostAllocMapped) device pointer
@@ -50,8 +89,9 @@ struct KernelStatus {
     uint64_t timeout_ns;     // wait limit in nanoseconds of %globaltimer
     int rank;
     int pad;
+    TraceRing* trace;        // device trace ring, or null (tracing off)
 };
-static_assert(sizeof(KernelStatus) == 32, "KernelStatus ABI");
+static_assert(sizeof(KernelStatus) == 40, "KernelStatus ABI");
 
 // Peer table: base address of the same symmetric region on every rank (index = rank). Entry
 // `rank` is the local base. Passed by value (64 bytes).

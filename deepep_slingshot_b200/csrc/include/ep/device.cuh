@@ -103,6 +103,31 @@ __device__ __forceinline__ bool aborted(const KernelStatus& st) {
     return st.abort_flag != nullptr && ld_volatile(st.abort_flag) != 0;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Device trace ring (see TraceRing): `trace_begin` reads the clock only when tracing is on.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t trace_begin(const KernelStatus& st) {
+    return st.trace != nullptr ? globaltimer_ns() : 0;
+}
+__device__ __forceinline__ void trace_end(const KernelStatus& st, int event, uint64_t start, int a = 0, int b = 0) {
+    if (st.trace == nullptr) return;
+    TraceRing* tr = st.trace;
+    const unsigned long long i = atomicAdd(tr->cursor, 1ull);
+    if (i >= tr->capacity) return;
+    uint32_t sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    TraceRecord r;
+    r.start_ns = start;
+    r.end_ns = globaltimer_ns();
+    r.event = event;
+    r.block = (int)blockIdx.x;
+    r.smid = (int)sm;
+    r.rank = st.rank;
+    r.a = a;
+    r.b = b;
+    tr->records[i] = r;
+}
+
 // Spin until `*flag >= target` (signed comparison over a monotonic epoch) with a time limit.
 // Returns true on success. On timeout it reports `code` and returns false; it also gives up early
 // when another block of this launch has already set the abort flag.

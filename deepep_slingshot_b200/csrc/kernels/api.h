@@ -118,6 +118,8 @@ void launch_combine(const CombineArgs& a, int num_sms, cudaStream_t stream);
 
 // ---------------------------------------------------------------- barrier
 void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st, cudaStream_t stream);
+// Writes the GPU's %globaltimer (ns) into `out` (trace clock alignment).
+void launch_read_globaltimer(unsigned long long* out, cudaStream_t stream);
 
 // ---------------------------------------------------------------- low-latency mode
 struct LLDispatchArgs {

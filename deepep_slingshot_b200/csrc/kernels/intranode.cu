@@ -92,13 +92,15 @@ void launch_dispatch_layout(const int64_t* topk_idx, int num_tokens, int num_top
 // =================================================================================================
 // stage: one record per token into the local staging area, FP8 quantization fused.
 // =================================================================================================
-__global__ void __launch_bounds__(256) dispatch_stage_kernel(StageArgs a) {
+__global__ void __launch_bounds__(256, 4) dispatch_stage_kernel(StageArgs a) {
+    const uint64_t t_start = trace_begin(a.st);
     if ((int)threadIdx.x < a.num_ranks) {
         // Receivers must have finished pulling the previous dispatch before the staging is rewritten.
         const int prev_epoch = ld_volatile(a.dispatch_epoch);
         if (prev_epoch > 0) wait_ge(&a.pull_done[threadIdx.x], prev_epoch, a.st, kErrTimeoutPullDone, threadIdx.x);
     }
     __syncthreads();
+    if (threadIdx.x == 0) trace_end(a.st, kTraceStageWait, t_start, a.num_tokens);
     if (aborted(a.st)) return;
 
     const int lane = lane_id();
@@ -142,6 +144,10 @@ __global__ void __launch_bounds__(256) dispatch_stage_kernel(StageArgs a) {
             if (lane == 0) a.token_mask[t] = (uint8_t)m;
             if (idx >= 0 && idx < a.num_experts) atomicAdd(&a.expert_counts[idx], 1);
         }
+    }
+    if (a.st.trace != nullptr) {
+        __syncthreads();
+        if (threadIdx.x == 0) trace_end(a.st, kTraceStage, t_start, a.num_tokens);
     }
 }
 
@@ -226,6 +232,7 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
     const int tid = threadIdx.x, nt = blockDim.x;
     const int R = a.num_ranks;
     NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
+    const uint64_t t_start = trace_begin(a.st);
     if (tid == 0) s_epoch = ld_volatile(&my_ctrl->dispatch_epoch) + 1;
     __syncthreads();
     const int epoch = s_epoch, parity = epoch & 1;
@@ -281,15 +288,20 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
         }
     }
     __syncthreads();
+    const uint64_t t_wait = trace_begin(a.st);
     if (tid < R) {
         fence_sys();
         st_release_sys(&ctrl_of(a.peers, a.layout, tid)->notify_flag[a.rank], epoch);
         wait_ge(&my_ctrl->notify_flag[tid], epoch, a.st, kErrTimeoutNotify, tid);
     }
     __syncthreads();
+    if (tid == 0) trace_end(a.st, kTraceNotifyWait, t_wait, epoch);
     if (aborted(a.st)) return;
     if (a.cached) {
-        if (tid == 0) my_ctrl->dispatch_epoch = epoch;
+        if (tid == 0) {
+            my_ctrl->dispatch_epoch = epoch;
+            trace_end(a.st, kTraceNotify, t_start, 1);
+        }
         return;
     }
 
@@ -327,7 +339,10 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
         a.num_recv_per_expert[le] = al;
     }
     __syncthreads();
-    if (tid == 0) my_ctrl->dispatch_epoch = epoch;
+    if (tid == 0) {
+        my_ctrl->dispatch_epoch = epoch;
+        trace_end(a.st, kTraceNotify, t_start, 0);
+    }
 }
 
 void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream) {
@@ -451,6 +466,7 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
     const int R = a.num_ranks;
     const int slot_bytes = (a.rec.bytes + 127) / 128 * 128;
     const PipeSmem p = pipe_smem(smem, pair, a.stages, slot_bytes);
+    const uint64_t t_start = trace_begin(a.st);
     pipe_init(p);
     if (threadIdx.x == 0) {
         s_prefix[0] = 0;
@@ -560,6 +576,7 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
     __syncthreads();
     // The last block tells every source that its staging may be reused.
     if (threadIdx.x == 0) {
+        trace_end(a.st, kTracePull, t_start, num_recv);
         NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
         fence_sys();
         const int old = atom_add_acq_rel_gpu(&my_ctrl->pull_finished_blocks, 1);
@@ -718,6 +735,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
     const bool pusher = (int)blockIdx.x < a.push_blocks;
     const int row_bytes = H * 2;
     const int slot_bytes = (row_bytes + 127) / 128 * 128;
+    const uint64_t t_start = trace_begin(a.st);
 
     if (pusher && (int)threadIdx.x < R)
         // Destination `tid` must have finished reducing the previous combine before its slots are reused.
@@ -810,10 +828,12 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
             }
         }
     }
+    if (pusher && lane == 0 && warp < 2 * kPairs) trace_end(a.st, kTraceCombinePush, t_start, warp);
     // Every warp (push warps once their rows are sent) reduces tokens of this rank.
     if (!aborted(a.st)) combine_reduce_loop(a, my_ctrl, s_red_base);
     __syncthreads();
     if (threadIdx.x == 0) {
+        trace_end(a.st, kTraceCombine, t_start, pusher ? 1 : 0);
         const int old = atom_add_acq_rel_gpu(&my_ctrl->combine_reduced_blocks, 1);
         if (old == (int)gridDim.x - 1) {
             my_ctrl->combine_reduced_blocks = 0;
@@ -848,6 +868,7 @@ void launch_combine(const CombineArgs& a_in, int num_sms, cudaStream_t stream) {
 // =================================================================================================
 __global__ void barrier_kernel(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st) {
     const int r = threadIdx.x;
+    const uint64_t t_start = trace_begin(st);
     NormalCtrl* mine = reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(peers.base[rank]) + ctrl_off);
     const int epoch = ld_volatile(&mine->barrier_epoch) + 1;
     if (r < num_ranks) {
@@ -857,11 +878,20 @@ __global__ void barrier_kernel(PeerTable peers, int64_t ctrl_off, int rank, int 
         wait_ge(&mine->barrier_flag[r], epoch, st, kErrTimeoutBarrier, r);
     }
     __syncwarp();
-    if (r == 0) mine->barrier_epoch = epoch;
+    if (r == 0) {
+        mine->barrier_epoch = epoch;
+        trace_end(st, kTraceBarrier, t_start, epoch);
+    }
 }
 
 void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st, cudaStream_t stream) {
     barrier_kernel<<<1, 32, 0, stream>>>(peers, ctrl_off, rank, num_ranks, st);
+}
+
+__global__ void read_globaltimer_kernel(unsigned long long* out) { *out = globaltimer_ns(); }
+
+void launch_read_globaltimer(unsigned long long* out, cudaStream_t stream) {
+    read_globaltimer_kernel<<<1, 1, 0, stream>>>(out);
 }
 
 }  // namespace ep

@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
     const int slots = R * L.max_tokens;
     const int nb = H / 128;
     const int row_bytes = a.use_fp8 ? H : 2 * H;
+    const uint64_t t_start = trace_begin(a.st);
     __shared__ uint32_t s_masked;
     if (threadIdx.x == 0) s_masked = load_mask_bits(a.mask, R);
     __syncthreads();
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
         }
         __syncthreads();
         if (threadIdx.x == 0) {
+            trace_end(a.st, kTraceLLDispatchSend, t_start, a.num_tokens);
             LLHalf mine = half_of(a.peers, L, a.rank, a.half);
             fence_sys();
             const int old = atom_add_acq_rel_gpu(&mine.ctrl()->send_finished_blocks, 1);
@@ -178,6 +180,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
     }
 
     if (a.phases & 2) {
+        const uint64_t t_recv = trace_begin(a.st);
         LLHalf mine = half_of(a.peers, L, a.rank, a.half);
         if ((int)threadIdx.x < R && !((masked >> threadIdx.x) & 1u))
             ll_wait(&mine.ctrl()->dispatch_done[threadIdx.x], 1, a.st, kErrTimeoutLLDispatch, threadIdx.x, a.mask,
@@ -209,6 +212,7 @@ __global__ void __launch_bounds__(256) ll_dispatch_kernel(LLDispatchArgs a) {
                 a.layout_range[(int64_t)le * R + threadIdx.x] = (int64_t)s_src_count[threadIdx.x];
             __syncthreads();
         }
+        if (threadIdx.x == 0) trace_end(a.st, kTraceLLDispatchRecv, t_recv);
     }
 }
 
@@ -241,6 +245,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
     const int H = L.hidden, K = L.num_topk, R = L.num_ranks, E_l = L.num_local_experts;
     const int slots = R * L.max_tokens;
     const int row_bytes = 2 * H;
+    const uint64_t t_start = trace_begin(a.st);
     __shared__ uint32_t s_masked;
     if (threadIdx.x == 0) s_masked = load_mask_bits(a.mask, R);
     __syncthreads();
@@ -287,6 +292,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
         }
         __syncthreads();
         if (threadIdx.x == 0) {
+            trace_end(a.st, kTraceLLCombineSend, t_start);
             LLHalf mine = half_of(a.peers, L, a.rank, a.half);
             fence_sys();
             const int old = atom_add_acq_rel_gpu(&mine.ctrl()->csend_finished_blocks, 1);
@@ -302,6 +308,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
     }
 
     if (a.phases & 2) {
+        const uint64_t t_recv = trace_begin(a.st);
         LLHalf mine = half_of(a.peers, L, a.rank, a.half);
         if ((int)threadIdx.x < R && !((masked >> threadIdx.x) & 1u))
             ll_wait(&mine.ctrl()->combine_done[threadIdx.x], 1, a.st, kErrTimeoutLLCombine, threadIdx.x, a.mask,
@@ -369,6 +376,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 *reinterpret_cast<int4*>(static_cast<__nv_bfloat16*>(a.out) + (int64_t)t * H + e0) = o;
             }
         }
+        if (threadIdx.x == 0) trace_end(a.st, kTraceLLCombineRecv, t_recv, a.num_tokens);
     }
 }
 

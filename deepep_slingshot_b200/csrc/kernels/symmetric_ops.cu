@@ -63,6 +63,7 @@ __device__ bool tma_copy(const uint8_t* src, uint8_t* dst, int64_t n, uint8_t* s
 __global__ void __launch_bounds__(32, 1) pp_copy_kernel(PPArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     if (threadIdx.x != 0) return;
+    const uint64_t t_start = trace_begin(a.st);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kCopyStages * kCopyStageBytes);
     const int c = ld_volatile(a.count);
     // send: the slot is free once the neighbour released tensor c - inflight; recv: tensor c arrived
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(32, 1) pp_copy_kernel(PPArgs a) {
         if (ok && blockIdx.x == 0)
             for (int64_t i = body; i < a.bytes; ++i) dst[i] = src[i];
     }
+    trace_end(a.st, kTracePP, t_start, a.is_send, (int)::min(a.bytes, (int64_t)0x7fffffff));
     fence_proxy_async_global();
     __threadfence_system();
     const int t = atomicAdd(a.ticket, 1);

@@ -61,6 +61,10 @@ PYBIND11_MODULE(_C, m) {
         .def("clear_error", &ep::Buffer::clear_error)
         .def("set_timeout_secs", &ep::Buffer::set_timeout_secs)
         .def("get_profile", &ep::Buffer::get_profile)
+        .def("enable_trace", &ep::Buffer::enable_trace)
+        .def("disable_trace", &ep::Buffer::disable_trace)
+        .def("read_trace", &ep::Buffer::read_trace)
+        .def("sample_clock", &ep::Buffer::sample_clock)
         .def("get_dispatch_layout", &ep::Buffer::get_dispatch_layout)
         .def("intranode_dispatch", &ep::Buffer::intranode_dispatch)
         .def("intranode_combine", &ep::Buffer::intranode_combine)

@@ -316,6 +316,12 @@ void Buffer::destroy() {
     if (ll_base_) cudaFree(ll_base_);
     if (dev_workspace_) cudaFree(dev_workspace_);
     if (mask_) cudaFree(mask_);
+    if (trace_dev_) {
+        cudaFree(trace_dev_);
+        cudaFree(trace_records_);
+        cudaFree(trace_cursor_);
+        trace_dev_ = nullptr;
+    }
     if (host_error_) cudaFreeHost(host_error_);
     if (host_counters_) cudaFreeHost(host_counters_);
     nvl_base_ = ll_base_ = nullptr;
@@ -357,7 +363,61 @@ KernelStatus Buffer::status() const {
     s.abort_flag = dev_workspace_;
     s.timeout_ns = timeout_ns_;
     s.rank = rank_;
+    s.trace = trace_dev_;
     return s;
+}
+
+void Buffer::enable_trace(int64_t capacity) {
+    TORCH_CHECK(capacity > 0, "trace capacity must be positive");
+    disable_trace();
+    EP_CUDA_CHECK(cudaMalloc(&trace_records_, sizeof(TraceRecord) * capacity));
+    EP_CUDA_CHECK(cudaMalloc(&trace_cursor_, sizeof(unsigned long long)));
+    EP_CUDA_CHECK(cudaMemset(trace_cursor_, 0, sizeof(unsigned long long)));
+    EP_CUDA_CHECK(cudaMalloc(&trace_dev_, sizeof(TraceRing)));
+    TraceRing ring{trace_records_, trace_cursor_, (uint64_t)capacity};
+    EP_CUDA_CHECK(cudaMemcpy(trace_dev_, &ring, sizeof(ring), cudaMemcpyHostToDevice));
+    trace_capacity_ = capacity;
+}
+
+void Buffer::disable_trace() {
+    if (trace_dev_ == nullptr) return;
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
+    cudaFree(trace_dev_);
+    cudaFree(trace_records_);
+    cudaFree(trace_cursor_);
+    trace_dev_ = nullptr;
+    trace_records_ = nullptr;
+    trace_cursor_ = nullptr;
+    trace_capacity_ = 0;
+}
+
+std::tuple<torch::Tensor, int64_t> Buffer::read_trace(bool reset) {
+    TORCH_CHECK(trace_dev_ != nullptr, "tracing is not enabled");
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
+    unsigned long long n = 0;
+    EP_CUDA_CHECK(cudaMemcpy(&n, trace_cursor_, sizeof(n), cudaMemcpyDeviceToHost));
+    const int64_t kept = std::min<int64_t>((int64_t)n, trace_capacity_);
+    auto out = torch::empty({kept, (int64_t)sizeof(TraceRecord)}, torch::dtype(torch::kUInt8));
+    if (kept > 0)
+        EP_CUDA_CHECK(cudaMemcpy(out.data_ptr(), trace_records_, sizeof(TraceRecord) * kept, cudaMemcpyDeviceToHost));
+    if (reset) EP_CUDA_CHECK(cudaMemset(trace_cursor_, 0, sizeof(unsigned long long)));
+    return {out, (int64_t)n};
+}
+
+std::tuple<int64_t, int64_t, int64_t> Buffer::sample_clock() {
+    auto stream = at::cuda::getCurrentCUDAStream();
+    EP_CUDA_CHECK(cudaStreamSynchronize(stream));
+    auto mono = []() {
+        return (int64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                   std::chrono::steady_clock::now().time_since_epoch()).count();
+    };
+    auto cell = torch::zeros({1}, torch::dtype(torch::kInt64).device(torch::kCUDA, device_id_));
+    EP_CUDA_CHECK(cudaStreamSynchronize(stream));
+    const int64_t before = mono();
+    launch_read_globaltimer(reinterpret_cast<unsigned long long*>(cell.data_ptr<int64_t>()), stream.stream());
+    EP_CUDA_CHECK(cudaStreamSynchronize(stream));
+    const int64_t after = mono();
+    return {before, cell.cpu().item<int64_t>(), after};
 }
 
 void Buffer::check_error() const {

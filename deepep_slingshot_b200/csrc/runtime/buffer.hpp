@@ -90,6 +90,14 @@ class Buffer {
     void set_timeout_secs(double secs);
     std::map<std::string, double> get_profile();
 
+    // Device trace ring (off by default): every traced kernel appends per-block records.
+    void enable_trace(int64_t capacity);
+    void disable_trace();
+    // (records [n, 40] uint8 on the CPU, appended count; count > capacity means records were dropped)
+    std::tuple<torch::Tensor, int64_t> read_trace(bool reset);
+    // (host CLOCK_MONOTONIC ns before, GPU %globaltimer ns, host ns after) for clock alignment.
+    std::tuple<int64_t, int64_t, int64_t> sample_clock();
+
     // ---------------------------------------------------------------- normal mode
     std::tuple<torch::Tensor, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, std::optional<EventHandle>>
     get_dispatch_layout(const torch::Tensor& topk_idx, int num_experts, std::optional<EventHandle>& previous_event,
@@ -170,6 +178,10 @@ class Buffer {
     HostCounters* host_counters_dev_ = nullptr;
     int* dev_workspace_ = nullptr;  // [0] abort flag, [1] num_recv, [2..] scratch
     int* mask_ = nullptr;           // [kMaxRanks] shrink-mode mask
+    TraceRing* trace_dev_ = nullptr;
+    TraceRecord* trace_records_ = nullptr;
+    unsigned long long* trace_cursor_ = nullptr;
+    int64_t trace_capacity_ = 0;
 
     at::cuda::CUDAStream comm_stream_;
     int dispatch_epoch_ = 0, combine_seq_ = 0, barrier_epoch_ = 0, ll_dispatch_seq_ = 0, ll_combine_seq_ = 0;

@@ -1,0 +1,232 @@
+"""EP benchmark with an exact reference: correctness before timing, per case.
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m deepep_slingshot_b200.harness.ep_benchmark \
+        --models v4flash qwen3 minimax deepseek_v3 --routing uniform mixed skew2 hot_rank --dtype fp8 bf16 \
+        --out ep_results
+
+For every (model, tokens, dtype, routing, seed) case each rank:
+  1. builds its routing (`harness.routing`), inputs and routing weights;
+  2. checks a fresh dispatch against `ReferenceBuffer` (NCCL all_to_all_single): received payload
+     and FP8 scales byte for byte, top-k ids, weights, source indices and the 128-aligned
+     per-expert counts; then checks combine;
+  3. times fresh dispatch, cached dispatch and combine with CUDA events after an L2 flush, taking
+     the per-iteration max over ranks.
+Records: `manifest-rank{r}.jsonl` (source hashes, versions, environment), `correctness-rank{r}.jsonl`,
+`timings-rank{r}.jsonl`; rank 0 writes `summary.csv` and `repeatability.json` (`harness.summarize`).
+Model shapes follow the reference's benchmark (backend/tests/ep_benchmark.py:19) plus DeepSeek-V3.
+"""
+import argparse
+import datetime
+import hashlib
+import json
+import os
+import platform
+import socket
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+MODELS = {'v4flash': (4096, 256, 6), 'qwen3': (4096, 128, 8), 'minimax': (3072, 256, 8),
+          'deepseek_v3': (7168, 256, 8)}
+
+
+def dispatch_bytes(num_recv: int, hidden: int, num_topk: int, fp8: bool) -> int:
+    """DeepEP v2 logical bytes of a dispatch: received rows x (row + scales + int64 ids + fp32 weights)."""
+    row = hidden if fp8 else 2 * hidden
+    scales = (hidden // 128) * 4 if fp8 else 0
+    return num_recv * (row + scales + 8 * num_topk + 4 * num_topk)
+
+
+def combine_bytes(num_recv: int, hidden: int, num_topk: int) -> int:
+    return num_recv * (2 * hidden + 4 * num_topk)
+
+
+def source_hashes() -> dict:
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = {}
+    for d, _, files in os.walk(root):
+        for f in sorted(files):
+            if f.endswith(('.py', '.cu', '.cuh', '.cpp', '.hpp', '.h')):
+                p = os.path.join(d, f)
+                with open(p, 'rb') as fh:
+                    out[os.path.relpath(p, root)] = hashlib.sha256(fh.read()).hexdigest()
+    return out
+
+
+def manifest(args) -> dict:
+    return {'kind': 'manifest', 'rank': dist.get_rank(), 'world': dist.get_world_size(), 'host': socket.gethostname(),
+            'time': datetime.datetime.utcnow().isoformat() + 'Z', 'argv': sys.argv, 'python': platform.python_version(),
+            'torch': torch.__version__, 'cuda': torch.version.cuda,
+            'nccl': '.'.join(map(str, torch.cuda.nccl.version())) if torch.cuda.is_available() else None,
+            'gpu': torch.cuda.get_device_name() if torch.cuda.is_available() else None,
+            'env': {k: v for k, v in os.environ.items() if k.startswith(('DEEPEP_', 'NCCL_', 'CUDA_', 'EP_'))},
+            'sources': source_hashes()}
+
+
+class _Jsonl:
+    def __init__(self, path):
+        self.f = open(path, 'a')
+
+    def write(self, rec):
+        self.f.write(json.dumps(rec) + '\n')
+        self.f.flush()
+
+
+def _check_equal(name, a, b):
+    if not torch.equal(a, b):
+        raise AssertionError(f'{name} mismatch')
+
+
+def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
+    from ..utils.testing import bench, hash_tensor, rank_max
+    from .routing import make_routing
+    rank, R = dist.get_rank(), dist.get_world_size()
+    H, E, K = MODELS[model]
+    fp8 = dtype == 'fp8'
+    idx = make_routing(routing, rank, R, tokens, E, K, seed).cuda()
+    g = torch.Generator(device='cuda').manual_seed(seed * 1000 + rank)
+    w = torch.rand((tokens, K), device='cuda', generator=g)
+    w = torch.where(idx < 0, torch.zeros_like(w), w)
+    w = w / w.sum(1, keepdim=True).clamp_min(1e-6)
+    x = torch.randn((tokens, H), device='cuda', generator=g).to(torch.bfloat16)
+    case = {'model': model, 'hidden': H, 'experts': E, 'topk': K, 'tokens_per_rank': tokens, 'ranks': R,
+            'dispatch_dtype': dtype, 'combine_dtype': 'bf16', 'routing': routing, 'seed': seed,
+            'route_sha256': hash_tensor(idx), 'input_sha256': hash_tensor(x), 'alignment': 128,
+            'num_sms': args.num_sms or buf.num_sms, 'flush_l2': True}
+
+    # ---- correctness (fresh dispatch, then combine)
+    kw = dict(topk_idx=idx, topk_weights=w, num_experts=E, expert_alignment=128)
+    if fp8:
+        kw['quantize_fp8'] = True
+    rx, ri, rw, counts, handle, _ = buf.dispatch(x, **kw)
+    ex, ei, ew, ecounts, ehandle, _ = ref.dispatch(x, **kw)
+    torch.cuda.synchronize()
+    num_recv = (rx[0] if fp8 else rx).shape[0]
+    y = torch.randn((num_recv, H), device='cuda', generator=g).to(torch.bfloat16)
+    error = None
+    try:
+        if fp8:
+            _check_equal('payload', rx[0].view(torch.uint8), ex[0].view(torch.uint8))
+            _check_equal('scales', rx[1], ex[1])
+        else:
+            _check_equal('payload', rx.view(torch.uint8), ex.view(torch.uint8))
+        _check_equal('expert ids', ri, ei)
+        _check_equal('weights', rw, ew)
+        _check_equal('source ids', handle[3], ehandle[3].to(handle[3].dtype))
+        if list(counts) != list(ecounts):
+            raise AssertionError('padded per-expert counts mismatch')
+    except AssertionError as e:
+        error = str(e)
+    # combine is collective: every rank runs it even after a local dispatch mismatch
+    cx, cw, _ = buf.combine(y, handle, topk_weights=rw)
+    ecx, ecw, _ = ref.combine(y, ehandle, topk_weights=ew)
+    torch.cuda.synchronize()
+    if error is None and not torch.allclose(cx.float(), ecx.float(), atol=2e-2, rtol=2e-2):
+        error = 'combine output mismatch'
+    ok = torch.tensor([0 if error else 1], device='cuda')
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok.item()) == 0:
+        raise AssertionError(error or 'a peer rank failed its correctness check')
+    logs['correctness'].write({'kind': 'correctness', **case, 'num_recv': num_recv, 'passed': True})
+
+    # ---- timing (rank-max per iteration)
+    def fresh():
+        buf.dispatch(x, **kw)
+
+    def cached():
+        buf.dispatch(x, handle=handle, quantize_fp8=fp8) if fp8 else buf.dispatch(x, handle=handle)
+
+    def comb():
+        buf.combine(y, handle, topk_weights=rw)
+
+    ops = {'dispatch': (fresh, dispatch_bytes(num_recv, H, K, fp8)),
+           'cached_dispatch': (cached, dispatch_bytes(num_recv, H, K, fp8)),
+           'combine': (comb, combine_bytes(num_recv, H, K))}
+    result = {}
+    for op, (fn, nbytes) in ops.items():
+        dist.barrier()
+        host = []
+
+        def timed():
+            t0 = time.perf_counter()
+            fn()
+            host.append((time.perf_counter() - t0) * 1e6)
+        _, _, _, times = bench(timed, num_warmups=args.warmup, num_tests=args.iters, flush_l2=True)
+        local_us = [t * 1e6 for t in times[1:]]
+        rmax_us = rank_max(local_us)
+        host_max = rank_max([max(host[args.warmup:] or [0.0])])[0]
+        bytes_max = rank_max([float(nbytes)])[0]
+        rec = {'kind': 'timing', **case, 'op': op, 'bytes': nbytes, 'local_us': local_us, 'rank_max_us': rmax_us,
+               'max_host_us_per_iteration': host_max, 'bytes_rank_max': bytes_max}
+        logs['timings'].write(rec)
+        result[op] = rec
+    return case, result
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.split('\n')[0])
+    p.add_argument('--models', nargs='+', choices=list(MODELS), default=['v4flash', 'qwen3', 'minimax'])
+    p.add_argument('--tokens', nargs='+', type=int, default=[4096])
+    p.add_argument('--dtype', nargs='+', choices=['fp8', 'bf16'], default=['fp8'])
+    p.add_argument('--routing', nargs='+', default=['uniform', 'mixed'])
+    p.add_argument('--seeds', nargs='+', type=int, default=[0])
+    p.add_argument('--iters', type=int, default=20)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--num-sms', type=int, default=0)
+    p.add_argument('--out', default='ep_results')
+    args = p.parse_args(argv)
+
+    from .. import Buffer, ReferenceBuffer
+    from .summarize import summarize_dir
+    owns_group = not dist.is_initialized()
+    if owns_group:
+        rank = int(os.environ.get('RANK', '0'))
+        world = int(os.environ.get('WORLD_SIZE', '1'))
+        local = int(os.environ.get('LOCAL_RANK', '0'))
+        torch.cuda.set_device(local)
+        os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
+        os.environ.setdefault('MASTER_PORT', '29561')
+        dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    os.makedirs(args.out, exist_ok=True)
+    logs = {k: _Jsonl(os.path.join(args.out, f'{k}-rank{rank}.jsonl')) for k in ('manifest', 'correctness', 'timings')}
+    logs['manifest'].write(manifest(args))
+    max_tokens = max(args.tokens)
+    max_hidden = max(MODELS[m][0] for m in args.models)
+    buf = Buffer(dist.group.WORLD, num_nvl_bytes=Buffer.get_nvl_buffer_size_hint(max_tokens, max_hidden, world))
+    if args.num_sms:
+        Buffer.set_num_sms(args.num_sms)
+    ref = ReferenceBuffer(dist.group.WORLD)
+    failures = 0
+    for model in args.models:
+        for tokens in args.tokens:
+            for dtype in args.dtype:
+                for routing in args.routing:
+                    for seed in args.seeds:
+                        try:
+                            case, res = run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs)
+                            if rank == 0:
+                                line = ', '.join(f"{op} {sorted(r['rank_max_us'])[len(r['rank_max_us']) // 2]:.1f} us"
+                                                 for op, r in res.items())
+                                print(f'[ep_benchmark] {model} T={tokens} {dtype} {routing} seed {seed}: {line}', flush=True)
+                        except (AssertionError, ValueError) as e:
+                            failures += 1
+                            logs['correctness'].write({'kind': 'correctness', 'model': model, 'tokens_per_rank': tokens,
+                                                       'dispatch_dtype': dtype, 'routing': routing, 'seed': seed,
+                                                       'passed': False, 'error': str(e)})
+                            if rank == 0:
+                                print(f'[ep_benchmark] {model} {dtype} {routing} seed {seed}: FAILED: {e}', flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if rank == 0:
+        summarize_dir(args.out)
+    if owns_group:
+        dist.destroy_process_group()
+    return 1 if failures else 0
+
+
+if __name__ == '__main__':
+    sys.exit(main())

@@ -17,6 +17,7 @@ a caller can see:
   * the normal-mode region holds a fixed number of tokens per rank per call, derived from
     `num_nvl_bytes` (`Buffer.get_nvl_buffer_size_hint(num_max_tokens, hidden, num_ranks)`).
 """
+import functools
 import os
 from typing import Callable, List, Optional, Tuple, Union
 
@@ -32,6 +33,26 @@ topk_idx_t = torch.int64
 
 def _default_timeout() -> float:
     return float(os.environ.get('DEEPEP_B200_GPU_TIMEOUT_SECS', '100'))
+
+
+_NVTX = os.environ.get('DEEPEP_B200_NVTX', '0') == '1'
+
+
+def nvtx_range(name: str):
+    """Wrap an API method in an NVTX range named `name` when DEEPEP_B200_NVTX=1 (profiler timelines;
+    the reference wraps its API calls the same way, backend/tests/profile_capture.py:11-62)."""
+    def deco(fn):
+        @functools.wraps(fn)
+        def wrapper(*args, **kwargs):
+            if not _NVTX:
+                return fn(*args, **kwargs)
+            torch.cuda.nvtx.range_push(name)
+            try:
+                return fn(*args, **kwargs)
+            finally:
+                torch.cuda.nvtx.range_pop()
+        return wrapper
+    return deco
 
 
 class Config:
@@ -159,8 +180,23 @@ class Buffer:
         recorded only when the process runs with DEEPEP_B200_PROFILE=1 (diagnostics; adds events)."""
         return dict(self.runtime.get_profile())
 
+    @nvtx_range('ep.barrier')
     def barrier(self, use_comm_stream: bool = True, with_cpu_sync: bool = False) -> None:
         self.runtime.barrier(use_comm_stream, with_cpu_sync)
+
+    # ------------------------------------------------------------------ device trace ring
+    def enable_trace(self, capacity: int = 1 << 20) -> None:
+        """Start appending per-block kernel records (40 B each) to a device ring of `capacity`."""
+        self.runtime.enable_trace(capacity)
+
+    def disable_trace(self) -> None:
+        self.runtime.disable_trace()
+
+    def read_trace(self, reset: bool = True):
+        """(decoded records, appended count); see `deepep_slingshot_b200.utils.trace`."""
+        from ..utils.trace import decode
+        raw, appended = self.runtime.read_trace(reset)
+        return decode(raw), appended
 
     @staticmethod
     def _unpack_bias(bias):
@@ -183,6 +219,7 @@ class Buffer:
         return Config(Buffer.num_sms, 4, 256, 6, 128)
 
     # ------------------------------------------------------------------ normal mode
+    @nvtx_range('ep.get_dispatch_layout')
     def get_dispatch_layout(self, topk_idx: torch.Tensor, num_experts: int,
                             previous_event: Optional[EventOverlap] = None, async_finish: bool = False,
                             allocate_on_comm_stream: bool = False):
@@ -193,6 +230,7 @@ class Buffer:
         return num_tokens_per_rank, num_tokens_per_rdma_rank, num_tokens_per_expert, is_token_in_rank, \
             EventOverlap(event)
 
+    @nvtx_range('ep.dispatch')
     def dispatch(self, x: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]], handle: Optional[Tuple] = None,
                  num_tokens_per_rank: Optional[torch.Tensor] = None,
                  num_tokens_per_rdma_rank: Optional[torch.Tensor] = None,
@@ -240,6 +278,7 @@ class Buffer:
         return (recv_x, recv_scales) if recv_scales is not None else recv_x, recv_topk_idx, recv_topk_weights, \
             num_recv_tokens_per_expert_list, handle, EventOverlap(event)
 
+    @nvtx_range('ep.combine')
     def combine(self, x: torch.Tensor, handle: Tuple, topk_weights: Optional[torch.Tensor] = None,
                 bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None,
                 config: Optional[Config] = None, previous_event: Optional[EventOverlap] = None,
@@ -264,6 +303,7 @@ class Buffer:
     def clean_low_latency_buffer(self, num_max_dispatch_tokens_per_rank: int, hidden: int, num_experts: int) -> None:
         self.runtime.clean_low_latency_buffer(num_max_dispatch_tokens_per_rank, hidden, num_experts)
 
+    @nvtx_range('ep.low_latency_dispatch')
     def low_latency_dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, num_max_dispatch_tokens_per_rank: int,
                              num_experts: int, cumulative_local_expert_recv_stats: Optional[torch.Tensor] = None,
                              dispatch_wait_recv_cost_stats: Optional[torch.Tensor] = None, use_fp8: bool = True,
@@ -305,6 +345,7 @@ class Buffer:
                              cumulative_local_expert_recv_stats)
         return recv, recv_count, handle, EventOverlap(event, tensors_to_record if async_finish else None), hook
 
+    @nvtx_range('ep.low_latency_combine')
     def low_latency_combine(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor, handle: tuple,
                             use_logfmt: bool = False, zero_copy: bool = False, async_finish: bool = False,
                             return_recv_hook: bool = False, out: Optional[torch.Tensor] = None,

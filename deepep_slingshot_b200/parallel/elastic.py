@@ -18,7 +18,7 @@ from ..utils.event import EventOverlap
 from ..utils.envs import get_nvlink_gbs
 from ..utils.math import align
 from ..ops.permute import permute, unpermute
-from .buffer import Buffer
+from .buffer import Buffer, nvtx_range
 
 
 class EPHandle:
@@ -134,6 +134,7 @@ class ElasticBuffer:
     def get_theoretical_num_qps(self, num_sms: int) -> int:
         return min(num_sms, 8 + 1)
 
+    @nvtx_range('ep.elastic.dispatch')
     def dispatch(self, x: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]],
                  topk_idx: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
                  cumulative_local_expert_recv_stats: Optional[torch.Tensor] = None, num_experts: Optional[int] = None,
@@ -215,6 +216,7 @@ class ElasticBuffer:
         rows = int(handle.expert_offsets[-1].item())
         return perm.x[:rows], (perm.scales[:rows] if perm.scales is not None else None)
 
+    @nvtx_range('ep.elastic.combine')
     def combine(self, x: torch.Tensor, handle: EPHandle, topk_weights: Optional[torch.Tensor] = None,
                 bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None, num_sms: int = 0,
                 num_qps: int = 0, previous_event=None, previous_event_before_epilogue=None,
