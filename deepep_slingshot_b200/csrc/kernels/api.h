@@ -110,7 +110,7 @@ struct CombineArgs {
     void* out;                       // bf16 [N][H]
     float* out_topk_weights;         // [N][K] or null
     int push_blocks;                 // set by the launcher
-    int chunk;                       // rows dealt to push pairs in chunks of this size (0: contiguous)
+    int chunk;                       // push order: -1 wavefront over destinations, 0 contiguous, N chunks of N rows
     int stages;
     KernelStatus st;
 };

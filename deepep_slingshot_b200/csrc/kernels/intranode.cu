@@ -428,6 +428,26 @@ __device__ __forceinline__ int pair_row(int g, int P, int k, int chunk, int n) {
     if (chunk == 0) return g * ((n + P - 1) / P) + k;
     return ((k / chunk) * P + g) * chunk + (k % chunk);
 }
+// Combine push order with chunk == -1 ("wavefront"): at step k pair g serves destination
+// s = (k + g) % R, row (k / R) * P + g of that destination's segment (-1 past its end). Every pair
+// spreads its stores over all destinations (no incast), and all ranks walk each destination's tokens
+// in increasing order at the same pace, so a token's contributions from every source land close
+// together and the reducers (which take tokens in increasing order) follow the pushes instead of
+// waiting for the end of the push phase.
+__device__ __forceinline__ int wave_row(int g, int P, int k, const int* prefix, int R, int n) {
+    const int s = (k + g) % R;
+    const int i = (k / R) * P + g;
+    const int lo = min(prefix[s], n), hi = min(prefix[s + 1], n);
+    return i < hi - lo ? lo + i : -1;
+}
+__device__ __forceinline__ int wave_num_rows(int g, int P, const int* prefix, int R, int n) {
+    int rows = 0;
+    for (int s = 0; s < R; ++s) {
+        const int len = min(prefix[s + 1], n) - min(prefix[s], n);
+        if (len > g) rows += (len - g + P - 1) / P;
+    }
+    return rows;
+}
 __device__ __forceinline__ int pair_num_rows(int g, int P, int n, int chunk) {
     if (chunk == 0) {
         const int per = (n + P - 1) / P;
@@ -758,21 +778,27 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
         const bool producer = (warp & 1) == 0;
         const int num_recv = min(s_prefix[R], a.num_recv_max);
         const int g = blockIdx.x * kPairs + pair, P = a.push_blocks * kPairs;
-        const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
+        const bool wave = a.chunk < 0;
+        const int my_rows = wave ? wave_num_rows(g, P, s_prefix, R, num_recv) : pair_num_rows(g, P, num_recv, a.chunk);
+        // k walks the schedule, c counts this pair's rows (pipeline slot / phase / announce index)
+        auto row_at = [&](int k) { return wave ? wave_row(g, P, k, s_prefix, R, num_recv) : pair_row(g, P, k, a.chunk, num_recv); };
         const int S = p.S;
         const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
         if (producer) {
-            for (int k = 0; k < my_rows; ++k) {
+            for (int k = 0, c = 0; c < my_rows; ++k) {
+                const int j = row_at(k);
+                if (j < 0) continue;
                 if (lane == 0) {
-                    const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
+                    const int slot = c % S;
                     bool ok = true;
-                    if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
+                    if (c >= S) ok = mbar_wait(&p.empty[slot], ((c / S) - 1) & 1, a.st, kErrTimeoutTma);
                     if (ok) {
                         mbar_arrive_expect_tx(&p.full[slot], row_bytes);
                         tma_load_1d(p.slots + (size_t)slot * slot_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)j * row_bytes,
                                     row_bytes, &p.full[slot]);
                     }
                 }
+                ++c;
             }
         } else {
             // Slots recycle on read-completion (as in the pull). Arrivals are announced per batch of
@@ -785,8 +811,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
             for (int r = 0; r < kMaxRanks; ++r)
                 arrivals[r] = r < R ? reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[r]) + a.layout.arrival_off) : nullptr;
             int pend_t = -1, pend_d = 0;  // lane i holds the i-th row of the current announce batch
-            for (int k = 0; k < my_rows; ++k) {
-                const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
+            for (int kk = 0, k = 0; k < my_rows; ++kk) {
+                const int j = row_at(kk);
+                if (j < 0) continue;
+                const int slot = k % S;
                 const int d = find_source(s_prefix, R, j);
                 const int64_t drow = s_base[d] + (j - s_prefix[d]);
                 int good = 1;
@@ -825,6 +853,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
                     }
                 }
                 __syncwarp();
+                ++k;
             }
         }
     }

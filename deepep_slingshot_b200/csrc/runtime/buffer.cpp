@@ -226,6 +226,9 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     // Row dealing of the pull/push pipelines: chunks of N rows round-robin over pairs (0: contiguous).
     const char* chunk = std::getenv("DEEPEP_B200_ROW_CHUNK");
     row_chunk_ = chunk != nullptr ? std::max(0, std::atoi(chunk)) : 0;
+    // Combine push order: -1 = wavefront over destinations in token order (default), >= 0 as above.
+    const char* cchunk = std::getenv("DEEPEP_B200_COMBINE_ROW_CHUNK");
+    combine_row_chunk_ = cchunk != nullptr ? std::max(-1, std::atoi(cchunk)) : -1;
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
@@ -799,7 +802,7 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     ca.out = out.data_ptr();
     ca.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
     ca.stages = 0;
-    ca.chunk = row_chunk_;
+    ca.chunk = combine_row_chunk_;
     ca.st = st;
     prof_mark(stream, 4);
     launch_combine(ca, num_sms, stream);

@@ -155,6 +155,7 @@ class Buffer {
     void prof_mark(cudaStream_t stream, int point);
     bool profile_enabled_ = false;
     int row_chunk_ = 0;
+    int combine_row_chunk_ = -1;
     std::vector<std::pair<int, cudaEvent_t>> prof_events_;
 
     int rank_, num_ranks_, device_id_;
