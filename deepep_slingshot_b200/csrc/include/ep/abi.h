@@ -183,6 +183,7 @@ struct LLLayout {
     int64_t recv_src_meta_off;  // i32 [E_l][R*maxT] src_rank * topk + k
     int64_t combine_recv_off;   // bf16 [maxT][topk][hidden]
     int64_t combine_send_off;   // bf16 [E_l][R*maxT][hidden] zero-copy send buffer
+    int64_t combine_meta_off;   // u32 [maxT][topk][hidden/128] LogFMT group metadata (amax | amin << 16)
     int32_t max_tokens;
     int32_t hidden;
     int32_t num_experts;

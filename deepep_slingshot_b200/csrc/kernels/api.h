@@ -159,6 +159,7 @@ struct LLCombineArgs {
     int shrink;
     void* out;                       // bf16 [N][H]
     int64_t* wait_stats;             // [R] optional
+    int use_logfmt;                  // rows travel LogFMT-10 encoded where a 128-group qualifies
     KernelStatus st;
 };
 void launch_ll_combine(const LLCombineArgs& a, cudaStream_t stream);

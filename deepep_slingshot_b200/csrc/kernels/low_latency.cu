@@ -22,6 +22,7 @@
 #include <cuda_fp8.h>
 
 #include "../include/ep/device.cuh"
+#include "../include/ep/logfmt.cuh"
 #include "../include/ep/quant.cuh"
 #include "api.h"
 
@@ -38,6 +39,7 @@ struct LLHalf {
     __device__ int* src_info() const { return reinterpret_cast<int*>(base + l->recv_src_info_off); }
     __device__ int* src_meta() const { return reinterpret_cast<int*>(base + l->recv_src_meta_off); }
     __device__ __nv_bfloat16* combine_recv() const { return reinterpret_cast<__nv_bfloat16*>(base + l->combine_recv_off); }
+    __device__ uint32_t* combine_meta() const { return reinterpret_cast<uint32_t*>(base + l->combine_meta_off); }
 };
 
 __device__ __forceinline__ LLHalf half_of(const PeerTable& p, const LLLayout& l, int rank, int half) {
@@ -237,6 +239,7 @@ void launch_ll_dispatch(const LLDispatchArgs& a, cudaStream_t stream) {
 // =================================================================================================
 // LL combine
 // =================================================================================================
+template <bool kLogFMT>
 __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t s_bar[8];
@@ -272,19 +275,45 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 continue;
             }
             if (((masked >> (src))) & 1u) continue;
-            if (lane == 0) {
-                bulk_wait_read<0>();
-                mbar_arrive_expect_tx(&s_bar[warp], row_bytes);
-                tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + ((int64_t)le * slots + j) * row_bytes, row_bytes, &s_bar[warp]);
-                ok = mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma);
+            if constexpr (kLogFMT) {
+                // Every lane waits for the row (the whole warp reads it), encodes it in place, then
+                // lane 0 stores the compacted bytes; group metadata goes out with plain stores.
+                if (lane == 0) {
+                    bulk_wait_read<0>();
+                    mbar_arrive_expect_tx(&s_bar[warp], row_bytes);
+                    tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + ((int64_t)le * slots + j) * row_bytes, row_bytes,
+                                &s_bar[warp]);
+                }
+                __syncwarp();
+                ok = __all_sync(0xffffffffu, mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma) ? 1 : 0) != 0;
                 phase ^= 1u;
                 if (ok) {
                     LLHalf dh = half_of(a.peers, L, src, a.half);
-                    tma_store_1d(dh.combine_recv() + ((int64_t)t * K + k) * H, buf, row_bytes);
-                    bulk_commit();
+                    uint32_t* meta = dh.combine_meta() + ((int64_t)t * K + k) * (H / 128);
+                    const int n = logfmt_encode_row(buf, H, meta);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_1d(dh.combine_recv() + ((int64_t)t * K + k) * H, buf, n);
+                        bulk_commit();
+                    }
                 }
+            } else {
+                if (lane == 0) {
+                    bulk_wait_read<0>();
+                    mbar_arrive_expect_tx(&s_bar[warp], row_bytes);
+                    tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + ((int64_t)le * slots + j) * row_bytes, row_bytes,
+                                &s_bar[warp]);
+                    ok = mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma);
+                    phase ^= 1u;
+                    if (ok) {
+                        LLHalf dh = half_of(a.peers, L, src, a.half);
+                        tma_store_1d(dh.combine_recv() + ((int64_t)t * K + k) * H, buf, row_bytes);
+                        bulk_commit();
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
         if (lane == 0) {
             bulk_wait<0>();
@@ -350,6 +379,42 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
             }
             const __nv_bfloat16* trow = recv + (int64_t)t * K * H;
             const int h0 = warp * span, h1 = min(H, h0 + span);
+            if constexpr (kLogFMT) {
+                // Encoded groups before each group of slot ks[q]: one ballot per 32 groups.
+                const uint32_t* meta_t = mine.combine_meta() + (int64_t)t * K * (H / 128);
+                const int groups = H / 128;
+                uint32_t cmask[kMaxTopk][kLogFmtMaxGroupsPerLane];
+                for (int q = 0; q < n; ++q)
+#pragma unroll
+                    for (int i = 0; i < kLogFmtMaxGroupsPerLane; ++i) {
+                        const int gg = i * 32 + lane;
+                        const uint32_t m = gg < groups ? ld_volatile_u32(meta_t + (int64_t)ks[q] * groups + gg) : 0u;
+                        cmask[q][i] = __ballot_sync(0xffffffffu, (m & 0x8000u) != 0);
+                    }
+                for (int e0 = h0 + lane * 8; e0 < h1; e0 += 256) {
+                    const int g = e0 >> 7, p = e0 & 127;
+                    float acc[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+                    for (int q = 0; q < n; ++q) {
+                        int before = 0;
+#pragma unroll
+                        for (int i = 0; i < kLogFmtMaxGroupsPerLane; ++i) {
+                            const int lo = i * 32;
+                            if (g > lo) before += __popc(g - lo >= 32 ? cmask[q][i] : (cmask[q][i] & ((1u << (g - lo)) - 1u)));
+                        }
+                        const uint32_t m = ld_volatile_u32(meta_t + (int64_t)ks[q] * groups + g);
+                        logfmt_accumulate8(reinterpret_cast<const uint8_t*>(trow + (int64_t)ks[q] * H), g, p, before, m,
+                                           ws[q], acc);
+                    }
+                    int4 o;
+                    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+                    *reinterpret_cast<int4*>(static_cast<__nv_bfloat16*>(a.out) + (int64_t)t * H + e0) = o;
+                }
+                continue;
+            }
             for (int e0 = h0 + lane * 8; e0 < h1; e0 += 256) {
                 int4 v[kMaxTopk];
 #pragma unroll
@@ -393,8 +458,13 @@ void launch_ll_combine(const LLCombineArgs& a, cudaStream_t stream) {
         if (blocks > num_sms) blocks = num_sms;
     }
     if (blocks < 1) blocks = 1;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(ll_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    ll_combine_kernel<<<blocks, W * 32, smem, stream>>>(a);
+    if (a.use_logfmt) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(ll_combine_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ll_combine_kernel<true><<<blocks, W * 32, smem, stream>>>(a);
+    } else {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(ll_combine_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ll_combine_kernel<false><<<blocks, W * 32, smem, stream>>>(a);
+    }
 }
 
 // =================================================================================================

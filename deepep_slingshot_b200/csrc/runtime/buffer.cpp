@@ -167,6 +167,8 @@ LLLayout compute_ll_layout(int64_t region_bytes, int max_tokens, int hidden, int
     off = align_up(off + (int64_t)max_tokens * kMaxTopk * hidden * 2, kAlign);
     l.combine_send_off = off;
     off = align_up(off + E_l * slots * hidden * 2, kAlign);
+    l.combine_meta_off = off;
+    off = align_up(off + (int64_t)max_tokens * kMaxTopk * nb * 4, kAlign);
     l.half_bytes = align_up(off, 4096);
     (void)region_bytes;
     return l;
@@ -932,7 +934,7 @@ std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::functio
     int num_experts, bool use_logfmt, bool zero_copy, bool async, bool return_recv_hook, const std::optional<torch::Tensor>& out) {
     check_error();
     TORCH_CHECK(available_ && ll_base_ != nullptr, "low-latency mode needs num_rdma_bytes > 0");
-    TORCH_CHECK(!use_logfmt, "LogFMT combine is not supported by this build");
+    TORCH_CHECK(!(use_logfmt && zero_copy), "LogFMT combine encodes from the caller's tensor: zero_copy is not allowed");
     const int R = num_ranks_, maxT = num_max_dispatch_tokens_per_rank;
     TORCH_CHECK(x.dim() == 3 && x.scalar_type() == torch::kBFloat16 && x.is_contiguous());
     const int H = (int)x.size(2), N = (int)topk_idx.size(0), K = (int)topk_idx.size(1);
@@ -971,6 +973,8 @@ std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::functio
     a.wait_stats = combine_wait_recv_cost_stats.has_value() ? combine_wait_recv_cost_stats->data_ptr<int64_t>() : nullptr;
     a.st = status();
     a.phases = return_recv_hook ? 1 : 3;
+    a.use_logfmt = use_logfmt ? 1 : 0;
+    TORCH_CHECK(!use_logfmt || H <= 128 * 128, "LogFMT combine supports hidden <= 16384");
     launch_ll_combine(a, launch_stream.stream());
     EP_CUDA_CHECK(cudaGetLastError());
 

@@ -259,6 +259,9 @@ class ReferenceBuffer:
         src_info, layout_range, maxT, H, num_experts, recv_count, _, src_meta = handle
         K = topk_idx.shape[1]
         epr = num_experts // R
+        if use_logfmt:
+            from ..utils.math import logfmt10_roundtrip
+            x = logfmt10_roundtrip(x)
         parts, counts = [], []
         for r in range(R):
             rows_r = []
@@ -268,13 +271,13 @@ class ReferenceBuffer:
                 t = src_info[e, sel].to(torch.int64)
                 k = (src_meta[e, sel] % K).to(torch.int64)
                 meta = torch.stack([t, k], dim=1)
-                rows_r.append(torch.cat([_as_bytes(x[e, sel].to(torch.bfloat16)), _as_bytes(meta)], dim=1))
-            part = torch.cat(rows_r, dim=0) if rows_r else torch.empty((0, 2 * H + 16), dtype=torch.uint8, device=x.device)
+                rows_r.append(torch.cat([_as_bytes(x[e, sel].float()), _as_bytes(meta)], dim=1))
+            part = torch.cat(rows_r, dim=0) if rows_r else torch.empty((0, 4 * H + 16), dtype=torch.uint8, device=x.device)
             parts.append(part)
             counts.append(part.shape[0])
         rows, _ = self._exchange(torch.cat(parts, dim=0), counts)
-        vals = _from_bytes(rows[:, :2 * H], torch.bfloat16, H).float()
-        meta = _from_bytes(rows[:, 2 * H:2 * H + 16], torch.int64, 2)
+        vals = _from_bytes(rows[:, :4 * H], torch.float32, H)
+        meta = _from_bytes(rows[:, 4 * H:4 * H + 16], torch.int64, 2)
         N = topk_idx.shape[0]
         w = topk_weights[meta[:, 0], meta[:, 1]].float().unsqueeze(1)
         acc = torch.zeros((N, H), dtype=torch.float32, device=x.device)

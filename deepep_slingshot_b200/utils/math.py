@@ -70,6 +70,30 @@ def per_token_cast_back(x_fp8: torch.Tensor, x_scales: torch.Tensor) -> torch.Te
     return (x_fp32 * x_scales).view(m, aligned_n).to(torch.bfloat16)[:, :n].contiguous()
 
 
+def logfmt10_roundtrip(x: torch.Tensor) -> torch.Tensor:
+    """What a LogFMT-10 receiver reconstructs from bf16 rows `x [..., hidden]` (fp32 result): per
+    128-group, groups with max|x| < 1 and some spread are coded as sign + 9-bit log2 level between
+    log2(min|x|) (clamped to log2(max|x|) - 32) and log2(max|x|), rounded to the nearer level in linear
+    space; other groups pass through unchanged. Oracle of the sm_100a LL combine with `use_logfmt`."""
+    shape = x.shape
+    g = x.to(torch.bfloat16).float().reshape(-1, shape[-1] // 128, 128)
+    a = g.abs()
+    amax = a.amax(-1, keepdim=True)
+    amin = a.amin(-1, keepdim=True)
+    log_amax = torch.log2(amax)
+    log_amin = torch.maximum(torch.log2(amin), log_amax - 32)
+    cast = (log_amax < 0) & (log_amin < log_amax)
+    step = (log_amax - log_amin) / 510
+    safe_step = torch.where(cast, step, torch.ones_like(step))
+    up = torch.log2((1 + torch.exp2(safe_step)) * 0.5) / safe_step
+    t = (torch.log2(a) - log_amin) / safe_step
+    code = torch.floor(t + 2 - up).clamp(0, 511)
+    code = torch.where(a == 0, torch.zeros_like(code), code)
+    dec = torch.where(code == 0, torch.zeros_like(a), torch.exp2((code - 1) * safe_step + log_amin)) * torch.sign(g)
+    out = torch.where(cast, dec, g)
+    return out.reshape(shape)
+
+
 def pack_ue8m0(scales: torch.Tensor) -> torch.Tensor:
     """fp32 power-of-two scales [..., nb] -> packed UE8M0 int32 [..., nb/4] (exponent bytes, little endian)."""
     assert scales.shape[-1] % 4 == 0

@@ -82,3 +82,46 @@ def test_low_latency(world, use_fp8, hook):
 @pytest.mark.parametrize('world', _worlds()[-1:])
 def test_low_latency_deepseek_shape(world):
     run_ranks(_ll_body, world, 'nccl', args=(128, 7168, 256, 8, True, True))
+
+
+def _ll_logfmt_body(rank, world, N, H, E, K, hook):
+    """LL combine with `use_logfmt=True`: expert outputs below 1 travel LogFMT-10 encoded, larger
+    ones as raw bf16 groups; compared with the oracle that applies the same number format."""
+    from deepep_slingshot_b200 import Buffer, ReferenceBuffer
+    from deepep_slingshot_b200.utils.math import calc_diff
+    group = dist.group.WORLD
+    buf = Buffer(group, num_rdma_bytes=Buffer.get_low_latency_rdma_size_hint(N, H, world, E), low_latency_mode=True,
+                 num_gpu_timeout_secs=20)
+    ref = ReferenceBuffer(group)
+    E_l = E // world
+    for it in range(3):
+        x, idx, w = _make_inputs(rank, N - rank, H, E, K, seed=10 + it, kind='uniform')
+        recv, cnt, h, _, hk = buf.low_latency_dispatch(x, idx, N, E, use_fp8=False, return_recv_hook=hook)
+        if hook:
+            hk()
+        erecv, ecnt, eh, _, _ = ref.low_latency_dispatch(x, idx, N, E, use_fp8=False)
+        # most experts produce small outputs (encoded); expert 0 produces large ones (raw groups);
+        # the first 64 columns are zeroed on expert 1 (zeros inside encoded groups)
+        scale = torch.full((E_l, 1, 1), 0.03, device='cuda')
+        scale[0] = 2.0
+        xs = (recv.float() * scale).to(torch.bfloat16)
+        exs = (erecv.float() * scale).to(torch.bfloat16)
+        if E_l > 1:
+            xs[1, :, :64] = 0
+            exs[1, :, :64] = 0
+        out, _, chk = buf.low_latency_combine(xs, idx, w, h, use_logfmt=True, return_recv_hook=hook)
+        if hook:
+            chk()
+        eout, _, _ = ref.low_latency_combine(exs, idx, w, eh, use_logfmt=True)
+        plain, _, _ = ref.low_latency_combine(exs, idx, w, eh)
+        torch.cuda.synchronize()
+        assert calc_diff(out.float(), eout.float()) < 1e-5, calc_diff(out.float(), eout.float())
+        assert torch.allclose(out.float(), eout.float(), atol=2e-3, rtol=3e-2)
+        assert calc_diff(out.float(), plain.float()) < 1e-4  # the format itself stays close to bf16
+    buf.check_error()
+
+
+@pytest.mark.parametrize('world', _worlds())
+@pytest.mark.parametrize('hook', [True, False])
+def test_low_latency_logfmt(world, hook):
+    run_ranks(_ll_logfmt_body, world, 'nccl', args=(64, 2048, 32, 8, hook))
