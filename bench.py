@@ -300,6 +300,7 @@ def main():
     moe = {}
     if not args.no_moe and args.impl == 'ours':
         from deepep_slingshot_b200.models import MoEFFN
+        from deepep_slingshot_b200.models import moe as _moe_mod
         inter = 2048
         gm = torch.Generator().manual_seed(4321)
         layer = MoEFFN(buf, H, inter, E, K, config=cfg, init_std=0.02, generator=gm)
@@ -340,7 +341,7 @@ def main():
                'moe_roofline_fraction': max(t_compute, t_comm) / (ms_moe * 1e-3),
                'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
                               'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs',
-                              'backward': 'bf16 per-expert torch matmuls (stand-in)',
+                              'backward': ('bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled'] else 'bf16 per-expert torch matmuls (stand-in)'),
                               'roofline': 'max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes at 770 GB/s)'}}
         del layer
         torch.cuda.empty_cache()

@@ -121,13 +121,13 @@ __device__ __forceinline__ void logfmt_accumulate8(const uint8_t* row, int g, in
     const int off = 160 * cast_before + 256 * (g - cast_before);
     if (meta & 0x8000u) {
         const LogFmtGroup prm = logfmt_params(bf16_bits_to_float(meta & 0x7fffu), bf16_bits_to_float(meta >> 16));
+        // 10 bytes = two encoder lanes x 40 bits (four codes each); each half fits a 64-bit word.
         const uint16_t* s = reinterpret_cast<const uint16_t*>(row + off + (p / 8) * 10);
-        uint64_t bits = 0;
-#pragma unroll
-        for (int i = 0; i < 5; ++i) bits |= (uint64_t)s[i] << (16 * i);
+        const uint64_t half0 = (uint64_t)s[0] | ((uint64_t)s[1] << 16) | ((uint64_t)(s[2] & 0xffu) << 32);
+        const uint64_t half1 = (uint64_t)(s[2] >> 8) | ((uint64_t)s[3] << 8) | ((uint64_t)s[4] << 24);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t code = (uint32_t)(bits >> (10 * i)) & 0x3ffu;
+            const uint32_t code = (uint32_t)((i < 4 ? half0 : half1) >> (10 * (i & 3))) & 0x3ffu;
             const uint32_t mag = code & 511u;
             float val = mag == 0 ? 0.f : exp2f((float)(mag - 1) * prm.step + prm.log_amin);
             if (code >> 9) val = -val;

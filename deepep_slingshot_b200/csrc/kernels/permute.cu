@@ -198,6 +198,20 @@ __global__ void __launch_bounds__(512) permute_copy_kernel(PermuteArgs a) {
     }
 }
 
+// One CTA per expert: zero rows [offset[e] + count[e], offset[e + 1]) of x_perm (and their scales).
+__global__ void __launch_bounds__(256) permute_zero_padding_kernel(PermuteArgs a) {
+    const int e = blockIdx.x;
+    const int r0 = a.expert_offsets[e] + a.expert_counts[e], r1 = a.expert_offsets[e + 1];
+    const int row_bytes = a.hidden * a.x_elem_bytes;
+    const int nb = a.hidden / 128;
+    for (int r = r0; r < r1; ++r) {
+        int4* d = reinterpret_cast<int4*>(static_cast<uint8_t*>(a.x_perm) + (int64_t)r * row_bytes);
+        for (int o = threadIdx.x; o < row_bytes / 16; o += blockDim.x) d[o] = make_int4(0, 0, 0, 0);
+        if (a.scales_perm != nullptr)
+            for (int b = threadIdx.x; b < nb; b += blockDim.x) a.scales_perm[(int64_t)r * nb + b] = 0.f;
+    }
+}
+
 void launch_permute(const PermuteArgs& a, cudaStream_t stream) {
     const int num_chunks = (a.num_tokens + 31) / 32;
     cudaMemsetAsync(a.counts, 0, sizeof(int) * (size_t)num_chunks * a.num_experts, stream);
@@ -215,6 +229,8 @@ void launch_permute(const PermuteArgs& a, cudaStream_t stream) {
         const int copy_blocks = (int)std::min<int64_t>((items + 15) / 16, 148 * 4);
         permute_copy_kernel<<<copy_blocks, 512, 0, stream>>>(a);
     }
+    if (a.zero_padding && a.alignment > 1 && a.expert_counts != nullptr)
+        permute_zero_padding_kernel<<<a.num_experts, 256, 0, stream>>>(a);
 }
 
 // out[t] = sum_k w[t][k] * y[row_map[t][k]] (fp32 accumulation in k order, bf16 out).

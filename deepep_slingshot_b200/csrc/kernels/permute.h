@@ -21,6 +21,7 @@ struct PermuteArgs {
     void* x_perm;                // [rows][H] out
     float* scales_perm;          // [rows][H/128] out (when x_scales)
     float* probs_perm;           // [rows] out (when probs)
+    int zero_padding;            // zero the alignment padding rows of x_perm / scales_perm (grouped GEMMs over whole groups)
 };
 
 void launch_permute(const PermuteArgs& a, cudaStream_t stream);

@@ -108,4 +108,64 @@ void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_
                                                                 static_cast<__nv_bfloat16*>(out_bf16));
 }
 
+// 128x128 block FP8 quantization of expert weights [E][n][k] (bf16): one CTA per block, each thread
+// owns 8 rows x 8 columns (eight 16-byte loads in flight). Numerics of the torch definition used as
+// the oracle: amax clamped at 1e-4, scale = amax / 448, q = saturate(v / scale) (true division,
+// round-to-nearest-even into e4m3).
+__global__ void __launch_bounds__(256) quantize_weights_fp8_kernel(const __nv_bfloat16* __restrict__ w, int n, int k,
+                                                                    uint8_t* __restrict__ q, float* __restrict__ scales) {
+    __shared__ float s_red[8];
+    const int kb = k / 128, nb = n / 128;
+    const int64_t blk = blockIdx.x;
+    const int e = (int)(blk / ((int64_t)nb * kb));
+    const int rem = (int)(blk % ((int64_t)nb * kb));
+    const int bn = rem / kb, bk = rem % kb;
+    const int tid = threadIdx.x;
+    const int c = (tid & 15) * 8;
+    const int r0 = tid >> 4;  // rows r0, r0 + 16, ..., r0 + 112
+    const int64_t base = ((int64_t)e * n + (int64_t)bn * 128) * k + (int64_t)bk * 128 + c;
+    int4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = ld_nc_v4(reinterpret_cast<const int4*>(w + base + (int64_t)(r0 + 16 * i) * k));
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h2[j]);
+            amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+    }
+    amax = warp_reduce_max(amax);
+    if (lane_id() == 0) s_red[warp_id()] = amax;
+    __syncthreads();
+    amax = s_red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) amax = fmaxf(amax, s_red[i]);
+    amax = fmaxf(amax, 1e-4f);
+    const float scale = amax / 448.0f;
+    if (tid == 0) scales[blk] = scale;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+        uint32_t packed[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float2 a = __bfloat1622float2(h2[2 * j]), b = __bfloat1622float2(h2[2 * j + 1]);
+            const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a.x / scale, a.y / scale), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(b.x / scale, b.y / scale), __NV_SATFINITE, __NV_E4M3);
+            packed[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+        }
+        *reinterpret_cast<uint2*>(q + base + (int64_t)(r0 + 16 * i) * k) = make_uint2(packed[0], packed[1]);
+    }
+}
+
+void launch_quantize_weights_fp8(const void* w, int num_experts, int n, int k, void* q, float* scales, cudaStream_t stream) {
+    const int64_t blocks = (int64_t)num_experts * (n / 128) * (k / 128);
+    if (blocks == 0) return;
+    quantize_weights_fp8_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(w), n, k,
+                                                                       static_cast<uint8_t*>(q), scales);
+}
+
 }  // namespace ep

@@ -103,6 +103,18 @@ torch::Tensor per_token_cast_back(const torch::Tensor& x, const torch::Tensor& s
 }
 
 // a = silu(h[:, :I]) * h[:, I:] (bf16) and its 1x128 FP8 quantization.
+// Expert weights [E, n, k] bf16 -> (fp8 e4m3 [E, n, k], fp32 128x128 block scales [E, n/128, k/128]).
+std::tuple<torch::Tensor, torch::Tensor> quantize_weights_fp8(const torch::Tensor& w) {
+    TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.scalar_type() == torch::kBFloat16 && w.is_contiguous(),
+                "quantize_weights_fp8: contiguous [E, n, k] bf16 CUDA tensor");
+    const int E = (int)w.size(0), n = (int)w.size(1), k = (int)w.size(2);
+    TORCH_CHECK(n % 128 == 0 && k % 128 == 0, "n and k must be multiples of 128");
+    auto q = torch::empty({E, n, k}, w.options().dtype(torch::kFloat8_e4m3fn));
+    auto s = torch::empty({E, n / 128, k / 128}, w.options().dtype(torch::kFloat32));
+    launch_quantize_weights_fp8(w.data_ptr(), E, n, k, q.data_ptr(), s.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+    return {q, s};
+}
+
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> swiglu_quant(const torch::Tensor& h, bool round_scale) {
     TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.is_contiguous() && h.scalar_type() == torch::kBFloat16);
     const int rows = (int)h.size(0), inter = (int)h.size(1) / 2;
@@ -119,7 +131,7 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> swiglu_quant(const torch
 // (`num_out_rows`, default N*K + E*(alignment-1)); rows past expert_offsets[E] are unused.
 std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor>
 permute(const torch::Tensor& x, const std::optional<torch::Tensor>& x_scales, const torch::Tensor& topk_idx,
-        const std::optional<torch::Tensor>& probs, int num_experts, int alignment, int64_t num_out_rows) {
+        const std::optional<torch::Tensor>& probs, int num_experts, int alignment, int64_t num_out_rows, bool zero_padding) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous());
     TORCH_CHECK(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat8_e4m3fn);
     TORCH_CHECK(topk_idx.scalar_type() == torch::kInt64 && topk_idx.is_contiguous() && topk_idx.size(0) == x.size(0));
@@ -163,6 +175,7 @@ permute(const torch::Tensor& x, const std::optional<torch::Tensor>& x_scales, co
     a.expert_counts = ecounts.data_ptr<int>();
     a.row_map = row_map.data_ptr<int>();
     a.x_perm = x_perm.data_ptr();
+    a.zero_padding = zero_padding ? 1 : 0;
     launch_permute(a, at::cuda::getCurrentCUDAStream());
     return {x_perm, sp, pp, row_map, offsets, ecounts};
 }
@@ -184,9 +197,11 @@ torch::Tensor unpermute(const torch::Tensor& y, const torch::Tensor& row_map, co
 
 void register_ops(pybind11::module_& m) {
     m.def("permute", &permute, pybind11::arg("x"), pybind11::arg("x_scales"), pybind11::arg("topk_idx"), pybind11::arg("probs"),
-          pybind11::arg("num_experts"), pybind11::arg("alignment") = 1, pybind11::arg("num_out_rows") = 0);
+          pybind11::arg("num_experts"), pybind11::arg("alignment") = 1, pybind11::arg("num_out_rows") = 0,
+          pybind11::arg("zero_padding") = false);
     m.def("unpermute", &unpermute);
     m.def("swiglu_quant", &swiglu_quant, pybind11::arg("h"), pybind11::arg("round_scale") = false);
+    m.def("quantize_weights_fp8", &quantize_weights_fp8, pybind11::arg("w"));
     m.def("grouped_gemm_fp8", &grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"), pybind11::arg("b"), pybind11::arg("sb"),
           pybind11::arg("offsets"), pybind11::arg("counts") = pybind11::none(), pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 10.0);

@@ -6,12 +6,14 @@ Forward per rank (every step on hand-written sm_100a kernels):
   grouped FP8 GEMM down -> top-k weighted unpermute -> combine (sum over ranks).
 Backward: combine^T = cached dispatch of the output gradient; dispatch^T = combine; the expert
 GEMM gradients run in bf16 (straight-through through the FP8 quantization). In this version the
-backward grouped GEMMs are per-expert torch matmuls (cuBLAS), a stand-in for tcgen05 kernels.
+backward GEMMs are torch's grouped bf16 GEMM over the aligned expert groups (a library stand-in for
+tcgen05 kernels; per-expert matmuls when the grouped GEMM is unavailable or DEEPEP_B200_MOE_BWD=loop).
 
 The reference library has no model layer (its expert compute is SGLang + DeepGEMM,
 backend/tests/sglang_dispatcher_smoke.py:107-124); this is the flagship workload of the benchmark
 config "full MoE layer forward+backward".
 """
+import os
 from typing import Optional
 
 import torch
@@ -26,6 +28,44 @@ def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
     off = offsets.tolist()
     cnt = counts.tolist()
     return [(off[e], off[e] + cnt[e]) for e in range(len(cnt))]
+
+
+_GROUPED_BWD = {'enabled': os.environ.get('DEEPEP_B200_MOE_BWD', 'grouped') == 'grouped'}
+
+
+def _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx) -> bool:
+    """Expert GEMM gradients as four grouped bf16 GEMMs over whole 128-aligned groups (torch's
+    grouped GEMM: a library stand-in for tcgen05 grouped kernels). Padding rows are masked to zero
+    so they contribute nothing. Returns False (and the caller loops over experts) when the grouped
+    GEMM is unavailable in this torch build."""
+    if not _GROUPED_BWD['enabled'] or not hasattr(torch, '_grouped_mm'):
+        return False
+    R = int(offsets[-1].item())
+    offs = offsets[1:].to(torch.int32).contiguous()
+    live = torch.zeros((R, 1), dtype=torch.bool, device=g_y.device)
+    live[rows[rows < R]] = True
+    zero = torch.zeros((), dtype=torch.bfloat16, device=g_y.device)
+    try:
+        gy = g_y[:R]
+        aa = torch.where(live, a[:R], zero)
+        hh = torch.where(live, h[:R], zero).float()
+        xx = torch.where(live, xf[:R], zero)
+        g_a = torch._grouped_mm(gy, w2, offs=offs).float()                         # [R, I]
+        g_w2 = torch._grouped_mm(gy.t(), aa, offs=offs)                            # [E, H, I]
+        gate, up = hh[:, :inter], hh[:, inter:]
+        s = torch.sigmoid(gate)
+        g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
+        g_xp[:R] = torch._grouped_mm(g_h, w1, offs=offs)                           # [R, H]
+        g_w1 = torch._grouped_mm(g_h.t(), xx, offs=offs)                           # [E, 2I, H]
+    except (RuntimeError, NotImplementedError):
+        _GROUPED_BWD['enabled'] = False
+        return False
+    empty = counts == 0
+    if bool(empty.any()):
+        g_w1[empty] = 0
+        g_w2[empty] = 0
+    ctx.g_w1, ctx.g_w2 = g_w1.contiguous(), g_w2.contiguous()
+    return True
 
 
 class _MoEFunction(torch.autograd.Function):
@@ -66,21 +106,25 @@ class _MoEFunction(torch.autograd.Function):
         g_rw[valid] = (g_tok[t_of].float() * y[rows].float()).sum(-1)
         xf = (xp.float().view(xp.shape[0], -1, 128) * xs.unsqueeze(-1)).view(xp.shape).to(torch.bfloat16)
         g_xp = torch.zeros_like(xf)
-        g_w1 = torch.zeros_like(w1)
-        g_w2 = torch.zeros_like(w2)
-        gate, up = h[:, :inter].float(), h[:, inter:].float()
-        sig = torch.sigmoid(gate)
-        for e, (r0, r1) in enumerate(_expert_rows(offsets, counts)):
-            if r1 <= r0:
-                continue
-            gy = g_y[r0:r1]
-            g_a = gy @ w2[e]                                   # [m, H] x [H, I]
-            g_w2[e] = gy.t() @ a[r0:r1]                        # [H, m] x [m, I]
-            s, gt, u = sig[r0:r1], gate[r0:r1], up[r0:r1]
-            gaf = g_a.float()
-            g_h = torch.cat([gaf * u * s * (1 + gt * (1 - s)), gaf * gt * s], dim=1).to(torch.bfloat16)
-            g_xp[r0:r1] = g_h @ w1[e]                          # [m, 2I] x [2I, H]
-            g_w1[e] = g_h.t() @ xf[r0:r1]                      # [2I, m] x [m, H]
+        if not _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx):
+            gate, up = h[:, :inter].float(), h[:, inter:].float()
+            sig = torch.sigmoid(gate)
+            g_w1 = torch.zeros_like(w1)
+            g_w2 = torch.zeros_like(w2)
+            for e, (r0, r1) in enumerate(_expert_rows(offsets, counts)):
+                if r1 <= r0:
+                    continue
+                gy = g_y[r0:r1]
+                g_a = gy @ w2[e]                                   # [m, H] x [H, I]
+                g_w2[e] = gy.t() @ a[r0:r1]                        # [H, m] x [m, I]
+                s, gt, u = sig[r0:r1], gate[r0:r1], up[r0:r1]
+                gaf = g_a.float()
+                g_h = torch.cat([gaf * u * s * (1 + gt * (1 - s)), gaf * gt * s], dim=1).to(torch.bfloat16)
+                g_xp[r0:r1] = g_h @ w1[e]                          # [m, 2I] x [2I, H]
+                g_w1[e] = g_h.t() @ xf[r0:r1]                      # [2I, m] x [m, H]
+        else:
+            g_w1, g_w2 = ctx.g_w1, ctx.g_w2
+            del ctx.g_w1, ctx.g_w2
         # permute^T: sum the k copies of each received token; dispatch^T = combine (sum over ranks)
         g_recv = unpermute(g_xp, row_map, None)
         g_x, g_topk_w, _ = buffer.combine(g_recv, ctx.handle, topk_weights=g_rw, config=config)
@@ -116,13 +160,13 @@ class MoEFFN(torch.nn.Module):
 def moe_reference(x, topk_idx, topk_weights, w1_all, w2_all):
     """Single-process fp32 oracle with the layer's quantization points (FP8 x, FP8 weights, bf16 h,
     FP8 a, bf16 y); w*_all hold every expert of the group: [E, 2I, H] and [E, H, I]."""
-    from ..ops.gemm import dequant_blocks
+    from ..ops.gemm import dequant_blocks, quantize_weights_fp8_reference
     from ..utils.math import per_token_cast_back, per_token_cast_to_fp8
     inter = w1_all.shape[1] // 2
     xq, xs = per_token_cast_to_fp8(x)
     xf = per_token_cast_back(xq, xs).float()
-    w1q, w1s = quantize_weights_fp8(w1_all)
-    w2q, w2s = quantize_weights_fp8(w2_all)
+    w1q, w1s = quantize_weights_fp8_reference(w1_all)
+    w2q, w2s = quantize_weights_fp8_reference(w2_all)
     w1f, w2f = dequant_blocks(w1q, w1s), dequant_blocks(w2q, w2s)
     out = torch.zeros_like(x, dtype=torch.float32)
     for k in range(topk_idx.shape[1]):

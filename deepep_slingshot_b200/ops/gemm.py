@@ -34,7 +34,16 @@ def dequant_blocks(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
 
 
 def quantize_weights_fp8(w: torch.Tensor):
-    """bf16/fp32 [E, n, k] -> (fp8 [E, n, k], fp32 128x128 block scales [E, n/128, k/128])."""
+    """bf16/fp32 [E, n, k] -> (fp8 [E, n, k], fp32 128x128 block scales [E, n/128, k/128]).
+    Contiguous bf16 CUDA weights go through the sm_100a block-quantization kernel (one HBM pass);
+    other inputs use `quantize_weights_fp8_reference` (the same numerics in torch)."""
+    if w.is_cuda and w.dtype == torch.bfloat16 and w.is_contiguous() and w.dim() == 3:
+        return require_ext().quantize_weights_fp8(w)
+    return quantize_weights_fp8_reference(w)
+
+
+def quantize_weights_fp8_reference(w: torch.Tensor):
+    """Torch definition of the 128x128 block weight quantization (oracle of the kernel)."""
     E, n, k = w.shape
     v = w.float().view(E, n // 128, 128, k // 128, 128)
     amax = v.abs().amax(dim=(2, 4)).clamp(min=1e-4)

@@ -23,8 +23,10 @@ class Permuted(NamedTuple):
 
 def permute(x: torch.Tensor, topk_idx: torch.Tensor, num_experts: int, alignment: int = 1,
             probs: Optional[torch.Tensor] = None, x_scales: Optional[torch.Tensor] = None,
-            num_out_rows: int = 0) -> Permuted:
-    out = require_ext().permute(x, x_scales, topk_idx, probs, num_experts, alignment, num_out_rows)
+            num_out_rows: int = 0, zero_padding: bool = False) -> Permuted:
+    """`zero_padding` zeroes each expert's alignment rows (and their scales), so grouped GEMMs may run
+    over whole aligned groups."""
+    out = require_ext().permute(x, x_scales, topk_idx, probs, num_experts, alignment, num_out_rows, zero_padding)
     return Permuted(*out)
 
 

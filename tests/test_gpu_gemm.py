@@ -32,3 +32,16 @@ def test_grouped_gemm_fp8(counts, n, k):
             got, exp = d[r0:r1].float(), ref[r0:r1]
             err = (got - exp).abs().max().item()
             assert err <= 2e-2 * exp.abs().max().item() + 1e-3, (e, err, exp.abs().max().item())
+
+
+@pytest.mark.parametrize('E,n,k', [(3, 256, 384), (2, 4096, 7168)])
+def test_quantize_weights_kernel_matches_torch(E, n, k):
+    from deepep_slingshot_b200.ops.gemm import quantize_weights_fp8, quantize_weights_fp8_reference
+    g = torch.Generator().manual_seed(E * n)
+    w = (torch.randn((E, n, k), generator=g) * torch.rand((E, 1, 1), generator=g) * 0.1).to(torch.bfloat16).cuda()
+    w[0, :128, :128] = 0  # an all-zero block takes the 1e-4 floor
+    q, s = quantize_weights_fp8(w)
+    rq, rs = quantize_weights_fp8_reference(w)
+    torch.cuda.synchronize()
+    assert torch.equal(s, rs)
+    assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8))

@@ -41,3 +41,18 @@ def test_permute_unpermute(N, H, E, K, align, fp8):
     out = unpermute(y, rm, w)
     ref = unpermute_reference(y, rm, w)
     assert torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=1e-2)
+
+
+def test_permute_zero_padding():
+    from deepep_slingshot_b200.ops.permute import permute
+    from deepep_slingshot_b200.utils.math import per_token_cast_to_fp8
+    g = torch.Generator().manual_seed(5)
+    N, H, E, K = 300, 512, 8, 2
+    x, xs = per_token_cast_to_fp8(torch.randn((N, H), generator=g).to(torch.bfloat16).cuda())
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)]).cuda()
+    p = permute(x, idx, E, alignment=128, x_scales=xs, zero_padding=True)
+    torch.cuda.synchronize()
+    off, cnt = p.expert_offsets.tolist(), p.expert_counts.tolist()
+    for e in range(E):
+        pad = slice(off[e] + cnt[e], off[e + 1])
+        assert (p.x[pad].view(torch.uint8) == 0).all() and (p.scales[pad] == 0).all()
