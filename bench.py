@@ -341,7 +341,9 @@ def main():
                'moe_roofline_fraction': max(t_compute, t_comm) / (ms_moe * 1e-3),
                'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
                               'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs',
-                              'backward': ('bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled'] else 'bf16 per-expert torch matmuls (stand-in)'),
+                              'backward': ('bf16 tcgen05 grouped GEMMs (dgrad M-grouped, wgrad K-grouped)' if _moe_mod._GROUPED_BWD['tcgen05']
+                                           else 'bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled']
+                                           else 'bf16 per-expert torch matmuls (stand-in)'),
                               'roofline': 'max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes at 770 GB/s)'}}
         del layer
         torch.cuda.empty_cache()

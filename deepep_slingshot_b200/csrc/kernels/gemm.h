@@ -27,4 +27,20 @@ struct GemmArgs {
 // Returns 0 on success, 1 bad shapes, 2 tensor-map encode failure, 3 launch failure.
 int launch_grouped_gemm_fp8(const GemmArgs& a, int num_sms, cudaStream_t stream);
 
+// bf16 grouped GEMMs with both operands K-major (gemm_bf16_sm100.cu).
+//   mode 0 (M-grouped): a [rows][k], b [E*n][k], d [rows][n]; rows of expert e at offsets[e], 128-aligned
+//   mode 1 (K-grouped): a [m][k], b [n][k], d [E][m][n]; expert e contracts k in [offsets[e], offsets[e+1])
+struct Bf16GemmArgs {
+    const void* a;
+    const void* b;
+    const int* offsets;       // [E+1] (mode 0: 128-aligned rows; mode 1: 64-aligned K offsets)
+    const int* expert_counts; // mode 0: [E] valid rows per expert (null: the aligned block)
+    void* d;
+    int mode;
+    int rows, m, n, k, num_experts;
+    int stages;
+    KernelStatus st;
+};
+int launch_grouped_gemm_bf16(const Bf16GemmArgs& a, int num_sms, cudaStream_t stream);
+
 }  // namespace ep

@@ -1,0 +1,332 @@
+// Grouped bf16 GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a: the backward
+// ("dgrad" and "wgrad") GEMMs of the MoE expert FFN. Both operands are K-major ("NT"):
+//
+//   mode 0, M-grouped: D[r, n] = sum_k A[r, k] * B[e*N + n, k] for rows r of expert e
+//                      (A: [rows, K], rows of expert e at [offsets[e], offsets[e] + counts[e]),
+//                       128-aligned; B: [E*N, K]; D: [rows, N])
+//   mode 1, K-grouped: D[e, m, n] = sum_{k in [offsets[e], offsets[e+1])} A[m, k] * B[n, k]
+//                      (A: [M, Ktot]; B: [N, Ktot]; D: [E, M, N]; an expert with no rows gets zeros)
+//
+// Structure (same roles as the FP8 kernel, without the per-block scale promotion):
+//  * one persistent CTA per SM walks output tiles of 128 x 128;
+//  * warp 0, one thread: TMA 2D loads (128-byte swizzle, no multicast) of 64-wide K blocks of the A
+//    and B tiles into an S-stage shared-memory ring;
+//  * warp 1, one thread: four `tcgen05.mma.cta_group::1.kind::f16` (bf16 x bf16 -> fp32, M=128,
+//    N=128, K=16) per K block, accumulating the whole K range of a tile in one TMEM buffer; two
+//    buffers alternate between tiles so the epilogue of one tile overlaps the MMAs of the next;
+//  * warps 2..9: `tcgen05.ld` the finished accumulator, release it, write bf16.
+// Every mbarrier wait is bounded (a status is reported, the kernel returns).
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "../include/ep/device.cuh"
+#include "gemm.h"
+
+namespace ep {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;          // BK = 64 bf16 = one 128-byte swizzle row
+constexpr int kStageBytes = (kBM + kBN) * kBK * 2;       // 32 KiB
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 2 * kBN;
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major tile, 128-byte swizzle, 8-row core groups 1024 B apart (same byte layout as the FP8 tiles).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3fffu);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: BF16 x BF16 -> F32 (D format bit 4, A/B formats = 1 at bits
+// 7 and 10), both K-major, M = 128, N = kBN.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld_32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%"
+        "22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+struct Tile {
+    int e, m0, n0;     // expert, first output row, first output column
+    int k0, kblocks;   // first K element and number of 64-wide K blocks
+    int64_t d_row0;    // first row of D (mode 1: e * M + m0)
+    int b_row0;        // first row of the B tile in its tensor map
+};
+
+// Tile t of the launch (n innermost). Mode 0 uses the per-expert m-tile prefix in shared memory.
+__device__ __forceinline__ bool tile_of(int t, const Bf16GemmArgs& a, const int* s_prefix, Tile& ti) {
+    const int n_tiles = a.n / kBN;
+    if (a.mode == 0) {
+        const int total = s_prefix[a.num_experts] * n_tiles;
+        if (t >= total) return false;
+        const int mt = t / n_tiles, nt = t % n_tiles;
+        int lo = 0, hi = a.num_experts - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_prefix[mid] <= mt) lo = mid;
+            else hi = mid - 1;
+        }
+        ti.e = lo;
+        ti.m0 = a.offsets[lo] + (mt - s_prefix[lo]) * kBM;
+        ti.n0 = nt * kBN;
+        ti.k0 = 0;
+        ti.kblocks = a.k / kBK;
+        ti.d_row0 = ti.m0;
+        ti.b_row0 = lo * a.n + ti.n0;
+        return true;
+    }
+    const int m_tiles = a.m / kBM;
+    const int per_e = m_tiles * n_tiles;
+    if (t >= a.num_experts * per_e) return false;
+    ti.e = t / per_e;
+    const int r = t % per_e;
+    ti.m0 = (r / n_tiles) * kBM;
+    ti.n0 = (r % n_tiles) * kBN;
+    ti.k0 = a.offsets[ti.e];
+    ti.kblocks = (a.offsets[ti.e + 1] - a.offsets[ti.e]) / kBK;
+    ti.d_row0 = (int64_t)ti.e * a.m + ti.m0;
+    ti.b_row0 = ti.n0;
+    return true;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                      const __grid_constant__ CUtensorMap map_b,
+                                                                      Bf16GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
+    __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_prefix[kMaxGemmExperts + 1];
+
+    const int warp = warp_id(), lane = lane_id();
+    const int S = a.stages;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_tfull[b], 1);
+            mbar_init(&s_tempty[b], kEpiWarps);
+        }
+        fence_mbar_init();
+        if (a.mode == 0) {
+            int acc = 0;
+            s_prefix[0] = 0;
+            for (int e = 0; e < a.num_experts; ++e) {
+                const int rows = a.expert_counts != nullptr ? a.expert_counts[e] : a.offsets[e + 1] - a.offsets[e];
+                acc += (rows + kBM - 1) / kBM;
+                s_prefix[e + 1] = acc;
+            }
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            Tile ti;
+            for (int t = blockIdx.x; ok && tile_of(t, a, s_prefix, ti); t += gridDim.x) {
+                for (int kb = 0; kb < ti.kblocks && ok; ++kb, ++g) {
+                    const int s = g % S;
+                    ok = mbar_wait(&s_empty[s], ((g / S) & 1) ^ 1, a.st, kErrTimeoutTma);
+                    if (!ok) break;
+                    uint8_t* sa_tile = smem + (size_t)s * kStageBytes;
+                    uint8_t* sb_tile = sa_tile + kBM * kBK * 2;
+                    mbar_arrive_expect_tx(&s_full[s], kStageBytes);
+                    tma_load_2d(sa_tile, &map_a, ti.k0 + kb * kBK, ti.m0, &s_full[s]);
+                    tma_load_2d(sb_tile, &map_b, ti.k0 + kb * kBK, ti.b_row0, &s_full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN);
+            uint32_t g = 0, j = 0;  // g: K-block stages consumed, j: non-empty tiles (TMEM buffer index)
+            bool ok = true;
+            Tile ti;
+            for (int t = blockIdx.x; ok && tile_of(t, a, s_prefix, ti); t += gridDim.x) {
+                if (ti.kblocks == 0) continue;
+                const int b = j & 1;
+                ok = mbar_wait(&s_tempty[b], ((j >> 1) & 1) ^ 1, a.st, kErrTimeoutTma);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(b * kBN);
+                for (int kb = 0; kb < ti.kblocks && ok; ++kb, ++g) {
+                    const int s = g % S;
+                    ok = mbar_wait(&s_full[s], (g / S) & 1, a.st, kErrTimeoutTma);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t sa_addr = smem_u32(smem + (size_t)s * kStageBytes);
+                    const uint32_t sb_addr = sa_addr + kBM * kBK * 2;
+                    const uint64_t da = smem_desc_sw128(sa_addr), db = smem_desc_sw128(sb_addr);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)  // K = 16 bf16 = 32 bytes per instruction: +2 in 16-byte units
+                        mma_bf16(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(&s_empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&s_tfull[b]);
+                ++j;
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int ew = warp - 2;
+        const int q = warp & 3;   // TMEM lane quarter of this warp
+        const int h = ew >> 2;    // column half [64h, 64h + 64)
+        const int row = 32 * q + lane;
+        uint32_t j = 0;
+        Tile ti;
+        for (int t = blockIdx.x; tile_of(t, a, s_prefix, ti); t += gridDim.x) {
+            __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (ti.d_row0 + row) * (int64_t)a.n + ti.n0 + 64 * h;
+            if (ti.kblocks == 0) {  // empty K range (mode 1): the result is zero
+#pragma unroll
+                for (int c = 0; c < 64; c += 8) *reinterpret_cast<int4*>(d + c) = make_int4(0, 0, 0, 0);
+                continue;
+            }
+            const int b = j & 1;
+            int good = 1;
+            if (lane == 0) good = mbar_wait(&s_tfull[b], (j >> 1) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
+            if (!__shfl_sync(0xffffffffu, good, 0)) break;
+            tc_fence_after();
+            float v[64];
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + 64 * h);
+            tmem_ld_32(taddr, v);
+            tmem_ld_32(taddr + 32, v + 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_tempty[b]);
+            ++j;
+#pragma unroll
+            for (int c = 0; c < 64; c += 8) {
+                int4 o;
+                __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(v[c + 2 * i], v[c + 2 * i + 1]);
+                *reinterpret_cast<int4*>(d + c) = o;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D bf16 map over [rows][cols] (row-major), box 64 x 128 elements (128 x 128 bytes), 128-byte swizzle.
+bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, 128};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int launch_grouped_gemm_bf16(const Bf16GemmArgs& args_in, int num_sms, cudaStream_t stream) {
+    Bf16GemmArgs a = args_in;
+    if (a.n % kBN != 0 || a.num_experts <= 0 || a.num_experts > kMaxGemmExperts) return 1;
+    CUtensorMap map_a, map_b;
+    if (a.mode == 0) {
+        if (a.k % kBK != 0 || a.rows <= 0) return 1;
+        if (!make_map_bf16(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
+        if (!make_map_bf16(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k)) return 2;
+    } else {
+        if (a.m % kBM != 0 || a.k % kBK != 0 || a.k <= 0) return 1;  // k = Ktot, offsets multiples of 64
+        if (!make_map_bf16(&map_a, a.a, (uint64_t)a.m, (uint64_t)a.k)) return 2;
+        if (!make_map_bf16(&map_b, a.b, (uint64_t)a.n, (uint64_t)a.k)) return 2;
+    }
+    if (a.stages <= 0) a.stages = 6;
+    if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
+    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
+    cudaFuncSetAttribute(grouped_gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    grouped_gemm_bf16_kernel<<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace ep

@@ -80,6 +80,52 @@ torch::Tensor grouped_gemm_fp8(const torch::Tensor& a, const torch::Tensor& sa, 
     return d;
 }
 
+// bf16 grouped GEMM, both operands K-major. mode 0: a [rows, k] grouped by `offsets` (128-aligned),
+// b [E, n, k] -> d [rows, n]. mode 1: a [m, Ktot], b [n, Ktot], offsets [E+1] over K -> d [E, m, n].
+torch::Tensor grouped_gemm_bf16(const torch::Tensor& a, const torch::Tensor& b, const torch::Tensor& offsets,
+                                const std::optional<torch::Tensor>& counts, int mode, int num_sms, double timeout_s) {
+    TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.is_contiguous() && a.scalar_type() == torch::kBFloat16);
+    TORCH_CHECK(b.is_cuda() && b.is_contiguous() && b.scalar_type() == torch::kBFloat16);
+    TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.is_contiguous() && offsets.dim() == 1);
+    TORCH_CHECK(mode == 0 || mode == 1, "mode must be 0 (M-grouped) or 1 (K-grouped)");
+    const int E = (int)offsets.numel() - 1;
+    TORCH_CHECK(E >= 1 && E <= 1024);
+    Bf16GemmArgs g{};
+    torch::Tensor d;
+    if (mode == 0) {
+        TORCH_CHECK(b.dim() == 3 && b.size(0) == E && b.size(2) == a.size(1), "mode 0: b must be [E, n, k]");
+        g.rows = (int)a.size(0);
+        g.k = (int)a.size(1);
+        g.n = (int)b.size(1);
+        TORCH_CHECK(g.k % 64 == 0 && g.n % 128 == 0, "mode 0: k % 64 == 0 and n % 128 == 0");
+        if (counts.has_value()) TORCH_CHECK(counts->scalar_type() == torch::kInt32 && counts->numel() == E);
+        d = torch::empty({g.rows, g.n}, a.options());
+    } else {
+        TORCH_CHECK(b.dim() == 2 && b.size(1) == a.size(1), "mode 1: b must be [n, Ktot]");
+        g.m = (int)a.size(0);
+        g.k = (int)a.size(1);
+        g.n = (int)b.size(0);
+        TORCH_CHECK(g.m % 128 == 0 && g.n % 128 == 0 && g.k % 64 == 0, "mode 1: m, n % 128 == 0 and Ktot % 64 == 0");
+        d = torch::empty({E, g.m, g.n}, a.options());
+    }
+    if (num_sms <= 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    g.a = a.data_ptr();
+    g.b = b.data_ptr();
+    g.offsets = offsets.data_ptr<int>();
+    g.expert_counts = (mode == 0 && counts.has_value()) ? counts->data_ptr<int>() : nullptr;
+    g.d = d.data_ptr();
+    g.mode = mode;
+    g.num_experts = E;
+    g.st = op_status(timeout_s);
+    const int rc = launch_grouped_gemm_bf16(g, num_sms, at::cuda::getCurrentCUDAStream());
+    TORCH_CHECK(rc == 0, "grouped_gemm_bf16 launch failed (code " + std::to_string(rc) + ")");
+    return d;
+}
+
 std::tuple<torch::Tensor, torch::Tensor> per_token_cast_to_fp8(const torch::Tensor& x, bool round_scale) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16,
                 "x must be a contiguous CUDA bf16 [tokens, hidden] tensor");
@@ -202,6 +248,9 @@ void register_ops(pybind11::module_& m) {
     m.def("unpermute", &unpermute);
     m.def("swiglu_quant", &swiglu_quant, pybind11::arg("h"), pybind11::arg("round_scale") = false);
     m.def("quantize_weights_fp8", &quantize_weights_fp8, pybind11::arg("w"));
+    m.def("grouped_gemm_bf16", &grouped_gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("offsets"),
+          pybind11::arg("counts") = std::nullopt, pybind11::arg("mode") = 0, pybind11::arg("num_sms") = 0,
+          pybind11::arg("timeout_s") = 10.0);
     m.def("grouped_gemm_fp8", &grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"), pybind11::arg("b"), pybind11::arg("sb"),
           pybind11::arg("offsets"), pybind11::arg("counts") = pybind11::none(), pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 10.0);

@@ -5,9 +5,9 @@ Forward per rank (every step on hand-written sm_100a kernels):
   grouped FP8 GEMM gate/up (tcgen05, 1x128 x 128x128 block scales) -> fused SwiGLU + FP8 requant ->
   grouped FP8 GEMM down -> top-k weighted unpermute -> combine (sum over ranks).
 Backward: combine^T = cached dispatch of the output gradient; dispatch^T = combine; the expert
-GEMM gradients run in bf16 (straight-through through the FP8 quantization). In this version the
-backward GEMMs are torch's grouped bf16 GEMM over the aligned expert groups (a library stand-in for
-tcgen05 kernels; per-expert matmuls when the grouped GEMM is unavailable or DEEPEP_B200_MOE_BWD=loop).
+GEMM gradients run in bf16 (straight-through through the FP8 quantization) on this library's tcgen05
+grouped bf16 GEMMs (input gradients M-grouped, weight gradients K-grouped over the expert row ranges);
+DEEPEP_B200_MOE_BWD=grouped selects torch's grouped GEMM and `loop` per-expert matmuls.
 
 The reference library has no model layer (its expert compute is SGLang + DeepGEMM,
 backend/tests/sglang_dispatcher_smoke.py:107-124); this is the flagship workload of the benchmark
@@ -30,30 +30,45 @@ def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
     return [(off[e], off[e] + cnt[e]) for e in range(len(cnt))]
 
 
-_GROUPED_BWD = {'enabled': os.environ.get('DEEPEP_B200_MOE_BWD', 'grouped') == 'grouped'}
+_BWD_MODE = os.environ.get('DEEPEP_B200_MOE_BWD', 'tcgen05')  # tcgen05 | grouped (torch) | loop
+_GROUPED_BWD = {'enabled': _BWD_MODE in ('tcgen05', 'grouped'), 'tcgen05': _BWD_MODE == 'tcgen05'}
 
 
 def _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx) -> bool:
-    """Expert GEMM gradients as four grouped bf16 GEMMs over whole 128-aligned groups (torch's
-    grouped GEMM: a library stand-in for tcgen05 grouped kernels). Padding rows are masked to zero
-    so they contribute nothing. Returns False (and the caller loops over experts) when the grouped
-    GEMM is unavailable in this torch build."""
-    if not _GROUPED_BWD['enabled'] or not hasattr(torch, '_grouped_mm'):
+    """Expert GEMM gradients as four grouped bf16 GEMMs over whole 128-aligned groups: this library's
+    tcgen05 kernels by default (DEEPEP_B200_MOE_BWD=tcgen05), torch's grouped GEMM with `grouped`.
+    Padding rows are masked to zero so they contribute nothing. Returns False (and the caller loops
+    over experts) for `loop` or when torch's grouped GEMM is unavailable."""
+    if not _GROUPED_BWD['enabled']:
+        return False
+    if not _GROUPED_BWD['tcgen05'] and not hasattr(torch, '_grouped_mm'):
         return False
     R = int(offsets[-1].item())
     offs = offsets[1:].to(torch.int32).contiguous()
     live = torch.zeros((R, 1), dtype=torch.bool, device=g_y.device)
     live[rows[rows < R]] = True
     zero = torch.zeros((), dtype=torch.bfloat16, device=g_y.device)
+    gy = g_y[:R]
+    aa = torch.where(live, a[:R], zero)
+    hh = torch.where(live, h[:R], zero).float()
+    xx = torch.where(live, xf[:R], zero)
+    gate, up = hh[:, :inter], hh[:, inter:]
+    s = torch.sigmoid(gate)
+    if _GROUPED_BWD['tcgen05']:
+        # sm_100a kernels: dgrad M-grouped against K-major (transposed) weights, wgrad K-grouped over
+        # the expert row ranges of the transposed activations.
+        from ..ops.gemm import grouped_gemm_bf16, grouped_gemm_bf16_wgrad
+        offs32 = offsets.to(torch.int32).contiguous()
+        g_a = grouped_gemm_bf16(gy, w2.transpose(1, 2).contiguous(), offs32, counts).float()          # [R, I]
+        g_w2 = grouped_gemm_bf16_wgrad(gy.t().contiguous(), aa.t().contiguous(), offs32)            # [E, H, I]
+        g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
+        g_xp[:R] = grouped_gemm_bf16(g_h, w1.transpose(1, 2).contiguous(), offs32, counts)           # [R, H]
+        g_w1 = grouped_gemm_bf16_wgrad(g_h.t().contiguous(), xx.t().contiguous(), offs32)           # [E, 2I, H]
+        ctx.g_w1, ctx.g_w2 = g_w1, g_w2
+        return True
     try:
-        gy = g_y[:R]
-        aa = torch.where(live, a[:R], zero)
-        hh = torch.where(live, h[:R], zero).float()
-        xx = torch.where(live, xf[:R], zero)
         g_a = torch._grouped_mm(gy, w2, offs=offs).float()                         # [R, I]
         g_w2 = torch._grouped_mm(gy.t(), aa, offs=offs)                            # [E, H, I]
-        gate, up = hh[:, :inter], hh[:, inter:]
-        s = torch.sigmoid(gate)
         g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
         g_xp[:R] = torch._grouped_mm(g_h, w1, offs=offs)                           # [R, H]
         g_w1 = torch._grouped_mm(g_h.t(), xx, offs=offs)                           # [E, 2I, H]

@@ -2,7 +2,8 @@
 
 `grouped_gemm_fp8`: rows of A grouped by expert (128-aligned blocks from `permute(..., alignment=128)`),
 per-token 1x128 activation scales, 128x128 weight scales, fp32 promotion per 128-wide K block, bf16 out.
-`grouped_gemm_fp8_reference` is the fp32 torch oracle.
+`grouped_gemm_bf16` / `grouped_gemm_bf16_wgrad`: bf16 x bf16 -> fp32 TMEM accumulation, the backward
+(input- and weight-gradient) GEMMs of the expert FFN. `*_reference` are the fp32 torch oracles.
 """
 from typing import Optional
 
@@ -14,6 +15,40 @@ from .._ext import require_ext
 def grouped_gemm_fp8(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, offsets: torch.Tensor,
                      counts: Optional[torch.Tensor] = None, num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
     return require_ext().grouped_gemm_fp8(a, sa, b, sb, offsets, counts, num_sms, timeout_s)
+
+
+def grouped_gemm_bf16(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, counts: Optional[torch.Tensor] = None,
+                      num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
+    """M-grouped bf16 GEMM on tcgen05: rows of `a [rows, k]` grouped by expert (`offsets [E+1]`,
+    128-aligned) times `b [E, n, k]` (K-major weights) -> `[rows, n]` bf16 (fp32 accumulation)."""
+    return require_ext().grouped_gemm_bf16(a, b, offsets, counts, 0, num_sms, timeout_s)
+
+
+def grouped_gemm_bf16_wgrad(a_t: torch.Tensor, b_t: torch.Tensor, offsets: torch.Tensor, num_sms: int = 0,
+                            timeout_s: float = 10.0) -> torch.Tensor:
+    """K-grouped bf16 GEMM on tcgen05 (weight gradients): `a_t [m, Ktot]`, `b_t [n, Ktot]` with expert e
+    owning K range [offsets[e], offsets[e+1]) -> `[E, m, n]` = per-expert a_t[:, K_e] @ b_t[:, K_e]^T."""
+    return require_ext().grouped_gemm_bf16(a_t, b_t, offsets, None, 1, num_sms, timeout_s)
+
+
+def grouped_gemm_bf16_reference(a, b, offsets, counts=None) -> torch.Tensor:
+    out = torch.zeros((a.shape[0], b.shape[1]), dtype=torch.float32, device=a.device)
+    off = offsets.tolist()
+    for e in range(b.shape[0]):
+        r1 = off[e] + (int(counts[e]) if counts is not None else off[e + 1] - off[e])
+        if r1 > off[e]:
+            out[off[e]:r1] = a[off[e]:r1].float() @ b[e].float().t()
+    return out
+
+
+def grouped_gemm_bf16_wgrad_reference(a_t, b_t, offsets) -> torch.Tensor:
+    off = offsets.tolist()
+    E = len(off) - 1
+    out = torch.zeros((E, a_t.shape[0], b_t.shape[0]), dtype=torch.float32, device=a_t.device)
+    for e in range(E):
+        if off[e + 1] > off[e]:
+            out[e] = a_t[:, off[e]:off[e + 1]].float() @ b_t[:, off[e]:off[e + 1]].float().t()
+    return out
 
 
 def op_error_state(clear: bool = False):

@@ -45,3 +45,43 @@ def test_quantize_weights_kernel_matches_torch(E, n, k):
     torch.cuda.synchronize()
     assert torch.equal(s, rs)
     assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8))
+
+
+@pytest.mark.parametrize('E,n,k,rows_per', [(3, 256, 512, [130, 0, 300]), (4, 2048, 7168, [256, 128, 37, 500])])
+def test_grouped_gemm_bf16_dgrad(E, n, k, rows_per):
+    """M-grouped bf16 tcgen05 GEMM (activation gradients) against an fp32 torch oracle."""
+    from deepep_slingshot_b200.ops.gemm import grouped_gemm_bf16, grouped_gemm_bf16_reference
+    g = torch.Generator().manual_seed(n + k)
+    counts = torch.tensor(rows_per, dtype=torch.int32)
+    aligned = (counts + 127) // 128 * 128
+    offsets = torch.zeros(E + 1, dtype=torch.int32)
+    offsets[1:] = aligned.cumsum(0)
+    rows = int(offsets[-1])
+    a = torch.randn((rows, k), generator=g).to(torch.bfloat16).cuda()
+    b = (torch.randn((E, n, k), generator=g) * 0.05).to(torch.bfloat16).cuda()
+    d = grouped_gemm_bf16(a, b, offsets.cuda(), counts.cuda())
+    ref = grouped_gemm_bf16_reference(a, b, offsets, counts)
+    torch.cuda.synchronize()
+    for e in range(E):
+        r0, r1 = int(offsets[e]), int(offsets[e]) + rows_per[e]
+        if r1 > r0:
+            assert torch.allclose(d[r0:r1].float(), ref[r0:r1], atol=2e-2, rtol=2e-2), (e, (d[r0:r1].float() - ref[r0:r1]).abs().max())
+
+
+@pytest.mark.parametrize('m,n,rows_per', [(256, 384, [128, 0, 256, 64]), (2048, 7168, [512, 1024, 128])])
+def test_grouped_gemm_bf16_wgrad(m, n, rows_per):
+    """K-grouped bf16 tcgen05 GEMM (weight gradients) against an fp32 torch oracle; an expert with
+    no rows gets a zero gradient."""
+    from deepep_slingshot_b200.ops.gemm import grouped_gemm_bf16_wgrad, grouped_gemm_bf16_wgrad_reference
+    g = torch.Generator().manual_seed(m + n)
+    E = len(rows_per)
+    offsets = torch.zeros(E + 1, dtype=torch.int32)
+    offsets[1:] = torch.tensor(rows_per, dtype=torch.int32).cumsum(0)
+    K = int(offsets[-1])
+    a_t = torch.randn((m, K), generator=g).to(torch.bfloat16).cuda()
+    b_t = (torch.randn((n, K), generator=g) * 0.05).to(torch.bfloat16).cuda()
+    d = grouped_gemm_bf16_wgrad(a_t, b_t, offsets.cuda())
+    ref = grouped_gemm_bf16_wgrad_reference(a_t, b_t, offsets)
+    torch.cuda.synchronize()
+    assert d.shape == (E, m, n)
+    assert torch.allclose(d.float(), ref, atol=5e-2, rtol=2e-2), (d.float() - ref).abs().max()
