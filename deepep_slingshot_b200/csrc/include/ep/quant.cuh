@@ -44,6 +44,8 @@ __device__ __forceinline__ uint2 quantize_8(const int4& v, bool round_scale, flo
 
 // `out_x` and `out_scales` may point to global or shared memory. `hidden` % 128 == 0.
 // Loads are batched four 256-element slices at a time so each lane keeps 4 x 16 B in flight.
+// With kSmemSource the row is read from shared memory (plain loads) instead of global memory.
+template <bool kSmemSource = false>
 __device__ __forceinline__ void quantize_row_to_fp8(const __nv_bfloat16* __restrict__ xr, uint8_t* __restrict__ out_x,
                                                     float* __restrict__ out_scales, int hidden, bool round_scale) {
     const int lane = lane_id();
@@ -53,7 +55,10 @@ __device__ __forceinline__ void quantize_row_to_fp8(const __nv_bfloat16* __restr
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int e = base + u * 256 + lane * 8;
-            v[u] = e < hidden ? ld_nc_v4(reinterpret_cast<const int4*>(xr + e)) : make_int4(0, 0, 0, 0);
+            if constexpr (kSmemSource)
+                v[u] = e < hidden ? *reinterpret_cast<const int4*>(xr + e) : make_int4(0, 0, 0, 0);
+            else
+                v[u] = e < hidden ? ld_nc_v4(reinterpret_cast<const int4*>(xr + e)) : make_int4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {

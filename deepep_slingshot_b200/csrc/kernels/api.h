@@ -28,6 +28,7 @@ struct StageArgs {
     int in_elem_bytes;           // 2 = bf16 input, 1 = fp8 input
     int quantize;                // 1: fuse bf16 -> fp8 e4m3 1x128 quantization
     int round_scale;             // 1: power-of-two scales
+    int tma_rows;                // 1 (set by the launcher): rows are TMA-loaded into shared memory before quantizing
     int num_ranks;
     const int* dispatch_epoch;   // local ctrl.dispatch_epoch: wait until pull_done[r] >= it
     const bool* is_token_in_rank;  // [N][R] or null

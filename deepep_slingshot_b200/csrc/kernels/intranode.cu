@@ -92,8 +92,16 @@ void launch_dispatch_layout(const int64_t* topk_idx, int num_tokens, int num_top
 // =================================================================================================
 // stage: one record per token into the local staging area, FP8 quantization fused.
 // =================================================================================================
-__global__ void __launch_bounds__(256, 4) dispatch_stage_kernel(StageArgs a) {
+__global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
+    // With tma_rows each warp owns one row buffer of dynamic shared memory: a single bulk copy brings
+    // the whole bf16 row in (no registers held for loads in flight), the warp quantizes from there.
+    extern __shared__ __align__(128) uint8_t s_rows[];
+    __shared__ __align__(8) uint64_t s_bar[8];
     const uint64_t t_start = trace_begin(a.st);
+    if (a.tma_rows && lane_id() == 0) {
+        mbar_init(&s_bar[warp_id()], 1);
+        fence_mbar_init();
+    }
     if ((int)threadIdx.x < a.num_ranks) {
         // Receivers must have finished pulling the previous dispatch before the staging is rewritten.
         const int prev_epoch = ld_volatile(a.dispatch_epoch);
@@ -106,9 +114,23 @@ __global__ void __launch_bounds__(256, 4) dispatch_stage_kernel(StageArgs a) {
     const int lane = lane_id();
     const int warps = blockDim.x / 32;
     const int total_warps = gridDim.x * warps;
+    uint32_t phase = 0;
     for (int t = blockIdx.x * warps + warp_id(); t < a.num_tokens; t += total_warps) {
         uint8_t* rec = a.staging + (int64_t)t * a.record_stride;
-        if (a.quantize) {
+        if (a.quantize && a.tma_rows) {
+            const uint32_t row_bytes = (uint32_t)a.hidden * 2;
+            uint8_t* buf = s_rows + (size_t)warp_id() * row_bytes;
+            if (lane == 0) {
+                fence_proxy_async_smem();  // the previous row's generic reads precede this async write
+                mbar_arrive_expect_tx(&s_bar[warp_id()], row_bytes);
+                tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + (int64_t)t * row_bytes, row_bytes, &s_bar[warp_id()]);
+            }
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma) ? 1 : 0)) break;
+            phase ^= 1u;
+            quantize_row_to_fp8<true>(reinterpret_cast<const __nv_bfloat16*>(buf), rec,
+                                      reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
+            __syncwarp();
+        } else if (a.quantize) {
             quantize_row_to_fp8(static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * a.hidden, rec,
                                 reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
         } else {
@@ -151,11 +173,24 @@ __global__ void __launch_bounds__(256, 4) dispatch_stage_kernel(StageArgs a) {
     }
 }
 
-void launch_dispatch_stage(const StageArgs& a, int num_sms, cudaStream_t stream) {
+void launch_dispatch_stage(const StageArgs& a_in, int num_sms, cudaStream_t stream) {
     (void)num_sms;
+    StageArgs a = a_in;
     int blocks = (a.num_tokens + 7) / 8;
     if (blocks < 1) blocks = 1;
-    dispatch_stage_kernel<<<blocks, 256, 0, stream>>>(a);
+    size_t smem = 0;
+    const size_t row_bytes = (size_t)a.hidden * 2;
+    // TMA row loads: 8 row buffers per block (two blocks per SM up to hidden 7168), 16-byte aligned rows.
+    a.tma_rows = a.quantize && row_bytes % 16 == 0 && 8 * row_bytes <= 112 * 1024 &&
+                 reinterpret_cast<uintptr_t>(a.x) % 16 == 0;
+    if (a.tma_rows) {
+        smem = 8 * row_bytes;
+        int sm_count = 148, dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (blocks > 2 * sm_count) blocks = 2 * sm_count;  // grid-stride: every block resident
+        cudaFuncSetAttribute(dispatch_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
+    dispatch_stage_kernel<<<blocks, 256, smem, stream>>>(a);
 }
 
 // =================================================================================================

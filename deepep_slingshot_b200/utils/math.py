@@ -38,6 +38,9 @@ def per_token_cast_to_fp8(x: torch.Tensor, round_scale: bool = False) -> Tuple[t
     assert x.dim() == 2
     m, n = x.shape
     aligned_n = align(n, 128)
+    if m == 0:
+        return (torch.empty((0, n), dtype=torch.float8_e4m3fn, device=x.device),
+                torch.empty((0, aligned_n // 128), dtype=torch.float32, device=x.device))
     x_padded = torch.nn.functional.pad(x, (0, aligned_n - n), mode='constant', value=0)
     x_view = x_padded.view(m, -1, 128)
     x_amax = x_view.abs().float().amax(dim=2).view(m, -1).clamp(1e-4)

@@ -50,3 +50,34 @@ def _body(rank, world):
 
 def test_gloo_world2_plumbing():
     run_ranks(_body, 2, 'gloo')
+
+
+def _edge_oracle_body(rank, world):
+    """Oracle with ranks holding 0..3 tokens and a hot rank (CPU, gloo)."""
+    import torch.distributed as dist
+    from deepep_slingshot_b200 import ReferenceBuffer
+    ref = ReferenceBuffer(dist.group.WORLD)
+    H, E, K = 256, 8, 2
+    g = torch.Generator().manual_seed(rank)
+    for case in range(3):
+        N = [0, 1, 3, 2][(rank + case) % 4]
+        x = torch.randn((N, H), generator=g).to(torch.bfloat16)
+        if case == 2:
+            idx = torch.arange(K, dtype=torch.int64).expand(N, K).contiguous()
+        else:
+            idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)]) if N else \
+                torch.empty((0, K), dtype=torch.int64)
+        w = torch.rand((N, K), generator=g)
+        for fp8 in (False, True):
+            rx, ri, rw, lst, h, _ = ref.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, quantize_fp8=fp8)
+            n = (rx[0] if fp8 else rx).shape[0]
+            out, ow, _ = ref.combine(torch.ones((n, H), dtype=torch.bfloat16), h, topk_weights=rw)
+            # every token comes back once per destination rank holding one of its experts
+            dst = (idx // (E // world)).tolist()
+            expect = torch.tensor([len(set(d)) for d in dst], dtype=torch.float32)
+            assert out.shape == (N, H) and torch.equal(out[:, 0].float(), expect)
+
+
+def test_reference_edge_cases_gloo():
+    from tests._dist import run_ranks
+    run_ranks(_edge_oracle_body, 2)
