@@ -5,9 +5,10 @@ Forward per rank (every step on hand-written sm_100a kernels):
   grouped FP8 GEMM gate/up (tcgen05, 1x128 x 128x128 block scales) -> fused SwiGLU + FP8 requant ->
   grouped FP8 GEMM down -> top-k weighted unpermute -> combine (sum over ranks).
 Backward: combine^T = cached dispatch of the output gradient; dispatch^T = combine; the expert
-GEMM gradients run in bf16 (straight-through through the FP8 quantization) on this library's tcgen05
-grouped bf16 GEMMs (input gradients M-grouped, weight gradients K-grouped over the expert row ranges);
-DEEPEP_B200_MOE_BWD=grouped selects torch's grouped GEMM and `loop` per-expert matmuls.
+GEMM gradients run in bf16 (straight-through through the FP8 quantization) as grouped GEMMs over the
+aligned expert groups: torch's grouped bf16 GEMM by default (a library stand-in), this library's
+tcgen05 grouped bf16 GEMMs with DEEPEP_B200_MOE_BWD=tcgen05 (input gradients M-grouped, weight
+gradients K-grouped over the expert row ranges), per-expert matmuls with `loop`.
 
 The reference library has no model layer (its expert compute is SGLang + DeepGEMM,
 backend/tests/sglang_dispatcher_smoke.py:107-124); this is the flagship workload of the benchmark
@@ -30,13 +31,17 @@ def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
     return [(off[e], off[e] + cnt[e]) for e in range(len(cnt))]
 
 
-_BWD_MODE = os.environ.get('DEEPEP_B200_MOE_BWD', 'tcgen05')  # tcgen05 | grouped (torch) | loop
+# Backward expert GEMMs: `grouped` (torch's grouped bf16 GEMM, default), `tcgen05` (this library's
+# kernels; they take K-major operands, so the weights are transposed every step: with 256 local
+# experts on one GPU that costs ~45 GB of copies and made the step 2x slower, measured 107 vs 52 ms),
+# `loop` (per-expert matmuls).
+_BWD_MODE = os.environ.get('DEEPEP_B200_MOE_BWD', 'grouped')
 _GROUPED_BWD = {'enabled': _BWD_MODE in ('tcgen05', 'grouped'), 'tcgen05': _BWD_MODE == 'tcgen05'}
 
 
 def _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx) -> bool:
-    """Expert GEMM gradients as four grouped bf16 GEMMs over whole 128-aligned groups: this library's
-    tcgen05 kernels by default (DEEPEP_B200_MOE_BWD=tcgen05), torch's grouped GEMM with `grouped`.
+    """Expert GEMM gradients as four grouped bf16 GEMMs over whole 128-aligned groups: torch's grouped
+    GEMM by default (`grouped`), this library's tcgen05 kernels with DEEPEP_B200_MOE_BWD=tcgen05.
     Padding rows are masked to zero so they contribute nothing. Returns False (and the caller loops
     over experts) for `loop` or when torch's grouped GEMM is unavailable."""
     if not _GROUPED_BWD['enabled']:
