@@ -1,7 +1,7 @@
 """Headline benchmark: DeepSeek-V3-shape normal-mode dispatch + combine over NVLink on N B200s,
 plus the low-latency decode dispatch / combine latencies.
 
-Config: per rank 4096 tokens, hidden 7168, bf16 activations ~N(0,1),
+Config (the headline DeepSeek-V3 EP config): per rank 4096 tokens, hidden 7168, bf16 activations ~N(0,1),
 256 experts (256/N per rank), top-8 from N(0,1) router logits with softmax weights; dispatch in
 FP8 e4m3 with per-token 1x128 fp32 scales (quantization fused into the dispatch), combine in bf16.
 One step = get_dispatch_layout + dispatch + combine (fresh, CPU-synced receive counts).

@@ -10,7 +10,7 @@
 //               trapping (reference: backend/device/cxi_primitives.cuh:39 default_timeout and
 //               backend/device/gin_cxi.cuh:9 `require` trap; DeepEP `timeout_while`
 //               [DE]deep_ep/include/deep_ep/common/comm.cuh:30-53 prints and traps).
-// No `.multicast::cluster` form of any TMA copy appears here: these kernels run on 2..8 GPUs.
+// No cluster-multicast form of any TMA copy is used here: these kernels run on 2..8 GPUs.
 #pragma once
 
 #include <cstdint>
