@@ -41,6 +41,37 @@ PYBIND11_MODULE(_C, m) {
     m.def("normal_layout_capacity", [](int64_t region_bytes, int hidden, int num_ranks) {
         return ep::compute_normal_layout(region_bytes, hidden, num_ranks).capacity;
     });
+    m.def("normal_layout", [](int64_t region_bytes, int hidden, int num_ranks) {
+        const ep::NormalLayout l = ep::compute_normal_layout(region_bytes, hidden, num_ranks);
+        py::dict d;
+        d["ctrl_off"] = l.ctrl_off;
+        d["list_off"] = l.list_off;
+        d["staging_off"] = l.staging_off;
+        d["combine_off"] = l.combine_off;
+        d["combine_w_off"] = l.combine_w_off;
+        d["scratch_off"] = l.scratch_off;
+        d["arrival_off"] = l.arrival_off;
+        d["total_bytes"] = l.total_bytes;
+        d["capacity"] = l.capacity;
+        d["record_bytes"] = l.record_bytes;
+        return d;
+    });
+    m.def("ll_layout", [](int max_tokens, int hidden, int num_ranks, int num_experts) {
+        const ep::LLLayout l = ep::compute_ll_layout(0, max_tokens, hidden, num_experts, num_ranks);
+        py::dict d;
+        d["half_bytes"] = l.half_bytes;
+        d["ctrl_off"] = l.ctrl_off;
+        d["recv_x_off"] = l.recv_x_off;
+        d["recv_scales_off"] = l.recv_scales_off;
+        d["recv_src_info_off"] = l.recv_src_info_off;
+        d["recv_src_meta_off"] = l.recv_src_meta_off;
+        d["combine_recv_off"] = l.combine_recv_off;
+        d["combine_send_off"] = l.combine_send_off;
+        d["combine_meta_off"] = l.combine_meta_off;
+        return d;
+    });
+    m.attr("sym_ctrl_bytes") = ep::kSymCtrlBytes;
+    m.attr("sym_ctrl_struct_bytes") = (int64_t)sizeof(ep::SymCtrl);
 
     py::class_<ep::Buffer>(m, "Buffer")
         .def(py::init<int, int, int64_t, int64_t, bool, bool, bool, double>())

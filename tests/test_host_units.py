@@ -62,3 +62,75 @@ def test_routings_shapes_and_weights():
 
 def test_align():
     assert align(5, 4) == 8 and align(8, 4) == 8
+
+
+@pytest.mark.parametrize('tokens,hidden,ranks,experts', [(128, 7168, 8, 256), (64, 2048, 2, 32), (1, 256, 1, 8)])
+def test_ll_layout_offsets(tokens, hidden, ranks, experts):
+    """Low-latency half layout: ordered, 128-byte aligned, non-overlapping sections that fit the half
+    (the LogFMT metadata section included)."""
+    ext = _ext()
+    l = ext.ll_layout(tokens, hidden, ranks, experts)
+    order = ['ctrl_off', 'recv_x_off', 'recv_scales_off', 'recv_src_info_off', 'recv_src_meta_off',
+             'combine_recv_off', 'combine_send_off', 'combine_meta_off']
+    offs = [l[k] for k in order]
+    assert all(o % 128 == 0 for o in offs)
+    assert offs == sorted(offs) and len(set(offs)) == len(offs)
+    e_l, slots = experts // ranks, ranks * tokens
+    assert l['recv_scales_off'] - l['recv_x_off'] >= e_l * slots * hidden * 2
+    assert l['combine_send_off'] - l['combine_recv_off'] >= tokens * 16 * hidden * 2
+    assert l['half_bytes'] - l['combine_meta_off'] >= tokens * 16 * (hidden // 128) * 4
+    assert 2 * l['half_bytes'] <= ext.ll_region_size_for(tokens, hidden, ranks, experts)
+
+
+@pytest.mark.parametrize('hidden,ranks', [(7168, 8), (1024, 2)])
+def test_normal_layout_offsets(hidden, ranks):
+    ext = _ext()
+    size = ext.normal_region_size_for(4096, hidden, ranks)
+    l = ext.normal_layout(size, hidden, ranks)
+    for k in ('list_off', 'staging_off', 'combine_off', 'combine_w_off', 'scratch_off', 'arrival_off'):
+        assert l[k] % 128 == 0 and l[k] < l['total_bytes'] <= size, k
+    assert l['record_bytes'] % 16 == 0 and l['record_bytes'] >= hidden  # FP8 row + metadata, TMA-sized
+    assert l['capacity'] >= 4096
+
+
+def test_symmetric_ctrl_fits():
+    ext = _ext()
+    assert ext.sym_ctrl_struct_bytes <= ext.sym_ctrl_bytes and ext.sym_ctrl_bytes % 4096 == 0
+
+
+def test_logfmt_oracle_properties():
+    from deepep_slingshot_b200.utils.math import logfmt10_roundtrip
+    g = torch.Generator().manual_seed(0)
+    small = (torch.randn((8, 1024), generator=g) * 0.05).to(torch.bfloat16)
+    big = (torch.randn((8, 1024), generator=g) * 4).to(torch.bfloat16)
+    rs = logfmt10_roundtrip(small)
+    rel = (rs - small.float()).abs() / small.float().abs().clamp_min(1e-30)
+    assert float(rel[small != 0].max()) < 0.05          # 9-bit log levels over <= 32 octaves
+    assert torch.equal(torch.sign(rs), torch.sign(small.float()))
+    assert torch.equal(logfmt10_roundtrip(big), big.float())  # groups with |x| >= 1 travel raw
+    z = small.clone()
+    z[:, :128] = 0
+    assert (logfmt10_roundtrip(z)[:, :128] == 0).all()
+
+
+def test_analyze_trace_synthetic():
+    from deepep_slingshot_b200.harness.analyze_trace import analyze
+    ev = []
+    for r in range(2):
+        off = 10.0 * r
+        for name, s, d in (('dispatch.stage.wait_receivers', 0, 1), ('dispatch.stage', 0, 30), ('dispatch.notify', 31, 20),
+                           ('dispatch.pull', 52, 100), ('combine.block', 160, 200)):
+            ev.append({'name': name, 'pid': r, 'ts': s + off, 'dur': d})
+    rep = analyze({'traceEvents': ev})
+    assert len(rep) == 1
+    p = rep[0]['phases']
+    assert p['dispatch.stage']['start_spread_us'] == 10.0 and p['combine.block']['last_rank'] == 1
+    assert [c['phase'] for c in rep[0]['critical_path']] == ['dispatch.stage', 'dispatch.notify', 'dispatch.pull',
+                                                              'combine.block']
+
+
+def test_ep_benchmark_byte_counts():
+    from deepep_slingshot_b200.harness.ep_benchmark import combine_bytes, dispatch_bytes
+    assert dispatch_bytes(10, 7168, 8, True) == 10 * (7168 + 56 * 4 + 64 + 32)
+    assert dispatch_bytes(10, 7168, 8, False) == 10 * (2 * 7168 + 64 + 32)
+    assert combine_bytes(10, 7168, 8) == 10 * (2 * 7168 + 32)
