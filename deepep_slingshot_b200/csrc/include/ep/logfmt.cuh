@@ -18,6 +18,8 @@
 // group; a group's offset is 160 x (encoded groups before it) + 256 x (raw groups before it).
 #pragma once
 
+#include <cstring>
+
 #include <cuda_bf16.h>
 
 #include "device.cuh"
@@ -40,13 +42,53 @@ struct LogFmtGroup {
 };
 
 // Derive the group parameters from amax / amin exactly as both sides must.
-__device__ __forceinline__ LogFmtGroup logfmt_params(float amax, float amin) {
+__host__ __device__ __forceinline__ LogFmtGroup logfmt_params(float amax, float amin) {
     LogFmtGroup g;
     const float log_amax = log2f(amax);
     g.log_amin = fmaxf(log2f(amin), log_amax - 32.0f);
     g.cast = (log_amax < 0.0f) && (g.log_amin < log_amax);
     g.step = (log_amax - g.log_amin) / 510.0f;
     return g;
+}
+
+// 10-bit code of one value of an encoded group: sign << 9 | magnitude level (0 = zero).
+// `inv` = 1 / step, `up` = log2((1 + 2^step) / 2) / step (the linear-space rounding point).
+__host__ __device__ __forceinline__ uint32_t logfmt_code(float v, const LogFmtGroup& p, float inv, float up) {
+    int code = 0;
+    if (v != 0.f) {
+        const float t = (log2f(fabsf(v)) - p.log_amin) * inv;
+        const float f = floorf(t + 2.0f - up);
+        code = f < 0.f ? 0 : (f > 511.f ? 511 : (int)f);
+    }
+    uint32_t sign;
+    memcpy(&sign, &v, sizeof(sign));
+    return (uint32_t)code | ((sign >> 31) << 9);
+}
+
+// Four 10-bit codes -> 5 bytes (little-endian 40-bit word).
+__host__ __device__ __forceinline__ void logfmt_pack4(const uint32_t* c, uint8_t* d) {
+    const uint32_t lo = c[0] | (c[1] << 10) | (c[2] << 20) | (c[3] << 30);
+    const uint32_t hi = c[3] >> 2;
+    d[0] = (uint8_t)lo;
+    d[1] = (uint8_t)(lo >> 8);
+    d[2] = (uint8_t)(lo >> 16);
+    d[3] = (uint8_t)(lo >> 24);
+    d[4] = (uint8_t)hi;
+}
+
+// 10 bytes read as five little-endian 16-bit words (two encoder lanes x 40 bits) -> 8 codes. Each
+// 40-bit half is assembled in its own 64-bit word.
+__host__ __device__ __forceinline__ void logfmt_unpack8(const uint16_t* s, uint32_t* codes) {
+    const uint64_t half0 = (uint64_t)s[0] | ((uint64_t)s[1] << 16) | ((uint64_t)(s[2] & 0xffu) << 32);
+    const uint64_t half1 = (uint64_t)(s[2] >> 8) | ((uint64_t)s[3] << 8) | ((uint64_t)s[4] << 24);
+    for (int i = 0; i < 8; ++i) codes[i] = (uint32_t)((i < 4 ? half0 : half1) >> (10 * (i & 3))) & 0x3ffu;
+}
+
+// Value of a 10-bit code of an encoded group.
+__host__ __device__ __forceinline__ float logfmt_value(uint32_t code, const LogFmtGroup& p) {
+    const uint32_t mag = code & 511u;
+    const float val = mag == 0 ? 0.f : exp2f((float)(mag - 1) * p.step + p.log_amin);
+    return (code >> 9) ? -val : val;
 }
 
 // Encode a bf16 row held in shared memory IN PLACE (one warp); returns the compacted byte count
@@ -84,23 +126,8 @@ __device__ __forceinline__ int logfmt_encode_row(uint8_t* buf, int hidden, uint3
             const float up = log2f((1.0f + exp2f(p.step)) * 0.5f) * inv;
             uint32_t c[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                int code = 0;
-                if (v[i] != 0.f) {
-                    const float t = (log2f(fabsf(v[i])) - p.log_amin) * inv;
-                    const float f = floorf(t + 2.0f - up);
-                    code = f < 0.f ? 0 : (f > 511.f ? 511 : (int)f);
-                }
-                c[i] = (uint32_t)code | ((__float_as_uint(v[i]) >> 31) << 9);
-            }
-            const uint32_t lo = c[0] | (c[1] << 10) | (c[2] << 20) | (c[3] << 30);
-            const uint32_t hi = c[3] >> 2;
-            uint8_t* d = buf + off + lane * 5;
-            d[0] = (uint8_t)lo;
-            d[1] = (uint8_t)(lo >> 8);
-            d[2] = (uint8_t)(lo >> 16);
-            d[3] = (uint8_t)(lo >> 24);
-            d[4] = (uint8_t)hi;
+            for (int i = 0; i < 4; ++i) c[i] = logfmt_code(v[i], p, inv, up);
+            logfmt_pack4(c, buf + off + lane * 5);
             off += 160;
         } else {
             *reinterpret_cast<uint2*>(buf + off + lane * 8) = raw;
@@ -121,18 +148,10 @@ __device__ __forceinline__ void logfmt_accumulate8(const uint8_t* row, int g, in
     const int off = 160 * cast_before + 256 * (g - cast_before);
     if (meta & 0x8000u) {
         const LogFmtGroup prm = logfmt_params(bf16_bits_to_float(meta & 0x7fffu), bf16_bits_to_float(meta >> 16));
-        // 10 bytes = two encoder lanes x 40 bits (four codes each); each half fits a 64-bit word.
-        const uint16_t* s = reinterpret_cast<const uint16_t*>(row + off + (p / 8) * 10);
-        const uint64_t half0 = (uint64_t)s[0] | ((uint64_t)s[1] << 16) | ((uint64_t)(s[2] & 0xffu) << 32);
-        const uint64_t half1 = (uint64_t)(s[2] >> 8) | ((uint64_t)s[3] << 8) | ((uint64_t)s[4] << 24);
+        uint32_t codes[8];
+        logfmt_unpack8(reinterpret_cast<const uint16_t*>(row + off + (p / 8) * 10), codes);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t code = (uint32_t)((i < 4 ? half0 : half1) >> (10 * (i & 3))) & 0x3ffu;
-            const uint32_t mag = code & 511u;
-            float val = mag == 0 ? 0.f : exp2f((float)(mag - 1) * prm.step + prm.log_amin);
-            if (code >> 9) val = -val;
-            acc[i] = fmaf(w, val, acc[i]);
-        }
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, logfmt_value(codes[i], prm), acc[i]);
     } else {
         const int4 v = *reinterpret_cast<const int4*>(row + off + p * 2);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);

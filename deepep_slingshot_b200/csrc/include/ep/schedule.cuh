@@ -1,0 +1,72 @@
+// Row schedules of the pipelined dispatch-pull and combine-push kernels (host + device, so the host
+// model tests exercise the exact functions the kernels run).
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace ep {
+
+__host__ __device__ __forceinline__ int sched_min(int a, int b) { return a < b ? a : b; }
+
+// Rows are dealt to pairs in chunks of `chunk`: pair g owns chunks g, g + P, g + 2P, ... so every
+// pair sees rows of every source/destination rank (receive rows are sorted by rank).
+// chunk == 0 deals contiguous ranges instead (pair g owns rows [g*per, (g+1)*per)).
+__host__ __device__ __forceinline__ int pair_row(int g, int P, int k, int chunk, int n) {
+    if (chunk == 0) return g * ((n + P - 1) / P) + k;
+    return ((k / chunk) * P + g) * chunk + (k % chunk);
+}
+
+// Combine push order with chunk == -1 ("wavefront"): at step k pair g serves destination
+// s = (k + g) % R, row (k / R) * P + g of that destination's segment (-1 past its end). Every pair
+// spreads its stores over all destinations (no incast), and all ranks walk each destination's tokens
+// in increasing order at the same pace, so a token's contributions from every source land close
+// together and the reducers (which take tokens in increasing order) follow the pushes instead of
+// waiting for the end of the push phase.
+__host__ __device__ __forceinline__ int wave_row(int g, int P, int k, const int* prefix, int R, int n) {
+    const int s = (k + g) % R;
+    const int i = (k / R) * P + g;
+    const int lo = sched_min(prefix[s], n), hi = sched_min(prefix[s + 1], n);
+    return i < hi - lo ? lo + i : -1;
+}
+__host__ __device__ __forceinline__ int wave_num_rows(int g, int P, const int* prefix, int R, int n) {
+    int rows = 0;
+    for (int s = 0; s < R; ++s) {
+        const int len = sched_min(prefix[s + 1], n) - sched_min(prefix[s], n);
+        if (len > g) rows += (len - g + P - 1) / P;
+    }
+    return rows;
+}
+__host__ __device__ __forceinline__ int pair_num_rows(int g, int P, int n, int chunk) {
+    if (chunk == 0) {
+        const int per = (n + P - 1) / P;
+        const int r0 = sched_min(n, g * per);
+        return sched_min(n, r0 + per) - r0;
+    }
+    const int full_chunks = n / chunk, rem = n % chunk;
+    int c = full_chunks > g ? (full_chunks - g + P - 1) / P : 0;
+    int rows = c * chunk;
+    if (rem > 0 && full_chunks % P == g) rows += rem;  // the trailing partial chunk
+    return rows;
+}
+
+// Contiguous row range of pair `g` out of `total_pairs` for `n` rows.
+__host__ __device__ __forceinline__ void pair_range(int n, int g, int total_pairs, int& r0, int& r1) {
+    const int per = (n + total_pairs - 1) / total_pairs;
+    r0 = sched_min(n, g * per);
+    r1 = sched_min(n, r0 + per);
+}
+
+// Source rank of receive row j (rows sorted by source; prefix[s] = first row of source s).
+__host__ __device__ __forceinline__ int find_source(const int* prefix, int R, int j) {
+    int s = 0;
+    while (s + 1 < R && j >= prefix[s + 1]) ++s;
+    return s;
+}
+
+// Pipeline ring direction of `other` seen from `me`: 0 when `other` is my previous rank, else 1.
+// With two ranks (or one) the neighbour is both and the index is 0 on both sides.
+__host__ __device__ __forceinline__ int ring_dir(int me, int other, int num_ranks) {
+    return other == (me + num_ranks - 1) % num_ranks ? 0 : 1;
+}
+
+}  // namespace ep

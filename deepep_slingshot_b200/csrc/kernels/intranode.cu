@@ -28,6 +28,7 @@
 
 #include "../include/ep/device.cuh"
 #include "../include/ep/quant.cuh"
+#include "../include/ep/schedule.cuh"
 #include "api.h"
 
 namespace ep {
@@ -456,61 +457,9 @@ __device__ __forceinline__ void pipe_init(const PipeSmem& p) {
     }
 }
 
-// Rows are dealt to pairs in chunks of kChunk: pair g owns chunks g, g + P, g + 2P, ... so every pair
-// sees rows of every source/destination rank (receive rows are sorted by rank).
-// chunk == 0 deals contiguous ranges instead (pair g owns rows [g*per, (g+1)*per)).
-__device__ __forceinline__ int pair_row(int g, int P, int k, int chunk, int n) {
-    if (chunk == 0) return g * ((n + P - 1) / P) + k;
-    return ((k / chunk) * P + g) * chunk + (k % chunk);
-}
-// Combine push order with chunk == -1 ("wavefront"): at step k pair g serves destination
-// s = (k + g) % R, row (k / R) * P + g of that destination's segment (-1 past its end). Every pair
-// spreads its stores over all destinations (no incast), and all ranks walk each destination's tokens
-// in increasing order at the same pace, so a token's contributions from every source land close
-// together and the reducers (which take tokens in increasing order) follow the pushes instead of
-// waiting for the end of the push phase.
-__device__ __forceinline__ int wave_row(int g, int P, int k, const int* prefix, int R, int n) {
-    const int s = (k + g) % R;
-    const int i = (k / R) * P + g;
-    const int lo = min(prefix[s], n), hi = min(prefix[s + 1], n);
-    return i < hi - lo ? lo + i : -1;
-}
-__device__ __forceinline__ int wave_num_rows(int g, int P, const int* prefix, int R, int n) {
-    int rows = 0;
-    for (int s = 0; s < R; ++s) {
-        const int len = min(prefix[s + 1], n) - min(prefix[s], n);
-        if (len > g) rows += (len - g + P - 1) / P;
-    }
-    return rows;
-}
-__device__ __forceinline__ int pair_num_rows(int g, int P, int n, int chunk) {
-    if (chunk == 0) {
-        const int per = (n + P - 1) / P;
-        const int r0 = min(n, g * per);
-        return min(n, r0 + per) - r0;
-    }
-    const int full_chunks = n / chunk, rem = n % chunk;
-    int c = full_chunks > g ? (full_chunks - g + P - 1) / P : 0;
-    int rows = c * chunk;
-    if (rem > 0 && full_chunks % P == g) rows += rem;  // the trailing partial chunk
-    return rows;
-}
-
-// Contiguous row range of pair `g` out of `total_pairs` for `n` rows.
-__device__ __forceinline__ void pair_range(int n, int g, int total_pairs, int& r0, int& r1) {
-    const int per = (n + total_pairs - 1) / total_pairs;
-    r0 = min(n, g * per);
-    r1 = min(n, r0 + per);
-}
-
 // =================================================================================================
 // pull (dispatch receive): rows of my receive block are pulled from the sources' staging.
 // =================================================================================================
-__device__ __forceinline__ int find_source(const int* prefix, int R, int j) {
-    int s = 0;
-    while (s + 1 < R && j >= prefix[s + 1]) ++s;
-    return s;
-}
 
 __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];

@@ -10,6 +10,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "../include/ep/schedule.cuh"
 #include "../kernels/symmetric_ops.h"
 #include "buffer.hpp"
 
@@ -26,10 +27,6 @@ namespace ep {
 namespace {
 
 int64_t align_to(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
-
-// Ring direction of `other` seen from `me`: 0 when `other` is my previous rank, else 1. With two
-// ranks (or one) the neighbour is both and the index is 0 on both sides.
-int ring_dir(int me, int other, int num_ranks) { return other == (me + num_ranks - 1) % num_ranks ? 0 : 1; }
 
 }  // namespace
 

@@ -270,7 +270,8 @@ class ElasticBuffer:
 
     def pp_set_config(self, num_max_tensor_bytes: int, num_max_inflight_tensors: int) -> None:
         """(Experimental) Size the pipeline ring: `num_max_inflight_tensors` receive slots of
-        `num_max_tensor_bytes` per neighbour (collective; includes a barrier)."""
+        `num_max_tensor_bytes` per neighbour (collective; includes a barrier). A send waits for a free
+        slot; with one or two ranks the previous and next rank are the same and share one ring."""
         slot = align(num_max_tensor_bytes, 128)
         self._pp = self._side_region('pp', 2 * slot * num_max_inflight_tensors)
         self._pp.pp_set_config(num_max_tensor_bytes, num_max_inflight_tensors)

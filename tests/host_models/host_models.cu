@@ -1,0 +1,208 @@
+// Host models of device-side logic (no GPU needed; compiled by nvcc for the host).
+//
+// The scheduling and LogFMT helpers below are the same __host__ __device__ functions the kernels
+// call (csrc/include/ep/schedule.cuh, logfmt.cuh), so these checks exercise the production code:
+//   1. row dealing of the pull / push pipelines covers every row exactly once and every loop ends;
+//   2. the pipeline-ring credit protocol (counters, slots, ring directions) delivers every message in
+//      order, never overwrites an unconsumed slot and never deadlocks, under random interleavings;
+//   3. LogFMT-10 packing round-trips and the code -> value mapping stays within its error bound.
+// Prints "ALL OK" and exits 0 on success.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <deque>
+#include <random>
+#include <vector>
+
+#include "../../deepep_slingshot_b200/csrc/include/ep/logfmt.cuh"
+#include "../../deepep_slingshot_b200/csrc/include/ep/schedule.cuh"
+
+#define CHECK(cond, ...)                                   \
+    do {                                                   \
+        if (!(cond)) {                                     \
+            std::printf("FAILED %s:%d: ", __FILE__, __LINE__); \
+            std::printf(__VA_ARGS__);                      \
+            std::printf("\n");                             \
+            std::exit(1);                                  \
+        }                                                  \
+    } while (0)
+
+static void check_dealing(std::mt19937& rng) {
+    for (int trial = 0; trial < 4000; ++trial) {
+        const int R = 1 + rng() % 8;
+        const int P = std::vector<int>{1, 2, 4, 16, 128, 296}[rng() % 6];
+        std::vector<int> prefix(R + 1, 0);
+        for (int s = 0; s < R; ++s) {
+            const int kind = rng() % 4;
+            const int len = kind == 0 ? 0 : kind == 1 ? 1 + rng() % 5 : rng() % 3000;
+            prefix[s + 1] = prefix[s] + len;
+        }
+        const int n = (rng() % 4 == 0) ? (int)(rng() % (prefix[R] + 1)) : prefix[R];
+        // wavefront (combine push)
+        std::vector<int> owner(n, -1);
+        for (int g = 0; g < P; ++g) {
+            const int rows = ep::wave_num_rows(g, P, prefix.data(), R, n);
+            int c = 0;
+            for (int k = 0; c < rows; ++k) {
+                CHECK(k < 100000000, "wave loop does not end (g=%d)", g);
+                const int j = ep::wave_row(g, P, k, prefix.data(), R, n);
+                if (j < 0) continue;
+                CHECK(j < n && owner[j] == -1, "wave row %d dealt twice", j);
+                owner[j] = g;
+                ++c;
+            }
+        }
+        for (int j = 0; j < n; ++j) CHECK(owner[j] >= 0, "wave row %d never dealt (R=%d P=%d)", j, R, P);
+        // chunked / contiguous (pull, combine with chunk >= 0)
+        for (int chunk : {0, 1, 8, 33}) {
+            std::vector<int> seen(n, 0);
+            for (int g = 0; g < P; ++g) {
+                const int rows = ep::pair_num_rows(g, P, n, chunk);
+                for (int k = 0; k < rows; ++k) {
+                    const int j = ep::pair_row(g, P, k, chunk, n);
+                    CHECK(j >= 0 && j < n, "pair_row out of range (chunk %d)", chunk);
+                    seen[j]++;
+                }
+            }
+            for (int j = 0; j < n; ++j) CHECK(seen[j] == 1, "chunk %d: row %d dealt %d times", chunk, j, seen[j]);
+        }
+        for (int j = 0; j < prefix[R]; ++j) {
+            const int s = ep::find_source(prefix.data(), R, j);
+            CHECK(prefix[s] <= j && j < prefix[s + 1], "find_source(%d) = %d", j, s);
+        }
+    }
+    std::printf("dealing ok\n");
+}
+
+// Pipeline ring: the counters and credit rule of pp_copy_kernel, the slot sets chosen with
+// ring_dir as in SymmetricRegion::pp_send / pp_recv.
+struct RankState {
+    int send_count[2] = {0, 0}, recv_count[2] = {0, 0};
+    int arrival[2] = {0, 0}, release[2] = {0, 0};
+    std::vector<long> slots[2];  // message id per slot, -1 = free
+};
+
+static void check_pp_ring(std::mt19937& rng) {
+    for (int trial = 0; trial < 3000; ++trial) {
+        const int R = 1 + rng() % 8, msgs = 1 + rng() % 12;
+        // With one or two ranks both neighbours are the same rank and share one slot ring, so the two
+        // sends of an iteration need two slots (fewer would block the stream, as on the GPU).
+        const int inflight = (R <= 2 ? 2 : 1) + rng() % 3;
+        std::vector<RankState> st(R);
+        for (auto& s : st)
+            for (int d = 0; d < 2; ++d) s.slots[d].assign(inflight, -1);
+        // program per rank: per message: send next, send prev, recv prev, recv next (stream order)
+        struct Op { int kind, peer; };  // kind 0 send, 1 recv
+        std::vector<std::vector<Op>> prog(R);
+        for (int r = 0; r < R; ++r) {
+            const int prev = (r + R - 1) % R, next = (r + 1) % R;
+            for (int m = 0; m < msgs; ++m) {
+                prog[r].push_back({0, next});
+                prog[r].push_back({0, prev});
+                prog[r].push_back({1, prev});
+                prog[r].push_back({1, next});
+            }
+        }
+        // sent[src][dst] = FIFO of message ids in flight from src to dst (per slot set)
+        std::vector<std::vector<std::deque<long>>> fifo(R, std::vector<std::deque<long>>(R));
+        std::vector<size_t> pc(R, 0);
+        long next_id = 0;
+        int idle = 0;
+        while (true) {
+            bool all_done = true;
+            for (int r = 0; r < R; ++r) all_done &= pc[r] == prog[r].size();
+            if (all_done) break;
+            const int r = rng() % R;
+            if (pc[r] == prog[r].size()) continue;
+            const Op op = prog[r][pc[r]];
+            bool progressed = false;
+            if (op.kind == 0) {
+                const int dst = op.peer, ds = ep::ring_dir(r, dst, R), dr = ep::ring_dir(dst, r, R);
+                const int c = st[r].send_count[ds];
+                if (st[r].release[ds] - (c + 1 - inflight) >= 0) {  // credit rule of the kernel
+                    long& slot = st[dst].slots[dr][(unsigned)c % (unsigned)inflight];
+                    CHECK(slot == -1, "send %d->%d overwrites an unconsumed slot", r, dst);
+                    slot = next_id;
+                    fifo[r][dst].push_back(next_id++);
+                    st[dst].arrival[dr] += 1;
+                    st[r].send_count[ds] = c + 1;
+                    progressed = true;
+                }
+            } else {
+                const int src = op.peer, dr = ep::ring_dir(r, src, R), ds = ep::ring_dir(src, r, R);
+                const int c = st[r].recv_count[dr];
+                if (st[r].arrival[dr] - (c + 1) >= 0) {
+                    long& slot = st[r].slots[dr][(unsigned)c % (unsigned)inflight];
+                    CHECK(slot != -1, "recv %d<-%d reads an empty slot", r, src);
+                    // with two ranks both neighbours are one rank: the slot set is shared, FIFO per pair
+                    CHECK(!fifo[src][r].empty() && fifo[src][r].front() == slot, "recv %d<-%d out of order", r, src);
+                    fifo[src][r].pop_front();
+                    slot = -1;
+                    st[src].release[ds] += 1;
+                    st[r].recv_count[dr] = c + 1;
+                    progressed = true;
+                }
+            }
+            if (progressed) {
+                ++pc[r];
+                idle = 0;
+            } else {
+                CHECK(++idle < 100000, "pipeline ring deadlock (R=%d inflight=%d)", R, inflight);
+            }
+        }
+        for (int a = 0; a < R; ++a)
+            for (int b = 0; b < R; ++b) CHECK(fifo[a][b].empty(), "undelivered messages %d->%d", a, b);
+    }
+    std::printf("pipeline ring ok\n");
+}
+
+static void check_logfmt(std::mt19937& rng) {
+    // packing round trip
+    for (int trial = 0; trial < 20000; ++trial) {
+        uint32_t c[8], out[8];
+        uint8_t bytes[10];
+        for (int i = 0; i < 8; ++i) c[i] = rng() & 0x3ffu;
+        ep::logfmt_pack4(c, bytes);
+        ep::logfmt_pack4(c + 4, bytes + 5);
+        uint16_t words[5];
+        for (int i = 0; i < 5; ++i) words[i] = (uint16_t)(bytes[2 * i] | (bytes[2 * i + 1] << 8));
+        ep::logfmt_unpack8(words, out);
+        for (int i = 0; i < 8; ++i) CHECK(out[i] == c[i], "pack/unpack code %d: %u != %u", i, out[i], c[i]);
+    }
+    // code -> value: nearest level in linear space, within one step of relative error
+    std::uniform_real_distribution<float> u(0.f, 1.f);
+    for (int trial = 0; trial < 2000; ++trial) {
+        const float amax = std::ldexp(0.5f + 0.5f * u(rng), -(int)(rng() % 20));  // below 1
+        const float amin = amax * std::ldexp(u(rng) + 1e-3f, -(int)(rng() % 40));
+        const ep::LogFmtGroup p = ep::logfmt_params(amax, amin);
+        if (!p.cast) continue;
+        const float inv = 1.0f / p.step;
+        const float up = log2f((1.0f + exp2f(p.step)) * 0.5f) * inv;
+        uint32_t last = 0;
+        for (int i = 0; i <= 200; ++i) {
+            const float v = amin + (amax - amin) * (float)i / 200.f;
+            const uint32_t code = ep::logfmt_code(v, p, inv, up);
+            CHECK((code >> 9) == 0, "positive value got a sign bit");
+            CHECK((code & 511u) >= (last & 511u), "codes not monotonic");
+            last = code;
+            const float back = ep::logfmt_value(code, p);
+            if (v >= exp2f(p.log_amin)) {  // values below the clamped range flush towards zero by design
+                const float rel = std::fabs(back - v) / v;
+                CHECK(rel <= exp2f(p.step) - 1.f + 1e-5f, "relative error %g above the level spacing", rel);
+            }
+            const uint32_t neg = ep::logfmt_code(-v, p, inv, up);
+            CHECK(neg == (code | (v != 0.f ? 512u : 0u)) || (v == 0.f && neg == 512u), "sign handling");
+        }
+        CHECK(ep::logfmt_code(0.f, p, inv, up) == 0 && ep::logfmt_value(0, p) == 0.f, "zero encodes to code 0");
+    }
+    std::printf("logfmt ok\n");
+}
+
+int main() {
+    std::mt19937 rng(12345);
+    check_dealing(rng);
+    check_pp_ring(rng);
+    check_logfmt(rng);
+    std::printf("ALL OK\n");
+    return 0;
+}
