@@ -11,13 +11,20 @@ the same position).
 Other routings: `uniform` (top-k of uniform logits), `hot_rank` (every token on rank 0's first
 experts: the other ranks receive nothing), `self` (every token stays on its own rank: no NVLink
 traffic), `remote` (two destinations, never the source rank).
+
+Count-driven routings (the reference replays per-expert counts of real traces,
+backend/tests/bank_routing.py:25-61; the trace data itself is not part of this library):
+`routes_from_counts` realises exact per-expert counts as a top-k table with distinct experts per
+token, `greedy_placement` / `random_placement` map logical experts to physical ids. Names:
+`zipf<s>[_greedy|_random]` (Zipf(s) expert popularity per rank) and `counts:<file.npy>[:greedy|:random]`
+(a [ranks, experts] array of per-rank counts, e.g. from a router trace).
 """
 from typing import Tuple
 
 import numpy as np
 import torch
 
-ROUTINGS = ['uniform', 'mixed', 'skew1.5', 'skew2', 'skew4', 'hot_rank', 'self', 'remote']
+ROUTINGS = ['uniform', 'mixed', 'skew1.5', 'skew2', 'skew4', 'hot_rank', 'self', 'remote', 'zipf1.1', 'zipf1.1_greedy']
 
 
 def skew_routes(num_tokens: int, num_ranks: int, num_experts: int, num_topk: int, skew: float, seed: int,
@@ -60,6 +67,102 @@ def skew_routes(num_tokens: int, num_ranks: int, num_experts: int, num_topk: int
     return idx.astype(np.int64), matrix
 
 
+def routes_from_counts(counts, num_tokens: int, num_topk: int, seed: int) -> np.ndarray:
+    """`[num_tokens, num_topk]` expert ids whose histogram is exactly `counts` (sum <= tokens*topk, each
+    count <= tokens), distinct experts per token; missing assignments are -1. A cursor walks the token
+    positions cyclically and each expert (random order) takes its count of consecutive positions, so
+    every position is visited exactly `num_topk` times and no expert meets a token twice; tokens are
+    then shuffled."""
+    counts = np.asarray(counts, dtype=np.int64)
+    n, k = num_tokens, num_topk
+    deficit = n * k - int(counts.sum())
+    if deficit < 0 or (counts.size and counts.max() > n) or deficit > n * k:
+        raise ValueError('counts must sum to at most tokens * topk with no count above tokens')
+    rng = np.random.default_rng(seed)
+    full = np.append(counts, deficit)  # last entry: the "no expert" filler
+    table = np.full((n, k), -1, dtype=np.int64)
+    fill = np.zeros(n, dtype=np.int64)
+    cursor = 0
+    for e in rng.permutation(full.size):
+        left = int(full[e])
+        while left > 0:  # only the filler can exceed n; it may repeat a token (several -1 entries)
+            c = min(left, n)
+            pos = (cursor + np.arange(c)) % n
+            table[pos, fill[pos]] = e if e < counts.size else -1
+            fill[pos] += 1
+            cursor = (cursor + c) % n
+            left -= c
+    assert (fill == k).all()
+    return table[rng.permutation(n)]
+
+
+def greedy_placement(load, experts_per_rank: int) -> np.ndarray:
+    """perm[logical expert] = physical expert id: experts by decreasing load, each onto the
+    least-loaded rank with a free slot (balanced partition, no replicas)."""
+    load = np.asarray(load, dtype=np.float64)
+    ranks = load.size // experts_per_rank
+    rank_load = np.zeros(ranks)
+    fill = np.zeros(ranks, dtype=np.int64)
+    perm = np.empty(load.size, dtype=np.int64)
+    for e in np.argsort(-load, kind='stable'):
+        free = np.nonzero(fill < experts_per_rank)[0]
+        r = free[np.argmin(rank_load[free])]
+        perm[e] = r * experts_per_rank + fill[r]
+        fill[r] += 1
+        rank_load[r] += load[e]
+    return perm
+
+
+def random_placement(num_experts: int, seed: int) -> np.ndarray:
+    return np.random.default_rng(seed).permutation(num_experts)
+
+
+def zipf_counts(num_experts: int, num_tokens: int, num_topk: int, s: float, seed: int) -> np.ndarray:
+    """Per-expert counts summing to tokens * topk with Zipf(s) popularity over a random expert order,
+    capped at `num_tokens` per expert (overflow redistributed)."""
+    rng = np.random.default_rng(seed)
+    w = 1.0 / np.arange(1, num_experts + 1) ** s
+    w = w[rng.permutation(num_experts)]
+    total = num_tokens * num_topk
+    counts = np.floor(w / w.sum() * total).astype(np.int64)
+    counts[np.argsort(-w)[: total - counts.sum()]] += 1
+    while counts.max() > num_tokens:
+        over = counts - num_tokens
+        spill = int(over[over > 0].sum())
+        counts = np.minimum(counts, num_tokens)
+        room = num_tokens - counts
+        order = np.argsort(room)[::-1]
+        for e in order:
+            take = min(int(room[e]), spill)
+            counts[e] += take
+            spill -= take
+            if spill == 0:
+                break
+    return counts
+
+
+def _count_routing(name: str, rank: int, num_ranks: int, N: int, E: int, K: int, seed: int) -> torch.Tensor:
+    placement = None
+    if name.startswith('counts:'):
+        parts = name.split(':')
+        all_counts = np.load(parts[1])
+        counts = np.asarray(all_counts[rank % all_counts.shape[0]], dtype=np.int64)
+        placement = parts[2] if len(parts) > 2 else None
+        load = np.asarray(all_counts, dtype=np.float64).sum(0)
+    else:
+        base, _, placement = name.partition('_')
+        s = float(base[4:])
+        counts = zipf_counts(E, N, K, s, seed * 100 + rank)
+        load = sum(zipf_counts(E, N, K, s, seed * 100 + r) for r in range(num_ranks)).astype(np.float64)
+    if counts.size != E:
+        raise ValueError(f'counts have {counts.size} experts, the model has {E}')
+    idx = routes_from_counts(counts, N, K, seed * 1000 + rank)
+    if placement in ('greedy', 'random'):
+        perm = greedy_placement(load, E // num_ranks) if placement == 'greedy' else random_placement(E, seed)
+        idx = np.where(idx >= 0, np.append(perm, -1)[idx], -1)
+    return torch.from_numpy(idx.astype(np.int64))
+
+
 def make_routing(name: str, rank: int, num_ranks: int, num_tokens: int, num_experts: int, num_topk: int,
                  seed: int) -> torch.Tensor:
     """This rank's `[num_tokens, num_topk]` int64 expert ids for routing `name` (CPU tensor)."""
@@ -75,6 +178,8 @@ def make_routing(name: str, rank: int, num_ranks: int, num_tokens: int, num_expe
         assert K <= le
         g = torch.Generator().manual_seed(seed * 100 + rank)
         return (torch.rand((N, le), generator=g).topk(K, dim=1).indices + rank * le).to(torch.int64)
+    if name.startswith('zipf') or name.startswith('counts:'):
+        return _count_routing(name, rank, R, N, E, K, seed)
     if R == 1:
         raise ValueError(f'routing {name} needs at least two ranks')
     if name == 'mixed':

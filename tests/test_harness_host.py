@@ -65,3 +65,41 @@ def test_trace_decode_and_chrome():
     assert s['dispatch.pull']['count'] == 2 and s['dispatch.pull']['union_us'] == 1.5
     tr = to_chrome_trace({0: out}, {0: 0})
     assert len(tr['traceEvents']) == 3 and tr['traceEvents'][0]['ts'] == 0.0
+
+
+def test_routes_from_counts_exact():
+    from deepep_slingshot_b200.harness.routing import routes_from_counts, zipf_counts
+    for seed in range(5):
+        counts = zipf_counts(256, 4096, 6, 1.2, seed)
+        assert counts.sum() == 4096 * 6 and counts.max() <= 4096
+        idx = routes_from_counts(counts, 4096, 6, seed)
+        assert idx.shape == (4096, 6)
+        assert (np.bincount(idx[idx >= 0], minlength=256) == counts).all()
+        s = np.sort(idx, axis=1)
+        assert ((np.diff(s, axis=1) != 0) | (s[:, 1:] < 0)).all()  # distinct experts per token
+    # a deficit becomes -1 entries (tokens routed to fewer than k experts)
+    idx = routes_from_counts(np.array([3, 3, 2]), 4, 2, 0)
+    assert (idx == -1).sum() == 0 and np.bincount(idx.ravel(), minlength=3).tolist() == [3, 3, 2]
+    idx = routes_from_counts(np.array([2, 1]), 4, 2, 0)
+    assert (idx == -1).sum() == 5
+
+
+def test_placements_and_count_routing():
+    from deepep_slingshot_b200.harness.routing import greedy_placement, make_routing, route_matrix
+    load = np.array([10, 1, 1, 1, 9, 1, 1, 1], dtype=np.float64)
+    perm = greedy_placement(load, 4)
+    assert sorted(perm.tolist()) == list(range(8))
+    assert (perm[0] // 4) != (perm[4] // 4)  # the two hot experts land on different ranks
+    a = make_routing('zipf1.1', 0, 8, 512, 256, 8, 0)
+    b = make_routing('zipf1.1_greedy', 0, 8, 512, 256, 8, 0)
+    assert a.shape == b.shape == (512, 8)
+    # greedy placement balances the group-wide expert load (assignments of every rank's tokens)
+    def group_load(name):
+        tot = np.zeros(8, dtype=np.int64)
+        for r in range(8):
+            t = make_routing(name, r, 8, 512, 256, 8, 0).numpy()
+            tot += np.bincount(t[t >= 0] // 32, minlength=8)
+        return tot
+    la, lb = group_load('zipf1.1'), group_load('zipf1.1_greedy')
+    assert la.sum() == lb.sum() and lb.max() / lb.mean() < la.max() / la.mean()
+    assert route_matrix(b.numpy(), 8, 256).sum() > 0
