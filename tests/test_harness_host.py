@@ -103,3 +103,54 @@ def test_placements_and_count_routing():
     la, lb = group_load('zipf1.1'), group_load('zipf1.1_greedy')
     assert la.sum() == lb.sum() and lb.max() / lb.mean() < la.max() / la.mean()
     assert route_matrix(b.numpy(), 8, 256).sum() > 0
+
+
+def _write_results(d, world=2, fail_rank=None, drop_timing=None, sources=None):
+    import json as _json
+    for r in range(world):
+        man = {'kind': 'manifest', 'rank': r, 'world': world, 'sources': sources[r] if sources else {'a.py': 'x'}}
+        (d / f'manifest-rank{r}.jsonl').write_text(_json.dumps(man) + '\n')
+        case = {'model': 'qwen3', 'tokens_per_rank': 512, 'dispatch_dtype': 'fp8', 'routing': 'mixed', 'seed': 0}
+        cor = dict(case, kind='correctness', passed=(r != fail_rank))
+        (d / f'correctness-rank{r}.jsonl').write_text(_json.dumps(cor) + '\n')
+        lines = []
+        for op in ('dispatch', 'cached_dispatch', 'combine'):
+            if drop_timing == (r, op):
+                continue
+            lines.append(_json.dumps(dict(case, kind='timing', op=op, ranks=world, bytes=100, rank_max_us=[10.0, 11.0],
+                                          max_host_us_per_iteration=5.0)))
+        (d / f'timings-rank{r}.jsonl').write_text('\n'.join(lines) + '\n')
+
+
+def test_validate_results(tmp_path):
+    from deepep_slingshot_b200.harness.summarize import summarize_dir
+    from deepep_slingshot_b200.harness.validate import validate
+    good = tmp_path / 'good'
+    good.mkdir()
+    _write_results(good)
+    summarize_dir(str(good))
+    assert validate(str(good), ranks=2) == []
+    bad = tmp_path / 'bad'
+    bad.mkdir()
+    _write_results(bad, fail_rank=1, drop_timing=(0, 'combine'), sources=[{'a.py': 'x'}, {'a.py': 'y'}])
+    summarize_dir(str(bad))
+    probs = validate(str(bad), ranks=2)
+    text = '\n'.join(probs)
+    assert 'source hashes differ' in text and 'correctness failed' in text
+    assert validate(str(tmp_path / 'missing')) != []
+
+
+def test_kernel_summary_aggregates_device_events():
+    import torch
+    from deepep_slingshot_b200.harness.profile_capture import kernel_summary
+
+    class Ev:
+        def __init__(self, name, dev, t):
+            self.name, self.device_type, self.device_time_total = name, dev, t
+
+    cuda, cpu = torch.autograd.DeviceType.CUDA, torch.autograd.DeviceType.CPU
+    rows = kernel_summary([Ev('pull', cuda, 30.0), Ev('pull', cuda, 10.0), Ev('combine', cuda, 60.0),
+                           Ev('python', cpu, 999.0)], steps=2)
+    assert [r['kernel'] for r in rows] == ['combine', 'pull']
+    assert rows[1]['calls'] == 2 and rows[1]['mean_us'] == 20.0 and rows[1]['per_step_us'] == 20.0
+    assert abs(rows[0]['share'] - 0.6) < 1e-9
