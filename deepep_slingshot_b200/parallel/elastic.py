@@ -100,6 +100,34 @@ class ElasticBuffer:
     def get_elastic_buffer_alignment() -> int:
         return 2 << 20
 
+    # Size hints of the experimental side features (their regions: [64 KiB control | data], 2 MiB
+    # aligned; the reference carves the same features out of its one symmetric window).
+    @staticmethod
+    def get_engram_storage_size_hint(num_entries: int, hidden: int, num_max_tokens_per_rank: int,
+                                     dtype: torch.dtype = torch.bfloat16) -> Tuple[int, int]:
+        """(fetch receive bytes, storage bytes), each 2 MiB aligned. Rows are bf16 here; the fetched
+        rows land in a fresh tensor, the storage lives in GPU memory."""
+        row = align(hidden * dtype.itemsize, 32)
+        a = ElasticBuffer.get_elastic_buffer_alignment()
+        return align(row * num_max_tokens_per_rank, a), align(64 * 1024 + row * num_entries, a)
+
+    @staticmethod
+    def get_pp_buffer_size_hint(num_max_tensor_bytes: int, num_max_inflight_tensors: int) -> int:
+        """Bytes of the pipeline region: a receive slot ring per neighbour (two neighbours)."""
+        slot = align(num_max_tensor_bytes, 128)
+        return align(64 * 1024 + 2 * slot * num_max_inflight_tensors, ElasticBuffer.get_elastic_buffer_alignment())
+
+    @staticmethod
+    def get_agrs_num_max_session_bytes(group: dist.ProcessGroup, shapes, dtype: torch.dtype) -> int:
+        """Session bytes that all-gathers of these local shapes use (each gathered tensor 32-byte aligned)."""
+        if not isinstance(shapes[0], (tuple, list, torch.Size)):
+            shapes = (shapes,)
+        return sum(align(group.size() * math.prod(s) * dtype.itemsize, 32) for s in shapes)
+
+    @staticmethod
+    def get_agrs_buffer_size_hint(group: dist.ProcessGroup, num_max_session_bytes: int) -> int:
+        return align(64 * 1024 + num_max_session_bytes, ElasticBuffer.get_elastic_buffer_alignment())
+
     def barrier(self, use_comm_stream: bool = True, with_cpu_sync: bool = False) -> None:
         self._buffer.barrier(use_comm_stream, with_cpu_sync)
 

@@ -76,3 +76,49 @@ def nvidia_smi_clocks() -> Optional[str]:
                                        text=True, timeout=10)
     except Exception:
         return None
+
+
+_SEEDS = {'local': None, 'global': None}
+
+
+def init_seed(global_seed: int) -> None:
+    """Seed torch / random with `global_seed + rank` (the local seed) for reproducible runs."""
+    import random
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    _SEEDS['global'], _SEEDS['local'] = global_seed, global_seed + rank
+    torch.manual_seed(global_seed + rank)
+    random.seed(global_seed + rank)
+
+
+def get_local_seed() -> Optional[int]:
+    return _SEEDS['local']
+
+
+def get_global_seed() -> Optional[int]:
+    return _SEEDS['global']
+
+
+def dist_print(s: str = '', once_in_node: bool = False) -> None:
+    """Print from every rank (or only local rank 0 with `once_in_node`), then barrier."""
+    local_rank = int(os.environ.get('LOCAL_RANK', dist.get_rank() if dist.is_initialized() else 0))
+    if not once_in_node or local_rank == 0:
+        print(s, flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+
+
+def get_physical_domain_size(group: dist.ProcessGroup) -> Tuple[int, int]:
+    """(RDMA ranks, NVLink ranks): one NVLink domain here."""
+    return 1, group.size()
+
+
+def get_logical_domain_size(group: dist.ProcessGroup, allow_hybrid_mode: bool = True) -> Tuple[int, int]:
+    """(scale-out ranks, scale-up ranks): one NVLink domain here."""
+    return 1, group.size()
+
+
+def check_torch_deterministic() -> None:
+    """Deterministic algorithms together with `fill_uninitialized_memory` make `torch.empty` launch an
+    initialisation kernel that can overlap with communication: refuse that combination."""
+    import torch.utils.deterministic
+    assert not (torch.are_deterministic_algorithms_enabled() and torch.utils.deterministic.fill_uninitialized_memory)

@@ -47,15 +47,124 @@ def zipf_routing(num_tokens: int, num_experts: int, num_topk: int, s: float = 1.
     return _select(scores, num_topk)
 
 
-def get_unbalanced_scores(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, ratio: float = 1.0,
-                          generator: Optional[torch.Generator] = None) -> torch.Tensor:
-    """Scores whose rank-level load is skewed by `ratio` (1.0 = balanced): the first rank's experts get
-    their logits lifted so it receives about `ratio` times the average traffic."""
-    scores = torch.randn((num_tokens, num_experts), generator=generator).abs() + 1
-    if ratio > 1.0:
-        epr = num_experts // num_ranks
-        scores[:, :epr] *= ratio
+def get_scores_by_factor(num_tokens: int, num_experts: int, num_ranks: int, factor: float,
+                         generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    """Router scores where rank 0's experts draw from U(0, factor) and all others from U(0, 1): a
+    factor above 1 makes rank 0 hot."""
+    epr = num_experts // num_ranks
+    scores = torch.rand((num_tokens, num_experts), generator=generator)
+    scores[:, :epr] *= factor
     return scores
+
+
+def _rank0_ratio(scores: torch.Tensor, num_ranks: int, num_topk: int) -> float:
+    epr = scores.shape[1] // num_ranks
+    ranks = torch.topk(scores, num_topk, dim=-1).indices // epr
+    hit = torch.zeros((scores.shape[0], num_ranks), dtype=torch.bool)
+    hit.scatter_(1, ranks, True)
+    per_rank = hit.float().sum(0)
+    return float(per_rank[0] / per_rank[1:].mean().clamp_min(1e-9))
+
+
+def map_unbalanced_ratio_to_factor(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, ratio: float,
+                                   generator: Optional[torch.Generator] = None, iterations: int = 20) -> float:
+    """Bisection for the score factor whose top-k routing sends rank 0 about `ratio` times the tokens
+    of an average other rank."""
+    lo, hi = 1.0, 100.0
+    for _ in range(iterations):
+        mid = (lo + hi) / 2
+        r = _rank0_ratio(get_scores_by_factor(num_tokens, num_experts, num_ranks, mid, generator), num_ranks, num_topk)
+        if r > ratio:
+            hi = mid
+        else:
+            lo = mid
+    return lo
+
+
+def get_random_unbalanced_scores(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, ratio: float,
+                                 generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    """Random scores whose top-k makes rank 0 receive about `ratio` times the average traffic."""
+    factor = 1.0 if ratio == 1.0 else map_unbalanced_ratio_to_factor(num_tokens, num_experts, num_ranks, num_topk,
+                                                                     ratio, generator)
+    return get_scores_by_factor(num_tokens, num_experts, num_ranks, factor, generator)
+
+
+def generate_rank_count(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, ratio: float,
+                        generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    """`[num_tokens, num_ranks]` int32: how many of token t's top-k experts live on rank r, with every
+    row summing to `num_topk`, and rank 0 (the special rank) holding experts of `ratio` times as many
+    tokens as an average other rank (exact up to rounding). Each token spreads over as many distinct
+    ranks as uniform top-k routing would give it (capped so the special rank's share stays reachable);
+    the special rank is put on the chosen number of tokens, the other rank slots are dealt round-robin
+    over a random order of the other ranks."""
+    assert ratio >= 1.0 and num_ranks >= 1
+    R, N, K = num_ranks, num_tokens, num_topk
+    epr = num_experts // R
+    if R == 1:
+        return torch.full((N, 1), K, dtype=torch.int32)
+    # distinct ranks per token under uniform top-k, capped so the special rank's share is reachable
+    ranks = torch.topk(torch.rand((N, num_experts), generator=generator), K, dim=-1).indices // epr
+    hit = torch.zeros((N, R), dtype=torch.bool)
+    hit.scatter_(1, ranks, True)
+    cap = min(R, int((R - 1) / ratio) + 1)
+    spread = hit.sum(1).clamp(min=max(1, -(-K // epr)), max=cap)
+    total = int(spread.sum())
+    must = spread == R  # a token on every rank includes the special rank
+    special = round(total * ratio / (R - 1 + ratio))
+    special = min(N, max(int(must.sum()), special))
+    rest = torch.nonzero(~must).flatten()
+    rest = rest[torch.randperm(rest.numel(), generator=generator)]
+    with_special = must.clone()
+    with_special[rest[:special - int(must.sum())]] = True
+    counts = torch.zeros((N, R), dtype=torch.int32)
+    normal = (torch.randperm(R - 1, generator=generator) + 1).tolist()
+    cursor = 0
+    spread_l, special_l = spread.tolist(), with_special.tolist()
+    for t in range(N):
+        a = spread_l[t]
+        picks = [0] if special_l[t] else []
+        seen = set(picks)
+        while len(picks) < a:  # a - len(picks) <= R - 1 distinct normal ranks always exist
+            r = normal[cursor % (R - 1)]
+            cursor += 1
+            if r not in seen:
+                seen.add(r)
+                picks.append(r)
+        for i in range(K):  # the k experts over the picked ranks, at most epr per rank
+            counts[t, picks[i % a]] += 1
+    return counts
+
+
+def generate_topk_idx(rank_count: torch.Tensor, num_tokens: int, num_experts: int, num_ranks: int, num_topk: int,
+                      generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    """Expert ids realising `rank_count`: `rank_count[t, r]` distinct random experts of rank r per token."""
+    assert tuple(rank_count.shape) == (num_tokens, num_ranks)
+    assert bool((rank_count.sum(1) == num_topk).all())
+    epr = num_experts // num_ranks
+    perm = torch.argsort(torch.rand((num_tokens, num_ranks, epr), generator=generator), dim=-1)
+    experts = perm + torch.arange(num_ranks).view(1, num_ranks, 1) * epr
+    take = torch.arange(epr).view(1, 1, epr) < rank_count.cpu().view(num_tokens, num_ranks, 1)
+    return experts[take].view(num_tokens, num_topk).to(torch.int64)
+
+
+def get_precise_unbalanced_scores(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, ratio: float,
+                                  generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    """Scores whose top-k follows `generate_rank_count` exactly: chosen experts score in (0.9, 1],
+    the rest in [0, 0.9)."""
+    counts = generate_rank_count(num_tokens, num_experts, num_ranks, num_topk, ratio, generator)
+    idx = generate_topk_idx(counts, num_tokens, num_experts, num_ranks, num_topk, generator)
+    scores = torch.rand((num_tokens, num_experts), generator=generator) * 0.9
+    top = 0.9 + 1e-6 + torch.rand((num_tokens, num_topk), generator=generator) * (0.1 - 1e-6)
+    scores.scatter_(1, idx, top)
+    return scores
+
+
+def get_unbalanced_scores(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, ratio: float = 1.0,
+                          precise: bool = False, generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    """Router scores with rank 0 receiving about (`precise`: exactly) `ratio` times the average traffic."""
+    if precise:
+        return get_precise_unbalanced_scores(num_tokens, num_experts, num_ranks, num_topk, ratio, generator)
+    return get_random_unbalanced_scores(num_tokens, num_experts, num_ranks, num_topk, ratio, generator)
 
 
 def hot_rank_routing(num_tokens: int, num_experts: int, num_ranks: int, num_topk: int, hot_rank: int = 0,

@@ -131,3 +131,23 @@ def count_bytes(*tensors) -> int:
         elif t is not None:
             total += t.numel() * t.element_size()
     return total
+
+
+def create_grouped_scores(scores: torch.Tensor, group_idx: torch.Tensor, num_groups: int) -> torch.Tensor:
+    """Zero the scores of every expert group a token did not select (group-limited routing):
+    `scores [N, E]` viewed as `[N, num_groups, E / num_groups]`, `group_idx [N, g]` the kept groups."""
+    n, e = scores.shape
+    keep = torch.zeros((n, num_groups), dtype=torch.bool, device=scores.device)
+    keep.scatter_(1, group_idx, True)
+    return (scores.view(n, num_groups, -1) * keep.unsqueeze(-1)).view(n, e)
+
+
+def hash_tensors(*tensors) -> int:
+    """XOR of `hash_tensor` over tensors (nested tuples / lists allowed, None skipped)."""
+    value = 0
+    for t in tensors:
+        if isinstance(t, (tuple, list)):
+            value ^= hash_tensors(*t)
+        elif isinstance(t, torch.Tensor):
+            value ^= hash_tensor(t)
+    return value

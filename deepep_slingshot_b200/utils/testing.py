@@ -1,6 +1,8 @@
 """Timing helpers: CUDA-event benchmark with an L2 flush, per-kernel timing through the torch
 profiler, and rank-max aggregation (the reference's `bench` / `bench_kineto`,
 [DE]deep_ep/utils/testing.py:60-219, re-written for this library)."""
+import os
+import sys
 from typing import Callable, Dict, List, Optional, Sequence, Tuple, Union
 
 import torch
@@ -90,3 +92,41 @@ def hash_tensor(t: torch.Tensor) -> str:
     """SHA-256 of a tensor's bytes (inputs / routes in benchmark records)."""
     import hashlib
     return hashlib.sha256(t.detach().contiguous().cpu().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def flush_l2_cache(enabled: bool = True) -> None:
+    """Evict the GPU L2 (126 MB on B200) with a 256 MB write."""
+    if enabled:
+        _flush_buffer().zero_()
+
+
+class empty_suppress:
+    """No-op context manager (the counterpart of `suppress_stdout_stderr`)."""
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *_):
+        return False
+
+
+class suppress_stdout_stderr:
+    """Silence the process's stdout/stderr file descriptors (also output of C/C++ code) inside the block."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        sys.stderr.flush()
+        self._devnull = os.open(os.devnull, os.O_WRONLY)
+        self._saved = [os.dup(1), os.dup(2)]
+        os.dup2(self._devnull, 1)
+        os.dup2(self._devnull, 2)
+        return self
+
+    def __exit__(self, *_):
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os.dup2(self._saved[0], 1)
+        os.dup2(self._saved[1], 2)
+        for fd in self._saved + [self._devnull]:
+            os.close(fd)
+        return False

@@ -134,3 +134,48 @@ def test_ep_benchmark_byte_counts():
     assert dispatch_bytes(10, 7168, 8, True) == 10 * (7168 + 56 * 4 + 64 + 32)
     assert dispatch_bytes(10, 7168, 8, False) == 10 * (2 * 7168 + 64 + 32)
     assert combine_bytes(10, 7168, 8) == 10 * (2 * 7168 + 32)
+
+
+@pytest.mark.parametrize('ratio', [1.0, 1.5, 3.0])
+def test_precise_unbalanced_routing(ratio):
+    g = torch.Generator().manual_seed(3)
+    N, E, R, K = 2048, 256, 8, 8
+    counts = gate.generate_rank_count(N, E, R, K, ratio, generator=g)
+    assert (counts.sum(1) == K).all() and int(counts.max()) <= E // R
+    tokens_per_rank = (counts > 0).sum(0).float()
+    assert abs(float(tokens_per_rank[0] / tokens_per_rank[1:].mean()) - ratio) < 0.05 * ratio
+    idx = gate.generate_topk_idx(counts, N, E, R, K, generator=g)
+    assert idx.shape == (N, K)
+    assert (torch.sort(idx, 1).values.diff(dim=1) != 0).all()
+    back = torch.zeros((N, R), dtype=torch.int32)
+    back.scatter_add_(1, idx // (E // R), torch.ones_like(idx, dtype=torch.int32))
+    assert torch.equal(back, counts)
+    scores = gate.get_unbalanced_scores(N, E, R, K, ratio, precise=True, generator=g)
+    assert scores.shape == (N, E)
+
+
+def test_random_unbalanced_scores_ratio():
+    g = torch.Generator().manual_seed(4)
+    scores = gate.get_unbalanced_scores(4096, 256, 8, 8, 2.0, generator=g)
+    epr = 32
+    hit = torch.zeros((4096, 8), dtype=torch.bool)
+    hit.scatter_(1, torch.topk(scores, 8, dim=-1).indices // epr, True)
+    per = hit.float().sum(0)
+    assert 1.6 < float(per[0] / per[1:].mean()) < 2.4
+
+
+def test_elastic_side_feature_size_hints():
+    import torch.distributed as dist
+    from deepep_slingshot_b200.parallel.elastic import ElasticBuffer
+
+    class G:
+        def size(self):
+            return 8
+    a = ElasticBuffer.get_elastic_buffer_alignment()
+    gpu, cpu = ElasticBuffer.get_engram_storage_size_hint(1000, 4096, 128)
+    assert gpu % a == 0 and cpu % a == 0 and cpu >= 1000 * 4096 * 2
+    pp = ElasticBuffer.get_pp_buffer_size_hint(3 << 20, 2)
+    assert pp % a == 0 and pp >= 2 * 2 * (3 << 20)
+    nb = ElasticBuffer.get_agrs_num_max_session_bytes(G(), [(33, 64), (7,)], torch.bfloat16)
+    assert nb == (8 * 33 * 64 * 2 + 31) // 32 * 32 + (8 * 7 * 2 + 31) // 32 * 32
+    assert ElasticBuffer.get_agrs_buffer_size_hint(G(), nb) % a == 0

@@ -81,3 +81,60 @@ def _edge_oracle_body(rank, world):
 def test_reference_edge_cases_gloo():
     from tests._dist import run_ranks
     run_ranks(_edge_oracle_body, 2)
+
+
+def _refs_body(rank, world):
+    """Functional reference API (dispatch / generate_pre_combine_data / combine / ordered_accumulate)."""
+    import torch.distributed as dist
+    from deepep_slingshot_b200.utils import refs
+    from deepep_slingshot_b200.utils.gate import normal_routing
+    N, H, E, K, maxT = 32, 128, 8, 2, 64
+    g = torch.Generator().manual_seed(rank)
+    x = torch.randn((N, H), generator=g).to(torch.bfloat16)
+    idx, w = normal_routing(N, E, K, generator=g)
+    rx, ri, rw, gidx, per_rank = refs.dispatch(x, idx, w, maxT, E)
+    assert int(per_rank.sum()) == rx.shape[0] and torch.equal(gidx, torch.sort(gidx).values)
+    # every received row is the source token identified by its global index
+    all_x = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(all_x, x)
+    for i, gi in enumerate(gidx.tolist()):
+        assert torch.equal(rx[i], all_x[gi // maxT][gi % maxT])
+    # the same (token, k) data regenerates identically on every rank
+    y = refs.generate_pre_combine_data(torch.arange(N) + rank * maxT, maxT, K, H)
+    y2 = refs.generate_pre_combine_data(torch.arange(N) + rank * maxT, maxT, K, H)
+    assert torch.equal(y, y2) and y.shape == (N, K, H)
+    flat = refs.combine(y, idx, 1, world, E, reduce_in_local=False)
+    assert torch.equal(flat, refs.ordered_accumulate(y))
+    local = refs.combine(y, idx, 1, world, E, reduce_in_local=True)
+    assert torch.allclose(local.float(), flat.float(), atol=3e-2, rtol=2e-2)
+
+
+def test_functional_refs_gloo():
+    from tests._dist import run_ranks
+    run_ranks(_refs_body, 2)
+
+
+def test_small_helpers():
+    from deepep_slingshot_b200.utils.math import create_grouped_scores, hash_tensors
+    from deepep_slingshot_b200.utils.semantic import value_or, weak_lru
+    from deepep_slingshot_b200.utils.testing import empty_suppress, suppress_stdout_stderr
+    s = torch.arange(16, dtype=torch.float32).view(2, 8) + 1
+    gs = create_grouped_scores(s, torch.tensor([[0], [3]]), 4)
+    assert gs[0, :2].tolist() == [1.0, 2.0] and gs[0, 2:].abs().sum() == 0 and gs[1, 6:].tolist() == [15.0, 16.0]
+    a, b = torch.arange(4, dtype=torch.int32), torch.ones(3, dtype=torch.int32)
+    assert hash_tensors(a, [b, None]) == (int(a.sum()) ^ int(b.sum()))
+    assert value_or(None, 3) == 3 and value_or(0, 3) == 0
+
+    class C:
+        calls = 0
+
+        @weak_lru(maxsize=4)
+        def f(self, v):
+            C.calls += 1
+            return v * 2
+    c = C()
+    assert c.f(2) == 4 and c.f(2) == 4 and C.calls == 1
+    with suppress_stdout_stderr():
+        print('hidden')
+    with empty_suppress():
+        pass
