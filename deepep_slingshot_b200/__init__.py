@@ -9,6 +9,7 @@ import torch
 
 from ._ext import load_ext
 from .parallel import Buffer, Config, ElasticBuffer, EPHandle, ReferenceBuffer, topk_idx_t
+from .utils.envs import get_logical_domain_size, get_physical_domain_size
 from .utils.event import EventOverlap
 
 __version__ = '0.1.0'
