@@ -162,7 +162,39 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
                'max_host_us_per_iteration': host_max, 'bytes_rank_max': bytes_max}
         logs['timings'].write(rec)
         result[op] = rec
+    if args.stall_us is not None:
+        result['stall'] = _stall_loop(buf, fresh, comb, args, case, logs)
     return case, result
+
+
+def _stall_loop(buf, dispatch_fn, combine_fn, args, case, logs):
+    """Dispatch -> GPU stall of `--stall-us` (standing in for the expert GEMMs) -> combine, looped;
+    per-op device times averaged after a 20% ramp, max over ranks (the reference's stall ablation,
+    tests/elastic/test_ep_stall.py:206-258)."""
+    from ..utils.testing import rank_max
+    n = args.stall_iters
+    clock_mhz = torch.cuda.get_device_properties(torch.cuda.current_device()).clock_rate / 1e3
+    cycles = int(args.stall_us * clock_mhz)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+    buf.barrier()
+    torch.cuda.synchronize()
+    for i in range(n):
+        ev[i][0].record()
+        dispatch_fn()
+        ev[i][1].record()
+        if cycles > 0:
+            torch.cuda._sleep(cycles)
+        ev[i][2].record()
+        combine_fn()
+        ev[i][3].record()
+    torch.cuda.synchronize()
+    warm = n // 5
+    d_us = sum(ev[i][0].elapsed_time(ev[i][1]) for i in range(warm, n)) / max(1, n - warm) * 1e3
+    c_us = sum(ev[i][2].elapsed_time(ev[i][3]) for i in range(warm, n)) / max(1, n - warm) * 1e3
+    d_max, c_max = rank_max([d_us, c_us])
+    rec = {'kind': 'stall', **case, 'stall_us': args.stall_us, 'iters': n, 'dispatch_us': d_max, 'combine_us': c_max}
+    logs['timings'].write(rec)
+    return rec
 
 
 def main(argv=None):
@@ -176,6 +208,9 @@ def main(argv=None):
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--num-sms', type=int, default=0)
     p.add_argument('--out', default='ep_results')
+    p.add_argument('--stall-us', type=float, default=None,
+                   help='also run dispatch -> GPU stall -> combine loops (expert-compute stand-in)')
+    p.add_argument('--stall-iters', type=int, default=200)
     args = p.parse_args(argv)
 
     from .. import Buffer, ReferenceBuffer
@@ -210,7 +245,10 @@ def main(argv=None):
                             case, res = run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs)
                             if rank == 0:
                                 line = ', '.join(f"{op} {sorted(r['rank_max_us'])[len(r['rank_max_us']) // 2]:.1f} us"
-                                                 for op, r in res.items())
+                                                 for op, r in res.items() if op != 'stall')
+                                if 'stall' in res:
+                                    line += (f", with {args.stall_us:g} us stall: dispatch {res['stall']['dispatch_us']:.1f} us"
+                                             f" combine {res['stall']['combine_us']:.1f} us")
                                 print(f'[ep_benchmark] {model} T={tokens} {dtype} {routing} seed {seed}: {line}', flush=True)
                         except (AssertionError, ValueError) as e:
                             failures += 1

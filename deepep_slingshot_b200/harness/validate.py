@@ -76,6 +76,8 @@ def validate(out_dir: str, max_cv: float = 0.1, ranks: int = 0) -> List[str]:
             problems.append(f'missing timings-rank{r}.jsonl')
             continue
         for x in _read_jsonl(path):
+            if x.get('kind') != 'timing':
+                continue
             key = (x['model'], x['tokens_per_rank'], x['dispatch_dtype'], x['routing'], x['seed'])
             timings[key].setdefault(x['op'], {})[r] = x
     ops = ('dispatch', 'cached_dispatch', 'combine')
