@@ -154,3 +154,24 @@ def test_kernel_summary_aggregates_device_events():
     assert [r['kernel'] for r in rows] == ['combine', 'pull']
     assert rows[1]['calls'] == 2 and rows[1]['mean_us'] == 20.0 and rows[1]['per_step_us'] == 20.0
     assert abs(rows[0]['share'] - 0.6) < 1e-9
+
+
+def test_ladder_stops_and_resumes(tmp_path):
+    from deepep_slingshot_b200.harness.ladder import load_state, run_ladder
+    gates = [{'name': 'a', 'args': []}, {'name': 'b', 'args': []}, {'name': 'c', 'args': []}]
+    calls = []
+    outcome = {'a': [], 'b': ['bad'], 'c': []}
+
+    def fake(gate, d):
+        calls.append(gate['name'])
+        return outcome[gate['name']]
+    out = str(tmp_path / 'ladder')
+    assert not run_ladder(out, fake, gates)
+    assert calls == ['a', 'b'] and load_state(out + '/ladder_state.json')['failed'] == 'b'
+    assert not run_ladder(out, fake, gates)          # refuses to run without a resume reason
+    assert calls == ['a', 'b']
+    outcome['b'] = []
+    assert run_ladder(out, fake, gates, resume_reason='fixed the notify wait')
+    assert calls == ['a', 'b', 'b', 'c']             # passed gates are skipped
+    st = load_state(out + '/ladder_state.json')
+    assert st['passed'] == ['a', 'b', 'c'] and st['resumes'][0]['reason'] == 'fixed the notify wait'
