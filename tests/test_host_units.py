@@ -179,3 +179,34 @@ def test_elastic_side_feature_size_hints():
     nb = ElasticBuffer.get_agrs_num_max_session_bytes(G(), [(33, 64), (7,)], torch.bfloat16)
     assert nb == (8 * 33 * 64 * 2 + 31) // 32 * 32 + (8 * 7 * 2 + 31) // 32 * 32
     assert ElasticBuffer.get_agrs_buffer_size_hint(G(), nb) % a == 0
+
+
+def test_nvlink_gbs_with_fake_nvml(monkeypatch):
+    """NVLink bandwidth from the NVML link count (a fake NVML: reads only, nothing is changed)."""
+    import sys
+    import types
+    from deepep_slingshot_b200.utils import envs
+
+    def fake(links_up):
+        m = types.ModuleType('pynvml')
+        m.NVML_FEATURE_ENABLED = 1
+
+        class NVMLError(Exception):
+            pass
+        m.NVMLError = NVMLError
+        m.nvmlInit = lambda: None
+        m.nvmlShutdown = lambda: None
+        m.nvmlDeviceGetHandleByIndex = lambda i: 'h'
+
+        def state(h, i):
+            if i >= 18:
+                raise NVMLError()
+            return 1 if i < links_up else 0
+        m.nvmlDeviceGetNvLinkState = state
+        return m
+    monkeypatch.setitem(sys.modules, 'pynvml', fake(18))
+    assert abs(envs.get_nvlink_gbs() - envs.B200_NVLINK_GBS) < 1e-6
+    monkeypatch.setitem(sys.modules, 'pynvml', fake(9))
+    assert abs(envs.get_nvlink_gbs() - envs.B200_NVLINK_GBS / 2) < 1e-6
+    monkeypatch.setitem(sys.modules, 'pynvml', fake(0))
+    assert envs.get_nvlink_gbs() == envs.B200_NVLINK_GBS  # no links reported: measured fallback
