@@ -164,7 +164,38 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
         result[op] = rec
     if args.stall_us is not None:
         result['stall'] = _stall_loop(buf, fresh, comb, args, case, logs)
+    if args.sweep_sms:
+        result['sweep'] = _sms_sweep(buf, fresh, comb, ops, args, case, logs)
     return case, result
+
+
+def _sms_sweep(buf, dispatch_fn, combine_fn, ops, args, case, logs):
+    """Time dispatch and combine for each SM count of `--sweep-sms` (DeepEP's tuning sweep); the
+    rank-max median per op and the best setting are recorded."""
+    from ..utils.testing import bench, rank_max
+    saved = type(buf).num_sms
+    best = {}
+    rows = []
+    try:
+        for sms in args.sweep_sms:
+            type(buf).num_sms = sms
+            row = {'num_sms': sms}
+            for op, fn in (('dispatch', dispatch_fn), ('combine', combine_fn)):
+                _, _, _, times = bench(fn, num_warmups=2, num_tests=max(4, args.iters // 2), flush_l2=True)
+                med = sorted(rank_max([t * 1e6 for t in times[1:]]))[len(times[1:]) // 2]
+                gbps = ops[op][1] / (med * 1e-6) / 1e9
+                row[op + '_us'], row[op + '_gbps'] = med, gbps
+                if op not in best or med < best[op]['us']:
+                    best[op] = {'num_sms': sms, 'us': med, 'gbps': gbps}
+            rows.append(row)
+    finally:
+        type(buf).num_sms = saved
+    rec = {'kind': 'sweep', **case, 'rows': rows, 'best': best}
+    logs['timings'].write(rec)
+    if dist.get_rank() == 0:
+        for op, b in best.items():
+            print(f"[ep_benchmark] best {op}: {b['num_sms']} SMs, {b['us']:.1f} us, {b['gbps']:.0f} GB/s per rank", flush=True)
+    return rec
 
 
 def _stall_loop(buf, dispatch_fn, combine_fn, args, case, logs):
@@ -211,6 +242,8 @@ def main(argv=None):
     p.add_argument('--stall-us', type=float, default=None,
                    help='also run dispatch -> GPU stall -> combine loops (expert-compute stand-in)')
     p.add_argument('--stall-iters', type=int, default=200)
+    p.add_argument('--sweep-sms', type=lambda v: [int(x) for x in v.split(',')], default=None,
+                   help='comma-separated SM counts to time dispatch / combine with (tuning sweep)')
     args = p.parse_args(argv)
 
     from .. import Buffer, ReferenceBuffer
@@ -245,7 +278,7 @@ def main(argv=None):
                             case, res = run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs)
                             if rank == 0:
                                 line = ', '.join(f"{op} {sorted(r['rank_max_us'])[len(r['rank_max_us']) // 2]:.1f} us"
-                                                 for op, r in res.items() if op != 'stall')
+                                                 for op, r in res.items() if op not in ('stall', 'sweep'))
                                 if 'stall' in res:
                                     line += (f", with {args.stall_us:g} us stall: dispatch {res['stall']['dispatch_us']:.1f} us"
                                              f" combine {res['stall']['combine_us']:.1f} us")
