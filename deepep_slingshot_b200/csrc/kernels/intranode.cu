@@ -11,17 +11,20 @@
 //    * notify (one CTA): builds the per-destination token lists and `send_head`, pushes the count
 //               row and the per-expert counts into every peer's control block, releases a flag, waits
 //               for every peer's flag and computes the receive layout (prefix matrices, aligned
-//               per-expert counts) into device memory and into host-mapped counters.
+//               per-expert counts) into device memory.
 //    * pull   (num_sms CTAs): every receiver pulls the records it needs straight out of the
 //               sources' staging with TMA bulk loads over NVLink (no multicast) into a shared-memory
 //               ring and TMA-stores them into its own output tensors. There is no receive ring and
-//               no copy epilogue: the output tensors are written once.
-//  combine = push -> reduce
-//    * push   : each rank TMA-stores its expert-output rows into the source rank's combine slots
-//               (slot = send_prefix + position, known from the dispatch layout) and adds the row count
-//               to a counter in the source's memory with a sys-scope release.
-//    * reduce : the source waits for all rows, sums them in fp32 (+ bias), casts to bf16, sums the
-//               top-k weights, and releases `combine_ready` so peers may reuse its slots.
+//               no copy epilogue: the output tensors are written once. The last block publishes the
+//               received counts to host-mapped memory (the CPU sync) and releases the sources' staging.
+//  combine = one kernel, push and reduce overlapped
+//    * push warps TMA-store this rank's expert-output rows into the source ranks' combine slots
+//               (slot = send_prefix + position, known from the dispatch layout), walking the
+//               destinations in a wavefront so each token's contributions arrive close together, and
+//               announce arrivals per token in batches (one drain + system fence per batch);
+//    * reducer warps (and push warps once done) take tokens from a shared cursor, wait until all
+//               of a token's contributions arrived, sum them in fp32 (+ bias), cast to bf16, sum the
+//               top-k weights; the last block releases `combine_ready` so peers may reuse the slots.
 // Every wait is bounded and reports an error code instead of trapping.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
