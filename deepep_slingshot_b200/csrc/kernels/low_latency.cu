@@ -4,18 +4,21 @@
 // dispatch, :715-1230 combine, :1241-1256 clean, :1258-1289 mask ops; Python surface
 // [DE]deep_ep/buffers/legacy.py:538-713), re-designed for one NVLink domain:
 //
-//  * dispatch send phase: one warp per token quantizes the bf16 row to FP8 e4m3 with 1x128 scales
-//    (optional power-of-two / UE8M0 scales) into shared memory, then for each top-k expert claims a
-//    slot in the destination's per-expert receive block with ONE remote atomic (so rows land already
-//    compacted: valid rows of expert e are [0, recv_count[e]) with no receive-side packing copy) and
-//    TMA-stores the row straight into `recv_x[e][slot]`; scales go into the column-major scale block
-//    and (token, src rank, k) into the src-info arrays. The last block releases a per-source
-//    `dispatch_done` flag (value = call sequence) in every destination.
-//  * dispatch recv phase (the hook): bounded wait on the R flags, then per local expert read/reset
-//    the slot counter and produce recv_count / layout_range / statistics.
+//  * dispatch send phase: one block per token; its 8 warps quantize the bf16 row to FP8 e4m3 with
+//    1x128 scales (optional power-of-two / UE8M0 scales) into shared memory together, then warp k
+//    claims a slot for top-k choice k in the destination's per-expert receive block with ONE remote
+//    atomic (so rows land already compacted: valid rows of expert e are [0, recv_count[e]) with no
+//    receive-side packing copy) and TMA-stores the row straight into `recv_x[e][slot]`; scales go into
+//    the column-major scale block and (token, src rank, k) into the src-info arrays. The last block
+//    sets a per-source `dispatch_done` flag in every destination.
+//  * dispatch recv phase (the hook): bounded wait on the R flags (the last block resets them, so no
+//    sequence numbers are needed and captured graphs replay), then per local expert read/reset the
+//    slot counter and produce recv_count / layout_range / statistics.
 //  * combine send phase: every received row (expert output) is TMA-copied back into the source
-//    rank's [token][k] slot; the last block releases `combine_done`.
-//  * combine recv phase (the hook): bounded wait, then the top-k WEIGHTED fp32 reduction + bf16 cast.
+//    rank's [token][k] slot (with `use_logfmt` encoded in place to LogFMT-10 first); the last block
+//    sets `combine_done`.
+//  * combine recv phase (the hook): bounded wait, then the top-k WEIGHTED fp32 reduction + bf16 cast,
+//    eight warps per token (decoding LogFMT groups on the fly).
 // Two halves alternate (double buffering), as in the reference. In shrink mode an expired wait
 // masks the silent rank instead of failing.
 #include <cuda_bf16.h>
