@@ -1,5 +1,6 @@
 // C++ runtime of the B200 expert-parallel buffer. See buffer.hpp for the design summary.
 #include "buffer.hpp"
+#include "cuda_check.hpp"
 
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -13,13 +14,6 @@
 
 namespace ep {
 
-#define EP_CUDA_CHECK(cmd)                                                                                   \
-    do {                                                                                                     \
-        cudaError_t e_ = (cmd);                                                                              \
-        if (e_ != cudaSuccess)                                                                               \
-            throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " at " __FILE__ ":" + \
-                                     std::to_string(__LINE__));                                              \
-    } while (0)
 
 namespace {
 

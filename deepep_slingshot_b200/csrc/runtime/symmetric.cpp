@@ -1,6 +1,7 @@
 // Symmetric side regions: pipeline send/recv, AGRS all-gather sessions, Engram storage/fetch.
 // See symmetric.hpp for the design summary.
 #include "symmetric.hpp"
+#include "cuda_check.hpp"
 
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDACachingAllocator.h>
@@ -16,13 +17,6 @@
 
 namespace ep {
 
-#define SYM_CUDA_CHECK(cmd)                                                                                  \
-    do {                                                                                                     \
-        cudaError_t e_ = (cmd);                                                                              \
-        if (e_ != cudaSuccess)                                                                               \
-            throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " at " __FILE__ ":" + \
-                                     std::to_string(__LINE__));                                              \
-    } while (0)
 
 namespace {
 
@@ -35,17 +29,17 @@ SymmetricRegion::SymmetricRegion(int rank, int num_ranks, int64_t data_bytes, do
       timeout_s_(timeout_s), copy_stream_(at::cuda::getStreamFromPool(true)) {
     TORCH_CHECK(num_ranks >= 1 && num_ranks <= kMaxRanks, "SymmetricRegion: 1..8 ranks on one NVLink domain");
     TORCH_CHECK(rank >= 0 && rank < num_ranks);
-    SYM_CUDA_CHECK(cudaGetDevice(&device_id_));
+    EP_CUDA_CHECK(cudaGetDevice(&device_id_));
     const int64_t total = kSymCtrlBytes + data_bytes_;
-    SYM_CUDA_CHECK(cudaMalloc(&base_, total));
-    SYM_CUDA_CHECK(cudaMemset(base_, 0, total));
-    SYM_CUDA_CHECK(cudaIpcGetMemHandle(&ipc_, base_));
-    SYM_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&host_error_), sizeof(ErrorState), cudaHostAllocMapped));
+    EP_CUDA_CHECK(cudaMalloc(&base_, total));
+    EP_CUDA_CHECK(cudaMemset(base_, 0, total));
+    EP_CUDA_CHECK(cudaIpcGetMemHandle(&ipc_, base_));
+    EP_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&host_error_), sizeof(ErrorState), cudaHostAllocMapped));
     std::memset(host_error_, 0, sizeof(ErrorState));
-    SYM_CUDA_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_error_dev_), host_error_, 0));
-    SYM_CUDA_CHECK(cudaMalloc(&abort_flag_, sizeof(int)));
-    SYM_CUDA_CHECK(cudaMemset(abort_flag_, 0, sizeof(int)));
-    SYM_CUDA_CHECK(cudaDeviceSynchronize());
+    EP_CUDA_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_error_dev_), host_error_, 0));
+    EP_CUDA_CHECK(cudaMalloc(&abort_flag_, sizeof(int)));
+    EP_CUDA_CHECK(cudaMemset(abort_flag_, 0, sizeof(int)));
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
     peer_[rank_] = base_;
 }
 
@@ -68,7 +62,7 @@ void SymmetricRegion::sync(const std::vector<pybind11::bytes>& handles) {
         TORCH_CHECK(h.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
         cudaIpcMemHandle_t ipc;
         std::memcpy(&ipc, h.data(), sizeof(ipc));
-        SYM_CUDA_CHECK(cudaIpcOpenMemHandle(&peer_[r], ipc, cudaIpcMemLazyEnablePeerAccess));
+        EP_CUDA_CHECK(cudaIpcOpenMemHandle(&peer_[r], ipc, cudaIpcMemLazyEnablePeerAccess));
         peer_opened_[r] = true;
     }
     available_ = true;
@@ -123,10 +117,10 @@ std::tuple<int, int, int, int> SymmetricRegion::get_error_state() const {
 }
 
 void SymmetricRegion::clear_error() {
-    SYM_CUDA_CHECK(cudaDeviceSynchronize());
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
     if (host_error_) std::memset(host_error_, 0, sizeof(ErrorState));
-    if (abort_flag_) SYM_CUDA_CHECK(cudaMemset(abort_flag_, 0, sizeof(int)));
-    SYM_CUDA_CHECK(cudaDeviceSynchronize());
+    if (abort_flag_) EP_CUDA_CHECK(cudaMemset(abort_flag_, 0, sizeof(int)));
+    EP_CUDA_CHECK(cudaDeviceSynchronize());
 }
 
 void SymmetricRegion::barrier() {
@@ -143,8 +137,8 @@ void SymmetricRegion::barrier() {
     a.st = status();
     auto stream = at::cuda::getCurrentCUDAStream();
     launch_signal_wait(a, stream);
-    SYM_CUDA_CHECK(cudaGetLastError());
-    SYM_CUDA_CHECK(cudaStreamSynchronize(stream));
+    EP_CUDA_CHECK(cudaGetLastError());
+    EP_CUDA_CHECK(cudaStreamSynchronize(stream));
     check_error();
 }
 
@@ -185,7 +179,7 @@ void SymmetricRegion::pp_send(const torch::Tensor& x, int dst_rank, int num_sms)
     a.st = status();
     const int blocks = (int)std::min<int64_t>(num_sms > 0 ? num_sms : 32, std::max<int64_t>(1, (a.bytes + 65535) / 65536));
     launch_pp_copy(a, blocks, at::cuda::getCurrentCUDAStream());
-    SYM_CUDA_CHECK(cudaGetLastError());
+    EP_CUDA_CHECK(cudaGetLastError());
 }
 
 void SymmetricRegion::pp_recv(const torch::Tensor& x, int src_rank, int num_sms) {
@@ -212,7 +206,7 @@ void SymmetricRegion::pp_recv(const torch::Tensor& x, int src_rank, int num_sms)
     a.st = status();
     const int blocks = (int)std::min<int64_t>(num_sms > 0 ? num_sms : 32, std::max<int64_t>(1, (a.bytes + 65535) / 65536));
     launch_pp_copy(a, blocks, at::cuda::getCurrentCUDAStream());
-    SYM_CUDA_CHECK(cudaGetLastError());
+    EP_CUDA_CHECK(cudaGetLastError());
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -258,7 +252,7 @@ void SymmetricRegion::destroy_agrs_session() {
     a.code = kErrTimeoutAgrs;
     a.st = status();
     launch_signal_wait(a, copy_stream_.stream());
-    SYM_CUDA_CHECK(cudaGetLastError());
+    EP_CUDA_CHECK(cudaGetLastError());
 }
 
 std::vector<torch::Tensor> SymmetricRegion::agrs_get_inplace_tensor(const std::vector<int64_t>& num_bytes_list) {
@@ -311,7 +305,7 @@ SymmetricRegion::all_gather(const std::vector<torch::Tensor>& tensors) {
             const auto& x = tensors[j];
             uint8_t* dst = data_of(r) + offsets[j] + (int64_t)x.nbytes() * rank_;
             if (dst == static_cast<const uint8_t*>(x.data_ptr())) continue;
-            SYM_CUDA_CHECK(cudaMemcpyAsync(dst, x.data_ptr(), x.nbytes(), cudaMemcpyDefault, copy_stream_.stream()));
+            EP_CUDA_CHECK(cudaMemcpyAsync(dst, x.data_ptr(), x.nbytes(), cudaMemcpyDefault, copy_stream_.stream()));
         }
     }
     for (const auto& x : tensors) c10::cuda::CUDACachingAllocator::recordStream(x.storage().data_ptr(), copy_stream_);
@@ -326,7 +320,7 @@ SymmetricRegion::all_gather(const std::vector<torch::Tensor>& tensors) {
     a.code = kErrTimeoutAgrs;
     a.st = status();
     launch_signal_wait(a, copy_stream_.stream());
-    SYM_CUDA_CHECK(cudaGetLastError());
+    EP_CUDA_CHECK(cudaGetLastError());
     auto done = std::make_shared<at::cuda::CUDAEvent>();
     done->record(copy_stream_);
 
@@ -346,7 +340,7 @@ void SymmetricRegion::engram_write(const torch::Tensor& storage) {
     TORCH_CHECK((int64_t)storage.nbytes() <= data_bytes_, "engram storage exceeds the region");
     TORCH_CHECK((storage.size(1) * 2) % 16 == 0, "engram hidden * 2 bytes must be a multiple of 16");
     barrier();  // earlier fetches by peers have finished reading the old storage
-    SYM_CUDA_CHECK(cudaMemcpyAsync(data_of(rank_), storage.data_ptr(), storage.nbytes(), cudaMemcpyDeviceToDevice,
+    EP_CUDA_CHECK(cudaMemcpyAsync(data_of(rank_), storage.data_ptr(), storage.nbytes(), cudaMemcpyDeviceToDevice,
                                    at::cuda::getCurrentCUDAStream()));
     barrier();  // every rank's storage is in place
     engram_entries_ = (int)storage.size(0);
@@ -375,7 +369,7 @@ std::function<torch::Tensor()> SymmetricRegion::engram_fetch(const torch::Tensor
     a.num_ranks = num_ranks_;
     a.st = status();
     launch_engram_fetch(a, num_sms > 0 ? num_sms : 148, copy_stream_.stream());
-    SYM_CUDA_CHECK(cudaGetLastError());
+    EP_CUDA_CHECK(cudaGetLastError());
     c10::cuda::CUDACachingAllocator::recordStream(indices.storage().data_ptr(), copy_stream_);
     c10::cuda::CUDACachingAllocator::recordStream(out.storage().data_ptr(), copy_stream_);
     auto done = std::make_shared<at::cuda::CUDAEvent>();
