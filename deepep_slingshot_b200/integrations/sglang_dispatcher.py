@@ -11,6 +11,7 @@ standalone object with the same `_dispatch_core` / `_combine_core` / `close` met
 Environment knobs: DEEPEP_B200_SGLANG_MAX_TOKENS (capacity, default 4096),
 DEEPEP_B200_SGLANG_SMS (SMs for dispatch/combine, default 64).
 """
+import functools
 import logging
 import os
 from typing import Dict, Optional, Tuple
@@ -111,8 +112,10 @@ class DeepEPB200Normal:
         self._buffer_key = None
 
 
+@functools.lru_cache(maxsize=None)
 def make_sglang_dispatcher_class():
-    """Subclass of SGLang's `_DeepEPDispatcherImplNormal` using this library (needs SGLang)."""
+    """Subclass of SGLang's `_DeepEPDispatcherImplNormal` using this library (needs SGLang); one
+    class per process, so every layer's dispatcher has the same type."""
     from sglang.srt.layers.moe.token_dispatcher.deepep import _DeepEPDispatcherImplNormal  # noqa: F401
 
     class DeepEPB200SGLangNormal(_DeepEPDispatcherImplNormal):
