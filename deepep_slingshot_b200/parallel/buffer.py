@@ -25,7 +25,9 @@ import torch
 import torch.distributed as dist
 
 from .._ext import require_ext
+from ..utils import lifecycle
 from ..utils.event import EventOverlap
+from ..utils.runtime_guard import check_nccl_runtime
 from ..utils.math import pack_ue8m0
 
 topk_idx_t = torch.int64
@@ -90,6 +92,8 @@ class Buffer:
         _C = require_ext()
         if group is None:
             raise ValueError('a torch.distributed process group is required')
+        check_nccl_runtime()
+        used_before = lifecycle.snapshot()
         self.rank = group.rank()
         self.group = group
         self.group_size = group.size()
@@ -116,12 +120,14 @@ class Buffer:
         assert self.runtime.is_available()
         torch.cuda.synchronize()
         dist.barrier(group)
+        lifecycle.record('create', 'Buffer', self, num_nvl_bytes + num_rdma_bytes, used_before)
 
     # ------------------------------------------------------------------ lifecycle / info
     def destroy(self) -> None:
         assert self.explicitly_destroy, '`explicitly_destroy` flag must be set'
         self.runtime.destroy()
         self.runtime = None
+        lifecycle.record('destroy', 'Buffer', self)
 
     @staticmethod
     def is_sm90_compiled() -> bool:

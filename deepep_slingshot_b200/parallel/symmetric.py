@@ -12,6 +12,7 @@ import torch
 import torch.distributed as dist
 
 from .._ext import require_ext
+from ..utils import lifecycle
 
 
 def _default_timeout() -> float:
@@ -24,6 +25,7 @@ class SymmetricRegion:
 
     def __init__(self, group: dist.ProcessGroup, data_bytes: int, timeout_secs: Optional[float] = None):
         _C = require_ext()
+        used_before = lifecycle.snapshot()
         self.group = group
         self.rank = group.rank()
         self.num_ranks = group.size()
@@ -34,6 +36,7 @@ class SymmetricRegion:
         self.runtime.sync(handles)
         torch.cuda.synchronize()
         dist.barrier(group)
+        lifecycle.record('create', 'SymmetricRegion', self, int(data_bytes), used_before)
 
     @property
     def data_bytes(self) -> int:
@@ -43,6 +46,7 @@ class SymmetricRegion:
         if self.runtime is not None:
             self.runtime.destroy()
             self.runtime = None
+            lifecycle.record('destroy', 'SymmetricRegion', self)
 
     def check_error(self) -> None:
         self.runtime.check_error()
