@@ -4,13 +4,17 @@ summary (the reference's `profile_capture.py`: torch.profiler + NVTX + kernel su
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m deepep_slingshot_b200.harness.profile_capture \
         --tokens 4096 --hidden 7168 --experts 256 --topk 8 --steps 5 --out prof_ep8
 
-Every rank writes `kernels-rank{r}.csv` (kernel, calls, total µs, mean µs, share of device time);
-rank 0 also writes `trace-rank0.json` (Chrome trace with the NVTX ranges). Profiled numbers are for
-shares and timelines, not benchmark values.
+Each operation (fresh dispatch with its layout, cached dispatch, combine, dispatch + combine cycle)
+is profiled on its own, every call inside an `ep/<operation>/iteration<i>` range. Every rank writes,
+per operation, `kernels-<op>-rank{r}.csv` (kernel, calls, total µs, mean µs, share of device time),
+the Chrome trace `<op>-rank{r}.json` and `<op>-rank{r}-summary.json` (the case, with input and route
+hashes); `harness.analyze_profiles` turns them into span/union/gap/overlap figures. Profiled numbers
+are for shares and timelines, not benchmark values.
 """
 import argparse
 import csv
 import datetime
+import json
 import os
 from collections import defaultdict
 from typing import Iterable, List
@@ -37,6 +41,9 @@ def kernel_summary(events: Iterable, steps: int = 1) -> List[dict]:
     return sorted(rows, key=lambda r: -r['total_us'])
 
 
+OPERATIONS = ('dispatch', 'cached_dispatch', 'combine', 'cycle')
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument('--tokens', type=int, default=4096)
@@ -45,11 +52,13 @@ def main(argv=None):
     p.add_argument('--topk', type=int, default=8)
     p.add_argument('--steps', type=int, default=5)
     p.add_argument('--warmup', type=int, default=3)
+    p.add_argument('--ops', nargs='+', default=list(OPERATIONS), choices=OPERATIONS)
     p.add_argument('--out', default='prof_out')
     args = p.parse_args(argv)
     from .. import Buffer
     from ..parallel import buffer as buffer_mod
     from ..utils import gate
+    from ..utils.testing import hash_tensor
     buffer_mod._NVTX = True  # NVTX ranges around every API call for this capture
     owns = not dist.is_initialized()
     if owns:
@@ -63,35 +72,55 @@ def main(argv=None):
     idx, w = gate.normal_routing(N, E, K, generator=g)
     idx, w = idx.cuda(), w.cuda()
     buf = Buffer(dist.group.WORLD, num_nvl_bytes=Buffer.get_nvl_buffer_size_hint(N, H, world))
-    y = torch.randn((N * world, H), generator=g).to(torch.bfloat16).cuda()
+    y_all = torch.randn((N * world, H), generator=g).to(torch.bfloat16).cuda()
+    case = {'tokens': N, 'hidden': H, 'experts': E, 'topk': K, 'world': world, 'dtype': 'fp8',
+            'input_sha256': hash_tensor(x), 'route_sha256': hash_tensor(idx)}
 
-    def step():
+    def fresh():
         ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(idx, E)
-        (rx, rs), ri, rw, _, h, _ = buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
-                                                 num_tokens_per_expert=ntpe, topk_idx=idx, topk_weights=w,
-                                                 quantize_fp8=True)
-        buf.combine(y[:rx.shape[0]], h, topk_weights=rw)
+        return buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe,
+                            topk_idx=idx, topk_weights=w, quantize_fp8=True)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    acts = [torch.profiler.ProfilerActivity.CPU, torch.profiler.ProfilerActivity.CUDA]
-    with torch.profiler.profile(activities=acts) as prof:
-        for _ in range(args.steps):
-            step()
-        torch.cuda.synchronize()
+    (rx, _), _, rw, _, handle, _ = fresh()
+    y = y_all[:rx.shape[0]]
+
+    def cached():
+        buf.dispatch(x, handle=handle, quantize_fp8=True)
+
+    def comb():
+        buf.combine(y, handle, topk_weights=rw)
+
+    def cycle():
+        (cx, _), _, cw, _, h, _ = fresh()
+        buf.combine(y_all[:cx.shape[0]], h, topk_weights=cw)
+
+    fns = {'dispatch': fresh, 'cached_dispatch': cached, 'combine': comb, 'cycle': cycle}
     os.makedirs(args.out, exist_ok=True)
-    rows = kernel_summary(prof.events(), args.steps)
-    with open(os.path.join(args.out, f'kernels-rank{rank}.csv'), 'w', newline='') as f:
-        wr = csv.DictWriter(f, fieldnames=['kernel', 'calls', 'total_us', 'mean_us', 'per_step_us', 'share'])
-        wr.writeheader()
-        wr.writerows(rows)
-    if rank == 0:
-        prof.export_chrome_trace(os.path.join(args.out, 'trace-rank0.json'))
-        for r in rows[:12]:
-            print(f"{r['share']:6.1%} {r['per_step_us']:9.1f} us/step  {r['kernel'][:90]}")
-    dist.barrier()
+    acts = [torch.profiler.ProfilerActivity.CPU, torch.profiler.ProfilerActivity.CUDA]
+    for op in args.ops:
+        fn = fns[op]
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.profiler.profile(activities=acts) as prof:
+            for i in range(args.steps):
+                with torch.profiler.record_function(f'ep/{op}/iteration{i}'):
+                    fn()
+                    torch.cuda.synchronize()
+        rows = kernel_summary(prof.events(), args.steps)
+        with open(os.path.join(args.out, f'kernels-{op}-rank{rank}.csv'), 'w', newline='') as f:
+            wr = csv.DictWriter(f, fieldnames=['kernel', 'calls', 'total_us', 'mean_us', 'per_step_us', 'share'])
+            wr.writeheader()
+            wr.writerows(rows)
+        prof.export_chrome_trace(os.path.join(args.out, f'{op}-rank{rank}.json'))
+        with open(os.path.join(args.out, f'{op}-rank{rank}-summary.json'), 'w') as f:
+            json.dump({'operation': op, 'rank': rank, 'profiled_iterations': args.steps, 'case': case}, f)
+        if rank == 0:
+            print(f'-- {op}')
+            for r in rows[:8]:
+                print(f"{r['share']:6.1%} {r['per_step_us']:9.1f} us/step  {r['kernel'][:90]}")
+        dist.barrier()
     if owns:
         dist.destroy_process_group()
 
