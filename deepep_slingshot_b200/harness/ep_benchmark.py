@@ -13,7 +13,9 @@ For every (model, tokens, dtype, routing, seed) case each rank:
      the per-iteration max over ranks.
 Records: `manifest-rank{r}.jsonl` (source hashes, versions, environment), `correctness-rank{r}.jsonl`,
 `timings-rank{r}.jsonl`; rank 0 writes `summary.csv` and `repeatability.json` (`harness.summarize`).
-Model shapes follow the reference's benchmark (backend/tests/ep_benchmark.py:19) plus DeepSeek-V3.
+Model shapes follow the reference's benchmark (backend/tests/ep_benchmark.py:19) plus DeepSeek-V3 and
+a Mixtral-style small-expert-count shape (hidden 4096, 8 experts, top-2), swept as
+`--models mixtral --dtype bf16 --routing uniform --tokens 128 512 2048 8192`.
 """
 import argparse
 import datetime
@@ -29,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 MODELS = {'v4flash': (4096, 256, 6), 'qwen3': (4096, 128, 8), 'minimax': (3072, 256, 8),
-          'deepseek_v3': (7168, 256, 8)}
+          'deepseek_v3': (7168, 256, 8), 'mixtral': (4096, 8, 2)}
 
 
 def dispatch_bytes(num_recv: int, hidden: int, num_topk: int, fp8: bool) -> int:

@@ -171,11 +171,13 @@ def make_routing(name: str, rank: int, num_ranks: int, num_tokens: int, num_expe
         g = torch.Generator().manual_seed(seed * 100 + rank)
         return torch.rand((N, E), generator=g).topk(K, dim=1).indices.to(torch.int64)
     if name == 'hot_rank':
-        assert K <= E // R
+        if K > E // R:
+            raise ValueError(f'routing hot_rank puts all top-{K} choices on rank 0, which owns only {E // R} experts')
         return torch.arange(K, dtype=torch.int64)[None, :].expand(N, K).contiguous()
     if name == 'self':
         le = E // R
-        assert K <= le
+        if K > le:
+            raise ValueError(f'routing self keeps all top-{K} choices on the source rank, which owns only {le} experts')
         g = torch.Generator().manual_seed(seed * 100 + rank)
         return (torch.rand((N, le), generator=g).topk(K, dim=1).indices + rank * le).to(torch.int64)
     if name.startswith('zipf') or name.startswith('counts:'):
