@@ -60,6 +60,7 @@ enum TraceEvent : int {
     kTraceLLDispatchRecv = 121,
     kTraceLLCombineSend = 122,
     kTraceLLCombineRecv = 123,
+    kTraceLLDispatchRecvGemm = 124,  // fused receive of the masked GEMM: wait for the peers, a = 1 if complete
     kTraceBarrier = 130,
     kTracePP = 140,             // pipeline copy CTA, a = is_send, b = bytes
 };

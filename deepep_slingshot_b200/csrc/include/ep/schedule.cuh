@@ -69,4 +69,18 @@ __host__ __device__ __forceinline__ int ring_dir(int me, int other, int num_rank
     return other == (me + num_ranks - 1) % num_ranks ? 0 : 1;
 }
 
+// Tile order of the masked grouped GEMM: (m-tile, expert, n-tile), n-tile innermost. A grid of G
+// persistent CTAs takes tiles c, c + G, ...; the first E * n_tiles tiles are every expert's first
+// m-tile, so a decode batch (at most one m-tile per expert) spreads evenly over the CTAs.
+// Returns false past the last potential tile.
+__host__ __device__ __forceinline__ bool masked_gemm_tile(int t, int E, int n_tiles, int m_tiles, int& mt, int& e, int& nt) {
+    const int per_mt = E * n_tiles;
+    if (t < 0 || t >= per_mt * m_tiles) return false;
+    mt = t / per_mt;
+    const int r = t - mt * per_mt;
+    e = r / n_tiles;
+    nt = r - e * n_tiles;
+    return true;
+}
+
 }  // namespace ep

@@ -43,4 +43,29 @@ struct Bf16GemmArgs {
 };
 int launch_grouped_gemm_bf16(const Bf16GemmArgs& a, int num_sms, cudaStream_t stream);
 
+// Masked grouped FP8 GEMM over the low-latency per-expert padded layout (gemm_masked_sm100.cu).
+//   a [E][slots][k] e4m3; scale of (e, m, kb) at sa[e*sa_e + kb*sa_k + m*sa_m]; b [E][n][k] e4m3;
+//   sb [E][n/128][k/128]; d [E][slots][n] bf16, rows m < count[e] written.
+// Counts come either from `counts` (device, [E]) or, fused with the low-latency dispatch receive,
+// from the slot counters of `ll` once every rank's dispatch_done flag is set (exactly one is set).
+struct MaskedGemmArgs {
+    const void* a;
+    const float* sa;
+    int64_t sa_e, sa_k, sa_m;
+    const void* b;
+    const float* sb;
+    const int* counts;
+    void* d;
+    int num_experts, slots, n, k;
+    int stages;
+    LLCtrl* ll;                 // fused receive: this rank's control block of the dispatch half
+    int num_ranks;
+    int* recv_count;            // fused: [E] out
+    int* cumulative_stats;      // fused: [E] += counts (optional)
+    int64_t l2_prefetch_bytes;  // fused: weights each CTA prefetches into L2 while it waits
+    KernelStatus st;
+};
+// Returns 0 on success, 1 bad arguments, 2 tensor-map encode failure, 3 launch failure.
+int launch_masked_gemm_fp8(const MaskedGemmArgs& a, int num_sms, cudaStream_t stream);
+
 }  // namespace ep

@@ -1,6 +1,7 @@
 // C++ runtime of the B200 expert-parallel buffer. See buffer.hpp for the design summary.
 #include "buffer.hpp"
 #include "cuda_check.hpp"
+#include "../kernels/gemm.h"
 
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -920,6 +921,61 @@ Buffer::low_latency_dispatch(const torch::Tensor& x, const torch::Tensor& topk_i
         stream_wait(compute, comm_stream_);
     }
     return {recv_x, recv_scales, recv_count, src_info, src_meta, layout_range, half, event, hook};
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int>
+Buffer::low_latency_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& topk_idx,
+                                  const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats,
+                                  int num_max_dispatch_tokens_per_rank, int num_experts, const torch::Tensor& w,
+                                  const torch::Tensor& w_scales, bool round_scale, int num_sms) {
+    TORCH_CHECK(!enable_shrink_, "the fused receive does not support shrink mode");
+    const int R = num_ranks_, maxT = num_max_dispatch_tokens_per_rank, H = (int)x.size(1);
+    // Send phase only (on the compute stream); the hook is dropped: the GEMM kernel below receives.
+    auto sent = low_latency_dispatch(x, topk_idx, std::nullopt, std::nullopt, maxT, num_experts, /*use_fp8=*/true,
+                                     round_scale, /*use_ue8m0=*/false, /*async=*/false, /*return_recv_hook=*/true);
+    torch::Tensor recv_x = std::get<0>(sent), recv_count = std::get<2>(sent);
+    torch::Tensor recv_scales = std::get<1>(sent).value();
+    const int half = std::get<6>(sent);
+    const LLLayout L = compute_ll_layout(num_rdma_bytes_, maxT, H, num_experts, R);
+    const int E_l = L.num_local_experts, slots = R * maxT;
+    TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.is_contiguous() && w.scalar_type() == torch::kFloat8_e4m3fn && w.size(0) == E_l &&
+                    w.size(2) == H && w.size(1) % 128 == 0,
+                "weights must be contiguous [num_local_experts, n, hidden] e4m3 with n % 128 == 0");
+    const int n = (int)w.size(1);
+    TORCH_CHECK(w_scales.scalar_type() == torch::kFloat32 && w_scales.is_contiguous() && w_scales.dim() == 3 &&
+                    w_scales.size(0) == E_l && w_scales.size(1) == n / 128 && w_scales.size(2) == H / 128,
+                "weight scales must be [num_local_experts, n/128, hidden/128] fp32");
+    if (cumulative_local_expert_recv_stats.has_value())
+        TORCH_CHECK(cumulative_local_expert_recv_stats->scalar_type() == torch::kInt32 &&
+                    cumulative_local_expert_recv_stats->numel() == E_l);
+    if (num_sms <= 0) EP_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device_id_));
+    auto out = torch::empty({E_l, slots, n}, x.options());
+    MaskedGemmArgs g{};
+    g.a = recv_x.data_ptr();
+    g.sa = recv_scales.data_ptr<float>();
+    g.sa_e = recv_scales.stride(0);
+    g.sa_m = recv_scales.stride(1);
+    g.sa_k = recv_scales.stride(2);
+    g.b = w.data_ptr();
+    g.sb = w_scales.data_ptr<float>();
+    g.counts = nullptr;
+    g.d = out.data_ptr();
+    g.num_experts = E_l;
+    g.slots = slots;
+    g.n = n;
+    g.k = H;
+    uint8_t* half_base = static_cast<uint8_t*>(ll_base_) + (int64_t)half * L.half_bytes;
+    g.ll = reinterpret_cast<LLCtrl*>(half_base + L.ctrl_off);
+    g.num_ranks = R;
+    g.recv_count = recv_count.data_ptr<int>();
+    g.cumulative_stats =
+        cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
+    // About 3/4 of the 126 MB L2 for weights fetched while the peers' tokens are in flight.
+    g.l2_prefetch_bytes = ((int64_t)(96 << 20) / num_sms) & ~(int64_t)15;
+    g.st = status();
+    const int rc = launch_masked_gemm_fp8(g, num_sms, at::cuda::getCurrentCUDAStream().stream());
+    TORCH_CHECK(rc == 0, "fused low-latency receive + masked GEMM launch failed (code " + std::to_string(rc) + ")");
+    return {out, recv_x, recv_scales, recv_count, std::get<3>(sent), std::get<4>(sent), half};
 }
 
 std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::function<void()>>> Buffer::low_latency_combine(

@@ -134,6 +134,13 @@ class Buffer {
                          const std::optional<torch::Tensor>& dispatch_wait_recv_cost_stats,
                          int num_max_dispatch_tokens_per_rank, int num_experts, bool use_fp8, bool round_scale,
                          bool use_ue8m0, bool async, bool return_recv_hook);
+    // FP8 low-latency dispatch whose receive runs inside the first expert GEMM (masked, tcgen05):
+    // returns (gemm out [E_l, slots, n] bf16, recv_x, recv_scales, recv_count, src_info, src_meta, half).
+    std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int>
+    low_latency_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& topk_idx,
+                              const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats,
+                              int num_max_dispatch_tokens_per_rank, int num_experts, const torch::Tensor& w,
+                              const torch::Tensor& w_scales, bool round_scale, int num_sms);
     std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::function<void()>>> low_latency_combine(
         const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights,
         const torch::Tensor& recv_count, int dispatch_half, const std::optional<torch::Tensor>& combine_wait_recv_cost_stats,

@@ -80,6 +80,49 @@ torch::Tensor grouped_gemm_fp8(const torch::Tensor& a, const torch::Tensor& sa, 
     return d;
 }
 
+// Masked grouped FP8 GEMM (tcgen05) over the low-latency per-expert padded layout:
+// a [E, slots, k] e4m3, sa [E, slots, k/128] fp32 (any strides, e.g. the dispatch's column-major
+// scales), counts [E] int32 valid rows -> d [E, slots, n] bf16; rows at or beyond counts[e] are left
+// unwritten (unspecified).
+torch::Tensor masked_grouped_gemm_fp8(const torch::Tensor& a, const torch::Tensor& sa, const torch::Tensor& counts,
+                                      const torch::Tensor& b, const torch::Tensor& sb, int num_sms, double timeout_s) {
+    TORCH_CHECK(a.is_cuda() && a.dim() == 3 && a.is_contiguous() && a.scalar_type() == torch::kFloat8_e4m3fn,
+                "a must be a contiguous [E, slots, k] e4m3 tensor");
+    TORCH_CHECK(b.dim() == 3 && b.is_contiguous() && b.scalar_type() == torch::kFloat8_e4m3fn, "b must be [E, n, k] e4m3");
+    const int E = (int)a.size(0), slots = (int)a.size(1), k = (int)a.size(2), n = (int)b.size(1);
+    TORCH_CHECK(b.size(0) == E && b.size(2) == k && k % 128 == 0 && n % 128 == 0, "k and n must be multiples of 128");
+    TORCH_CHECK(E <= kMaxLocalExperts, "too many experts");
+    TORCH_CHECK(sa.scalar_type() == torch::kFloat32 && sa.dim() == 3 && sa.size(0) == E && sa.size(1) == slots &&
+                sa.size(2) == k / 128, "sa must be [E, slots, k/128] fp32");
+    TORCH_CHECK(sb.scalar_type() == torch::kFloat32 && sb.is_contiguous() && sb.size(0) == E && sb.size(1) == n / 128 &&
+                sb.size(2) == k / 128, "sb must be [E, n/128, k/128] fp32");
+    TORCH_CHECK(counts.scalar_type() == torch::kInt32 && counts.is_contiguous() && counts.numel() == E && counts.is_cuda());
+    auto d = torch::empty({E, slots, n}, a.options().dtype(torch::kBFloat16));
+    if (num_sms <= 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    MaskedGemmArgs g{};
+    g.a = a.data_ptr();
+    g.sa = sa.data_ptr<float>();
+    g.sa_e = sa.stride(0);
+    g.sa_m = sa.stride(1);
+    g.sa_k = sa.stride(2);
+    g.b = b.data_ptr();
+    g.sb = sb.data_ptr<float>();
+    g.counts = counts.data_ptr<int>();
+    g.d = d.data_ptr();
+    g.num_experts = E;
+    g.slots = slots;
+    g.n = n;
+    g.k = k;
+    g.st = op_status(timeout_s);
+    const int rc = launch_masked_gemm_fp8(g, num_sms, at::cuda::getCurrentCUDAStream());
+    TORCH_CHECK(rc == 0, "masked_grouped_gemm_fp8 launch failed (code " + std::to_string(rc) + ")");
+    return d;
+}
+
 // bf16 grouped GEMM, both operands K-major. mode 0: a [rows, k] grouped by `offsets` (128-aligned),
 // b [E, n, k] -> d [rows, n]. mode 1: a [m, Ktot], b [n, Ktot], offsets [E+1] over K -> d [E, m, n].
 torch::Tensor grouped_gemm_bf16(const torch::Tensor& a, const torch::Tensor& b, const torch::Tensor& offsets,
@@ -251,6 +294,9 @@ void register_ops(pybind11::module_& m) {
     m.def("grouped_gemm_bf16", &grouped_gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("offsets"),
           pybind11::arg("counts") = std::nullopt, pybind11::arg("mode") = 0, pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 10.0);
+    m.def("masked_grouped_gemm_fp8", &masked_grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"),
+          pybind11::arg("counts"), pybind11::arg("b"), pybind11::arg("sb"), pybind11::arg("num_sms") = 0,
+          pybind11::arg("timeout_s") = 100.0);
     m.def("grouped_gemm_fp8", &grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"), pybind11::arg("b"), pybind11::arg("sb"),
           pybind11::arg("offsets"), pybind11::arg("counts") = pybind11::none(), pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 10.0);

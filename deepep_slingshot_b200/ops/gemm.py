@@ -2,6 +2,9 @@
 
 `grouped_gemm_fp8`: rows of A grouped by expert (128-aligned blocks from `permute(..., alignment=128)`),
 per-token 1x128 activation scales, 128x128 weight scales, fp32 promotion per 128-wide K block, bf16 out.
+`masked_grouped_gemm_fp8`: the same math over the low-latency per-expert padded layout `[E, slots, k]`
+with per-expert valid-row counts (the decode path; fused with the dispatch receive in
+`Buffer.low_latency_dispatch_gemm`).
 `grouped_gemm_bf16` / `grouped_gemm_bf16_wgrad`: bf16 x bf16 -> fp32 TMEM accumulation, the backward
 (input- and weight-gradient) GEMMs of the expert FFN. `*_reference` are the fp32 torch oracles.
 """
@@ -98,4 +101,26 @@ def grouped_gemm_fp8_reference(a, sa, b, sb, offsets, counts=None) -> torch.Tens
         r0, r1 = off[e], off[e] + cnt[e]
         if r1 > r0:
             out[r0:r1] = af[r0:r1] @ bf[e].t()
+    return out
+
+
+def masked_grouped_gemm_fp8(a: torch.Tensor, sa: torch.Tensor, counts: torch.Tensor, b: torch.Tensor, sb: torch.Tensor,
+                            num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
+    """Masked grouped FP8 GEMM on tcgen05 over the low-latency per-expert padded layout:
+    `a [E, slots, k]` e4m3 with 1x128 scales `sa [E, slots, k/128]` (any strides, e.g. the dispatch's
+    column-major scales), `counts [E]` int32 valid rows per expert, `b [E, n, k]` e4m3 with 128x128
+    scales `sb [E, n/128, k/128]` -> `[E, slots, n]` bf16. Rows at or beyond `counts[e]` are left
+    unwritten. `Buffer.low_latency_dispatch_gemm` runs the same kernel fused with the dispatch receive."""
+    return require_ext().masked_grouped_gemm_fp8(a, sa, counts, b, sb, num_sms, timeout_s)
+
+
+def masked_grouped_gemm_fp8_reference(a, sa, counts, b, sb) -> torch.Tensor:
+    """fp32 torch oracle of `masked_grouped_gemm_fp8` (rows at or beyond `counts[e]` are zero)."""
+    E, slots, k = a.shape
+    bf = dequant_blocks(b, sb)
+    out = torch.zeros((E, slots, b.shape[1]), dtype=torch.float32, device=a.device)
+    for e, c in enumerate(counts.tolist()):
+        c = max(0, min(int(c), slots))
+        if c > 0:
+            out[e, :c] = dequant_rows(a[e, :c], sa[e, :c].contiguous()) @ bf[e].t()
     return out

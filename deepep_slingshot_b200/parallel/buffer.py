@@ -351,6 +351,29 @@ class Buffer:
                              cumulative_local_expert_recv_stats)
         return recv, recv_count, handle, EventOverlap(event, tensors_to_record if async_finish else None), hook
 
+    @nvtx_range('ep.low_latency_dispatch_gemm')
+    def low_latency_dispatch_gemm(self, x: torch.Tensor, topk_idx: torch.Tensor, num_max_dispatch_tokens_per_rank: int,
+                                  num_experts: int, weights: torch.Tensor, weight_scales: torch.Tensor,
+                                  cumulative_local_expert_recv_stats: Optional[torch.Tensor] = None,
+                                  round_scale: bool = False, num_sms: int = 0):
+        """FP8 low-latency dispatch straight into the first expert GEMM.
+
+        The send phase is `low_latency_dispatch(..., use_fp8=True, return_recv_hook=True)`; instead of
+        the hook, one masked grouped FP8 GEMM kernel (tcgen05) prefetches `weights` into L2 while the
+        tokens cross NVLink, waits for every rank, takes the per-expert counts and computes
+        `out[e, m] = x_e[m] @ weights[e]^T` for the received rows. `weights [E_local, n, hidden]` e4m3 with
+        128x128 scales `weight_scales [E_local, n/128, hidden/128]` (`ops.gemm.quantize_weights_fp8`).
+
+        Returns `(out [E_local, R * max_tokens, n] bf16 (rows < recv_count[e] valid), recv_count, handle,
+        (recv_x, recv_scales))`; the handle is the one `low_latency_combine` takes (its layout range is
+        not computed). Not available in shrink mode.
+        """
+        out, recv_x, recv_scales, recv_count, src_info, src_meta, half = self.runtime.low_latency_dispatch_gemm(
+            x, topk_idx, cumulative_local_expert_recv_stats, num_max_dispatch_tokens_per_rank, num_experts, weights,
+            weight_scales, round_scale, num_sms)
+        handle = (src_info, None, num_max_dispatch_tokens_per_rank, x.size(1), num_experts, recv_count, half, src_meta)
+        return out, recv_count, handle, (recv_x, recv_scales)
+
     @nvtx_range('ep.low_latency_combine')
     def low_latency_combine(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor, handle: tuple,
                             use_logfmt: bool = False, zero_copy: bool = False, async_finish: bool = False,

@@ -26,6 +26,7 @@ TRACE_EVENTS: Dict[int, str] = {
     103: 'dispatch.notify.wait_counts', 104: 'dispatch.pull',
     110: 'combine.block', 111: 'combine.push_warp',
     120: 'll_dispatch.send', 121: 'll_dispatch.recv', 122: 'll_combine.send', 123: 'll_combine.recv',
+    124: 'll_dispatch.recv_gemm',
     130: 'barrier', 140: 'pp.copy',
 }
 

@@ -4,6 +4,9 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+# Tests of kernels that have not run on a B200 yet; they move into tests/ after their first GPU run.
+collect_ignore = ['pending']
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 

@@ -5,8 +5,10 @@
 //   1. row dealing of the pull / push pipelines covers every row exactly once and every loop ends;
 //   2. the pipeline-ring credit protocol (counters, slots, ring directions) delivers every message in
 //      order, never overwrites an unconsumed slot and never deadlocks, under random interleavings;
-//   3. LogFMT-10 packing round-trips and the code -> value mapping stays within its error bound.
+//   3. LogFMT-10 packing round-trips and the code -> value mapping stays within its error bound;
+//   4. the masked grouped GEMM's tile order covers every tile once and balances decode batches.
 // Prints "ALL OK" and exits 0 on success.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -198,9 +200,45 @@ static void check_logfmt(std::mt19937& rng) {
     std::printf("logfmt ok\n");
 }
 
+// Masked grouped GEMM tile order: every potential tile is visited exactly once over the grid, the
+// live tiles (m0 < count) are exactly those the roles compute, and a decode batch (count <= 128 per
+// expert) gives every CTA floor or ceil of its share of live tiles.
+static void check_masked_tiles(std::mt19937& rng) {
+    for (int trial = 0; trial < 3000; ++trial) {
+        const int E = 1 + rng() % 64, n_tiles = 1 + rng() % 64, slots = 1 + rng() % 2048;
+        const int m_tiles = (slots + 127) / 128;
+        const int G = std::vector<int>{1, 7, 148, 296}[rng() % 4];
+        const bool decode = rng() % 2 == 0;
+        std::vector<int> count(E);
+        for (int e = 0; e < E; ++e) count[e] = decode ? rng() % 129 : rng() % (slots + 1);
+        std::vector<int> seen((size_t)E * n_tiles * m_tiles, 0);
+        int live_min = 1 << 30, live_max = 0;
+        for (int c = 0; c < G; ++c) {
+            int live = 0;
+            int mt, e, nt;
+            for (int t = c; ep::masked_gemm_tile(t, E, n_tiles, m_tiles, mt, e, nt); t += G) {
+                CHECK(mt >= 0 && mt < m_tiles && e >= 0 && e < E && nt >= 0 && nt < n_tiles, "tile %d out of range", t);
+                ++seen[((size_t)mt * E + e) * n_tiles + nt];
+                if (mt * 128 < count[e]) ++live;
+            }
+            live_min = std::min(live_min, live);
+            live_max = std::max(live_max, live);
+        }
+        for (size_t i = 0; i < seen.size(); ++i) CHECK(seen[i] == 1, "tile %zu visited %d times", i, seen[i]);
+        int mt, e, nt;
+        CHECK(!ep::masked_gemm_tile(E * n_tiles * m_tiles, E, n_tiles, m_tiles, mt, e, nt), "tile past the end accepted");
+        if (decode) {
+            bool all_nonempty = true;
+            for (int x = 0; x < E; ++x) all_nonempty &= count[x] > 0;
+            if (all_nonempty) CHECK(live_max - live_min <= 1, "decode imbalance %d..%d (E=%d NT=%d G=%d)", live_min, live_max, E, n_tiles, G);
+        }
+    }
+}
+
 int main() {
     std::mt19937 rng(12345);
     check_dealing(rng);
+    check_masked_tiles(rng);
     check_pp_ring(rng);
     check_logfmt(rng);
     std::printf("ALL OK\n");

@@ -210,3 +210,22 @@ def test_nvlink_gbs_with_fake_nvml(monkeypatch):
     assert abs(envs.get_nvlink_gbs() - envs.B200_NVLINK_GBS / 2) < 1e-6
     monkeypatch.setitem(sys.modules, 'pynvml', fake(0))
     assert envs.get_nvlink_gbs() == envs.B200_NVLINK_GBS  # no links reported: measured fallback
+
+
+def test_masked_gemm_oracle_matches_grouped_oracle():
+    """The masked-layout oracle equals the packed grouped oracle on the same rows (CPU), and leaves
+    rows at or beyond the counts zero."""
+    from deepep_slingshot_b200.ops.gemm import (grouped_gemm_fp8_reference, masked_grouped_gemm_fp8_reference,
+                                                quantize_weights_fp8_reference)
+    from deepep_slingshot_b200.utils.math import per_token_cast_to_fp8
+    torch.manual_seed(0)
+    E, slots, K, N = 3, 256, 256, 128
+    xq, xs = per_token_cast_to_fp8(torch.randn((E * slots, K)))
+    a, sa = xq.view(E, slots, K), xs.view(E, slots, K // 128)
+    wq, ws = quantize_weights_fp8_reference(torch.randn((E, N, K)) * 0.05)
+    counts = torch.tensor([5, 0, 256], dtype=torch.int32)
+    masked = masked_grouped_gemm_fp8_reference(a, sa.transpose(1, 2).contiguous().transpose(1, 2), counts, wq, ws)
+    offsets = torch.arange(0, (E + 1) * slots, slots, dtype=torch.int32)
+    packed = grouped_gemm_fp8_reference(xq, xs, wq, ws, offsets, counts).view(E, slots, N)
+    assert torch.equal(masked, packed)
+    assert masked[0, 5:].abs().sum() == 0 and masked[1].abs().sum() == 0
