@@ -170,8 +170,10 @@ void launch_ll_clean(PeerTable peers, LLLayout layout, int rank, KernelStatus st
 // ---------------------------------------------------------------- standalone ops
 void launch_per_token_cast_to_fp8(const void* x, int num_tokens, int hidden, void* out_fp8, float* out_scales,
                                   int round_scale, cudaStream_t stream);
+// `counts` (optional, device [E]) masks the per-expert layout [E][slots]: rows at or beyond counts[e]
+// are skipped (their outputs are left unwritten).
 void launch_swiglu_quant(const void* h, int rows, int inter, void* a, void* a_q, float* a_s, int round_scale,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const int* counts = nullptr, int slots = 0);
 void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_tokens, int hidden, void* out_bf16,
                                 cudaStream_t stream);
 void launch_quantize_weights_fp8(const void* w, int num_experts, int n, int k, void* q, float* scales, cudaStream_t stream);

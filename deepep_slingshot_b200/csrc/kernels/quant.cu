@@ -44,12 +44,16 @@ __global__ void __launch_bounds__(256) per_token_cast_back_kernel(const uint8_t*
 // SwiGLU + per-token FP8 requantization, one warp per row:
 //   a = silu(h[:, :I]) * h[:, I:]  (fp32 math, rounded to bf16 and stored for the backward pass),
 //   (a_q, a_s) = 1x128 FP8 quantization of the bf16 `a` (the input of the down projection).
+// With `counts` the rows are the masked per-expert layout [E][slots]: row r belongs to expert
+// r / slots and is skipped unless r % slots < counts[r / slots].
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ h, int rows, int inter,
                                                            __nv_bfloat16* __restrict__ a, uint8_t* __restrict__ a_q,
-                                                           float* __restrict__ a_s, int round_scale) {
+                                                           float* __restrict__ a_s, int round_scale,
+                                                           const int* __restrict__ counts, int slots) {
     const int lane = lane_id();
     const int warps = blockDim.x / 32;
     for (int r = blockIdx.x * warps + warp_id(); r < rows; r += gridDim.x * warps) {
+        if (counts != nullptr && r % slots >= __ldg(counts + r / slots)) continue;
         const __nv_bfloat16* gate = h + (int64_t)r * 2 * inter;
         const __nv_bfloat16* up = gate + inter;
         for (int base = 0; base < inter; base += 256) {
@@ -81,12 +85,14 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
     }
 }
 
-void launch_swiglu_quant(const void* h, int rows, int inter, void* a, void* a_q, float* a_s, int round_scale, cudaStream_t stream) {
+void launch_swiglu_quant(const void* h, int rows, int inter, void* a, void* a_q, float* a_s, int round_scale, cudaStream_t stream,
+                         const int* counts, int slots) {
     if (rows == 0) return;
     int blocks = (rows + 7) / 8;
     if (blocks > 4736) blocks = 4736;
     swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(h), rows, inter,
-                                                    static_cast<__nv_bfloat16*>(a), static_cast<uint8_t*>(a_q), a_s, round_scale);
+                                                    static_cast<__nv_bfloat16*>(a), static_cast<uint8_t*>(a_q), a_s, round_scale,
+                                                    counts, counts != nullptr ? slots : 1);
 }
 
 void launch_per_token_cast_to_fp8(const void* x, int num_tokens, int hidden, void* out_fp8, float* out_scales,

@@ -204,15 +204,32 @@ std::tuple<torch::Tensor, torch::Tensor> quantize_weights_fp8(const torch::Tenso
     return {q, s};
 }
 
-std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> swiglu_quant(const torch::Tensor& h, bool round_scale) {
-    TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.is_contiguous() && h.scalar_type() == torch::kBFloat16);
-    const int rows = (int)h.size(0), inter = (int)h.size(1) / 2;
-    TORCH_CHECK(h.size(1) % 256 == 0, "2*intermediate must be a multiple of 256");
-    auto a = torch::empty({rows, inter}, h.options());
-    auto aq = torch::empty({rows, inter}, h.options().dtype(torch::kFloat8_e4m3fn));
-    auto as = torch::empty({rows, inter / 128}, h.options().dtype(torch::kFloat32));
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> swiglu_quant(const torch::Tensor& h, bool round_scale,
+                                                                     const std::optional<torch::Tensor>& counts) {
+    TORCH_CHECK(h.is_cuda() && h.is_contiguous() && h.scalar_type() == torch::kBFloat16);
+    TORCH_CHECK(counts.has_value() ? h.dim() == 3 : h.dim() == 2, "h must be [rows, 2I], or [E, slots, 2I] with counts");
+    const int inter = (int)h.size(-1) / 2;
+    TORCH_CHECK(h.size(-1) % 256 == 0, "2*intermediate must be a multiple of 256");
+    std::vector<int64_t> lead(h.sizes().begin(), h.sizes().end() - 1);
+    const int rows = (int)(h.numel() / h.size(-1));
+    auto shape = [&](int64_t last) {
+        auto v = lead;
+        v.push_back(last);
+        return v;
+    };
+    const int* cnt = nullptr;
+    int slots = 0;
+    if (counts.has_value()) {
+        TORCH_CHECK(counts->is_cuda() && counts->scalar_type() == torch::kInt32 && counts->is_contiguous() &&
+                    counts->numel() == h.size(0), "counts must be int32 [E]");
+        cnt = counts->data_ptr<int>();
+        slots = (int)h.size(1);
+    }
+    auto a = torch::empty(shape(inter), h.options());
+    auto aq = torch::empty(shape(inter), h.options().dtype(torch::kFloat8_e4m3fn));
+    auto as = torch::empty(shape(inter / 128), h.options().dtype(torch::kFloat32));
     launch_swiglu_quant(h.data_ptr(), rows, inter, a.data_ptr(), aq.data_ptr(), as.data_ptr<float>(), round_scale ? 1 : 0,
-                        at::cuda::getCurrentCUDAStream());
+                        at::cuda::getCurrentCUDAStream(), cnt, slots);
     return {a, aq, as};
 }
 
@@ -289,7 +306,8 @@ void register_ops(pybind11::module_& m) {
           pybind11::arg("num_experts"), pybind11::arg("alignment") = 1, pybind11::arg("num_out_rows") = 0,
           pybind11::arg("zero_padding") = false);
     m.def("unpermute", &unpermute);
-    m.def("swiglu_quant", &swiglu_quant, pybind11::arg("h"), pybind11::arg("round_scale") = false);
+    m.def("swiglu_quant", &swiglu_quant, pybind11::arg("h"), pybind11::arg("round_scale") = false,
+          pybind11::arg("counts") = std::nullopt);
     m.def("quantize_weights_fp8", &quantize_weights_fp8, pybind11::arg("w"));
     m.def("grouped_gemm_bf16", &grouped_gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("offsets"),
           pybind11::arg("counts") = std::nullopt, pybind11::arg("mode") = 0, pybind11::arg("num_sms") = 0,

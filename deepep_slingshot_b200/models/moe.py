@@ -176,6 +176,35 @@ class MoEFFN(torch.nn.Module):
         return _MoEFunction.apply(x, topk_idx, topk_weights, self.w1, self.w2, self.buffer, self.num_experts,
                                   self.config)
 
+    def quantized_weights(self):
+        """FP8 weights with 128x128 scales (w1q, w1s, w2q, w2s), re-quantized only after the bf16
+        master weights change (inference reuses them across decode steps)."""
+        key = (self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(), self.w2._version)
+        if getattr(self, '_wq_key', None) != key:
+            w1q, w1s = quantize_weights_fp8(self.w1.detach())
+            w2q, w2s = quantize_weights_fp8(self.w2.detach())
+            self._wq = (w1q, w1s.contiguous(), w2q, w2s.contiguous())
+            self._wq_key = key
+        return self._wq
+
+    @torch.no_grad()
+    def forward_low_latency(self, ll_buffer, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
+                            num_max_dispatch_tokens_per_rank: int) -> torch.Tensor:
+        """Decode forward (inference) on the low-latency path, every step a hand-written sm_100a kernel:
+        FP8 dispatch with its receive fused into the masked gate/up GEMM
+        (`Buffer.low_latency_dispatch_gemm`) -> masked SwiGLU + FP8 requant -> masked down GEMM ->
+        top-k weighted `low_latency_combine`. `ll_buffer` is a `Buffer` with a low-latency region for
+        (num_max_dispatch_tokens_per_rank, hidden, num_experts); no permute, no packing copy."""
+        from ..ops.gemm import masked_grouped_gemm_fp8
+        from ..ops.quant import swiglu_quant
+        w1q, w1s, w2q, w2s = self.quantized_weights()
+        h, counts, handle, _ = ll_buffer.low_latency_dispatch_gemm(x, topk_idx, num_max_dispatch_tokens_per_rank,
+                                                                   self.num_experts, w1q, w1s)
+        _, aq, as_ = swiglu_quant(h, counts=counts)
+        y = masked_grouped_gemm_fp8(aq, as_, counts, w2q, w2s)
+        out, _, _ = ll_buffer.low_latency_combine(y, topk_idx, topk_weights, handle)
+        return out
+
 
 def moe_reference(x, topk_idx, topk_weights, w1_all, w2_all):
     """Single-process fp32 oracle with the layer's quantization points (FP8 x, FP8 weights, bf16 h,

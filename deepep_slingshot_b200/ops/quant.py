@@ -1,5 +1,5 @@
 """Per-token 1x128 FP8 e4m3 cast kernels (sm_100a) with the numerics of `utils.math`'s torch oracle."""
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -14,3 +14,21 @@ def per_token_cast_to_fp8(x: torch.Tensor, round_scale: bool = False) -> Tuple[t
 
 def per_token_cast_back(x: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return require_ext().per_token_cast_back(x, scales)
+
+
+def swiglu_quant(h: torch.Tensor, round_scale: bool = False, counts: Optional[torch.Tensor] = None):
+    """SwiGLU + 1x128 FP8 requantization on sm_100a: `h [rows, 2I]` (gate | up) -> (a bf16 [rows, I],
+    a_q fp8 [rows, I], a_s fp32 [rows, I/128]). With `counts` (int32 [E]) `h` is the masked per-expert
+    layout `[E, slots, 2I]`, outputs keep that shape, and rows at or beyond `counts[e]` are skipped
+    (left unwritten)."""
+    return require_ext().swiglu_quant(h, round_scale, counts)
+
+
+def swiglu_quant_reference(h: torch.Tensor, round_scale: bool = False):
+    """Torch oracle of `swiglu_quant` (fp32 math, bf16 `a`, then the per-token cast)."""
+    from ..utils.math import per_token_cast_to_fp8 as cast
+    inter = h.shape[-1] // 2
+    hf = h.float()
+    a = (torch.nn.functional.silu(hf[..., :inter]) * hf[..., inter:]).to(torch.bfloat16)
+    aq, as_ = cast(a.reshape(-1, inter), round_scale)
+    return a, aq.view(a.shape), as_.view(*a.shape[:-1], inter // 128)

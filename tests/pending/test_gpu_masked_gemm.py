@@ -90,3 +90,49 @@ def test_low_latency_dispatch_gemm(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f'needs {world} GPUs')
     run_ranks(_fused_body, world, backend='nccl', args=(64, 512, 8 * world, 4, 256))
+
+
+def test_masked_swiglu_quant():
+    from deepep_slingshot_b200.ops.quant import swiglu_quant, swiglu_quant_reference
+    torch.manual_seed(0)
+    E, slots, I = 3, 200, 256
+    h = torch.randn((E, slots, 2 * I), device='cuda').to(torch.bfloat16)
+    counts = torch.tensor([0, 7, 200], dtype=torch.int32, device='cuda')
+    a, aq, as_ = swiglu_quant(h, counts=counts)
+    ra, raq, ras = swiglu_quant_reference(h)
+    torch.cuda.synchronize()
+    for e, c in enumerate(counts.tolist()):
+        assert torch.equal(a[e, :c], ra[e, :c])
+        assert torch.equal(aq[e, :c].view(torch.uint8), raq[e, :c].view(torch.uint8))
+        assert torch.equal(as_[e, :c], ras[e, :c])
+
+
+def _moe_decode_body(rank, world, N, H, I, E, K):
+    from deepep_slingshot_b200 import Buffer
+    from deepep_slingshot_b200.models.moe import MoEFFN, moe_reference
+    group = dist.group.WORLD
+    buf = Buffer(group, num_rdma_bytes=Buffer.get_low_latency_rdma_size_hint(N, H, world, E), low_latency_mode=True,
+                 num_gpu_timeout_secs=20)
+    g = torch.Generator().manual_seed(7)  # same weights on every rank; each rank keeps its experts
+    w1_all = (torch.randn((E, 2 * I, H), generator=g) * 0.05).to(torch.bfloat16).cuda()
+    w2_all = (torch.randn((E, H, I), generator=g) * 0.05).to(torch.bfloat16).cuda()
+    E_l = E // world
+    layer = MoEFFN(buf, H, I, E, K)
+    with torch.no_grad():
+        layer.w1.copy_(w1_all[rank * E_l:(rank + 1) * E_l])
+        layer.w2.copy_(w2_all[rank * E_l:(rank + 1) * E_l])
+    gi = torch.Generator(device='cuda').manual_seed(100 + rank)
+    x = torch.randn((N, H), device='cuda', generator=gi).to(torch.bfloat16)
+    idx = torch.rand((N, E), device='cuda', generator=gi).topk(K, dim=1).indices.to(torch.int64)
+    wts = torch.softmax(torch.rand((N, K), device='cuda', generator=gi), dim=1)
+    out = layer.forward_low_latency(buf, x, idx, wts, N)
+    ref = moe_reference(x, idx, wts, w1_all, w2_all)
+    torch.cuda.synchronize()
+    assert _rel_err(out, ref.float()) < 3e-2
+
+
+@pytest.mark.parametrize('world', [1, 2])
+def test_moe_forward_low_latency(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f'needs {world} GPUs')
+    run_ranks(_moe_decode_body, world, backend='nccl', args=(32, 512, 256, 8 * world, 4))
