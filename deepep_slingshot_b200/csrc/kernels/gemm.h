@@ -30,6 +30,8 @@ int launch_grouped_gemm_fp8(const GemmArgs& a, int num_sms, cudaStream_t stream)
 // bf16 grouped GEMMs with both operands K-major (gemm_bf16_sm100.cu).
 //   mode 0 (M-grouped): a [rows][k], b [E*n][k], d [rows][n]; rows of expert e at offsets[e], 128-aligned
 //   mode 1 (K-grouped): a [m][k], b [n][k], d [E][m][n]; expert e contracts k in [offsets[e], offsets[e+1])
+// MN-major operands: b_mn_major makes b [E*k][n] (mode 0) or [k][n] (mode 1); a_mn_major (mode 1
+// only) makes a [k][m].
 struct Bf16GemmArgs {
     const void* a;
     const void* b;
@@ -39,6 +41,7 @@ struct Bf16GemmArgs {
     int mode;
     int rows, m, n, k, num_experts;
     int stages;
+    int a_mn_major, b_mn_major;
     KernelStatus st;
 };
 int launch_grouped_gemm_bf16(const Bf16GemmArgs& a, int num_sms, cudaStream_t stream);

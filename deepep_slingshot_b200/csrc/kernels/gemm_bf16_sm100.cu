@@ -1,11 +1,18 @@
 // Grouped bf16 GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a: the backward
-// ("dgrad" and "wgrad") GEMMs of the MoE expert FFN. Both operands are K-major ("NT"):
+// ("dgrad" and "wgrad") GEMMs of the MoE expert FFN. Operands are K-major by default ("NT"):
 //
 //   mode 0, M-grouped: D[r, n] = sum_k A[r, k] * B[e*N + n, k] for rows r of expert e
 //                      (A: [rows, K], rows of expert e at [offsets[e], offsets[e] + counts[e]),
 //                       128-aligned; B: [E*N, K]; D: [rows, N])
 //   mode 1, K-grouped: D[e, m, n] = sum_{k in [offsets[e], offsets[e+1])} A[m, k] * B[n, k]
 //                      (A: [M, Ktot]; B: [N, Ktot]; D: [E, M, N]; an expert with no rows gets zeros)
+//
+// MN-major operands (the tensor as it lies in memory, no transpose copy): with `b_mn_major` B is
+// [E*K, N] in mode 0 (the expert weights [E, K, N] of the forward) or [Ktot, N] in mode 1; with
+// `a_mn_major` (mode 1) A is [Ktot, M]. An MN-major tile is loaded as two TMA boxes of 64 K rows x
+// 64 MN elements (128-byte swizzle) 8 KiB apart and described to the MMA with the MN-major
+// descriptor (LBO = 8 KiB between MN atoms, SBO = 1 KiB between 8-row K groups) and the
+// instruction descriptor's transpose bit; each K = 16 instruction advances 2 KiB.
 //
 // Structure (same roles as the FP8 kernel, without the per-block scale promotion):
 //  * one persistent CTA per SM walks output tiles of 128 x 128;
@@ -37,6 +44,7 @@ __device__ __forceinline__ void tc_fence_after() { tc::fence_after(); }
 
 constexpr int kBM = 128, kBN = 128, kBK = 64;          // BK = 64 bf16 = one 128-byte swizzle row
 constexpr int kStageBytes = (kBM + kBN) * kBK * 2;       // 32 KiB
+constexpr int kMNAtomBytes = kBK * 128;                   // one MN-major box: 64 K rows x 128 bytes
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 2 * kBN;
@@ -59,7 +67,8 @@ struct Tile {
     int e, m0, n0;     // expert, first output row, first output column
     int k0, kblocks;   // first K element and number of 64-wide K blocks
     int64_t d_row0;    // first row of D (mode 1: e * M + m0)
-    int b_row0;        // first row of the B tile in its tensor map
+    int b_row0;        // first row of the B tile in its tensor map (K-major B)
+    int b_k_base;      // first K row of this expert in an MN-major B map (mode 0: e * K)
 };
 
 // Tile t of the launch (n innermost). Mode 0 uses the per-expert m-tile prefix in shared memory.
@@ -82,6 +91,7 @@ __device__ __forceinline__ bool tile_of(int t, const Bf16GemmArgs& a, const int*
         ti.kblocks = a.k / kBK;
         ti.d_row0 = ti.m0;
         ti.b_row0 = lo * a.n + ti.n0;
+        ti.b_k_base = lo * a.k;
         return true;
     }
     const int m_tiles = a.m / kBM;
@@ -95,11 +105,37 @@ __device__ __forceinline__ bool tile_of(int t, const Bf16GemmArgs& a, const int*
     ti.kblocks = (a.offsets[ti.e + 1] - a.offsets[ti.e]) / kBK;
     ti.d_row0 = (int64_t)ti.e * a.m + ti.m0;
     ti.b_row0 = ti.n0;
+    ti.b_k_base = 0;
     return true;
 }
 
+// Operand tile of one K block into shared memory: K-major, one box of 128 rows x 64 K; MN-major,
+// two boxes of 64 K rows x 64 MN elements.
+template <bool kMN>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, int k_row, int mn0, int kmajor_row0,
+                                             int k_elem, uint64_t* bar) {
+    if constexpr (kMN) {
+        tma_load_2d(dst, map, mn0, k_row, bar);
+        tma_load_2d(dst + kMNAtomBytes, map, mn0 + 64, k_row, bar);
+    } else {
+        tma_load_2d(dst, map, k_elem, kmajor_row0, bar);
+    }
+}
+
+template <bool kMN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t addr) {
+    if constexpr (kMN) return tc::smem_desc_mn_sw128(addr, kMNAtomBytes);
+    else return smem_desc_sw128(addr);
+}
+
+// Descriptor advance per K = 16 instruction, in 16-byte units: 32 bytes inside the K-major swizzle
+// row, or two 8-row K groups (2 KiB) of an MN-major tile.
+template <bool kMN>
+constexpr uint64_t kStep = kMN ? (16 * 128) / 16 : 2;
+
 }  // namespace
 
+template <bool kAMN, bool kBMN>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                       const __grid_constant__ CUtensorMap map_b,
                                                                       Bf16GemmArgs a) {
@@ -157,16 +193,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
                     if (!ok) break;
                     uint8_t* sa_tile = smem + (size_t)s * kStageBytes;
                     uint8_t* sb_tile = sa_tile + kBM * kBK * 2;
+                    const int kx = ti.k0 + kb * kBK;
                     mbar_arrive_expect_tx(&s_full[s], kStageBytes);
-                    tma_load_2d(sa_tile, &map_a, ti.k0 + kb * kBK, ti.m0, &s_full[s]);
-                    tma_load_2d(sb_tile, &map_b, ti.k0 + kb * kBK, ti.b_row0, &s_full[s]);
+                    load_operand<kAMN>(sa_tile, &map_a, kx, ti.m0, ti.m0, kx, &s_full[s]);
+                    load_operand<kBMN>(sb_tile, &map_b, ti.b_k_base + kx, ti.n0, ti.b_row0, kx, &s_full[s]);
                 }
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN);
+            constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN) | (kAMN ? 1u << 15 : 0u) | (kBMN ? 1u << 16 : 0u);
             uint32_t g = 0, j = 0;  // g: K-block stages consumed, j: non-empty tiles (TMEM buffer index)
             bool ok = true;
             Tile ti;
@@ -184,10 +221,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
                     tc_fence_after();
                     const uint32_t sa_addr = smem_u32(smem + (size_t)s * kStageBytes);
                     const uint32_t sb_addr = sa_addr + kBM * kBK * 2;
-                    const uint64_t da = smem_desc_sw128(sa_addr), db = smem_desc_sw128(sb_addr);
+                    const uint64_t da = operand_desc<kAMN>(sa_addr), db = operand_desc<kBMN>(sb_addr);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)  // K = 16 bf16 = 32 bytes per instruction: +2 in 16-byte units
-                        mma_bf16(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < kBK / 16; ++k)  // K = 16 bf16 per instruction
+                        mma_bf16(d_tmem, da + kStep<kAMN> * k, db + kStep<kBMN> * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                     mma_commit(&s_empty[s]);
                 }
                 if (!ok) break;
@@ -247,9 +284,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
 // ------------------------------------------------------------------------------------------------
 namespace {
 
-// 2D bf16 map over [rows][cols] (row-major), box 64 x 128 elements (128 x 128 bytes), 128-byte swizzle.
-bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
-    return tc::make_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, (uint32_t)kBK);
+// 2D bf16 map over [rows][cols] (row-major), 128-byte swizzle. K-major operand tiles: box 64 x 128
+// elements (K x rows); MN-major: box 64 x 64 (MN x K rows).
+bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, bool mn_major = false) {
+    return tc::make_map_2d_box(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, (uint32_t)kBK,
+                               mn_major ? (uint32_t)kBK : 128u);
+}
+
+template <bool kAMN, bool kBMN>
+int launch_instance(const CUtensorMap& map_a, const CUtensorMap& map_b, const Bf16GemmArgs& a, int num_sms,
+                    cudaStream_t stream) {
+    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
+    cudaFuncSetAttribute(grouped_gemm_bf16_kernel<kAMN, kBMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    grouped_gemm_bf16_kernel<kAMN, kBMN><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 }  // namespace
@@ -257,22 +305,31 @@ bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 int launch_grouped_gemm_bf16(const Bf16GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     Bf16GemmArgs a = args_in;
     if (a.n % kBN != 0 || a.num_experts <= 0 || a.num_experts > kMaxGemmExperts) return 1;
+    const bool amn = a.a_mn_major != 0, bmn = a.b_mn_major != 0;
     CUtensorMap map_a, map_b;
     if (a.mode == 0) {
-        if (a.k % kBK != 0 || a.rows <= 0) return 1;
+        if (a.k % kBK != 0 || a.rows <= 0 || amn) return 1;  // M-grouped rows are always K-major
         if (!make_map_bf16(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
-        if (!make_map_bf16(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k)) return 2;
+        if (bmn) {
+            if (!make_map_bf16(&map_b, a.b, (uint64_t)a.num_experts * a.k, (uint64_t)a.n, true)) return 2;
+        } else if (!make_map_bf16(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k)) {
+            return 2;
+        }
     } else {
         if (a.m % kBM != 0 || a.k % kBK != 0 || a.k <= 0) return 1;  // k = Ktot, offsets multiples of 64
-        if (!make_map_bf16(&map_a, a.a, (uint64_t)a.m, (uint64_t)a.k)) return 2;
-        if (!make_map_bf16(&map_b, a.b, (uint64_t)a.n, (uint64_t)a.k)) return 2;
+        if (amn ? !make_map_bf16(&map_a, a.a, (uint64_t)a.k, (uint64_t)a.m, true)
+                : !make_map_bf16(&map_a, a.a, (uint64_t)a.m, (uint64_t)a.k))
+            return 2;
+        if (bmn ? !make_map_bf16(&map_b, a.b, (uint64_t)a.k, (uint64_t)a.n, true)
+                : !make_map_bf16(&map_b, a.b, (uint64_t)a.n, (uint64_t)a.k))
+            return 2;
     }
     if (a.stages <= 0) a.stages = 6;
     if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
-    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
-    cudaFuncSetAttribute(grouped_gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    grouped_gemm_bf16_kernel<<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
-    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+    if (amn) return bmn ? launch_instance<true, true>(map_a, map_b, a, num_sms, stream)
+                        : launch_instance<true, false>(map_a, map_b, a, num_sms, stream);
+    return bmn ? launch_instance<false, true>(map_a, map_b, a, num_sms, stream)
+               : launch_instance<false, false>(map_a, map_b, a, num_sms, stream);
 }
 
 }  // namespace ep

@@ -68,18 +68,38 @@ inline EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2D map over a row-major [rows][cols] tensor of `type` (`elem_bytes` each), box `box_cols` x 128 rows
-// (box_cols * elem_bytes = 128 bytes), 128-byte swizzle.
-inline bool make_map_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base, uint64_t rows,
-                        uint64_t cols, uint32_t box_cols) {
+// K-major-in-memory operands read as MN-major (the contiguous dimension is M or N): 128-byte swizzle,
+// 8-row K groups 1024 B apart (stride byte offset), 64-element (128-byte) MN atoms `lbo_bytes` apart
+// (leading byte offset). One MMA of K = 16 16-bit elements covers two K groups: advance the start
+// address by 2048 bytes per instruction.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3fffu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3fffu) << 16;  // leading byte offset: next MN atom
+    d |= (uint64_t)(1024 >> 4) << 32;                   // stride byte offset: next 8-row K group
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// 2D map over a row-major [rows][cols] tensor of `type` (`elem_bytes` each), box `box_cols` x
+// `box_rows` (box_cols * elem_bytes = 128 bytes), 128-byte swizzle.
+inline bool make_map_2d_box(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base, uint64_t rows,
+                            uint64_t cols, uint32_t box_cols, uint32_t box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return false;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * (uint64_t)elem_bytes};
-    const cuuint32_t box[2] = {box_cols, 128};
+    const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t elem[2] = {1, 1};
     return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Box of 128 rows (the K-major tiles of the GEMM kernels).
+inline bool make_map_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base, uint64_t rows,
+                        uint64_t cols, uint32_t box_cols) {
+    return make_map_2d_box(map, type, elem_bytes, base, rows, cols, box_cols, 128);
 }
 
 }  // namespace tc

@@ -126,7 +126,8 @@ torch::Tensor masked_grouped_gemm_fp8(const torch::Tensor& a, const torch::Tenso
 // bf16 grouped GEMM, both operands K-major. mode 0: a [rows, k] grouped by `offsets` (128-aligned),
 // b [E, n, k] -> d [rows, n]. mode 1: a [m, Ktot], b [n, Ktot], offsets [E+1] over K -> d [E, m, n].
 torch::Tensor grouped_gemm_bf16(const torch::Tensor& a, const torch::Tensor& b, const torch::Tensor& offsets,
-                                const std::optional<torch::Tensor>& counts, int mode, int num_sms, double timeout_s) {
+                                const std::optional<torch::Tensor>& counts, int mode, int num_sms, double timeout_s,
+                                bool a_mn_major, bool b_mn_major) {
     TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.is_contiguous() && a.scalar_type() == torch::kBFloat16);
     TORCH_CHECK(b.is_cuda() && b.is_contiguous() && b.scalar_type() == torch::kBFloat16);
     TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.is_contiguous() && offsets.dim() == 1);
@@ -136,18 +137,24 @@ torch::Tensor grouped_gemm_bf16(const torch::Tensor& a, const torch::Tensor& b, 
     Bf16GemmArgs g{};
     torch::Tensor d;
     if (mode == 0) {
-        TORCH_CHECK(b.dim() == 3 && b.size(0) == E && b.size(2) == a.size(1), "mode 0: b must be [E, n, k]");
+        TORCH_CHECK(!a_mn_major, "mode 0: a is always [rows, k]");
+        if (b_mn_major) {
+            TORCH_CHECK(b.dim() == 3 && b.size(0) == E && b.size(1) == a.size(1), "mode 0, MN-major b: b must be [E, k, n]");
+        } else {
+            TORCH_CHECK(b.dim() == 3 && b.size(0) == E && b.size(2) == a.size(1), "mode 0: b must be [E, n, k]");
+        }
         g.rows = (int)a.size(0);
         g.k = (int)a.size(1);
-        g.n = (int)b.size(1);
+        g.n = (int)(b_mn_major ? b.size(2) : b.size(1));
         TORCH_CHECK(g.k % 64 == 0 && g.n % 128 == 0, "mode 0: k % 64 == 0 and n % 128 == 0");
         if (counts.has_value()) TORCH_CHECK(counts->scalar_type() == torch::kInt32 && counts->numel() == E);
         d = torch::empty({g.rows, g.n}, a.options());
     } else {
-        TORCH_CHECK(b.dim() == 2 && b.size(1) == a.size(1), "mode 1: b must be [n, Ktot]");
-        g.m = (int)a.size(0);
-        g.k = (int)a.size(1);
-        g.n = (int)b.size(0);
+        g.m = (int)(a_mn_major ? a.size(1) : a.size(0));
+        g.k = (int)(a_mn_major ? a.size(0) : a.size(1));
+        TORCH_CHECK(b.dim() == 2 && (b_mn_major ? b.size(0) : b.size(1)) == g.k,
+                    b_mn_major ? "mode 1, MN-major b: b must be [Ktot, n]" : "mode 1: b must be [n, Ktot]");
+        g.n = (int)(b_mn_major ? b.size(1) : b.size(0));
         TORCH_CHECK(g.m % 128 == 0 && g.n % 128 == 0 && g.k % 64 == 0, "mode 1: m, n % 128 == 0 and Ktot % 64 == 0");
         d = torch::empty({E, g.m, g.n}, a.options());
     }
@@ -163,6 +170,8 @@ torch::Tensor grouped_gemm_bf16(const torch::Tensor& a, const torch::Tensor& b, 
     g.d = d.data_ptr();
     g.mode = mode;
     g.num_experts = E;
+    g.a_mn_major = a_mn_major ? 1 : 0;
+    g.b_mn_major = b_mn_major ? 1 : 0;
     g.st = op_status(timeout_s);
     const int rc = launch_grouped_gemm_bf16(g, num_sms, at::cuda::getCurrentCUDAStream());
     TORCH_CHECK(rc == 0, "grouped_gemm_bf16 launch failed (code " + std::to_string(rc) + ")");
@@ -311,7 +320,7 @@ void register_ops(pybind11::module_& m) {
     m.def("quantize_weights_fp8", &quantize_weights_fp8, pybind11::arg("w"));
     m.def("grouped_gemm_bf16", &grouped_gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("offsets"),
           pybind11::arg("counts") = std::nullopt, pybind11::arg("mode") = 0, pybind11::arg("num_sms") = 0,
-          pybind11::arg("timeout_s") = 10.0);
+          pybind11::arg("timeout_s") = 10.0, pybind11::arg("a_mn_major") = false, pybind11::arg("b_mn_major") = false);
     m.def("masked_grouped_gemm_fp8", &masked_grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"),
           pybind11::arg("counts"), pybind11::arg("b"), pybind11::arg("sb"), pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 100.0);

@@ -32,11 +32,13 @@ def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
 
 
 # Backward expert GEMMs: `grouped` (torch's grouped bf16 GEMM, default), `tcgen05` (this library's
-# kernels; they take K-major operands, so the weights are transposed every step: with 256 local
-# experts on one GPU that costs ~45 GB of copies and made the step 2x slower, measured 107 vs 52 ms),
-# `loop` (per-expert matmuls).
+# kernels with K-major operands, so the weights and activations are transposed every step: with 256
+# local experts on one GPU that costs ~45 GB of copies and made the step 2x slower, measured 107 vs
+# 52 ms), `tcgen05_mn` (the same kernels reading the weights and activations as they lie, through
+# MN-major operand descriptors: no transposes), `loop` (per-expert matmuls).
 _BWD_MODE = os.environ.get('DEEPEP_B200_MOE_BWD', 'grouped')
-_GROUPED_BWD = {'enabled': _BWD_MODE in ('tcgen05', 'grouped'), 'tcgen05': _BWD_MODE == 'tcgen05'}
+_GROUPED_BWD = {'enabled': _BWD_MODE in ('tcgen05', 'tcgen05_mn', 'grouped'),
+                'tcgen05': _BWD_MODE in ('tcgen05', 'tcgen05_mn'), 'mn_major': _BWD_MODE == 'tcgen05_mn'}
 
 
 def _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx) -> bool:
@@ -62,8 +64,15 @@ def _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp,
     if _GROUPED_BWD['tcgen05']:
         # sm_100a kernels: dgrad M-grouped against K-major (transposed) weights, wgrad K-grouped over
         # the expert row ranges of the transposed activations.
-        from ..ops.gemm import grouped_gemm_bf16, grouped_gemm_bf16_wgrad
+        from ..ops.gemm import grouped_gemm_bf16, grouped_gemm_bf16_wgrad, grouped_gemm_bf16_wgrad_rows
         offs32 = offsets.to(torch.int32).contiguous()
+        if _GROUPED_BWD['mn_major']:
+            g_a = grouped_gemm_bf16(gy, w2, offs32, counts, b_mn_major=True).float()                 # [R, I]
+            g_w2 = grouped_gemm_bf16_wgrad_rows(gy, aa, offs32)                                       # [E, H, I]
+            g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
+            g_xp[:R] = grouped_gemm_bf16(g_h, w1, offs32, counts, b_mn_major=True)                   # [R, H]
+            ctx.g_w1, ctx.g_w2 = grouped_gemm_bf16_wgrad_rows(g_h, xx, offs32), g_w2                 # [E, 2I, H]
+            return True
         g_a = grouped_gemm_bf16(gy, w2.transpose(1, 2).contiguous(), offs32, counts).float()          # [R, I]
         g_w2 = grouped_gemm_bf16_wgrad(gy.t().contiguous(), aa.t().contiguous(), offs32)            # [E, H, I]
         g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)

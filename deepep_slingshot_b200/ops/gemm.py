@@ -21,10 +21,12 @@ def grouped_gemm_fp8(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: tor
 
 
 def grouped_gemm_bf16(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, counts: Optional[torch.Tensor] = None,
-                      num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
+                      num_sms: int = 0, timeout_s: float = 10.0, b_mn_major: bool = False) -> torch.Tensor:
     """M-grouped bf16 GEMM on tcgen05: rows of `a [rows, k]` grouped by expert (`offsets [E+1]`,
-    128-aligned) times `b [E, n, k]` (K-major weights) -> `[rows, n]` bf16 (fp32 accumulation)."""
-    return require_ext().grouped_gemm_bf16(a, b, offsets, counts, 0, num_sms, timeout_s)
+    128-aligned) times `b [E, n, k]` (K-major weights) -> `[rows, n]` bf16 (fp32 accumulation).
+    With `b_mn_major=True`, `b` is `[E, k, n]` and is read as it lies (no transpose copy): the forward
+    weights of the layer serve the input-gradient GEMM directly."""
+    return require_ext().grouped_gemm_bf16(a, b, offsets, counts, 0, num_sms, timeout_s, False, b_mn_major)
 
 
 def grouped_gemm_bf16_wgrad(a_t: torch.Tensor, b_t: torch.Tensor, offsets: torch.Tensor, num_sms: int = 0,
@@ -32,6 +34,14 @@ def grouped_gemm_bf16_wgrad(a_t: torch.Tensor, b_t: torch.Tensor, offsets: torch
     """K-grouped bf16 GEMM on tcgen05 (weight gradients): `a_t [m, Ktot]`, `b_t [n, Ktot]` with expert e
     owning K range [offsets[e], offsets[e+1]) -> `[E, m, n]` = per-expert a_t[:, K_e] @ b_t[:, K_e]^T."""
     return require_ext().grouped_gemm_bf16(a_t, b_t, offsets, None, 1, num_sms, timeout_s)
+
+
+def grouped_gemm_bf16_wgrad_rows(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, num_sms: int = 0,
+                                 timeout_s: float = 10.0) -> torch.Tensor:
+    """K-grouped bf16 GEMM on tcgen05 over row-major activations, read as they lie (MN-major operands,
+    no transposes): `a [Ktot, m]`, `b [Ktot, n]` with expert e owning rows [offsets[e], offsets[e+1])
+    (64-aligned) -> `[E, m, n]` = per-expert a[K_e]^T @ b[K_e]."""
+    return require_ext().grouped_gemm_bf16(a, b, offsets, None, 1, num_sms, timeout_s, True, True)
 
 
 def grouped_gemm_bf16_reference(a, b, offsets, counts=None) -> torch.Tensor:
