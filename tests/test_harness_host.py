@@ -175,3 +175,31 @@ def test_ladder_stops_and_resumes(tmp_path):
     assert calls == ['a', 'b', 'b', 'c']             # passed gates are skipped
     st = load_state(out + '/ladder_state.json')
     assert st['passed'] == ['a', 'b', 'c'] and st['resumes'][0]['reason'] == 'fixed the notify wait'
+
+
+_TOPO = """\tGPU0\tGPU1\tGPU2\tNIC0\tCPU Affinity\tNUMA Affinity\tGPU NUMA ID
+GPU0\t X \tNV18\tNV18\tSYS\t0-55\t0\t\tN/A
+GPU1\tNV18\t X \tNV18\tSYS\t0-55\t0\t\tN/A
+GPU2\tNV18\tNV18\t X \tNODE\t56-111\t1\t\tN/A
+NIC0\tSYS\tSYS\tNODE\t X \t\t\t\t
+
+Legend:
+
+  X    = Self
+  NV#  = Connection traversing a bonded set of # NVLinks
+"""
+
+
+def test_box_probe_topology_and_cpu_collect(tmp_path):
+    from deepep_slingshot_b200.harness import box_probe
+    m = box_probe.parse_topo_matrix(_TOPO)
+    assert sorted(m) == ['GPU0', 'GPU1', 'GPU2']
+    assert m['GPU0'] == {'GPU0': 'X', 'GPU1': 'NV18', 'GPU2': 'NV18'}
+    assert m['GPU2']['GPU1'] == 'NV18'
+    assert box_probe.parse_topo_matrix('') == {}
+    (tmp_path / 'MEASURED_PEAKS.json').write_text('{"hbm_gbs": 1.0}')
+    info = box_probe.collect(bandwidth=True, repo_root=str(tmp_path))  # CPU box: no GPUs, no failure
+    assert info['measured_peaks'] == {'hbm_gbs': 1.0}
+    assert isinstance(info['gpus'], list) and isinstance(info['peer_access'], list)
+    assert box_probe.main(['--out', str(tmp_path / 'box.json')]) == 0
+    assert (tmp_path / 'box.json').exists()
