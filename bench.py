@@ -130,6 +130,26 @@ def init(args):
     return rank, world, local
 
 
+def moe_roofline_seconds(rows: float, hidden: int, inter: int, local_experts: int, world: int, num_recv: float,
+                         bf16_flops: float = 1650.1e12, hbm_bytes_per_s: float = 6558.4e9,
+                         nvlink_bytes_per_s: float = 770e9) -> dict:
+    """Lower bounds of one MoE training step (forward + backward) per rank, in seconds:
+    compute (FP8 forward at 2x the measured bf16 peak, bf16 backward at the measured peak), NVLink
+    (dispatch + combine of the forward and their mirrors in the backward), and HBM: every local
+    expert weight element moves at least 8 bytes per step (bf16 master read + FP8 write by the
+    quantization, FP8 read by the forward GEMMs, bf16 read by the input-gradient GEMMs, bf16 weight
+    gradient write). The step can be no faster than the largest of the three."""
+    fwd_flops = 6.0 * rows * hidden * inter
+    bwd_flops = 12.0 * rows * hidden * inter
+    t_compute = fwd_flops / (2 * bf16_flops) + bwd_flops / bf16_flops
+    remote = (world - 1) / world
+    nv_bytes = 2 * remote * num_recv * ((hidden + hidden // 128 * 4) + 2 * hidden)
+    t_comm = nv_bytes / nvlink_bytes_per_s
+    weight_elems = local_experts * 3.0 * hidden * inter
+    t_hbm = 8.0 * weight_elems / hbm_bytes_per_s
+    return {'compute': t_compute, 'nvlink': t_comm, 'hbm': t_hbm, 'bound': max(t_compute, t_comm, t_hbm)}
+
+
 def max_over_ranks(values):
     t = torch.tensor(values, dtype=torch.float64, device='cuda')
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -330,21 +350,18 @@ def main():
         mts = max_over_ranks(mts)
         ms_moe = sum(mts) / len(mts)
         rows = sum_over_ranks(int((midx >= 0).sum())) / world  # expert rows per rank (average)
-        fwd_flops = 6.0 * rows * H * inter
-        bwd_flops = 12.0 * rows * H * inter
-        peak = 1650.1e12  # measured cuBLAS bf16 burst (MEASURED_PEAKS.json); FP8 counted at 2x
-        t_compute = fwd_flops / (2 * peak) + bwd_flops / peak
-        remote = (world - 1) / world
-        nv_bytes = 2 * remote * num_recv * ((H + H // 128 * 4) + 2 * H)  # fwd dispatch+combine, bwd mirror
-        t_comm = nv_bytes / 770e9
+        # measured peaks (MEASURED_PEAKS.json): cuBLAS bf16 burst, STREAM-style copy; FP8 counted at 2x bf16
+        roof = moe_roofline_seconds(rows, H, inter, E // world, world, num_recv)
         moe = {'moe_tokens_per_s': N * world / (ms_moe * 1e-3), 'moe_ms_per_step': ms_moe,
-               'moe_roofline_fraction': max(t_compute, t_comm) / (ms_moe * 1e-3),
+               'moe_roofline_fraction': roof['bound'] / (ms_moe * 1e-3),
+               'moe_roofline_ms': {k: v * 1e3 for k, v in roof.items()},
                'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
                               'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs',
                               'backward': ('bf16 tcgen05 grouped GEMMs (dgrad M-grouped, wgrad K-grouped)' if _moe_mod._GROUPED_BWD['tcgen05']
                                            else 'bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled']
                                            else 'bf16 per-expert torch matmuls (stand-in)'),
-                              'roofline': 'max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes at 770 GB/s)'}}
+                              'roofline': ('max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes '
+                                           'at 770 GB/s, 8 bytes per local weight element per step at measured 6558 GB/s HBM)')}}
         del layer
         torch.cuda.empty_cache()
 

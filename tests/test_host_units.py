@@ -229,3 +229,19 @@ def test_masked_gemm_oracle_matches_grouped_oracle():
     packed = grouped_gemm_fp8_reference(xq, xs, wq, ws, offsets, counts).view(E, slots, N)
     assert torch.equal(masked, packed)
     assert masked[0, 5:].abs().sum() == 0 and masked[1].abs().sum() == 0
+
+
+def test_bench_moe_roofline_bounds():
+    """The MoE step's lower bound is the largest of compute, NVLink and the weight bytes through HBM."""
+    import importlib.util
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), 'bench.py')
+    spec = importlib.util.spec_from_file_location('_bench_under_test', path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    one = bench.moe_roofline_seconds(32768, 7168, 2048, 256, 1, 4096)
+    assert one['nvlink'] == 0 and one['bound'] == one['hbm']          # all 256 experts on one GPU
+    assert abs(one['hbm'] - 8 * 256 * 3 * 7168 * 2048 / 6558.4e9) < 1e-12
+    eight = bench.moe_roofline_seconds(32768, 7168, 2048, 32, 8, 21900)
+    assert eight['bound'] == eight['compute'] and eight['hbm'] == one['hbm'] / 8
+    assert abs(eight['compute'] - (6 * 32768 * 7168 * 2048 / (2 * 1650.1e12) + 12 * 32768 * 7168 * 2048 / 1650.1e12)) < 1e-12
