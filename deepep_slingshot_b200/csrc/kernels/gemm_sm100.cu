@@ -19,7 +19,13 @@
 //  * warps 2..9: read the K-block partial with `tcgen05.ld`, release the TMEM buffer at once, and
 //    accumulate sa*sb*partial in fp32 registers (the per-block scale promotion that fp32 scales need);
 //    after the last K block they write bf16 rows.
+// Tile width: 128 (default) or 256 columns (`DEEPEP_B200_GEMM_BN=256`, when N allows): a 256-wide
+// tile stages 48 KiB of A and B per 8.4 MFLOP instead of 32 KiB per 4.2 MFLOP, easing the L2 ->
+// shared-memory feed; the two accumulators then fill all 512 TMEM columns and each epilogue thread
+// promotes 128 columns, 32 at a time.
 // Every mbarrier wait is bounded (a status is reported, the kernel returns).
+#include <cstdlib>
+
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -39,11 +45,15 @@ using tc::tmem_wait_ld;
 __device__ __forceinline__ void tc_fence_before() { tc::fence_before(); }
 __device__ __forceinline__ void tc_fence_after() { tc::fence_after(); }
 
-constexpr int kBM = 128, kBN = 128, kBK = 128;  // tile; BK = 128 fp8 = one 128-byte swizzle row
-constexpr int kStageBytes = (kBM + kBN) * kBK;  // 32 KiB
+constexpr int kBM = 128, kBK = 128;  // BK = 128 fp8 = one 128-byte swizzle row
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
-constexpr uint32_t kTmemCols = 2 * kBN;        // two fp32 accumulators of 128 columns
+// Tile width kBN (128 or 256): a stage holds A (kBM x kBK) and B (kBN x kBK); TMEM holds two fp32
+// accumulators of kBN columns. 256-wide tiles stage 48 KiB per 8.4 MFLOP instead of 32 KiB per 4.2.
+template <int kBN>
+constexpr int kStageBytesT = (kBM + kBN) * kBK;
+template <int kBN>
+constexpr uint32_t kTmemColsT = 2 * kBN;
 
 // Instruction descriptor, kind::f8f6f4: E4M3 x E4M3 -> F32, both K-major, M = 128, N = kBN.
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
@@ -69,6 +79,7 @@ struct TileInfo {
 };
 
 // Map a linear tile index to (expert, m0, n0) using the per-expert m-tile prefix in shared memory.
+template <int kBN>
 __device__ __forceinline__ bool tile_of(int t, const int* s_mt_prefix, int E, int n_tiles, const int* offsets, TileInfo& ti) {
     const int total = s_mt_prefix[E] * n_tiles;
     if (t >= total) return false;
@@ -87,8 +98,12 @@ __device__ __forceinline__ bool tile_of(int t, const int* s_mt_prefix, int E, in
 
 }  // namespace
 
+template <int kBN>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                      const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+    constexpr int kStageBytes = kStageBytesT<kBN>;
+    constexpr uint32_t kTmemCols = kTmemColsT<kBN>;
+    constexpr int kCols = kBN / 2;  // accumulator columns per epilogue thread (one row, one half)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
     __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
@@ -136,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             uint32_t g = 0;
             bool ok = true;
             TileInfo ti;
-            for (int t = blockIdx.x; ok && tile_of(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+            for (int t = blockIdx.x; ok && tile_of<kBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
                 for (int kb = 0; kb < KB && ok; ++kb, ++g) {
                     const int s = g % S;
                     ok = wait_bar(&s_empty[s], ((g / S) & 1) ^ 1, a.st);
@@ -156,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             uint32_t g = 0;
             bool ok = true;
             TileInfo ti;
-            for (int t = blockIdx.x; ok && tile_of(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+            for (int t = blockIdx.x; ok && tile_of<kBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
                 for (int kb = 0; kb < KB && ok; ++kb, ++g) {
                     const int s = g % S, b = g & 1;
                     ok = wait_bar(&s_tempty[b], ((g >> 1) & 1) ^ 1, a.st) && wait_bar(&s_full[s], (g / S) & 1, a.st);
@@ -178,18 +193,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
         // ---------------------------------------------------------------- epilogue / scale promotion
         const int ew = warp - 2;
         const int q = warp & 3;      // TMEM lane quarter this warp may access
-        const int h = ew >> 2;       // column half: [64h, 64h + 64)
+        const int h = ew >> 2;       // column half: [kCols * h, kCols * (h + 1))
         const int row = 32 * q + lane;
         uint32_t g = 0;
         bool ok = true;
         TileInfo ti;
-        for (int t = blockIdx.x; ok && tile_of(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
-            float acc[64];
+        for (int t = blockIdx.x; ok && tile_of<kBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+            float acc[kCols];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            for (int i = 0; i < kCols; ++i) acc[i] = 0.f;
             const int m = ti.m0 + row;
             const float* sa_row = a.sa + (int64_t)m * KB;
-            const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + ti.n0 / 128) * KB;
+            const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + (ti.n0 + kCols * h) / 128) * KB;
             for (int kb = 0; kb < KB; ++kb, ++g) {
                 const int b = g & 1;
                 const float scale = sa_row[kb] * sb_blk[kb];
@@ -200,21 +215,36 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                     break;
                 }
                 tc_fence_after();
-                float v[64];
-                const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + 64 * h);
-                tmem_ld_32(taddr, v);
-                tmem_ld_32(taddr + 32, v + 32);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_tempty[b]);
+                const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + kCols * h);
+                if constexpr (kCols == 64) {
+                    float v[64];
+                    tmem_ld_32(taddr, v);
+                    tmem_ld_32(taddr + 32, v + 32);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_tempty[b]);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) acc[i] = fmaf(scale, v[i], acc[i]);
+                    for (int i = 0; i < 64; ++i) acc[i] = fmaf(scale, v[i], acc[i]);
+                } else {
+                    // 128 columns: 32 at a time (register budget: 128 accumulators + 32 staged values).
+#pragma unroll
+                    for (int c = 0; c < kCols; c += 32) {
+                        float v[32];
+                        tmem_ld_32(taddr + c, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_tempty[b]);
+                }
             }
             if (!ok) break;
-            __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + 64 * h;
+            __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + kCols * h;
 #pragma unroll
-            for (int c = 0; c < 64; c += 8) {
+            for (int c = 0; c < kCols; c += 8) {
                 int4 o;
                 __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
@@ -236,25 +266,44 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
 // ------------------------------------------------------------------------------------------------
 namespace {
 
-// 2D uint8 map over [rows][cols] (row-major), box 128 x 128 bytes, 128-byte swizzle.
-bool make_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
-    return tc::make_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols, 128);
+// 2D uint8 map over [rows][cols] (row-major), box 128 bytes x `box_rows` rows, 128-byte swizzle.
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows = 128) {
+    return tc::make_map_2d_box(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols, 128, box_rows);
+}
+
+// Tile width: 128 by default; DEEPEP_B200_GEMM_BN=256 selects 256-wide tiles when n allows.
+int tile_width(int n) {
+    static const int requested = [] {
+        const char* v = std::getenv("DEEPEP_B200_GEMM_BN");
+        return v != nullptr ? std::atoi(v) : 128;
+    }();
+    return requested == 256 && n % 256 == 0 ? 256 : 128;
+}
+
+template <int kBN>
+int launch_tiles(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
+    constexpr int kStageBytes = kStageBytesT<kBN>;
+    GemmArgs a = args_in;
+    CUtensorMap map_a, map_b;
+    if (!make_map_u8(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
+    if (!make_map_u8(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k, (uint32_t)kBN)) return 2;
+    // Stages that fit the 227 KiB a CTA may use next to the static shared memory.
+    const int max_stages = (int)((220 * 1024 - 1024) / kStageBytes);
+    if (a.stages <= 0) a.stages = 6;
+    if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
+    if (a.stages > max_stages) a.stages = max_stages;
+    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
+    cudaFuncSetAttribute(grouped_gemm_fp8_kernel<kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    grouped_gemm_fp8_kernel<kBN><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 }  // namespace
 
 int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
-    GemmArgs a = args_in;
-    if (a.k % kBK != 0 || a.n % kBN != 0 || a.num_experts > kMaxGemmExperts || a.rows <= 0) return 1;
-    CUtensorMap map_a, map_b;
-    if (!make_map_u8(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
-    if (!make_map_u8(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k)) return 2;
-    if (a.stages <= 0) a.stages = 6;
-    if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
-    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
-    cudaFuncSetAttribute(grouped_gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    grouped_gemm_fp8_kernel<<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
-    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+    if (args_in.k % kBK != 0 || args_in.n % 128 != 0 || args_in.num_experts > kMaxGemmExperts || args_in.rows <= 0) return 1;
+    return tile_width(args_in.n) == 256 ? launch_tiles<256>(args_in, num_sms, stream)
+                                        : launch_tiles<128>(args_in, num_sms, stream);
 }
 
 }  // namespace ep
