@@ -113,6 +113,7 @@ struct CombineArgs {
     int push_blocks;                 // set by the launcher
     int chunk;                       // push order: -1 wavefront over destinations, 0 contiguous, N chunks of N rows
     int stages;
+    int announce_lagged;             // 1: announce a batch of rows one batch later, without draining the stores
     KernelStatus st;
 };
 void launch_combine(const CombineArgs& a, int num_sms, cudaStream_t stream);

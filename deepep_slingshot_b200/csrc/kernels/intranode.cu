@@ -790,14 +790,19 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
         } else {
             // Slots recycle on read-completion (as in the pull). Arrivals are announced per batch of
             // kAnnounce rows: one drain of this thread's bulk stores, one sys-scope fence, then relaxed
-            // reds (a release per row would wait for an NVLink round trip every row).
+            // reds (a release per row would wait for an NVLink round trip every row). With
+            // `announce_lagged` the batch is announced when the NEXT batch is complete issued:
+            // `wait_group kAnnounce` then only waits for the older batch, so the stores of the newer
+            // one stay in flight instead of draining the pipe every kAnnounce rows.
             constexpr int kAnnounce = 16;
             const int lag = S / 2 < 4 ? S / 2 : 4;
+            const bool lagged = a.announce_lagged != 0;
             int* arrivals[kMaxRanks];
 #pragma unroll
             for (int r = 0; r < kMaxRanks; ++r)
                 arrivals[r] = r < R ? reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[r]) + a.layout.arrival_off) : nullptr;
             int pend_t = -1, pend_d = 0;  // lane i holds the i-th row of the current announce batch
+            int prev_t = -1, prev_d = 0, prev_cnt = 0;  // lagged mode: the batch waiting for announcement
             for (int kk = 0, k = 0; k < my_rows; ++kk) {
                 const int j = row_at(kk);
                 if (j < 0) continue;
@@ -827,7 +832,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
                     release_slots(p, k, lag);
                 }
                 const bool flush = (k % kAnnounce) == kAnnounce - 1 || k + 1 == my_rows;
-                if (flush) {
+                if (flush && !lagged) {
                     const int cnt = (k % kAnnounce) + 1;
                     if (lane == 0) {
                         bulk_wait<0>();
@@ -838,9 +843,48 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
                         const int tt = __shfl_sync(0xffffffffu, pend_t, i), dd = __shfl_sync(0xffffffffu, pend_d, i);
                         if (lane == 0) atomicAdd_system(arrivals[dd] + tt, 1);
                     }
+                } else if (flush) {
+                    // The previous batch's groups are all older than the kAnnounce (or fewer) groups
+                    // just committed for the current batch: waiting until at most kAnnounce remain
+                    // completes exactly them. The last batch drains everything and announces both.
+                    const int cnt = (k % kAnnounce) + 1;
+                    const bool last = k + 1 == my_rows;
+                    if (lane == 0) {
+                        if (last || cnt < kAnnounce) bulk_wait<0>();
+                        else bulk_wait<kAnnounce>();
+                        fence_proxy_async_global();
+                        fence_sys();
+                    }
+                    for (int i = 0; i < prev_cnt; ++i) {
+                        const int tt = __shfl_sync(0xffffffffu, prev_t, i), dd = __shfl_sync(0xffffffffu, prev_d, i);
+                        if (lane == 0) atomicAdd_system(arrivals[dd] + tt, 1);
+                    }
+                    if (last) {
+                        for (int i = 0; i < cnt; ++i) {
+                            const int tt = __shfl_sync(0xffffffffu, pend_t, i), dd = __shfl_sync(0xffffffffu, pend_d, i);
+                            if (lane == 0) atomicAdd_system(arrivals[dd] + tt, 1);
+                        }
+                        prev_cnt = 0;
+                    } else {
+                        prev_t = pend_t;
+                        prev_d = pend_d;
+                        prev_cnt = cnt;
+                    }
                 }
                 __syncwarp();
                 ++k;
+            }
+            if (lagged && prev_cnt > 0) {
+                // The loop left early (an expired wait or a bounds error): announce what completed.
+                if (lane == 0) {
+                    bulk_wait<0>();
+                    fence_proxy_async_global();
+                    fence_sys();
+                }
+                for (int i = 0; i < prev_cnt; ++i) {
+                    const int tt = __shfl_sync(0xffffffffu, prev_t, i), dd = __shfl_sync(0xffffffffu, prev_d, i);
+                    if (lane == 0) atomicAdd_system(arrivals[dd] + tt, 1);
+                }
             }
         }
     }

@@ -226,6 +226,10 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     // Combine push order: -1 = wavefront over destinations in token order (default), >= 0 as above.
     const char* cchunk = std::getenv("DEEPEP_B200_COMBINE_ROW_CHUNK");
     combine_row_chunk_ = cchunk != nullptr ? std::max(-1, std::atoi(cchunk)) : -1;
+    // Combine arrival announcements: "drain" (default) waits for a batch's stores before announcing
+    // it; "lagged" announces each batch one batch later and keeps the newer stores in flight.
+    const char* announce = std::getenv("DEEPEP_B200_COMBINE_ANNOUNCE");
+    combine_announce_lagged_ = announce != nullptr && std::string(announce) == "lagged";
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
@@ -800,6 +804,7 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     ca.out_topk_weights = out_w.has_value() ? out_w->data_ptr<float>() : nullptr;
     ca.stages = 0;
     ca.chunk = combine_row_chunk_;
+    ca.announce_lagged = combine_announce_lagged_ ? 1 : 0;
     ca.st = st;
     prof_mark(stream, 4);
     launch_combine(ca, num_sms, stream);

@@ -163,6 +163,7 @@ class Buffer {
     bool profile_enabled_ = false;
     int row_chunk_ = 0;
     int combine_row_chunk_ = -1;
+    bool combine_announce_lagged_ = false;
     std::vector<std::pair<int, cudaEvent_t>> prof_events_;
 
     int rank_, num_ranks_, device_id_;
