@@ -83,4 +83,54 @@ __host__ __device__ __forceinline__ bool masked_gemm_tile(int t, int E, int n_ti
     return true;
 }
 
+// Tile order of the fused dispatch -> grouped GEMM: level-major, where level l holds the l-th m-tile
+// of every expert that has more than l m-tiles, n-tile innermost. The receive side fills each
+// expert's rows in claim order, so an expert's tile l completes before its tile l + 1 and the
+// level-0 tiles of all experts complete first; taking tiles in level order follows the arrivals.
+// `fused_gemm_levels` sorts experts by decreasing m-tile count (counting sort) so each level's
+// experts are a prefix of `order`, and writes level_prefix[l] = tiles (in units of n-tile rows)
+// before level l, for l = 0..levels. `hist` needs max_levels + 1 ints. Returns the number of
+// levels (the largest m-tile count), or -1 if it exceeds max_levels.
+__host__ __device__ __forceinline__ int fused_gemm_levels(const int* m_tiles, int E, int* order, int* level_prefix,
+                                                          int max_levels, int* hist) {
+    int levels = 0;
+    for (int v = 0; v <= max_levels; ++v) hist[v] = 0;
+    for (int e = 0; e < E; ++e) {
+        const int v = m_tiles[e];
+        if (v > max_levels) return -1;
+        ++hist[v];
+        if (v > levels) levels = v;
+    }
+    // Descending order: experts with value v start after all experts with a larger value.
+    int above = 0;  // experts with m_tiles > v
+    for (int v = max_levels; v >= 0; --v) {
+        const int c = hist[v];
+        hist[v] = above;  // first position of value v
+        above += c;
+    }
+    for (int e = 0; e < E; ++e) order[hist[m_tiles[e]]++] = e;
+    // After the placement hist[v] = first position of value v + its count = experts with m_tiles >= v.
+    level_prefix[0] = 0;
+    for (int l = 0; l < levels; ++l) level_prefix[l + 1] = level_prefix[l] + hist[l + 1];
+    return levels;
+}
+
+// Tile t of the fused order: (level mt, expert e, n-tile nt); false past the last tile.
+__host__ __device__ __forceinline__ bool fused_gemm_tile(int t, int n_tiles, const int* level_prefix, int levels,
+                                                         const int* order, int& mt, int& e, int& nt) {
+    if (t < 0 || levels <= 0) return false;
+    const int r = t / n_tiles;
+    if (r >= level_prefix[levels]) return false;
+    int lo = 0, hi = levels - 1;  // largest level with level_prefix[level] <= r
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (level_prefix[mid] <= r) lo = mid;
+        else hi = mid - 1;
+    }
+    mt = lo;
+    e = order[r - level_prefix[lo]];
+    nt = t - r * n_tiles;
+    return true;
+}
+
 }  // namespace ep

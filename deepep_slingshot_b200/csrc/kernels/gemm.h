@@ -71,4 +71,40 @@ struct MaskedGemmArgs {
 // Returns 0 on success, 1 bad arguments, 2 tensor-map encode failure, 3 launch failure.
 int launch_masked_gemm_fp8(const MaskedGemmArgs& a, int num_sms, cudaStream_t stream);
 
+// Normal-mode dispatch receive fused with the gate/up grouped FP8 GEMM (fused_dispatch_gemm.cu).
+// Launched after the dispatch's stage and notify steps (expert alignment 128). Zeroed on entry:
+// claim [E_l], landed [E_l * max_mtiles], tile_counter [1].
+struct FusedDispatchGemmArgs {
+    PeerTable peers;
+    NormalLayout layout;
+    RecordFormat rec;                // FP8 records (x_bytes == hidden)
+    int rank, num_ranks, num_local_experts, num_topk;
+    const int* rank_prefix_matrix;   // [R][R] from notify
+    const int* dev_num_recv;         // received tokens (device, from notify)
+    int num_out_rows;                // rows allocated in row_map / recv_* (>= received tokens)
+    int pull_ctas;                   // CTAs that pull first, then join the GEMM
+    int chunk;                       // row dealing of the pull pairs (as the plain pull)
+    const int* num_recv_per_expert;  // [E_l] 128-aligned counts from notify
+    const int* raw_counts;           // [E_l] received rows per expert (notify's statistics output)
+    int* claim;                      // [E_l] slot counters
+    int* landed;                     // [E_l][max_mtiles] rows landed per 128-row tile
+    int max_mtiles;                  // m-tiles per expert the buffers allow
+    uint8_t* a;                      // [rows_cap][hidden] e4m3, experts at 128-aligned offsets
+    float* sa;                       // [rows_cap][hidden/128]
+    int rows_cap;
+    int* row_map;                    // [num_out_rows][K]: operand row of (received token, k), -1 if not local
+    float* recv_topk_weights;        // [num_out_rows][K]: local weights (0 elsewhere)
+    int* recv_src_idx;               // [num_out_rows]: source token of every received row
+    HostCounters* host;              // host-mapped counts (null: none)
+    int host_ticket;
+    const void* b;                   // [E_l][n][hidden] e4m3 weights
+    const float* sb;                 // [E_l][n/128][hidden/128]
+    int n;
+    void* d;                         // [rows_cap][n] bf16
+    int* tile_counter;
+    KernelStatus st;
+};
+// Returns 0 on success, 1 bad arguments, 2 tensor-map encode failure, 3 launch failure.
+int launch_fused_dispatch_gemm(const FusedDispatchGemmArgs& a, int num_sms, cudaStream_t stream);
+
 }  // namespace ep

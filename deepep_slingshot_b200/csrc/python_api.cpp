@@ -98,6 +98,7 @@ PYBIND11_MODULE(_C, m) {
         .def("sample_clock", &ep::Buffer::sample_clock)
         .def("get_dispatch_layout", &ep::Buffer::get_dispatch_layout)
         .def("intranode_dispatch", &ep::Buffer::intranode_dispatch)
+        .def("intranode_dispatch_gemm", &ep::Buffer::intranode_dispatch_gemm)
         .def("intranode_combine", &ep::Buffer::intranode_combine)
         .def("barrier", &ep::Buffer::barrier)
         .def("clean_low_latency_buffer", &ep::Buffer::clean_low_latency_buffer)

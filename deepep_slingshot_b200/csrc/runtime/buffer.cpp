@@ -752,6 +752,170 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
             recv_src_idx, send_head, num_recv_per_expert, event};
 }
 
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+           torch::Tensor, std::vector<int>, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
+Buffer::intranode_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights,
+                                int num_experts, const torch::Tensor& w, const torch::Tensor& w_scales, bool round_scale,
+                                int num_sms, int pull_ctas) {
+    check_error();
+    TORCH_CHECK(available_, "buffer not synced");
+    TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16, "x must be contiguous bf16 [tokens, hidden]");
+    const int N = (int)x.size(0), H = (int)x.size(1), R = num_ranks_;
+    TORCH_CHECK(H % 128 == 0, "hidden must be a multiple of 128");
+    TORCH_CHECK(topk_idx.scalar_type() == torch::kInt64 && topk_idx.is_contiguous() && topk_idx.dim() == 2 && topk_idx.size(0) == N);
+    const int K = (int)topk_idx.size(1);
+    TORCH_CHECK(K <= kMaxTopk, "top-k larger than 16 is not supported");
+    TORCH_CHECK(topk_weights.scalar_type() == torch::kFloat32 && topk_weights.is_contiguous() && topk_weights.size(0) == N &&
+                topk_weights.size(1) == K);
+    TORCH_CHECK(num_experts > 0 && num_experts % R == 0 && num_experts / R <= kMaxLocalExperts);
+    const int E_l = num_experts / R;
+    TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.is_contiguous() && w.scalar_type() == torch::kFloat8_e4m3fn && w.size(0) == E_l &&
+                    w.size(2) == H && w.size(1) % 128 == 0,
+                "weights must be contiguous [num_local_experts, n, hidden] e4m3 with n % 128 == 0");
+    const int n = (int)w.size(1);
+    TORCH_CHECK(w_scales.scalar_type() == torch::kFloat32 && w_scales.is_contiguous() && w_scales.dim() == 3 &&
+                w_scales.size(0) == E_l && w_scales.size(1) == n / 128 && w_scales.size(2) == H / 128);
+    const NormalLayout L = compute_normal_layout(num_nvl_bytes_, H, R);
+    TORCH_CHECK(N <= L.capacity, "num_tokens exceeds the buffer capacity");
+    const RecordFormat rec = record_format(H, K, /*fp8=*/true);
+    int sm_count = 148;
+    EP_CUDA_CHECK(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device_id_));
+    if (num_sms <= 0 || num_sms > sm_count) num_sms = sm_count;
+    if (pull_ctas <= 0) pull_ctas = std::min(32, num_sms);
+    TORCH_CHECK(pull_ctas <= num_sms, "pull_ctas must not exceed num_sms");
+    const int num_out_rows = R * L.capacity;  // received tokens, worst case
+    const int max_mtiles = (num_out_rows + 127) / 128;
+    TORCH_CHECK(max_mtiles <= 512, "the fused dispatch supports at most 65536 received rows per expert; use dispatch()");
+    const int64_t rows_cap = (int64_t)num_out_rows * std::min(K, E_l) + (int64_t)E_l * 127;
+    TORCH_CHECK(rows_cap < (int64_t)1 << 31);
+
+    auto i32 = torch::dtype(torch::kInt32).device(torch::kCUDA);
+    // Zeroed on the compute stream before the comm stream waits for it.
+    auto raw_counts = torch::zeros({E_l}, i32);
+    auto counters = torch::zeros({E_l + (int64_t)E_l * max_mtiles + 1}, i32);  // claim | landed | tile counter
+
+    const int ticket = ++dispatch_epoch_;
+    std::optional<EventHandle> no_event;
+    StreamScope scope(comm_stream_, no_event, false);
+    auto stream = scope.comm.stream();
+    const KernelStatus st = status();
+    const PeerTable peers = nvl_peers();
+    uint8_t* my_base = static_cast<uint8_t*>(nvl_base_);
+
+    // 1) stage (bf16 -> FP8 records), as dispatch()
+    StageArgs sa{};
+    sa.x = x.data_ptr();
+    sa.topk_idx = topk_idx.data_ptr<int64_t>();
+    sa.topk_weights = topk_weights.data_ptr<float>();
+    sa.staging = my_base + L.staging_off;
+    sa.pull_done = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->pull_done;
+    sa.num_tokens = N;
+    sa.hidden = H;
+    sa.num_topk = K;
+    sa.topk_pad = (int)align_up(K, 4);
+    sa.in_elem_bytes = 2;
+    sa.quantize = 1;
+    sa.round_scale = round_scale ? 1 : 0;
+    sa.num_ranks = R;
+    sa.dispatch_epoch = &reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->dispatch_epoch;
+    sa.token_mask = my_base + L.scratch_off;
+    sa.expert_counts = reinterpret_cast<int*>(my_base + L.scratch_off + align_up(L.capacity, kAlign));
+    sa.num_experts = num_experts;
+    sa.num_local_experts = E_l;
+    sa.rec = rec;
+    sa.record_stride = L.record_bytes;
+    sa.st = st;
+    launch_dispatch_stage(sa, num_sms, stream);
+
+    // 2) notify: counts, 128-aligned per-expert rows, raw per-expert rows (statistics output)
+    auto send_head = torch::empty({N, R}, i32);
+    auto rpm = torch::empty({R, R}, i32);
+    auto spm = torch::empty({R, R}, i32);
+    auto recv_rank_prefix = torch::empty({R + 1}, i32);
+    auto aligned_counts = torch::empty({E_l}, i32);
+    NotifyArgs na{};
+    na.topk_idx = sa.topk_idx;
+    na.num_tokens = N;
+    na.num_topk = K;
+    na.num_experts = num_experts;
+    na.num_local_experts = E_l;
+    na.num_ranks = R;
+    na.rank = rank_;
+    na.host_ticket = ticket;
+    na.token_mask = sa.token_mask;
+    na.expert_counts = sa.expert_counts;
+    na.expert_alignment = 128;
+    na.peers = peers;
+    na.layout = L;
+    na.send_head = send_head.data_ptr<int>();
+    na.rank_prefix_matrix = rpm.data_ptr<int>();
+    na.send_prefix_matrix = spm.data_ptr<int>();
+    na.recv_rank_prefix = recv_rank_prefix.data_ptr<int>();
+    na.num_recv_per_expert = aligned_counts.data_ptr<int>();
+    na.dev_num_recv = dev_workspace_ + 1;
+    na.cumulative_stats = raw_counts.data_ptr<int>();
+    na.host = host_counters_dev_;
+    na.st = st;
+    launch_dispatch_notify(na, stream);
+
+    // 3) outputs (worst-case rows; exact views after the CPU sync) + the fused receive / GEMM
+    auto a_rows = torch::empty({rows_cap, H}, x.options().dtype(torch::kFloat8_e4m3fn));
+    auto a_scales = torch::empty({rows_cap, H / 128}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+    auto h = torch::empty({rows_cap, n}, x.options());
+    auto row_map = torch::empty({num_out_rows, K}, i32);
+    auto recv_w = torch::empty({num_out_rows, K}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+    auto recv_src_idx = torch::empty({num_out_rows}, i32);
+
+    FusedDispatchGemmArgs fa{};
+    fa.peers = peers;
+    fa.layout = L;
+    fa.rec = rec;
+    fa.rank = rank_;
+    fa.num_ranks = R;
+    fa.num_local_experts = E_l;
+    fa.num_topk = K;
+    fa.rank_prefix_matrix = rpm.data_ptr<int>();
+    fa.dev_num_recv = dev_workspace_ + 1;
+    fa.num_out_rows = num_out_rows;
+    fa.pull_ctas = pull_ctas;
+    fa.chunk = row_chunk_;
+    fa.num_recv_per_expert = aligned_counts.data_ptr<int>();
+    fa.raw_counts = raw_counts.data_ptr<int>();
+    fa.claim = counters.data_ptr<int>();
+    fa.landed = fa.claim + E_l;
+    fa.max_mtiles = max_mtiles;
+    fa.tile_counter = fa.landed + (int64_t)E_l * max_mtiles;
+    fa.a = static_cast<uint8_t*>(a_rows.data_ptr());
+    fa.sa = a_scales.data_ptr<float>();
+    fa.rows_cap = (int)rows_cap;
+    fa.row_map = row_map.data_ptr<int>();
+    fa.recv_topk_weights = recv_w.data_ptr<float>();
+    fa.recv_src_idx = recv_src_idx.data_ptr<int>();
+    fa.host = host_counters_dev_;
+    fa.host_ticket = ticket;
+    fa.b = w.data_ptr();
+    fa.sb = w_scales.data_ptr<float>();
+    fa.n = n;
+    fa.d = h.data_ptr();
+    fa.st = st;
+    const int rc = launch_fused_dispatch_gemm(fa, num_sms, stream);
+    TORCH_CHECK(rc == 0, "fused dispatch + GEMM launch failed (code " + std::to_string(rc) + ")");
+    EP_CUDA_CHECK(cudaGetLastError());
+
+    wait_host_counters(ticket);
+    const int num_recv = host_counters_->num_recv_tokens;
+    std::vector<int> per_expert_list(host_counters_->num_recv_tokens_per_expert,
+                                     host_counters_->num_recv_tokens_per_expert + E_l);
+    int64_t rows = 0;
+    for (int c : per_expert_list) rows += c;
+    scope.finish(false, {});
+    auto offsets = torch::zeros({E_l + 1}, i32);
+    offsets.narrow(0, 1, E_l).copy_(aligned_counts.cumsum(0));
+    return {h.narrow(0, 0, rows), a_rows.narrow(0, 0, rows), a_scales.narrow(0, 0, rows), row_map.narrow(0, 0, num_recv),
+            recv_w.narrow(0, 0, num_recv), offsets, raw_counts, recv_src_idx.narrow(0, 0, num_recv), per_expert_list, rpm, spm,
+            recv_rank_prefix, send_head};
+}
+
 std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandle>> Buffer::intranode_combine(
     const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
     const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,

@@ -134,6 +134,17 @@ class Buffer {
                          const std::optional<torch::Tensor>& dispatch_wait_recv_cost_stats,
                          int num_max_dispatch_tokens_per_rank, int num_experts, bool use_fp8, bool round_scale,
                          bool use_ue8m0, bool async, bool return_recv_hook);
+    // Normal-mode FP8 dispatch whose receive writes the expert-grouped GEMM operand and runs the
+    // gate/up grouped GEMM in the same launch, tile by tile as rows land (fused_dispatch_gemm.cu).
+    // Returns (h [rows, n] bf16, a [rows, hidden] e4m3, a_scales [rows, hidden/128], row_map
+    // [num_recv, K], recv_topk_weights [num_recv, K], expert_offsets [E_l + 1], expert_counts [E_l],
+    // recv_src_idx, aligned per-expert counts (host), rank_prefix_matrix, send_prefix_matrix,
+    // recv_rank_prefix, send_head).
+    std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+               torch::Tensor, std::vector<int>, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
+    intranode_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights,
+                            int num_experts, const torch::Tensor& w, const torch::Tensor& w_scales, bool round_scale,
+                            int num_sms, int pull_ctas);
     // FP8 low-latency dispatch whose receive runs inside the first expert GEMM (masked, tcgen05):
     // returns (gemm out [E_l, slots, n] bf16, recv_x, recv_scales, recv_count, src_info, src_meta, half).
     std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int>

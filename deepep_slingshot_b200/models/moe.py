@@ -15,6 +15,7 @@ backend/tests/sglang_dispatcher_smoke.py:107-124); this is the flagship workload
 config "full MoE layer forward+backward".
 """
 import os
+from types import SimpleNamespace
 from typing import Optional
 
 import torch
@@ -36,6 +37,9 @@ def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
 # local experts on one GPU that costs ~45 GB of copies and made the step 2x slower, measured 107 vs
 # 52 ms), `tcgen05_mn` (the same kernels reading the weights and activations as they lie, through
 # MN-major operand descriptors: no transposes), `loop` (per-expert matmuls).
+# DEEPEP_B200_MOE_FUSED_DISPATCH=1: the forward's dispatch receive and gate/up GEMM run as one kernel
+# (Buffer.dispatch_gemm) instead of dispatch -> permute -> grouped GEMM.
+_FUSED_DISPATCH = {'enabled': os.environ.get('DEEPEP_B200_MOE_FUSED_DISPATCH', '0') == '1'}
 _BWD_MODE = os.environ.get('DEEPEP_B200_MOE_BWD', 'grouped')
 _GROUPED_BWD = {'enabled': _BWD_MODE in ('tcgen05', 'tcgen05_mn', 'grouped'),
                 'tcgen05': _BWD_MODE in ('tcgen05', 'tcgen05_mn'), 'mn_major': _BWD_MODE == 'tcgen05_mn'}
@@ -103,11 +107,20 @@ class _MoEFunction(torch.autograd.Function):
     def forward(ctx, x, topk_idx, topk_weights, w1, w2, buffer, num_experts, config):
         E_l = w1.shape[0]
         inter = w1.shape[1] // 2
-        (rxq, rxs), ridx, rw, _, handle, _ = buffer.dispatch(x, topk_idx=topk_idx, topk_weights=topk_weights,
-                                                             num_experts=num_experts, quantize_fp8=True, config=config)
-        p = permute(rxq, ridx, E_l, alignment=128, probs=rw, x_scales=rxs)
-        w1q, w1s = quantize_weights_fp8(w1.detach())
-        h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts)
+        if _FUSED_DISPATCH['enabled']:
+            w1q, w1s = quantize_weights_fp8(w1.detach())
+            # Dispatch receive and gate/up GEMM in one launch, tile by tile (Buffer.dispatch_gemm).
+            h, grp, handle = buffer.dispatch_gemm(x, topk_idx, topk_weights.float().contiguous(), num_experts, w1q,
+                                                  w1s.contiguous())
+            p = SimpleNamespace(x=grp['x'], scales=grp['scales'], row_map=grp['row_map'],
+                                expert_offsets=grp['expert_offsets'], expert_counts=grp['expert_counts'])
+            rw = grp['topk_weights']
+        else:
+            (rxq, rxs), ridx, rw, _, handle, _ = buffer.dispatch(x, topk_idx=topk_idx, topk_weights=topk_weights,
+                                                                 num_experts=num_experts, quantize_fp8=True, config=config)
+            p = permute(rxq, ridx, E_l, alignment=128, probs=rw, x_scales=rxs)
+            w1q, w1s = quantize_weights_fp8(w1.detach())
+            h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts)
         a, aq, as_ = require_ext().swiglu_quant(h, False)
         w2q, w2s = quantize_weights_fp8(w2.detach())
         y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts)

@@ -284,6 +284,33 @@ class Buffer:
         return (recv_x, recv_scales) if recv_scales is not None else recv_x, recv_topk_idx, recv_topk_weights, \
             num_recv_tokens_per_expert_list, handle, EventOverlap(event)
 
+    @nvtx_range('ep.dispatch_gemm')
+    def dispatch_gemm(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor, num_experts: int,
+                      weights: torch.Tensor, weight_scales: torch.Tensor, round_scale: bool = False, num_sms: int = 0,
+                      pull_ctas: int = 0):
+        """FP8 dispatch whose receive feeds the gate/up grouped GEMM in the same launch.
+
+        The stage and notify steps are `dispatch(..., quantize_fp8=True, expert_alignment=128)`'s.
+        Then one persistent kernel pulls every received token, writes it once per local expert it
+        selected into an expert-grouped, 128-aligned FP8 operand, and runs the grouped FP8 GEMM with
+        `weights [E_local, n, hidden]` (e4m3, 128x128 `weight_scales`) tile by tile as the rows land;
+        `pull_ctas` CTAs pull first and then join the GEMM (default: 32).
+
+        Returns `(h, grouped, handle)`: `h [rows, n]` bf16 (rows of expert e at
+        `grouped['expert_offsets'][e]`, valid for the first `grouped['expert_counts'][e]` of them),
+        `grouped` with `x` / `scales` (the FP8 operand and its 1x128 scales), `row_map [num_recv, K]`
+        (operand row of (received token, k), -1 if not local), `topk_weights [num_recv, K]` (local),
+        `expert_offsets`, `expert_counts` and the aligned `num_recv_tokens_per_expert_list`; `handle`
+        is the one `combine` takes.
+        """
+        (h, a, a_scales, row_map, recv_w, offsets, counts, recv_src_idx, per_expert, rank_prefix_matrix,
+         send_prefix_matrix, recv_rank_prefix, send_head) = self.runtime.intranode_dispatch_gemm(
+            x, topk_idx, topk_weights, num_experts, weights, weight_scales, round_scale, num_sms, pull_ctas)
+        handle = (rank_prefix_matrix, send_prefix_matrix, recv_rank_prefix, recv_src_idx, send_head >= 0, send_head)
+        grouped = {'x': a, 'scales': a_scales, 'row_map': row_map, 'topk_weights': recv_w, 'expert_offsets': offsets,
+                   'expert_counts': counts, 'num_recv_tokens_per_expert_list': per_expert}
+        return h, grouped, handle
+
     @nvtx_range('ep.combine')
     def combine(self, x: torch.Tensor, handle: Tuple, topk_weights: Optional[torch.Tensor] = None,
                 bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None,

@@ -6,7 +6,8 @@
 //   2. the pipeline-ring credit protocol (counters, slots, ring directions) delivers every message in
 //      order, never overwrites an unconsumed slot and never deadlocks, under random interleavings;
 //   3. LogFMT-10 packing round-trips and the code -> value mapping stays within its error bound;
-//   4. the masked grouped GEMM's tile order covers every tile once and balances decode batches.
+//   4. the masked grouped GEMM's tile order covers every tile once and balances decode batches;
+//   5. the fused dispatch -> GEMM tile order covers every live tile once, level by level.
 // Prints "ALL OK" and exits 0 on success.
 #include <algorithm>
 #include <cmath>
@@ -235,10 +236,46 @@ static void check_masked_tiles(std::mt19937& rng) {
     }
 }
 
+// Fused dispatch -> GEMM tile order: every (expert, m-tile, n-tile) with m-tile < the expert's count
+// appears exactly once, levels come in order, and each level lists experts with that many tiles.
+static void check_fused_tiles(std::mt19937& rng) {
+    for (int trial = 0; trial < 3000; ++trial) {
+        const int E = 1 + rng() % 300, n_tiles = 1 + rng() % 40, max_levels = 1 + rng() % 64;
+        std::vector<int> mt(E), order(E, -1), prefix(max_levels + 1, 0), hist(max_levels + 1);
+        for (int e = 0; e < E; ++e) mt[e] = rng() % 3 == 0 ? 0 : (int)(rng() % (max_levels + 1));
+        const int levels = ep::fused_gemm_levels(mt.data(), E, order.data(), prefix.data(), max_levels, hist.data());
+        int want = 0;
+        for (int e = 0; e < E; ++e) want = std::max(want, mt[e]);
+        CHECK(levels == want, "levels %d != %d", levels, want);
+        std::vector<int> pos(E, 0);
+        for (int i = 0; i < E; ++i) {
+            CHECK(order[i] >= 0 && order[i] < E && ++pos[order[i]] == 1, "order is not a permutation");
+            if (i) CHECK(mt[order[i - 1]] >= mt[order[i]], "order not descending");
+        }
+        std::vector<int> seen((size_t)E * (max_levels + 1) * n_tiles, 0);
+        int total = 0, last_level = 0;
+        int l, e, nt;
+        for (int t = 0; ep::fused_gemm_tile(t, n_tiles, prefix.data(), levels, order.data(), l, e, nt); ++t) {
+            CHECK(l < mt[e] && nt >= 0 && nt < n_tiles, "invalid tile %d (l=%d e=%d mt=%d)", t, l, e, mt[e]);
+            CHECK(l >= last_level, "levels out of order");
+            last_level = l;
+            CHECK(++seen[((size_t)e * (max_levels + 1) + l) * n_tiles + nt] == 1, "tile visited twice");
+            ++total;
+        }
+        int expect = 0;
+        for (int x = 0; x < E; ++x) expect += mt[x] * n_tiles;
+        CHECK(total == expect, "%d tiles visited, expected %d", total, expect);
+    }
+    int hist[4], order[2], prefix[4];
+    const int too_many[2] = {5, 1};
+    CHECK(ep::fused_gemm_levels(too_many, 2, order, prefix, 3, hist) == -1, "overflow not reported");
+}
+
 int main() {
     std::mt19937 rng(12345);
     check_dealing(rng);
     check_masked_tiles(rng);
+    check_fused_tiles(rng);
     check_pp_ring(rng);
     check_logfmt(rng);
     std::printf("ALL OK\n");
