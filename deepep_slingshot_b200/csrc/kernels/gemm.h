@@ -66,6 +66,13 @@ struct MaskedGemmArgs {
     int* recv_count;            // fused: [E] out
     int* cumulative_stats;      // fused: [E] += counts (optional)
     int64_t l2_prefetch_bytes;  // fused: weights each CTA prefetches into L2 while it waits
+    // Fused low-latency combine send (combine != 0): row m of expert e goes to its source rank's
+    // combine slot [token][k] of the combine half (from the dispatch half's source info) instead of
+    // d; the last CTA then releases `combine_done` in every rank, as the combine's send phase does.
+    int combine;
+    PeerTable ll_peers;
+    LLLayout ll_layout;
+    int dispatch_half, combine_half, rank;
     KernelStatus st;
 };
 // Returns 0 on success, 1 bad arguments, 2 tensor-map encode failure, 3 launch failure.

@@ -25,8 +25,11 @@
 // publishes them to the CTA through an mbarrier. The weights stream from HBM while the tokens are
 // still crossing NVLink. The last CTA to read the counters does the receive bookkeeping of the
 // low-latency dispatch hook: recv_count, cumulative statistics, and the reset of the flags and
-// slot counters for the next use of the half. All waits are bounded; an expired wait reports and
-// the kernel returns.
+// slot counters for the next use of the half. Fused combine send (`combine`): the epilogue stores
+// each finished row straight into its source rank's combine slot over NVLink (the down projection's
+// output never lands locally) and the last CTA releases the combine's flags; the receive hook of
+// `low_latency_combine` then does the weighted reduction. All waits are bounded; an expired wait
+// reports and the kernel returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -262,7 +265,25 @@ __global__ void __launch_bounds__(kThreads, 1) masked_gemm_fp8_kernel(const __gr
             }
             if (!ok) break;
             if (m < count) {
-                __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + ((int64_t)ti.e * a.slots + m) * a.n + ti.n0 + 64 * h;
+                __nv_bfloat16* d = nullptr;
+                if (!a.combine) {
+                    d = static_cast<__nv_bfloat16*>(a.d) + ((int64_t)ti.e * a.slots + m) * a.n + ti.n0 + 64 * h;
+                } else {
+                    // The row's combine slot on its source rank (peer store over NVLink).
+                    const LLLayout& L = a.ll_layout;
+                    const uint8_t* dsp = static_cast<const uint8_t*>(a.ll_peers.base[a.rank]) + (int64_t)a.dispatch_half * L.half_bytes;
+                    const int64_t idx = (int64_t)ti.e * a.slots + m;
+                    const int meta = reinterpret_cast<const int*>(dsp + L.recv_src_meta_off)[idx];
+                    const int tok = reinterpret_cast<const int*>(dsp + L.recv_src_info_off)[idx];
+                    const int src = meta / L.num_topk, k = meta % L.num_topk;
+                    if (src < 0 || src >= L.num_ranks || tok < 0 || tok >= L.max_tokens) {
+                        report_error(a.st, kErrBounds, src, tok);
+                        continue;
+                    }
+                    uint8_t* dst = static_cast<uint8_t*>(a.ll_peers.base[src]) + (int64_t)a.combine_half * L.half_bytes +
+                                   L.combine_recv_off;
+                    d = reinterpret_cast<__nv_bfloat16*>(dst) + ((int64_t)tok * L.num_topk + k) * L.hidden + ti.n0 + 64 * h;
+                }
 #pragma unroll
                 for (int c = 0; c < 64; c += 8) {
                     int4 o;
@@ -280,6 +301,23 @@ __global__ void __launch_bounds__(kThreads, 1) masked_gemm_fp8_kernel(const __gr
         tc::fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
     }
+    if (a.combine && threadIdx.x == 0) {
+        // Every thread's peer stores precede the barrier above; the system fence orders them before
+        // the counter, and the last CTA releases this rank's flag in every rank's combine half.
+        const LLLayout& L = a.ll_layout;
+        uint8_t* mine = static_cast<uint8_t*>(a.ll_peers.base[a.rank]) + (int64_t)a.combine_half * L.half_bytes;
+        LLCtrl* ctrl = reinterpret_cast<LLCtrl*>(mine + L.ctrl_off);
+        fence_sys();
+        const int old = atom_add_acq_rel_gpu(&ctrl->csend_finished_blocks, 1);
+        if (old == (int)gridDim.x - 1) {
+            ctrl->csend_finished_blocks = 0;
+            fence_sys();
+            for (int d = 0; d < L.num_ranks; ++d) {
+                uint8_t* peer = static_cast<uint8_t*>(a.ll_peers.base[d]) + (int64_t)a.combine_half * L.half_bytes;
+                st_release_sys(&reinterpret_cast<LLCtrl*>(peer + L.ctrl_off)->combine_done[a.rank], 1);
+            }
+        }
+    }
 }
 
 int launch_masked_gemm_fp8(const MaskedGemmArgs& args_in, int num_sms, cudaStream_t stream) {
@@ -288,6 +326,8 @@ int launch_masked_gemm_fp8(const MaskedGemmArgs& args_in, int num_sms, cudaStrea
         num_sms <= 0)
         return 1;
     if ((a.ll == nullptr) == (a.counts == nullptr)) return 1;  // exactly one source of counts
+    if (a.combine && (a.n != a.ll_layout.hidden || a.ll_layout.num_ranks <= 0 || a.rank < 0 || a.rank >= a.ll_layout.num_ranks))
+        return 1;
     if (a.ll != nullptr && (a.recv_count == nullptr || a.num_ranks <= 0 || a.num_ranks > kMaxRanks)) return 1;
     CUtensorMap map_a, map_b;
     if (!tc::make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.a, (uint64_t)a.num_experts * a.slots, (uint64_t)a.k, 128))

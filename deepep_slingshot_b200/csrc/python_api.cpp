@@ -104,6 +104,7 @@ PYBIND11_MODULE(_C, m) {
         .def("clean_low_latency_buffer", &ep::Buffer::clean_low_latency_buffer)
         .def("low_latency_dispatch", &ep::Buffer::low_latency_dispatch)
         .def("low_latency_dispatch_gemm", &ep::Buffer::low_latency_dispatch_gemm)
+        .def("low_latency_gemm_combine", &ep::Buffer::low_latency_gemm_combine)
         .def("low_latency_combine", &ep::Buffer::low_latency_combine)
         .def("get_next_low_latency_combine_buffer", &ep::Buffer::get_next_low_latency_combine_buffer)
         .def("low_latency_update_mask_buffer", &ep::Buffer::low_latency_update_mask_buffer)

@@ -1147,6 +1147,83 @@ Buffer::low_latency_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& t
     return {out, recv_x, recv_scales, recv_count, std::get<3>(sent), std::get<4>(sent), half};
 }
 
+torch::Tensor Buffer::low_latency_gemm_combine(const torch::Tensor& a, const torch::Tensor& a_scales,
+                                              const torch::Tensor& recv_count, const torch::Tensor& w, const torch::Tensor& w_scales,
+                                              const torch::Tensor& topk_idx, const torch::Tensor& topk_weights, int dispatch_half,
+                                              int num_max_dispatch_tokens_per_rank, int num_experts, int num_sms) {
+    check_error();
+    TORCH_CHECK(available_ && ll_base_ != nullptr, "low-latency mode needs num_rdma_bytes > 0");
+    TORCH_CHECK(!enable_shrink_, "the fused combine does not support shrink mode");
+    const int R = num_ranks_, maxT = num_max_dispatch_tokens_per_rank;
+    TORCH_CHECK(a.is_cuda() && a.dim() == 3 && a.is_contiguous() && a.scalar_type() == torch::kFloat8_e4m3fn,
+                "a must be a contiguous [num_local_experts, slots, k] e4m3 tensor");
+    TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == torch::kFloat8_e4m3fn, "w must be [E_l, hidden, k] e4m3");
+    const int E_l = (int)a.size(0), slots = (int)a.size(1), k = (int)a.size(2), H = (int)w.size(1);
+    TORCH_CHECK(slots == R * maxT && w.size(0) == E_l && w.size(2) == k && k % 128 == 0 && H % 128 == 0);
+    TORCH_CHECK(a_scales.scalar_type() == torch::kFloat32 && a_scales.dim() == 3 && a_scales.size(0) == E_l &&
+                a_scales.size(1) == slots && a_scales.size(2) == k / 128);
+    TORCH_CHECK(w_scales.scalar_type() == torch::kFloat32 && w_scales.is_contiguous() && w_scales.size(0) == E_l &&
+                w_scales.size(1) == H / 128 && w_scales.size(2) == k / 128);
+    TORCH_CHECK(recv_count.scalar_type() == torch::kInt32 && recv_count.is_contiguous() && recv_count.numel() == E_l);
+    const int N = (int)topk_idx.size(0), K = (int)topk_idx.size(1);
+    TORCH_CHECK(topk_idx.scalar_type() == torch::kInt64 && topk_idx.is_contiguous() && N <= maxT && K <= kMaxTopk);
+    TORCH_CHECK(topk_weights.scalar_type() == torch::kFloat32 && topk_weights.is_contiguous() && topk_weights.size(0) == N);
+    LLLayout L = compute_ll_layout(num_rdma_bytes_, maxT, H, num_experts, R);
+    TORCH_CHECK(2 * L.half_bytes <= num_rdma_bytes_, "low-latency region too small");
+    TORCH_CHECK(L.num_local_experts == E_l, "a must hold every local expert");
+    L.num_topk = K;
+    const int half = (++ll_combine_seq_) & 1;
+    auto compute = at::cuda::getCurrentCUDAStream();
+    if (num_sms <= 0) EP_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device_id_));
+
+    // 1) down projection whose epilogue stores rows into the sources' combine slots (send phase)
+    MaskedGemmArgs g{};
+    g.a = a.data_ptr();
+    g.sa = a_scales.data_ptr<float>();
+    g.sa_e = a_scales.stride(0);
+    g.sa_m = a_scales.stride(1);
+    g.sa_k = a_scales.stride(2);
+    g.b = w.data_ptr();
+    g.sb = w_scales.data_ptr<float>();
+    g.counts = recv_count.data_ptr<int>();
+    g.d = nullptr;
+    g.num_experts = E_l;
+    g.slots = slots;
+    g.n = H;
+    g.k = k;
+    g.combine = 1;
+    g.ll_peers = ll_peers();
+    g.ll_layout = L;
+    g.dispatch_half = dispatch_half;
+    g.combine_half = half;
+    g.rank = rank_;
+    g.st = status();
+    const int rc = launch_masked_gemm_fp8(g, num_sms, compute.stream());
+    TORCH_CHECK(rc == 0, "fused masked GEMM + combine send launch failed (code " + std::to_string(rc) + ")");
+
+    // 2) the combine's receive phase: weighted top-k reduction
+    auto combined = torch::empty({N, H}, topk_weights.options().dtype(torch::kBFloat16));
+    LLCombineArgs ca{};
+    ca.peers = ll_peers();
+    ca.layout = L;
+    ca.half = half;
+    ca.dispatch_half = dispatch_half;
+    ca.x = nullptr;
+    ca.recv_count = recv_count.data_ptr<int>();
+    ca.topk_idx = topk_idx.data_ptr<int64_t>();
+    ca.topk_weights = topk_weights.data_ptr<float>();
+    ca.num_tokens = N;
+    ca.rank = rank_;
+    ca.mask = mask_;
+    ca.shrink = 0;
+    ca.out = combined.data_ptr();
+    ca.st = status();
+    ca.phases = 2;
+    launch_ll_combine(ca, compute.stream());
+    EP_CUDA_CHECK(cudaGetLastError());
+    return combined;
+}
+
 std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::function<void()>>> Buffer::low_latency_combine(
     const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights, const torch::Tensor& recv_count,
     int dispatch_half, const std::optional<torch::Tensor>& combine_wait_recv_cost_stats, int num_max_dispatch_tokens_per_rank,

@@ -152,6 +152,12 @@ class Buffer {
                               const std::optional<torch::Tensor>& cumulative_local_expert_recv_stats,
                               int num_max_dispatch_tokens_per_rank, int num_experts, const torch::Tensor& w,
                               const torch::Tensor& w_scales, bool round_scale, int num_sms);
+    // Down projection (masked grouped FP8 GEMM) whose epilogue is the low-latency combine's send, then
+    // the combine's receive (weighted reduction): returns the combined [num_tokens, hidden] bf16.
+    torch::Tensor low_latency_gemm_combine(const torch::Tensor& a, const torch::Tensor& a_scales, const torch::Tensor& recv_count,
+                                           const torch::Tensor& w, const torch::Tensor& w_scales, const torch::Tensor& topk_idx,
+                                           const torch::Tensor& topk_weights, int dispatch_half,
+                                           int num_max_dispatch_tokens_per_rank, int num_experts, int num_sms);
     std::tuple<torch::Tensor, std::optional<EventHandle>, std::optional<std::function<void()>>> low_latency_combine(
         const torch::Tensor& x, const torch::Tensor& topk_idx, const torch::Tensor& topk_weights,
         const torch::Tensor& recv_count, int dispatch_half, const std::optional<torch::Tensor>& combine_wait_recv_cost_stats,

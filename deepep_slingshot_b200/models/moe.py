@@ -211,18 +211,23 @@ class MoEFFN(torch.nn.Module):
 
     @torch.no_grad()
     def forward_low_latency(self, ll_buffer, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
-                            num_max_dispatch_tokens_per_rank: int) -> torch.Tensor:
+                            num_max_dispatch_tokens_per_rank: int, fuse_combine: bool = True) -> torch.Tensor:
         """Decode forward (inference) on the low-latency path, every step a hand-written sm_100a kernel:
         FP8 dispatch with its receive fused into the masked gate/up GEMM
         (`Buffer.low_latency_dispatch_gemm`) -> masked SwiGLU + FP8 requant -> masked down GEMM ->
         top-k weighted `low_latency_combine`. `ll_buffer` is a `Buffer` with a low-latency region for
-        (num_max_dispatch_tokens_per_rank, hidden, num_experts); no permute, no packing copy."""
+        (num_max_dispatch_tokens_per_rank, hidden, num_experts); no permute, no packing copy. With
+        `fuse_combine` the down projection's epilogue stores its rows straight into the sources'
+        combine slots (`Buffer.low_latency_gemm_combine`)."""
         from ..ops.gemm import masked_grouped_gemm_fp8
         from ..ops.quant import swiglu_quant
         w1q, w1s, w2q, w2s = self.quantized_weights()
         h, counts, handle, _ = ll_buffer.low_latency_dispatch_gemm(x, topk_idx, num_max_dispatch_tokens_per_rank,
                                                                    self.num_experts, w1q, w1s)
         _, aq, as_ = swiglu_quant(h, counts=counts)
+        if fuse_combine:
+            # down projection whose epilogue is the combine's send, then the weighted receive
+            return ll_buffer.low_latency_gemm_combine(aq, as_, w2q, w2s, topk_idx, topk_weights.float().contiguous(), handle)
         y = masked_grouped_gemm_fp8(aq, as_, counts, w2q, w2s)
         out, _, _ = ll_buffer.low_latency_combine(y, topk_idx, topk_weights, handle)
         return out

@@ -401,6 +401,21 @@ class Buffer:
         handle = (src_info, None, num_max_dispatch_tokens_per_rank, x.size(1), num_experts, recv_count, half, src_meta)
         return out, recv_count, handle, (recv_x, recv_scales)
 
+    @nvtx_range('ep.low_latency_gemm_combine')
+    def low_latency_gemm_combine(self, x: torch.Tensor, x_scales: torch.Tensor, weights: torch.Tensor,
+                                 weight_scales: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor,
+                                 handle: tuple, num_sms: int = 0) -> torch.Tensor:
+        """Down projection and low-latency combine in two launches: a masked grouped FP8 GEMM over the
+        dispatch's per-expert layout (`x [E_local, R * max_tokens, k]` e4m3 with 1x128 `x_scales`,
+        `weights [E_local, hidden, k]` e4m3 with 128x128 `weight_scales`) whose epilogue stores each
+        output row straight into its source rank's combine slot over NVLink, then the combine's
+        receive (top-k weighted reduction). Returns the combined `[num_tokens, hidden]` bf16. `handle`
+        is the dispatch's (`low_latency_dispatch` or `low_latency_dispatch_gemm`). Not available in
+        shrink mode."""
+        src_info, _, num_max_dispatch_tokens_per_rank, hidden, num_experts, recv_count, half, _ = handle
+        return self.runtime.low_latency_gemm_combine(x, x_scales, recv_count, weights, weight_scales, topk_idx, topk_weights,
+                                                     half, num_max_dispatch_tokens_per_rank, num_experts, num_sms)
+
     @nvtx_range('ep.low_latency_combine')
     def low_latency_combine(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor, handle: tuple,
                             use_logfmt: bool = False, zero_copy: bool = False, async_finish: bool = False,

@@ -126,9 +126,12 @@ def _moe_decode_body(rank, world, N, H, I, E, K):
     idx = torch.rand((N, E), device='cuda', generator=gi).topk(K, dim=1).indices.to(torch.int64)
     wts = torch.softmax(torch.rand((N, K), device='cuda', generator=gi), dim=1)
     out = layer.forward_low_latency(buf, x, idx, wts, N)
+    out_unfused = layer.forward_low_latency(buf, x, idx, wts, N, fuse_combine=False)
     ref = moe_reference(x, idx, wts, w1_all, w2_all)
     torch.cuda.synchronize()
     assert _rel_err(out, ref.float()) < 3e-2
+    # the fused down projection + combine send gives the same rows as GEMM then combine
+    assert torch.equal(out, out_unfused)
 
 
 @pytest.mark.parametrize('world', [1, 2])
