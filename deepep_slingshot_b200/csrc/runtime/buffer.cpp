@@ -58,6 +58,11 @@ struct StreamScope {
     }
 };
 
+// Fill a tensor's bytes with 0xFF on `stream` (the poison of DEEPEP_B200_POISON_OUTPUTS).
+void poison(const torch::Tensor& t, cudaStream_t stream) {
+    if (t.numel() > 0) EP_CUDA_CHECK(cudaMemsetAsync(t.data_ptr(), 0xFF, t.numel() * t.element_size(), stream));
+}
+
 }  // namespace
 
 const char* error_name(int code) {
@@ -228,6 +233,8 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     combine_row_chunk_ = cchunk != nullptr ? std::max(-1, std::atoi(cchunk)) : -1;
     // Combine arrival announcements: "drain" (default) waits for a batch's stores before announcing
     // it; "lagged" announces each batch one batch later and keeps the newer stores in flight.
+    const char* poison_env = std::getenv("DEEPEP_B200_POISON_OUTPUTS");
+    poison_outputs_ = poison_env != nullptr && std::string(poison_env) == "1";
     const char* announce = std::getenv("DEEPEP_B200_COMBINE_ANNOUNCE");
     combine_announce_lagged_ = announce != nullptr && std::string(announce) == "lagged";
 
@@ -699,6 +706,15 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     if (!cached && topk_weights.has_value())
         recv_topk_weights = torch::empty({num_out_rows, K}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
     torch::Tensor recv_src_idx = cached ? *cached_recv_src_idx : torch::empty({num_out_rows}, i32);
+    if (poison_outputs_) {
+        // Debug: every output byte starts as 0xFF (NaN for the float types, -1 for ids), so a row the
+        // kernels should have written but did not shows up in the caller's checks.
+        poison(recv_x, stream);
+        if (recv_scales.has_value()) poison(scales_storage.has_value() ? *scales_storage : *recv_scales, stream);
+        if (recv_topk_idx.has_value()) poison(*recv_topk_idx, stream);
+        if (recv_topk_weights.has_value()) poison(*recv_topk_weights, stream);
+        if (!cached) poison(recv_src_idx, stream);
+    }
 
     PullArgs pa{};
     pa.peers = peers;
@@ -944,6 +960,10 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     auto out = torch::empty({N, H}, x.options());
     std::optional<torch::Tensor> out_w;
     if (topk_weights.has_value()) out_w = torch::empty({N, K}, torch::dtype(torch::kFloat32).device(torch::kCUDA));
+    if (poison_outputs_) {
+        poison(out, stream);
+        if (out_w.has_value()) poison(*out_w, stream);
+    }
     const KernelStatus st = status();
     const PeerTable peers = nvl_peers();
 

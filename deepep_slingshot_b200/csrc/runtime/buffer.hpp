@@ -181,6 +181,7 @@ class Buffer {
     int row_chunk_ = 0;
     int combine_row_chunk_ = -1;
     bool combine_announce_lagged_ = false;
+    bool poison_outputs_ = false;  // DEEPEP_B200_POISON_OUTPUTS=1: outputs start as 0xFF bytes
     std::vector<std::pair<int, cudaEvent_t>> prof_events_;
 
     int rank_, num_ranks_, device_id_;
