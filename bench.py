@@ -61,6 +61,10 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--no-moe', action='store_true')
     p.add_argument('--moe-steps', type=int, default=3)
+    p.add_argument('--moe-fused-dispatch', action='store_true',
+                   help='MoE forward with the dispatch receive fused into the gate/up GEMM (Buffer.dispatch_gemm)')
+    p.add_argument('--ll-moe', action='store_true',
+                   help='also time the decode MoE layer (MoEFFN.forward_low_latency) at the low-latency shape')
     p.add_argument('--check', action='store_true', help='verify against the torch oracle before timing')
     return p.parse_args()
 
@@ -322,6 +326,7 @@ def main():
         from deepep_slingshot_b200.models import MoEFFN
         from deepep_slingshot_b200.models import moe as _moe_mod
         inter = 2048
+        _moe_mod._FUSED_DISPATCH['enabled'] = args.moe_fused_dispatch
         gm = torch.Generator().manual_seed(4321)
         layer = MoEFFN(buf, H, inter, E, K, config=cfg, init_std=0.02, generator=gm)
         mx = torch.randn((N, H), generator=gm).to(torch.bfloat16).cuda().requires_grad_(True)
@@ -356,13 +361,39 @@ def main():
                'moe_roofline_fraction': roof['bound'] / (ms_moe * 1e-3),
                'moe_roofline_ms': {k: v * 1e3 for k, v in roof.items()},
                'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
-                              'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs',
+                              'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs' +
+                              (', dispatch receive fused into the gate/up GEMM' if args.moe_fused_dispatch else ''),
                               'backward': ('bf16 tcgen05 grouped GEMMs (dgrad M-grouped, wgrad K-grouped)' if _moe_mod._GROUPED_BWD['tcgen05']
                                            else 'bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled']
                                            else 'bf16 per-expert torch matmuls (stand-in)'),
                               'roofline': ('max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes '
                                            'at 770 GB/s, 8 bytes per local weight element per step at measured 6558 GB/s HBM)')}}
         del layer
+        torch.cuda.empty_cache()
+
+    # ---------------------------------------------------------------- decode MoE layer (opt-in)
+    if args.ll_moe and not args.no_ll and args.impl == 'ours':
+        from deepep_slingshot_b200.models import MoEFFN
+        dlayer = MoEFFN(buf, H, 2048, E, K, config=cfg, init_std=0.02, generator=torch.Generator().manual_seed(2468))
+        lwf = lw.float().contiguous()
+        for _ in range(args.warmup):
+            dlayer.forward_low_latency(buf, lx, lidx, lwf, T)
+        torch.cuda.synchronize()
+        dist.barrier()
+        dts = []
+        for _ in range(iters):
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record()
+            dlayer.forward_low_latency(buf, lx, lidx, lwf, T)
+            d1.record()
+            torch.cuda.synchronize()
+            dts.append(d0.elapsed_time(d1) * 1e3)
+        dts = max_over_ranks(dts)
+        ll.update({'ll_moe_forward_us': statistics.median(dts),
+                   'll_moe_config': {'tokens_per_rank': T, 'hidden': H, 'inter': 2048, 'experts': E, 'topk': K,
+                                     'path': 'fused LL dispatch + masked gate/up GEMM, masked SwiGLU requant, '
+                                             'masked down GEMM with the combine send as its epilogue, weighted combine'}})
+        del dlayer
         torch.cuda.empty_cache()
 
     # ---------------------------------------------------------------- end to end through the public API
