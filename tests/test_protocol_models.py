@@ -1,0 +1,141 @@
+"""CPU model of the mbarrier phase protocol used by the tcgen05 kernels, driven by random schedules.
+
+An mbarrier completes a phase when its expected arrivals have arrived; `try_wait.parity(P)` succeeds
+once the phase with parity P has completed, so waiting on parity ((i / depth) & 1) ^ 1 passes at
+once for the first `depth` uses (the idiom every ring here uses). The models check, over many random
+interleavings of the roles, the rings whose ordering the kernels rely on:
+  * the tile-id queue of the fused dispatch -> GEMM kernel (one producer, the MMA warp and eight
+    epilogue warps, depth 4): every consumer reads every id in order, no slot is overwritten before
+    all nine consumers read it, and the sentinel ends every consumer;
+  * the shared-memory stage ring (TMA producer -> MMA, depth S) and the two TMEM accumulators
+    (MMA -> eight epilogue warps) of the grouped GEMMs: stages and accumulators are never reused
+    before they are released.
+"""
+import random
+
+import pytest
+
+
+class MBarrier:
+    def __init__(self, count):
+        self.count = count
+        self.pending = count
+        self.phase = 0  # number of completed phases
+
+    def arrive(self):
+        assert self.pending > 0
+        self.pending -= 1
+        if self.pending == 0:
+            self.phase += 1
+            self.pending = self.count
+
+
+
+def _done(bar, parity):
+    """`mbarrier.try_wait.parity(parity)`: the hardware tracks only the parity of the current
+    (incomplete) phase, and the wait succeeds when it differs from `parity`."""
+    return (bar.phase & 1) != parity
+
+
+@pytest.mark.parametrize('seed', range(40))
+def test_tile_queue_protocol(seed):
+    rng = random.Random(seed)
+    Q, consumers, tiles = 4, 9, rng.randint(0, 25)
+    qfull = [MBarrier(1) for _ in range(Q)]
+    qempty = [MBarrier(consumers) for _ in range(Q)]
+    slots = [None] * Q
+    seq = list(range(tiles)) + [-1]
+    prod = {'q': 0, 'state': 'wait_empty', 'done': False}
+    cons = [{'q': 0, 'read': [], 'done': False} for _ in range(consumers)]
+    reads_left = {}  # slot -> consumers that still have to read its current value
+
+    for step in range(100000):
+        actors = [('p', None)] if not prod['done'] else []
+        actors += [('c', i) for i in range(consumers) if not cons[i]['done']]
+        if not actors:
+            break
+        kind, i = rng.choice(actors)
+        if kind == 'p':
+            q = prod['q']
+            s = q % Q
+            if _done(qempty[s], ((q // Q) & 1) ^ 1):
+                assert reads_left.get(s, 0) == 0, 'slot overwritten before every consumer read it'
+                slots[s] = seq[q]
+                reads_left[s] = consumers
+                qfull[s].arrive()
+                prod['q'] += 1
+                prod['done'] = seq[q] == -1
+        else:
+            c = cons[i]
+            q = c['q']
+            s = q % Q
+            if _done(qfull[s], (q // Q) & 1):
+                t = slots[s]
+                reads_left[s] -= 1
+                qempty[s].arrive()
+                c['q'] += 1
+                if t < 0:
+                    c['done'] = True
+                else:
+                    c['read'].append(t)
+    assert prod['done'] and all(c['done'] for c in cons)
+    for c in cons:
+        assert c['read'] == list(range(tiles))
+
+
+@pytest.mark.parametrize('seed', range(40))
+def test_stage_ring_and_accumulators(seed):
+    rng = random.Random(seed)
+    S, KB, tiles, epi = rng.choice([4, 6, 8]), rng.randint(1, 6), rng.randint(1, 6), 8
+    full = [MBarrier(1) for _ in range(S)]
+    empty = [MBarrier(1) for _ in range(S)]
+    tfull = [MBarrier(1) for _ in range(2)]
+    tempty = [MBarrier(epi) for _ in range(2)]
+    total = tiles * KB
+    stage_owner = [None] * S     # k-block whose data is in the stage
+    acc_owner = [None] * 2       # k-block whose partial is in the accumulator
+    acc_reads = [0] * 2
+    prod = {'g': 0}
+    mma = {'g': 0}
+    epis = [{'g': 0} for _ in range(epi)]
+    for step in range(200000):
+        actors = []
+        if prod['g'] < total:
+            actors.append('p')
+        if mma['g'] < total:
+            actors.append('m')
+        actors += [i for i in range(epi) if epis[i]['g'] < total]
+        if not actors:
+            break
+        a = rng.choice(actors)
+        if a == 'p':
+            g = prod['g']
+            s = g % S
+            if _done(empty[s], ((g // S) & 1) ^ 1):
+                assert stage_owner[s] is None, 'stage refilled before the MMA released it'
+                stage_owner[s] = g
+                full[s].arrive()  # the TMA bytes landed
+                prod['g'] += 1
+        elif a == 'm':
+            g = mma['g']
+            s, b = g % S, g & 1
+            if _done(tempty[b], ((g >> 1) & 1) ^ 1) and _done(full[s], (g // S) & 1):
+                assert stage_owner[s] == g and acc_owner[b] is None
+                acc_owner[b] = g
+                acc_reads[b] = 0
+                stage_owner[s] = None
+                empty[s].arrive()   # tcgen05.commit -> stage free
+                tfull[b].arrive()   # tcgen05.commit -> accumulator ready
+                mma['g'] += 1
+        else:
+            e = epis[a]
+            g = e['g']
+            b = g & 1
+            if _done(tfull[b], (g >> 1) & 1):
+                assert acc_owner[b] == g, 'epilogue read an accumulator of another k-block'
+                acc_reads[b] += 1
+                if acc_reads[b] == epi:
+                    acc_owner[b] = None
+                tempty[b].arrive()
+                e['g'] += 1
+    assert prod['g'] == mma['g'] == total and all(e['g'] == total for e in epis)
