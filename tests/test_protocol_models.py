@@ -30,7 +30,6 @@ class MBarrier:
             self.pending = self.count
 
 
-
 def _done(bar, parity):
     """`mbarrier.try_wait.parity(parity)`: the hardware tracks only the parity of the current
     (incomplete) phase, and the wait succeeds when it differs from `parity`."""
@@ -45,7 +44,7 @@ def test_tile_queue_protocol(seed):
     qempty = [MBarrier(consumers) for _ in range(Q)]
     slots = [None] * Q
     seq = list(range(tiles)) + [-1]
-    prod = {'q': 0, 'state': 'wait_empty', 'done': False}
+    prod = {'q': 0, 'done': False}
     cons = [{'q': 0, 'read': [], 'done': False} for _ in range(consumers)]
     reads_left = {}  # slot -> consumers that still have to read its current value
 
