@@ -92,11 +92,16 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
     w = torch.rand((tokens, K), device='cuda', generator=g)
     w = torch.where(idx < 0, torch.zeros_like(w), w)
     w = w / w.sum(1, keepdim=True).clamp_min(1e-6)
+    if args.drop_every > 0:
+        # Dropped tokens (the reference's CXI_EP_DROP_EVERY, backend/tests/ep_benchmark.py:158-162):
+        # every n-th token selects no expert at all.
+        idx[::args.drop_every] = -1
+        w[::args.drop_every] = 0
     x = torch.randn((tokens, H), device='cuda', generator=g).to(torch.bfloat16)
     case = {'model': model, 'hidden': H, 'experts': E, 'topk': K, 'tokens_per_rank': tokens, 'ranks': R,
             'dispatch_dtype': dtype, 'combine_dtype': 'bf16', 'routing': routing, 'seed': seed,
             'route_sha256': hash_tensor(idx), 'input_sha256': hash_tensor(x), 'alignment': 128,
-            'num_sms': args.num_sms or buf.num_sms, 'flush_l2': True}
+            'num_sms': args.num_sms or buf.num_sms, 'flush_l2': True, 'drop_every': args.drop_every}
 
     # ---- correctness (fresh dispatch, then combine)
     kw = dict(topk_idx=idx, topk_weights=w, num_experts=E, expert_alignment=128)
@@ -237,6 +242,7 @@ def main(argv=None):
     p.add_argument('--dtype', nargs='+', choices=['fp8', 'bf16'], default=['fp8'])
     p.add_argument('--routing', nargs='+', default=['uniform', 'mixed'])
     p.add_argument('--seeds', nargs='+', type=int, default=[0])
+    p.add_argument('--drop-every', type=int, default=0, help='every n-th token selects no expert (0: none)')
     p.add_argument('--iters', type=int, default=20)
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--num-sms', type=int, default=0)

@@ -1,6 +1,8 @@
 """Qualification ladder: serial gates over the EP benchmark, each validated fail-closed before the
 next one runs (the reference's gate controller, harness/runner/controller.py:36-125, and its ladders:
-irregular stress, 4K correctness FP8 + BF16, performance).
+irregular stress, 4K correctness FP8 + BF16, dropped tokens, sustained 16K, performance with
+counterbalanced repeats). A gate with `compare_with` must also reproduce an earlier gate's medians
+within `max_rel_diff` (the repeat runs the models in the opposite order, so drift over time shows).
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m deepep_slingshot_b200.harness.ladder --out ladder_ep8
 
@@ -21,10 +23,44 @@ GATES: List[Dict] = [
     {'name': 'correctness_4k', 'args': ['--models', 'v4flash', 'qwen3', 'minimax', '--tokens', '4096', '--dtype', 'fp8',
                                         'bf16', '--routing', 'uniform', 'mixed', 'skew2', '--iters', '3', '--warmup', '1'],
      'max_cv': 10.0},
+    {'name': 'dropped_tokens', 'args': ['--models', 'v4flash', 'deepseek_v3', '--tokens', '4096', '--dtype', 'fp8',
+                                        'bf16', '--routing', 'uniform', 'mixed', '--drop-every', '7', '--iters', '3',
+                                        '--warmup', '1'], 'max_cv': 10.0},
+    {'name': 'sustained_16k', 'args': ['--models', 'v4flash', '--tokens', '16384', '--dtype', 'fp8', '--routing',
+                                       'uniform', 'mixed', '--seeds', '0', '1', '--iters', '20', '--warmup', '5'],
+     'max_cv': 0.15},
     {'name': 'perf_4k', 'args': ['--models', 'deepseek_v3', 'v4flash', '--tokens', '4096', '--dtype', 'fp8',
                                  '--routing', 'uniform', 'mixed', '--seeds', '0', '1', '2', '--iters', '20',
                                  '--warmup', '5'], 'max_cv': 0.15},
+    {'name': 'perf_4k_repeat', 'args': ['--models', 'v4flash', 'deepseek_v3', '--tokens', '4096', '--dtype', 'fp8',
+                                        '--routing', 'mixed', 'uniform', '--seeds', '0', '1', '2', '--iters', '20',
+                                        '--warmup', '5'], 'max_cv': 0.15, 'compare_with': 'perf_4k', 'max_rel_diff': 0.1},
 ]
+
+
+def compare_summaries(dir_a: str, dir_b: str, max_rel_diff: float) -> List[str]:
+    """Problems where a case's median differs between two gates' summary.csv by more than
+    `max_rel_diff`, or where the gates cover different cases."""
+    import csv
+    keys = ('model', 'tokens_per_rank', 'ranks', 'dispatch_dtype', 'routing', 'seed', 'op')
+
+    def load(d):
+        path = os.path.join(d, 'summary.csv')
+        if not os.path.exists(path):
+            return None
+        with open(path) as f:
+            return {tuple(r[k] for k in keys): float(r['median_rank_max_us']) for r in csv.DictReader(f)}
+    a, b = load(dir_a), load(dir_b)
+    if a is None or b is None:
+        return [f'missing summary.csv in {dir_a if a is None else dir_b}']
+    if set(a) != set(b):
+        return [f'the gates cover different cases ({len(set(a) ^ set(b))} differ)']
+    problems = []
+    for k in sorted(a):
+        lo, hi = min(a[k], b[k]), max(a[k], b[k])
+        if lo <= 0 or (hi - lo) / lo > max_rel_diff:
+            problems.append(f'{k}: median {a[k]:.1f} vs {b[k]:.1f} us (more than {max_rel_diff:.0%} apart)')
+    return problems
 
 
 def load_state(path: str) -> dict:
@@ -59,6 +95,9 @@ def run_ladder(out: str, run_gate: Callable[[dict, str], List[str]], gates: List
         if gate['name'] in state['passed']:
             continue
         problems = run_gate(gate, os.path.join(out, gate['name']))
+        if not problems and gate.get('compare_with'):
+            problems = compare_summaries(os.path.join(out, gate['compare_with']), os.path.join(out, gate['name']),
+                                         gate.get('max_rel_diff', 0.1))
         if problems:
             state['failed'] = gate['name']
             state['problems'] = problems[:50]

@@ -203,3 +203,42 @@ def test_box_probe_topology_and_cpu_collect(tmp_path):
     assert isinstance(info['gpus'], list) and isinstance(info['peer_access'], list)
     assert box_probe.main(['--out', str(tmp_path / 'box.json')]) == 0
     assert (tmp_path / 'box.json').exists()
+
+
+def test_ladder_counterbalanced_repeat(tmp_path):
+    """A repeat gate must reproduce the earlier gate's medians within its tolerance."""
+    import csv
+    from deepep_slingshot_b200.harness.ladder import GATES, compare_summaries, run_ladder
+    names = [g['name'] for g in GATES]
+    assert names.index('perf_4k_repeat') > names.index('perf_4k')
+    assert any('--drop-every' in g['args'] for g in GATES) and any('16384' in g['args'] for g in GATES)
+
+    def write(d, medians):
+        os.makedirs(d, exist_ok=True)
+        with open(os.path.join(d, 'summary.csv'), 'w', newline='') as f:
+            w = csv.DictWriter(f, fieldnames=['model', 'tokens_per_rank', 'ranks', 'dispatch_dtype', 'routing', 'seed',
+                                              'op', 'median_rank_max_us'])
+            w.writeheader()
+            for (op, m) in medians.items():
+                w.writerow(dict(model='v4flash', tokens_per_rank=4096, ranks=8, dispatch_dtype='fp8', routing='mixed',
+                                seed=0, op=op, median_rank_max_us=m))
+    a, b = str(tmp_path / 'a'), str(tmp_path / 'b')
+    write(a, {'dispatch': 100.0, 'combine': 200.0})
+    write(b, {'dispatch': 104.0, 'combine': 195.0})
+    assert compare_summaries(a, b, 0.1) == []
+    write(b, {'dispatch': 130.0, 'combine': 195.0})
+    assert len(compare_summaries(a, b, 0.1)) == 1
+    write(b, {'dispatch': 100.0})
+    assert 'different cases' in compare_summaries(a, b, 0.1)[0]
+    assert 'missing summary' in compare_summaries(a, str(tmp_path / 'none'), 0.1)[0]
+
+    gates = [{'name': 'p', 'args': []}, {'name': 'r', 'args': [], 'compare_with': 'p', 'max_rel_diff': 0.1}]
+    out = str(tmp_path / 'ladder')
+    medians = {'p': {'dispatch': 100.0}, 'r': {'dispatch': 150.0}}
+
+    def fake(gate, d):
+        write(d, medians[gate['name']])
+        return []
+    assert not run_ladder(out, fake, gates)            # the repeat is 50% off: fails closed
+    medians['r'] = {'dispatch': 103.0}
+    assert run_ladder(out, fake, gates, resume_reason='quiet box')
