@@ -11,6 +11,7 @@ _err = None
 
 
 def load_ext():
+    """The in-tree extension module, or None when it is not built (the error is kept for `require_ext`)."""
     global _ext, _err
     if _ext is None and _err is None:
         try:
@@ -21,6 +22,7 @@ def load_ext():
 
 
 def require_ext():
+    """The in-tree extension module; raises with the build command when it is not built."""
     ext = load_ext()
     if ext is None:
         raise RuntimeError('deepep_slingshot_b200._C is not built: run `python setup.py build_ext --inplace` '

@@ -22,12 +22,15 @@ from typing import Dict, Iterable, List
 
 
 def read_log(path: str) -> List[dict]:
+    """Records of one lifecycle JSONL file."""
     with open(path) as f:
         return [json.loads(line) for line in f if line.strip()]
 
 
 def audit_rank(records: Iterable[dict], rank: int, cycles: int, kind: str = 'Buffer',
                tolerance_bytes: int = 4 << 20) -> Dict[str, int]:
+    """Audit one rank's records of one kind (see the module docstring); returns the cycle
+    count, peak live objects, baseline and largest growth, or raises ValueError."""
     recs = [r for r in records if r.get('rank') == rank and r.get('kind') == kind]
     if not recs:
         raise ValueError(f'no {kind} lifecycle events for rank {rank}')

@@ -50,6 +50,8 @@ def split_steps(events: List[dict], gap_us: float = 50.0) -> List[List[dict]]:
 
 
 def analyze(trace: dict) -> List[dict]:
+    """Per-step phase rows (window, busy union, duty, skew over ranks) of a Chrome trace written by
+    `harness.trace_capture`."""
     by_rank: Dict[int, List[dict]] = defaultdict(list)
     for e in trace['traceEvents']:
         by_rank[e['pid']].append(e)

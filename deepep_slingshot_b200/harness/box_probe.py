@@ -92,6 +92,7 @@ def peer_copy_gbs(src: int, dst: int, nbytes: int = 256 << 20, repeats: int = 5)
 
 
 def collect(bandwidth: bool = False, repo_root: Optional[str] = None) -> dict:
+    """Everything the probe records, as a dict (see the module docstring)."""
     import torch
     info = {'host': socket.gethostname(), 'torch': torch.__version__, 'cuda': torch.version.cuda,
             'nccl': None, 'driver': None, 'gpus': [], 'peer_access': [], 'topology': {}, 'nvlink_status': None,

@@ -80,6 +80,8 @@ def _summary(out_dir: str) -> Dict[tuple, dict]:
 
 
 def compare(dir_a: str, dir_b: str, allow_other_host: bool = False) -> Tuple[dict, List[dict]]:
+    """Pair two result directories rank by rank (see the module docstring); returns the differences
+    that are the experiment (changed sources / env) and the per-case paired rows."""
     man_a, cases_a = _load_run(dir_a)
     man_b, cases_b = _load_run(dir_b)
     if sorted(man_a) != sorted(man_b):

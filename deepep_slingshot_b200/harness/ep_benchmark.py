@@ -42,10 +42,12 @@ def dispatch_bytes(num_recv: int, hidden: int, num_topk: int, fp8: bool) -> int:
 
 
 def combine_bytes(num_recv: int, hidden: int, num_topk: int) -> int:
+    """DeepEP v2 logical bytes of a combine: received rows x (bf16 row + fp32 top-k weights)."""
     return num_recv * (2 * hidden + 4 * num_topk)
 
 
 def source_hashes() -> dict:
+    """SHA-256 of every source file of the package (the manifest's code identity)."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     out = {}
     for d, _, files in os.walk(root):
@@ -58,6 +60,7 @@ def source_hashes() -> dict:
 
 
 def manifest(args) -> dict:
+    """This rank's manifest record: world, host, versions, environment knobs, source hashes."""
     return {'kind': 'manifest', 'rank': dist.get_rank(), 'world': dist.get_world_size(), 'host': socket.gethostname(),
             'time': datetime.datetime.utcnow().isoformat() + 'Z', 'argv': sys.argv, 'python': platform.python_version(),
             'torch': torch.__version__, 'cuda': torch.version.cuda,
@@ -82,6 +85,7 @@ def _check_equal(name, a, b):
 
 
 def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
+    """One (model, tokens, dtype, routing, seed) case: correctness against the oracle, then timings."""
     from ..utils.testing import bench, hash_tensor, rank_max
     from .routing import make_routing
     rank, R = dist.get_rank(), dist.get_world_size()

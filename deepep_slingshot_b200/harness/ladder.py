@@ -64,6 +64,7 @@ def compare_summaries(dir_a: str, dir_b: str, max_rel_diff: float) -> List[str]:
 
 
 def load_state(path: str) -> dict:
+    """The ladder state file (passed gates, the failed gate, resume reasons), or a fresh one."""
     if os.path.exists(path):
         with open(path) as f:
             return json.load(f)
@@ -71,6 +72,7 @@ def load_state(path: str) -> dict:
 
 
 def save_state(path: str, state: dict) -> None:
+    """Write the ladder state atomically (temporary file + rename)."""
     tmp = path + '.tmp'
     with open(tmp, 'w') as f:
         json.dump(state, f, indent=1)

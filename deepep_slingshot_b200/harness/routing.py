@@ -114,6 +114,7 @@ def greedy_placement(load, experts_per_rank: int) -> np.ndarray:
 
 
 def random_placement(num_experts: int, seed: int) -> np.ndarray:
+    """A seeded random permutation of the experts (a placement that ignores load)."""
     return np.random.default_rng(seed).permutation(num_experts)
 
 

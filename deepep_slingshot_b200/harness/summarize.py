@@ -26,6 +26,7 @@ def _pct(values: List[float], q: float) -> float:
 
 
 def load_timings(out_dir: str) -> Dict[tuple, List[dict]]:
+    """Timing records of every rank grouped by (case, op)."""
     groups: Dict[tuple, List[dict]] = defaultdict(list)
     for path in sorted(glob.glob(os.path.join(out_dir, 'timings-rank*.jsonl'))):
         with open(path) as f:
@@ -37,6 +38,7 @@ def load_timings(out_dir: str) -> Dict[tuple, List[dict]]:
 
 
 def summarize_dir(out_dir: str) -> List[dict]:
+    """Write `summary.csv` and `repeatability.json` for a results directory; returns the rows."""
     rows = []
     for key, recs in load_timings(out_dir).items():
         rmax = recs[0]['rank_max_us']

@@ -17,6 +17,9 @@ from .._ext import require_ext
 
 def grouped_gemm_fp8(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, offsets: torch.Tensor,
                      counts: Optional[torch.Tensor] = None, num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
+    """Grouped block-scaled FP8 GEMM on tcgen05: rows of `a [rows, k]` (1x128 scales `sa`) grouped by
+    expert at 128-aligned `offsets`, times `b [E, n, k]` (128x128 scales `sb`) -> `[rows, n]` bf16; only the
+    first `counts[e]` rows of each group are meaningful."""
     return require_ext().grouped_gemm_fp8(a, sa, b, sb, offsets, counts, num_sms, timeout_s)
 
 
@@ -45,6 +48,7 @@ def grouped_gemm_bf16_wgrad_rows(a: torch.Tensor, b: torch.Tensor, offsets: torc
 
 
 def grouped_gemm_bf16_reference(a, b, offsets, counts=None) -> torch.Tensor:
+    """fp32 torch oracle of `grouped_gemm_bf16` (mode 0); rows past `counts[e]` stay zero."""
     out = torch.zeros((a.shape[0], b.shape[1]), dtype=torch.float32, device=a.device)
     off = offsets.tolist()
     for e in range(b.shape[0]):
@@ -55,6 +59,7 @@ def grouped_gemm_bf16_reference(a, b, offsets, counts=None) -> torch.Tensor:
 
 
 def grouped_gemm_bf16_wgrad_reference(a_t, b_t, offsets) -> torch.Tensor:
+    """fp32 torch oracle of `grouped_gemm_bf16_wgrad` (K-grouped)."""
     off = offsets.tolist()
     E = len(off) - 1
     out = torch.zeros((E, a_t.shape[0], b_t.shape[0]), dtype=torch.float32, device=a_t.device)
@@ -101,6 +106,8 @@ def quantize_weights_fp8_reference(w: torch.Tensor):
 
 
 def grouped_gemm_fp8_reference(a, sa, b, sb, offsets, counts=None) -> torch.Tensor:
+    """fp32 torch oracle of `grouped_gemm_fp8` with the same dequantisation; rows past
+    `counts[e]` stay zero."""
     af = dequant_rows(a, sa)
     bf = dequant_blocks(b, sb)
     out = torch.zeros((a.shape[0], b.shape[1]), dtype=torch.float32, device=a.device)

@@ -13,6 +13,8 @@ from .._ext import require_ext
 
 
 class Permuted(NamedTuple):
+    """Result of `permute`: expert-grouped rows (and scales / probs), the (token, k) -> row map and the
+    per-expert offsets and counts."""
     x: torch.Tensor                 # [rows, H] grouped by expert (rows past offsets[E] unused)
     scales: Optional[torch.Tensor]  # [rows, H/128] FP8 block scales
     probs: Optional[torch.Tensor]   # [rows] top-k weight of each grouped row
@@ -31,6 +33,8 @@ def permute(x: torch.Tensor, topk_idx: torch.Tensor, num_experts: int, alignment
 
 
 def unpermute(y: torch.Tensor, row_map: torch.Tensor, weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Sum each token's rows back from the expert-grouped layout (`row_map [N, K]`, -1 = none),
+    weighted by `probs [N, K]` when given (sm_100a kernel)."""
     return require_ext().unpermute(y, row_map, weights)
 
 
@@ -45,6 +49,7 @@ def permute_reference(topk_idx: torch.Tensor, num_experts: int, alignment: int =
 
 
 def unpermute_reference(y: torch.Tensor, row_map: torch.Tensor, weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Torch oracle of `unpermute` (fp32 accumulation, bf16 result)."""
     N, K = row_map.shape
     w = weights if weights is not None else torch.ones((N, K), device=y.device)
     valid = row_map >= 0

@@ -13,6 +13,7 @@ def per_token_cast_to_fp8(x: torch.Tensor, round_scale: bool = False) -> Tuple[t
 
 
 def per_token_cast_back(x: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """FP8 e4m3 [N, H] with 1x128 fp32 scales [N, H/128] -> bf16 (sm_100a kernel)."""
     return require_ext().per_token_cast_back(x, scales)
 
 

@@ -8,4 +8,6 @@ from .reference import ReferenceBuffer
 
 
 class NcclAllToAllEP(ReferenceBuffer):
+    """Dispatch / combine as `all_to_all_single` over NCCL with torch FP8 casts: the baseline the
+    library is measured against, not the product."""
     pass

@@ -71,6 +71,7 @@ def get_rdma_gbs() -> float:
 
 
 def nvidia_smi_clocks() -> Optional[str]:
+    """One `nvidia-smi` clock / throttle-reason sample of this GPU, or None without nvidia-smi."""
     try:
         return subprocess.check_output(['nvidia-smi', '--query-gpu=clocks.sm,clocks.max.sm', '--format=csv,noheader'],
                                        text=True, timeout=10)
@@ -91,10 +92,12 @@ def init_seed(global_seed: int) -> None:
 
 
 def get_local_seed() -> Optional[int]:
+    """The seed of this rank set by `init_seed` (None before)."""
     return _SEEDS['local']
 
 
 def get_global_seed() -> Optional[int]:
+    """The global seed set by `init_seed` (None before)."""
     return _SEEDS['global']
 
 

@@ -9,6 +9,9 @@ import torch
 
 
 class EventOverlap:
+    """A CUDA event of an asynchronous call plus the tensors it keeps alive until the caller
+    waits on it (`current_stream_wait`), usable as a context manager (the reference's `EventOverlap`)."""
+
     def __init__(self, event=None, extra_tensors: Optional[Tuple[torch.Tensor, ...]] = None) -> None:
         self.event = event
         self.extra_tensors = extra_tensors

@@ -24,6 +24,7 @@ _alive: Counter = Counter()
 
 
 def enabled() -> bool:
+    """Whether lifecycle logging is on (`DEEPEP_B200_LIFECYCLE_LOG` set)."""
     return bool(os.environ.get(_ENV))
 
 

@@ -11,6 +11,8 @@ import torch
 
 
 def calc_diff(x: torch.Tensor, y: torch.Tensor) -> float:
+    """1 - 2<x+1, y+1> / (|x+1|^2 + |y+1|^2): 0 for identical tensors (the reference's comparison
+    metric)."""
     x, y = x.double() + 1, y.double() + 1
     denominator = (x * x + y * y).sum()
     sim = 2 * (x * y).sum() / denominator
@@ -18,6 +20,7 @@ def calc_diff(x: torch.Tensor, y: torch.Tensor) -> float:
 
 
 def safe_div(a, b) -> float:
+    """a / b, or 0 when b is 0."""
     if b == 0:
         if a == 0:
             return 0
@@ -26,10 +29,12 @@ def safe_div(a, b) -> float:
 
 
 def ceil_div(x: int, y: int) -> int:
+    """Ceiling of a / b for positive integers."""
     return (x + y - 1) // y
 
 
 def align(x: int, y: int) -> int:
+    """`x` rounded up to a multiple of `y`."""
     return ceil_div(x, y) * y
 
 
@@ -59,6 +64,7 @@ def per_token_cast_to_fp8(x: torch.Tensor, round_scale: bool = False) -> Tuple[t
 
 
 def per_token_cast_back(x_fp8: torch.Tensor, x_scales: torch.Tensor) -> torch.Tensor:
+    """Torch definition of the FP8 -> bf16 cast with 1x128 scales (oracle of the kernel)."""
     if x_fp8.numel() == 0:
         return x_fp8.to(torch.bfloat16)
     assert x_fp8.dim() == 2
@@ -105,6 +111,8 @@ def pack_ue8m0(scales: torch.Tensor) -> torch.Tensor:
 
 
 def inplace_unique(x: torch.Tensor, num_slots: int) -> None:
+    """Replace each row of `x` (values in [0, num_slots) or negative) by its unique values in
+    descending order, padded with -1 (in place)."""
     assert x.dim() == 2
     mask = x < 0
     x_padded = x.masked_fill(mask, num_slots)
@@ -120,10 +128,13 @@ def inplace_unique(x: torch.Tensor, num_slots: int) -> None:
 
 
 def hash_tensor(t: torch.Tensor) -> int:
+    """Sum of the tensor's bytes viewed as int32: a cheap content checksum (insensitive to element
+    order), for comparing runs."""
     return t.view(torch.int).sum().item()
 
 
 def count_bytes(*tensors) -> int:
+    """Total bytes of the given tensors (nested tuples / lists allowed, None entries count 0)."""
     total = 0
     for t in tensors:
         if isinstance(t, (tuple, list)):

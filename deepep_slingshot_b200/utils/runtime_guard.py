@@ -27,6 +27,7 @@ _RUNTIME_NAME = re.compile(r'libnccl\.so(?:\.\d+)*')
 
 
 class NcclRuntimeError(RuntimeError):
+    """Two NCCL runtimes, or an unexpected one, are mapped into this process."""
     pass
 
 

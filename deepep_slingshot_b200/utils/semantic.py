@@ -5,6 +5,7 @@ from typing import Any, Optional
 
 
 def value_or(value: Optional[Any], default: Any) -> Any:
+    """`value` unless it is None, else `default`."""
     return default if value is None else value
 
 

@@ -32,6 +32,7 @@ TRACE_EVENTS: Dict[int, str] = {
 
 
 class TraceOverflow(RuntimeError):
+    """The device trace ring filled up during a capture (the capture is invalid)."""
     pass
 
 
