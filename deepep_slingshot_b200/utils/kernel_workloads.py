@@ -7,6 +7,8 @@ Used to profile kernels in isolation (for example with Nsight Compute, filtering
 
 With `--time R` each workload is also timed: R repetitions, each bracketed by CUDA events on the
 current stream after a 256 MB write that evicts L2, median reported in microseconds.
+`--pending --only masked_gemm,ll_dispatch_gemm,bf16_mn,fused_dispatch_gemm` builds and runs the
+workloads of the kernels that have not run on a GPU yet (they are never in the default set).
 
 Sizes default to inputs larger than L2 for the bandwidth-bound kernels while keeping the whole
 process within a few GB of device memory.
@@ -93,8 +95,42 @@ def build(args):
     def barrier():
         buf.barrier()
 
-    return {'layout': layout, 'dispatch': dispatch, 'combine': combine, 'low_latency': ll, 'cast': cast,
+    work = {'layout': layout, 'dispatch': dispatch, 'combine': combine, 'low_latency': ll, 'cast': cast,
             'grouped_gemm': grouped_gemm, 'swiglu_quant': swiglu, 'permute': perm, 'barrier': barrier}
+    if not args.pending:
+        return work
+
+    # Kernels that have not run on a GPU yet (opt-in with --pending).
+    slots = T  # world 1: the low-latency layout has num_ranks * max_tokens slots per expert
+    n_small = 512  # weights generated on the device, kept to a few GB
+    mw1, mw1s = gemm.quantize_weights_fp8((torch.randn((E_ll, n_small, H), device='cuda') * 0.02).to(torch.bfloat16))
+    mw1s = mw1s.contiguous()
+    mx, msx = quant.per_token_cast_to_fp8(torch.randn((E_ll * slots, H), generator=g).to(torch.bfloat16).cuda())
+    mcnt = torch.full((E_ll,), min(slots, max(1, T * K // E_ll)), dtype=torch.int32, device='cuda')
+
+    def masked_gemm():
+        gemm.masked_grouped_gemm_fp8(mx.view(E_ll, slots, H), msx.view(E_ll, slots, H // 128), mcnt, mw1, mw1s)
+
+    def ll_dispatch_gemm():
+        out, cnt, hh, _ = buf.low_latency_dispatch_gemm(lx, lidx, T, E_ll, mw1, mw1s)
+        buf.low_latency_combine(ly, lidx, lw, hh)
+
+    bw = (torch.randn((e_g, k1, n1), generator=g) * 0.02).to(torch.bfloat16).cuda()  # [E, k, n] as it lies
+    ba = torch.randn((rows_per * e_g, k1), generator=g).to(torch.bfloat16).cuda()
+
+    def bf16_mn():
+        gemm.grouped_gemm_bf16(ba, bw, goff, gcnt, b_mn_major=True)
+
+    fw, fws = gemm.quantize_weights_fp8((torch.randn((E, n_small, H), device='cuda') * 0.02).to(torch.bfloat16))
+    fws = fws.contiguous()
+
+    def fused_dispatch_gemm():
+        h, grp, hnd = buf.dispatch_gemm(x, idx, w.float().contiguous(), E, fw, fws)
+        buf.combine(y_recv[:hnd[3].shape[0]], hnd, topk_weights=grp['topk_weights'])
+
+    work.update({'masked_gemm': masked_gemm, 'll_dispatch_gemm': ll_dispatch_gemm, 'bf16_mn': bf16_mn,
+                 'fused_dispatch_gemm': fused_dispatch_gemm})
+    return work
 
 
 def main():
@@ -110,10 +146,14 @@ def main():
     p.add_argument('--gemm-rows', type=int, default=1024)
     p.add_argument('--gemm-experts', type=int, default=4)
     p.add_argument('--time', type=int, default=0, help='timed repetitions per workload (0: profile pass only)')
+    p.add_argument('--pending', action='store_true',
+                   help='also build the workloads of kernels that have not run on a GPU yet (name them with --only)')
     args = p.parse_args()
     _init_single_rank()
     work = build(args)
-    names = [n for n in work if not args.only or n in args.only.split(',')]
+    default = {'layout', 'dispatch', 'combine', 'low_latency', 'cast', 'grouped_gemm', 'swiglu_quant', 'permute', 'barrier'}
+    wanted = set(args.only.split(',')) if args.only else default
+    names = [n for n in work if n in wanted]
     for n in names:  # warm-up outside the profiled range
         work[n]()
     torch.cuda.synchronize()
