@@ -20,7 +20,7 @@ def calc_diff(x: torch.Tensor, y: torch.Tensor) -> float:
 
 
 def safe_div(a, b) -> float:
-    """a / b, or 0 when b is 0."""
+    """a / b; 0 / 0 is 0 (any other division by zero raises)."""
     if b == 0:
         if a == 0:
             return 0
