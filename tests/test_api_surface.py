@@ -51,3 +51,28 @@ def test_leading_parameters():
     assert params(ep.Buffer.low_latency_combine)[:4] == ['x', 'topk_idx', 'topk_weights', 'handle']
     assert params(ep.ElasticBuffer.dispatch)[:3] == ['x', 'topk_idx', 'topk_weights']
     assert params(ep.ElasticBuffer.combine)[:3] == ['x', 'handle', 'topk_weights']
+
+
+def test_every_kernel_source_is_built():
+    """setup.py compiles every .cu / .cpp source of the extension (a new kernel file cannot be left out)."""
+    import glob
+    import os
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    setup = open(os.path.join(root, 'setup.py')).read()
+    listed = set(re.findall(r'"(kernels|runtime)", "([A-Za-z0-9_]+\.(?:cu|cpp))"', setup))
+    csrc = os.path.join(root, 'deepep_slingshot_b200', 'csrc')
+    on_disk = {(os.path.basename(os.path.dirname(p)), os.path.basename(p))
+               for p in glob.glob(os.path.join(csrc, 'kernels', '*.cu')) + glob.glob(os.path.join(csrc, 'runtime', '*.cpp'))}
+    assert on_disk <= listed, sorted(on_disk - listed)
+
+
+def test_fused_entry_points_exist():
+    from deepep_slingshot_b200 import Buffer
+    from deepep_slingshot_b200.models import MoEFFN
+    from deepep_slingshot_b200.ops import gemm, quant
+    for name in ('dispatch_gemm', 'low_latency_dispatch_gemm', 'low_latency_gemm_combine'):
+        assert callable(getattr(Buffer, name))
+    assert callable(MoEFFN.forward_low_latency) and callable(MoEFFN.quantized_weights)
+    assert callable(gemm.masked_grouped_gemm_fp8) and callable(gemm.grouped_gemm_bf16_wgrad_rows)
+    assert callable(quant.swiglu_quant)
