@@ -125,3 +125,26 @@ def check_torch_deterministic() -> None:
     initialisation kernel that can overlap with communication: refuse that combination."""
     import torch.utils.deterministic
     assert not (torch.are_deterministic_algorithms_enabled() and torch.utils.deterministic.fill_uninitialized_memory)
+
+
+def check_fast_rdma_atomic_support(nic_name: str = 'mlx5_0') -> bool:
+    """Whether the named RDMA NIC supports fast atomics (the reference sizes its QP count with it,
+    [DE]deep_ep/utils/envs.py:223, [DE]deep_ep/buffers/elastic.py:203). One NVLink box has no RDMA
+    transport in this library, so the answer only reports what `ibstat` says and nothing here
+    depends on it; False without `ibstat` or without the NIC."""
+    import subprocess
+    try:
+        out = subprocess.run(['ibstat', nic_name], capture_output=True, text=True, timeout=10)
+    except (OSError, subprocess.TimeoutExpired):
+        return False
+    if out.returncode != 0:
+        return False
+    # ConnectX-7 (MT4129) and older lack them; MT4131 (ConnectX-8) and newer have them.
+    for line in out.stdout.splitlines():
+        line = line.strip()
+        if line.startswith('CA type:') and 'MT' in line:
+            try:
+                return int(line.split('MT')[-1].strip()) >= 4131
+            except ValueError:
+                return False
+    return False

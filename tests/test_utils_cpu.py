@@ -76,3 +76,18 @@ def _refs_body(rank, world):
 @pytest.mark.parametrize('world', [1, 2])
 def test_functional_refs_gloo(world):
     run_ranks(_refs_body, world, 'gloo')
+
+
+def test_fast_rdma_atomic_check_without_nic(monkeypatch):
+    import subprocess
+    from deepep_slingshot_b200.utils.envs import check_fast_rdma_atomic_support
+
+    class Out:
+        def __init__(self, code, text):
+            self.returncode, self.stdout = code, text
+    monkeypatch.setattr(subprocess, 'run', lambda *a, **k: Out(0, "CA 'mlx5_0'\n\tCA type: MT4131\n"))
+    assert check_fast_rdma_atomic_support()
+    monkeypatch.setattr(subprocess, 'run', lambda *a, **k: Out(0, "\tCA type: MT4129\n"))
+    assert not check_fast_rdma_atomic_support()
+    monkeypatch.setattr(subprocess, 'run', lambda *a, **k: Out(1, ''))
+    assert not check_fast_rdma_atomic_support()
