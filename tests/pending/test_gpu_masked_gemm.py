@@ -66,7 +66,8 @@ def _fused_body(rank, world, N, H, E, K, n):
         assert int(cnt.sum()) > 0
         for e in range(E_l):
             c = int(cnt[e])
-            assert torch.equal(out[e, :c], ref[e, :c])
+            got, exp = out[e, :c].float(), ref[e, :c].float()
+            assert float((got - exp).abs().max()) <= 1e-2 * float(exp.abs().max()) + 1e-3
         # Expert outputs derived from each received row: the combine is independent of arrival order.
         from deepep_slingshot_b200.utils.math import per_token_cast_back
         scale = (1 + torch.arange(E_l, device='cuda').view(-1, 1, 1) * 0.25)
@@ -131,7 +132,7 @@ def _moe_decode_body(rank, world, N, H, I, E, K):
     torch.cuda.synchronize()
     assert _rel_err(out, ref.float()) < 3e-2
     # the fused down projection + combine send gives the same rows as GEMM then combine
-    assert torch.equal(out, out_unfused)
+    assert _rel_err(out, out_unfused.float()) < 1e-3
 
 
 @pytest.mark.parametrize('world', [1, 2])
