@@ -242,3 +242,28 @@ def test_ladder_counterbalanced_repeat(tmp_path):
     assert not run_ladder(out, fake, gates)            # the repeat is 50% off: fails closed
     medians['r'] = {'dispatch': 103.0}
     assert run_ladder(out, fake, gates, resume_reason='quiet box')
+
+
+def test_bench_report(tmp_path):
+    from deepep_slingshot_b200.harness import report
+    line1 = {'metric': 'm', 'value': 496.6, 'n_gpus': 1, 'vs_baseline': 0.676, 'dispatch_gbps_per_rank': 333.7,
+             'combine_gbps_per_rank': 666.0, 'dispatch_ms': 0.0919, 'combine_ms': 0.0884, 'll_dispatch_us': 24.7,
+             'll_combine_us': 34.8, 'moe_tokens_per_s': 79000.0, 'moe_ms_per_step': 51.8, 'moe_roofline_fraction': 0.27,
+             'moe_roofline_ms': {'compute': 4.4, 'nvlink': 0.0, 'hbm': 13.7, 'bound': 13.7},
+             'e2e': {'value': 80.0, 'ms_per_step': 1.1, 'h2d_bytes_per_step': 59113472, 'schedule': 'pipelined',
+                     'serial_value': 39.8},
+             'clocks': {'sm_mhz': 1965.0, 'sm_max_mhz': 1965.0, 'reasons': []}}
+    line8 = dict(line1, value=4091.0, n_gpus=8)
+    f = tmp_path / 'b.json'
+    f.write_text('NCCL version 2.28\n' + json.dumps(line1) + '\n' + json.dumps(line8) + '\nnot json {\n'
+                 + json.dumps({'impl': 'reference', 'unavailable': 'not installable'}) + '\n')
+    recs = report.load_lines([str(f)])
+    assert len(recs) == 3
+    rows = report.summarize(recs[0], {'hbm_gbs': 6558.4, 'bf16_tflops': 1650.1})
+    text = '\n'.join(rows)
+    assert '0.676' in text and '0.46 of published 726' in text and '3.12x faster' in text
+    assert 'HBM 13.7' in text and 'serial 39.8' in text and 'reasons: none' in text
+    assert 'unavailable' in report.summarize(recs[2])[0]
+    sc = '\n'.join(report.scaling(recs))
+    assert '| 8 | 4091.0 | 511.4 | 1.03 |' in sc
+    assert report.main([str(f), '--peaks', str(tmp_path / 'missing.json')]) == 0
