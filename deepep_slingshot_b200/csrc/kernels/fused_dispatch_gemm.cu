@@ -134,6 +134,11 @@ __device__ void pull_role(const FusedDispatchGemmArgs& a, FusedShared& sh, uint8
     const bool active = warp < 2 * kPullPairs;
     const int pair = warp >> 1;
     const bool producer = (warp & 1) == 0;
+    // Checked before the ring's mbarriers exist, so that an early return leaves none behind.
+    if (num_recv > a.num_out_rows) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) report_error(a.st, kErrCapacity, -1, num_recv);
+        return;
+    }
     PullRing p{};
     if (active) {
         p = pull_ring(smem, pair, S, slot_bytes);
@@ -156,14 +161,13 @@ __device__ void pull_role(const FusedDispatchGemmArgs& a, FusedShared& sh, uint8
         }
     }
     __syncthreads();
-    if (num_recv > a.num_out_rows) {
-        if (threadIdx.x == 0 && blockIdx.x == 0) report_error(a.st, kErrCapacity, -1, num_recv);
-        return;
-    }
     if (active) {
         const int g = blockIdx.x * kPullPairs + pair, P = a.pull_ctas * kPullPairs;
         const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
         if (producer) {
+            // Lane 0 issues the loads; after an expired wait it issues no more (the consumer stops
+            // at the first row that does not arrive) instead of waiting out every later row.
+            int failed = 0, issued = 0;
             for (int base = 0; base < my_rows; base += 32) {
                 const int kk = base + lane;
                 int src = 0, t = 0;
@@ -177,20 +181,28 @@ __device__ void pull_role(const FusedDispatchGemmArgs& a, FusedShared& sh, uint8
                 const int n = min(32, my_rows - base);
                 for (int i = 0; i < n; ++i) {
                     const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
-                    if (lane == 0) {
+                    if (lane == 0 && !failed) {
                         const int k = base + i, slot = k % S;
-                        bool ok = true;
-                        if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
-                        if (ok) {
+                        if (k >= S && !mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma)) {
+                            failed = 1;
+                        } else {
                             p.side[slot] = pt;
                             const uint8_t* gsrc = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
                                                   (int64_t)pt * a.layout.record_bytes;
                             mbar_arrive_expect_tx(&p.full[slot], a.rec.bytes);
                             tma_load_1d(p.slots + (size_t)slot * slot_bytes, gsrc, a.rec.bytes, &p.full[slot]);
+                            ++issued;
                         }
                     }
                 }
+                if (__shfl_sync(0xffffffffu, failed, 0)) break;
             }
+            // Every issued load lands before the ring's shared memory is reused (after a failure the
+            // consumer may have stopped short of them). Rows the consumer took already passed their
+            // wait; each slot's last use is the only phase still to check.
+            if (lane == 0)
+                for (int k = max(0, issued - S); k < issued; ++k)
+                    if (!mbar_wait(&p.full[k % S], (k / S) & 1, a.st, kErrTimeoutTma)) break;
         } else {
             // Lane 0 issues the stores and, kLag rows later, publishes their completion: it alone
             // observed the completion, fenced the async proxy and releases the counters.
@@ -399,6 +411,11 @@ __device__ void gemm_role(const CUtensorMap* map_a, const CUtensorMap* map_b, co
             int mt, e, nt;
             if (t < 0 || !fused_gemm_tile(t, n_tiles, sh.level, levels, sh.order, mt, e, nt)) break;
             const int rows = tile_rows(sh, e, mt);
+            // The tile's rows and scales were stored by pull CTAs, and the producer may not have
+            // seen them land yet: acquire the landed counter before reading the scales. After an
+            // expired wait the tile still completes, as in the producer.
+            if (lane == 0) wait_landed(a.landed + e * a.max_mtiles + mt, rows, a.st, t);
+            __syncwarp();
             const int m = sh.off[e] + mt * kBM + r_in;
             const float* sa_row = a.sa + (int64_t)m * nb;
             const float* sb_blk = a.sb + ((int64_t)e * (a.n / 128) + nt) * KB;

@@ -9,7 +9,10 @@ interleavings of the roles, the rings whose ordering the kernels rely on:
     all nine consumers read it, and the sentinel ends every consumer;
   * the shared-memory stage ring (TMA producer -> MMA, depth S) and the two TMEM accumulators
     (MMA -> eight epilogue warps) of the grouped GEMMs: stages and accumulators are never reused
-    before they are released.
+    before they are released;
+  * the pull ring of the fused kernel (slots freed kLag rows late, a failed wait partway, the
+    drain of loads in flight before its shared memory is reused);
+  * the order of the fused kernel's epilogue scale reads after the rows landed.
 """
 import random
 
@@ -138,3 +141,110 @@ def test_stage_ring_and_accumulators(seed):
                 tempty[b].arrive()
                 e['g'] += 1
     assert prod['g'] == mma['g'] == total and all(e['g'] == total for e in epis)
+
+
+@pytest.mark.parametrize('seed', range(60))
+def test_pull_ring_lagged_release_and_drain(seed):
+    """The pull ring of the fused dispatch -> GEMM kernel: the producer TMA-loads rows into S slots;
+    the consumer frees a slot only kLag rows after it took it (its stores may still read the slot),
+    so the ring runs iff S > kLag. A wait that expires stops the producer: it issues nothing more
+    and then waits for every load it issued (the last use of each slot) before the ring's shared
+    memory is reused. Loads land at random times (a separate actor)."""
+    rng = random.Random(seed)
+    lag = 4
+    S = rng.choice([lag + 1, lag + 2, 8])
+    rows = rng.randint(0, 40)
+    fail_at = rng.choice([None, None, rng.randint(0, max(0, rows - 1))])  # consumer stops at this row
+    full = [MBarrier(1) for _ in range(S)]
+    empty = [MBarrier(1) for _ in range(S)]
+    slot_row = [None] * S      # row whose load targets the slot
+    in_flight = set()          # rows whose loads have not landed
+    prod = {'k': 0, 'failed': False, 'issued': 0, 'drained': False}
+    cons = {'k': 0, 'done': False}
+    for step in range(200000):
+        actors = []
+        if not prod['drained']:
+            actors.append('p')
+        if not cons['done']:
+            actors.append('c')
+        if in_flight:
+            actors.append('land')
+        if not actors:
+            break
+        a = rng.choice(actors)
+        if a == 'land':
+            k = rng.choice(sorted(in_flight))
+            in_flight.discard(k)
+            full[k % S].arrive()
+        elif a == 'p':
+            k = prod['k']
+            if not prod['failed'] and k < rows:
+                s = k % S
+                if k < S or _done(empty[s], ((k // S) - 1) & 1):
+                    assert slot_row[s] is None or slot_row[s] <= k - S, 'slot reused before its row was released'
+                    assert all(r % S != s for r in in_flight), 'two loads in flight into one slot'
+                    slot_row[s] = k
+                    in_flight.add(k)
+                    prod['k'] += 1
+                    prod['issued'] += 1
+                elif cons['done']:
+                    prod['failed'] = True  # nobody will free the slot: the bounded wait expires
+            else:
+                # drain: the last use of every slot has landed before the memory is reused
+                issued = prod['issued']
+                if all(_done(full[k % S], (k // S) & 1) for k in range(max(0, issued - S), issued)):
+                    assert not in_flight, 'drain passed with a load still in flight'
+                    prod['drained'] = True
+        else:
+            k = cons['k']
+            if k >= rows or (fail_at is not None and k == fail_at):
+                cons['done'] = True   # finished, or its wait on row k expired
+                continue
+            s = k % S
+            if _done(full[s], (k // S) & 1):
+                assert slot_row[s] == k and k not in in_flight
+                if k >= lag:
+                    empty[(k - lag) % S].arrive()
+                cons['k'] += 1
+    assert prod['drained'] and cons['done'] and not in_flight
+    if fail_at is None:
+        assert cons['k'] == rows and prod['issued'] == rows
+
+
+@pytest.mark.parametrize('epilogue_acquires', [True, False])
+def test_tile_scales_read_after_rows_landed(epilogue_acquires):
+    """The GEMM producer of the fused kernel publishes a tile id before it waits for the tile's rows
+    to land; the epilogue reads the rows' scales with plain loads. Only an acquire of the landed
+    counter by the epilogue itself orders those loads after the rows. Without it, some schedule
+    reads a scale before its row landed (the case the kernel guards against)."""
+    violations = 0
+    for seed in range(200):
+        rng = random.Random(seed)
+        rows = 3
+        landed = 0
+        pushed = False
+        prod_waited = False
+        epi_state = 'wait_id'
+        bad = False
+        while epi_state != 'done':
+            a = rng.choice(['pull', 'prod', 'epi'])
+            if a == 'pull' and landed < rows:
+                landed += 1
+            elif a == 'prod':
+                if not pushed:
+                    pushed = True
+                elif not prod_waited and landed == rows:
+                    prod_waited = True
+            elif a == 'epi':
+                if epi_state == 'wait_id' and pushed:
+                    epi_state = 'acquire' if epilogue_acquires else 'read'
+                elif epi_state == 'acquire' and landed == rows:
+                    epi_state = 'read'
+                elif epi_state == 'read':
+                    bad |= landed < rows
+                    epi_state = 'done'
+        violations += bad
+    if epilogue_acquires:
+        assert violations == 0
+    else:
+        assert violations > 0
