@@ -15,7 +15,6 @@ import datetime
 import json
 import os
 
-import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -33,7 +32,7 @@ def main(argv=None):
     args = p.parse_args(argv)
     from .. import Buffer
     from ..utils import gate
-    from ..utils.trace import TRACE_EVENTS, capture, gather_and_write
+    from ..utils.trace import capture, gather_and_write
     owns = not dist.is_initialized()
     if owns:
         local = int(os.environ.get('LOCAL_RANK', '0'))

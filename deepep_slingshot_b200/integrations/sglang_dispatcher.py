@@ -14,7 +14,7 @@ DEEPEP_B200_SGLANG_SMS (SMs for dispatch/combine, default 64).
 import functools
 import logging
 import os
-from typing import Dict, Optional, Tuple
+from typing import Dict, Optional
 
 import torch
 import torch.distributed as dist

@@ -19,7 +19,6 @@ from types import SimpleNamespace
 from typing import Optional
 
 import torch
-import torch.distributed as dist
 
 from ..ops.gemm import grouped_gemm_fp8, quantize_weights_fp8
 from ..ops.permute import permute, unpermute

@@ -19,7 +19,7 @@ a caller can see:
 """
 import functools
 import os
-from typing import List, Optional, Tuple, Union
+from typing import Optional, Tuple, Union
 
 import torch
 import torch.distributed as dist

@@ -6,7 +6,7 @@ exchanges the handles over `torch.distributed` and opens every peer's region. Co
 collective call. The reference carves the same features out of its NCCL symmetric window
 ([DE]csrc/elastic/buffer.hpp:212-470); here each feature owns a region so they never alias.
 """
-from typing import Callable, List, Optional, Sequence, Tuple
+from typing import Callable, Optional, Tuple
 
 import torch
 import torch.distributed as dist

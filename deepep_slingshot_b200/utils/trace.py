@@ -10,7 +10,7 @@ sample (`Buffer.sample_clock`), and an overflowing ring raises instead of return
 Traced runs are for timelines, never for timing numbers.
 """
 import json
-from typing import Callable, Dict, Iterable, List, Optional
+from typing import Callable, Dict, List, Optional
 
 import numpy as np
 import torch

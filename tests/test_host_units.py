@@ -165,7 +165,6 @@ def test_random_unbalanced_scores_ratio():
 
 
 def test_elastic_side_feature_size_hints():
-    import torch.distributed as dist
     from deepep_slingshot_b200.parallel.elastic import ElasticBuffer
 
     class G:
