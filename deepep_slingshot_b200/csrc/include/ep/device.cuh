@@ -209,6 +209,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     }
 }
 
+// Bounded wait until the loads a ring producer issued into its last min(S, issued) slots have
+// landed (the last use of each slot; earlier uses completed before their slot was refilled). The
+// producer calls it before its CTA exits or reuses the ring's shared memory, so that no copy into
+// shared memory is still in flight after a consumer stopped early. Costs nothing once the consumer
+// has taken every row (those phases are complete).
+__device__ __forceinline__ void ring_drain(uint64_t* full, int S, int issued, const KernelStatus& st, int code) {
+    for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+        if (!mbar_wait(&full[i % S], (uint32_t)((i / S) & 1), st, code)) return;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

@@ -198,11 +198,8 @@ __device__ void pull_role(const FusedDispatchGemmArgs& a, FusedShared& sh, uint8
                 if (__shfl_sync(0xffffffffu, failed, 0)) break;
             }
             // Every issued load lands before the ring's shared memory is reused (after a failure the
-            // consumer may have stopped short of them). Rows the consumer took already passed their
-            // wait; each slot's last use is the only phase still to check.
-            if (lane == 0)
-                for (int k = max(0, issued - S); k < issued; ++k)
-                    if (!mbar_wait(&p.full[k % S], (k / S) & 1, a.st, kErrTimeoutTma)) break;
+            // consumer may have stopped short of them).
+            if (lane == 0) ring_drain(p.full, S, issued, a.st, kErrTimeoutTma);
         } else {
             // Lane 0 issues the stores and, kLag rows later, publishes their completion: it alone
             // observed the completion, fenced the async proxy and releases the counters.

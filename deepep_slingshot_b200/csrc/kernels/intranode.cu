@@ -512,6 +512,9 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
     const int S = p.S;
 
     if (producer) {
+        // After an expired wait lane 0 issues nothing more (the consumer stops at the first row that
+        // does not arrive) instead of waiting out every later row; then it drains what it issued.
+        int failed = 0, issued = 0;
         for (int base = 0; base < my_rows; base += 32) {
             const int kk = base + lane;
             int src = 0, t = 0;
@@ -529,20 +532,23 @@ __global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) 
             const int n = min(32, my_rows - base);
             for (int i = 0; i < n; ++i) {
                 const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
-                if (lane == 0) {
+                if (lane == 0 && !failed) {
                     const int k = base + i, slot = k % S;
-                    bool ok = true;
-                    if (k >= S) ok = mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma);
-                    if (ok) {
+                    if (k >= S && !mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma)) {
+                        failed = 1;
+                    } else {
                         p.side[2 * slot] = pt;
                         const uint8_t* gsrc = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
                                               (int64_t)pt * a.layout.record_bytes;
                         mbar_arrive_expect_tx(&p.full[slot], a.rec.bytes);
                         tma_load_1d(p.slots + (size_t)slot * slot_bytes, gsrc, a.rec.bytes, &p.full[slot]);
+                        ++issued;
                     }
                 }
             }
+            if (__shfl_sync(0xffffffffu, failed, 0)) break;
         }
+        if (lane == 0) ring_drain(p.full, S, issued, a.st, kErrTimeoutTma);
     } else {
         const int x_bytes = a.rec.x_bytes;
         const int nb = a.rec.scale_bytes > 0 ? a.layout.hidden / 128 : 0;
@@ -772,21 +778,22 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
         const int S = p.S;
         const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
         if (producer) {
-            for (int k = 0, c = 0; c < my_rows; ++k) {
+            // Only lane 0 works in this loop (no warp-wide step), so it alone stops at an expired
+            // wait (the consumer stops at the first row that does not arrive) and drains what it issued.
+            int c = 0;
+            for (int k = 0; c < my_rows; ++k) {
                 const int j = row_at(k);
                 if (j < 0) continue;
                 if (lane == 0) {
                     const int slot = c % S;
-                    bool ok = true;
-                    if (c >= S) ok = mbar_wait(&p.empty[slot], ((c / S) - 1) & 1, a.st, kErrTimeoutTma);
-                    if (ok) {
-                        mbar_arrive_expect_tx(&p.full[slot], row_bytes);
-                        tma_load_1d(p.slots + (size_t)slot * slot_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)j * row_bytes,
-                                    row_bytes, &p.full[slot]);
-                    }
+                    if (c >= S && !mbar_wait(&p.empty[slot], ((c / S) - 1) & 1, a.st, kErrTimeoutTma)) break;
+                    mbar_arrive_expect_tx(&p.full[slot], row_bytes);
+                    tma_load_1d(p.slots + (size_t)slot * slot_bytes, static_cast<const uint8_t*>(a.x) + (int64_t)j * row_bytes,
+                                row_bytes, &p.full[slot]);
                 }
                 ++c;
             }
+            if (lane == 0) ring_drain(p.full, S, c, a.st, kErrTimeoutTma);
         } else {
             // Slots recycle on read-completion (as in the pull). Arrivals are announced per batch of
             // kAnnounce rows: one drain of this thread's bulk stores, one sys-scope fence, then relaxed
@@ -874,6 +881,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
                 __syncwarp();
                 ++k;
             }
+            // After an early exit (an expired wait or a bounds error) stores of the unannounced batch
+            // may still read the ring: complete them before this warp moves on.
+            if (lane == 0) bulk_wait<0>();
             if (lagged && prev_cnt > 0) {
                 // The loop left early (an expired wait or a bounds error): announce what completed.
                 if (lane == 0) {
