@@ -335,6 +335,8 @@ void Buffer::destroy() {
     }
     if (host_error_) cudaFreeHost(host_error_);
     if (host_counters_) cudaFreeHost(host_counters_);
+    for (auto& pe : prof_events_) cudaEventDestroy(pe.second);  // profile points never collected
+    prof_events_.clear();
     nvl_base_ = ll_base_ = nullptr;
     dev_workspace_ = mask_ = nullptr;
     host_error_ = nullptr;
