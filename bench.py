@@ -169,7 +169,8 @@ def sum_over_ranks(v):
 def main():
     args = parse()
     if args.impl == 'reference':
-        print(json.dumps({'impl': 'reference', 'unavailable': REFERENCE_UNAVAILABLE}))
+        if int(os.environ.get('RANK', '0')) == 0:  # one line per job, also under torchrun
+            print(json.dumps({'impl': 'reference', 'unavailable': REFERENCE_UNAVAILABLE}))
         return 0
     rank, world, local = init(args)
     from deepep_slingshot_b200 import Buffer

@@ -267,3 +267,21 @@ def test_bench_report(tmp_path):
     sc = '\n'.join(report.scaling(recs))
     assert '| 8 | 4091.0 | 511.4 | 1.03 |' in sc
     assert report.main([str(f), '--peaks', str(tmp_path / 'missing.json')]) == 0
+
+
+def test_bench_reference_arm_prints_one_line_per_job():
+    """`bench.py --impl reference` exits 0 with one `unavailable` JSON line from rank 0 only (the
+    driver launches it under torchrun like the own arm)."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    outs = {}
+    for rank in ('0', '1'):
+        env = dict(os.environ, RANK=rank, WORLD_SIZE='2')
+        r = subprocess.run([sys.executable, os.path.join(root, 'bench.py'), '--impl', 'reference', '--gpus', '2'],
+                           cwd=root, env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs[rank] = [line for line in r.stdout.splitlines() if line.strip()]
+    assert len(outs['0']) == 1 and outs['1'] == []
+    rec = json.loads(outs['0'][0])
+    assert rec['impl'] == 'reference' and rec['unavailable']
