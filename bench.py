@@ -136,22 +136,59 @@ def init(args):
 
 def moe_roofline_seconds(rows: float, hidden: int, inter: int, local_experts: int, world: int, num_recv: float,
                          bf16_flops: float = 1650.1e12, hbm_bytes_per_s: float = 6558.4e9,
-                         nvlink_bytes_per_s: float = 770e9) -> dict:
-    """Lower bounds of one MoE training step (forward + backward) per rank, in seconds:
-    compute (FP8 forward at 2x the measured bf16 peak, bf16 backward at the measured peak), NVLink
-    (dispatch + combine of the forward and their mirrors in the backward), and HBM: every local
-    expert weight element moves at least 8 bytes per step (bf16 master read + FP8 write by the
-    quantization, FP8 read by the forward GEMMs, bf16 read by the input-gradient GEMMs, bf16 weight
-    gradient write). The step can be no faster than the largest of the three."""
+                         nvlink_bytes_per_s: float = 770e9, remote_in: float = None, remote_out: float = None) -> dict:
+    """Lower bounds of one MoE training step (forward + backward) on one rank, in seconds:
+    compute (FP8 forward at 2x the measured bf16 peak, bf16 backward at the measured peak) over the
+    rank's `rows` expert rows; NVLink per direction: the forward dispatch (FP8 rows + scales) and
+    combine (bf16 rows) and their bf16 mirrors in the backward, for the `remote_in` tokens this rank
+    receives from other ranks and the `remote_out` tokens it sends to them (both default to
+    (world - 1) / world of `num_recv`); and HBM: every local expert weight element moves at least
+    8 bytes per step (bf16 master read + FP8 write by the quantization, FP8 read by the forward
+    GEMMs, bf16 read by the input-gradient GEMMs, bf16 weight gradient write). The rank can be no
+    faster than the largest of the three."""
     fwd_flops = 6.0 * rows * hidden * inter
     bwd_flops = 12.0 * rows * hidden * inter
     t_compute = fwd_flops / (2 * bf16_flops) + bwd_flops / bf16_flops
-    remote = (world - 1) / world
-    nv_bytes = 2 * remote * num_recv * ((hidden + hidden // 128 * 4) + 2 * hidden)
-    t_comm = nv_bytes / nvlink_bytes_per_s
+    remote = (world - 1) / world * num_recv
+    r_in = remote if remote_in is None else remote_in
+    s_out = remote if remote_out is None else remote_out
+    fp8_row, bf16_row = hidden + hidden // 128 * 4, 2 * hidden
+    # forward: dispatch in / out (FP8), combine out / in (bf16); backward: the same tokens in bf16 both ways
+    bytes_in = r_in * fp8_row + s_out * bf16_row + (r_in + s_out) * bf16_row
+    bytes_out = s_out * fp8_row + r_in * bf16_row + (r_in + s_out) * bf16_row
+    t_comm = max(bytes_in, bytes_out) / nvlink_bytes_per_s
     weight_elems = local_experts * 3.0 * hidden * inter
     t_hbm = 8.0 * weight_elems / hbm_bytes_per_s
     return {'compute': t_compute, 'nvlink': t_comm, 'hbm': t_hbm, 'bound': max(t_compute, t_comm, t_hbm)}
+
+
+def moe_route_loads(topk_idx: torch.Tensor, num_experts: int, world: int):
+    """This rank's contribution to every destination rank under a routing `topk_idx [N, K]` (-1 =
+    dropped): expert rows (one per (token, k) whose expert lives there) and tokens (one per token with
+    at least one expert there)."""
+    per_rank = num_experts // world
+    valid = topk_idx >= 0
+    dest = torch.where(valid, topk_idx // per_rank, torch.zeros_like(topk_idx))
+    hit = torch.zeros((topk_idx.shape[0], world), dtype=torch.int64, device=topk_idx.device)
+    hit.scatter_add_(1, dest, valid.long())
+    return hit.sum(0), (hit > 0).sum(0)
+
+
+def moe_step_roofline(rows_to, tokens_from, hidden: int, inter: int, local_experts: int, **peaks) -> dict:
+    """Roofline of one MoE step for a routing: `rows_to[d]` expert rows rank d computes,
+    `tokens_from[s][d]` tokens rank s sends to rank d. Each rank's bound uses its own rows and its own
+    remote traffic; the exchanges are synchronous, so the step is bounded by the slowest rank (under
+    a skewed routing the rank that holds the popular experts, not the average rank)."""
+    world = len(rows_to)
+    worst = None
+    for d in range(world):
+        r_in = sum(tokens_from[s][d] for s in range(world) if s != d)
+        s_out = sum(tokens_from[d][s] for s in range(world) if s != d)
+        b = moe_roofline_seconds(rows_to[d], hidden, inter, local_experts, world, 0, remote_in=r_in, remote_out=s_out,
+                                 **peaks)
+        if worst is None or b['bound'] > worst['bound']:
+            worst = dict(b, rank=d, rows=float(rows_to[d]), remote_in=float(r_in), remote_out=float(s_out))
+    return worst
 
 
 def max_over_ranks(values):
@@ -336,6 +373,11 @@ def main():
         gout = torch.randn((N, H), generator=gm).to(torch.bfloat16).cuda()
 
         def moe_step():
+            # A training step starts from cleared gradients (optimizer.zero_grad(set_to_none=True), the
+            # PyTorch default): backward writes each gradient once instead of adding it to the last step's.
+            layer.zero_grad(set_to_none=True)
+            mx.grad = None
+            mw.grad = None
             out = layer(mx, midx, mw)
             out.backward(gout)
             return out
@@ -355,20 +397,31 @@ def main():
             mts.append(a0.elapsed_time(a1))
         mts = max_over_ranks(mts)
         ms_moe = sum(mts) / len(mts)
-        rows = sum_over_ranks(int((midx >= 0).sum())) / world  # expert rows per rank (average)
+        # The routing's load per rank: expert rows each rank computes, tokens each pair of ranks exchanges.
+        rows_to, tok_to = moe_route_loads(midx, E, world)
+        rows_all = rows_to.double().cuda()
+        dist.all_reduce(rows_all)
+        tok_mat = torch.zeros((world, world), dtype=torch.float64, device='cuda')
+        tok_mat[rank] = tok_to.double().cuda()
+        dist.all_reduce(tok_mat)
         # measured peaks (MEASURED_PEAKS.json): cuBLAS bf16 burst, STREAM-style copy; FP8 counted at 2x bf16
-        roof = moe_roofline_seconds(rows, H, inter, E // world, world, num_recv)
+        roof = moe_step_roofline(rows_all.tolist(), tok_mat.tolist(), H, inter, E // world)
         moe = {'moe_tokens_per_s': N * world / (ms_moe * 1e-3), 'moe_ms_per_step': ms_moe,
                'moe_roofline_fraction': roof['bound'] / (ms_moe * 1e-3),
-               'moe_roofline_ms': {k: v * 1e3 for k, v in roof.items()},
+               'moe_roofline_ms': {k: roof[k] * 1e3 for k in ('compute', 'nvlink', 'hbm', 'bound')},
+               'moe_roofline_rank': {'rank': roof['rank'], 'expert_rows': roof['rows'],
+                                     'expert_rows_mean': float(rows_all.mean()), 'remote_tokens_in': roof['remote_in'],
+                                     'remote_tokens_out': roof['remote_out']},
                'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
-                              'routing': 'zipf s=1.1', 'forward': 'fp8 block-scaled tcgen05 grouped GEMMs' +
+                              'routing': 'zipf s=1.1', 'grads': 'set to None before every step (zero_grad(set_to_none=True))',
+                              'forward': 'fp8 block-scaled tcgen05 grouped GEMMs' +
                               (', dispatch receive fused into the gate/up GEMM' if args.moe_fused_dispatch else ''),
                               'backward': ('bf16 tcgen05 grouped GEMMs (dgrad M-grouped, wgrad K-grouped)' if _moe_mod._GROUPED_BWD['tcgen05']
                                            else 'bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled']
                                            else 'bf16 per-expert torch matmuls (stand-in)'),
-                              'roofline': ('max(fp8 fwd at 2x bf16 peak + bf16 bwd at measured 1650 TFLOP/s, NVLink bytes '
-                                           'at 770 GB/s, 8 bytes per local weight element per step at measured 6558 GB/s HBM)')}}
+                              'roofline': ('slowest rank of max(its fp8 fwd at 2x bf16 peak + bf16 bwd at measured '
+                                           '1650 TFLOP/s over its expert rows, its NVLink bytes per direction at 770 GB/s, '
+                                           '8 bytes per local weight element per step at measured 6558 GB/s HBM)')}}
         del layer
         torch.cuda.empty_cache()
 

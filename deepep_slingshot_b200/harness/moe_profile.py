@@ -54,6 +54,9 @@ def main(argv=None):
     gout = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
 
     def step(times=None):
+        layer.zero_grad(set_to_none=True)  # as the bench's step: gradients written once, not accumulated
+        x.grad = None
+        w.grad = None
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         out = layer(x, idx, w)

@@ -244,3 +244,33 @@ def test_bench_moe_roofline_bounds():
     eight = bench.moe_roofline_seconds(32768, 7168, 2048, 32, 8, 21900)
     assert eight['bound'] == eight['compute'] and eight['hbm'] == one['hbm'] / 8
     assert abs(eight['compute'] - (6 * 32768 * 7168 * 2048 / (2 * 1650.1e12) + 12 * 32768 * 7168 * 2048 / 1650.1e12)) < 1e-12
+
+
+def test_bench_moe_roofline_uses_the_slowest_rank():
+    """Under a skewed routing the step's bound is the rank that holds the popular experts: its own
+    expert rows and its own remote traffic, not the average rank's."""
+    import importlib.util
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), 'bench.py')
+    spec = importlib.util.spec_from_file_location('_bench_under_test2', path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    E, world, N, K = 16, 4, 6, 2
+    idx = torch.tensor([[0, 1], [0, 5], [2, -1], [9, 13], [3, 4], [-1, -1]])
+    rows, toks = bench.moe_route_loads(idx, E, world)
+    assert rows.tolist() == [5, 2, 1, 1] and toks.tolist() == [4, 2, 1, 1]
+    # every rank sends the same routing: rank 0 computes 20 of the 36 rows
+    rows_to = [4 * r for r in rows.tolist()]
+    tokens_from = [toks.tolist() for _ in range(world)]
+    worst = bench.moe_step_roofline(rows_to, tokens_from, 7168, 2048, E // world)
+    assert worst['rank'] == 0 and worst['rows'] == 20
+    assert worst['remote_in'] == 3 * 4 and worst['remote_out'] == 2 + 1 + 1
+    alone = bench.moe_roofline_seconds(20, 7168, 2048, E // world, world, 0, remote_in=12, remote_out=4)
+    assert abs(worst['bound'] - alone['bound']) < 1e-15
+    mean = bench.moe_roofline_seconds(sum(rows_to) / world, 7168, 2048, E // world, world, 0, remote_in=12,
+                                      remote_out=4)
+    assert worst['compute'] > mean['compute']
+    # per direction: a rank that only receives tokens takes in their FP8 rows and one bf16 gradient
+    # row each, and sends back two bf16 rows each (forward combine, backward gradient combine)
+    b = bench.moe_roofline_seconds(0, 7168, 2048, 1, 2, 0, remote_in=100, remote_out=0, nvlink_bytes_per_s=1.0)
+    assert b['nvlink'] == max(100 * ((7168 + 56 * 4) + 2 * 7168), 100 * 2 * 2 * 7168)
