@@ -128,6 +128,10 @@ def init(args):
     os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
     os.environ.setdefault('MASTER_PORT', str(29600 + os.getpid() % 1000))
     torch.cuda.set_device(local)
+    # Run (and allocate pinned inputs) on the CPUs next to this GPU, before NCCL starts its threads.
+    from deepep_slingshot_b200.utils.numa import bind_process_to_gpu
+    cpus = bind_process_to_gpu(local)
+    args.host_cpus = f'{len(cpus)} CPUs local to the GPU (NVML affinity)' if cpus else 'process affinity unchanged'
     import datetime
     dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
                             device_id=torch.device('cuda', local))
@@ -560,6 +564,7 @@ def main():
                        'global_batch': N * world, 'seq_len': N, 'tokens_per_rank': N,
                        'parallelism': f'ep{world}', 'dispatch_dtype': 'fp8_e4m3 1x128 (fused quantization)',
                        'combine_dtype': 'bf16', 'num_sms': num_sms, 'l2': 'flushed before every timed step',
+                       'host_cpus': getattr(args, 'host_cpus', None),
                        'byte_definition': 'DeepEP v2 logical bytes incl. local traffic, summed over ranks',
                        'baseline': f'{BASELINE_CYCLE_GBPS_PER_RANK} GB/s per rank x n_gpus (published SM100 EP8 726/740)'},
             'dispatch_ms': ms_disp, 'combine_ms': ms_comb,
