@@ -77,7 +77,10 @@ class ClockSampler:
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
 
     def __init__(self, device: int):
-        self.device = device
+        # nvidia-smi numbers GPUs in PCI order whatever CUDA_VISIBLE_DEVICES says: name this process's
+        # GPU by its PCI bus id (the CUDA index only when the bus id is unknown).
+        from deepep_slingshot_b200.utils.numa import pci_bus_id
+        self.device = pci_bus_id(device) or str(device)
         self.proc = None
         self.file = None
 
@@ -85,7 +88,7 @@ class ClockSampler:
         try:
             self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200', '-i', str(self.device)], stdout=self.file,
+                                          '-lms', '200', '-i', self.device], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None

@@ -11,7 +11,8 @@ import os
 from typing import Optional, Set
 
 
-def _pci_bus_id(device: int) -> Optional[str]:
+def pci_bus_id(device: int) -> Optional[str]:
+    """PCI bus id of CUDA device `device` in NVML / nvidia-smi form (`00000000:18:00.0`)."""
     try:
         import torch
         p = torch.cuda.get_device_properties(device)
@@ -24,7 +25,7 @@ def gpu_local_cpus(device: int, nvml=None, num_cpus: Optional[int] = None) -> Op
     """CPUs NVML reports as close to CUDA device `device` (matched by PCI bus id, so the CUDA and
     NVML orderings may differ), intersected with the CPUs this process may use; None when NVML or the
     device is unavailable or the set would be empty. `nvml` defaults to the `pynvml` module."""
-    bus = _pci_bus_id(device)
+    bus = pci_bus_id(device)
     if bus is None:
         return None
     try:

@@ -29,7 +29,7 @@ class FakeNvml:
 
 @pytest.fixture
 def fake_bus(monkeypatch):
-    monkeypatch.setattr(numa, '_pci_bus_id', lambda device: f'00000000:{0x18 + device:02x}:00.0')
+    monkeypatch.setattr(numa, 'pci_bus_id', lambda device: f'00000000:{0x18 + device:02x}:00.0')
 
 
 def test_local_cpus_from_the_affinity_mask(fake_bus, monkeypatch):
@@ -51,7 +51,7 @@ def test_unavailable_nvml_or_device_changes_nothing(fake_bus, monkeypatch):
     applied = []
     monkeypatch.setattr(os, 'sched_setaffinity', lambda pid, cpus: applied.append(cpus))
     assert numa.bind_process_to_gpu(0, nvml=FakeNvml([0xff], fail=True)) is None
-    monkeypatch.setattr(numa, '_pci_bus_id', lambda device: None)
+    monkeypatch.setattr(numa, 'pci_bus_id', lambda device: None)
     assert numa.bind_process_to_gpu(0, nvml=FakeNvml([0xff])) is None
     assert applied == []
 
