@@ -71,10 +71,13 @@ def get_rdma_gbs() -> float:
 
 
 def nvidia_smi_clocks() -> Optional[str]:
-    """One `nvidia-smi` clock / throttle-reason sample of this GPU, or None without nvidia-smi."""
+    """One `nvidia-smi` sample (current and maximum SM clock) of the current CUDA device, named by
+    its PCI bus id so that CUDA_VISIBLE_DEVICES does not matter; None without nvidia-smi."""
+    from .numa import pci_bus_id
+    dev = pci_bus_id(torch.cuda.current_device()) if torch.cuda.is_available() else None
     try:
-        return subprocess.check_output(['nvidia-smi', '--query-gpu=clocks.sm,clocks.max.sm', '--format=csv,noheader'],
-                                       text=True, timeout=10)
+        return subprocess.check_output(['nvidia-smi', '--query-gpu=clocks.sm,clocks.max.sm', '--format=csv,noheader'] +
+                                       (['-i', dev] if dev else []), text=True, timeout=10)
     except Exception:
         return None
 
