@@ -356,7 +356,10 @@ __device__ void gemm_role(const CUtensorMap* map_a, const CUtensorMap* map_b, co
                     tc::tma_load_2d(sa_tile, map_a, kb * kBK, a_row, &s_full[s]);
                     tc::tma_load_2d(sa_tile + kBM * kBK, map_b, kb * kBK, b_row, &s_full[s]);
                 }
-                if (!loaded) break;
+                if (!loaded) {
+                    ring_drain(s_full, kGemmStages, (int)g, a.st, kErrTimeoutTma);  // issued loads land first
+                    break;
+                }
             }
         }
     } else if (warp == 1) {
@@ -387,6 +390,9 @@ __device__ void gemm_role(const CUtensorMap* map_a, const CUtensorMap* map_b, co
                     tc::mma_commit(&s_tfull[b]);
                 }
             }
+            // After an expired wait: issued MMAs complete before the TMEM is freed.
+            if (!ok && g > 0)
+                mbar_wait(&s_empty[(g - 1) % kGemmStages], ((g - 1) / kGemmStages) & 1, a.st, kErrTimeoutTma);
         }
     } else {
         // ---------------------------------------------------------------- epilogue / scale promotion

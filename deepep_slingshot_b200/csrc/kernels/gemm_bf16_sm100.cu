@@ -199,6 +199,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
                     load_operand<kBMN>(sb_tile, &map_b, ti.b_k_base + kx, ti.n0, ti.b_row0, kx, &s_full[s]);
                 }
             }
+            // After an expired wait: the loads already issued land before the CTA exits.
+            if (!ok) ring_drain(s_full, S, (int)g, a.st, kErrTimeoutTma);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
@@ -231,6 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
                 mma_commit(&s_tfull[b]);
                 ++j;
             }
+            // After an expired wait: issued MMAs complete before the TMEM is freed.
+            if (!ok && g > 0) mbar_wait(&s_empty[(g - 1) % S], ((g - 1) / S) & 1, a.st, kErrTimeoutTma);
         }
     } else {
         // ---------------------------------------------------------------- epilogue

@@ -192,7 +192,10 @@ __global__ void __launch_bounds__(kThreads, 1) masked_gemm_fp8_kernel(const __gr
                     tc::tma_load_2d(sa_tile, &map_a, kb * kBK, ti.e * a.slots + ti.m0, &s_full[s]);
                     tc::tma_load_2d(sa_tile + kABytes, &map_b, kb * kBK, ti.e * a.n + ti.n0, &s_full[s]);
                 }
-                if (!good) break;
+                if (!good) {
+                    ring_drain(s_full, S, (int)g, a.st, kErrTimeoutTma);  // issued loads land before exit
+                    break;
+                }
             }
         }
     } else if (warp == 1) {
@@ -220,6 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1) masked_gemm_fp8_kernel(const __gr
                     tc::mma_commit(&s_tfull[b]);
                 }
             }
+            // After an expired wait: issued MMAs complete before the TMEM is freed.
+            if (!ok && g > 0) mbar_wait(&s_empty[(g - 1) % S], ((g - 1) / S) & 1, a.st, kErrTimeoutTma);
         }
     } else {
         // ---------------------------------------------------------------- epilogue / scale promotion

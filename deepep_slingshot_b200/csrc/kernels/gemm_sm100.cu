@@ -163,6 +163,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                     tma_load_2d(sb_tile, &map_b, kb * kBK, ti.e * a.n + ti.n0, &s_full[s]);
                 }
             }
+            // After an expired wait: the loads already issued land before the CTA exits.
+            if (!ok) ring_drain(s_full, S, (int)g, a.st, kErrTimeoutTma);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
@@ -188,6 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                     mma_commit(&s_tfull[b]);
                 }
             }
+            // After an expired wait: the MMAs already issued complete before the TMEM is freed (the
+            // last commit tracks every earlier MMA of this thread).
+            if (!ok && g > 0) wait_bar(&s_empty[(g - 1) % S], ((g - 1) / S) & 1, a.st);
         }
     } else {
         // ---------------------------------------------------------------- epilogue / scale promotion
