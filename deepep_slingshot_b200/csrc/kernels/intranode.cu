@@ -129,7 +129,10 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
                 mbar_arrive_expect_tx(&s_bar[warp_id()], row_bytes);
                 tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + (int64_t)t * row_bytes, row_bytes, &s_bar[warp_id()]);
             }
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma) ? 1 : 0)) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma) ? 1 : 0)) {
+                if (lane == 0) mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma);  // the row lands before exit
+                break;
+            }
             phase ^= 1u;
             quantize_row_to_fp8<true>(reinterpret_cast<const __nv_bfloat16*>(buf), rec,
                                       reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);

@@ -289,6 +289,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                 }
                 __syncwarp();
                 ok = __all_sync(0xffffffffu, mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma) ? 1 : 0) != 0;
+                if (!ok && lane == 0) mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma);  // the row lands before exit
                 phase ^= 1u;
                 if (ok) {
                     LLHalf dh = half_of(a.peers, L, src, a.half);
@@ -308,6 +309,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
                     tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + ((int64_t)le * slots + j) * row_bytes, row_bytes,
                                 &s_bar[warp]);
                     ok = mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma);
+                    if (!ok) mbar_wait(&s_bar[warp], phase, a.st, kErrTimeoutTma);  // the row lands before exit
                     phase ^= 1u;
                     if (ok) {
                         LLHalf dh = half_of(a.peers, L, src, a.half);

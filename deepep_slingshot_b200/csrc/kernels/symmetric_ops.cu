@@ -31,7 +31,9 @@ __device__ bool tma_copy(const uint8_t* src, uint8_t* dst, int64_t n, uint8_t* s
     if (n <= 0) return true;
     const int64_t iters = (n + kCopyStageBytes - 1) / kCopyStageBytes;
     auto len = [&](int64_t i) { const int64_t r = n - i * kCopyStageBytes; return (uint32_t)(r < kCopyStageBytes ? r : kCopyStageBytes); };
+    int64_t issued = 0;  // loads issued so far (in index order)
     auto issue_load = [&](int64_t i) {
+        issued = i + 1;
         const int s = (int)(i % kCopyStages);
         mbar_arrive_expect_tx(&bars[s], len(i));
         tma_load_1d(smem + s * kCopyStageBytes, src + i * kCopyStageBytes, len(i), &bars[s]);
@@ -41,6 +43,7 @@ __device__ bool tma_copy(const uint8_t* src, uint8_t* dst, int64_t n, uint8_t* s
         const int s = (int)(i % kCopyStages);
         if (!mbar_wait(&bars[s], (uint32_t)((i / kCopyStages) & 1), st, code)) {
             bulk_wait<0>();
+            ring_drain(bars, kCopyStages, (int)issued, st, code);  // loads in flight land before the return
             return false;
         }
         tma_store_1d(dst + i * kCopyStageBytes, smem + s * kCopyStageBytes, len(i));
