@@ -16,6 +16,9 @@ Records: `manifest-rank{r}.jsonl` (source hashes, versions, environment), `corre
 Model shapes follow the reference's benchmark (backend/tests/ep_benchmark.py:19) plus DeepSeek-V3 and
 a Mixtral-style small-expert-count shape (hidden 4096, 8 experts, top-2), swept as
 `--models mixtral --dtype bf16 --routing uniform --tokens 128 512 2048 8192`.
+`--impl nccl` runs the same cases through the NCCL all-to-all baseline (`parallel.nccl_baseline`);
+`python -m deepep_slingshot_b200.harness.compare <ours_dir> <nccl_dir>` then pairs the two runs case by
+case (same inputs, routes and placement) and prints the speedup at every point.
 """
 import argparse
 import datetime
@@ -67,7 +70,7 @@ def manifest(args) -> dict:
             'nccl': '.'.join(map(str, torch.cuda.nccl.version())) if torch.cuda.is_available() else None,
             'gpu': torch.cuda.get_device_name() if torch.cuda.is_available() else None,
             'env': {k: v for k, v in os.environ.items() if k.startswith(('DEEPEP_', 'NCCL_', 'CUDA_', 'EP_'))},
-            'sources': source_hashes()}
+            'sources': source_hashes(), 'impl': getattr(args, 'impl', 'ours')}
 
 
 class _Jsonl:
@@ -105,7 +108,8 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
     case = {'model': model, 'hidden': H, 'experts': E, 'topk': K, 'tokens_per_rank': tokens, 'ranks': R,
             'dispatch_dtype': dtype, 'combine_dtype': 'bf16', 'routing': routing, 'seed': seed,
             'route_sha256': hash_tensor(idx), 'input_sha256': hash_tensor(x), 'alignment': 128,
-            'num_sms': args.num_sms or buf.num_sms, 'flush_l2': True, 'drop_every': args.drop_every}
+            'num_sms': args.num_sms or getattr(buf, 'num_sms', 0), 'flush_l2': True, 'drop_every': args.drop_every,
+            'impl': getattr(args, 'impl', 'ours')}
 
     # ---- correctness (fresh dispatch, then combine)
     kw = dict(topk_idx=idx, topk_weights=w, num_experts=E, expert_alignment=128)
@@ -251,12 +255,17 @@ def main(argv=None):
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--num-sms', type=int, default=0)
     p.add_argument('--out', default='ep_results')
+    p.add_argument('--impl', choices=['ours', 'nccl'], default='ours',
+                   help="'nccl': the same cases through all_to_all_single over NCCL with torch FP8 casts (the "
+                        "baseline; pair two result directories with harness.compare)")
     p.add_argument('--stall-us', type=float, default=None,
                    help='also run dispatch -> GPU stall -> combine loops (expert-compute stand-in)')
     p.add_argument('--stall-iters', type=int, default=200)
     p.add_argument('--sweep-sms', type=lambda v: [int(x) for x in v.split(',')], default=None,
                    help='comma-separated SM counts to time dispatch / combine with (tuning sweep)')
     args = p.parse_args(argv)
+    if args.impl == 'nccl' and (args.sweep_sms or args.stall_us is not None):
+        p.error('--sweep-sms and --stall-us time this library\'s kernels only (not --impl nccl)')
 
     from .. import Buffer, ReferenceBuffer
     from .summarize import summarize_dir
@@ -276,9 +285,13 @@ def main(argv=None):
     logs['manifest'].write(manifest(args))
     max_tokens = max(args.tokens)
     max_hidden = max(MODELS[m][0] for m in args.models)
-    buf = Buffer(dist.group.WORLD, num_nvl_bytes=Buffer.get_nvl_buffer_size_hint(max_tokens, max_hidden, world))
-    if args.num_sms:
-        Buffer.set_num_sms(args.num_sms)
+    if args.impl == 'nccl':
+        from ..parallel.nccl_baseline import NcclAllToAllEP
+        buf = NcclAllToAllEP(dist.group.WORLD)
+    else:
+        buf = Buffer(dist.group.WORLD, num_nvl_bytes=Buffer.get_nvl_buffer_size_hint(max_tokens, max_hidden, world))
+        if args.num_sms:
+            Buffer.set_num_sms(args.num_sms)
     ref = ReferenceBuffer(dist.group.WORLD)
     failures = 0
     for model in args.models:

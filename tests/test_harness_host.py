@@ -285,3 +285,16 @@ def test_bench_reference_arm_prints_one_line_per_job():
     assert len(outs['0']) == 1 and outs['1'] == []
     rec = json.loads(outs['0'][0])
     assert rec['impl'] == 'reference' and rec['unavailable']
+
+
+def test_ep_benchmark_nccl_arm_options():
+    """`--impl nccl` times the NCCL all-to-all baseline on the same cases; the kernel-only options
+    are refused before any process group or device is touched."""
+    from deepep_slingshot_b200.harness import ep_benchmark
+    for bad in (['--impl', 'nccl', '--sweep-sms', '8,16'], ['--impl', 'nccl', '--stall-us', '50']):
+        with pytest.raises(SystemExit) as e:
+            ep_benchmark.main(bad)
+        assert e.value.code == 2
+    from deepep_slingshot_b200.parallel.nccl_baseline import NcclAllToAllEP
+    from deepep_slingshot_b200 import ReferenceBuffer
+    assert issubclass(NcclAllToAllEP, ReferenceBuffer)
