@@ -8,9 +8,10 @@ For every (model, tokens, dtype, routing, seed) case each rank:
   1. builds its routing (`harness.routing`), inputs and routing weights;
   2. checks a fresh dispatch against `ReferenceBuffer` (NCCL all_to_all_single): received payload
      and FP8 scales byte for byte, top-k ids, weights, source indices and the 128-aligned
-     per-expert counts; then checks combine;
-  3. times fresh dispatch, cached dispatch and combine with CUDA events after an L2 flush, taking
-     the per-iteration max over ranks.
+     per-expert counts; then the combine (float rows within tolerance, integer-valued rows
+     exactly) and the cached dispatch (byte for byte against the fresh one);
+  3. times fresh dispatch, cached dispatch, combine and the full cycle (fresh dispatch + combine)
+     with CUDA events after an L2 flush, taking the per-iteration max over ranks.
 Records: `manifest-rank{r}.jsonl` (source hashes, versions, environment), `correctness-rank{r}.jsonl`,
 `timings-rank{r}.jsonl`; rank 0 writes `summary.csv` and `repeatability.json` (`harness.summarize`).
 Model shapes follow the reference's benchmark (backend/tests/ep_benchmark.py:19) plus DeepSeek-V3 and
@@ -137,9 +138,26 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
     # combine is collective: every rank runs it even after a local dispatch mismatch
     cx, cw, _ = buf.combine(y, handle, topk_weights=rw)
     ecx, ecw, _ = ref.combine(y, ehandle, topk_weights=ew)
+    # cached dispatch (the handle's layout, no count exchange) reproduces the fresh one byte for byte
+    crx = buf.dispatch(x, handle=handle, quantize_fp8=True)[0] if fp8 else buf.dispatch(x, handle=handle)[0]
+    # integer-valued rows: every partial sum is exact in fp32 and bf16, so the combine must equal the
+    # oracle's exactly, whatever the order of its reduction
+    yi = torch.randint(-4, 5, (num_recv, H), device='cuda', generator=g).to(torch.bfloat16)
+    ix, _, _ = buf.combine(yi, handle)
+    eix, _, _ = ref.combine(yi, ehandle)
     torch.cuda.synchronize()
     if error is None and not torch.allclose(cx.float(), ecx.float(), atol=2e-2, rtol=2e-2):
         error = 'combine output mismatch'
+    if error is None:
+        try:
+            if fp8:
+                _check_equal('cached dispatch payload', crx[0].view(torch.uint8), rx[0].view(torch.uint8))
+                _check_equal('cached dispatch scales', crx[1], rx[1])
+            else:
+                _check_equal('cached dispatch payload', crx.view(torch.uint8), rx.view(torch.uint8))
+            _check_equal('integer combine', ix, eix)
+        except AssertionError as e:
+            error = str(e)
     ok = torch.tensor([0 if error else 1], device='cuda')
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if int(ok.item()) == 0:
@@ -156,9 +174,14 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
     def comb():
         buf.combine(y, handle, topk_weights=rw)
 
+    def cycle():  # a full step: fresh dispatch, then the combine of its handle
+        h = buf.dispatch(x, **kw)[4]
+        buf.combine(y, h, topk_weights=rw)
+
     ops = {'dispatch': (fresh, dispatch_bytes(num_recv, H, K, fp8)),
            'cached_dispatch': (cached, dispatch_bytes(num_recv, H, K, fp8)),
-           'combine': (comb, combine_bytes(num_recv, H, K))}
+           'combine': (comb, combine_bytes(num_recv, H, K)),
+           'cycle': (cycle, dispatch_bytes(num_recv, H, K, fp8) + combine_bytes(num_recv, H, K))}
     result = {}
     for op, (fn, nbytes) in ops.items():
         dist.barrier()
