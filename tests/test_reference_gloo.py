@@ -138,3 +138,38 @@ def test_small_helpers():
         print('hidden')
     with empty_suppress():
         pass
+
+
+def _matrix_oracle_body(rank, world):
+    """The oracle over the normal-mode matrix the GPU test enumerates (CPU, gloo): FP8 / bf16 x
+    expert alignment 1 / 128 x 0 / 1 / 2 biases, and the cached dispatch through a copied handle."""
+    import itertools
+    from deepep_slingshot_b200 import ReferenceBuffer
+    ref = ReferenceBuffer(dist.group.WORLD)
+    N, H, E, K = 24 - rank, 256, 8, 2
+    g = torch.Generator().manual_seed(50 + rank)
+    for i, (fp8, align, nbias) in enumerate(itertools.product((True, False), (1, 128), (0, 1, 2))):
+        x = torch.randn((N, H), generator=g).to(torch.bfloat16)
+        idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)])
+        w = torch.rand((N, K), generator=g)
+        rx, ri, rw, counts, h, _ = ref.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E,
+                                                expert_alignment=align, quantize_fp8=fp8)
+        assert all(c % align == 0 for c in counts)
+        hc = tuple(t.clone() if isinstance(t, torch.Tensor) else t for t in h)
+        cx = ref.dispatch(x, handle=hc, quantize_fp8=fp8)[0]
+        if fp8:
+            assert torch.equal(cx[0].view(torch.uint8), rx[0].view(torch.uint8)) and torch.equal(cx[1], rx[1])
+        else:
+            assert torch.equal(cx, rx)
+        n = (rx[0] if fp8 else rx).shape[0]
+        biases = [torch.full((N, H), float(b + 1), dtype=torch.bfloat16) for b in range(nbias)]
+        bias = None if nbias == 0 else (biases[0] if nbias == 1 else tuple(biases))
+        out, ow, _ = ref.combine(torch.ones((n, H), dtype=torch.bfloat16), h, topk_weights=rw, bias=bias)
+        dst = (idx // (E // world)).tolist()
+        expect = torch.tensor([len(set(d)) for d in dst], dtype=torch.float32) + sum(b + 1 for b in range(nbias))
+        assert torch.equal(out[:, 0].float(), expect), (i, out[:, 0], expect)
+        assert torch.allclose(ow, w, atol=1e-6)
+
+
+def test_reference_mode_matrix_gloo():
+    run_ranks(_matrix_oracle_body, 2, 'gloo')
