@@ -279,7 +279,16 @@ class Buffer:
             expert_alignment, num_worst_tokens, quantize_fp8, round_scale, scales_col_major, None, config.num_sms,
             prev, async_finish, allocate_on_comm_stream)
         if is_token_in_rank is None:
-            is_token_in_rank = send_head >= 0
+            if async_finish:
+                # Nothing waited for the comm stream (no CPU sync with num_worst_tokens): derive the mask
+                # there, after the kernels that write send_head, and return an event that covers it.
+                comm = self.get_comm_stream()
+                with torch.cuda.stream(comm):
+                    is_token_in_rank = send_head >= 0
+                    event = require_ext().EventHandle()
+                is_token_in_rank.record_stream(torch.cuda.current_stream())
+            else:
+                is_token_in_rank = send_head >= 0
         handle = (rank_prefix_matrix, send_prefix_matrix, recv_rank_prefix, recv_src_idx, is_token_in_rank, send_head)
         return (recv_x, recv_scales) if recv_scales is not None else recv_x, recv_topk_idx, recv_topk_weights, \
             num_recv_tokens_per_expert_list, handle, EventOverlap(event)
@@ -369,6 +378,14 @@ class Buffer:
                 def hook():
                     raw_hook()
                     _fill()
+            elif async_finish:
+                # The dispatch ran on the comm stream and nothing waited for it: pack there, after it,
+                # and hand back an event that also covers the packing.
+                comm = self.get_comm_stream()
+                packed.record_stream(comm)
+                with torch.cuda.stream(comm):
+                    _fill()
+                    event = require_ext().EventHandle()  # recorded on the comm stream, after the packing
             else:
                 _fill()
             recv = (recv_x, packed)

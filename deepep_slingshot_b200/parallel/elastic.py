@@ -21,6 +21,33 @@ from ..ops.permute import permute, unpermute
 from .buffer import Buffer, nvtx_range
 
 
+@contextmanager
+def _no_stream_change():
+    yield
+
+
+def _record_on_current_stream(*objs) -> None:
+    """`record_stream` every tensor reachable from `objs` (tuples, lists, EPHandle attributes) on the
+    current stream: they were allocated on the comm stream and are used on this one."""
+    cur = torch.cuda.current_stream()
+    seen = set()
+
+    def walk(o):
+        if isinstance(o, torch.Tensor):
+            if id(o) not in seen:
+                seen.add(id(o))
+                o.record_stream(cur)
+        elif isinstance(o, (tuple, list)):
+            for x in o:
+                walk(x)
+        elif isinstance(o, EPHandle):
+            for x in vars(o).values():
+                walk(x)
+
+    for o in objs:
+        walk(o)
+
+
 class EPHandle:
     """Routing state returned by `ElasticBuffer.dispatch`, reusable as a cached handle and consumed by
     `combine` (fields follow [DE]deep_ep/buffers/elastic.py:24-87)."""
@@ -184,11 +211,18 @@ class ElasticBuffer:
                 x, sf, None, None, None, 0, rpm, spm, src_idx, send_head, handle.expert_alignment, 0, quantize_fp8,
                 round_scale, use_tma_aligned_col_major_sf and not handle.do_expand, None, num_sms, prev,
                 async_with_compute_stream, allocate_on_comm_stream)
-            rx, rs = out[0], out[1]
+            rx, rs, event = out[0], out[1], out[11]
             if handle.do_expand:
-                rx, rs = self._expand_rows(rx, rs, handle)
+                if async_with_compute_stream:
+                    # as in the fresh dispatch: expand after the kernels, on the comm stream
+                    with torch.cuda.stream(self.get_comm_stream()):
+                        rx, rs = self._expand_rows(rx, rs, handle)
+                        event = require_ext().EventHandle()
+                    _record_on_current_stream(rx, rs)
+                else:
+                    rx, rs = self._expand_rows(rx, rs, handle)
             recv_x = (rx, rs) if rs is not None else rx
-            return recv_x, None, None, handle, EventOverlap(out[11])
+            return recv_x, None, None, handle, EventOverlap(event)
         assert topk_idx is not None and num_experts is not None
         num_topk = topk_idx.shape[1]
         num_sms = self.get_theoretical_num_sms(num_experts, num_topk) if num_sms == 0 else num_sms
@@ -201,38 +235,47 @@ class ElasticBuffer:
             x, sf, topk_idx, topk_weights, None, num_experts, None, None, None, None, expert_alignment, num_worst,
             quantize_fp8, round_scale, use_tma_aligned_col_major_sf, cumulative_local_expert_recv_stats, num_sms,
             previous_event, async_with_compute_stream, allocate_on_comm_stream)
-        is_token_in_rank = send_head >= 0
-        legacy = (rpm, spm, rrp, src_idx, is_token_in_rank, send_head)
-        # source metadata: [global source token index, source rank]
-        num_rows = src_idx.shape[0]
-        src_rank = torch.searchsorted(rrp[1:].to(torch.int64),
-                                      torch.arange(num_rows, device=src_idx.device, dtype=torch.int64), right=True)
-        src_rank = src_rank.clamp_(max=self.num_ranks - 1).to(torch.int32)
-        recv_src_metadata = torch.stack([src_rank * num_max_tokens_per_rank + src_idx, src_rank], dim=1)
-        psum_expert = per_expert_dev.cumsum(0).to(torch.int32)
-        ep_handle = EPHandle(do_expand, num_experts, expert_alignment, num_max_tokens_per_rank, num_sms,
-                             topk_idx.clone() if do_handle_copy else topk_idx, per_expert_list, rrp[1:], psum_expert,
-                             recv_src_metadata, legacy)
-        if do_expand:
-            # Expanded layout: one row per (received token, local expert), grouped by expert with every
-            # group padded to `expert_alignment` (the permute kernels). recv_src_metadata gains the row
-            # of each top-k slot (-1 if not local); psum per expert = aligned start + unpadded count.
-            E_l = num_experts // self.num_ranks
-            ep_handle.recv_topk_idx_local = recv_topk_idx
-            perm = permute(recv_x, recv_topk_idx, E_l, alignment=expert_alignment, probs=recv_topk_weights,
-                           x_scales=recv_sf.contiguous() if recv_sf is not None else None)
-            ep_handle.row_map = perm.row_map
-            ep_handle.expert_offsets = perm.expert_offsets
-            ep_handle.recv_src_metadata = torch.cat([recv_src_metadata, perm.row_map], dim=1)
-            ep_handle.psum_num_recv_tokens_per_expert = (perm.expert_offsets[:-1] + perm.expert_counts).to(torch.int32)
-            ep_handle.num_recv_tokens_per_expert_list = perm.expert_counts.tolist() if do_cpu_sync else []
-            rows = int(perm.expert_offsets[-1].item())
-            recv_x = perm.x[:rows]
-            recv_sf = perm.scales[:rows] if perm.scales is not None else None
-            if recv_sf is not None and use_tma_aligned_col_major_sf:
-                recv_sf = recv_sf.t().contiguous().t()
-            recv_topk_weights = perm.probs[:rows] if perm.probs is not None else None
+        # Asynchronous mode: nothing has waited for the comm stream, so everything below, which reads the
+        # pulled rows and their metadata, runs there after the kernels, and the returned event is
+        # recorded after it; the outputs are then marked for use on the caller's stream.
+        comm = self.get_comm_stream() if async_with_compute_stream else None
+        with (torch.cuda.stream(comm) if comm is not None else _no_stream_change()):
+            is_token_in_rank = send_head >= 0
+            legacy = (rpm, spm, rrp, src_idx, is_token_in_rank, send_head)
+            # source metadata: [global source token index, source rank]
+            num_rows = src_idx.shape[0]
+            src_rank = torch.searchsorted(rrp[1:].to(torch.int64),
+                                          torch.arange(num_rows, device=src_idx.device, dtype=torch.int64), right=True)
+            src_rank = src_rank.clamp_(max=self.num_ranks - 1).to(torch.int32)
+            recv_src_metadata = torch.stack([src_rank * num_max_tokens_per_rank + src_idx, src_rank], dim=1)
+            psum_expert = per_expert_dev.cumsum(0).to(torch.int32)
+            ep_handle = EPHandle(do_expand, num_experts, expert_alignment, num_max_tokens_per_rank, num_sms,
+                                 topk_idx.clone() if do_handle_copy else topk_idx, per_expert_list, rrp[1:], psum_expert,
+                                 recv_src_metadata, legacy)
+            if do_expand:
+                # Expanded layout: one row per (received token, local expert), grouped by expert with every
+                # group padded to `expert_alignment` (the permute kernels). recv_src_metadata gains the row
+                # of each top-k slot (-1 if not local); psum per expert = aligned start + unpadded count.
+                E_l = num_experts // self.num_ranks
+                ep_handle.recv_topk_idx_local = recv_topk_idx
+                perm = permute(recv_x, recv_topk_idx, E_l, alignment=expert_alignment, probs=recv_topk_weights,
+                               x_scales=recv_sf.contiguous() if recv_sf is not None else None)
+                ep_handle.row_map = perm.row_map
+                ep_handle.expert_offsets = perm.expert_offsets
+                ep_handle.recv_src_metadata = torch.cat([recv_src_metadata, perm.row_map], dim=1)
+                ep_handle.psum_num_recv_tokens_per_expert = (perm.expert_offsets[:-1] + perm.expert_counts).to(torch.int32)
+                ep_handle.num_recv_tokens_per_expert_list = perm.expert_counts.tolist() if do_cpu_sync else []
+                rows = int(perm.expert_offsets[-1].item())
+                recv_x = perm.x[:rows]
+                recv_sf = perm.scales[:rows] if perm.scales is not None else None
+                if recv_sf is not None and use_tma_aligned_col_major_sf:
+                    recv_sf = recv_sf.t().contiguous().t()
+                recv_topk_weights = perm.probs[:rows] if perm.probs is not None else None
+            if comm is not None:
+                event = require_ext().EventHandle()
         out_x = (recv_x, recv_sf) if recv_sf is not None else recv_x
+        if comm is not None:
+            _record_on_current_stream(out_x, recv_topk_idx, recv_topk_weights, ep_handle)
         return out_x, recv_topk_idx, recv_topk_weights, ep_handle, EventOverlap(event)
 
     @staticmethod

@@ -34,3 +34,4 @@ class EventOverlap:
         if self.event is not None:
             self.current_stream_wait(release_handle=self._release_handle_by_call)
         self._release_handle_by_call = False
+
