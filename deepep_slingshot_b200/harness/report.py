@@ -67,6 +67,11 @@ def summarize(rec: dict, peaks: Optional[dict] = None) -> List[str]:
         rows.append(f"| MoE fwd+bwd | {_fmt(rec['moe_tokens_per_s'], 0)} tok/s ({_fmt(rec.get('moe_ms_per_step'))} ms) | "
                     f"{_fmt(rec.get('moe_roofline_fraction'), 3)} of the roofline (bound {_fmt(roof.get('bound'))} ms: "
                     f"compute {_fmt(roof.get('compute'))}, NVLink {_fmt(roof.get('nvlink'))}, HBM {_fmt(roof.get('hbm'))}) |")
+        hot = rec.get('moe_roofline_rank')
+        if hot:
+            rows.append(f"| MoE bounding rank | rank {hot.get('rank')}: {_fmt(hot.get('expert_rows'), 0)} expert rows | "
+                        f"mean {_fmt(hot.get('expert_rows_mean'), 0)} rows per rank; remote tokens in "
+                        f"{_fmt(hot.get('remote_tokens_in'), 0)}, out {_fmt(hot.get('remote_tokens_out'), 0)} |")
     e2e = rec.get('e2e')
     if e2e:
         rows.append(f"| end to end | {_fmt(e2e.get('value'))} GB/s ({_fmt(e2e.get('ms_per_step'), 3)} ms/step) | "

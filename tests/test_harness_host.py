@@ -253,7 +253,9 @@ def test_bench_report(tmp_path):
              'e2e': {'value': 80.0, 'ms_per_step': 1.1, 'h2d_bytes_per_step': 59113472, 'schedule': 'pipelined',
                      'serial_value': 39.8},
              'clocks': {'sm_mhz': 1965.0, 'sm_max_mhz': 1965.0, 'reasons': []}}
-    line8 = dict(line1, value=4091.0, n_gpus=8)
+    line8 = dict(line1, value=4091.0, n_gpus=8,
+                 moe_roofline_rank={'rank': 2, 'expert_rows': 41932.0, 'expert_rows_mean': 32768.0,
+                                    'remote_tokens_in': 21852.0, 'remote_tokens_out': 17853.0})
     f = tmp_path / 'b.json'
     f.write_text('NCCL version 2.28\n' + json.dumps(line1) + '\n' + json.dumps(line8) + '\nnot json {\n'
                  + json.dumps({'impl': 'reference', 'unavailable': 'not installable'}) + '\n')
@@ -264,6 +266,7 @@ def test_bench_report(tmp_path):
     assert '0.676' in text and '0.46 of published 726' in text and '3.12x faster' in text
     assert 'HBM 13.7' in text and 'serial 39.8' in text and 'reasons: none' in text
     assert 'unavailable' in report.summarize(recs[2])[0]
+    assert 'rank 2: 41932 expert rows' in '\n'.join(report.summarize(recs[1]))
     sc = '\n'.join(report.scaling(recs))
     assert '| 8 | 4091.0 | 511.4 | 1.03 |' in sc
     assert report.main([str(f), '--peaks', str(tmp_path / 'missing.json')]) == 0
