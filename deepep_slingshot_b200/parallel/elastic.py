@@ -21,6 +21,12 @@ from ..ops.permute import permute, unpermute
 from .buffer import Buffer, nvtx_range
 
 
+def _native_event(previous_event):
+    """The native event of `previous_event` (an `EventOverlap`, as dispatch / combine return, or the
+    native event itself), or None."""
+    return getattr(previous_event, 'event', previous_event)
+
+
 @contextmanager
 def _no_stream_change():
     yield
@@ -205,7 +211,7 @@ class ElasticBuffer:
             assert not do_cpu_sync, 'Cannot do CPU sync with cached handle'
             num_experts = num_experts or handle.num_experts
             num_sms = num_sms or handle.num_sms
-            prev = previous_event
+            prev = _native_event(previous_event)
             rpm, spm, rrp, src_idx, itir, send_head = handle.legacy_handle
             out = self.runtime.intranode_dispatch(
                 x, sf, None, None, None, 0, rpm, spm, src_idx, send_head, handle.expert_alignment, 0, quantize_fp8,
@@ -234,7 +240,7 @@ class ElasticBuffer:
          per_expert_dev, event) = self.runtime.intranode_dispatch(
             x, sf, topk_idx, topk_weights, None, num_experts, None, None, None, None, expert_alignment, num_worst,
             quantize_fp8, round_scale, use_tma_aligned_col_major_sf, cumulative_local_expert_recv_stats, num_sms,
-            previous_event, async_with_compute_stream, allocate_on_comm_stream)
+            _native_event(previous_event), async_with_compute_stream, allocate_on_comm_stream)
         # Asynchronous mode: nothing has waited for the comm stream, so everything below, which reads the
         # pulled rows and their metadata, runs there after the kernels, and the returned event is
         # recorded after it; the outputs are then marked for use on the caller's stream.
@@ -301,8 +307,8 @@ class ElasticBuffer:
         rpm, spm, _, src_idx, _, send_head = handle.legacy_handle
         bias_0, bias_1 = Buffer._unpack_bias(bias)
         combined_x, combined_w, event = self.runtime.intranode_combine(
-            x, topk_weights, bias_0, bias_1, rpm, spm, send_head, src_idx, num_sms, previous_event, async_with_compute_stream,
-            allocate_on_comm_stream)
+            x, topk_weights, bias_0, bias_1, rpm, spm, send_head, src_idx, num_sms, _native_event(previous_event),
+            async_with_compute_stream, allocate_on_comm_stream)
         return combined_x, combined_w, EventOverlap(event)
 
     # ------------------------------------------------------------------ experimental side features

@@ -274,3 +274,14 @@ def test_bench_moe_roofline_uses_the_slowest_rank():
     # row each, and sends back two bf16 rows each (forward combine, backward gradient combine)
     b = bench.moe_roofline_seconds(0, 7168, 2048, 1, 2, 0, remote_in=100, remote_out=0, nvlink_bytes_per_s=1.0)
     assert b['nvlink'] == max(100 * ((7168 + 56 * 4) + 2 * 7168), 100 * 2 * 2 * 7168)
+
+
+def test_elastic_previous_event_unwrapping():
+    """v2 calls accept the `EventOverlap` that dispatch / combine return as `previous_event` (the
+    native call gets its event), a native event as is, or nothing."""
+    from deepep_slingshot_b200.parallel.elastic import _native_event
+    from deepep_slingshot_b200.utils.event import EventOverlap
+    native = object()
+    assert _native_event(EventOverlap(native)) is native
+    assert _native_event(native) is native
+    assert _native_event(None) is None
