@@ -212,9 +212,10 @@ __global__ void __launch_bounds__(256) permute_zero_padding_kernel(PermuteArgs a
     }
 }
 
-void launch_permute(const PermuteArgs& a, cudaStream_t stream) {
+cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream) {
     const int num_chunks = (a.num_tokens + 31) / 32;
-    cudaMemsetAsync(a.counts, 0, sizeof(int) * (size_t)num_chunks * a.num_experts, stream);
+    cudaError_t err = cudaMemsetAsync(a.counts, 0, sizeof(int) * (size_t)num_chunks * a.num_experts, stream);
+    if (err != cudaSuccess) return err;
     const int blocks = (num_chunks + 7) / 8;
     if (num_chunks > 0)
         permute_count_kernel<<<blocks, 256, 0, stream>>>(a.topk_idx, a.num_tokens, a.num_topk, a.num_experts, a.counts);
@@ -222,7 +223,10 @@ void launch_permute(const PermuteArgs& a, cudaStream_t stream) {
                                                 a.expert_offsets, a.expert_counts);
     if (num_chunks > 0) {
         const size_t smem = sizeof(int) * 8 * (size_t)a.num_experts;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(permute_rowmap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (smem > 48 * 1024) {
+            err = cudaFuncSetAttribute(permute_rowmap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (err != cudaSuccess) return err;
+        }
         permute_rowmap_kernel<<<blocks, 256, smem, stream>>>(a);
         const int row_bytes = a.hidden * a.x_elem_bytes;
         const int64_t items = (int64_t)a.num_tokens * ((row_bytes + kPermuteSegBytes - 1) / kPermuteSegBytes);
@@ -231,6 +235,7 @@ void launch_permute(const PermuteArgs& a, cudaStream_t stream) {
     }
     if (a.zero_padding && a.alignment > 1 && a.expert_counts != nullptr)
         permute_zero_padding_kernel<<<a.num_experts, 256, 0, stream>>>(a);
+    return cudaPeekAtLastError();
 }
 
 // out[t] = sum_k w[t][k] * y[row_map[t][k]] (fp32 accumulation in k order, bf16 out).

@@ -24,7 +24,9 @@ struct PermuteArgs {
     int zero_padding;            // zero the alignment padding rows of x_perm / scales_perm (grouped GEMMs over whole groups)
 };
 
-void launch_permute(const PermuteArgs& a, cudaStream_t stream);
+// Returns the first error of its own set-up calls (memset, function attribute), else
+// cudaPeekAtLastError() after the launches (which does not clear it).
+cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream);
 void launch_unpermute(const void* y, const int* row_map, const float* w, int N, int H, int K, void* out,
                       cudaStream_t stream);
 

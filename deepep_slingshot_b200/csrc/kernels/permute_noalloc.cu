@@ -43,6 +43,9 @@ extern "C" __attribute__((visibility("default"))) int ep_permute_noalloc(
         return EP_PERMUTE_NOALLOC_ERR_BAD_ARGS;
     const int64_t chunks = (num_tokens + 31) / 32;
     if (chunks * num_experts > EP_PERMUTE_NOALLOC_SCRATCH_INTS || num_experts > 4096) return EP_PERMUTE_NOALLOC_ERR_TOO_LARGE;
+    // An error left pending by earlier work is reported as such, not taken for this call's launch
+    // failure (and not cleared: it belongs to the caller).
+    if (cudaPeekAtLastError() != cudaSuccess) return EP_PERMUTE_NOALLOC_ERR_PENDING;
     int* scratch = nullptr;
     const int rc = scratch_for_current_device(&scratch);
     if (rc != EP_PERMUTE_NOALLOC_OK) return rc;
@@ -66,8 +69,11 @@ extern "C" __attribute__((visibility("default"))) int ep_permute_noalloc(
     a.x_perm = x_perm;
     a.scales_perm = scales_perm;
     a.probs_perm = probs_perm;
-    ep::launch_permute(a, stream);
-    return cudaGetLastError() == cudaSuccess ? EP_PERMUTE_NOALLOC_OK : EP_PERMUTE_NOALLOC_ERR_LAUNCH;
+    // No error was pending at entry, so what is pending now comes from this call's own set-up or
+    // launches; clear it and report it.
+    const cudaError_t err = ep::launch_permute(a, stream);
+    const cudaError_t last = cudaGetLastError();
+    return (err == cudaSuccess && last == cudaSuccess) ? EP_PERMUTE_NOALLOC_OK : EP_PERMUTE_NOALLOC_ERR_LAUNCH;
 }
 
 extern "C" __attribute__((visibility("default"))) const char* ep_permute_noalloc_strerror(int code) {
@@ -77,7 +83,9 @@ extern "C" __attribute__((visibility("default"))) const char* ep_permute_noalloc
         case EP_PERMUTE_NOALLOC_ERR_TOO_LARGE:
             return "too large: ceil(num_tokens/32) * num_experts exceeds the fixed scratch of 65536 entries";
         case EP_PERMUTE_NOALLOC_ERR_SYMBOL: return "could not look up the device scratch array (cudaGetSymbolAddress failed)";
-        case EP_PERMUTE_NOALLOC_ERR_LAUNCH: return "kernel launch failed";
+        case EP_PERMUTE_NOALLOC_ERR_LAUNCH: return "kernel launch or its set-up (memset, function attribute) failed";
+        case EP_PERMUTE_NOALLOC_ERR_PENDING:
+            return "a CUDA error from earlier work was already pending (left in place; nothing was launched)";
         default: return "unknown error";
     }
 }

@@ -39,6 +39,7 @@
 #define EP_PERMUTE_NOALLOC_ERR_TOO_LARGE 2
 #define EP_PERMUTE_NOALLOC_ERR_SYMBOL 3
 #define EP_PERMUTE_NOALLOC_ERR_LAUNCH 4
+#define EP_PERMUTE_NOALLOC_ERR_PENDING 5
 
 extern "C" {
 

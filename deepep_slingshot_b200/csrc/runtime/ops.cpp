@@ -291,7 +291,7 @@ permute(const torch::Tensor& x, const std::optional<torch::Tensor>& x_scales, co
     a.row_map = row_map.data_ptr<int>();
     a.x_perm = x_perm.data_ptr();
     a.zero_padding = zero_padding ? 1 : 0;
-    launch_permute(a, at::cuda::getCurrentCUDAStream());
+    C10_CUDA_CHECK(launch_permute(a, at::cuda::getCurrentCUDAStream()));
     return {x_perm, sp, pp, row_map, offsets, ecounts};
 }
 

@@ -36,6 +36,8 @@ import torch.distributed as dist
 
 MODELS = {'v4flash': (4096, 256, 6), 'qwen3': (4096, 128, 8), 'minimax': (3072, 256, 8),
           'deepseek_v3': (7168, 256, 8), 'mixtral': (4096, 8, 2)}
+# The operations every case times, in order; summary.csv has one row per (case, op).
+TIMED_OPS = ('dispatch', 'cached_dispatch', 'combine', 'cycle')
 
 
 def dispatch_bytes(num_recv: int, hidden: int, num_topk: int, fp8: bool) -> int:
@@ -182,6 +184,7 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
            'cached_dispatch': (cached, dispatch_bytes(num_recv, H, K, fp8)),
            'combine': (comb, combine_bytes(num_recv, H, K)),
            'cycle': (cycle, dispatch_bytes(num_recv, H, K, fp8) + combine_bytes(num_recv, H, K))}
+    assert tuple(ops) == TIMED_OPS
     result = {}
     for op, (fn, nbytes) in ops.items():
         dist.barrier()

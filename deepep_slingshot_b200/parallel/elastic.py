@@ -205,6 +205,13 @@ class ElasticBuffer:
                  handle: Optional[EPHandle] = None, do_handle_copy: bool = True, do_cpu_sync: Optional[bool] = None,
                  do_expand: bool = False, use_tma_aligned_col_major_sf: bool = False, quantize_fp8: bool = False,
                  round_scale: bool = False):
+        """v2 dispatch ([DE]deep_ep/buffers/elastic.py:708-855): returns
+        `(recv_x, recv_topk_idx, recv_topk_weights, EPHandle, EventOverlap)`.
+
+        With `async_with_compute_stream` the kernels and the post-processing run on the comm stream and
+        the returned event covers both. `do_expand` sizes its expanded outputs from the received row
+        count, which the host reads, so with `do_expand` the call waits for the comm stream before it
+        returns even in the asynchronous mode (the event is then already complete)."""
         x, sf = x if isinstance(x, tuple) else (x, None)
         if handle is not None:
             assert topk_idx is None and topk_weights is None
@@ -236,6 +243,10 @@ class ElasticBuffer:
         expert_alignment = expert_alignment or 1
         do_cpu_sync = True if do_cpu_sync is None else do_cpu_sync
         num_worst = 0 if do_cpu_sync else num_max_tokens_per_rank * self.num_ranks
+        # The handle's copy of the routing is taken on the caller's stream, before the call returns, so a
+        # later in-place write to `topk_idx` on that stream cannot reach the cached handle (in the
+        # asynchronous mode the post-processing below runs later, on the comm stream).
+        handle_topk_idx = topk_idx.clone() if do_handle_copy else topk_idx
         (recv_x, recv_sf, recv_topk_idx, recv_topk_weights, per_expert_list, rpm, spm, rrp, src_idx, send_head,
          per_expert_dev, event) = self.runtime.intranode_dispatch(
             x, sf, topk_idx, topk_weights, None, num_experts, None, None, None, None, expert_alignment, num_worst,
@@ -256,7 +267,7 @@ class ElasticBuffer:
             recv_src_metadata = torch.stack([src_rank * num_max_tokens_per_rank + src_idx, src_rank], dim=1)
             psum_expert = per_expert_dev.cumsum(0).to(torch.int32)
             ep_handle = EPHandle(do_expand, num_experts, expert_alignment, num_max_tokens_per_rank, num_sms,
-                                 topk_idx.clone() if do_handle_copy else topk_idx, per_expert_list, rrp[1:], psum_expert,
+                                 handle_topk_idx, per_expert_list, rrp[1:], psum_expert,
                                  recv_src_metadata, legacy)
             if do_expand:
                 # Expanded layout: one row per (received token, local expert), grouped by expert with every

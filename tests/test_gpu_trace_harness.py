@@ -65,7 +65,8 @@ def test_ep_benchmark_harness(world, tmp_path):
     with open(os.path.join(out, 'summary.csv')) as f:
         lines = f.read().strip().splitlines()
     n_routings = 2 if world == 1 else 3
-    assert len(lines) == 1 + n_routings * 2 * 3  # routings x dtypes x ops
+    from deepep_slingshot_b200.harness.ep_benchmark import TIMED_OPS
+    assert len(lines) == 1 + n_routings * 2 * len(TIMED_OPS)  # routings x dtypes x ops
     for r in range(world):
         recs = [json.loads(l) for l in open(os.path.join(out, f'correctness-rank{r}.jsonl'))]
         assert recs and all(x['passed'] for x in recs)

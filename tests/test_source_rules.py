@@ -1,7 +1,6 @@
 """Source rules of the GPU pool, checked over every file that travels with the repository.
 
 Patterns are assembled from fragments so that this file does not contain them itself:
-  * no TMA / bulk load with cluster multicast anywhere (multi-GPU runs must never reach one);
   * none of the four batched-copy calls that faulted GPUs on this driver;
   * no `__trap` in device code (failures are reported through status words, never by trapping);
   * comments and docstrings name no build notes (the project's .md working files), no machine path
@@ -34,10 +33,6 @@ def _hits(pattern):
                 if rx.search(line):
                     out.append(f'{os.path.relpath(path, ROOT)}:{n}: {line.strip()[:120]}')
     return out
-
-
-def test_no_cluster_multicast_loads():
-    assert _hits('multicast' + '::' + 'cluster') == []
 
 
 def test_no_batched_copy_calls():
