@@ -114,6 +114,13 @@ struct CombineArgs {
     int chunk;                       // push order: -1 wavefront over destinations, 0 contiguous, N chunks of N rows
     int stages;
     int announce_lagged;             // 1: announce a batch of rows one batch later, without draining the stores
+    // Expanded mode (row_map != null): x holds one row per (received token, local expert) in any
+    // order (the expert-grouped GEMM output) and the sender reduces each token's rows before the
+    // push: slot = bf16(sum_k row_weights[j][k] * x[row_map[j][k]]), fp32 accumulation in k order.
+    const int* row_map;              // [num_recv][row_map_k] row of x, -1 = not a local expert of the token
+    const float* row_weights;        // [num_recv][row_map_k] fp32 factors, or null (plain sum)
+    int row_map_k;
+    int x_rows;                      // rows of x (bounds of row_map entries)
     KernelStatus st;
 };
 void launch_combine(const CombineArgs& a, int num_sms, cudaStream_t stream);

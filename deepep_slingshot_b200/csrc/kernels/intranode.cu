@@ -740,6 +740,122 @@ __device__ __forceinline__ void combine_reduce_loop(const CombineArgs& a, Normal
     }
 }
 
+// Expanded mode, sender side: bf16(sum_q w[q] * x[rows[q]]) of one token into a ring slot (shared
+// memory), fp32 accumulation in q order. Each lane owns 8 columns per 256-column step and keeps
+// kU x kN independent 16-byte loads in flight.
+template <int kU, int kN>
+__device__ __forceinline__ void expanded_rows_to_slot(const __nv_bfloat16* __restrict__ x, const int* rows, const float* ws,
+                                                      int n, int H, uint8_t* slot) {
+    const int lane = lane_id();
+    int4 v[kU][kN];
+    for (int e0 = lane * 8; e0 - lane * 8 < H; e0 += 256 * kU) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int e = e0 + u * 256;
+#pragma unroll
+            for (int q = 0; q < kN; ++q)
+                if (q < n && e < H) v[u][q] = ld_nc_v4(reinterpret_cast<const int4*>(x + (int64_t)rows[q] * H + e));
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int e = e0 + u * 256;
+            if (e >= H) break;
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+            for (int q = 0; q < kN; ++q) {
+                if (q >= n) break;
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v[u][q]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __bfloat1622float2(h2[i]);
+                    acc[2 * i] = fmaf(ws[q], f.x, acc[2 * i]);
+                    acc[2 * i + 1] = fmaf(ws[q], f.y, acc[2 * i + 1]);
+                }
+            }
+            int4 o;
+            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+            *reinterpret_cast<int4*>(slot + (size_t)e * 2) = o;
+        }
+    }
+}
+
+// More than 8 local rows of one token (top-k above 8): the q-th row and factor come from the lane
+// that holds them (q-th set bit of `valid`) inside the column loop; off the common path.
+__device__ __forceinline__ void expanded_rows_to_slot_many(const __nv_bfloat16* __restrict__ x, int r, float w,
+                                                           uint32_t valid, int n, int H, uint8_t* slot) {
+    const int lane = lane_id();
+    for (int e0 = 0; e0 < H; e0 += 256) {
+        const int e = e0 + lane * 8;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int q = 0; q < n; ++q) {
+            const int src = (int)__fns(valid, 0, q + 1);
+            const int row = __shfl_sync(0xffffffffu, r, src);
+            const float wq = __shfl_sync(0xffffffffu, w, src);
+            if (e < H) {
+                const int4 v = ld_nc_v4(reinterpret_cast<const int4*>(x + (int64_t)row * H + e));
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __bfloat1622float2(h2[i]);
+                    acc[2 * i] = fmaf(wq, f.x, acc[2 * i]);
+                    acc[2 * i + 1] = fmaf(wq, f.y, acc[2 * i + 1]);
+                }
+            }
+        }
+        if (e < H) {
+            int4 o;
+            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+            *reinterpret_cast<int4*>(slot + (size_t)e * 2) = o;
+        }
+    }
+}
+
+// One token of the expanded mode into `slot`: gather its local rows and factors (row_map order),
+// report and skip an out-of-range row (the call then fails on the host), reduce.
+__device__ __forceinline__ void expanded_token_to_slot(const CombineArgs& a, int j, uint8_t* slot) {
+    const int lane = lane_id(), K = a.row_map_k, H = a.layout.hidden;
+    int r = -1;
+    float w = 1.f;
+    if (lane < K) {
+        r = a.row_map[(int64_t)j * K + lane];
+        if (a.row_weights != nullptr) w = a.row_weights[(int64_t)j * K + lane];
+        if (r >= a.x_rows) {
+            report_error(a.st, kErrBounds, j, r);
+            r = -1;
+        }
+    }
+    const uint32_t valid = __ballot_sync(0xffffffffu, r >= 0);
+    const int n = __popc(valid);
+    const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(a.x);
+    if (n > 8) {
+        expanded_rows_to_slot_many(x, r, w, valid, n, H, slot);
+        return;
+    }
+    int rows[8];
+    float ws[8];
+    uint32_t m = valid;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const int src = m ? __ffs(m) - 1 : 0;
+        rows[q] = __shfl_sync(0xffffffffu, r, src);
+        ws[q] = __shfl_sync(0xffffffffu, w, src);
+        if (m) m &= m - 1;
+    }
+    if (n <= 1) expanded_rows_to_slot<8, 1>(x, rows, ws, n, H, slot);
+    else if (n == 2) expanded_rows_to_slot<4, 2>(x, rows, ws, n, H, slot);
+    else if (n <= 4) expanded_rows_to_slot<2, 4>(x, rows, ws, n, H, slot);
+    else expanded_rows_to_slot<1, 8>(x, rows, ws, n, H, slot);
+}
+
+template <bool kExpanded>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_prefix[kMaxRanks + 1];
@@ -765,13 +881,18 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
             s_red_base[s] = a.send_prefix_matrix[a.rank * R + s];
         }
     }
-    const PipeSmem p = pipe_smem(smem, warp >> 1, a.stages, slot_bytes);
-    if (pusher && warp < 2 * kPairs) pipe_init(p);
+    // Warps 0..2*kPairs-1 form the (producer, consumer) pairs. In the expanded mode the other warps of
+    // a push block are extra producers (two per pair), since each row is computed, not copied.
+    const bool pair_warp = warp < 2 * kPairs;
+    const int pair = pair_warp ? warp >> 1 : (warp - 2 * kPairs) >> 1;
+    constexpr int kProducers = kExpanded ? 1 + (kCombineThreads / 32 - 2 * kPairs) / kPairs : 1;
+    const int prod_idx = pair_warp ? 0 : 1 + ((warp - 2 * kPairs) % (kProducers - 1 > 0 ? kProducers - 1 : 1));
+    const PipeSmem p = pipe_smem(smem, pair, a.stages, slot_bytes);
+    if (pusher && pair_warp) pipe_init(p);
     __syncthreads();
 
-    if (pusher && warp < 2 * kPairs && !aborted(a.st)) {
-        const int pair = warp >> 1;
-        const bool producer = (warp & 1) == 0;
+    if (pusher && (pair_warp || kExpanded) && !aborted(a.st)) {
+        const bool producer = !pair_warp || (warp & 1) == 0;
         const int num_recv = min(s_prefix[R], a.num_recv_max);
         const int g = blockIdx.x * kPairs + pair, P = a.push_blocks * kPairs;
         const bool wave = a.chunk < 0;
@@ -780,7 +901,26 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
         auto row_at = [&](int k) { return wave ? wave_row(g, P, k, s_prefix, R, num_recv) : pair_row(g, P, k, a.chunk, num_recv); };
         const int S = p.S;
         const int64_t rows_cap = (int64_t)a.layout.capacity * a.layout.num_ranks;
-        if (producer) {
+        if (producer && kExpanded) {
+            // Producer prod_idx computes the pair's rows c with c % kProducers == prod_idx straight into
+            // their slots (generic stores, then a proxy fence so the consumer's TMA store sees them).
+            int c = 0;
+            for (int k = 0; c < my_rows; ++k) {
+                const int j = row_at(k);
+                if (j < 0) continue;
+                if (c % kProducers == prod_idx) {
+                    const int slot = c % S;
+                    int good = 1;
+                    if (lane == 0 && c >= S) good = mbar_wait(&p.empty[slot], ((c / S) - 1) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
+                    if (!__shfl_sync(0xffffffffu, good, 0)) break;
+                    expanded_token_to_slot(a, j, p.slots + (size_t)slot * slot_bytes);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&p.full[slot]);
+                }
+                ++c;
+            }
+        } else if (producer) {
             // Only lane 0 works in this loop (no warp-wide step), so it alone stops at an expired
             // wait (the consumer stops at the first row that does not arrive) and drains what it issued.
             int c = 0;
@@ -901,7 +1041,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
             }
         }
     }
-    if (pusher && lane == 0 && warp < 2 * kPairs) trace_end(a.st, kTraceCombinePush, t_start, warp);
+    if (pusher && lane == 0 && pair_warp) trace_end(a.st, kTraceCombinePush, t_start, warp);
     // Every warp (push warps once their rows are sent) reduces tokens of this rank.
     if (!aborted(a.st)) combine_reduce_loop(a, my_ctrl, s_red_base);
     __syncthreads();
@@ -932,8 +1072,13 @@ void launch_combine(const CombineArgs& a_in, int num_sms, cudaStream_t stream) {
     if (a.push_blocks < 1) a.push_blocks = 1;
     const int reduce_blocks = sm_count - a.push_blocks;
     const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
-    cudaFuncSetAttribute(combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    combine_kernel<<<a.push_blocks + reduce_blocks, kCombineThreads, smem, stream>>>(a);
+    if (a.row_map != nullptr) {
+        cudaFuncSetAttribute(combine_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        combine_kernel<true><<<a.push_blocks + reduce_blocks, kCombineThreads, smem, stream>>>(a);
+    } else {
+        cudaFuncSetAttribute(combine_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        combine_kernel<false><<<a.push_blocks + reduce_blocks, kCombineThreads, smem, stream>>>(a);
+    }
 }
 
 // =================================================================================================

@@ -198,7 +198,8 @@ __global__ void __launch_bounds__(512) permute_copy_kernel(PermuteArgs a) {
     }
 }
 
-// One CTA per expert: zero rows [offset[e] + count[e], offset[e + 1]) of x_perm (and their scales).
+// One CTA per expert: zero rows [offset[e] + count[e], offset[e + 1]) of x_perm (and their scales
+// and probabilities).
 __global__ void __launch_bounds__(256) permute_zero_padding_kernel(PermuteArgs a) {
     const int e = blockIdx.x;
     const int r0 = a.expert_offsets[e] + a.expert_counts[e], r1 = a.expert_offsets[e + 1];
@@ -209,6 +210,7 @@ __global__ void __launch_bounds__(256) permute_zero_padding_kernel(PermuteArgs a
         for (int o = threadIdx.x; o < row_bytes / 16; o += blockDim.x) d[o] = make_int4(0, 0, 0, 0);
         if (a.scales_perm != nullptr)
             for (int b = threadIdx.x; b < nb; b += blockDim.x) a.scales_perm[(int64_t)r * nb + b] = 0.f;
+        if (a.probs_perm != nullptr && threadIdx.x == 0) a.probs_perm[r] = 0.f;
     }
 }
 

@@ -938,10 +938,26 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
     const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,
     const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, const torch::Tensor& recv_src_idx, int num_sms,
-    std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream) {
+    std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream,
+    const std::optional<torch::Tensor>& row_map, const std::optional<torch::Tensor>& row_weights) {
     check_error();
-    TORCH_CHECK(recv_src_idx.scalar_type() == torch::kInt32 && recv_src_idx.is_contiguous() && recv_src_idx.size(0) >= x.size(0),
-                "handle's recv_src_idx must cover every row of x");
+    // Expanded mode: x has one row per (received token, local expert); row_map [num_recv][K] names
+    // each token's rows, row_weights [num_recv][K] (optional) their fp32 factors.
+    const bool expanded = row_map.has_value();
+    const int64_t num_recv_rows = expanded ? row_map->size(0) : x.size(0);
+    if (expanded) {
+        TORCH_CHECK(row_map->dim() == 2 && row_map->scalar_type() == torch::kInt32 && row_map->is_contiguous() &&
+                        row_map->size(1) >= 1 && row_map->size(1) <= 32,
+                    "row_map must be contiguous int32 [num_recv, K] with 1 <= K <= 32");
+        if (row_weights.has_value())
+            TORCH_CHECK(row_weights->scalar_type() == torch::kFloat32 && row_weights->is_contiguous() &&
+                            row_weights->sizes() == row_map->sizes(),
+                        "row_weights must be contiguous fp32 with row_map's shape");
+    } else {
+        TORCH_CHECK(!row_weights.has_value(), "row_weights needs row_map");
+    }
+    TORCH_CHECK(recv_src_idx.scalar_type() == torch::kInt32 && recv_src_idx.is_contiguous() && recv_src_idx.size(0) >= num_recv_rows,
+                "handle's recv_src_idx must cover every received token");
     TORCH_CHECK(available_, "buffer not synced");
     TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16, "x must be contiguous bf16 [rows, hidden]");
     const int H = (int)x.size(1), R = num_ranks_;
@@ -950,7 +966,7 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     const int K = topk_weights.has_value() ? (int)topk_weights->size(1) : 0;
     if (topk_weights.has_value())
         TORCH_CHECK(topk_weights->scalar_type() == torch::kFloat32 && topk_weights->is_contiguous() &&
-                    topk_weights->size(0) == x.size(0));
+                    topk_weights->size(0) == num_recv_rows);
     for (const auto* b : {&bias_0, &bias_1})
         if (b->has_value())
             TORCH_CHECK((*b)->scalar_type() == torch::kBFloat16 && (*b)->is_contiguous() && (*b)->size(0) == N && (*b)->size(1) == H);
@@ -977,7 +993,11 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     ca.num_topk = K;
     ca.x = x.data_ptr();
     ca.topk_weights = topk_weights.has_value() ? topk_weights->data_ptr<float>() : nullptr;
-    ca.num_recv_max = (int)x.size(0);
+    ca.num_recv_max = (int)num_recv_rows;
+    ca.row_map = expanded ? row_map->data_ptr<int>() : nullptr;
+    ca.row_weights = row_weights.has_value() ? row_weights->data_ptr<float>() : nullptr;
+    ca.row_map_k = expanded ? (int)row_map->size(1) : 0;
+    ca.x_rows = (int)x.size(0);
     ca.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
     ca.send_prefix_matrix = send_prefix_matrix.data_ptr<int>();
     ca.recv_src_idx = recv_src_idx.data_ptr<int>();
@@ -996,7 +1016,8 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     launch_combine(ca, num_sms, stream);
     prof_mark(stream, 5);
     EP_CUDA_CHECK(cudaGetLastError());
-    auto event = scope.finish(async, {x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, out, out_w});
+    auto event = scope.finish(async, {x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, out, out_w,
+                                      row_map, row_weights});
     return {out, out_w, event};
 }
 

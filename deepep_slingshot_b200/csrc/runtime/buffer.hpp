@@ -121,7 +121,8 @@ class Buffer {
         const torch::Tensor& x, const std::optional<torch::Tensor>& topk_weights, const std::optional<torch::Tensor>& bias_0,
         const std::optional<torch::Tensor>& bias_1, const torch::Tensor& rank_prefix_matrix,
         const torch::Tensor& send_prefix_matrix, const torch::Tensor& send_head, const torch::Tensor& recv_src_idx, int num_sms,
-        std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream);
+        std::optional<EventHandle>& previous_event, bool async, bool allocate_on_comm_stream,
+        const std::optional<torch::Tensor>& row_map, const std::optional<torch::Tensor>& row_weights);
 
     void barrier(bool use_comm_stream, bool with_cpu_sync);
 

@@ -3,7 +3,8 @@
 Forward per rank (every step on hand-written sm_100a kernels):
   dispatch (FP8 1x128 quantization fused) -> permute (expert-grouped, 128-aligned) ->
   grouped FP8 GEMM gate/up (tcgen05, 1x128 x 128x128 block scales) -> fused SwiGLU + FP8 requant ->
-  grouped FP8 GEMM down -> top-k weighted unpermute -> combine (sum over ranks).
+  grouped FP8 GEMM down -> combine with the top-k weighted reduction of each token's grouped rows
+  fused into its sender side (one kernel: weighted fp32 sum, bf16 cast, NVLink push, sum over ranks).
 Backward: combine^T = cached dispatch of the output gradient; dispatch^T = combine; the expert
 GEMM gradients run in bf16 (straight-through through the FP8 quantization) as grouped GEMMs over the
 aligned expert groups: torch's grouped bf16 GEMM by default (a library stand-in), this library's
@@ -21,7 +22,7 @@ from typing import Optional
 import torch
 
 from ..ops.gemm import grouped_gemm_fp8, quantize_weights_fp8
-from ..ops.permute import permute, unpermute
+from ..ops.permute import permute
 from .._ext import require_ext
 
 
@@ -123,8 +124,8 @@ class _MoEFunction(torch.autograd.Function):
         a, aq, as_ = require_ext().swiglu_quant(h, False)
         w2q, w2s = quantize_weights_fp8(w2.detach())
         y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts)
-        y_tok = unpermute(y, p.row_map, rw)
-        out, _, _ = buffer.combine(y_tok, handle, config=config)
+        # Top-k weighted reduction of the grouped rows, bf16 cast and exchange in one kernel.
+        out, _, _ = buffer.combine(y, handle, config=config, row_map=p.row_map, row_weights=rw)
         ctx.buffer, ctx.config, ctx.inter = buffer, config, inter
         ctx.handle = handle
         ctx.save_for_backward(p.x, p.scales, p.row_map, p.expert_offsets, p.expert_counts, rw, h, a, y, w1, w2)
@@ -166,9 +167,8 @@ class _MoEFunction(torch.autograd.Function):
         else:
             g_w1, g_w2 = ctx.g_w1, ctx.g_w2
             del ctx.g_w1, ctx.g_w2
-        # permute^T: sum the k copies of each received token; dispatch^T = combine (sum over ranks)
-        g_recv = unpermute(g_xp, row_map, None)
-        g_x, g_topk_w, _ = buffer.combine(g_recv, ctx.handle, topk_weights=g_rw, config=config)
+        # permute^T (sum the k copies of each received token) fused with dispatch^T = combine (sum over ranks)
+        g_x, g_topk_w, _ = buffer.combine(g_xp, ctx.handle, topk_weights=g_rw, config=config, row_map=row_map)
         return g_x, None, g_topk_w, g_w1, g_w2, None, None, None
 
 

@@ -324,15 +324,26 @@ class Buffer:
     def combine(self, x: torch.Tensor, handle: Tuple, topk_weights: Optional[torch.Tensor] = None,
                 bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None,
                 config: Optional[Config] = None, previous_event: Optional[EventOverlap] = None,
-                async_finish: bool = False, allocate_on_comm_stream: bool = False):
+                async_finish: bool = False, allocate_on_comm_stream: bool = False,
+                row_map: Optional[torch.Tensor] = None, row_weights: Optional[torch.Tensor] = None):
         """Sum (without weights) every rank's row of each token back on its source rank (+ bias);
-        also returns the summed top-k weights. Returns `(combined_x, combined_topk_weights, event)`."""
+        also returns the summed top-k weights. Returns `(combined_x, combined_topk_weights, event)`
+        ([DE]deep_ep/buffers/legacy.py:408-455).
+
+        Weighted expanded mode (this library's addition, the MoE layer's combine): with `row_map`
+        (int32 [num_recv, K], the grouped row of each (received token, top-k slot) or -1, as `permute`
+        returns it) `x` is the expert-grouped output with one row per (received token, local expert).
+        Each rank first reduces a token's local rows in fp32 with the factors `row_weights` (fp32
+        [num_recv, K], typically the received top-k weights; None sums them), casts to bf16 and pushes
+        that one row; the source rank then sums the ranks' rows in fp32 (+ bias) and casts to bf16.
+        The top-k weighted reduction, the bf16 casts and the exchange are one kernel; no unpermute pass
+        runs and only one row per (token, rank) crosses NVLink."""
         config = self.get_combine_config(self.group_size) if config is None else config
         rank_prefix_matrix, send_prefix_matrix, _, recv_src_idx, _, send_head = handle
         bias_0, bias_1 = Buffer._unpack_bias(bias)
         recv_x, recv_topk_weights, event = self.runtime.intranode_combine(
             x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, recv_src_idx, config.num_sms,
-            getattr(previous_event, 'event', None), async_finish, allocate_on_comm_stream)
+            getattr(previous_event, 'event', None), async_finish, allocate_on_comm_stream, row_map, row_weights)
         return recv_x, recv_topk_weights, EventOverlap(event)
 
     def internode_dispatch(self, *args, **kwargs):

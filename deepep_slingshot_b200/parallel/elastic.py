@@ -17,7 +17,7 @@ from .._ext import require_ext
 from ..utils.event import EventOverlap
 from ..utils.envs import get_nvlink_gbs
 from ..utils.math import align
-from ..ops.permute import permute, unpermute
+from ..ops.permute import permute
 from .buffer import Buffer, nvtx_range
 
 
@@ -275,8 +275,10 @@ class ElasticBuffer:
                 # of each top-k slot (-1 if not local); psum per expert = aligned start + unpadded count.
                 E_l = num_experts // self.num_ranks
                 ep_handle.recv_topk_idx_local = recv_topk_idx
+                # padding rows are zeroed, so the expanded outputs are fully defined (two calls with the
+                # same inputs return the same bytes, and a grouped GEMM may run over whole groups)
                 perm = permute(recv_x, recv_topk_idx, E_l, alignment=expert_alignment, probs=recv_topk_weights,
-                               x_scales=recv_sf.contiguous() if recv_sf is not None else None)
+                               x_scales=recv_sf.contiguous() if recv_sf is not None else None, zero_padding=True)
                 ep_handle.row_map = perm.row_map
                 ep_handle.expert_offsets = perm.expert_offsets
                 ep_handle.recv_src_metadata = torch.cat([recv_src_metadata, perm.row_map], dim=1)
@@ -300,7 +302,7 @@ class ElasticBuffer:
         """Cached-mode expansion with the handle's grouped layout."""
         E_l = handle.expert_offsets.numel() - 1
         perm = permute(rx, handle.recv_topk_idx_local, E_l, alignment=handle.expert_alignment,
-                       x_scales=rs.contiguous() if rs is not None else None)
+                       x_scales=rs.contiguous() if rs is not None else None, zero_padding=True)
         rows = int(handle.expert_offsets[-1].item())
         return perm.x[:rows], (perm.scales[:rows] if perm.scales is not None else None)
 
@@ -310,16 +312,19 @@ class ElasticBuffer:
                 num_qps: int = 0, previous_event=None, previous_event_before_epilogue=None,
                 async_with_compute_stream: bool = False, allocate_on_comm_stream: bool = False):
         num_sms = handle.num_sms if num_sms == 0 else num_sms
+        row_map = None
         if handle.do_expand:
-            # One row per (token, local expert): sum each token's rows first (weights already applied
-            # by the caller, as in the reference's expanded combine), then combine across ranks.
-            x = unpermute(x.contiguous(), handle.row_map, None)
+            # One row per (token, local expert): the combine kernel sums each token's rows on the
+            # sender before the exchange (weights already applied by the caller, as in the reference's
+            # expanded combine, [DE]deep_ep/include/deep_ep/impls/combine.cuh), then across ranks.
+            x = x.contiguous()
+            row_map = handle.row_map
             topk_weights = None
         rpm, spm, _, src_idx, _, send_head = handle.legacy_handle
         bias_0, bias_1 = Buffer._unpack_bias(bias)
         combined_x, combined_w, event = self.runtime.intranode_combine(
             x, topk_weights, bias_0, bias_1, rpm, spm, send_head, src_idx, num_sms, _native_event(previous_event),
-            async_with_compute_stream, allocate_on_comm_stream)
+            async_with_compute_stream, allocate_on_comm_stream, row_map, None)
         return combined_x, combined_w, EventOverlap(event)
 
     # ------------------------------------------------------------------ experimental side features

@@ -167,12 +167,24 @@ class ReferenceBuffer:
 
     def combine(self, x: torch.Tensor, handle: tuple, topk_weights: Optional[torch.Tensor] = None,
                 bias: Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor], None] = None, config=None,
-                previous_event=None, async_finish=False, allocate_on_comm_stream=False):
+                previous_event=None, async_finish=False, allocate_on_comm_stream=False,
+                row_map: Optional[torch.Tensor] = None, row_weights: Optional[torch.Tensor] = None):
         R, me = self.group_size, self.rank
         rank_prefix_matrix, _, recv_rank_prefix, recv_src_idx, is_token_in_rank, send_head = handle
         N = send_head.shape[0]
         H = x.shape[1]
         num_recv = int(recv_rank_prefix[-1].item())
+        if row_map is not None:
+            # Expanded mode: fp32 sum of each received token's local rows, weighted by row_weights,
+            # rounded to bf16 before the exchange (the row that crosses the link).
+            rm = row_map[:num_recv].long()
+            wts = row_weights[:num_recv].float() if row_weights is not None else torch.ones(rm.shape, device=x.device)
+            valid = rm >= 0
+            rows_f = x.float()[rm.clamp(min=0)] * (wts * valid).unsqueeze(-1)
+            x = torch.zeros((num_recv, H), dtype=torch.float32, device=x.device)
+            for k in range(rm.shape[1]):  # k order, as the kernel accumulates
+                x += rows_f[:, k]
+            x = x.to(torch.bfloat16)
         x = x[:num_recv]
         K = topk_weights.shape[1] if topk_weights is not None else 0
         counts = (recv_rank_prefix[1:] - recv_rank_prefix[:-1]).tolist()

@@ -5,9 +5,6 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
-# Tests of kernels that have not run on a B200 yet; they move into tests/ after their first GPU run.
-# DEEPEP_B200_RUN_PENDING=1 collects them (python -m pytest tests/pending -m gpu).
-collect_ignore = [] if os.environ.get('DEEPEP_B200_RUN_PENDING') == '1' else ['pending']
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 

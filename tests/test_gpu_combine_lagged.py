@@ -1,8 +1,6 @@
 """GPU test of the combine with lagged arrival announcements (DEEPEP_B200_COMBINE_ANNOUNCE=lagged):
 the normal-mode dispatch/combine tests, run in a child process with the knob set (the runtime reads
 it when a buffer is built).
-
-This file sits in `tests/pending/` (not collected) until the lagged mode has run once on a B200.
 """
 import os
 import subprocess

@@ -1,8 +1,6 @@
 """GPU test of the v2 dispatch in asynchronous mode (`async_with_compute_stream=True`): the wrapper's
 post-processing (source metadata, expert prefix sums, the expanded layout) runs on the comm stream
 after the kernels, the returned event covers it, and every output equals the synchronous call's.
-
-This file sits in `tests/pending/` (not collected) until it has run once on a B200.
 """
 import pytest
 import torch
@@ -26,8 +24,9 @@ def _async_body(rank, world, N, H, E, K):
         torch.cuda.synchronize()
         (ax, as_), ai, aw, ah, ev = buf.dispatch(x, **kw, async_with_compute_stream=True)
         ev.current_stream_wait()
-        assert torch.equal(ax.view(torch.uint8), sx.view(torch.uint8)) and torch.equal(as_, ss)
-        assert torch.equal(ai, si) and torch.equal(aw, sw)
+        assert torch.equal(ax.view(torch.uint8), sx.view(torch.uint8)), ('x', expand)
+        assert torch.equal(as_, ss), ('scales', expand)
+        assert torch.equal(ai, si) and torch.equal(aw, sw), ('ids/weights', expand)
         assert torch.equal(ah.recv_src_metadata, sh.recv_src_metadata)
         assert torch.equal(ah.psum_num_recv_tokens_per_expert, sh.psum_num_recv_tokens_per_expert)
         # cached dispatch through the async handle, asynchronously as well

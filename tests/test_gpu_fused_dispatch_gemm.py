@@ -1,8 +1,6 @@
 """GPU tests of the normal-mode dispatch fused with the gate/up grouped FP8 GEMM
 (`Buffer.dispatch_gemm`), against dispatch -> permute -> grouped_gemm_fp8 on the same inputs, and of
 the MoE layer with the fused forward.
-
-This file sits in `tests/pending/` (not collected) until the fused kernel has run once on a B200.
 """
 import pytest
 import torch

@@ -1,7 +1,5 @@
 """GPU tests of the bf16 tcgen05 grouped GEMMs with MN-major operands (weights and activations read
 as they lie, no transposes), against fp32 torch references.
-
-This file sits in `tests/pending/` (not collected) until the MN-major path has run once on a B200.
 """
 import pytest
 import torch

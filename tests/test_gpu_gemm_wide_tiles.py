@@ -1,8 +1,6 @@
 """GPU test of the FP8 grouped GEMM with 256-wide tiles (DEEPEP_B200_GEMM_BN=256), against the same
 fp32 oracle and the default 128-wide tiles. The tile width is read once per process, so each case
 runs in a child process.
-
-This file sits in `tests/pending/` (not collected) until the 256-wide variant has run once on a B200.
 """
 import os
 import subprocess

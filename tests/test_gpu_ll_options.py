@@ -1,8 +1,6 @@
 """GPU test of the low-latency FP8 dispatch options DeepEP's low-latency test covers and the other
 GPU tests do not: power-of-two scales (`round_scale`), packed UE8M0 scales (`use_ue8m0`), and the
 asynchronous mode without a hook (`async_finish` + the returned event), against `ReferenceBuffer`.
-
-This file sits in `tests/pending/` (not collected) until it has run once on a B200.
 """
 import pytest
 import torch

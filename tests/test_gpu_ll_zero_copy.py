@@ -1,8 +1,6 @@
 """GPU test of the low-latency combine in zero-copy mode: the expert outputs are written into the
 registered send buffer (`get_next_low_latency_combine_buffer`) and combined with `zero_copy=True`;
 the result must equal the copying combine's.
-
-This file sits in `tests/pending/` (not collected) until it has run once on a B200.
 """
 import pytest
 import torch

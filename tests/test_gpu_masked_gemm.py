@@ -1,8 +1,4 @@
-"""GPU tests of the masked grouped FP8 GEMM and of the low-latency dispatch fused with it.
-
-This file sits in `tests/pending/` (not collected) until the kernels have run once on a B200;
-then it moves to `tests/`.
-"""
+"""GPU tests of the masked grouped FP8 GEMM and of the low-latency dispatch fused with it."""
 import pytest
 import torch
 import torch.distributed as dist

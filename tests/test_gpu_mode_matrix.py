@@ -2,9 +2,6 @@
 (tests/elastic/test_ep.py:22-558 of the DeepEP tree): dispatch dtype FP8 / bf16 x expert alignment
 1 / 128 x bias none / one / two x (previous event + async + allocation on the comm stream) on / off
 x a copied handle for the cached dispatch, every case against `ReferenceBuffer`.
-
-This file sits in `tests/pending/` (not collected) until it has run once on a B200 (the two-bias
-combine has no GPU test before it); then it moves to `tests/`.
 """
 import copy
 import itertools

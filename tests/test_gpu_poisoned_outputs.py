@@ -1,8 +1,6 @@
 """Initialisation check without compute-sanitizer: the normal-mode dispatch / combine tests rerun with
 DEEPEP_B200_POISON_OUTPUTS=1, so every output byte starts as 0xFF (NaN for floats, -1 for ids) and a
 row the kernels fail to write breaks the byte-for-byte comparison with the torch oracle.
-
-This file sits in `tests/pending/` (not collected) until it has run once on a B200.
 """
 import os
 import subprocess

@@ -41,6 +41,15 @@ def _body(rank, world):
     expect = x_bf.float() * topk_w.sum(dim=1, keepdim=True)
     assert torch.allclose(out.float(), expect, atol=3e-2, rtol=2e-2), (out.float() - expect).abs().max()
     assert torch.allclose(out_w, topk_w, atol=1e-6)
+    # weighted expanded combine: one row per (received token, local expert), reduced with the
+    # received top-k weights on the sender, gives the same result
+    valid = recv_idx >= 0
+    row_map = torch.full(recv_idx.shape, -1, dtype=torch.int32)
+    row_map[valid] = torch.arange(int(valid.sum()), dtype=torch.int32)
+    y_exp = recv_x[torch.nonzero(valid)[:, 0]]
+    out3, out3_w, _ = buf.combine(y_exp, handle, topk_weights=recv_w, row_map=row_map, row_weights=recv_w)
+    assert torch.allclose(out3.float(), expect, atol=3e-2, rtol=2e-2), (out3.float() - expect).abs().max()
+    assert torch.allclose(out3_w, topk_w, atol=1e-6)
     # low-latency reference: weighted combine of identity experts gives x * sum(w) as well
     recv, cnt, h, _, hook = buf.low_latency_dispatch(x_bf, topk_idx, 64, E, use_fp8=False, return_recv_hook=True)
     hook()
