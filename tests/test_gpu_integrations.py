@@ -31,11 +31,11 @@ def _adapter_body(rank, world):
         eo, _, _ = ref.combine(y, eh)
         torch.cuda.synchronize()
         assert torch.allclose(out.float(), eo.float(), atol=1e-2, rtol=1e-2)
-    assert layers[0]._elastic is layers[1]._elastic
+    assert layers[0].buffer is layers[1].buffer
     layers[0].close()
-    assert len(DeepEPB200Normal._buffers) == 1
+    assert len(DeepEPB200Normal.pool) == 1
     layers[1].close()
-    assert len(DeepEPB200Normal._buffers) == 0
+    assert len(DeepEPB200Normal.pool) == 0
 
 
 @pytest.mark.parametrize('world', _worlds())

@@ -125,24 +125,12 @@ def test_functional_refs_gloo():
 
 def test_small_helpers():
     from deepep_slingshot_b200.utils.math import create_grouped_scores, hash_tensors
-    from deepep_slingshot_b200.utils.semantic import value_or, weak_lru
     from deepep_slingshot_b200.utils.testing import empty_suppress, suppress_stdout_stderr
     s = torch.arange(16, dtype=torch.float32).view(2, 8) + 1
     gs = create_grouped_scores(s, torch.tensor([[0], [3]]), 4)
     assert gs[0, :2].tolist() == [1.0, 2.0] and gs[0, 2:].abs().sum() == 0 and gs[1, 6:].tolist() == [15.0, 16.0]
     a, b = torch.arange(4, dtype=torch.int32), torch.ones(3, dtype=torch.int32)
     assert hash_tensors(a, [b, None]) == (int(a.sum()) ^ int(b.sum()))
-    assert value_or(None, 3) == 3 and value_or(0, 3) == 0
-
-    class C:
-        calls = 0
-
-        @weak_lru(maxsize=4)
-        def f(self, v):
-            C.calls += 1
-            return v * 2
-    c = C()
-    assert c.f(2) == 4 and c.f(2) == 4 and C.calls == 1
     with suppress_stdout_stderr():
         print('hidden')
     with empty_suppress():

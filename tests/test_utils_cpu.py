@@ -44,8 +44,30 @@ def test_event_overlap_without_event():
         pass
     with ev(release_handle=True):
         pass
-    with pytest.raises(AssertionError):
+    with pytest.raises(RuntimeError):
         ev.current_stream_wait()
+
+
+class _CountingEvent:
+    def __init__(self):
+        self.waits = 0
+
+    def current_stream_wait(self):
+        self.waits += 1
+
+
+def test_event_overlap_joins_and_releases():
+    native = _CountingEvent()
+    ev = EventOverlap(native)
+    with ev as inner:
+        assert inner is ev
+    assert native.waits == 1 and ev.event is native
+    with ev(release_handle=True) as inner:
+        assert inner is ev
+    assert native.waits == 2 and ev.event is None
+    with ev:  # nothing left to join
+        pass
+    assert native.waits == 2
 
 
 def _refs_body(rank, world):
