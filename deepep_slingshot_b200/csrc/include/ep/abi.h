@@ -11,14 +11,16 @@ namespace ep {
 constexpr int kMaxRanks = 8;        // one NVLink/NVSwitch domain (one B200 box)
 constexpr int kMaxTopk = 16;
 constexpr int kMaxLocalExperts = 1024;
-constexpr int kAbiVersion = 1;
+constexpr int kMaxCountCtas = 128;     // CTAs of the dispatch count kernel (per-CTA counts live in the control block)
+constexpr int kMaxStageChunks = 256;   // staged-chunk flags per source rank (chunk size >= capacity / 256)
+constexpr int kAbiVersion = 2;
 
 // ------------------------------------------------------------------------------------------------
 // Error codes written into the host-mapped `ErrorState` by kernels whose bounded waits expire.
 // ------------------------------------------------------------------------------------------------
 enum ErrorCode : int {
     kOk = 0,
-    kErrTimeoutNotify = 1,         // dispatch notify: counts/list of a peer never arrived
+    kErrTimeoutNotify = 1,         // dispatch count step: a peer's counts (or a count CTA's prefix) never arrived
     kErrTimeoutPullDone = 2,       // staging reuse: a receiver never finished pulling the last dispatch
     kErrTimeoutCombineReady = 3,   // combine: destination never finished its previous combine
     kErrTimeoutCombineArrive = 4,  // combine: contributions never all arrived
@@ -26,6 +28,7 @@ enum ErrorCode : int {
     kErrTimeoutLLDispatch = 6,
     kErrTimeoutLLCombine = 7,
     kErrTimeoutTma = 8,            // a TMA bulk copy never completed
+    kErrTimeoutStaged = 9,         // dispatch pull: a source never staged the chunk holding a wanted token
     kErrCapacity = 10,             // receive capacity exceeded (tokens beyond the buffer)
     kErrBounds = 11,               // an index outside its window (bounds check on every peer store)
     kErrBadArgs = 12,
@@ -49,10 +52,10 @@ static_assert(sizeof(ErrorState) == 32, "ErrorState ABI");
 // appended with one atomic; a full ring drops records and the host sees `cursor > capacity`.
 // ------------------------------------------------------------------------------------------------
 enum TraceEvent : int {
-    kTraceStage = 100,          // dispatch stage block (quantize + records), a = tokens
-    kTraceStageWait = 101,      // stage: wait for receivers of the previous dispatch
-    kTraceNotify = 102,         // notify kernel, a = 1 in cached mode
-    kTraceNotifyWait = 103,     // notify: count exchange wait, a = epoch
+    kTraceStage = 100,          // dispatch stage (quantize + records; stage warps or stage block), a = tokens
+    kTraceWaitReceivers = 101,  // dispatch: wait for the receivers of the previous dispatch
+    kTraceCount = 102,          // dispatch count kernel (lists + count exchange), a = 1 in cached mode
+    kTraceCountExchange = 103,  // count kernel: count exchange wait, a = epoch
     kTracePull = 104,           // pull block, a = received tokens
     kTraceCombine = 110,        // combine block (push + reduce), a = 1 for push blocks
     kTraceCombinePush = 111,    // combine push warp finished its rows, a = warp
@@ -123,6 +126,17 @@ struct alignas(128) NormalCtrl {
     int pad0[25];
     int token_counts[2][kMaxRanks][kMaxRanks];  // [parity][src][dst] tokens src sends to dst
     int expert_counts[2][kMaxRanks][kMaxLocalExperts];  // [parity][src][local expert] tokens from src
+    // Overlapped stage: the source's stage warps release staged[src][chunk] = dispatch epoch in every
+    // receiver's block once all tokens of that chunk are in its staging; pull producers wait on it.
+    int staged[kMaxRanks][kMaxStageChunks];
+    int stage_chunk_done[kMaxStageChunks];      // local: tokens of each chunk staged so far (reset by count)
+    // Count kernel (local): per-CTA per-destination token counts, published with the epoch in
+    // count_cta_flag so that later CTAs add up their predecessors' counts (ordered lists).
+    int count_cta_flag[kMaxCountCtas];
+    int count_cta_counts[kMaxCountCtas][kMaxRanks];
+    int count_done_ctas;                        // local ticket; the last CTA exchanges counts (and resets it)
+    int selftest_flag;                          // transport self-test: peers add to it, the owner waits
+    int pad1[30];
 };
 static_assert(sizeof(NormalCtrl) % 128 == 0, "NormalCtrl alignment");
 
@@ -146,7 +160,7 @@ struct NormalLayout {
     int64_t staging_off;     // records [capacity], record_bytes each
     int64_t combine_off;     // bf16 rows [capacity * num_ranks][hidden]
     int64_t combine_w_off;   // f32 [capacity * num_ranks][topk_pad]
-    int64_t scratch_off;     // local only: uint8 rank mask per token [capacity], then int expert counters
+    int64_t scratch_off;     // local only: [capacity] spare bytes, then int32 per-expert token counters [kMaxExperts] (zero between calls)
     int64_t arrival_off;     // int32 [capacity]: combine contributions landed per token (peers add, reducer resets)
     int64_t total_bytes;
     int32_t capacity;        // max tokens per rank per call

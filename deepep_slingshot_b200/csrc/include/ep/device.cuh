@@ -23,6 +23,15 @@
 namespace ep {
 
 // ------------------------------------------------------------------------------------------------
+// Window rule of every indexed peer access: the range [index, index + count) must lie inside
+// [0, window). Written without forming index + count, so huge or negative values cannot wrap.
+// Kernels report kErrBounds and skip the access when it fails (the address is never formed).
+// ------------------------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ bool in_window(int64_t index, int64_t count, int64_t window) {
+    return index >= 0 && count >= 0 && window >= 0 && count <= window && index <= window - count;
+}
+
+// ------------------------------------------------------------------------------------------------
 // Scalar memory-model helpers
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
@@ -62,6 +71,11 @@ __device__ __forceinline__ void red_add_release_sys(int* p, int v) {
 __device__ __forceinline__ int atom_add_relaxed_sys(int* p, int v) {
     int old;
     asm volatile("atom.relaxed.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ int atom_add_acq_rel_sys(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {

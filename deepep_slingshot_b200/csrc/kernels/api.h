@@ -23,34 +23,37 @@ struct StageArgs {
     const int64_t* topk_idx;     // [N][K] or null
     const float* topk_weights;   // [N][K] or null
     uint8_t* staging;            // local staging base (region base + staging_off)
-    const int* pull_done;        // local ctrl.pull_done
     int num_tokens, hidden, num_topk, topk_pad;
     int in_elem_bytes;           // 2 = bf16 input, 1 = fp8 input
     int quantize;                // 1: fuse bf16 -> fp8 e4m3 1x128 quantization
     int round_scale;             // 1: power-of-two scales
     int tma_rows;                // 1 (set by the launcher): rows are TMA-loaded into shared memory before quantizing
+    int chunk;                   // overlapped stage: tokens per staged-chunk flag (same on every rank)
+    // Standalone stage only: wait until every receiver pulled the previous dispatch (pull_done[r] >=
+    // *dispatch_epoch, read before the count step advances it).
+    const int* pull_done;
+    const int* dispatch_epoch;
     int num_ranks;
-    const int* dispatch_epoch;   // local ctrl.dispatch_epoch: wait until pull_done[r] >= it
-    const bool* is_token_in_rank;  // [N][R] or null
-    uint8_t* token_mask;         // scratch [N]: destination-rank bit mask per token (null: skip)
-    int* expert_counts;          // scratch [E]: tokens per expert (atomics; zeroed by notify after use)
-    int num_experts, num_local_experts;
     RecordFormat rec;
     int record_stride;
     KernelStatus st;
 };
+// Standalone stage (the fused dispatch + GEMM path runs it before the count exchange).
 void launch_dispatch_stage(const StageArgs& a, int num_sms, cudaStream_t stream);
 
-struct NotifyArgs {
+// Dispatch count step (multi-CTA): waits until every receiver has finished pulling the previous
+// dispatch, builds the ordered per-destination token lists and send_head from the routing alone
+// (each CTA adds up the per-destination counts of the CTAs before it), counts tokens per expert,
+// then its last CTA exchanges the counts with every peer and computes the receive layout.
+struct CountArgs {
     const int64_t* topk_idx;         // [N][K] or null
     const bool* is_token_in_rank;    // [N][R] or null (then derived from topk_idx)
     int num_tokens, num_topk, num_experts, num_local_experts;
     int num_ranks, rank;
-    int cached;                      // 1: only publish readiness and wait (handle reuse)
-    int host_ticket;                 // written to host->ready_ticket when the counts are valid
-    const uint8_t* token_mask;       // per-token destination masks computed by the stage kernel
-    int* expert_counts;              // per-expert token counts computed by the stage kernel
+    int cached;                      // 1: only wait for the previous pulls, reset, and exchange readiness
+    int tokens_per_cta;              // multiple of the block size; grid = ceil(N / tokens_per_cta) <= kMaxCountCtas
     int expert_alignment;
+    int stage_chunks;                // staged-chunk counters to reset for this dispatch's stage
     PeerTable peers;
     NormalLayout layout;
     int* send_head;                  // [N][R]
@@ -60,10 +63,10 @@ struct NotifyArgs {
     int* num_recv_per_expert;        // [E_l] aligned counts (device)
     int* dev_num_recv;               // [1]
     int* cumulative_stats;           // [E_l] optional
-    HostCounters* host;              // host-mapped
+    int* expert_counts;              // scratch [E]: zero at entry, zero again at exit
     KernelStatus st;
 };
-void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream);
+void launch_dispatch_count(const CountArgs& a, cudaStream_t stream);
 
 struct PullArgs {
     PeerTable peers;
@@ -88,6 +91,10 @@ struct PullArgs {
     const int* num_recv_per_expert;  // [E_l] aligned counts computed by notify
     int host_ticket;
     int chunk;                       // rows dealt to pipeline pairs in chunks of this size (0: contiguous)
+    // Overlapped stage: with stage_warps > 0 the same launch also stages this rank's tokens (stage
+    // warps next to the pull pairs) and the pull waits per (source, chunk) for the staged flags.
+    int stage_warps;
+    StageArgs stage;
     KernelStatus st;
 };
 void launch_dispatch_pull(const PullArgs& a, int num_sms, cudaStream_t stream);
@@ -124,6 +131,15 @@ struct CombineArgs {
     KernelStatus st;
 };
 void launch_combine(const CombineArgs& a, int num_sms, cudaStream_t stream);
+
+// ---------------------------------------------------------------- transport-contract checks
+// Multi-producer signalling: producer_blocks x warps warps each add 1 to *peer_flag `rounds` times
+// (sys-scope release reductions); one more block waits (bounded) until *my_flag == expected and
+// writes status[0] (0 exact, 1 overshoot, 2 wait expired) and status[1] (the value seen).
+void launch_signal_stress(int* peer_flag, int* my_flag, int producer_blocks, int warps, int rounds, int expected,
+                          int* status, KernelStatus st, cudaStream_t stream);
+// The window rule of indexed peer accesses on a table of (index, count, window): kOk or kErrBounds.
+void launch_window_check(const int64_t* cases, int n, int* codes, cudaStream_t stream);
 
 // ---------------------------------------------------------------- barrier
 void launch_barrier(PeerTable peers, int64_t ctrl_off, int rank, int num_ranks, KernelStatus st, cudaStream_t stream);

@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) masked_gemm_fp8_kernel(const __gr
                     const int meta = reinterpret_cast<const int*>(dsp + L.recv_src_meta_off)[idx];
                     const int tok = reinterpret_cast<const int*>(dsp + L.recv_src_info_off)[idx];
                     const int src = meta / L.num_topk, k = meta % L.num_topk;
-                    if (src < 0 || src >= L.num_ranks || tok < 0 || tok >= L.max_tokens) {
+                    if (!in_window(src, 1, L.num_ranks) || !in_window(tok, 1, L.max_tokens)) {
                         report_error(a.st, kErrBounds, src, tok);
                         continue;
                     }

@@ -4,18 +4,23 @@
 // [DE]csrc/kernels/legacy/intranode.cu:25-1117, v2 [DE]deep_ep/include/deep_ep/impls/dispatch.cuh,
 // combine.cuh, combine_reduce_epilogue.cuh), re-designed for B200:
 //
-//  dispatch = stage -> notify -> pull
-//    * stage  (many CTAs): each source rank writes one 16-byte-aligned RECORD per token into its own
-//               staging area: the row (bf16, or FP8 e4m3 with the 1x128 quantization fused here),
-//               its fp32 block scales and its top-k ids/weights. Local HBM traffic only.
-//    * notify (one CTA): builds the per-destination token lists and `send_head`, pushes the count
-//               row and the per-expert counts into every peer's control block, releases a flag, waits
-//               for every peer's flag and computes the receive layout (prefix matrices, aligned
-//               per-expert counts) into device memory.
-//    * pull   (num_sms CTAs): every receiver pulls the records it needs straight out of the
-//               sources' staging with TMA bulk loads over NVLink (no multicast) into a shared-memory
-//               ring and TMA-stores them into its own output tensors. There is no receive ring and
-//               no copy epilogue: the output tensors are written once. The last block publishes the
+//  dispatch = count -> (stage || pull), two launches
+//    * count  (up to 128 CTAs): waits until every receiver finished pulling the previous dispatch,
+//               then builds the ordered per-destination token lists and `send_head` from the routing
+//               alone (each CTA adds the per-destination counts its predecessors published) and the
+//               per-expert counts; its last CTA pushes the count row and the per-expert counts into
+//               every peer's control block, releases a flag, waits for every peer's flag and
+//               computes the receive layout (prefix matrices, aligned per-expert counts).
+//    * stage  (stage warps of the pull launch): each source writes one 16-byte-aligned RECORD per
+//               token into its own staging area (the row: bf16, or FP8 e4m3 with the 1x128
+//               quantization fused here; its fp32 block scales; its top-k ids/weights), in token
+//               order, and releases a staged flag per chunk of tokens in every receiver's control
+//               block. The quantization is thereby off the critical path: it overlaps the pulls.
+//    * pull   (pull pairs of the same launch): every receiver pulls the records it needs straight
+//               out of the sources' staging with TMA bulk loads over NVLink (no multicast) into a
+//               shared-memory ring, after a bounded wait on the (source, chunk) staged flag, and
+//               TMA-stores them into its own output tensors. There is no receive ring and no copy
+//               epilogue: the output tensors are written once. The last block publishes the
 //               received counts to host-mapped memory (the CPU sync) and releases the sources' staging.
 //  combine = one kernel, push and reduce overlapped
 //    * push warps TMA-store this rank's expert-output rows into the source ranks' combine slots
@@ -96,6 +101,45 @@ void launch_dispatch_layout(const int64_t* topk_idx, int num_tokens, int num_top
 // =================================================================================================
 // stage: one record per token into the local staging area, FP8 quantization fused.
 // =================================================================================================
+// Top-k ids and weights of token t into its record (lanes < topk_pad).
+__device__ __forceinline__ void stage_record_meta(const StageArgs& a, int t, uint8_t* rec) {
+    const int lane = lane_id();
+    int idx = -1;
+    float w = 0.f;
+    if (lane < a.num_topk) {
+        if (a.topk_idx != nullptr) idx = (int)a.topk_idx[(int64_t)t * a.num_topk + lane];
+        if (a.topk_weights != nullptr) w = a.topk_weights[(int64_t)t * a.num_topk + lane];
+    }
+    if (lane < a.topk_pad) {
+        reinterpret_cast<int*>(rec + a.rec.idx_off)[lane] = idx;
+        reinterpret_cast<float*>(rec + a.rec.w_off)[lane] = w;
+    }
+}
+
+// Whole record of token t through registers (one warp): quantized, copied bf16 or pre-quantized FP8
+// row, its scales and the top-k metadata.
+__device__ __forceinline__ void stage_token_regs(const StageArgs& a, int t) {
+    const int lane = lane_id();
+    uint8_t* rec = a.staging + (int64_t)t * a.record_stride;
+    if (a.quantize) {
+        quantize_row_to_fp8(static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * a.hidden, rec,
+                            reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
+    } else {
+        const int x_bytes = a.hidden * a.in_elem_bytes;
+        const uint8_t* src = static_cast<const uint8_t*>(a.x) + (int64_t)t * x_bytes;
+        for (int o = lane * 16; o < x_bytes; o += 512)
+            *reinterpret_cast<int4*>(rec + o) = ld_nc_v4(reinterpret_cast<const int4*>(src + o));
+        if (a.x_scales != nullptr) {
+            float* dst = reinterpret_cast<float*>(rec + a.rec.scale_off);
+            const int nb = a.hidden / 128;
+            for (int b = lane; b < nb; b += 32) dst[b] = a.x_scales[t * a.scale_stride_t + b * a.scale_stride_b];
+        }
+    }
+    stage_record_meta(a, t, rec);
+}
+
+// Standalone stage kernel (before the count exchange, whose barrier then orders every peer's pull
+// after this rank's staging).
 __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
     // With tma_rows each warp owns one row buffer of dynamic shared memory: a single bulk copy brings
     // the whole bf16 row in (no registers held for loads in flight), the warp quantizes from there.
@@ -106,13 +150,13 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
         mbar_init(&s_bar[warp_id()], 1);
         fence_mbar_init();
     }
-    if ((int)threadIdx.x < a.num_ranks) {
+    if ((int)threadIdx.x < a.num_ranks && a.pull_done != nullptr) {
         // Receivers must have finished pulling the previous dispatch before the staging is rewritten.
         const int prev_epoch = ld_volatile(a.dispatch_epoch);
         if (prev_epoch > 0) wait_ge(&a.pull_done[threadIdx.x], prev_epoch, a.st, kErrTimeoutPullDone, threadIdx.x);
     }
     __syncthreads();
-    if (threadIdx.x == 0) trace_end(a.st, kTraceStageWait, t_start, a.num_tokens);
+    if (threadIdx.x == 0) trace_end(a.st, kTraceWaitReceivers, t_start, a.num_tokens);
     if (aborted(a.st)) return;
 
     const int lane = lane_id();
@@ -120,59 +164,27 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
     const int total_warps = gridDim.x * warps;
     uint32_t phase = 0;
     for (int t = blockIdx.x * warps + warp_id(); t < a.num_tokens; t += total_warps) {
+        if (!(a.quantize && a.tma_rows)) {
+            stage_token_regs(a, t);
+            continue;
+        }
         uint8_t* rec = a.staging + (int64_t)t * a.record_stride;
-        if (a.quantize && a.tma_rows) {
-            const uint32_t row_bytes = (uint32_t)a.hidden * 2;
-            uint8_t* buf = s_rows + (size_t)warp_id() * row_bytes;
-            if (lane == 0) {
-                fence_proxy_async_smem();  // the previous row's generic reads precede this async write
-                mbar_arrive_expect_tx(&s_bar[warp_id()], row_bytes);
-                tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + (int64_t)t * row_bytes, row_bytes, &s_bar[warp_id()]);
-            }
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma) ? 1 : 0)) {
-                if (lane == 0) mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma);  // the row lands before exit
-                break;
-            }
-            phase ^= 1u;
-            quantize_row_to_fp8<true>(reinterpret_cast<const __nv_bfloat16*>(buf), rec,
-                                      reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
-            __syncwarp();
-        } else if (a.quantize) {
-            quantize_row_to_fp8(static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * a.hidden, rec,
-                                reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
-        } else {
-            const int x_bytes = a.hidden * a.in_elem_bytes;
-            const uint8_t* src = static_cast<const uint8_t*>(a.x) + (int64_t)t * x_bytes;
-            for (int o = lane * 16; o < x_bytes; o += 512)
-                *reinterpret_cast<int4*>(rec + o) = ld_nc_v4(reinterpret_cast<const int4*>(src + o));
-            if (a.x_scales != nullptr) {
-                float* dst = reinterpret_cast<float*>(rec + a.rec.scale_off);
-                const int nb = a.hidden / 128;
-                for (int b = lane; b < nb; b += 32) dst[b] = a.x_scales[t * a.scale_stride_t + b * a.scale_stride_b];
-            }
+        const uint32_t row_bytes = (uint32_t)a.hidden * 2;
+        uint8_t* buf = s_rows + (size_t)warp_id() * row_bytes;
+        if (lane == 0) {
+            fence_proxy_async_smem();  // the previous row's generic reads precede this async write
+            mbar_arrive_expect_tx(&s_bar[warp_id()], row_bytes);
+            tma_load_1d(buf, static_cast<const uint8_t*>(a.x) + (int64_t)t * row_bytes, row_bytes, &s_bar[warp_id()]);
         }
-        int idx = -1;
-        float w = 0.f;
-        if (lane < a.num_topk) {
-            if (a.topk_idx != nullptr) idx = (int)a.topk_idx[(int64_t)t * a.num_topk + lane];
-            if (a.topk_weights != nullptr) w = a.topk_weights[(int64_t)t * a.num_topk + lane];
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma) ? 1 : 0)) {
+            if (lane == 0) mbar_wait(&s_bar[warp_id()], phase, a.st, kErrTimeoutTma);  // the row lands before exit
+            break;
         }
-        if (lane < a.topk_pad) {
-            reinterpret_cast<int*>(rec + a.rec.idx_off)[lane] = idx;
-            reinterpret_cast<float*>(rec + a.rec.w_off)[lane] = w;
-        }
-        // Per-token destination-rank mask and per-expert counts for the notify step.
-        if (a.token_mask != nullptr) {
-            uint32_t bit = 0;
-            if (a.is_token_in_rank != nullptr) {
-                if (lane < a.num_ranks && a.is_token_in_rank[(int64_t)t * a.num_ranks + lane]) bit = 1u << lane;
-            } else if (idx >= 0 && idx < a.num_experts) {
-                bit = 1u << (idx / a.num_local_experts);
-            }
-            const uint32_t m = __reduce_or_sync(0xffffffffu, bit);
-            if (lane == 0) a.token_mask[t] = (uint8_t)m;
-            if (idx >= 0 && idx < a.num_experts) atomicAdd(&a.expert_counts[idx], 1);
-        }
+        phase ^= 1u;
+        quantize_row_to_fp8<true>(reinterpret_cast<const __nv_bfloat16*>(buf), rec,
+                                  reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
+        __syncwarp();
+        stage_record_meta(a, t, rec);
     }
     if (a.st.trace != nullptr) {
         __syncthreads();
@@ -201,9 +213,11 @@ void launch_dispatch_stage(const StageArgs& a_in, int num_sms, cudaStream_t stre
 }
 
 // =================================================================================================
-// notify: lists + send_head + count exchange + receive layout. One CTA of 1024 threads.
+// count: ordered per-destination lists + send_head + per-expert counts (all CTAs), then the count
+// exchange and the receive layout (last CTA). Only the routing is read, so this step does not wait
+// for the quantization; the staging itself overlaps the pulls (stage warps of the pull launch).
 // =================================================================================================
-__device__ __forceinline__ uint32_t token_rank_mask(const NotifyArgs& a, int t) {
+__device__ __forceinline__ uint32_t token_rank_mask(const CountArgs& a, int t) {
     uint32_t m = 0;
     if (a.is_token_in_rank != nullptr) {
         for (int r = 0; r < a.num_ranks; ++r) m |= (a.is_token_in_rank[(int64_t)t * a.num_ranks + r] ? 1u : 0u) << r;
@@ -216,106 +230,153 @@ __device__ __forceinline__ uint32_t token_rank_mask(const NotifyArgs& a, int t) 
     return m;
 }
 
-// Block-wide exclusive scan of eight 16-bit counters packed in two 64-bit words (one scan for all
-// destination ranks; per-rank totals < 65536 by construction: capacity checks bound the tokens).
-__device__ void block_exclusive_scan_u64x2(uint64_t& lo, uint64_t& hi, uint64_t* total_lo, uint64_t* total_hi,
-                                           uint64_t* ws /* 2*33 */) {
+// Block-wide exclusive scan of per-destination counts, two 32-bit counters per 64-bit word
+// (destination 2w in the low half of word w, 2w + 1 in the high half): one scan for all
+// destinations; each CTA counts at most tokens_per_cta < 2^31 tokens.
+constexpr int kCountWords = kMaxRanks / 2;
+__device__ void block_exclusive_scan_counts(uint64_t (&v)[kCountWords], uint64_t (&total)[kCountWords],
+                                            uint64_t* ws /* kCountWords * 33 */) {
     const int lane = lane_id(), warp = warp_id(), nwarps = (blockDim.x + 31) / 32;
-    uint64_t ilo = lo, ihi = hi;
+    uint64_t incl[kCountWords];
+#pragma unroll
+    for (int w = 0; w < kCountWords; ++w) incl[w] = v[w];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const uint64_t nlo = __shfl_up_sync(0xffffffffu, ilo, o), nhi = __shfl_up_sync(0xffffffffu, ihi, o);
-        if (lane >= o) {
-            ilo += nlo;
-            ihi += nhi;
+#pragma unroll
+        for (int w = 0; w < kCountWords; ++w) {
+            const uint64_t n = __shfl_up_sync(0xffffffffu, incl[w], o);
+            if (lane >= o) incl[w] += n;
         }
     }
-    if (lane == 31) {
-        ws[warp] = ilo;
-        ws[33 + warp] = ihi;
-    }
+    if (lane == 31)
+#pragma unroll
+        for (int w = 0; w < kCountWords; ++w) ws[w * 33 + warp] = incl[w];
     __syncthreads();
     if (warp == 0) {
-        uint64_t wlo = lane < nwarps ? ws[lane] : 0, whi = lane < nwarps ? ws[33 + lane] : 0;
-        uint64_t slo = wlo, shi = whi;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint64_t nlo = __shfl_up_sync(0xffffffffu, slo, o), nhi = __shfl_up_sync(0xffffffffu, shi, o);
-            if (lane >= o) {
-                slo += nlo;
-                shi += nhi;
+        for (int w = 0; w < kCountWords; ++w) {
+            const uint64_t own = lane < nwarps ? ws[w * 33 + lane] : 0;
+            uint64_t sc = own;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t n = __shfl_up_sync(0xffffffffu, sc, o);
+                if (lane >= o) sc += n;
             }
-        }
-        if (lane < nwarps) {
-            ws[lane] = slo - wlo;
-            ws[33 + lane] = shi - whi;
-        }
-        if (lane == nwarps - 1) {
-            ws[32] = slo;
-            ws[65] = shi;
+            if (lane < nwarps) ws[w * 33 + lane] = sc - own;
+            if (lane == nwarps - 1) ws[w * 33 + 32] = sc;
         }
     }
     __syncthreads();
-    lo = ws[warp] + ilo - lo;
-    hi = ws[33 + warp] + ihi - hi;
-    *total_lo = ws[32];
-    *total_hi = ws[65];
+#pragma unroll
+    for (int w = 0; w < kCountWords; ++w) {
+        v[w] = ws[w * 33 + warp] + incl[w] - v[w];
+        total[w] = ws[w * 33 + 32];
+    }
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
-    extern __shared__ __align__(16) int s_dyn[];  // [num_experts] counters, then [num_tokens] uint8 masks
-    __shared__ uint64_t s_ws[66];
+__device__ __forceinline__ int count_of(const uint64_t (&v)[kCountWords], int r) {
+    return (int)((v[r >> 1] >> (32 * (r & 1))) & 0xffffffffu);
+}
+
+constexpr int kCountThreads = 256;
+
+__global__ void __launch_bounds__(kCountThreads) dispatch_count_kernel(CountArgs a) {
+    extern __shared__ __align__(16) int s_ecnt[];  // [num_experts] per-CTA expert counts (fresh mode)
+    __shared__ uint64_t s_ws[kCountWords * 33];
+    __shared__ int s_base[kMaxRanks];
     __shared__ int s_total[kMaxRanks];
     __shared__ int s_tc[kMaxRanks][kMaxRanks];
-    __shared__ int s_epoch;
-    int* s_ecnt = s_dyn;
-    uint8_t* s_mask = reinterpret_cast<uint8_t*>(s_dyn + a.num_experts);
+    __shared__ int s_epoch, s_last;
     const int tid = threadIdx.x, nt = blockDim.x;
     const int R = a.num_ranks;
     NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
     const uint64_t t_start = trace_begin(a.st);
     if (tid == 0) s_epoch = ld_volatile(&my_ctrl->dispatch_epoch) + 1;
+    if (tid < kMaxRanks) s_base[tid] = 0;
     __syncthreads();
     const int epoch = s_epoch, parity = epoch & 1;
+    // Every receiver must have finished pulling the previous dispatch (it reads my lists and my
+    // staging) before this dispatch rewrites them.
+    if (tid < R && epoch > 1) wait_ge(&my_ctrl->pull_done[tid], epoch - 1, a.st, kErrTimeoutPullDone, tid);
+    __syncthreads();
+    if (blockIdx.x == 0 && tid == 0) trace_end(a.st, kTraceWaitReceivers, t_start, a.num_tokens);
+    if (aborted(a.st)) return;
 
     if (!a.cached) {
-        for (int i = tid; i < a.num_experts; i += nt) {
-            s_ecnt[i] = a.expert_counts[i];
-            a.expert_counts[i] = 0;  // ready for the next dispatch
-        }
-        const int chunk = (a.num_tokens + nt - 1) / nt;
-        const int t0 = min(a.num_tokens, tid * chunk), t1 = min(a.num_tokens, t0 + chunk);
-        uint64_t lo = 0, hi = 0;
+        const int per_thread = a.tokens_per_cta / nt;
+        const int t0 = blockIdx.x * a.tokens_per_cta + tid * per_thread;
+        const int t1 = min(a.num_tokens, t0 + per_thread);
+        for (int i = tid; i < a.num_experts; i += nt) s_ecnt[i] = 0;
+        __syncthreads();
+        uint64_t cnt[kCountWords] = {};
         for (int t = t0; t < t1; ++t) {
-            const uint32_t m = a.token_mask[t];
-            s_mask[t] = (uint8_t)m;
+            const uint32_t m = token_rank_mask(a, t);
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                lo += (uint64_t)((m >> r) & 1u) << (16 * r);
-                hi += (uint64_t)((m >> (r + 4)) & 1u) << (16 * r);
-            }
+            for (int r = 0; r < kMaxRanks; ++r) cnt[r >> 1] += (uint64_t)((m >> r) & 1u) << (32 * (r & 1));
+            if (a.topk_idx != nullptr)
+                for (int k = 0; k < a.num_topk; ++k) {
+                    const int64_t e = a.topk_idx[(int64_t)t * a.num_topk + k];
+                    if (e >= 0 && e < a.num_experts) atomicAdd(&s_ecnt[e], 1);
+                }
         }
-        uint64_t tlo, thi;
-        block_exclusive_scan_u64x2(lo, hi, &tlo, &thi, s_ws);
-        if (tid < R) s_total[tid] = (int)(((tid < 4 ? tlo : thi) >> (16 * (tid & 3))) & 0xffffu);
-        int base[kMaxRanks];
+        uint64_t tot[kCountWords];
+        block_exclusive_scan_counts(cnt, tot, s_ws);
+        // Publish this CTA's counts, then add up those of the CTAs before it (all CTAs are resident:
+        // the grid is at most kMaxCountCtas small CTAs).
+        if (tid < R) {
+            int mine = 0;  // count_of(tot, tid) with static indices (no local-memory copy of tot)
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) base[r] = (int)(((r < 4 ? lo : hi) >> (16 * (r & 3))) & 0xffffu);
+            for (int r = 0; r < kMaxRanks; ++r)
+                if (r == tid) mine = count_of(tot, r);
+            my_ctrl->count_cta_counts[blockIdx.x][tid] = mine;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            st_release_sys(&my_ctrl->count_cta_flag[blockIdx.x], epoch);
+        }
+        if (tid < (int)blockIdx.x) {
+            if (wait_ge(&my_ctrl->count_cta_flag[tid], epoch, a.st, kErrTimeoutNotify, -1))
+                for (int r = 0; r < R; ++r) atomicAdd(&s_base[r], ld_volatile(&my_ctrl->count_cta_counts[tid][r]));
+        }
+        __syncthreads();
+        if (aborted(a.st)) return;
+        int pos[kMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) pos[r] = r < R ? s_base[r] + count_of(cnt, r) : 0;
         int* list = reinterpret_cast<int*>(static_cast<uint8_t*>(a.peers.base[a.rank]) + a.layout.list_off);
         const int cap = a.layout.capacity;
         for (int t = t0; t < t1; ++t) {
-            const uint32_t m = s_mask[t];
+            const uint32_t m = token_rank_mask(a, t);
 #pragma unroll
             for (int r = 0; r < kMaxRanks; ++r) {
                 if (r >= R) break;
-                int pos = -1;
+                int p = -1;
                 if ((m >> r) & 1u) {
-                    pos = base[r]++;
-                    list[(int64_t)r * cap + pos] = t;
+                    p = pos[r]++;
+                    list[(int64_t)r * cap + p] = t;
                 }
-                a.send_head[(int64_t)t * R + r] = pos;
+                a.send_head[(int64_t)t * R + r] = p;
             }
+        }
+        for (int i = tid; i < a.num_experts; i += nt)
+            if (s_ecnt[i] != 0) atomicAdd(&a.expert_counts[i], s_ecnt[i]);
+    }
+    // The last CTA to finish runs the exchange.
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(&my_ctrl->count_done_ctas, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (!a.cached) {
+        if (tid < R) {
+            int total = 0;
+            for (int b = 0; b < (int)gridDim.x; ++b) total += ld_volatile(&my_ctrl->count_cta_counts[b][tid]);
+            s_total[tid] = total;
         }
         __syncthreads();
         // Push my count row and my per-expert counts into every destination's control block.
@@ -325,10 +386,13 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
         }
         for (int i = tid; i < R * a.num_local_experts; i += nt) {
             const int dst = i / a.num_local_experts, le = i % a.num_local_experts;
-            ctrl_of(a.peers, a.layout, dst)->expert_counts[parity][a.rank][le] =
-                a.topk_idx != nullptr ? s_ecnt[dst * a.num_local_experts + le] : 0;
+            int* c = &a.expert_counts[dst * a.num_local_experts + le];
+            ctrl_of(a.peers, a.layout, dst)->expert_counts[parity][a.rank][le] = a.topk_idx != nullptr ? ld_volatile(c) : 0;
+            *c = 0;  // ready for the next dispatch
         }
     }
+    for (int i = tid; i < a.stage_chunks; i += nt) my_ctrl->stage_chunk_done[i] = 0;
+    if (tid == 0) my_ctrl->count_done_ctas = 0;
     __syncthreads();
     const uint64_t t_wait = trace_begin(a.st);
     if (tid < R) {
@@ -337,12 +401,12 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
         wait_ge(&my_ctrl->notify_flag[tid], epoch, a.st, kErrTimeoutNotify, tid);
     }
     __syncthreads();
-    if (tid == 0) trace_end(a.st, kTraceNotifyWait, t_wait, epoch);
+    if (tid == 0) trace_end(a.st, kTraceCountExchange, t_wait, epoch);
     if (aborted(a.st)) return;
     if (a.cached) {
         if (tid == 0) {
             my_ctrl->dispatch_epoch = epoch;
-            trace_end(a.st, kTraceNotify, t_start, 1);
+            trace_end(a.st, kTraceCount, t_start, 1);
         }
         return;
     }
@@ -350,21 +414,20 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
     for (int i = tid; i < R * R; i += nt)
         s_tc[i / R][i % R] = ld_volatile(&my_ctrl->token_counts[parity][i / R][i % R]);
     __syncthreads();
-    if (tid == 0) {
-        for (int r = 0; r < R; ++r) {
-            int acc = 0;
-            for (int s = 0; s < R; ++s) {
-                acc += s_tc[s][r];
-                a.rank_prefix_matrix[s * R + r] = acc;
-            }
-        }
+    if (tid < R) {
+        // column `tid` of the inclusive prefix over sources, row `tid` of the exclusive prefix over destinations
+        int acc = 0;
         for (int s = 0; s < R; ++s) {
-            int acc = 0;
-            for (int r = 0; r < R; ++r) {
-                a.send_prefix_matrix[s * R + r] = acc;
-                acc += s_tc[s][r];
-            }
+            acc += s_tc[s][tid];
+            a.rank_prefix_matrix[s * R + tid] = acc;
         }
+        acc = 0;
+        for (int r = 0; r < R; ++r) {
+            a.send_prefix_matrix[tid * R + r] = acc;
+            acc += s_tc[tid][r];
+        }
+    }
+    if (tid == 0) {
         int acc = 0;
         a.recv_rank_prefix[0] = 0;
         for (int s = 0; s < R; ++s) {
@@ -383,14 +446,15 @@ __global__ void __launch_bounds__(1024) dispatch_notify_kernel(NotifyArgs a) {
     __syncthreads();
     if (tid == 0) {
         my_ctrl->dispatch_epoch = epoch;
-        trace_end(a.st, kTraceNotify, t_start, 0);
+        trace_end(a.st, kTraceCount, t_start, 0);
     }
 }
 
-void launch_dispatch_notify(const NotifyArgs& a, cudaStream_t stream) {
-    const size_t smem = sizeof(int) * (a.num_experts > 0 ? a.num_experts : 1) + (size_t)(a.cached ? 0 : a.num_tokens) + 16;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(dispatch_notify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dispatch_notify_kernel<<<1, 1024, smem, stream>>>(a);
+void launch_dispatch_count(const CountArgs& a, cudaStream_t stream) {
+    const int grid = a.cached ? 1 : std::max(1, (a.num_tokens + a.tokens_per_cta - 1) / a.tokens_per_cta);
+    const size_t smem = sizeof(int) * (size_t)std::max(a.cached ? 1 : a.num_experts, 1);
+    if (smem > 48 * 1024) cudaFuncSetAttribute(dispatch_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dispatch_count_kernel<<<grid, kCountThreads, smem, stream>>>(a);
 }
 
 // =================================================================================================
@@ -467,138 +531,186 @@ __device__ __forceinline__ void pipe_init(const PipeSmem& p) {
 // pull (dispatch receive): rows of my receive block are pulled from the sources' staging.
 // =================================================================================================
 
-__global__ void __launch_bounds__(64 * kPairs) dispatch_pull_kernel(PullArgs a) {
+constexpr int kStageWarps = 4;  // stage warps per pull block when the stage overlaps the pulls
+
+// Stage warps of the pull launch: stage this rank's tokens in token order (grid-stride over warps,
+// so low chunks complete first) and, once the last token of a chunk is in the staging, release
+// staged[rank][chunk] = epoch in every receiver's control block. A warp's stores are ordered
+// before lane 0's acq_rel add by __syncwarp; the add that completes a chunk has acquired every
+// earlier add of that chunk, so its releases cover the whole chunk.
+__device__ __forceinline__ void stage_warps_run(const PullArgs& a, NormalCtrl* my_ctrl, int epoch) {
+    const StageArgs& sa = a.stage;
+    const int lane = lane_id();
+    const int gw = blockIdx.x * kStageWarps + (warp_id() - 2 * kPairs), GW = gridDim.x * kStageWarps;
+    for (int t = gw; t < sa.num_tokens; t += GW) {
+        stage_token_regs(sa, t);
+        __syncwarp();
+        if (lane == 0) {
+            const int c = t / sa.chunk;
+            const int target = min(sa.chunk, sa.num_tokens - c * sa.chunk);
+            fence_proxy_async_global();  // receivers read the staging with TMA (async proxy)
+            if (atom_add_acq_rel_sys(&my_ctrl->stage_chunk_done[c], 1) == target - 1) {
+                for (int r = 0; r < a.num_ranks; ++r) st_release_sys(&ctrl_of(a.peers, a.layout, r)->staged[a.rank][c], epoch);
+            }
+        }
+        if ((t & 63) == 0 && aborted(a.st)) break;
+    }
+}
+
+__global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_kernel(PullArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_prefix[kMaxRanks + 1];
+    __shared__ int s_staged_chunk[kPairs][kMaxRanks];  // per pair (producer lane 0): last chunk of each source seen staged
     const int lane = lane_id(), warp = warp_id();
+    const bool pull_warp = warp < 2 * kPairs;
     const int pair = warp >> 1;
     const bool producer = (warp & 1) == 0;
     const int R = a.num_ranks;
     const int slot_bytes = (a.rec.bytes + 127) / 128 * 128;
-    const PipeSmem p = pipe_smem(smem, pair, a.stages, slot_bytes);
-    const uint64_t t_start = trace_begin(a.st);
-    pipe_init(p);
+    NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
+    const int epoch = ld_volatile(&my_ctrl->dispatch_epoch);
+    const PipeSmem p = pipe_smem(smem, pull_warp ? pair : 0, a.stages, slot_bytes);
+    if (pull_warp) pipe_init(p);
     if (threadIdx.x == 0) {
         s_prefix[0] = 0;
         for (int s = 0; s < R; ++s) s_prefix[s + 1] = a.rank_prefix_matrix[s * R + a.rank];
     }
+    if (threadIdx.x < kPairs * kMaxRanks) s_staged_chunk[threadIdx.x / kMaxRanks][threadIdx.x % kMaxRanks] = -1;
     __syncthreads();
 
     const int num_recv = a.dev_num_recv != nullptr ? ld_volatile(a.dev_num_recv) : a.num_recv_host;
     const int K = a.num_topk;
-    for (int j = num_recv + blockIdx.x * blockDim.x + threadIdx.x; a.fill_padding && j < a.num_out_rows;
-         j += gridDim.x * blockDim.x) {
-        if (a.recv_topk_idx != nullptr)
-            for (int k = 0; k < K; ++k) a.recv_topk_idx[(int64_t)j * K + k] = -1;
-        if (a.recv_topk_weights != nullptr)
-            for (int k = 0; k < K; ++k) a.recv_topk_weights[(int64_t)j * K + k] = 0.f;
-        if (a.recv_src_idx != nullptr) a.recv_src_idx[j] = -1;
-    }
-    if (num_recv > a.num_out_rows) {
+    // Trace start of the pull (thread 0 reports it); read after the set-up barrier, so no 64-bit
+    // value stays live through the pipeline loops.
+    uint64_t t_pull = threadIdx.x == 0 ? trace_begin(a.st) : 0;
+    if (!pull_warp) {
+        // Stage warps: they never wait for the pulls, so every rank's pulls make progress.
+        const uint64_t t_stage = trace_begin(a.st);
+        if (a.stage_warps > 0 && !aborted(a.st)) stage_warps_run(a, my_ctrl, epoch);
+        if (warp == 2 * kPairs && lane == 0 && a.stage_warps > 0) trace_end(a.st, kTraceStage, t_stage, a.stage.num_tokens);
+    } else if (num_recv > a.num_out_rows) {
         if (threadIdx.x == 0 && blockIdx.x == 0) report_error(a.st, kErrCapacity, -1, num_recv);
-        return;
-    }
-    // Host-mapped counts for the CPU (written here rather than by the notify kernel, so PCIe writes
-    // and their fence stay off the path to the first pull).
-    if (blockIdx.x == gridDim.x - 1 && warp == 1 && a.host != nullptr) {
-        for (int le = lane; le < a.num_local_experts; le += 32)
-            a.host->num_recv_tokens_per_expert[le] = a.num_recv_per_expert[le];
-        if (lane == 0) a.host->num_recv_tokens = num_recv;
-        __syncwarp();
-        if (lane == 0) {
-            __threadfence_system();
-            *reinterpret_cast<volatile int*>(&a.host->ready_ticket) = a.host_ticket;
+    } else {
+        const int pull_threads = 64 * kPairs;
+        for (int j = num_recv + blockIdx.x * pull_threads + threadIdx.x; a.fill_padding && j < a.num_out_rows;
+             j += gridDim.x * pull_threads) {
+            if (a.recv_topk_idx != nullptr)
+                for (int k = 0; k < K; ++k) a.recv_topk_idx[(int64_t)j * K + k] = -1;
+            if (a.recv_topk_weights != nullptr)
+                for (int k = 0; k < K; ++k) a.recv_topk_weights[(int64_t)j * K + k] = 0.f;
+            if (a.recv_src_idx != nullptr) a.recv_src_idx[j] = -1;
         }
-    }
-    const int g = blockIdx.x * kPairs + pair, P = gridDim.x * kPairs;
-    const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
-    const int S = p.S;
-
-    if (producer) {
-        // After an expired wait lane 0 issues nothing more (the consumer stops at the first row that
-        // does not arrive) instead of waiting out every later row; then it drains what it issued.
-        int failed = 0, issued = 0;
-        for (int base = 0; base < my_rows; base += 32) {
-            const int kk = base + lane;
-            int src = 0, t = 0;
-            if (kk < my_rows) {
-                const int j = pair_row(g, P, kk, a.chunk, num_recv);
-                src = find_source(s_prefix, R, j);
-                if (a.cached_src_idx != nullptr) {
-                    t = a.cached_src_idx[j];
-                } else {
-                    const int* list = reinterpret_cast<const int*>(static_cast<const uint8_t*>(a.peers.base[src]) + a.layout.list_off) +
-                                      (int64_t)a.rank * a.layout.capacity;
-                    t = ld_relaxed_sys(list + (j - s_prefix[src]));
-                }
+        // Host-mapped counts for the CPU (written here rather than by the count kernel, so PCIe
+        // writes and their fence stay off the path to the first pull).
+        if (blockIdx.x == gridDim.x - 1 && warp == 1 && a.host != nullptr) {
+            for (int le = lane; le < a.num_local_experts; le += 32)
+                a.host->num_recv_tokens_per_expert[le] = a.num_recv_per_expert[le];
+            if (lane == 0) a.host->num_recv_tokens = num_recv;
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_system();
+                *reinterpret_cast<volatile int*>(&a.host->ready_ticket) = a.host_ticket;
             }
-            const int n = min(32, my_rows - base);
-            for (int i = 0; i < n; ++i) {
-                const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
-                if (lane == 0 && !failed) {
-                    const int k = base + i, slot = k % S;
-                    if (k >= S && !mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma)) {
-                        failed = 1;
+        }
+        const int g = blockIdx.x * kPairs + pair, P = gridDim.x * kPairs;
+        const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
+        const int S = p.S;
+        const int chunk = a.stage_warps > 0 ? a.stage.chunk : 0;
+
+        if (producer) {
+            // After an expired wait lane 0 issues nothing more (the consumer stops at the first row that
+            // does not arrive) instead of waiting out every later row; then it drains what it issued.
+            int failed = 0, issued = 0;
+            for (int base = 0; base < my_rows; base += 32) {
+                const int kk = base + lane;
+                int src = 0, t = 0;
+                if (kk < my_rows) {
+                    const int j = pair_row(g, P, kk, a.chunk, num_recv);
+                    src = find_source(s_prefix, R, j);
+                    if (a.cached_src_idx != nullptr) {
+                        t = a.cached_src_idx[j];
                     } else {
-                        p.side[2 * slot] = pt;
-                        const uint8_t* gsrc = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
-                                              (int64_t)pt * a.layout.record_bytes;
-                        mbar_arrive_expect_tx(&p.full[slot], a.rec.bytes);
-                        tma_load_1d(p.slots + (size_t)slot * slot_bytes, gsrc, a.rec.bytes, &p.full[slot]);
-                        ++issued;
+                        const int* list = reinterpret_cast<const int*>(static_cast<const uint8_t*>(a.peers.base[src]) + a.layout.list_off) +
+                                          (int64_t)a.rank * a.layout.capacity;
+                        t = ld_relaxed_sys(list + (j - s_prefix[src]));
                     }
                 }
-            }
-            if (__shfl_sync(0xffffffffu, failed, 0)) break;
-        }
-        if (lane == 0) ring_drain(p.full, S, issued, a.st, kErrTimeoutTma);
-    } else {
-        const int x_bytes = a.rec.x_bytes;
-        const int nb = a.rec.scale_bytes > 0 ? a.layout.hidden / 128 : 0;
-        const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
-        const int E_l = a.num_local_experts, lo_e = a.rank * E_l;
-        const int lag = S / 2 < 4 ? S / 2 : 4;  // peer loads are the slow leg: favour loads in flight
-        for (int k = 0; k < my_rows; ++k) {
-            const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
-            int good = 1;
-            if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
-            if (!__shfl_sync(0xffffffffu, good, 0)) break;
-            const uint8_t* buf = p.slots + (size_t)slot * slot_bytes;
-            if (lane == 0) {
-                tma_store_1d(static_cast<uint8_t*>(a.recv_x) + (int64_t)j * x_bytes, buf, x_bytes);
-                if (scales_bulk) tma_store_1d(a.recv_scales + (int64_t)j * nb, buf + a.rec.scale_off, nb * 4);
-                bulk_commit();
-            }
-            if (a.recv_scales != nullptr && !scales_bulk) {
-                const float* sc = reinterpret_cast<const float*>(buf + a.rec.scale_off);
-                for (int b = lane; b < nb; b += 32) {
-                    if (a.scales_col_major) a.recv_scales[(int64_t)b * a.scales_ld + j] = sc[b];
-                    else a.recv_scales[(int64_t)j * nb + b] = sc[b];
+                const int n = min(32, my_rows - base);
+                for (int i = 0; i < n; ++i) {
+                    const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
+                    if (lane == 0 && !failed) {
+                        const int k = base + i, slot = k % S;
+                        if (chunk > 0 && s_staged_chunk[pair][ps] != pt / chunk) {
+                            // The source stages concurrently: wait (bounded, local flag) until the chunk
+                            // holding this token is in its staging, then order the TMA read after it.
+                            if (!wait_ge(&my_ctrl->staged[ps][pt / chunk], epoch, a.st, kErrTimeoutStaged, ps)) {
+                                failed = 1;
+                                continue;
+                            }
+                            s_staged_chunk[pair][ps] = pt / chunk;
+                            fence_proxy_async_global();
+                        }
+                        if (k >= S && !mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma)) {
+                            failed = 1;
+                        } else {
+                            p.side[2 * slot] = pt;
+                            const uint8_t* gsrc = static_cast<const uint8_t*>(a.peers.base[ps]) + a.layout.staging_off +
+                                                  (int64_t)pt * a.layout.record_bytes;
+                            mbar_arrive_expect_tx(&p.full[slot], a.rec.bytes);
+                            tma_load_1d(p.slots + (size_t)slot * slot_bytes, gsrc, a.rec.bytes, &p.full[slot]);
+                            ++issued;
+                        }
+                    }
                 }
+                if (__shfl_sync(0xffffffffu, failed, 0)) break;
             }
-            if (lane < K) {
-                const int e = reinterpret_cast<const int*>(buf + a.rec.idx_off)[lane];
-                const float w = reinterpret_cast<const float*>(buf + a.rec.w_off)[lane];
-                const bool mine = e >= lo_e && e < lo_e + E_l;
-                if (a.recv_topk_idx != nullptr) a.recv_topk_idx[(int64_t)j * K + lane] = mine ? (e - lo_e) : -1;
-                if (a.recv_topk_weights != nullptr) a.recv_topk_weights[(int64_t)j * K + lane] = mine ? w : 0.f;
+            if (lane == 0) ring_drain(p.full, S, issued, a.st, kErrTimeoutTma);
+        } else {
+            const int x_bytes = a.rec.x_bytes;
+            const int nb = a.rec.scale_bytes > 0 ? a.layout.hidden / 128 : 0;
+            const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
+            const int E_l = a.num_local_experts, lo_e = a.rank * E_l;
+            const int lag = S / 2 < 4 ? S / 2 : 4;  // peer loads are the slow leg: favour loads in flight
+            for (int k = 0; k < my_rows; ++k) {
+                const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
+                int good = 1;
+                if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, good, 0)) break;
+                const uint8_t* buf = p.slots + (size_t)slot * slot_bytes;
+                if (lane == 0) {
+                    tma_store_1d(static_cast<uint8_t*>(a.recv_x) + (int64_t)j * x_bytes, buf, x_bytes);
+                    if (scales_bulk) tma_store_1d(a.recv_scales + (int64_t)j * nb, buf + a.rec.scale_off, nb * 4);
+                    bulk_commit();
+                }
+                if (a.recv_scales != nullptr && !scales_bulk) {
+                    const float* sc = reinterpret_cast<const float*>(buf + a.rec.scale_off);
+                    for (int b = lane; b < nb; b += 32) {
+                        if (a.scales_col_major) a.recv_scales[(int64_t)b * a.scales_ld + j] = sc[b];
+                        else a.recv_scales[(int64_t)j * nb + b] = sc[b];
+                    }
+                }
+                if (lane < K) {
+                    const int e = reinterpret_cast<const int*>(buf + a.rec.idx_off)[lane];
+                    const float w = reinterpret_cast<const float*>(buf + a.rec.w_off)[lane];
+                    const bool mine = e >= lo_e && e < lo_e + E_l;
+                    if (a.recv_topk_idx != nullptr) a.recv_topk_idx[(int64_t)j * K + lane] = mine ? (e - lo_e) : -1;
+                    if (a.recv_topk_weights != nullptr) a.recv_topk_weights[(int64_t)j * K + lane] = mine ? w : 0.f;
+                }
+                if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[2 * slot];
+                __syncwarp();
+                if (lane == 0) release_slots(p, k, lag);
             }
-            if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[2 * slot];
-            __syncwarp();
-            if (lane == 0) release_slots(p, k, lag);
+            if (lane == 0) bulk_wait<0>();
         }
-        if (lane == 0) bulk_wait<0>();
     }
     __syncthreads();
     // The last block tells every source that its staging may be reused.
     if (threadIdx.x == 0) {
-        trace_end(a.st, kTracePull, t_start, num_recv);
-        NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
+        trace_end(a.st, kTracePull, t_pull, num_recv);
         fence_sys();
         const int old = atom_add_acq_rel_gpu(&my_ctrl->pull_finished_blocks, 1);
         if (old == (int)gridDim.x - 1) {
             my_ctrl->pull_finished_blocks = 0;
-            const int epoch = ld_volatile(&my_ctrl->dispatch_epoch);
             fence_sys();
             for (int s = 0; s < R; ++s) st_release_sys(&ctrl_of(a.peers, a.layout, s)->pull_done[a.rank], epoch);
         }
@@ -618,8 +730,9 @@ void launch_dispatch_pull(const PullArgs& a_in, int num_sms, cudaStream_t stream
     if (a.stages <= 0) a.stages = pipe_stages(slot_bytes, 16);
     if (a.stages < 4) a.stages = 4;
     const size_t smem = pipe_smem_bytes(a.stages, slot_bytes);
+    a.stage_warps = a.stage_warps > 0 ? kStageWarps : 0;
     cudaFuncSetAttribute(dispatch_pull_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dispatch_pull_kernel<<<num_sms, 64 * kPairs, smem, stream>>>(a);
+    dispatch_pull_kernel<<<num_sms, 64 * kPairs + 32 * a.stage_warps, smem, stream>>>(a);
 }
 
 // =================================================================================================
@@ -827,7 +940,7 @@ __device__ __forceinline__ void expanded_token_to_slot(const CombineArgs& a, int
     if (lane < K) {
         r = a.row_map[(int64_t)j * K + lane];
         if (a.row_weights != nullptr) w = a.row_weights[(int64_t)j * K + lane];
-        if (r >= a.x_rows) {
+        if (r >= 0 && !in_window(r, 1, a.x_rows)) {
             report_error(a.st, kErrBounds, j, r);
             r = -1;
         }
@@ -962,7 +1075,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs a)
                 int good = 1;
                 if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
                 if (!__shfl_sync(0xffffffffu, good, 0)) break;
-                if (drow < 0 || drow >= rows_cap) {
+                if (!in_window(drow, 1, rows_cap)) {
                     if (lane == 0) report_error(a.st, kErrBounds, d, (int)drow);
                     break;
                 }

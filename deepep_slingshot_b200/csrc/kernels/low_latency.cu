@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(256) ll_combine_kernel(LLCombineArgs a) {
             const int meta = dsp.src_meta()[(int64_t)le * slots + j];
             const int t = dsp.src_info()[(int64_t)le * slots + j];
             const int src = meta / K, k = meta % K;
-            if (src < 0 || src >= R || t < 0 || t >= L.max_tokens) {
+            if (!in_window(src, 1, R) || !in_window(t, 1, L.max_tokens)) {
                 if (lane == 0) report_error(a.st, kErrBounds, src, t);
                 continue;
             }

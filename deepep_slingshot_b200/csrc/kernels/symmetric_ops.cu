@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256) engram_fetch_kernel(EngramFetchArgs a) {
     for (int t = blockIdx.x * warps + warp_id(); t < a.num_tokens; t += gridDim.x * warps) {
         const int idx = a.indices[t];
         int4* dst = reinterpret_cast<int4*>(a.out + (int64_t)t * a.row_bytes);
-        if (idx < 0 || idx >= total) {
+        if (!in_window(idx, 1, total)) {
             for (int u = lane; u < units; u += 32) dst[u] = make_int4(0, 0, 0, 0);
             if (lane == 0) report_error(a.st, kErrBounds, -1, idx);
             continue;

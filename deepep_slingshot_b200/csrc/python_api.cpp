@@ -41,6 +41,15 @@ PYBIND11_MODULE(_C, m) {
     m.def("normal_layout_capacity", [](int64_t region_bytes, int hidden, int num_ranks) {
         return ep::compute_normal_layout(region_bytes, hidden, num_ranks).capacity;
     });
+    m.def("window_check", [](const torch::Tensor& cases) {
+        TORCH_CHECK(cases.is_cuda() && cases.scalar_type() == torch::kInt64 && cases.dim() == 2 && cases.size(1) == 3 &&
+                        cases.is_contiguous(),
+                    "cases must be a contiguous int64 CUDA tensor [n, 3] of (index, count, window)");
+        auto codes = torch::empty({cases.size(0)}, cases.options().dtype(torch::kInt32));
+        ep::launch_window_check(cases.data_ptr<int64_t>(), (int)cases.size(0), codes.data_ptr<int>(),
+                                at::cuda::getCurrentCUDAStream());
+        return codes;
+    });
     m.def("normal_layout", [](int64_t region_bytes, int hidden, int num_ranks) {
         const ep::NormalLayout l = ep::compute_normal_layout(region_bytes, hidden, num_ranks);
         py::dict d;
@@ -101,6 +110,7 @@ PYBIND11_MODULE(_C, m) {
         .def("intranode_dispatch_gemm", &ep::Buffer::intranode_dispatch_gemm)
         .def("intranode_combine", &ep::Buffer::intranode_combine)
         .def("barrier", &ep::Buffer::barrier)
+        .def("selftest_signal_stress", &ep::Buffer::selftest_signal_stress)
         .def("clean_low_latency_buffer", &ep::Buffer::clean_low_latency_buffer)
         .def("low_latency_dispatch", &ep::Buffer::low_latency_dispatch)
         .def("low_latency_dispatch_gemm", &ep::Buffer::low_latency_dispatch_gemm)

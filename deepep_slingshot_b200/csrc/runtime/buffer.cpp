@@ -67,7 +67,8 @@ void poison(const torch::Tensor& t, cudaStream_t stream) {
 
 const char* error_name(int code) {
     switch (code) {
-        case kErrTimeoutNotify: return "timeout waiting for a peer's dispatch counts (notify)";
+        case kErrTimeoutNotify: return "timeout waiting for a peer's dispatch counts (count step)";
+        case kErrTimeoutStaged: return "timeout waiting for a source to stage the tokens being pulled";
         case kErrTimeoutPullDone: return "timeout waiting for receivers to finish reading the staging area";
         case kErrTimeoutCombineReady: return "timeout waiting for a destination to finish its previous combine";
         case kErrTimeoutCombineArrive: return "timeout waiting for combine contributions to arrive";
@@ -468,7 +469,7 @@ PeerTable Buffer::ll_peers() const {
 
 // Opt-in kernel timing (env DEEPEP_B200_PROFILE=1): events at fixed points of every dispatch /
 // combine; `get_profile()` synchronizes and returns the mean milliseconds between marks.
-// Points: 0 stage, 1 notify, 2 pull, 3 dispatch end, 4 combine, 5 combine end.
+// Points: 0 count, 1 output allocation, 2 stage + pull, 3 dispatch end, 4 combine, 5 combine end.
 void Buffer::prof_mark(cudaStream_t stream, int point) {
     if (!profile_enabled_) return;
     cudaEvent_t e;
@@ -480,7 +481,7 @@ void Buffer::prof_mark(cudaStream_t stream, int point) {
 std::map<std::string, double> Buffer::get_profile() {
     std::map<std::string, double> out;
     cudaDeviceSynchronize();
-    const char* names[] = {"stage", "notify", "pull", "dispatch_end", "combine", "combine_end"};
+    const char* names[] = {"count", "outputs", "stage_pull", "dispatch_end", "combine", "combine_end"};
     std::map<std::string, std::pair<double, int>> acc;
     for (size_t i = 0; i + 1 < prof_events_.size(); ++i) {
         const int a = prof_events_[i].first, b = prof_events_[i + 1].first;
@@ -537,6 +538,37 @@ Buffer::get_dispatch_layout(const torch::Tensor& topk_idx, int num_experts, std:
                            num_tokens_per_expert.data_ptr<int>(), is_token_in_rank.data_ptr<bool>(), scope.comm.stream());
     auto event = scope.finish(async, {topk_idx, num_tokens_per_rank, num_tokens_per_expert, is_token_in_rank});
     return {num_tokens_per_rank, std::nullopt, num_tokens_per_expert, is_token_in_rank, event};
+}
+
+// Tokens per staged-chunk flag: the same on every rank (a function of the common capacity), with at
+// most kMaxStageChunks chunks per rank and at least 128 tokens per chunk.
+static int stage_chunk_tokens(int capacity) {
+    return std::max(128, (capacity + kMaxStageChunks - 1) / kMaxStageChunks);
+}
+
+// Count-step arguments shared by dispatch() and dispatch_gemm(); the caller fills the routing
+// inputs and the output tensors.
+CountArgs Buffer::count_args(const NormalLayout& L, int N, int K, int num_experts, bool cached, int expert_alignment,
+                             int stage_chunk) {
+    CountArgs na{};
+    na.num_tokens = N;
+    na.num_topk = K;
+    na.num_experts = num_experts;
+    na.num_local_experts = cached ? 0 : num_experts / num_ranks_;
+    na.num_ranks = num_ranks_;
+    na.rank = rank_;
+    na.cached = cached ? 1 : 0;
+    // at most kMaxCountCtas CTAs, each a multiple of the 256-thread block in tokens
+    const int per_cta = (N + kMaxCountCtas - 1) / kMaxCountCtas;
+    na.tokens_per_cta = std::max(1, (per_cta + 255) / 256) * 256;
+    na.expert_alignment = std::max(1, expert_alignment);
+    na.stage_chunks = (N + stage_chunk - 1) / stage_chunk;
+    na.peers = nvl_peers();
+    na.layout = L;
+    na.dev_num_recv = dev_workspace_ + 1;
+    na.expert_counts = reinterpret_cast<int*>(static_cast<uint8_t*>(nvl_base_) + L.scratch_off + align_up(L.capacity, kAlign));
+    na.st = status();
+    return na;
 }
 
 std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<torch::Tensor>, std::optional<torch::Tensor>,
@@ -596,42 +628,8 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     const PeerTable peers = nvl_peers();
     uint8_t* my_base = static_cast<uint8_t*>(nvl_base_);
 
-    // 1) stage
-    StageArgs sa{};
-    sa.x = x.data_ptr();
-    if (fp8_in) {
-        TORCH_CHECK(x_scales->scalar_type() == torch::kFloat32 && x_scales->dim() == 2 && x_scales->size(0) == N &&
-                        x_scales->size(1) == H / 128,
-                    "x scales must be float32 [num_tokens, hidden / 128]");
-        sa.x_scales = x_scales->data_ptr<float>();
-        sa.scale_stride_t = x_scales->stride(0);
-        sa.scale_stride_b = x_scales->stride(1);
-    }
-    sa.topk_idx = (!cached && topk_idx.has_value()) ? topk_idx->data_ptr<int64_t>() : nullptr;
-    sa.topk_weights = (!cached && topk_weights.has_value()) ? topk_weights->data_ptr<float>() : nullptr;
-    sa.staging = my_base + L.staging_off;
-    sa.pull_done = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->pull_done;
-    sa.num_tokens = N;
-    sa.hidden = H;
-    sa.num_topk = K;
-    sa.topk_pad = (int)align_up(K, 4);
-    sa.in_elem_bytes = fp8_in ? 1 : 2;
-    sa.quantize = quantize_fp8 ? 1 : 0;
-    sa.round_scale = round_scale ? 1 : 0;
-    sa.num_ranks = R;
-    sa.dispatch_epoch = &reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->dispatch_epoch;
-    sa.token_mask = cached ? nullptr : my_base + L.scratch_off;
-    sa.expert_counts = cached ? nullptr : reinterpret_cast<int*>(my_base + L.scratch_off + align_up(L.capacity, kAlign));
-    sa.is_token_in_rank = (!cached && is_token_in_rank.has_value()) ? is_token_in_rank->data_ptr<bool>() : nullptr;
-    sa.num_experts = cached ? 0 : num_experts;
-    sa.num_local_experts = E_l;
-    sa.rec = rec;
-    sa.record_stride = L.record_bytes;
-    sa.st = st;
-    prof_mark(stream, 0);
-    launch_dispatch_stage(sa, num_sms, stream);
-
-    // 2) notify
+    // 1) count: lists, send_head and per-expert counts from the routing alone, then the count
+    //    exchange and the receive layout. It does not wait for any quantization.
     torch::Tensor send_head, rpm, spm, recv_rank_prefix;
     std::optional<torch::Tensor> num_recv_per_expert;
     if (cached) {
@@ -646,33 +644,46 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
         recv_rank_prefix = torch::empty({R + 1}, i32);
         num_recv_per_expert = torch::empty({E_l}, i32);
     }
-    NotifyArgs na{};
-    na.topk_idx = sa.topk_idx;
+    const int stage_chunk = stage_chunk_tokens(L.capacity);
+    CountArgs na = count_args(L, N, K, cached ? 0 : num_experts, cached, expert_alignment, stage_chunk);
+    na.topk_idx = (!cached && topk_idx.has_value()) ? topk_idx->data_ptr<int64_t>() : nullptr;
     na.is_token_in_rank = (!cached && is_token_in_rank.has_value()) ? is_token_in_rank->data_ptr<bool>() : nullptr;
-    na.num_tokens = N;
-    na.num_topk = K;
-    na.num_experts = cached ? 0 : num_experts;
-    na.num_local_experts = E_l;
-    na.num_ranks = R;
-    na.rank = rank_;
-    na.cached = cached ? 1 : 0;
-    na.host_ticket = ticket;
-    na.token_mask = sa.token_mask;
-    na.expert_counts = sa.expert_counts;
-    na.expert_alignment = std::max(1, expert_alignment);
-    na.peers = peers;
-    na.layout = L;
     na.send_head = send_head.data_ptr<int>();
     na.rank_prefix_matrix = rpm.data_ptr<int>();
     na.send_prefix_matrix = spm.data_ptr<int>();
     na.recv_rank_prefix = cached ? nullptr : recv_rank_prefix.data_ptr<int>();
     na.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
-    na.dev_num_recv = dev_workspace_ + 1;
     na.cumulative_stats = cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
-    na.host = host_counters_dev_;
-    na.st = st;
+    prof_mark(stream, 0);
+    launch_dispatch_count(na, stream);
     prof_mark(stream, 1);
-    launch_dispatch_notify(na, stream);
+
+    // 2) the stage, run by stage warps of the pull launch (it overlaps the pulls chunk by chunk)
+    StageArgs sa{};
+    sa.x = x.data_ptr();
+    if (fp8_in) {
+        TORCH_CHECK(x_scales->scalar_type() == torch::kFloat32 && x_scales->dim() == 2 && x_scales->size(0) == N &&
+                        x_scales->size(1) == H / 128,
+                    "x scales must be float32 [num_tokens, hidden / 128]");
+        sa.x_scales = x_scales->data_ptr<float>();
+        sa.scale_stride_t = x_scales->stride(0);
+        sa.scale_stride_b = x_scales->stride(1);
+    }
+    sa.topk_idx = (!cached && topk_idx.has_value()) ? topk_idx->data_ptr<int64_t>() : nullptr;
+    sa.topk_weights = (!cached && topk_weights.has_value()) ? topk_weights->data_ptr<float>() : nullptr;
+    sa.staging = my_base + L.staging_off;
+    sa.num_tokens = N;
+    sa.hidden = H;
+    sa.num_topk = K;
+    sa.topk_pad = (int)align_up(K, 4);
+    sa.in_elem_bytes = fp8_in ? 1 : 2;
+    sa.quantize = quantize_fp8 ? 1 : 0;
+    sa.round_scale = round_scale ? 1 : 0;
+    sa.chunk = stage_chunk;
+    sa.num_ranks = R;
+    sa.rec = rec;
+    sa.record_stride = L.record_bytes;
+    sa.st = st;
 
     // 3) receive size. Cached: known. Worst case (`num_worst_tokens`): no CPU sync at all. Otherwise
     //    the pull is launched at once into outputs sized for the largest possible receive
@@ -744,6 +755,8 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
     pa.host_ticket = ticket;
     pa.chunk = row_chunk_;
+    pa.stage_warps = 1;
+    pa.stage = sa;
     pa.st = st;
     prof_mark(stream, 2);
     launch_dispatch_pull(pa, num_sms, stream);
@@ -820,13 +833,17 @@ Buffer::intranode_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& top
     const PeerTable peers = nvl_peers();
     uint8_t* my_base = static_cast<uint8_t*>(nvl_base_);
 
-    // 1) stage (bf16 -> FP8 records), as dispatch()
+    // 1) stage (bf16 -> FP8 records) as a kernel of its own: the count exchange below is then a
+    //    barrier after every rank's staging, which the fused receive relies on (it has no staged flags).
+    NormalCtrl* my_ctrl = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off);
     StageArgs sa{};
     sa.x = x.data_ptr();
     sa.topk_idx = topk_idx.data_ptr<int64_t>();
     sa.topk_weights = topk_weights.data_ptr<float>();
     sa.staging = my_base + L.staging_off;
-    sa.pull_done = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->pull_done;
+    sa.pull_done = my_ctrl->pull_done;
+    sa.dispatch_epoch = &my_ctrl->dispatch_epoch;
+    sa.num_ranks = R;
     sa.num_tokens = N;
     sa.hidden = H;
     sa.num_topk = K;
@@ -834,47 +851,26 @@ Buffer::intranode_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& top
     sa.in_elem_bytes = 2;
     sa.quantize = 1;
     sa.round_scale = round_scale ? 1 : 0;
-    sa.num_ranks = R;
-    sa.dispatch_epoch = &reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off)->dispatch_epoch;
-    sa.token_mask = my_base + L.scratch_off;
-    sa.expert_counts = reinterpret_cast<int*>(my_base + L.scratch_off + align_up(L.capacity, kAlign));
-    sa.num_experts = num_experts;
-    sa.num_local_experts = E_l;
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
     sa.st = st;
     launch_dispatch_stage(sa, num_sms, stream);
 
-    // 2) notify: counts, 128-aligned per-expert rows, raw per-expert rows (statistics output)
+    // 2) count: lists, counts, 128-aligned per-expert rows, raw per-expert rows (statistics output)
     auto send_head = torch::empty({N, R}, i32);
     auto rpm = torch::empty({R, R}, i32);
     auto spm = torch::empty({R, R}, i32);
     auto recv_rank_prefix = torch::empty({R + 1}, i32);
     auto aligned_counts = torch::empty({E_l}, i32);
-    NotifyArgs na{};
-    na.topk_idx = sa.topk_idx;
-    na.num_tokens = N;
-    na.num_topk = K;
-    na.num_experts = num_experts;
-    na.num_local_experts = E_l;
-    na.num_ranks = R;
-    na.rank = rank_;
-    na.host_ticket = ticket;
-    na.token_mask = sa.token_mask;
-    na.expert_counts = sa.expert_counts;
-    na.expert_alignment = 128;
-    na.peers = peers;
-    na.layout = L;
+    CountArgs na = count_args(L, N, K, num_experts, false, 128, stage_chunk_tokens(L.capacity));
+    na.topk_idx = topk_idx.data_ptr<int64_t>();
     na.send_head = send_head.data_ptr<int>();
     na.rank_prefix_matrix = rpm.data_ptr<int>();
     na.send_prefix_matrix = spm.data_ptr<int>();
     na.recv_rank_prefix = recv_rank_prefix.data_ptr<int>();
     na.num_recv_per_expert = aligned_counts.data_ptr<int>();
-    na.dev_num_recv = dev_workspace_ + 1;
     na.cumulative_stats = raw_counts.data_ptr<int>();
-    na.host = host_counters_dev_;
-    na.st = st;
-    launch_dispatch_notify(na, stream);
+    launch_dispatch_count(na, stream);
 
     // 3) outputs (worst-case rows; exact views after the CPU sync) + the fused receive / GEMM
     auto a_rows = torch::empty({rows_cap, H}, x.options().dtype(torch::kFloat8_e4m3fn));
@@ -1019,6 +1015,30 @@ std::tuple<torch::Tensor, std::optional<torch::Tensor>, std::optional<EventHandl
     auto event = scope.finish(async, {x, topk_weights, bias_0, bias_1, rank_prefix_matrix, send_prefix_matrix, send_head, out, out_w,
                                       row_map, row_weights});
     return {out, out_w, event};
+}
+
+std::vector<int> Buffer::selftest_signal_stress(int producer_blocks, int warps, int rounds) {
+    check_error();
+    TORCH_CHECK(available_, "buffer not synced");
+    TORCH_CHECK(producer_blocks >= 1 && producer_blocks <= 1024 && warps >= 1 && warps <= 32 && rounds >= 1,
+                "producer_blocks in [1, 1024], warps in [1, 32], rounds >= 1");
+    const int64_t total = (int64_t)producer_blocks * warps * rounds;
+    TORCH_CHECK(total < (int64_t)1 << 30, "too many signals for an int counter");
+    const NormalLayout L = compute_normal_layout(num_nvl_bytes_, 128, num_ranks_);
+    const int next = (rank_ + 1) % num_ranks_;
+    auto* mine = reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(nvl_base_) + L.ctrl_off);
+    auto* peer = reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(nvl_peer_[next]) + L.ctrl_off);
+    auto result = torch::full({2}, -1, torch::dtype(torch::kInt32).device(torch::kCUDA));
+    auto stream = at::cuda::getCurrentCUDAStream();
+    // every rank's flag starts at zero before any rank's producers run
+    EP_CUDA_CHECK(cudaMemsetAsync(&mine->selftest_flag, 0, sizeof(int), stream));
+    barrier(false, true);
+    launch_signal_stress(&peer->selftest_flag, &mine->selftest_flag, producer_blocks, warps, rounds, (int)total,
+                         result.data_ptr<int>(), status(), stream);
+    EP_CUDA_CHECK(cudaGetLastError());
+    auto host = result.cpu();
+    barrier(false, true);
+    return {host[0].item<int>(), host[1].item<int>()};
 }
 
 void Buffer::barrier(bool use_comm_stream, bool with_cpu_sync) {

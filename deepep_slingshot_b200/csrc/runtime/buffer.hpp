@@ -125,6 +125,9 @@ class Buffer {
         const std::optional<torch::Tensor>& row_map, const std::optional<torch::Tensor>& row_weights);
 
     void barrier(bool use_comm_stream, bool with_cpu_sync);
+    // Transport self-test (multi-producer signalling into the next rank's control block); returns
+    // {status, value seen} after synchronizing. Every rank must call it together.
+    std::vector<int> selftest_signal_stress(int producer_blocks, int warps, int rounds);
 
     // ---------------------------------------------------------------- low-latency mode
     void clean_low_latency_buffer(int num_max_dispatch_tokens_per_rank, int hidden, int num_experts);
@@ -173,6 +176,8 @@ class Buffer {
     int num_ranks() const { return num_ranks_; }
 
    private:
+    CountArgs count_args(const NormalLayout& L, int N, int K, int num_experts, bool cached, int expert_alignment,
+                         int stage_chunk);
     KernelStatus status() const;
     PeerTable nvl_peers() const;
     PeerTable ll_peers() const;

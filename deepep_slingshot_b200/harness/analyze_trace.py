@@ -16,7 +16,7 @@ import sys
 from collections import defaultdict
 from typing import Dict, List, Tuple
 
-PHASE_ORDER = ['dispatch.stage.wait_receivers', 'dispatch.stage', 'dispatch.notify', 'dispatch.notify.wait_counts',
+PHASE_ORDER = ['dispatch.wait_receivers', 'dispatch.count', 'dispatch.count.exchange', 'dispatch.stage',
                'dispatch.pull', 'combine.push_warp', 'combine.block', 'll_dispatch.send', 'll_dispatch.recv',
                'll_combine.send', 'll_combine.recv', 'barrier', 'pp.copy']
 
@@ -36,9 +36,10 @@ def _union(intervals: List[Tuple[float, float]]) -> float:
 
 
 def split_steps(events: List[dict], gap_us: float = 50.0) -> List[List[dict]]:
-    """Split one rank's events into steps at gaps between stage-kernel starts."""
+    """Split one rank's events into steps at gaps between dispatch starts (the count kernel's first
+    record of a step)."""
     events = sorted(events, key=lambda e: e['ts'])
-    starts = sorted(e['ts'] for e in events if e['name'] == 'dispatch.stage.wait_receivers')
+    starts = sorted(e['ts'] for e in events if e['name'] == 'dispatch.wait_receivers')
     bounds = [t for i, t in enumerate(starts) if i == 0 or t - starts[i - 1] > gap_us]
     if not bounds:
         return [events]
@@ -77,7 +78,9 @@ def analyze(trace: dict) -> List[dict]:
                     'last_rank': max(rows, key=lambda x: x['end'])['rank'],
                     'end': max(x['end'] for x in rows), 'start': min(x['start'] for x in rows)}
         chain, prev_end = [], None
-        for name in ('dispatch.stage', 'dispatch.notify', 'dispatch.pull', 'combine.block'):
+        # The stage runs concurrently with the pull (stage warps of the pull launch), so the chain is
+        # count -> pull -> combine; the stage's own window is reported among the phases.
+        for name in ('dispatch.count', 'dispatch.pull', 'combine.block'):
             if name in phases:
                 p = phases[name]
                 gap = 0.0 if prev_end is None else max(0.0, p['start'] - prev_end)

@@ -171,6 +171,15 @@ class Buffer:
         """Maximum tokens per rank per normal-mode call for this hidden size."""
         return self.runtime.get_capacity(hidden, 8)
 
+    def transport_selftest(self, producer_blocks: int = 64, warps: int = 8, rounds: int = 16) -> Tuple[int, int]:
+        """Multi-producer signalling check over NVLink (collective): producer_blocks x warps warps of
+        every rank add 1 to the next rank's self-test flag `rounds` times with sys-scope release
+        reductions, and every rank waits (bounded by the GPU timeout) for the exact total. Returns
+        (status, value seen): status 0 exact, 1 more adds than sent, 2 the wait expired
+        (capability of the reference's producer stress test, backend/tests/gin_producer_stress.cu)."""
+        status, seen = self.runtime.selftest_signal_stress(producer_blocks, warps, rounds)
+        return status, seen
+
     def check_error(self) -> None:
         """Raise if any kernel of this buffer reported a failed (timed-out) wait or bad index."""
         self.runtime.check_error()
@@ -182,7 +191,7 @@ class Buffer:
         self.runtime.clear_error()
 
     def get_profile(self) -> dict:
-        """Mean device milliseconds per phase (stage / notify / pull / combine) since the last call,
+        """Mean device milliseconds per phase (count / outputs / stage_pull / combine) since the last call,
         recorded only when the process runs with DEEPEP_B200_PROFILE=1 (diagnostics; adds events)."""
         return dict(self.runtime.get_profile())
 

@@ -22,8 +22,8 @@ assert TRACE_DTYPE.itemsize == 40
 
 # Event ids of `ep::TraceEvent` (csrc/include/ep/abi.h).
 TRACE_EVENTS: Dict[int, str] = {
-    100: 'dispatch.stage', 101: 'dispatch.stage.wait_receivers', 102: 'dispatch.notify',
-    103: 'dispatch.notify.wait_counts', 104: 'dispatch.pull',
+    100: 'dispatch.stage', 101: 'dispatch.wait_receivers', 102: 'dispatch.count',
+    103: 'dispatch.count.exchange', 104: 'dispatch.pull',
     110: 'combine.block', 111: 'combine.push_warp',
     120: 'll_dispatch.send', 121: 'll_dispatch.recv', 122: 'll_combine.send', 123: 'll_combine.recv',
     124: 'll_dispatch.recv_gemm',

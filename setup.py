@@ -25,6 +25,7 @@ SOURCES = [
     os.path.join(CSRC, "kernels", "gemm_masked_sm100.cu"),
     os.path.join(CSRC, "kernels", "fused_dispatch_gemm.cu"),
     os.path.join(CSRC, "kernels", "symmetric_ops.cu"),
+    os.path.join(CSRC, "kernels", "transport_checks.cu"),
 ]
 
 NVCC_FLAGS = [

@@ -118,15 +118,14 @@ def test_analyze_trace_synthetic():
     ev = []
     for r in range(2):
         off = 10.0 * r
-        for name, s, d in (('dispatch.stage.wait_receivers', 0, 1), ('dispatch.stage', 0, 30), ('dispatch.notify', 31, 20),
-                           ('dispatch.pull', 52, 100), ('combine.block', 160, 200)):
+        for name, s, d in (('dispatch.wait_receivers', 0, 1), ('dispatch.count', 0, 20), ('dispatch.stage', 25, 30),
+                           ('dispatch.pull', 25, 100), ('combine.block', 160, 200)):
             ev.append({'name': name, 'pid': r, 'ts': s + off, 'dur': d})
     rep = analyze({'traceEvents': ev})
     assert len(rep) == 1
     p = rep[0]['phases']
     assert p['dispatch.stage']['start_spread_us'] == 10.0 and p['combine.block']['last_rank'] == 1
-    assert [c['phase'] for c in rep[0]['critical_path']] == ['dispatch.stage', 'dispatch.notify', 'dispatch.pull',
-                                                              'combine.block']
+    assert [c['phase'] for c in rep[0]['critical_path']] == ['dispatch.count', 'dispatch.pull', 'combine.block']
 
 
 def test_ep_benchmark_byte_counts():
