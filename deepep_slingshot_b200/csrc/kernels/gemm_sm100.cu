@@ -14,8 +14,8 @@
 //  * warp 0, one thread: TMA 2D loads (128B swizzle, no multicast) of the A and B tiles of every
 //    128-wide K block into an S-stage shared-memory ring;
 //  * warp 1, one thread: four `tcgen05.mma.cta_group::1.kind::f8f6f4` (M=128, N=128, K=32) per K
-//    block into one of two TMEM accumulators (K blocks alternate), then `tcgen05.commit` frees the
-//    shared-memory stage and publishes the TMEM buffer;
+//    block into one of the TMEM accumulators (K blocks rotate over 512 / N of them: four at N = 128),
+//    then `tcgen05.commit` frees the shared-memory stage and publishes the TMEM buffer;
 //  * warps 2..9: read the K-block partial with `tcgen05.ld`, release the TMEM buffer at once, and
 //    accumulate sa*sb*partial in fp32 registers (the per-block scale promotion that fp32 scales need);
 //    after the last K block they write bf16 rows.
@@ -52,8 +52,12 @@ constexpr int kThreads = (2 + kEpiWarps) * 32;
 // accumulators of kBN columns. 256-wide tiles stage 48 KiB per 8.4 MFLOP instead of 32 KiB per 4.2.
 template <int kBN>
 constexpr int kStageBytesT = (kBM + kBN) * kBK;
+// TMEM accumulators: as many kBN-column buffers as the 512 columns hold (4 at 128 wide, 2 at 256),
+// so the MMA issuer runs up to kAcc - 1 K blocks ahead of the epilogue's scale promotion.
 template <int kBN>
-constexpr uint32_t kTmemColsT = 2 * kBN;
+constexpr int kAccT = 512 / kBN;
+template <int kBN>
+constexpr uint32_t kTmemColsT = 512;
 
 // Instruction descriptor, kind::f8f6f4: E4M3 x E4M3 -> F32, both K-major, M = 128, N = kBN.
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
@@ -106,7 +110,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
     constexpr int kCols = kBN / 2;  // accumulator columns per epilogue thread (one row, one half)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
-    __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
+    constexpr int kAcc = kAccT<kBN>;
+    __shared__ __align__(8) uint64_t s_tfull[kAcc], s_tempty[kAcc];
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_mt_prefix[kMaxGemmExperts + 1];
 
@@ -121,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             mbar_init(&s_full[s], 1);
             mbar_init(&s_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kAcc; ++b) {
             mbar_init(&s_tfull[b], 1);
             mbar_init(&s_tempty[b], kEpiWarps);
         }
@@ -175,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             TileInfo ti;
             for (int t = blockIdx.x; ok && tile_of<kBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
                 for (int kb = 0; kb < KB && ok; ++kb, ++g) {
-                    const int s = g % S, b = g & 1;
-                    ok = wait_bar(&s_tempty[b], ((g >> 1) & 1) ^ 1, a.st) && wait_bar(&s_full[s], (g / S) & 1, a.st);
+                    const int s = g % S, b = g % kAcc;
+                    ok = wait_bar(&s_tempty[b], ((g / kAcc) & 1) ^ 1, a.st) && wait_bar(&s_full[s], (g / S) & 1, a.st);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t sa_addr = smem_u32(smem + (size_t)s * kStageBytes);
@@ -211,10 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             const float* sa_row = a.sa + (int64_t)m * KB;
             const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + (ti.n0 + kCols * h) / 128) * KB;
             for (int kb = 0; kb < KB; ++kb, ++g) {
-                const int b = g & 1;
+                const int b = g % kAcc;
                 const float scale = sa_row[kb] * sb_blk[kb];
                 int good = 1;
-                if (lane == 0) good = wait_bar(&s_tfull[b], (g >> 1) & 1, a.st) ? 1 : 0;
+                if (lane == 0) good = wait_bar(&s_tfull[b], (g / kAcc) & 1, a.st) ? 1 : 0;
                 if (!__shfl_sync(0xffffffffu, good, 0)) {
                     ok = false;
                     break;

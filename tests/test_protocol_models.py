@@ -7,7 +7,7 @@ interleavings of the roles, the rings whose ordering the kernels rely on:
   * the tile-id queue of the fused dispatch -> GEMM kernel (one producer, the MMA warp and eight
     epilogue warps, depth 4): every consumer reads every id in order, no slot is overwritten before
     all nine consumers read it, and the sentinel ends every consumer;
-  * the shared-memory stage ring (TMA producer -> MMA, depth S) and the two TMEM accumulators
+  * the shared-memory stage ring (TMA producer -> MMA, depth S) and the 2 or 4 TMEM accumulators
     (MMA -> eight epilogue warps) of the grouped GEMMs: stages and accumulators are never reused
     before they are released;
   * the pull ring of the fused kernel (slots freed kLag rows late, a failed wait partway, the
@@ -86,17 +86,19 @@ def test_tile_queue_protocol(seed):
 
 
 @pytest.mark.parametrize('seed', range(40))
-def test_stage_ring_and_accumulators(seed):
+@pytest.mark.parametrize('n_acc', [2, 4])
+def test_stage_ring_and_accumulators(seed, n_acc):
+    """n_acc TMEM accumulators rotate over the K blocks (the FP8 GEMM keeps 512 / N of them)."""
     rng = random.Random(seed)
     S, KB, tiles, epi = rng.choice([4, 6, 8]), rng.randint(1, 6), rng.randint(1, 6), 8
     full = [MBarrier(1) for _ in range(S)]
     empty = [MBarrier(1) for _ in range(S)]
-    tfull = [MBarrier(1) for _ in range(2)]
-    tempty = [MBarrier(epi) for _ in range(2)]
+    tfull = [MBarrier(1) for _ in range(n_acc)]
+    tempty = [MBarrier(epi) for _ in range(n_acc)]
     total = tiles * KB
     stage_owner = [None] * S     # k-block whose data is in the stage
-    acc_owner = [None] * 2       # k-block whose partial is in the accumulator
-    acc_reads = [0] * 2
+    acc_owner = [None] * n_acc   # k-block whose partial is in the accumulator
+    acc_reads = [0] * n_acc
     prod = {'g': 0}
     mma = {'g': 0}
     epis = [{'g': 0} for _ in range(epi)]
@@ -120,8 +122,8 @@ def test_stage_ring_and_accumulators(seed):
                 prod['g'] += 1
         elif a == 'm':
             g = mma['g']
-            s, b = g % S, g & 1
-            if _done(tempty[b], ((g >> 1) & 1) ^ 1) and _done(full[s], (g // S) & 1):
+            s, b = g % S, g % n_acc
+            if _done(tempty[b], ((g // n_acc) & 1) ^ 1) and _done(full[s], (g // S) & 1):
                 assert stage_owner[s] == g and acc_owner[b] is None
                 acc_owner[b] = g
                 acc_reads[b] = 0
@@ -132,8 +134,8 @@ def test_stage_ring_and_accumulators(seed):
         else:
             e = epis[a]
             g = e['g']
-            b = g & 1
-            if _done(tfull[b], (g >> 1) & 1):
+            b = g % n_acc
+            if _done(tfull[b], (g // n_acc) & 1):
                 assert acc_owner[b] == g, 'epilogue read an accumulator of another k-block'
                 acc_reads[b] += 1
                 if acc_reads[b] == epi:
