@@ -19,8 +19,10 @@ dispatch (send + hook) and per combine (send + hook), max over ranks, median ove
 
 Timing: CUDA events on the launching stream per step, L2 flushed (a 256 MiB write) before every
 timed step, barrier + synchronize on both sides, max over ranks. SM clocks are sampled with
-nvidia-smi during the timed region. `--impl reference` runs the unmodified reference if it is
-installed under baseline/_ref; it is not installable offline here and prints why.
+nvidia-smi during the timed region. `--impl reference` runs the unmodified reference through its
+own public API when `import deep_ep` from baseline/_ref succeeds; otherwise it prints why it is
+unavailable (the missing install or the import error). `--impl nccl` times the NCCL all-to-all
+baseline (`parallel.nccl_baseline`) on the same step.
 """
 import argparse
 import json
@@ -39,10 +41,26 @@ sys.path.insert(0, ROOT)
 
 METRIC = 'dispatch/combine NVLink GB/s (normal) + LL dispatch/combine us, 8xB200'
 BASELINE_CYCLE_GBPS_PER_RANK = 735.1
-REFERENCE_UNAVAILABLE = ('reference (swiss-ai/DeepEP_Slingshot) is not installable offline: its root has no '
-                         'setup.py/pyproject.toml, and its vendored DeepEP v2 source fails to build against '
-                         'NCCL 2.28.9 (no GIN/LSA device API: ncclCommProperties, ncclGetLsaDevicePointer) and '
-                         'NVSHMEM IBGDA (missing infiniband/mlx5dv.h)')
+# Outcome of the offline install into baseline/_ref (pip reports the root as not installable; the
+# vendored DeepEP v2 source does not compile here): printed when baseline/_ref is absent.
+REFERENCE_INSTALL_OUTCOME = ('the offline install failed: the reference root has no setup.py/pyproject.toml '
+                             '("not installable"), and its vendored DeepEP v2 source fails to build against NCCL '
+                             '2.28.9 (no GIN/LSA device API: ncclCommProperties, ncclGetLsaDevicePointer) and '
+                             'NVSHMEM IBGDA (missing infiniband/mlx5dv.h)')
+
+
+def reference_module():
+    """(deep_ep module, None) when the unmodified reference imports from baseline/_ref, else (None,
+    the reason it is unavailable): a missing install or the actual import error."""
+    ref_dir = os.path.join(ROOT, 'baseline', '_ref')
+    if not os.path.isdir(ref_dir):
+        return None, 'baseline/_ref is absent; ' + REFERENCE_INSTALL_OUTCOME
+    sys.path.insert(0, ref_dir)
+    try:
+        import deep_ep
+    except Exception as exc:  # report the real error, whatever the failing import raises
+        return None, f'import deep_ep from baseline/_ref failed: {exc!r}'
+    return deep_ep, None
 
 
 def parse():
@@ -212,10 +230,13 @@ def sum_over_ranks(v):
 
 def main():
     args = parse()
+    deep_ep = None
     if args.impl == 'reference':
-        if int(os.environ.get('RANK', '0')) == 0:  # one line per job, also under torchrun
-            print(json.dumps({'impl': 'reference', 'unavailable': REFERENCE_UNAVAILABLE}))
-        return 0
+        deep_ep, reason = reference_module()
+        if deep_ep is None:
+            if int(os.environ.get('RANK', '0')) == 0:  # one line per job, also under torchrun
+                print(json.dumps({'impl': 'reference', 'unavailable': reason}))
+            return 0
     rank, world, local = init(args)
     from deepep_slingshot_b200 import Buffer
     from deepep_slingshot_b200.utils import gate
@@ -233,25 +254,36 @@ def main():
     nvl_bytes = Buffer.get_nvl_buffer_size_hint(N, H, world)
     ll_bytes = 0 if args.no_ll else Buffer.get_low_latency_rdma_size_hint(args.ll_tokens, H, world, E)
 
+    cast = None  # the reference arm quantizes with its own cast, then dispatches the FP8 pair
     if args.impl == 'nccl':
         from deepep_slingshot_b200.parallel.nccl_baseline import NcclAllToAllEP
         buf = NcclAllToAllEP(dist.group.WORLD)
+    elif args.impl == 'reference':
+        # the unmodified reference through its own public API (stock code path, its own configs)
+        from deep_ep.utils.math import per_token_cast_to_fp8 as cast
+        buf = deep_ep.Buffer(dist.group.WORLD, num_nvl_bytes=nvl_bytes, num_rdma_bytes=0)
+        cfg = deep_ep.Buffer.get_dispatch_config(world)
     else:
         buf = Buffer(dist.group.WORLD, num_nvl_bytes=nvl_bytes, num_rdma_bytes=ll_bytes, low_latency_mode=ll_bytes > 0)
     y_full = torch.randn((N * world, H), generator=g).to(torch.bfloat16).cuda()
     state = {}
 
+    def layout_and_dispatch(xb, ids, wts):
+        """get_dispatch_layout + FP8 dispatch of bf16 tokens through the arm's public API (ours and
+        the NCCL baseline quantize inside the dispatch; the reference casts first with its own op)."""
+        ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(ids, E)
+        xin, kw = (cast(xb), {}) if cast is not None else (xb, {'quantize_fp8': True})
+        return buf.dispatch(xin, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe,
+                            topk_idx=ids, topk_weights=wts, config=cfg, **kw)
+
     def step():
-        ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(idx, E)
-        (rx, rs), ri, rw, lst, h, _ = buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
-                                                   num_tokens_per_expert=ntpe, topk_idx=idx, topk_weights=w,
-                                                   config=cfg, quantize_fp8=True)
+        (rx, rs), ri, rw, lst, h, _ = layout_and_dispatch(x, idx, w)
         state['mid'].record()
         out, out_w, _ = buf.combine(y_full[:rx.shape[0]], h, topk_weights=rw, config=cfg)
         state['num_recv'] = rx.shape[0]
         return out
 
-    if args.check:
+    if args.check and args.impl != 'reference':
         from deepep_slingshot_b200 import ReferenceBuffer
         ref = ReferenceBuffer(dist.group.WORLD)
         (rx, rs), ri, rw, lst, h, _ = buf.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, quantize_fp8=True)
@@ -476,10 +508,7 @@ def main():
             dx = hx.cuda(non_blocking=True)
             didx = hidx.cuda(non_blocking=True)
             dw = hw.cuda(non_blocking=True)
-            ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(didx, E)
-            (rx, rs), ri, rw, lst, h, _ = buf.dispatch(dx, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
-                                                       num_tokens_per_expert=ntpe, topk_idx=didx, topk_weights=dw,
-                                                       config=cfg, quantize_fp8=True)
+            (rx, rs), ri, rw, lst, h, _ = layout_and_dispatch(dx, didx, dw)
             out, _, _ = buf.combine(y_full[:rx.shape[0]], h, topk_weights=rw, config=cfg)
             hy.copy_(out.float().sum().view(1), non_blocking=True)
             t1.record()
@@ -524,10 +553,7 @@ def main():
                     issue_copy(i + 1)
                 comp.wait_event(copied[i % 2])
                 dx, didx, dw = bufs[i % 2]
-                ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(didx, E)
-                (rx, rs), ri, rw, lst, h, _ = buf.dispatch(dx, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
-                                                           num_tokens_per_expert=ntpe, topk_idx=didx, topk_weights=dw,
-                                                           config=cfg, quantize_fp8=True)
+                (rx, rs), ri, rw, lst, h, _ = layout_and_dispatch(dx, didx, dw)
                 freed[i % 2].record(comp)  # the dispatch (synchronous) has consumed the inputs
                 out, _, _ = buf.combine(y_full[:rx.shape[0]], h, topk_weights=rw, config=cfg)
                 hys[i:i + 1].copy_(out.float().sum().view(1), non_blocking=True)
@@ -574,7 +600,8 @@ def main():
             'dispatch_gbps_per_rank': disp_gbps_rank, 'combine_gbps_per_rank': comb_gbps_rank,
             'num_recv_tokens_rank0': num_recv,
             'clocks': clocks,
-            'gpu_launches': args.steps * 5 if args.impl == 'ours' else 0,
+            # this library's kernels per timed step: layout, dispatch count, stage + pull, combine
+            'gpu_launches': args.steps * 4 if args.impl == 'ours' else 0,
         }
         if os.environ.get('DEEPEP_B200_PROFILE') == '1' and hasattr(buf, 'get_profile'):
             line['kernel_profile_rank0'] = buf.get_profile()

@@ -298,6 +298,46 @@ def test_ep_benchmark_nccl_arm_options():
         with pytest.raises(SystemExit) as e:
             ep_benchmark.main(bad)
         assert e.value.code == 2
-    from deepep_slingshot_b200.parallel.nccl_baseline import NcclAllToAllEP
+
+
+def _nccl_baseline_body(rank, world):
+    import torch.distributed as dist
     from deepep_slingshot_b200 import ReferenceBuffer
-    assert issubclass(NcclAllToAllEP, ReferenceBuffer)
+    from deepep_slingshot_b200.parallel.nccl_baseline import NcclAllToAllEP
+    from deepep_slingshot_b200.utils.gate import normal_routing
+    N, H, E, K = 96 - 7 * rank, 256, 8 * world, 4
+    g = torch.Generator().manual_seed(3 + rank)
+    x = torch.randn((N, H), generator=g).to(torch.bfloat16)
+    idx, w = normal_routing(N, E, K, generator=g)
+    idx[5] = -1  # a token routed nowhere
+    base, ref = NcclAllToAllEP(dist.group.WORLD), ReferenceBuffer(dist.group.WORLD)
+    a, b = base.get_dispatch_layout(idx, E), ref.get_dispatch_layout(idx, E)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
+    for fp8 in (False, True):
+        ox, oi, ow, ol, oh, _ = base.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, quantize_fp8=fp8,
+                                              expert_alignment=4)
+        ex, ei, ew, el, eh, _ = ref.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, quantize_fp8=fp8,
+                                             expert_alignment=4)
+        if fp8:
+            assert torch.equal(ox[0].view(torch.uint8), ex[0].view(torch.uint8)) and torch.equal(ox[1], ex[1])
+            ox, ex = ox[0], ex[0]
+        else:
+            assert torch.equal(ox, ex)
+        assert torch.equal(oi, ei) and torch.equal(ow, ew) and ol == el
+        assert torch.equal(oh[3], eh[3]) and torch.equal(oh[4], eh[4]) and torch.equal(oh[5], eh[5])
+        cx, *_ = base.dispatch((x, None)[0], handle=oh)  # cached: same rows without the routing
+        assert torch.equal(cx, ref.dispatch(x, handle=eh)[0])
+        y = (torch.randn((ox.shape[0], H), generator=g)).to(torch.bfloat16)
+        bias = torch.randn((N, H), generator=g).to(torch.bfloat16)
+        o, o_w, _ = base.combine(y, oh, topk_weights=ow, bias=bias)
+        e, e_w, _ = ref.combine(y, eh, topk_weights=ew, bias=bias)
+        assert torch.allclose(o.float(), e.float(), atol=1e-2, rtol=1e-2) and torch.allclose(o_w, e_w, atol=1e-6)
+    px, pi, *_ = base.dispatch(x, topk_idx=idx, topk_weights=w, num_experts=E, num_worst_tokens=N * world)
+    assert px.shape[0] == N * world and bool((pi[oi.shape[0]:] == -1).all())
+
+
+def test_nccl_baseline_matches_oracle_gloo():
+    """The NCCL baseline arm is its own implementation; on gloo ranks it must return exactly what
+    the oracle returns (receive order, handle fields, combine sums), so its timings compare."""
+    from tests._dist import run_ranks
+    run_ranks(_nccl_baseline_body, 2, 'gloo')
