@@ -455,9 +455,12 @@ def main():
                               'routing': 'zipf s=1.1', 'grads': 'set to None before every step (zero_grad(set_to_none=True))',
                               'forward': 'fp8 block-scaled tcgen05 grouped GEMMs' +
                               (', dispatch receive fused into the gate/up GEMM' if args.moe_fused_dispatch else ''),
-                              'backward': ('bf16 tcgen05 grouped GEMMs (dgrad M-grouped, wgrad K-grouped)' if _moe_mod._GROUPED_BWD['tcgen05']
-                                           else 'bf16 torch grouped GEMMs (library stand-in)' if _moe_mod._GROUPED_BWD['enabled']
-                                           else 'bf16 per-expert torch matmuls (stand-in)'),
+                              'backward': {'tcgen05_mn': 'bf16 tcgen05 grouped GEMMs on MN-major operands (no transposes), '
+                                                         'fused SwiGLU and unpermute backward kernels',
+                                           'tcgen05': 'bf16 tcgen05 grouped GEMMs on transposed (K-major) operands',
+                                           'grouped': 'bf16 torch grouped GEMMs (library stand-in, A/B only)',
+                                           'loop': 'bf16 per-expert torch matmuls (stand-in)'}.get(_moe_mod._BWD['mode'],
+                                                                                              _moe_mod._BWD['mode']),
                               'roofline': ('slowest rank of max(its fp8 fwd at 2x bf16 peak + bf16 bwd at measured '
                                            '1650 TFLOP/s over its expert rows, its NVLink bytes per direction at 770 GB/s, '
                                            '8 bytes per local weight element per step at measured 6558 GB/s HBM)')}}

@@ -132,6 +132,23 @@ struct CombineArgs {
 };
 void launch_combine(const CombineArgs& a, int num_sms, cudaStream_t stream);
 
+// ---------------------------------------------------------------- MoE backward helpers
+// g_y[row_map[j][k]] = bf16(g_tok[j] * w[j][k]) and g_w[j][k] = <g_tok[j], y[row_map[j][k]]> (0 for
+// row -1); K <= 16. g_y rows that no slot names are left as they are (the caller zeroes them).
+void launch_unpermute_backward(const void* g_tok, const int* row_map, const float* w, const void* y, int N, int H, int K,
+                               int y_rows, void* g_y, float* g_w, KernelStatus st, cudaStream_t stream);
+// SwiGLU backward: h [rows][2I] (gate | up), g_a [rows][I] -> g_h [rows][2I], all bf16, I % 8 == 0.
+void launch_swiglu_backward(const void* h, const void* g_a, int64_t rows, int inter, void* g_h, cudaStream_t stream);
+// Zero the padding rows [offsets[e] + counts[e], offsets[e + 1]) of up to three grouped tensors.
+struct ZeroPaddingArgs {
+    void* ptr[3];
+    int64_t row_bytes[3];  // multiples of 16
+    int num_tensors;
+    const int* offsets;    // [E + 1]
+    const int* counts;     // [E]
+};
+void launch_zero_group_padding(const ZeroPaddingArgs& a, int num_groups, cudaStream_t stream);
+
 // ---------------------------------------------------------------- transport-contract checks
 // Multi-producer signalling: producer_blocks x warps warps each add 1 to *peer_flag `rounds` times
 // (sys-scope release reductions); one more block waits (bounded) until *my_flag == expected and

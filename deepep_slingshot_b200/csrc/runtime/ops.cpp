@@ -308,9 +308,62 @@ torch::Tensor unpermute(const torch::Tensor& y, const torch::Tensor& row_map, co
     return out;
 }
 
+// MoE backward: g_y (caller-zeroed, [rows, H] bf16) receives bf16(g_tok[j] * w[j][k]) at row_map[j][k];
+// returns g_w [N, K] fp32 = <g_tok[j], y[row_map[j][k]]> (0 where row_map is -1).
+torch::Tensor unpermute_backward(const torch::Tensor& g_tok, const torch::Tensor& row_map, const torch::Tensor& w,
+                                 const torch::Tensor& y, torch::Tensor& g_y) {
+    TORCH_CHECK(g_tok.is_cuda() && g_tok.dim() == 2 && g_tok.is_contiguous() && g_tok.scalar_type() == torch::kBFloat16);
+    TORCH_CHECK(row_map.scalar_type() == torch::kInt32 && row_map.is_contiguous() && row_map.dim() == 2);
+    const int N = (int)row_map.size(0), K = (int)row_map.size(1), H = (int)g_tok.size(1);
+    TORCH_CHECK(g_tok.size(0) >= N, "g_tok must cover every row of row_map");
+    TORCH_CHECK(K <= kMaxTopk && H % 8 == 0, "top-k <= 16 and hidden % 8 == 0");
+    TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(0) == N && w.size(1) == K);
+    for (const torch::Tensor* t : {&y, static_cast<const torch::Tensor*>(&g_y)})
+        TORCH_CHECK(t->is_cuda() && t->dim() == 2 && t->is_contiguous() && t->scalar_type() == torch::kBFloat16 && t->size(1) == H);
+    TORCH_CHECK(g_y.size(0) == y.size(0), "g_y and y have the same rows");
+    auto g_w = torch::empty({N, K}, w.options());
+    launch_unpermute_backward(g_tok.data_ptr(), row_map.data_ptr<int>(), w.data_ptr<float>(), y.data_ptr(), N, H, K,
+                              (int)y.size(0), g_y.data_ptr(), g_w.data_ptr<float>(), op_status(10.0),
+                              at::cuda::getCurrentCUDAStream());
+    return g_w;
+}
+
+torch::Tensor swiglu_backward(const torch::Tensor& h, const torch::Tensor& g_a) {
+    TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.is_contiguous() && h.scalar_type() == torch::kBFloat16);
+    const int64_t rows = h.size(0);
+    const int inter = (int)h.size(1) / 2;
+    TORCH_CHECK(h.size(1) % 16 == 0, "2*intermediate must be a multiple of 16");
+    TORCH_CHECK(g_a.is_contiguous() && g_a.scalar_type() == torch::kBFloat16 && g_a.dim() == 2 && g_a.size(0) == rows &&
+                g_a.size(1) == inter);
+    auto g_h = torch::empty_like(h);
+    launch_swiglu_backward(h.data_ptr(), g_a.data_ptr(), rows, inter, g_h.data_ptr(), at::cuda::getCurrentCUDAStream());
+    return g_h;
+}
+
+void zero_group_padding(const std::vector<torch::Tensor>& tensors, const torch::Tensor& offsets, const torch::Tensor& counts) {
+    TORCH_CHECK(tensors.size() <= 3, "at most three tensors per call");
+    TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && counts.scalar_type() == torch::kInt32 && offsets.is_contiguous() &&
+                counts.is_contiguous() && offsets.numel() == counts.numel() + 1);
+    ZeroPaddingArgs a{};
+    for (size_t i = 0; i < tensors.size(); ++i) {
+        const auto& t = tensors[i];
+        TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.is_contiguous(), "grouped tensors must be contiguous 2D CUDA tensors");
+        a.ptr[i] = t.data_ptr();
+        a.row_bytes[i] = t.size(1) * t.element_size();
+        TORCH_CHECK(a.row_bytes[i] % 16 == 0, "row bytes must be a multiple of 16");
+    }
+    a.num_tensors = (int)tensors.size();
+    a.offsets = offsets.data_ptr<int>();
+    a.counts = counts.data_ptr<int>();
+    launch_zero_group_padding(a, (int)counts.numel(), at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace
 
 void register_ops(pybind11::module_& m) {
+    m.def("unpermute_backward", &unpermute_backward);
+    m.def("swiglu_backward", &swiglu_backward);
+    m.def("zero_group_padding", &zero_group_padding);
     m.def("permute", &permute, pybind11::arg("x"), pybind11::arg("x_scales"), pybind11::arg("topk_idx"), pybind11::arg("probs"),
           pybind11::arg("num_experts"), pybind11::arg("alignment") = 1, pybind11::arg("num_out_rows") = 0,
           pybind11::arg("zero_padding") = false);

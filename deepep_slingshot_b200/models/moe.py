@@ -5,11 +5,12 @@ Forward per rank (every step on hand-written sm_100a kernels):
   grouped FP8 GEMM gate/up (tcgen05, 1x128 x 128x128 block scales) -> fused SwiGLU + FP8 requant ->
   grouped FP8 GEMM down -> combine with the top-k weighted reduction of each token's grouped rows
   fused into its sender side (one kernel: weighted fp32 sum, bf16 cast, NVLink push, sum over ranks).
-Backward: combine^T = cached dispatch of the output gradient; dispatch^T = combine; the expert
-GEMM gradients run in bf16 (straight-through through the FP8 quantization) as grouped GEMMs over the
-aligned expert groups: torch's grouped bf16 GEMM by default (a library stand-in), this library's
-tcgen05 grouped bf16 GEMMs with DEEPEP_B200_MOE_BWD=tcgen05 (input gradients M-grouped, weight
-gradients K-grouped over the expert row ranges), per-expert matmuls with `loop`.
+Backward: combine^T = cached dispatch of the output gradient; unpermute^T (the gradient scattered to
+the grouped rows, scaled by the routing weights, and the routing weights' gradient in one kernel);
+the expert GEMM gradients in bf16 (straight-through through the FP8 quantization) as this library's
+tcgen05 grouped GEMMs with MN-major operands (no transposes) and the fused SwiGLU backward kernel;
+permute^T + dispatch^T = the weighted-expanded combine. Every alignment padding row stays zero, so
+the grouped GEMMs run over whole 128-row groups without masks.
 
 The reference library has no model layer (its expert compute is SGLang + DeepGEMM,
 backend/tests/sglang_dispatcher_smoke.py:107-124); this is the flagship workload of the benchmark
@@ -22,83 +23,71 @@ from typing import Optional
 import torch
 
 from ..ops.gemm import grouped_gemm_fp8, quantize_weights_fp8
-from ..ops.permute import permute
+from ..ops.permute import permute, unpermute_backward, zero_group_padding
+from ..ops.quant import per_token_cast_back, swiglu_backward
 from .._ext import require_ext
 
 
-def _expert_rows(offsets: torch.Tensor, counts: torch.Tensor):
-    off = offsets.tolist()
-    cnt = counts.tolist()
-    return [(off[e], off[e] + cnt[e]) for e in range(len(cnt))]
-
-
-# Backward expert GEMMs: `grouped` (torch's grouped bf16 GEMM, default), `tcgen05` (this library's
-# kernels with K-major operands, so the weights and activations are transposed every step: with 256
-# local experts on one GPU that costs ~45 GB of copies and made the step 2x slower, measured 107 vs
-# 52 ms), `tcgen05_mn` (the same kernels reading the weights and activations as they lie, through
-# MN-major operand descriptors: no transposes), `loop` (per-expert matmuls).
+# Backward expert GEMMs: `tcgen05_mn` (default: this library's tcgen05 grouped bf16 GEMMs reading the
+# weights and activations as they lie through MN-major operand descriptors, no transposes), `tcgen05`
+# (the same kernels with K-major operands: the weights are transposed every step), `grouped`
+# (torch's grouped bf16 GEMM, a library stand-in kept for A/B), `loop` (per-expert matmuls).
 # DEEPEP_B200_MOE_FUSED_DISPATCH=1: the forward's dispatch receive and gate/up GEMM run as one kernel
 # (Buffer.dispatch_gemm) instead of dispatch -> permute -> grouped GEMM.
 _FUSED_DISPATCH = {'enabled': os.environ.get('DEEPEP_B200_MOE_FUSED_DISPATCH', '0') == '1'}
-_BWD_MODE = os.environ.get('DEEPEP_B200_MOE_BWD', 'grouped')
-_GROUPED_BWD = {'enabled': _BWD_MODE in ('tcgen05', 'tcgen05_mn', 'grouped'),
-                'tcgen05': _BWD_MODE in ('tcgen05', 'tcgen05_mn'), 'mn_major': _BWD_MODE == 'tcgen05_mn'}
+_BWD = {'mode': os.environ.get('DEEPEP_B200_MOE_BWD', 'tcgen05_mn')}
 
 
-def _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx) -> bool:
-    """Expert GEMM gradients as four grouped bf16 GEMMs over whole 128-aligned groups: torch's grouped
-    GEMM by default (`grouped`), this library's tcgen05 kernels with DEEPEP_B200_MOE_BWD=tcgen05.
-    Padding rows are masked to zero so they contribute nothing. Returns False (and the caller loops
-    over experts) for `loop` or when torch's grouped GEMM is unavailable."""
-    if not _GROUPED_BWD['enabled']:
-        return False
-    if not _GROUPED_BWD['tcgen05'] and not hasattr(torch, '_grouped_mm'):
-        return False
-    R = int(offsets[-1].item())
-    offs = offsets[1:].to(torch.int32).contiguous()
-    live = torch.zeros((R, 1), dtype=torch.bool, device=g_y.device)
-    live[rows[rows < R]] = True
-    zero = torch.zeros((), dtype=torch.bfloat16, device=g_y.device)
-    gy = g_y[:R]
-    aa = torch.where(live, a[:R], zero)
-    hh = torch.where(live, h[:R], zero).float()
-    xx = torch.where(live, xf[:R], zero)
-    gate, up = hh[:, :inter], hh[:, inter:]
-    s = torch.sigmoid(gate)
-    if _GROUPED_BWD['tcgen05']:
-        # sm_100a kernels: dgrad M-grouped against K-major (transposed) weights, wgrad K-grouped over
-        # the expert row ranges of the transposed activations.
+def _aligned_rows(per_expert, alignment: int = 128) -> int:
+    """Rows of the expert-grouped layout from the host's per-expert counts (no device read)."""
+    return sum((c + alignment - 1) // alignment * alignment for c in per_expert)
+
+
+def _expert_grads(g_y, a, h, xf, offsets, counts, w1, w2, inter):
+    """(g_xp [R, H], g_w1, g_w2) of the expert FFNs over the grouped rows [0, R): padding rows of every
+    operand are zero, so whole 128-aligned groups can be multiplied. The SwiGLU backward is the
+    library's kernel in every mode."""
+    offs32 = offsets.to(torch.int32).contiguous()
+    mode = _BWD['mode']
+    if mode in ('tcgen05_mn', 'tcgen05'):
         from ..ops.gemm import grouped_gemm_bf16, grouped_gemm_bf16_wgrad, grouped_gemm_bf16_wgrad_rows
-        offs32 = offsets.to(torch.int32).contiguous()
-        if _GROUPED_BWD['mn_major']:
-            g_a = grouped_gemm_bf16(gy, w2, offs32, counts, b_mn_major=True).float()                 # [R, I]
-            g_w2 = grouped_gemm_bf16_wgrad_rows(gy, aa, offs32)                                       # [E, H, I]
-            g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
-            g_xp[:R] = grouped_gemm_bf16(g_h, w1, offs32, counts, b_mn_major=True)                   # [R, H]
-            ctx.g_w1, ctx.g_w2 = grouped_gemm_bf16_wgrad_rows(g_h, xx, offs32), g_w2                 # [E, 2I, H]
-            return True
-        g_a = grouped_gemm_bf16(gy, w2.transpose(1, 2).contiguous(), offs32, counts).float()          # [R, I]
-        g_w2 = grouped_gemm_bf16_wgrad(gy.t().contiguous(), aa.t().contiguous(), offs32)            # [E, H, I]
-        g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
-        g_xp[:R] = grouped_gemm_bf16(g_h, w1.transpose(1, 2).contiguous(), offs32, counts)           # [R, H]
-        g_w1 = grouped_gemm_bf16_wgrad(g_h.t().contiguous(), xx.t().contiguous(), offs32)           # [E, 2I, H]
-        ctx.g_w1, ctx.g_w2 = g_w1, g_w2
-        return True
-    try:
-        g_a = torch._grouped_mm(gy, w2, offs=offs).float()                         # [R, I]
-        g_w2 = torch._grouped_mm(gy.t(), aa, offs=offs)                            # [E, H, I]
-        g_h = torch.cat([g_a * up * s * (1 + gate * (1 - s)), g_a * gate * s], dim=1).to(torch.bfloat16)
-        g_xp[:R] = torch._grouped_mm(g_h, w1, offs=offs)                           # [R, H]
-        g_w1 = torch._grouped_mm(g_h.t(), xx, offs=offs)                           # [E, 2I, H]
-    except (RuntimeError, NotImplementedError):
-        _GROUPED_BWD['enabled'] = False
-        return False
-    empty = counts == 0
-    if bool(empty.any()):
+        if mode == 'tcgen05_mn':
+            g_a = grouped_gemm_bf16(g_y, w2, offs32, counts, b_mn_major=True)             # [R, I]
+            g_w2 = grouped_gemm_bf16_wgrad_rows(g_y, a, offs32)                           # [E, H, I]
+            g_h = swiglu_backward(h, g_a)                                                 # [R, 2I]
+            g_xp = grouped_gemm_bf16(g_h, w1, offs32, counts, b_mn_major=True)            # [R, H]
+            g_w1 = grouped_gemm_bf16_wgrad_rows(g_h, xf, offs32)                          # [E, 2I, H]
+            return g_xp, g_w1, g_w2
+        g_a = grouped_gemm_bf16(g_y, w2.transpose(1, 2).contiguous(), offs32, counts)
+        g_w2 = grouped_gemm_bf16_wgrad(g_y.t().contiguous(), a.t().contiguous(), offs32)
+        g_h = swiglu_backward(h, g_a)
+        g_xp = grouped_gemm_bf16(g_h, w1.transpose(1, 2).contiguous(), offs32, counts)
+        g_w1 = grouped_gemm_bf16_wgrad(g_h.t().contiguous(), xf.t().contiguous(), offs32)
+        return g_xp, g_w1, g_w2
+    if mode == 'grouped' and hasattr(torch, '_grouped_mm'):
+        offs = offs32[1:]
+        g_a = torch._grouped_mm(g_y, w2, offs=offs)
+        g_w2 = torch._grouped_mm(g_y.t(), a, offs=offs)
+        g_h = swiglu_backward(h, g_a.contiguous())
+        g_xp = torch._grouped_mm(g_h, w1, offs=offs)
+        g_w1 = torch._grouped_mm(g_h.t(), xf, offs=offs)
+        empty = counts == 0
         g_w1[empty] = 0
         g_w2[empty] = 0
-    ctx.g_w1, ctx.g_w2 = g_w1.contiguous(), g_w2.contiguous()
-    return True
+        return g_xp, g_w1.contiguous(), g_w2.contiguous()
+    g_xp = torch.zeros_like(xf)
+    g_w1, g_w2 = torch.zeros_like(w1), torch.zeros_like(w2)
+    off, cnt = offsets.tolist(), counts.tolist()
+    for e in range(w1.shape[0]):
+        r0, r1 = off[e], off[e] + cnt[e]
+        if r1 <= r0:
+            continue
+        g_a = g_y[r0:r1] @ w2[e]
+        g_w2[e] = g_y[r0:r1].t() @ a[r0:r1]
+        g_h = swiglu_backward(h[r0:r1].contiguous(), g_a.contiguous())
+        g_xp[r0:r1] = g_h @ w1[e]
+        g_w1[e] = g_h.t() @ xf[r0:r1]
+    return g_xp, g_w1, g_w2
 
 
 class _MoEFunction(torch.autograd.Function):
@@ -115,10 +104,16 @@ class _MoEFunction(torch.autograd.Function):
             p = SimpleNamespace(x=grp['x'], scales=grp['scales'], row_map=grp['row_map'],
                                 expert_offsets=grp['expert_offsets'], expert_counts=grp['expert_counts'])
             rw = grp['topk_weights']
+            rows = _aligned_rows(grp['num_recv_tokens_per_expert_list'], 1)
+            # The fused receive leaves the alignment padding of its operand unwritten: zero it (and
+            # the GEMM's rows computed from it) so the padding stays zero through the layer.
+            zero_group_padding([p.x, p.scales, h], p.expert_offsets, p.expert_counts)
         else:
-            (rxq, rxs), ridx, rw, _, handle, _ = buffer.dispatch(x, topk_idx=topk_idx, topk_weights=topk_weights,
-                                                                 num_experts=num_experts, quantize_fp8=True, config=config)
-            p = permute(rxq, ridx, E_l, alignment=128, probs=rw, x_scales=rxs)
+            (rxq, rxs), ridx, rw, per_expert, handle, _ = buffer.dispatch(
+                x, topk_idx=topk_idx, topk_weights=topk_weights, num_experts=num_experts, quantize_fp8=True,
+                config=config)
+            p = permute(rxq, ridx, E_l, alignment=128, probs=rw, x_scales=rxs, zero_padding=True)
+            rows = _aligned_rows(per_expert)
             w1q, w1s = quantize_weights_fp8(w1.detach())
             h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts)
         a, aq, as_ = require_ext().swiglu_quant(h, False)
@@ -126,7 +121,7 @@ class _MoEFunction(torch.autograd.Function):
         y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts)
         # Top-k weighted reduction of the grouped rows, bf16 cast and exchange in one kernel.
         out, _, _ = buffer.combine(y, handle, config=config, row_map=p.row_map, row_weights=rw)
-        ctx.buffer, ctx.config, ctx.inter = buffer, config, inter
+        ctx.buffer, ctx.config, ctx.inter, ctx.rows = buffer, config, inter, rows
         ctx.handle = handle
         ctx.save_for_backward(p.x, p.scales, p.row_map, p.expert_offsets, p.expert_counts, rw, h, a, y, w1, w2)
         return out
@@ -134,40 +129,16 @@ class _MoEFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_out):
         xp, xs, row_map, offsets, counts, rw, h, a, y, w1, w2 = ctx.saved_tensors
-        buffer, config, inter = ctx.buffer, ctx.config, ctx.inter
+        buffer, config, inter, R = ctx.buffer, ctx.config, ctx.inter, ctx.rows
         g_out = g_out.contiguous().to(torch.bfloat16)
         # combine^T: send the output gradient to the ranks that computed each token (cached layout)
         g_tok, *_ = buffer.dispatch(g_out, handle=ctx.handle, config=config)
-        valid = row_map >= 0
-        rows = row_map[valid].long()
-        t_of = torch.arange(row_map.shape[0], device=g_out.device).unsqueeze(1).expand_as(row_map)[valid]
         # unpermute^T: grouped output gradient (scaled by the routing weight) and the weight gradient
-        g_y = torch.zeros_like(y)
-        g_y[rows] = (g_tok[t_of].float() * rw[valid].unsqueeze(1)).to(torch.bfloat16)
-        g_rw = torch.zeros_like(rw)
-        g_rw[valid] = (g_tok[t_of].float() * y[rows].float()).sum(-1)
-        xf = (xp.float().view(xp.shape[0], -1, 128) * xs.unsqueeze(-1)).view(xp.shape).to(torch.bfloat16)
-        g_xp = torch.zeros_like(xf)
-        if not _grouped_backward(g_y, a, h, xf, rows, offsets, counts, w1, w2, inter, g_xp, ctx):
-            gate, up = h[:, :inter].float(), h[:, inter:].float()
-            sig = torch.sigmoid(gate)
-            g_w1 = torch.zeros_like(w1)
-            g_w2 = torch.zeros_like(w2)
-            for e, (r0, r1) in enumerate(_expert_rows(offsets, counts)):
-                if r1 <= r0:
-                    continue
-                gy = g_y[r0:r1]
-                g_a = gy @ w2[e]                                   # [m, H] x [H, I]
-                g_w2[e] = gy.t() @ a[r0:r1]                        # [H, m] x [m, I]
-                s, gt, u = sig[r0:r1], gate[r0:r1], up[r0:r1]
-                gaf = g_a.float()
-                g_h = torch.cat([gaf * u * s * (1 + gt * (1 - s)), gaf * gt * s], dim=1).to(torch.bfloat16)
-                g_xp[r0:r1] = g_h @ w1[e]                          # [m, 2I] x [2I, H]
-                g_w1[e] = g_h.t() @ xf[r0:r1]                      # [2I, m] x [m, H]
-        else:
-            g_w1, g_w2 = ctx.g_w1, ctx.g_w2
-            del ctx.g_w1, ctx.g_w2
-        # permute^T (sum the k copies of each received token) fused with dispatch^T = combine (sum over ranks)
+        g_y = torch.zeros((R, y.shape[1]), dtype=torch.bfloat16, device=y.device)
+        g_rw = unpermute_backward(g_tok, row_map, rw, y[:R], g_y)
+        xf = per_token_cast_back(xp[:R], xs[:R])  # zero padding rows dequantize to zero
+        g_xp, g_w1, g_w2 = _expert_grads(g_y, a[:R], h[:R], xf, offsets, counts, w1, w2, inter)
+        # permute^T (sum of each received token's rows) fused with dispatch^T = combine (sum over ranks)
         g_x, g_topk_w, _ = buffer.combine(g_xp, ctx.handle, topk_weights=g_rw, config=config, row_map=row_map)
         return g_x, None, g_topk_w, g_w1, g_w2, None, None, None
 

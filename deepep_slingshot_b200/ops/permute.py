@@ -55,3 +55,29 @@ def unpermute_reference(y: torch.Tensor, row_map: torch.Tensor, weights: Optiona
     valid = row_map >= 0
     g = y[row_map.clamp(min=0).long()].float() * (w * valid).unsqueeze(-1)
     return g.sum(1).to(torch.bfloat16)
+
+
+def unpermute_backward(g_tok: torch.Tensor, row_map: torch.Tensor, weights: torch.Tensor, y: torch.Tensor,
+                       g_y: torch.Tensor) -> torch.Tensor:
+    """Backward of the weighted unpermute (sm_100a kernel): writes `g_y[row_map[j, k]] =
+    bf16(g_tok[j] * weights[j, k])` into the caller's zeroed `g_y` and returns the weight gradient
+    `[N, K]` fp32, `<g_tok[j], y[row_map[j, k]]>` (0 where row_map is -1)."""
+    return require_ext().unpermute_backward(g_tok, row_map, weights, y, g_y)
+
+
+def unpermute_backward_reference(g_tok: torch.Tensor, row_map: torch.Tensor, weights: torch.Tensor, y: torch.Tensor):
+    """Torch oracle of `unpermute_backward` (fp32 math): returns (g_y, g_w)."""
+    valid = row_map >= 0
+    rows = row_map[valid].long()
+    t_of = torch.arange(row_map.shape[0], device=g_tok.device).unsqueeze(1).expand_as(row_map)[valid]
+    g_y = torch.zeros_like(y)
+    g_y[rows] = (g_tok[t_of].float() * weights[valid].unsqueeze(1)).to(torch.bfloat16)
+    g_w = torch.zeros_like(weights)
+    g_w[valid] = (g_tok[t_of].float() * y[rows].float()).sum(-1)
+    return g_y, g_w
+
+
+def zero_group_padding(tensors, offsets: torch.Tensor, counts: torch.Tensor) -> None:
+    """Zero the alignment padding rows `[offsets[e] + counts[e], offsets[e + 1])` of up to three
+    expert-grouped 2D tensors in place (sm_100a kernel)."""
+    require_ext().zero_group_padding(list(tensors), offsets, counts)

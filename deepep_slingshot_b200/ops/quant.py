@@ -33,3 +33,17 @@ def swiglu_quant_reference(h: torch.Tensor, round_scale: bool = False):
     a = (torch.nn.functional.silu(hf[..., :inter]) * hf[..., inter:]).to(torch.bfloat16)
     aq, as_ = cast(a.reshape(-1, inter), round_scale)
     return a, aq.view(a.shape), as_.view(*a.shape[:-1], inter // 128)
+
+
+def swiglu_backward(h: torch.Tensor, g_a: torch.Tensor) -> torch.Tensor:
+    """SwiGLU backward on sm_100a: `h [rows, 2I]` (gate | up) and the gradient of `a = silu(gate) * up`
+    `g_a [rows, I]` (bf16) -> `g_h [rows, 2I]` bf16 (fp32 math)."""
+    return require_ext().swiglu_backward(h, g_a)
+
+
+def swiglu_backward_reference(h: torch.Tensor, g_a: torch.Tensor) -> torch.Tensor:
+    """Torch oracle of `swiglu_backward` (fp32 math, bf16 result)."""
+    inter = h.shape[1] // 2
+    gate, up, ga = h[:, :inter].float(), h[:, inter:].float(), g_a.float()
+    s = torch.sigmoid(gate)
+    return torch.cat([ga * up * s * (1 + gate * (1 - s)), ga * gate * s], dim=1).to(torch.bfloat16)

@@ -26,6 +26,7 @@ SOURCES = [
     os.path.join(CSRC, "kernels", "fused_dispatch_gemm.cu"),
     os.path.join(CSRC, "kernels", "symmetric_ops.cu"),
     os.path.join(CSRC, "kernels", "transport_checks.cu"),
+    os.path.join(CSRC, "kernels", "moe_backward.cu"),
 ]
 
 NVCC_FLAGS = [

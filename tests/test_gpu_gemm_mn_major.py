@@ -52,10 +52,8 @@ def test_wgrad_mn_major_rows():
 
 
 def _moe_mn_body(rank, world, *args):
-    from deepep_slingshot_b200.models import moe as moe_mod
     from tests.test_gpu_moe import _moe_body
-    moe_mod._GROUPED_BWD['mn_major'] = True
-    _moe_body(rank, world, *args, bwd='tcgen05')
+    _moe_body(rank, world, *args, bwd='tcgen05_mn')
 
 
 @pytest.mark.parametrize('world', [1, 2])

@@ -28,11 +28,11 @@ def _ref_autograd(x, idx, w, w1_all, w2_all):
     return out
 
 
-def _moe_body(rank, world, N, H, I, E, K, bwd='grouped'):
+def _moe_body(rank, world, N, H, I, E, K, bwd='tcgen05_mn'):
     from deepep_slingshot_b200 import Buffer
     from deepep_slingshot_b200.models import MoEFFN, moe_reference
     from deepep_slingshot_b200.models import moe as moe_mod
-    moe_mod._GROUPED_BWD.update(enabled=bwd != 'loop', tcgen05=bwd == 'tcgen05')
+    moe_mod._BWD['mode'] = bwd
     from deepep_slingshot_b200.utils import gate
     from deepep_slingshot_b200.utils.math import calc_diff
     group = dist.group.WORLD
@@ -78,8 +78,9 @@ def _moe_body(rank, world, N, H, I, E, K, bwd='grouped'):
 
 
 @pytest.mark.parametrize('world', _worlds())
-@pytest.mark.parametrize('bwd', ['grouped', 'tcgen05'])
+@pytest.mark.parametrize('bwd', ['tcgen05_mn', 'tcgen05', 'grouped', 'loop'])
 def test_moe_layer_forward_backward(world, bwd):
     """Forward against the quantization-aware oracle; backward gradients (x, routing weights, w1, w2)
-    against fp32 autograd, with the backward GEMMs on torch's grouped GEMM or the tcgen05 kernels."""
+    against fp32 autograd, with the backward GEMMs on the tcgen05 kernels (MN-major operands, the
+    default, or K-major), torch's grouped GEMM (A/B stand-in) or per-expert matmuls."""
     run_ranks(_moe_body, world, 'nccl', args=(256, 1024, 512, 16, 4, bwd))

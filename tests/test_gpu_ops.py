@@ -56,3 +56,53 @@ def test_permute_zero_padding():
     for e in range(E):
         pad = slice(off[e] + cnt[e], off[e + 1])
         assert (p.x[pad].view(torch.uint8) == 0).all() and (p.scales[pad] == 0).all()
+
+
+@pytest.mark.parametrize('K', [8, 12])
+def test_unpermute_backward_matches_torch(K):
+    """g_y scatter (bf16(g * w)) exactly, routing-weight gradient (fp32 dots) within fp32 tolerance."""
+    from deepep_slingshot_b200.ops.permute import permute, unpermute_backward, unpermute_backward_reference
+    g = torch.Generator().manual_seed(K)
+    N, H, E = 700, 7168, 16
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)]).cuda()
+    idx[torch.rand((N, K), generator=g).cuda() < 0.3] = -1
+    w = torch.rand((N, K), generator=g).cuda()
+    x = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
+    p = permute(x, idx, E, alignment=128, probs=w, zero_padding=True)
+    R = int(p.expert_offsets[-1])
+    y = torch.randn((R, H), generator=g).to(torch.bfloat16).cuda()
+    g_tok = torch.randn((N, H), generator=g).to(torch.bfloat16).cuda()
+    g_y = torch.zeros_like(y)
+    g_w = unpermute_backward(g_tok, p.row_map, w, y, g_y)
+    ref_gy, ref_gw = unpermute_backward_reference(g_tok, p.row_map, w, y)
+    torch.cuda.synchronize()
+    assert torch.equal(g_y, ref_gy)
+    assert torch.allclose(g_w, ref_gw, rtol=1e-4, atol=1e-2), (g_w - ref_gw).abs().max()
+    assert bool((g_w[p.row_map < 0] == 0).all())
+
+
+def test_swiglu_backward_matches_torch():
+    from deepep_slingshot_b200.ops.quant import swiglu_backward, swiglu_backward_reference
+    g = torch.Generator().manual_seed(5)
+    h = (torch.randn((1000, 4096), generator=g) * 3).to(torch.bfloat16).cuda()
+    g_a = torch.randn((1000, 2048), generator=g).to(torch.bfloat16).cuda()
+    got = swiglu_backward(h, g_a)
+    exp = swiglu_backward_reference(h, g_a)
+    torch.cuda.synchronize()
+    # fp32 math on both sides; the kernel's exp and division round differently from torch's: one bf16 ulp
+    assert torch.allclose(got.float(), exp.float(), rtol=1e-2, atol=1e-3), (got.float() - exp.float()).abs().max()
+
+
+def test_zero_group_padding():
+    from deepep_slingshot_b200.ops.permute import zero_group_padding
+    offsets = torch.tensor([0, 128, 128, 384], dtype=torch.int32, device='cuda')
+    counts = torch.tensor([100, 0, 129], dtype=torch.int32, device='cuda')
+    a = torch.full((384, 64), 7.0, dtype=torch.bfloat16, device='cuda')
+    b = torch.full((384, 4), 3.0, dtype=torch.float32, device='cuda')
+    zero_group_padding([a, b], offsets, counts)
+    torch.cuda.synchronize()
+    live = torch.zeros(384, dtype=torch.bool, device='cuda')
+    live[0:100] = True
+    live[128:257] = True
+    assert bool((a[live] == 7).all()) and bool((a[~live] == 0).all())
+    assert bool((b[live] == 3).all()) and bool((b[~live] == 0).all())
