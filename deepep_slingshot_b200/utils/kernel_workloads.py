@@ -7,8 +7,13 @@ Used to profile kernels in isolation (for example with Nsight Compute, filtering
 
 With `--time R` each workload is also timed: R repetitions, each bracketed by CUDA events on the
 current stream after a 256 MB write that evicts L2, median reported in microseconds.
-`--pending --only masked_gemm,ll_dispatch_gemm,bf16_mn,fused_dispatch_gemm` builds and runs the
-workloads of the kernels that have not run on a GPU yet (they are never in the default set).
+Workloads (names for `--only`): layout, dispatch (count + stage/pull), combine, combine_expanded
+(weighted expanded combine, needs dispatch), low_latency, ll_logfmt, cast, quantize_weights,
+grouped_gemm, swiglu_quant (needs grouped_gemm), permute, barrier, masked_gemm, ll_dispatch_gemm,
+bf16_gemm, bf16_mn, bf16_wgrad, fused_dispatch_gemm (standalone stage + count + fused receive/GEMM),
+moe_backward_ops (needs dispatch and grouped_gemm), transport_checks, ll_clean, side_features (PP,
+AGRS, Engram).
+The default set is every workload.
 
 Sizes default to inputs larger than L2 for the bandwidth-bound kernels while keeping the whole
 process within a few GB of device memory.
@@ -95,12 +100,26 @@ def build(args):
     def barrier():
         buf.barrier()
 
-    work = {'layout': layout, 'dispatch': dispatch, 'combine': combine, 'low_latency': ll, 'cast': cast,
-            'grouped_gemm': grouped_gemm, 'swiglu_quant': swiglu, 'permute': perm, 'barrier': barrier}
-    if not args.pending:
-        return work
+    def quantize_weights():
+        gemm.quantize_weights_fp8(wq_src)
 
-    # Kernels that have not run on a GPU yet (opt-in with --pending).
+    wq_src = (torch.randn((e_g, n1, k1), generator=g) * 0.02).to(torch.bfloat16).cuda()
+
+    # combine in the weighted expanded mode: the grouped rows of the dispatch's tokens
+    def combine_expanded():
+        (rx, rs), ri, rw, _, h, _ = state['disp']
+        if 'perm' not in state:
+            state['perm'] = permute.permute(rx, ri, E, alignment=128, probs=rw, x_scales=rs, zero_padding=True)
+            state['y_exp'] = torch.randn((state['perm'].x.shape[0], H), generator=g).to(torch.bfloat16).cuda()
+        pm = state['perm']
+        buf.combine(state['y_exp'], h, row_map=pm.row_map, row_weights=rw)
+
+    def ll_logfmt():
+        recv, cnt, hh, _, hook = buf.low_latency_dispatch(lx, lidx, T, E_ll, use_fp8=True, return_recv_hook=True)
+        hook()
+        out, _, chook = buf.low_latency_combine(ly, lidx, lw, hh, use_logfmt=True, return_recv_hook=True)
+        chook()
+
     slots = T  # world 1: the low-latency layout has num_ranks * max_tokens slots per expert
     n_small = 512  # weights generated on the device, kept to a few GB
     mw1, mw1s = gemm.quantize_weights_fp8((torch.randn((E_ll, n_small, H), device='cuda') * 0.02).to(torch.bfloat16))
@@ -116,10 +135,18 @@ def build(args):
         buf.low_latency_combine(ly, lidx, lw, hh)
 
     bw = (torch.randn((e_g, k1, n1), generator=g) * 0.02).to(torch.bfloat16).cuda()  # [E, k, n] as it lies
+    bk = bw.transpose(1, 2).contiguous()                                              # [E, n, k]
     ba = torch.randn((rows_per * e_g, k1), generator=g).to(torch.bfloat16).cuda()
+    bg = torch.randn((rows_per * e_g, n1), generator=g).to(torch.bfloat16).cuda()
+
+    def bf16_gemm():
+        gemm.grouped_gemm_bf16(ba, bk, goff, gcnt)
 
     def bf16_mn():
         gemm.grouped_gemm_bf16(ba, bw, goff, gcnt, b_mn_major=True)
+
+    def bf16_wgrad():
+        gemm.grouped_gemm_bf16_wgrad_rows(bg, ba, goff)
 
     fw, fws = gemm.quantize_weights_fp8((torch.randn((E, n_small, H), device='cuda') * 0.02).to(torch.bfloat16))
     fws = fws.contiguous()
@@ -128,8 +155,51 @@ def build(args):
         h, grp, hnd = buf.dispatch_gemm(x, idx, w.float().contiguous(), E, fw, fws)
         buf.combine(y_recv[:hnd[3].shape[0]], hnd, topk_weights=grp['topk_weights'])
 
-    work.update({'masked_gemm': masked_gemm, 'll_dispatch_gemm': ll_dispatch_gemm, 'bf16_mn': bf16_mn,
-                 'fused_dispatch_gemm': fused_dispatch_gemm})
+    # MoE backward helpers on the grouped layout of the dispatch workload's tokens
+    def moe_backward_ops():
+        (rx, rs), ri, rw, _, h, _ = state['disp']
+        if 'perm' not in state:
+            combine_expanded()
+        pm = state['perm']
+        R = int(pm.expert_offsets[-1])
+        g_y = torch.zeros((R, H), dtype=torch.bfloat16, device='cuda')
+        permute.unpermute_backward(y_recv[:rx.shape[0]], pm.row_map, rw, state['y_exp'][:R], g_y)
+        quant.swiglu_backward(state['h'], state['h'][:, :n1 // 2].contiguous())
+        permute.zero_group_padding([pm.x, pm.scales], pm.expert_offsets, pm.expert_counts)
+
+    def transport_checks():
+        buf.transport_selftest(64, 8, 16)
+        require_ext().window_check(torch.tensor([[0, 1, 1], [5, 6, 10]], dtype=torch.int64, device='cuda'))
+        buf.runtime.sample_clock()  # the trace clock alignment's %globaltimer read
+
+    def ll_clean():
+        buf.clean_low_latency_buffer(T, H, E_ll)
+
+    from deepep_slingshot_b200 import ElasticBuffer
+    side = {}
+
+    def side_features():
+        if not side:
+            side['buf'] = ElasticBuffer(dist.group.WORLD, num_max_tokens_per_rank=64, hidden=256, num_topk=2)
+            side['buf'].pp_set_config(8 << 20, 2)
+            side['buf'].agrs_set_config(32 << 20, 4)
+            side['buf'].engram_write(torch.randn((4096, 1024), generator=g).to(torch.bfloat16).cuda())
+            side['payload'] = torch.randint(0, 256, (8 << 20,), generator=g, dtype=torch.uint8).cuda()
+            side['idx'] = torch.randint(0, 4096, (2048,), generator=g, dtype=torch.int32).cuda()
+        sb = side['buf']
+        sb.pp_send(side['payload'], 0)
+        got = torch.empty_like(side['payload'])
+        sb.pp_recv(got, 0)
+        with sb.agrs_new_session():
+            gathered, hook = sb.all_gather(side['payload'][:1 << 20].view(torch.int32))
+            hook()
+        sb.engram_fetch(side['idx'])()
+
+    work.update({'quantize_weights': quantize_weights, 'combine_expanded': combine_expanded, 'll_logfmt': ll_logfmt,
+                 'masked_gemm': masked_gemm, 'll_dispatch_gemm': ll_dispatch_gemm, 'bf16_gemm': bf16_gemm,
+                 'bf16_mn': bf16_mn, 'bf16_wgrad': bf16_wgrad, 'fused_dispatch_gemm': fused_dispatch_gemm,
+                 'moe_backward_ops': moe_backward_ops, 'transport_checks': transport_checks, 'll_clean': ll_clean,
+                 'side_features': side_features})
     return work
 
 
@@ -146,13 +216,10 @@ def main():
     p.add_argument('--gemm-rows', type=int, default=1024)
     p.add_argument('--gemm-experts', type=int, default=4)
     p.add_argument('--time', type=int, default=0, help='timed repetitions per workload (0: profile pass only)')
-    p.add_argument('--pending', action='store_true',
-                   help='also build the workloads of kernels that have not run on a GPU yet (name them with --only)')
     args = p.parse_args()
     _init_single_rank()
     work = build(args)
-    default = {'layout', 'dispatch', 'combine', 'low_latency', 'cast', 'grouped_gemm', 'swiglu_quant', 'permute', 'barrier'}
-    wanted = set(args.only.split(',')) if args.only else default
+    wanted = set(args.only.split(',')) if args.only else set(work)
     names = [n for n in work if n in wanted]
     for n in names:  # warm-up outside the profiled range
         work[n]()
