@@ -16,13 +16,13 @@
 //  * warp 1, one thread: four `tcgen05.mma.cta_group::1.kind::f8f6f4` (M=128, N=128, K=32) per K
 //    block into one of the TMEM accumulators (K blocks rotate over 512 / N of them: four at N = 128),
 //    then `tcgen05.commit` frees the shared-memory stage and publishes the TMEM buffer;
-//  * warps 2..9: read the K-block partial with `tcgen05.ld`, release the TMEM buffer at once, and
-//    accumulate sa*sb*partial in fp32 registers (the per-block scale promotion that fp32 scales need);
-//    after the last K block they write bf16 rows.
+//  * warps 2..17: read the K-block partial with `tcgen05.ld` (four warps per TMEM lane quarter, one
+//    column quarter each), release the TMEM buffer, and accumulate sa*sb*partial in fp32 registers
+//    (the per-block scale promotion that fp32 scales need); after the last K block they write bf16 rows.
 // Tile width: 128 (default) or 256 columns (`DEEPEP_B200_GEMM_BN=256`, when N allows): a 256-wide
 // tile stages 48 KiB of A and B per 8.4 MFLOP instead of 32 KiB per 4.2 MFLOP, easing the L2 ->
 // shared-memory feed; the two accumulators then fill all 512 TMEM columns and each epilogue thread
-// promotes 128 columns, 32 at a time.
+// promotes 64 columns, 16 at a time.
 // Every mbarrier wait is bounded (a status is reported, the kernel returns).
 #include <cstdlib>
 
@@ -40,13 +40,17 @@ namespace {
 using tc::mma_commit;
 using tc::smem_desc_sw128;
 using tc::tma_load_2d;
+using tc::tmem_ld_16;
 using tc::tmem_ld_32;
 using tc::tmem_wait_ld;
 __device__ __forceinline__ void tc_fence_before() { tc::fence_before(); }
 __device__ __forceinline__ void tc_fence_after() { tc::fence_after(); }
 
 constexpr int kBM = 128, kBK = 128;  // BK = 128 fp8 = one 128-byte swizzle row
-constexpr int kEpiWarps = 8;
+// Sixteen epilogue warps: four per TMEM lane quarter, each promoting a quarter of the tile's columns,
+// so one K block's promotion (TMEM load + scaled FMAs) takes half the time of eight warps and keeps
+// up with the MMA issuer (measured: with eight, the tensor pipe idled on the promotion).
+constexpr int kEpiWarps = 16;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 // Tile width kBN (128 or 256): a stage holds A (kBM x kBK) and B (kBN x kBK); TMEM holds two fp32
 // accumulators of kBN columns. 256-wide tiles stage 48 KiB per 8.4 MFLOP instead of 32 KiB per 4.2.
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                                                                      const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
     constexpr int kStageBytes = kStageBytesT<kBN>;
     constexpr uint32_t kTmemCols = kTmemColsT<kBN>;
-    constexpr int kCols = kBN / 2;  // accumulator columns per epilogue thread (one row, one half)
+    constexpr int kCols = kBN / 4;  // accumulator columns per epilogue thread (one row, one quarter)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
     constexpr int kAcc = kAccT<kBN>;
@@ -203,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
         // ---------------------------------------------------------------- epilogue / scale promotion
         const int ew = warp - 2;
         const int q = warp & 3;      // TMEM lane quarter this warp may access
-        const int h = ew >> 2;       // column half: [kCols * h, kCols * (h + 1))
+        const int h = ew >> 2;       // column quarter: [kCols * h, kCols * (h + 1))
         const int row = 32 * q + lane;
         uint32_t g = 0;
         bool ok = true;
@@ -226,30 +230,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                 }
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + kCols * h);
-                if constexpr (kCols == 64) {
-                    float v[64];
-                    tmem_ld_32(taddr, v);
-                    tmem_ld_32(taddr + 32, v + 32);
+                // TMEM -> registers kChunk columns per load (register budget at 576 threads: the kCols
+                // accumulators + kChunk staged values), then release the buffer to the MMA issuer.
+                constexpr int kChunk = kCols <= 32 ? 32 : 16;
+#pragma unroll
+                for (int c = 0; c < kCols; c += kChunk) {
+                    float v[kChunk];
+                    if constexpr (kChunk == 32) tmem_ld_32(taddr + c, v);
+                    else tmem_ld_16(taddr + c, v);
                     tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s_tempty[b]);
 #pragma unroll
-                    for (int i = 0; i < 64; ++i) acc[i] = fmaf(scale, v[i], acc[i]);
-                } else {
-                    // 128 columns: 32 at a time (register budget: 128 accumulators + 32 staged values).
-#pragma unroll
-                    for (int c = 0; c < kCols; c += 32) {
-                        float v[32];
-                        tmem_ld_32(taddr + c, v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s_tempty[b]);
+                    for (int i = 0; i < kChunk; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_tempty[b]);
             }
             if (!ok) break;
             __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + kCols * h;

@@ -2,6 +2,7 @@
 
 Only Blackwell datacenter parts are targeted: every CUDA translation unit is compiled with
 `-gencode arch=compute_100a,code=sm_100a`, which also keeps torch from adding its own arch list.
+A kernel that spills registers fails the build (ptxas --warn-on-spills --warning-as-error).
 """
 import os
 from setuptools import setup
@@ -34,6 +35,10 @@ NVCC_FLAGS = [
     "-lineinfo", "-O3", "-std=c++17",
     "--expt-relaxed-constexpr",
     "-Xptxas", "-v",
+    # Build-time gate on register spills (the reference's JIT fails a kernel that uses local memory
+    # for spills): ptxas turns a spill warning into a build error.
+    "-Xptxas", "--warn-on-spills",
+    "-Xptxas", "--warning-as-error",
     "--diag-suppress=177,550",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17", "-Wno-unused-function"]

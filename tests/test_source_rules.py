@@ -50,3 +50,16 @@ def test_no_build_notes_or_machine_paths_in_sources():
     assert _hits(notes) == []
     assert _hits('/' + 'root' + '/') == []
     assert _hits('gpu' + 'run') == []
+
+
+def test_build_fails_on_register_spills():
+    """Every CUDA translation unit is compiled with ptxas turning a spill into an error, the build-time
+    counterpart of the reference JIT's check that rejects kernels using local memory for spills."""
+    import ast
+    src = open(os.path.join(ROOT, 'setup.py')).read()
+    tree = ast.parse(src)
+    flags = next(ast.literal_eval(n.value) for n in ast.walk(tree)
+                 if isinstance(n, ast.Assign) and any(getattr(t, 'id', '') == 'NVCC_FLAGS' for t in n.targets))
+    pairs = list(zip(flags, flags[1:]))
+    assert ('-Xptxas', '--warn-on-spills') in pairs and ('-Xptxas', '--warning-as-error') in pairs
+    assert ('-gencode', 'arch=compute_100a,code=sm_100a') in pairs
