@@ -333,6 +333,33 @@ def main():
     disp_gbps_rank = disp_bytes / (ms_disp * 1e-3) / 1e9
     comb_gbps_rank = comb_bytes / (ms_comb * 1e-3) / 1e9
 
+    # The same dispatch without the CPU sync on the received counts (`num_worst_tokens`: outputs sized
+    # for the worst case, the CUDA-graph-compatible mode), timed the same way: it shows what the
+    # host round trip of the synced dispatch costs.
+    nosync = {}
+    if args.impl == 'ours':
+        worst = N * world
+        ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(idx, E)
+        for _ in range(args.warmup):
+            buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe, topk_idx=idx,
+                         topk_weights=w, config=cfg, quantize_fp8=True, num_worst_tokens=worst)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t_ns = []
+        for i in range(args.steps):
+            flush.zero_()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe, topk_idx=idx,
+                         topk_weights=w, config=cfg, quantize_fp8=True, num_worst_tokens=worst)
+            s1.record()
+            t_ns.append((s0, s1))
+        torch.cuda.synchronize()
+        t_ns = max_over_ranks([a.elapsed_time(b) for a, b in t_ns])
+        ms_ns = sum(t_ns) / len(t_ns)
+        nosync = {'dispatch_nosync_ms': ms_ns, 'dispatch_nosync_gbps_per_rank': disp_bytes / (ms_ns * 1e-3) / 1e9,
+                  'dispatch_nosync_note': 'num_worst_tokens = tokens x ranks: no CPU sync on the received counts'}
+
     # ---------------------------------------------------------------- low-latency
     ll = {}
     if not args.no_ll and args.impl == 'ours':
@@ -599,7 +626,7 @@ def main():
                        'host_cpus': getattr(args, 'host_cpus', None),
                        'byte_definition': 'DeepEP v2 logical bytes incl. local traffic, summed over ranks',
                        'baseline': f'{BASELINE_CYCLE_GBPS_PER_RANK} GB/s per rank x n_gpus (published SM100 EP8 726/740)'},
-            'dispatch_ms': ms_disp, 'combine_ms': ms_comb,
+            'dispatch_ms': ms_disp, 'combine_ms': ms_comb, **nosync,
             'dispatch_gbps_per_rank': disp_gbps_rank, 'combine_gbps_per_rank': comb_gbps_rank,
             'num_recv_tokens_rank0': num_recv,
             'clocks': clocks,
