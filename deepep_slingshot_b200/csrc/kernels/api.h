@@ -217,6 +217,8 @@ void launch_swiglu_quant(const void* h, int rows, int inter, void* a, void* a_q,
                          cudaStream_t stream, const int* counts = nullptr, int slots = 0);
 void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_tokens, int hidden, void* out_bf16,
                                 cudaStream_t stream);
-void launch_quantize_weights_fp8(const void* w, int num_experts, int n, int k, void* q, float* scales, cudaStream_t stream);
+// round_scale: power-of-two block scales (exact as UE8M0, as the block-scaled MMA needs).
+void launch_quantize_weights_fp8(const void* w, int num_experts, int n, int k, void* q, float* scales, cudaStream_t stream,
+                                 int round_scale = 0);
 
 }  // namespace ep

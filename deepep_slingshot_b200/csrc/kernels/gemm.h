@@ -21,6 +21,7 @@ struct GemmArgs {
     void* d;                  // [rows][n] bf16
     int rows, n, k, num_experts;
     int stages;
+    int block_scaled;         // 1: scales are powers of two, applied by the block-scaled MMA (UE8M0)
     KernelStatus st;
 };
 

@@ -267,6 +267,231 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
 }
 
 // ------------------------------------------------------------------------------------------------
+// Block-scaled variant (`kind::mxf8f6f4.block_scale`): with power-of-two scales (exact as UE8M0) the
+// tensor core applies the 1x128 activation and 128x128 weight scales itself, per 32-deep K step, so
+// the accumulator stays in TMEM over the whole K range and the epilogue runs once per tile instead of
+// promoting every K block. Per stage, warp 0 writes the tile's scale factors next to the TMA tiles in
+// the 128 x 4 UE8M0 atom the tensor core reads (byte (r % 32) * 16 + (r / 32) * 4 + j holds row r's
+// scale for the j-th 32-deep K step; every step of a 128 block has the same scale here); the MMA
+// thread copies them into TMEM (`tcgen05.cp ... 32x128b.warpx4`) and issues the four MMAs of the K
+// block, each naming its K step through the scale-factor byte id. The scale-factor columns are one
+// region, rewritten every K block: the copies and MMAs of the one issuing thread run in order.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kBsBN = 128;
+constexpr int kBsEpiWarps = 4;                       // one per TMEM lane quarter
+constexpr int kBsThreads = (2 + kBsEpiWarps) * 32;   // warp 0: TMA + scale factors, warp 1: MMA
+constexpr int kSfBytes = 512;                        // one 128-row x 4-step UE8M0 atom
+constexpr int kBsStageBytes = (kBM + kBsBN) * kBK + 2 * kSfBytes;  // A, B, SFA, SFB (33 KiB, 1 KiB multiple)
+constexpr uint32_t kBsSfaCol = 2 * kBsBN, kBsSfbCol = 2 * kBsBN + 4;  // after the two accumulators
+
+// Instruction descriptor, kind::mxf8f6f4.block_scale: E4M3 x E4M3 (formats 0), both K-major, UE8M0
+// scale factors (bit 23), N >> 3 at bit 17, M >> 4 at bit 24; the scale-factor byte ids of A (bits
+// 29-30) and B (bits 4-5) are or-ed in per K step.
+__host__ __device__ constexpr uint32_t idesc_mxf8_ue8m0(int m, int n) {
+    return (1u << 23) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_mxf8_bs(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t tmem_sfa, uint32_t tmem_sfb, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(tmem_d),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(tmem_sfa), "r"(tmem_sfb), "r"(accumulate)
+        : "memory");
+}
+
+// Shared-memory -> TMEM copy of one 32-row x 16-byte block, replicated into the four lane quarters.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t tmem_addr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_addr), "l"(sdesc) : "memory");
+}
+
+// No-swizzle K-major descriptor of a 32 x 16-byte block: 8-row core matrices of 128 bytes, 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sf(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3fffu);   // start address
+    d |= (uint64_t)(128 >> 4) << 16;          // leading byte offset (a single 16-byte column: unused)
+    d |= (uint64_t)(128 >> 4) << 32;          // stride byte offset: next 8-row core matrix
+    d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+    return d;                                 // layout type 0: no swizzle
+}
+
+// UE8M0 code of a positive power-of-two fp32 scale: its exponent field, repeated in four bytes.
+__device__ __forceinline__ uint32_t ue8m0_x4(float scale) {
+    return ((__float_as_uint(scale) >> 23) & 0xffu) * 0x01010101u;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kBsThreads, 1) grouped_gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                          const __grid_constant__ CUtensorMap map_b,
+                                                                          GemmArgs a) {
+    constexpr uint32_t kTmemCols = 512;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
+    __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_mt_prefix[kMaxGemmExperts + 1];
+
+    const int warp = warp_id(), lane = lane_id();
+    const int S = a.stages;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int KB = a.k / kBK;
+    const int n_tiles = a.n / kBsBN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_tfull[b], 1);
+            mbar_init(&s_tempty[b], kBsEpiWarps);
+        }
+        fence_mbar_init();
+        int acc = 0;
+        s_mt_prefix[0] = 0;
+        for (int e = 0; e < a.num_experts; ++e) {
+            const int rows = a.expert_counts != nullptr ? a.expert_counts[e] : a.offsets[e + 1] - a.offsets[e];
+            acc += (rows + kBM - 1) / kBM;
+            s_mt_prefix[e + 1] = acc;
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- scale factors + TMA producer
+        uint32_t g = 0;
+        int ok = 1;
+        TileInfo ti;
+        for (int t = blockIdx.x; ok && tile_of<kBsBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
+            const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + ti.n0 / 128) * KB;
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int s = g % S;
+                if (lane == 0) ok = wait_bar(&s_empty[s], ((g / S) & 1) ^ 1, a.st) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                uint8_t* st_a = smem + (size_t)s * kBsStageBytes;
+                uint8_t* st_b = st_a + kBM * kBK;
+                uint8_t* st_sfa = st_b + kBsBN * kBK;
+                uint8_t* st_sfb = st_sfa + kSfBytes;
+                // SFA: lane l writes the 16 bytes of row group l (rows l, l+32, l+64, l+96).
+                uint4 wa;
+                uint32_t* w4 = reinterpret_cast<uint32_t*>(&wa);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int m = ti.m0 + lane + 32 * j;
+                    w4[j] = m < a.rows ? ue8m0_x4(a.sa[(int64_t)m * KB + kb]) : 0x7f7f7f7fu;  // 2^0 past the rows
+                }
+                *reinterpret_cast<uint4*>(st_sfa + lane * 16) = wa;
+                // SFB: the tile lies in one 128x128 weight block, so every byte is that block's scale.
+                const uint32_t wb = ue8m0_x4(sb_blk[kb]);
+                *reinterpret_cast<uint4*>(st_sfb + lane * 16) = make_uint4(wb, wb, wb, wb);
+                fence_proxy_async_smem();  // generic writes -> the tensor core's reads (async proxy)
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&s_full[s], (kBM + kBsBN) * kBK);
+                    tma_load_2d(st_a, &map_a, kb * kBK, ti.m0, &s_full[s]);
+                    tma_load_2d(st_b, &map_b, kb * kBK, ti.e * a.n + ti.n0, &s_full[s]);
+                }
+            }
+        }
+        // After an expired wait: the loads already issued land before the CTA exits.
+        if (!ok && lane == 0) ring_drain(s_full, S, (int)g, a.st, kErrTimeoutTma);
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_mxf8_ue8m0(kBM, kBsBN);
+            uint32_t g = 0, j = 0;
+            bool ok = true;
+            TileInfo ti;
+            for (int t = blockIdx.x; ok && tile_of<kBsBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti);
+                 t += gridDim.x, ++j) {
+                const int b = j & 1;
+                ok = wait_bar(&s_tempty[b], ((j >> 1) & 1) ^ 1, a.st);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(b * kBsBN);
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int s = g % S;
+                    ok = wait_bar(&s_full[s], (g / S) & 1, a.st);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t sa_addr = smem_u32(smem + (size_t)s * kBsStageBytes);
+                    const uint32_t sb_addr = sa_addr + kBM * kBK;
+                    const uint32_t sfa_addr = sb_addr + kBsBN * kBK;
+                    tmem_cp_32x128b_x4(tmem_base + kBsSfaCol, smem_desc_sf(sfa_addr));
+                    tmem_cp_32x128b_x4(tmem_base + kBsSfbCol, smem_desc_sf(sfa_addr + kSfBytes));
+                    const uint64_t da = smem_desc_sw128(sa_addr), db = smem_desc_sw128(sb_addr);
+#pragma unroll
+                    for (int k = 0; k < kBK / 32; ++k)  // 32-deep steps; the scale-factor byte id is the step
+                        mma_mxf8_bs(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k),
+                                    idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4),
+                                    (tmem_base + kBsSfaCol) | ((uint32_t)k << 30),
+                                    (tmem_base + kBsSfbCol) | ((uint32_t)k << 30), (kb > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(&s_empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&s_tfull[b]);
+            }
+            // After an expired wait: the MMAs already issued complete before the TMEM is freed.
+            if (!ok && g > 0) wait_bar(&s_empty[(g - 1) % S], ((g - 1) / S) & 1, a.st);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue (once per tile)
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        uint32_t j = 0;
+        TileInfo ti;
+        for (int t = blockIdx.x; tile_of<kBsBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x, ++j) {
+            const int b = j & 1;
+            int good = 1;
+            if (lane == 0) good = wait_bar(&s_tfull[b], (j >> 1) & 1, a.st) ? 1 : 0;
+            if (!__shfl_sync(0xffffffffu, good, 0)) break;
+            tc_fence_after();
+            const int m = ti.m0 + 32 * q + lane;
+            __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0;
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBsBN);
+#pragma unroll
+            for (int c = 0; c < kBsBN; c += 32) {
+                float v[32];
+                tmem_ld_32(taddr + c, v);
+                tmem_wait_ld();
+                if (m < a.rows) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        int4 o;
+                        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) o2[u] = __floats2bfloat162_rn(v[i + 2 * u], v[i + 2 * u + 1]);
+                        *reinterpret_cast<int4*>(d + c + i) = o;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_tempty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // Host side: tensor maps through the driver entry point (no libcuda link), launch.
 // ------------------------------------------------------------------------------------------------
 namespace {
@@ -307,6 +532,20 @@ int launch_tiles(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
 
 int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     if (args_in.k % kBK != 0 || args_in.n % 128 != 0 || args_in.num_experts > kMaxGemmExperts || args_in.rows <= 0) return 1;
+    if (args_in.block_scaled) {
+        GemmArgs a = args_in;
+        CUtensorMap map_a, map_b;
+        if (!make_map_u8(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
+        if (!make_map_u8(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k, (uint32_t)kBsBN)) return 2;
+        const int max_stages = (int)((220 * 1024 - 1024) / kBsStageBytes);
+        if (a.stages <= 0) a.stages = 6;
+        if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
+        if (a.stages > max_stages) a.stages = max_stages;
+        const size_t smem = (size_t)a.stages * kBsStageBytes + 1024;
+        cudaFuncSetAttribute(grouped_gemm_fp8_bs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        grouped_gemm_fp8_bs_kernel<<<num_sms, kBsThreads, smem, stream>>>(map_a, map_b, a);
+        return cudaGetLastError() == cudaSuccess ? 0 : 3;
+    }
     return tile_width(args_in.n) == 256 ? launch_tiles<256>(args_in, num_sms, stream)
                                         : launch_tiles<128>(args_in, num_sms, stream);
 }

@@ -531,7 +531,7 @@ __device__ __forceinline__ void pipe_init(const PipeSmem& p) {
 // pull (dispatch receive): rows of my receive block are pulled from the sources' staging.
 // =================================================================================================
 
-constexpr int kStageWarps = 4;  // stage warps per pull block when the stage overlaps the pulls
+constexpr int kStageWarps = 8;  // stage warps per pull block when the stage overlaps the pulls
 
 // Stage warps of the pull launch: stage this rank's tokens in token order (grid-stride over warps,
 // so low chunks complete first) and, once the last token of a chunk is in the staging, release
@@ -613,19 +613,26 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
             }
         }
         const int g = blockIdx.x * kPairs + pair, P = gridDim.x * kPairs;
-        const int my_rows = pair_num_rows(g, P, num_recv, a.chunk);
+        // With the stage overlapped, rows follow the wavefront order: at step k pair g takes the next
+        // row of source (k + g) % R, so every pair walks every source's tokens in increasing order, at
+        // the pace its stage warps release them, with the loads spread over all sources. Otherwise
+        // rows are dealt in blocks (or chunks) of the receive order.
+        const bool wave = a.stage_warps > 0;
+        const int my_rows = wave ? wave_num_rows(g, P, s_prefix, R, num_recv) : pair_num_rows(g, P, num_recv, a.chunk);
+        auto row_at = [&](int k) { return wave ? wave_row(g, P, k, s_prefix, R, num_recv) : pair_row(g, P, k, a.chunk, num_recv); };
         const int S = p.S;
         const int chunk = a.stage_warps > 0 ? a.stage.chunk : 0;
 
         if (producer) {
             // After an expired wait lane 0 issues nothing more (the consumer stops at the first row that
             // does not arrive) instead of waiting out every later row; then it drains what it issued.
+            // Lanes look up 32 schedule steps at a time (a step past a source's rows is skipped).
             int failed = 0, issued = 0;
-            for (int base = 0; base < my_rows; base += 32) {
+            for (int base = 0; issued < my_rows && !failed; base += 32) {
                 const int kk = base + lane;
                 int src = 0, t = 0;
-                if (kk < my_rows) {
-                    const int j = pair_row(g, P, kk, a.chunk, num_recv);
+                const int j = row_at(kk);
+                if (j >= 0) {
                     src = find_source(s_prefix, R, j);
                     if (a.cached_src_idx != nullptr) {
                         t = a.cached_src_idx[j];
@@ -635,11 +642,12 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
                         t = ld_relaxed_sys(list + (j - s_prefix[src]));
                     }
                 }
-                const int n = min(32, my_rows - base);
-                for (int i = 0; i < n; ++i) {
+                const uint32_t live = __ballot_sync(0xffffffffu, j >= 0);
+                for (int i = 0; i < 32; ++i) {
+                    if (!((live >> i) & 1u)) continue;
                     const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
                     if (lane == 0 && !failed) {
-                        const int k = base + i, slot = k % S;
+                        const int k = issued, slot = k % S;
                         if (chunk > 0 && s_staged_chunk[pair][ps] != pt / chunk) {
                             // The source stages concurrently: wait (bounded, local flag) until the chunk
                             // holding this token is in its staging, then order the TMA read after it.
@@ -662,7 +670,8 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
                         }
                     }
                 }
-                if (__shfl_sync(0xffffffffu, failed, 0)) break;
+                failed = __shfl_sync(0xffffffffu, failed, 0);
+                issued = __shfl_sync(0xffffffffu, issued, 0);
             }
             if (lane == 0) ring_drain(p.full, S, issued, a.st, kErrTimeoutTma);
         } else {
@@ -671,8 +680,10 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
             const bool scales_bulk = a.recv_scales != nullptr && !a.scales_col_major && (nb * 4) % 16 == 0;
             const int E_l = a.num_local_experts, lo_e = a.rank * E_l;
             const int lag = S / 2 < 4 ? S / 2 : 4;  // peer loads are the slow leg: favour loads in flight
-            for (int k = 0; k < my_rows; ++k) {
-                const int j = pair_row(g, P, k, a.chunk, num_recv), slot = k % S;
+            for (int kk = 0, k = 0; k < my_rows; ++kk) {
+                const int j = row_at(kk);
+                if (j < 0) continue;
+                const int slot = k % S;
                 int good = 1;
                 if (lane == 0) good = mbar_wait(&p.full[slot], (k / S) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
                 if (!__shfl_sync(0xffffffffu, good, 0)) break;
@@ -699,6 +710,7 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
                 if (lane == 0 && a.recv_src_idx != nullptr) a.recv_src_idx[j] = p.side[2 * slot];
                 __syncwarp();
                 if (lane == 0) release_slots(p, k, lag);
+                ++k;
             }
             if (lane == 0) bulk_wait<0>();
         }

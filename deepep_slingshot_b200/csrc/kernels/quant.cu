@@ -119,7 +119,8 @@ void launch_per_token_cast_back(const void* x_fp8, const float* scales, int num_
 // the oracle: amax clamped at 1e-4, scale = amax / 448, q = saturate(v / scale) (true division,
 // round-to-nearest-even into e4m3).
 __global__ void __launch_bounds__(256) quantize_weights_fp8_kernel(const __nv_bfloat16* __restrict__ w, int n, int k,
-                                                                    uint8_t* __restrict__ q, float* __restrict__ scales) {
+                                                                    uint8_t* __restrict__ q, float* __restrict__ scales,
+                                                                    int round_scale) {
     __shared__ float s_red[8];
     const int kb = k / 128, nb = n / 128;
     const int64_t blk = blockIdx.x;
@@ -149,8 +150,8 @@ __global__ void __launch_bounds__(256) quantize_weights_fp8_kernel(const __nv_bf
     amax = s_red[0];
 #pragma unroll
     for (int i = 1; i < 8; ++i) amax = fmaxf(amax, s_red[i]);
-    amax = fmaxf(amax, 1e-4f);
-    const float scale = amax / 448.0f;
+    // amax / 448 (clamped), or that rounded up to a power of two with round_scale (UE8M0-exact)
+    const float scale = fp8_scale_from_amax(amax, round_scale != 0);
     if (tid == 0) scales[blk] = scale;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -167,11 +168,12 @@ __global__ void __launch_bounds__(256) quantize_weights_fp8_kernel(const __nv_bf
     }
 }
 
-void launch_quantize_weights_fp8(const void* w, int num_experts, int n, int k, void* q, float* scales, cudaStream_t stream) {
+void launch_quantize_weights_fp8(const void* w, int num_experts, int n, int k, void* q, float* scales, cudaStream_t stream,
+                                 int round_scale) {
     const int64_t blocks = (int64_t)num_experts * (n / 128) * (k / 128);
     if (blocks == 0) return;
     quantize_weights_fp8_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(w), n, k,
-                                                                       static_cast<uint8_t*>(q), scales);
+                                                                       static_cast<uint8_t*>(q), scales, round_scale);
 }
 
 }  // namespace ep

@@ -46,7 +46,7 @@ KernelStatus op_status(double timeout_s) {
 // Grouped block-scaled FP8 GEMM (tcgen05): d[rows, n] = per-expert A x B_e^T with 1x128 / 128x128 scales.
 torch::Tensor grouped_gemm_fp8(const torch::Tensor& a, const torch::Tensor& sa, const torch::Tensor& b, const torch::Tensor& sb,
                                const torch::Tensor& offsets, const std::optional<torch::Tensor>& counts, int num_sms,
-                               double timeout_s) {
+                               double timeout_s, bool ue8m0) {
     TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.is_contiguous() && a.scalar_type() == torch::kFloat8_e4m3fn);
     TORCH_CHECK(b.dim() == 3 && b.is_contiguous() && b.scalar_type() == torch::kFloat8_e4m3fn);
     const int rows = (int)a.size(0), k = (int)a.size(1), E = (int)b.size(0), n = (int)b.size(1);
@@ -74,6 +74,7 @@ torch::Tensor grouped_gemm_fp8(const torch::Tensor& a, const torch::Tensor& sa, 
     g.n = n;
     g.k = k;
     g.num_experts = E;
+    g.block_scaled = ue8m0 ? 1 : 0;
     g.st = op_status(timeout_s);
     const int rc = launch_grouped_gemm_fp8(g, num_sms, at::cuda::getCurrentCUDAStream());
     TORCH_CHECK(rc == 0, "grouped_gemm_fp8 launch failed (code " + std::to_string(rc) + ")");
@@ -202,14 +203,15 @@ torch::Tensor per_token_cast_back(const torch::Tensor& x, const torch::Tensor& s
 
 // a = silu(h[:, :I]) * h[:, I:] (bf16) and its 1x128 FP8 quantization.
 // Expert weights [E, n, k] bf16 -> (fp8 e4m3 [E, n, k], fp32 128x128 block scales [E, n/128, k/128]).
-std::tuple<torch::Tensor, torch::Tensor> quantize_weights_fp8(const torch::Tensor& w) {
+std::tuple<torch::Tensor, torch::Tensor> quantize_weights_fp8(const torch::Tensor& w, bool round_scale) {
     TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.scalar_type() == torch::kBFloat16 && w.is_contiguous(),
                 "quantize_weights_fp8: contiguous [E, n, k] bf16 CUDA tensor");
     const int E = (int)w.size(0), n = (int)w.size(1), k = (int)w.size(2);
     TORCH_CHECK(n % 128 == 0 && k % 128 == 0, "n and k must be multiples of 128");
     auto q = torch::empty({E, n, k}, w.options().dtype(torch::kFloat8_e4m3fn));
     auto s = torch::empty({E, n / 128, k / 128}, w.options().dtype(torch::kFloat32));
-    launch_quantize_weights_fp8(w.data_ptr(), E, n, k, q.data_ptr(), s.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+    launch_quantize_weights_fp8(w.data_ptr(), E, n, k, q.data_ptr(), s.data_ptr<float>(), at::cuda::getCurrentCUDAStream(),
+                                round_scale ? 1 : 0);
     return {q, s};
 }
 
@@ -370,7 +372,7 @@ void register_ops(pybind11::module_& m) {
     m.def("unpermute", &unpermute);
     m.def("swiglu_quant", &swiglu_quant, pybind11::arg("h"), pybind11::arg("round_scale") = false,
           pybind11::arg("counts") = std::nullopt);
-    m.def("quantize_weights_fp8", &quantize_weights_fp8, pybind11::arg("w"));
+    m.def("quantize_weights_fp8", &quantize_weights_fp8, pybind11::arg("w"), pybind11::arg("round_scale") = false);
     m.def("grouped_gemm_bf16", &grouped_gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("offsets"),
           pybind11::arg("counts") = std::nullopt, pybind11::arg("mode") = 0, pybind11::arg("num_sms") = 0,
           pybind11::arg("timeout_s") = 10.0, pybind11::arg("a_mn_major") = false, pybind11::arg("b_mn_major") = false);
@@ -379,7 +381,7 @@ void register_ops(pybind11::module_& m) {
           pybind11::arg("timeout_s") = 100.0);
     m.def("grouped_gemm_fp8", &grouped_gemm_fp8, pybind11::arg("a"), pybind11::arg("sa"), pybind11::arg("b"), pybind11::arg("sb"),
           pybind11::arg("offsets"), pybind11::arg("counts") = pybind11::none(), pybind11::arg("num_sms") = 0,
-          pybind11::arg("timeout_s") = 10.0);
+          pybind11::arg("timeout_s") = 10.0, pybind11::arg("ue8m0") = false);
     m.def("op_error_state", &op_error_state, pybind11::arg("clear") = false);
     m.def("per_token_cast_to_fp8", &per_token_cast_to_fp8, pybind11::arg("x"), pybind11::arg("round_scale") = false);
     m.def("per_token_cast_back", &per_token_cast_back);

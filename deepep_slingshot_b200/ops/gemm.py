@@ -16,11 +16,16 @@ from .._ext import require_ext
 
 
 def grouped_gemm_fp8(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor, offsets: torch.Tensor,
-                     counts: Optional[torch.Tensor] = None, num_sms: int = 0, timeout_s: float = 10.0) -> torch.Tensor:
+                     counts: Optional[torch.Tensor] = None, num_sms: int = 0, timeout_s: float = 10.0,
+                     ue8m0: bool = False) -> torch.Tensor:
     """Grouped block-scaled FP8 GEMM on tcgen05: rows of `a [rows, k]` (1x128 scales `sa`) grouped by
     expert at 128-aligned `offsets`, times `b [E, n, k]` (128x128 scales `sb`) -> `[rows, n]` bf16; only the
-    first `counts[e]` rows of each group are meaningful."""
-    return require_ext().grouped_gemm_fp8(a, sa, b, sb, offsets, counts, num_sms, timeout_s)
+    first `counts[e]` rows of each group are meaningful.
+
+    With `ue8m0=True` every scale must be a power of two (`round_scale=True` quantization): the
+    tensor core then applies the scales itself (`kind::mxf8f6f4.block_scale`) and accumulates over
+    the whole K range in TMEM, with no per-K-block promotion."""
+    return require_ext().grouped_gemm_fp8(a, sa, b, sb, offsets, counts, num_sms, timeout_s, ue8m0)
 
 
 def grouped_gemm_bf16(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, counts: Optional[torch.Tensor] = None,
@@ -86,21 +91,25 @@ def dequant_blocks(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     return (w.float().view(E, n // 128, 128, k // 128, 128) * s.view(E, n // 128, 1, k // 128, 1)).view(E, n, k)
 
 
-def quantize_weights_fp8(w: torch.Tensor):
+def quantize_weights_fp8(w: torch.Tensor, round_scale: bool = False):
     """bf16/fp32 [E, n, k] -> (fp8 [E, n, k], fp32 128x128 block scales [E, n/128, k/128]).
+    With `round_scale` the scales are rounded up to powers of two (exact as UE8M0, what the
+    block-scaled MMA path of `grouped_gemm_fp8(..., ue8m0=True)` needs).
     Contiguous bf16 CUDA weights go through the sm_100a block-quantization kernel (one HBM pass);
     other inputs use `quantize_weights_fp8_reference` (the same numerics in torch)."""
     if w.is_cuda and w.dtype == torch.bfloat16 and w.is_contiguous() and w.dim() == 3:
-        return require_ext().quantize_weights_fp8(w)
-    return quantize_weights_fp8_reference(w)
+        return require_ext().quantize_weights_fp8(w, round_scale)
+    return quantize_weights_fp8_reference(w, round_scale)
 
 
-def quantize_weights_fp8_reference(w: torch.Tensor):
+def quantize_weights_fp8_reference(w: torch.Tensor, round_scale: bool = False):
     """Torch definition of the 128x128 block weight quantization (oracle of the kernel)."""
     E, n, k = w.shape
     v = w.float().view(E, n // 128, 128, k // 128, 128)
     amax = v.abs().amax(dim=(2, 4)).clamp(min=1e-4)
     scale = amax / torch.full_like(amax, 448.0)
+    if round_scale:
+        scale = torch.pow(2.0, torch.ceil(torch.log2(scale)))
     q = (v / scale.view(E, n // 128, 1, k // 128, 1)).clamp(-448, 448).to(torch.float8_e4m3fn)
     return q.view(E, n, k), scale
 

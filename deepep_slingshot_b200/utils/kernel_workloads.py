@@ -195,6 +195,8 @@ def build(args):
             hook()
         sb.engram_fetch(side['idx'])()
 
+    work = {'layout': layout, 'dispatch': dispatch, 'combine': combine, 'low_latency': ll, 'cast': cast,
+            'grouped_gemm': grouped_gemm, 'swiglu_quant': swiglu, 'permute': perm, 'barrier': barrier}
     work.update({'quantize_weights': quantize_weights, 'combine_expanded': combine_expanded, 'll_logfmt': ll_logfmt,
                  'masked_gemm': masked_gemm, 'll_dispatch_gemm': ll_dispatch_gemm, 'bf16_gemm': bf16_gemm,
                  'bf16_mn': bf16_mn, 'bf16_wgrad': bf16_wgrad, 'fused_dispatch_gemm': fused_dispatch_gemm,
