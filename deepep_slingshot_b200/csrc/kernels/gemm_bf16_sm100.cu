@@ -21,7 +21,8 @@
 //  * warp 1, one thread: four `tcgen05.mma.cta_group::1.kind::f16` (bf16 x bf16 -> fp32, M=128,
 //    N=128, K=16) per K block, accumulating the whole K range of a tile in one TMEM buffer; two
 //    buffers alternate between tiles so the epilogue of one tile overlaps the MMAs of the next;
-//  * warps 2..9: `tcgen05.ld` the finished accumulator, release it, write bf16.
+//  * warps 2..9: `tcgen05.ld` the finished accumulator, release it, write bf16 through a per-warp
+//    shared-memory buffer so the global stores are whole 128-byte row segments.
 // Every mbarrier wait is bounded (a status is reported, the kernel returns).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -47,6 +48,7 @@ constexpr int kStageBytes = (kBM + kBN) * kBK * 2;       // 32 KiB
 constexpr int kMNAtomBytes = kBK * 128;                   // one MN-major box: 64 K rows x 128 bytes
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kEpiStageBytes = 32 * 128;                  // one epilogue warp's 32 rows x 64 bf16 store buffer
 constexpr uint32_t kTmemCols = 2 * kBN;
 
 // Instruction descriptor, kind::f16: BF16 x BF16 -> F32 (D format bit 4, A/B formats = 1 at bits
@@ -242,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
         const int q = warp & 3;   // TMEM lane quarter of this warp
         const int h = ew >> 2;    // column half [64h, 64h + 64)
         const int row = 32 * q + lane;
+        uint8_t* stg = smem + (size_t)a.stages * kStageBytes + (size_t)ew * kEpiStageBytes;  // this warp's store buffer
         uint32_t j = 0;
         Tile ti;
         for (int t = blockIdx.x; tile_of(t, a, s_prefix, ti); t += gridDim.x) {
@@ -265,14 +268,27 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_tempty[b]);
             ++j;
+            // Each lane holds one row's 64 values; the stores go out row-contiguous instead: the warp's
+            // 32 x 64 block is written to its shared-memory buffer (16-byte chunk c of row l at chunk
+            // c ^ (l & 7), conflict-free both ways) and read back so that every store instruction
+            // writes four full 128-byte row segments, not 32 rows' 16-byte pieces.
 #pragma unroll
-            for (int c = 0; c < 64; c += 8) {
+            for (int c = 0; c < 8; ++c) {
                 int4 o;
                 __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(v[c + 2 * i], v[c + 2 * i + 1]);
-                *reinterpret_cast<int4*>(d + c) = o;
+                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(v[8 * c + 2 * i], v[8 * c + 2 * i + 1]);
+                *reinterpret_cast<int4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = o;
             }
+            __syncwarp();
+            __nv_bfloat16* d0 = static_cast<__nv_bfloat16*>(a.d) + (ti.d_row0 + 32 * q) * (int64_t)a.n + ti.n0 + 64 * h;
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int r = it * 4 + (lane >> 3), cc = lane & 7;
+                const int4 o = *reinterpret_cast<const int4*>(stg + r * 128 + ((cc ^ (r & 7)) << 4));
+                *reinterpret_cast<int4*>(d0 + (int64_t)r * a.n + cc * 8) = o;
+            }
+            __syncwarp();  // the buffer is rewritten by the next tile
         }
     }
     tc_fence_before();
@@ -298,7 +314,7 @@ bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 template <bool kAMN, bool kBMN>
 int launch_instance(const CUtensorMap& map_a, const CUtensorMap& map_b, const Bf16GemmArgs& a, int num_sms,
                     cudaStream_t stream) {
-    const size_t smem = (size_t)a.stages * kStageBytes + 1024;
+    const size_t smem = (size_t)a.stages * kStageBytes + (size_t)kEpiWarps * kEpiStageBytes + 1024;
     cudaFuncSetAttribute(grouped_gemm_bf16_kernel<kAMN, kBMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     grouped_gemm_bf16_kernel<kAMN, kBMN><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
@@ -328,8 +344,9 @@ int launch_grouped_gemm_bf16(const Bf16GemmArgs& args_in, int num_sms, cudaStrea
                 : !make_map_bf16(&map_b, a.b, (uint64_t)a.n, (uint64_t)a.k))
             return 2;
     }
-    if (a.stages <= 0) a.stages = 6;
+    if (a.stages <= 0) a.stages = 5;  // 5 x 32 KiB ring + 32 KiB of epilogue store buffers
     if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
+    if (a.stages > 5) a.stages = 5;
     if (amn) return bmn ? launch_instance<true, true>(map_a, map_b, a, num_sms, stream)
                         : launch_instance<true, false>(map_a, map_b, a, num_sms, stream);
     return bmn ? launch_instance<false, true>(map_a, map_b, a, num_sms, stream)
