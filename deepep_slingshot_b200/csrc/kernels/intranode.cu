@@ -18,7 +18,9 @@
 //               block. The quantization is thereby off the critical path: it overlaps the pulls.
 //    * pull   (pull pairs of the same launch): every receiver pulls the records it needs straight
 //               out of the sources' staging with TMA bulk loads over NVLink (no multicast) into a
-//               shared-memory ring, after a bounded wait on the (source, chunk) staged flag, and
+//               shared-memory ring, in the wavefront order (at step k pair g takes the next row of
+//               source (k + g) % R, so all pairs walk every source's tokens in the order they are
+//               staged), after a bounded wait on the (source, chunk) staged flag, and
 //               TMA-stores them into its own output tensors. There is no receive ring and no copy
 //               epilogue: the output tensors are written once. The last block publishes the
 //               received counts to host-mapped memory (the CPU sync) and releases the sources' staging.
