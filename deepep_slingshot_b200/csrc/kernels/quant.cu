@@ -150,8 +150,12 @@ __global__ void __launch_bounds__(256) quantize_weights_fp8_kernel(const __nv_bf
     amax = s_red[0];
 #pragma unroll
     for (int i = 1; i < 8; ++i) amax = fmaxf(amax, s_red[i]);
-    // amax / 448 (clamped), or that rounded up to a power of two with round_scale (UE8M0-exact)
+    // amax / 448 (clamped), or that rounded up to a power of two with round_scale (UE8M0-exact); the
+    // values are multiplied by one per-block factor (448 / amax, or the exact inverse of the power of
+    // two) instead of divided by the scale element by element.
+    amax = fmaxf(amax, 1e-4f);
     const float scale = fp8_scale_from_amax(amax, round_scale != 0);
+    const float mult = round_scale != 0 ? 1.0f / scale : 448.0f / amax;
     if (tid == 0) scales[blk] = scale;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -160,8 +164,8 @@ __global__ void __launch_bounds__(256) quantize_weights_fp8_kernel(const __nv_bf
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const float2 a = __bfloat1622float2(h2[2 * j]), b = __bfloat1622float2(h2[2 * j + 1]);
-            const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a.x / scale, a.y / scale), __NV_SATFINITE, __NV_E4M3);
-            const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(b.x / scale, b.y / scale), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a.x * mult, a.y * mult), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(b.x * mult, b.y * mult), __NV_SATFINITE, __NV_E4M3);
             packed[j] = (uint32_t)lo | ((uint32_t)hi << 16);
         }
         *reinterpret_cast<uint2*>(q + base + (int64_t)(r0 + 16 * i) * k) = make_uint2(packed[0], packed[1]);

@@ -107,10 +107,14 @@ def quantize_weights_fp8_reference(w: torch.Tensor, round_scale: bool = False):
     E, n, k = w.shape
     v = w.float().view(E, n // 128, 128, k // 128, 128)
     amax = v.abs().amax(dim=(2, 4)).clamp(min=1e-4)
-    scale = amax / torch.full_like(amax, 448.0)
+    c448 = torch.full_like(amax, 448.0)
+    scale = amax / c448
     if round_scale:
         scale = torch.pow(2.0, torch.ceil(torch.log2(scale)))
-    q = (v / scale.view(E, n // 128, 1, k // 128, 1)).clamp(-448, 448).to(torch.float8_e4m3fn)
+        mult = 1.0 / scale
+    else:
+        mult = c448 / amax  # one factor per block, as the kernel applies it
+    q = (v * mult.view(E, n // 128, 1, k // 128, 1)).clamp(-448, 448).to(torch.float8_e4m3fn)
     return q.view(E, n, k), scale
 
 
