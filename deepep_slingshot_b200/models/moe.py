@@ -36,6 +36,10 @@ from .._ext import require_ext
 # (Buffer.dispatch_gemm) instead of dispatch -> permute -> grouped GEMM.
 _FUSED_DISPATCH = {'enabled': os.environ.get('DEEPEP_B200_MOE_FUSED_DISPATCH', '0') == '1'}
 _BWD = {'mode': os.environ.get('DEEPEP_B200_MOE_BWD', 'tcgen05_mn')}
+# DEEPEP_B200_MOE_UE8M0=1: every FP8 scale of the forward (dispatched activations, weights, SwiGLU
+# output) is a power of two, and the grouped GEMMs let the tensor core apply the scales
+# (`grouped_gemm_fp8(..., ue8m0=True)`, kind::mxf8f6f4.block_scale) instead of promoting every K block.
+_UE8M0 = {'enabled': os.environ.get('DEEPEP_B200_MOE_UE8M0', '0') == '1'}
 
 
 def _aligned_rows(per_expert, alignment: int = 128) -> int:
@@ -96,6 +100,7 @@ class _MoEFunction(torch.autograd.Function):
     def forward(ctx, x, topk_idx, topk_weights, w1, w2, buffer, num_experts, config):
         E_l = w1.shape[0]
         inter = w1.shape[1] // 2
+        ue8m0 = _UE8M0['enabled'] and not _FUSED_DISPATCH['enabled']
         if _FUSED_DISPATCH['enabled']:
             w1q, w1s = quantize_weights_fp8(w1.detach())
             # Dispatch receive and gate/up GEMM in one launch, tile by tile (Buffer.dispatch_gemm).
@@ -111,14 +116,14 @@ class _MoEFunction(torch.autograd.Function):
         else:
             (rxq, rxs), ridx, rw, per_expert, handle, _ = buffer.dispatch(
                 x, topk_idx=topk_idx, topk_weights=topk_weights, num_experts=num_experts, quantize_fp8=True,
-                config=config)
+                round_scale=ue8m0, config=config)
             p = permute(rxq, ridx, E_l, alignment=128, probs=rw, x_scales=rxs, zero_padding=True)
             rows = _aligned_rows(per_expert)
-            w1q, w1s = quantize_weights_fp8(w1.detach())
-            h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts)
-        a, aq, as_ = require_ext().swiglu_quant(h, False)
-        w2q, w2s = quantize_weights_fp8(w2.detach())
-        y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts)
+            w1q, w1s = quantize_weights_fp8(w1.detach(), round_scale=ue8m0)
+            h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts, ue8m0=ue8m0)
+        a, aq, as_ = require_ext().swiglu_quant(h, ue8m0)
+        w2q, w2s = quantize_weights_fp8(w2.detach(), round_scale=ue8m0)
+        y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts, ue8m0=ue8m0)
         # Top-k weighted reduction of the grouped rows, bf16 cast and exchange in one kernel.
         out, _, _ = buffer.combine(y, handle, config=config, row_map=p.row_map, row_weights=rw)
         ctx.buffer, ctx.config, ctx.inter, ctx.rows = buffer, config, inter, rows
@@ -203,16 +208,17 @@ class MoEFFN(torch.nn.Module):
         return out
 
 
-def moe_reference(x, topk_idx, topk_weights, w1_all, w2_all):
+def moe_reference(x, topk_idx, topk_weights, w1_all, w2_all, round_scale: bool = False):
     """Single-process fp32 oracle with the layer's quantization points (FP8 x, FP8 weights, bf16 h,
-    FP8 a, bf16 y); w*_all hold every expert of the group: [E, 2I, H] and [E, H, I]."""
+    FP8 a, bf16 y); w*_all hold every expert of the group: [E, 2I, H] and [E, H, I]. `round_scale`:
+    power-of-two scales everywhere (the layer's UE8M0 mode)."""
     from ..ops.gemm import dequant_blocks, quantize_weights_fp8_reference
     from ..utils.math import per_token_cast_back, per_token_cast_to_fp8
     inter = w1_all.shape[1] // 2
-    xq, xs = per_token_cast_to_fp8(x)
+    xq, xs = per_token_cast_to_fp8(x, round_scale=round_scale)
     xf = per_token_cast_back(xq, xs).float()
-    w1q, w1s = quantize_weights_fp8_reference(w1_all)
-    w2q, w2s = quantize_weights_fp8_reference(w2_all)
+    w1q, w1s = quantize_weights_fp8_reference(w1_all, round_scale)
+    w2q, w2s = quantize_weights_fp8_reference(w2_all, round_scale)
     w1f, w2f = dequant_blocks(w1q, w1s), dequant_blocks(w2q, w2s)
     out = torch.zeros_like(x, dtype=torch.float32)
     for k in range(topk_idx.shape[1]):
@@ -222,7 +228,7 @@ def moe_reference(x, topk_idx, topk_weights, w1_all, w2_all):
             sel = topk_idx[:, k] == e
             h = (xf[sel] @ w1f[e].t()).to(torch.bfloat16).float()
             a = (torch.nn.functional.silu(h[:, :inter]) * h[:, inter:]).to(torch.bfloat16)
-            aq, as_ = per_token_cast_to_fp8(a)
+            aq, as_ = per_token_cast_to_fp8(a, round_scale=round_scale)
             y = (per_token_cast_back(aq, as_).float() @ w2f[e].t()).to(torch.bfloat16).float()
             out[sel] += topk_weights[sel, k].unsqueeze(1) * y
     return out.to(torch.bfloat16)

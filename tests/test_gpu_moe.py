@@ -28,11 +28,12 @@ def _ref_autograd(x, idx, w, w1_all, w2_all):
     return out
 
 
-def _moe_body(rank, world, N, H, I, E, K, bwd='tcgen05_mn'):
+def _moe_body(rank, world, N, H, I, E, K, bwd='tcgen05_mn', ue8m0=False):
     from deepep_slingshot_b200 import Buffer
     from deepep_slingshot_b200.models import MoEFFN, moe_reference
     from deepep_slingshot_b200.models import moe as moe_mod
     moe_mod._BWD['mode'] = bwd
+    moe_mod._UE8M0['enabled'] = ue8m0
     from deepep_slingshot_b200.utils import gate
     from deepep_slingshot_b200.utils.math import calc_diff
     group = dist.group.WORLD
@@ -52,7 +53,7 @@ def _moe_body(rank, world, N, H, I, E, K, bwd='tcgen05_mn'):
     x.requires_grad_(True)
     w.requires_grad_(True)
     out = layer(x, idx, w)
-    ref = moe_reference(x.detach(), idx, w.detach(), w1_all, w2_all)
+    ref = moe_reference(x.detach(), idx, w.detach(), w1_all, w2_all, round_scale=ue8m0)
     torch.cuda.synchronize()
     d = calc_diff(out.float(), ref.float())
     assert d < 2e-4, d
@@ -84,3 +85,10 @@ def test_moe_layer_forward_backward(world, bwd):
     against fp32 autograd, with the backward GEMMs on the tcgen05 kernels (MN-major operands, the
     default, or K-major), torch's grouped GEMM (A/B stand-in) or per-expert matmuls."""
     run_ranks(_moe_body, world, 'nccl', args=(256, 1024, 512, 16, 4, bwd))
+
+
+@pytest.mark.parametrize('world', _worlds()[:2])
+def test_moe_layer_ue8m0_forward_backward(world):
+    """The layer with power-of-two scales and the block-scaled forward GEMMs, against the oracle with
+    the same quantization points (and the same backward checks)."""
+    run_ranks(_moe_body, world, 'nccl', args=(256, 1024, 512, 16, 4, 'tcgen05_mn', True))
