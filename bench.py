@@ -481,7 +481,9 @@ def main():
                'moe_config': {'tokens_per_rank': N, 'hidden': H, 'inter': inter, 'experts': E, 'topk': K,
                               'routing': 'zipf s=1.1', 'grads': 'set to None before every step (zero_grad(set_to_none=True))',
                               'forward': 'fp8 block-scaled tcgen05 grouped GEMMs' +
-                              (', dispatch receive fused into the gate/up GEMM' if args.moe_fused_dispatch else ''),
+                              (', dispatch receive fused into the gate/up GEMM' if args.moe_fused_dispatch else '') +
+                              (', power-of-two (UE8M0) scales applied by the MMA' if _moe_mod._UE8M0['enabled'] else
+                               ', fp32 scales promoted per 128-deep K block'),
                               'backward': {'tcgen05_mn': 'bf16 tcgen05 grouped GEMMs on MN-major operands (no transposes), '
                                                          'fused SwiGLU and unpermute backward kernels',
                                            'tcgen05': 'bf16 tcgen05 grouped GEMMs on transposed (K-major) operands',
