@@ -45,11 +45,11 @@ __device__ __forceinline__ uint2 quantize_8(const int4& v, bool round_scale, flo
 // `out_x` and `out_scales` may point to global or shared memory. `hidden` % 128 == 0.
 // Loads are batched four 256-element slices at a time so each lane keeps 4 x 16 B in flight.
 // With kSmemSource the row is read from shared memory (plain loads) instead of global memory.
-template <bool kSmemSource = false>
+// kUnroll: 256-column groups loaded before any is quantized (16-byte loads in flight per lane).
+template <bool kSmemSource = false, int kUnroll = 4>
 __device__ __forceinline__ void quantize_row_to_fp8(const __nv_bfloat16* __restrict__ xr, uint8_t* __restrict__ out_x,
                                                     float* __restrict__ out_scales, int hidden, bool round_scale) {
     const int lane = lane_id();
-    constexpr int kUnroll = 4;
     for (int base = 0; base < hidden; base += 256 * kUnroll) {
         int4 v[kUnroll];
 #pragma unroll

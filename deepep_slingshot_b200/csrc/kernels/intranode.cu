@@ -119,13 +119,14 @@ __device__ __forceinline__ void stage_record_meta(const StageArgs& a, int t, uin
 }
 
 // Whole record of token t through registers (one warp): quantized, copied bf16 or pre-quantized FP8
-// row, its scales and the top-k metadata.
+// row, its scales and the top-k metadata. Six 256-column groups in flight per lane (a 7168-wide
+// row in five rounds).
 __device__ __forceinline__ void stage_token_regs(const StageArgs& a, int t) {
     const int lane = lane_id();
     uint8_t* rec = a.staging + (int64_t)t * a.record_stride;
     if (a.quantize) {
-        quantize_row_to_fp8(static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * a.hidden, rec,
-                            reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
+        quantize_row_to_fp8<false, 6>(static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * a.hidden, rec,
+                                      reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
     } else {
         const int x_bytes = a.hidden * a.in_elem_bytes;
         const uint8_t* src = static_cast<const uint8_t*>(a.x) + (int64_t)t * x_bytes;
