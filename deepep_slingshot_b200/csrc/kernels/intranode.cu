@@ -563,7 +563,6 @@ __device__ __forceinline__ void stage_warps_run(const PullArgs& a, NormalCtrl* m
 __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_kernel(PullArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_prefix[kMaxRanks + 1];
-    __shared__ int s_staged_chunk[kPairs][kMaxRanks];  // per pair (producer lane 0): last chunk of each source seen staged
     const int lane = lane_id(), warp = warp_id();
     const bool pull_warp = warp < 2 * kPairs;
     const int pair = warp >> 1;
@@ -578,7 +577,6 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
         s_prefix[0] = 0;
         for (int s = 0; s < R; ++s) s_prefix[s + 1] = a.rank_prefix_matrix[s * R + a.rank];
     }
-    if (threadIdx.x < kPairs * kMaxRanks) s_staged_chunk[threadIdx.x / kMaxRanks][threadIdx.x % kMaxRanks] = -1;
     __syncthreads();
 
     const int num_recv = a.dev_num_recv != nullptr ? ld_volatile(a.dev_num_recv) : a.num_recv_host;
@@ -645,20 +643,24 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
                         t = ld_relaxed_sys(list + (j - s_prefix[src]));
                     }
                 }
+                // The sources stage concurrently: every lane checks its row's (source, chunk) staged flag
+                // (local memory) at once; lane 0 later waits (bounded) only for rows whose chunk was not
+                // staged yet, and a proxy fence orders its TMA reads after the flags it observed.
+                int ready = 1;
+                if (j >= 0 && chunk > 0) ready = (ld_acquire_sys(&my_ctrl->staged[src][t / chunk]) - epoch) >= 0;
                 const uint32_t live = __ballot_sync(0xffffffffu, j >= 0);
+                const uint32_t pending = __ballot_sync(0xffffffffu, !ready);
+                if (lane == 0 && chunk > 0) fence_proxy_async_global();
                 for (int i = 0; i < 32; ++i) {
                     if (!((live >> i) & 1u)) continue;
                     const int ps = __shfl_sync(0xffffffffu, src, i), pt = __shfl_sync(0xffffffffu, t, i);
                     if (lane == 0 && !failed) {
                         const int k = issued, slot = k % S;
-                        if (chunk > 0 && s_staged_chunk[pair][ps] != pt / chunk) {
-                            // The source stages concurrently: wait (bounded, local flag) until the chunk
-                            // holding this token is in its staging, then order the TMA read after it.
+                        if ((pending >> i) & 1u) {
                             if (!wait_ge(&my_ctrl->staged[ps][pt / chunk], epoch, a.st, kErrTimeoutStaged, ps)) {
                                 failed = 1;
                                 continue;
                             }
-                            s_staged_chunk[pair][ps] = pt / chunk;
                             fence_proxy_async_global();
                         }
                         if (k >= S && !mbar_wait(&p.empty[slot], ((k / S) - 1) & 1, a.st, kErrTimeoutTma)) {
