@@ -425,9 +425,15 @@ __device__ void gemm_role(const CUtensorMap* map_a, const CUtensorMap* map_b, co
             float acc[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            // the scales of K block kb + 1 load while block kb is waited for and promoted
+            float pa = r_in < rows ? sa_row[0] : 0.f, pb = sb_blk[0];
             for (int kb = 0; kb < KB; ++kb, ++g) {
                 const int b = g & 1;
-                const float scale = (r_in < rows ? sa_row[kb] : 0.f) * sb_blk[kb];
+                const float scale = pa * pb;
+                if (kb + 1 < KB) {
+                    pa = r_in < rows ? sa_row[kb + 1] : 0.f;
+                    pb = sb_blk[kb + 1];
+                }
                 int good = 1;
                 if (lane == 0) good = mbar_wait(&s_tfull[b], (g >> 1) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
                 if (!__shfl_sync(0xffffffffu, good, 0)) {

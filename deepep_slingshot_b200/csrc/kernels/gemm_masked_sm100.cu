@@ -247,9 +247,15 @@ __global__ void __launch_bounds__(kThreads, 1) masked_gemm_fp8_kernel(const __gr
             const int m_clamped = min(m, a.slots - 1);
             const float* sa_row = a.sa + (int64_t)ti.e * a.sa_e + (int64_t)m_clamped * a.sa_m;
             const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + ti.n0 / 128) * KB;
+            // the scales of K block kb + 1 load while block kb is waited for and promoted
+            float pa = sa_row[0], pb = sb_blk[0];
             for (int kb = 0; kb < KB; ++kb, ++g) {
                 const int b = g & 1;
-                const float scale = sa_row[(int64_t)kb * a.sa_k] * sb_blk[kb];
+                const float scale = pa * pb;
+                if (kb + 1 < KB) {
+                    pa = sa_row[(int64_t)(kb + 1) * a.sa_k];
+                    pb = sb_blk[kb + 1];
+                }
                 int good = 1;
                 if (lane == 0) good = mbar_wait(&s_tfull[b], (g >> 1) & 1, a.st, kErrTimeoutTma) ? 1 : 0;
                 if (!__shfl_sync(0xffffffffu, good, 0)) {

@@ -219,9 +219,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             const int m = ti.m0 + row;
             const float* sa_row = a.sa + (int64_t)m * KB;
             const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + (ti.n0 + kCols * h) / 128) * KB;
-            for (int kb = 0; kb < KB; ++kb, ++g) {
+            // Per K block: wait for its partial, promote it with the block's scale, release the buffer.
+            // The scales of block kb + 1 are loaded before block kb's partial is waited for and read
+            // (their latency would otherwise stall every K block of the promotion, which paces the MMA
+            // issuer).
+            float pa = sa_row[0], pb = sb_blk[0];
+            for (int kb = 0; kb < KB; ++kb) {
                 const int b = g % kAcc;
-                const float scale = sa_row[kb] * sb_blk[kb];
+                const float scale = pa * pb;
+                if (kb + 1 < KB) {
+                    pa = sa_row[kb + 1];
+                    pb = sb_blk[kb + 1];
+                }
                 int good = 1;
                 if (lane == 0) good = wait_bar(&s_tfull[b], (g / kAcc) & 1, a.st) ? 1 : 0;
                 if (!__shfl_sync(0xffffffffu, good, 0)) {
@@ -245,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_tempty[b]);
+                ++g;
             }
             if (!ok) break;
             __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + kCols * h;
@@ -372,31 +382,35 @@ __global__ void __launch_bounds__(kBsThreads, 1) grouped_gemm_fp8_bs_kernel(cons
 
     if (warp == 0) {
         // ---------------------------------------------------------------- scale factors + TMA producer
+        // The scales of K block kb + 2 are loaded while block kb is written, so their global-load
+        // latency overlaps two stages of the ring instead of stalling every TMA issue.
         uint32_t g = 0;
         int ok = 1;
         TileInfo ti;
         for (int t = blockIdx.x; ok && tile_of<kBsBN>(t, s_mt_prefix, a.num_experts, n_tiles, a.offsets, ti); t += gridDim.x) {
             const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + ti.n0 / 128) * KB;
-            for (int kb = 0; kb < KB; ++kb, ++g) {
+            // lane l covers the rows l, l + 32, l + 64, l + 96 of the tile (row group l of the atom)
+            auto fetch = [&](int kb, float (&va)[4], float& vb) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int m = ti.m0 + lane + 32 * j;
+                    va[j] = m < a.rows ? a.sa[(int64_t)m * KB + kb] : 1.f;  // 2^0 past the rows
+                }
+                vb = sb_blk[kb];
+            };
+            auto step = [&](int kb, float (&va)[4], float& vb) {
                 const int s = g % S;
                 if (lane == 0) ok = wait_bar(&s_empty[s], ((g / S) & 1) ^ 1, a.st) ? 1 : 0;
                 ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
+                if (!ok) return;
                 uint8_t* st_a = smem + (size_t)s * kBsStageBytes;
                 uint8_t* st_b = st_a + kBM * kBK;
                 uint8_t* st_sfa = st_b + kBsBN * kBK;
                 uint8_t* st_sfb = st_sfa + kSfBytes;
                 // SFA: lane l writes the 16 bytes of row group l (rows l, l+32, l+64, l+96).
-                uint4 wa;
-                uint32_t* w4 = reinterpret_cast<uint32_t*>(&wa);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int m = ti.m0 + lane + 32 * j;
-                    w4[j] = m < a.rows ? ue8m0_x4(a.sa[(int64_t)m * KB + kb]) : 0x7f7f7f7fu;  // 2^0 past the rows
-                }
-                *reinterpret_cast<uint4*>(st_sfa + lane * 16) = wa;
+                *reinterpret_cast<uint4*>(st_sfa + lane * 16) = make_uint4(ue8m0_x4(va[0]), ue8m0_x4(va[1]), ue8m0_x4(va[2]), ue8m0_x4(va[3]));
                 // SFB: the tile lies in one 128x128 weight block, so every byte is that block's scale.
-                const uint32_t wb = ue8m0_x4(sb_blk[kb]);
+                const uint32_t wb = ue8m0_x4(vb);
                 *reinterpret_cast<uint4*>(st_sfb + lane * 16) = make_uint4(wb, wb, wb, wb);
                 fence_proxy_async_smem();  // generic writes -> the tensor core's reads (async proxy)
                 __syncwarp();
@@ -405,6 +419,15 @@ __global__ void __launch_bounds__(kBsThreads, 1) grouped_gemm_fp8_bs_kernel(cons
                     tma_load_2d(st_a, &map_a, kb * kBK, ti.m0, &s_full[s]);
                     tma_load_2d(st_b, &map_b, kb * kBK, ti.e * a.n + ti.n0, &s_full[s]);
                 }
+                ++g;
+                if (kb + 2 < KB) fetch(kb + 2, va, vb);
+            };
+            float a0[4], a1[4], b0 = 1.f, b1 = 1.f;
+            fetch(0, a0, b0);
+            if (KB > 1) fetch(1, a1, b1);
+            for (int kb = 0; kb < KB && ok; kb += 2) {
+                step(kb, a0, b0);
+                if (ok && kb + 1 < KB) step(kb + 1, a1, b1);
             }
         }
         // After an expired wait: the loads already issued land before the CTA exits.

@@ -9,7 +9,7 @@ With `--time R` each workload is also timed: R repetitions, each bracketed by CU
 current stream after a 256 MB write that evicts L2, median reported in microseconds.
 Workloads (names for `--only`): layout, dispatch (count + stage/pull), combine, combine_expanded
 (weighted expanded combine, needs dispatch), low_latency, ll_logfmt, cast, quantize_weights,
-grouped_gemm, swiglu_quant (needs grouped_gemm), permute, barrier, masked_gemm, ll_dispatch_gemm,
+grouped_gemm, grouped_gemm_ue8m0 (power-of-two scales, block-scaled MMA), swiglu_quant (needs grouped_gemm), permute, barrier, masked_gemm, ll_dispatch_gemm,
 bf16_gemm, bf16_mn, bf16_wgrad, fused_dispatch_gemm (standalone stage + count + fused receive/GEMM),
 moe_backward_ops (needs dispatch and grouped_gemm), transport_checks, ll_clean, side_features (PP,
 AGRS, Engram).
@@ -89,6 +89,15 @@ def build(args):
 
     def grouped_gemm():
         state['h'] = gemm.grouped_gemm_fp8(ga, gsa, gb, gsb, goff, gcnt)
+
+    # the same shape with power-of-two scales on the block-scaled MMA path
+    ga_r, gsa_r = quant.per_token_cast_to_fp8(torch.randn((rows_per * e_g, k1), generator=g).to(torch.bfloat16).cuda(),
+                                              round_scale=True)
+    gb_r, gsb_r = gemm.quantize_weights_fp8((torch.randn((e_g, n1, k1), generator=g) * 0.02).cuda(), round_scale=True)
+    gsb_r = gsb_r.contiguous()
+
+    def grouped_gemm_ue8m0():
+        gemm.grouped_gemm_fp8(ga_r, gsa_r, gb_r, gsb_r, goff, gcnt, ue8m0=True)
 
     def swiglu():
         require_ext().swiglu_quant(state['h'], False)
@@ -196,7 +205,7 @@ def build(args):
         sb.engram_fetch(side['idx'])()
 
     work = {'layout': layout, 'dispatch': dispatch, 'combine': combine, 'low_latency': ll, 'cast': cast,
-            'grouped_gemm': grouped_gemm, 'swiglu_quant': swiglu, 'permute': perm, 'barrier': barrier}
+            'grouped_gemm': grouped_gemm, 'grouped_gemm_ue8m0': grouped_gemm_ue8m0, 'swiglu_quant': swiglu, 'permute': perm, 'barrier': barrier}
     work.update({'quantize_weights': quantize_weights, 'combine_expanded': combine_expanded, 'll_logfmt': ll_logfmt,
                  'masked_gemm': masked_gemm, 'll_dispatch_gemm': ll_dispatch_gemm, 'bf16_gemm': bf16_gemm,
                  'bf16_mn': bf16_mn, 'bf16_wgrad': bf16_wgrad, 'fused_dispatch_gemm': fused_dispatch_gemm,
