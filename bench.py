@@ -222,6 +222,12 @@ def max_over_ranks(values):
     return t.tolist()
 
 
+def min_over_ranks(v):
+    t = torch.tensor([float(v)], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return t.item()
+
+
 def sum_over_ranks(v):
     t = torch.tensor([float(v)], dtype=torch.float64, device='cuda')
     dist.all_reduce(t)
@@ -302,8 +308,11 @@ def main():
     dist.barrier()
     torch.cuda.synchronize()
 
+    from deepep_slingshot_b200.utils.nvlink_counters import NvlinkCounters
+    links = NvlinkCounters(local)  # read-only NVML per-link data counters
     sampler = ClockSampler(local)
     sampler.start()
+    link_before = links.read()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -314,6 +323,7 @@ def main():
         step()
         ends[i].record()
     torch.cuda.synchronize()
+    link_after = links.read()
     clocks = sampler.stop()
     dist.barrier()
     torch.cuda.synchronize()
@@ -332,6 +342,21 @@ def main():
     value = (total_disp + total_comb) / (ms_step * 1e-3) / 1e9
     disp_gbps_rank = disp_bytes / (ms_disp * 1e-3) / 1e9
     comb_gbps_rank = comb_bytes / (ms_comb * 1e-3) / 1e9
+    # Bytes that crossed this GPU's NVLinks per step (the GPU's own link counters, protocol overhead
+    # included) beside the algorithmic remote bytes: rows received from other ranks in the dispatch
+    # and pushed back to them in the combine (local rows never touch a link).
+    own_rows = int(((idx // E_l) == rank).any(dim=1).sum())
+    remote_rows = num_recv - own_rows
+    ok = link_before is not None and link_after is not None
+    moved = link_after - link_before if ok else None
+    # every rank joins the same reductions; -1 marks a rank without counters
+    tx, rx, payload = max_over_ranks([moved.tx_bytes / args.steps if ok else -1.0, moved.rx_bytes / args.steps if ok else -1.0,
+                                      remote_rows * ((H + H // 128 * 4 + K * 8 + K * 4) + (2 * H + K * 4))])
+    ok_all = min_over_ranks(1.0 if ok else 0.0) > 0
+    nvlink = ({'tx_bytes_per_step_max_rank': tx, 'rx_bytes_per_step_max_rank': rx,
+               'remote_payload_bytes_per_step_max_rank': payload,
+               'source': 'NVML per-link data counters, read before and after the timed steps'} if ok_all else
+              {'counters': 'unavailable (NVML NVLink byte counters not supported on every rank)'})
 
     # The same dispatch without the CPU sync on the received counts (`num_worst_tokens`: outputs sized
     # for the worst case, the CUDA-graph-compatible mode), timed the same way: it shows what the
@@ -627,11 +652,14 @@ def main():
                        'combine_dtype': 'bf16', 'num_sms': num_sms, 'l2': 'flushed before every timed step',
                        'host_cpus': getattr(args, 'host_cpus', None),
                        'byte_definition': 'DeepEP v2 logical bytes incl. local traffic, summed over ranks',
+                       'transport': ('one GPU: every byte is a local HBM copy, none crosses NVLink' if world == 1
+                                     else 'NVLink peer loads (dispatch) and stores (combine)'),
                        'baseline': f'{BASELINE_CYCLE_GBPS_PER_RANK} GB/s per rank x n_gpus (published SM100 EP8 726/740)'},
             'dispatch_ms': ms_disp, 'combine_ms': ms_comb, **nosync,
             'dispatch_gbps_per_rank': disp_gbps_rank, 'combine_gbps_per_rank': comb_gbps_rank,
             'num_recv_tokens_rank0': num_recv,
             'clocks': clocks,
+            'nvlink': nvlink,
             # this library's kernels per timed step: layout, dispatch count, stage + pull, combine
             'gpu_launches': args.steps * 4 if args.impl == 'ours' else 0,
         }
