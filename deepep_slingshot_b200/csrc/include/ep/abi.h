@@ -136,7 +136,8 @@ struct alignas(128) NormalCtrl {
     int count_cta_counts[kMaxCountCtas][kMaxRanks];
     int count_done_ctas;                        // local ticket; the last CTA exchanges counts (and resets it)
     int selftest_flag;                          // transport self-test: peers add to it, the owner waits
-    int pad1[30];
+    int probe_flag;                             // NVLink micro-probe: flag round trips (peer writes, owner waits)
+    int pad1[29];
 };
 static_assert(sizeof(NormalCtrl) % 128 == 0, "NormalCtrl alignment");
 

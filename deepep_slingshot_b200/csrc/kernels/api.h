@@ -156,6 +156,13 @@ void launch_zero_group_padding(const ZeroPaddingArgs& a, int num_groups, cudaStr
 void launch_signal_stress(int* peer_flag, int* my_flag, int producer_blocks, int warps, int rounds, int expected,
                           int* status, KernelStatus st, cudaStream_t stream);
 // The window rule of indexed peer accesses on a table of (index, count, window): kOk or kErrBounds.
+// NVLink micro-probes (transport_checks.cu). role: 0 initiator, 1 responder (one block each, on
+// two GPUs), 2 both sides as two blocks of one launch (one GPU). out_ns[block] = elapsed ns, -1 on
+// an expired wait.
+void launch_flag_pingpong(int* peer_flag, int* my_flag, int iters, int role, long long* out_ns, KernelStatus st,
+                          cudaStream_t stream);
+// vec: bytes per access (16, 8, 4, 2 or 1), dividing both addresses.
+void launch_probe_copy(void* dst, const void* src, int64_t bytes, int vec, int blocks, cudaStream_t stream);
 void launch_window_check(const int64_t* cases, int n, int* codes, cudaStream_t stream);
 
 // ---------------------------------------------------------------- barrier

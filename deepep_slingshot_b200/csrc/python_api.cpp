@@ -111,6 +111,8 @@ PYBIND11_MODULE(_C, m) {
         .def("intranode_combine", &ep::Buffer::intranode_combine)
         .def("barrier", &ep::Buffer::barrier)
         .def("selftest_signal_stress", &ep::Buffer::selftest_signal_stress)
+        .def("probe_flag_latency", &ep::Buffer::probe_flag_latency)
+        .def("probe_peer_copy", &ep::Buffer::probe_peer_copy)
         .def("clean_low_latency_buffer", &ep::Buffer::clean_low_latency_buffer)
         .def("low_latency_dispatch", &ep::Buffer::low_latency_dispatch)
         .def("low_latency_dispatch_gemm", &ep::Buffer::low_latency_dispatch_gemm)

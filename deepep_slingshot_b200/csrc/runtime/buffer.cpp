@@ -1041,6 +1041,74 @@ std::vector<int> Buffer::selftest_signal_stress(int producer_blocks, int warps, 
     return {host[0].item<int>(), host[1].item<int>()};
 }
 
+// NVLink micro-probes. Every rank calls them together, with no dispatch or combine in flight.
+// Flag round trip between rank 0 and `peer` (one GPU: between the two blocks of one launch): mean
+// round-trip ns on rank 0 and on `peer`, 0 on the other ranks; an expired wait raises.
+double Buffer::probe_flag_latency(int peer, int iters) {
+    check_error();
+    TORCH_CHECK(available_, "buffer not synced");
+    TORCH_CHECK(iters >= 1 && iters <= (1 << 20), "iters in [1, 2^20]");
+    TORCH_CHECK(num_ranks_ == 1 ? peer == 0 : (peer >= 1 && peer < num_ranks_), "peer must be another rank (0 on one GPU)");
+    const NormalLayout L = compute_normal_layout(num_nvl_bytes_, 128, num_ranks_);
+    auto ctrl_of = [&](void* base) { return reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(base) + L.ctrl_off); };
+    NormalCtrl* mine = ctrl_of(nvl_base_);
+    auto out = torch::zeros({2}, torch::dtype(torch::kInt64).device(torch::kCUDA));
+    auto stream = at::cuda::getCurrentCUDAStream();
+    EP_CUDA_CHECK(cudaMemsetAsync(&mine->probe_flag, 0, sizeof(int), stream));
+    EP_CUDA_CHECK(cudaMemsetAsync(&mine->selftest_flag, 0, sizeof(int), stream));
+    barrier(false, true);  // every flag is zero before either side writes
+    auto* ns = reinterpret_cast<long long*>(out.data_ptr<int64_t>());
+    const bool active = num_ranks_ == 1 || rank_ == 0 || rank_ == peer;
+    if (num_ranks_ == 1) launch_flag_pingpong(&mine->selftest_flag, &mine->probe_flag, iters, 2, ns, status(), stream);
+    else if (rank_ == 0) launch_flag_pingpong(&ctrl_of(nvl_peer_[peer])->probe_flag, &mine->probe_flag, iters, 0, ns, status(), stream);
+    else if (rank_ == peer) launch_flag_pingpong(&ctrl_of(nvl_peer_[0])->probe_flag, &mine->probe_flag, iters, 1, ns, status(), stream);
+    EP_CUDA_CHECK(cudaGetLastError());
+    const int64_t elapsed = out.cpu()[0].item<int64_t>();
+    barrier(false, true);  // raises if a wait expired
+    return active ? (double)elapsed / iters : 0.0;
+}
+
+// Copy `bytes` between `local` and the normal-mode region of rank (rank + shift) % R (past its
+// control block; dispatch / combine data there is overwritten), `offset` bytes in on both sides:
+// peer stores (`store`) or peer loads. Every rank copies at the same time, after a barrier. Returns
+// the `reps` CUDA-event timings of this rank's copy in milliseconds, then the access width used.
+std::vector<double> Buffer::probe_peer_copy(int shift, int64_t bytes, int64_t offset, bool store, int reps, int blocks,
+                                            const torch::Tensor& local) {
+    check_error();
+    TORCH_CHECK(available_, "buffer not synced");
+    TORCH_CHECK(shift >= 0 && shift < num_ranks_ && reps >= 1 && reps <= 1000 && blocks >= 1 && blocks <= 4096, "bad probe arguments");
+    TORCH_CHECK(local.is_cuda() && local.is_contiguous() && local.scalar_type() == torch::kUInt8, "local must be a contiguous uint8 CUDA tensor");
+    TORCH_CHECK(bytes >= 1 && offset >= 0 && offset + bytes <= local.numel(), "local tensor smaller than offset + bytes");
+    const int64_t data_off = align_up(sizeof(NormalCtrl), 4096);  // everything past the control block
+    TORCH_CHECK(offset + bytes <= num_nvl_bytes_ - data_off, "offset + bytes exceed the peer's normal-mode region");
+    uint8_t* remote = static_cast<uint8_t*>(nvl_peer_[(rank_ + shift) % num_ranks_]) + data_off + offset;
+    uint8_t* here = local.data_ptr<uint8_t>() + offset;
+    const uintptr_t both = reinterpret_cast<uintptr_t>(remote) | reinterpret_cast<uintptr_t>(here);
+    int vec = 16;
+    while (vec > 1 && (both % vec) != 0) vec >>= 1;
+    auto stream = at::cuda::getCurrentCUDAStream();
+    barrier(false, true);
+    std::vector<double> ms;
+    cudaEvent_t e0, e1;
+    EP_CUDA_CHECK(cudaEventCreate(&e0));
+    EP_CUDA_CHECK(cudaEventCreate(&e1));
+    for (int r = 0; r < reps; ++r) {
+        EP_CUDA_CHECK(cudaEventRecord(e0, stream));
+        if (store) launch_probe_copy(remote, here, bytes, vec, blocks, stream);
+        else launch_probe_copy(here, remote, bytes, vec, blocks, stream);
+        EP_CUDA_CHECK(cudaEventRecord(e1, stream));
+        EP_CUDA_CHECK(cudaEventSynchronize(e1));
+        float t = 0.f;
+        EP_CUDA_CHECK(cudaEventElapsedTime(&t, e0, e1));
+        ms.push_back(t);
+    }
+    EP_CUDA_CHECK(cudaEventDestroy(e0));
+    EP_CUDA_CHECK(cudaEventDestroy(e1));
+    barrier(false, true);
+    ms.push_back((double)vec);  // last entry: the access width used
+    return ms;
+}
+
 void Buffer::barrier(bool use_comm_stream, bool with_cpu_sync) {
     check_error();
     if (with_cpu_sync) EP_CUDA_CHECK(cudaDeviceSynchronize());

@@ -128,6 +128,9 @@ class Buffer {
     // Transport self-test (multi-producer signalling into the next rank's control block); returns
     // {status, value seen} after synchronizing. Every rank must call it together.
     std::vector<int> selftest_signal_stress(int producer_blocks, int warps, int rounds);
+    double probe_flag_latency(int peer, int iters);
+    std::vector<double> probe_peer_copy(int shift, int64_t bytes, int64_t offset, bool store, int reps, int blocks,
+                                        const torch::Tensor& local);
 
     // ---------------------------------------------------------------- low-latency mode
     void clean_low_latency_buffer(int num_max_dispatch_tokens_per_rank, int hidden, int num_experts);
