@@ -16,8 +16,9 @@ Count-driven routings (the reference replays per-expert counts of real traces,
 backend/tests/bank_routing.py:25-61; the trace data itself is not part of this library):
 `routes_from_counts` realises exact per-expert counts as a top-k table with distinct experts per
 token, `greedy_placement` / `random_placement` map logical experts to physical ids. Names:
-`zipf<s>[_greedy|_random]` (Zipf(s) expert popularity per rank) and `counts:<file.npy>[:greedy|:random]`
-(a [ranks, experts] array of per-rank counts, e.g. from a router trace).
+`zipf<s>[_greedy|_random]` (Zipf(s) expert popularity per rank), `counts:<file.npy>[:greedy|:random]`
+(a [ranks, experts] array of per-rank counts, e.g. from a router trace) and `bank:<scenario>[:greedy|:random]`
+(the built-in scenario tables of `BANK`).
 """
 from typing import Tuple
 
@@ -142,9 +143,82 @@ def zipf_counts(num_experts: int, num_tokens: int, num_topk: int, s: float, seed
     return counts
 
 
+def _spread(total: int, weights: np.ndarray, cap: int) -> np.ndarray:
+    """Integer counts proportional to `weights`, summing to `total`, none above `cap` (the overflow of
+    a capped entry goes to the others in proportion)."""
+    w = np.asarray(weights, dtype=np.float64)
+    counts = np.zeros(w.size, dtype=np.int64)
+    free = w > 0
+    left = total
+    while left > 0 and free.any():
+        share = np.where(free, w, 0.0)
+        raw = share / share.sum() * left
+        add = np.minimum(np.floor(raw).astype(np.int64), cap - counts)
+        if add.sum() == 0:  # hand out the remainder one by one, largest weights first
+            for e in np.argsort(-share):
+                if left == 0 or not free[e]:
+                    break
+                if counts[e] < cap:
+                    counts[e] += 1
+                    left -= 1
+        else:
+            counts += add
+            left -= int(add.sum())
+        free &= counts < cap
+    if left > 0:
+        raise ValueError('the capped counts cannot hold the total')
+    return counts
+
+
+# Built-in bank of per-expert count tables: named routing scenarios, deterministic per (rank, seed),
+# that stress the count-driven paths the way recorded router traces do (the reference replays per-
+# layer count tables of real traces, backend/tests/bank_routing.py:25-105; no trace is shipped
+# here, so the scenarios below are synthetic and named for the shape they produce).
+#   hot8        8 experts, the same on every rank, take half of all assignments; the rest is uniform
+#   drift       Zipf(1.2) popularity whose expert order differs per rank (rank-local hot experts)
+#   dead        a quarter of the experts (a random set shared by all ranks) receive nothing
+#   saturated   the top-k-1 most popular experts are chosen by every token (count = tokens, the cap);
+#               the last choice is uniform over the others
+BANK = ('hot8', 'drift', 'dead', 'saturated')
+
+
+def bank_counts(name: str, rank: int, num_ranks: int, N: int, E: int, K: int, seed: int) -> np.ndarray:
+    """This rank's per-expert counts (sum N * K, each <= N) for bank scenario `name`."""
+    total = N * K
+    shared = np.random.default_rng(seed)           # the same on every rank
+    local = np.random.default_rng(seed * 977 + rank)  # this rank's own
+    if name == 'hot8':
+        hot = shared.permutation(E)[:min(8, E)]
+        w = np.full(E, 0.5 / max(E - hot.size, 1))
+        w[hot] = 0.5 / hot.size
+        return _spread(total, w, N)
+    if name == 'drift':
+        w = 1.0 / np.arange(1, E + 1) ** 1.2
+        return _spread(total, w[local.permutation(E)], N)
+    if name == 'dead':
+        w = np.ones(E)
+        w[shared.permutation(E)[:E // 4]] = 0.0
+        return _spread(total, w, N)
+    if name == 'saturated':
+        if K < 2 or E <= K:
+            raise ValueError('bank scenario saturated needs 2 <= topk < experts')
+        top = shared.permutation(E)[:K - 1]
+        counts = np.zeros(E, dtype=np.int64)
+        counts[top] = N
+        rest = np.setdiff1d(np.arange(E), top)
+        counts[rest] = _spread(N, np.ones(rest.size), N)
+        return counts
+    raise ValueError(f'unknown bank scenario {name} (known: {", ".join(BANK)})')
+
+
 def _count_routing(name: str, rank: int, num_ranks: int, N: int, E: int, K: int, seed: int) -> torch.Tensor:
     placement = None
-    if name.startswith('counts:'):
+    if name.startswith('bank:'):
+        parts = name.split(':')
+        counts = bank_counts(parts[1], rank, num_ranks, N, E, K, seed)
+        placement = parts[2] if len(parts) > 2 else None
+        load = sum(bank_counts(parts[1], r, num_ranks, N, E, K, seed) for r in range(num_ranks)).astype(np.float64)
+    elif name.startswith('counts:'):
         parts = name.split(':')
         all_counts = np.load(parts[1])
         counts = np.asarray(all_counts[rank % all_counts.shape[0]], dtype=np.int64)
@@ -181,7 +255,7 @@ def make_routing(name: str, rank: int, num_ranks: int, num_tokens: int, num_expe
             raise ValueError(f'routing self keeps all top-{K} choices on the source rank, which owns only {le} experts')
         g = torch.Generator().manual_seed(seed * 100 + rank)
         return (torch.rand((N, le), generator=g).topk(K, dim=1).indices + rank * le).to(torch.int64)
-    if name.startswith('zipf') or name.startswith('counts:'):
+    if name.startswith('zipf') or name.startswith('counts:') or name.startswith('bank:'):
         return _count_routing(name, rank, R, N, E, K, seed)
     if R == 1:
         raise ValueError(f'routing {name} needs at least two ranks')

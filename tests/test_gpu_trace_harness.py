@@ -72,3 +72,22 @@ def test_ep_benchmark_harness(world, tmp_path):
         assert recs and all(x['passed'] for x in recs)
         man = json.loads(open(os.path.join(out, f'manifest-rank{r}.jsonl')).readline())
         assert man['sources'] and man['world'] == world
+
+
+def _bank_body(rank, world, out):
+    from deepep_slingshot_b200.harness.ep_benchmark import main
+    rc = main(['--models', 'qwen3', '--tokens', '512', '--dtype', 'fp8', '--routing', 'bank:hot8', 'bank:drift:greedy',
+               'bank:dead', 'bank:saturated', '--iters', '2', '--warmup', '1', '--out', out])
+    assert rc == 0
+
+
+@pytest.mark.parametrize('world', _worlds())
+def test_ep_benchmark_bank_routings(world, tmp_path):
+    """The built-in count-table scenarios through dispatch / combine, each checked exactly against the
+    oracle before it is timed (hot experts, rank-local drift with greedy placement, dead experts,
+    experts chosen by every token)."""
+    out = str(tmp_path / 'bank')
+    run_ranks(_bank_body, world, backend='nccl', args=(out,))
+    for r in range(world):
+        recs = [json.loads(l) for l in open(os.path.join(out, f'correctness-rank{r}.jsonl'))]
+        assert len({x['routing'] for x in recs}) == 4 and all(x['passed'] for x in recs)
