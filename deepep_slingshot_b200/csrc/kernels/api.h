@@ -30,16 +30,25 @@ struct StageArgs {
     int tma_rows;                // 1 (set by the launcher): rows are TMA-loaded into shared memory before quantizing
     int chunk;                   // overlapped stage: tokens per staged-chunk flag (same on every rank)
     // Standalone stage only: wait until every receiver pulled the previous dispatch (pull_done[r] >=
-    // *dispatch_epoch, read before the count step advances it).
+    // epoch - 1; with epoch 0, >= *dispatch_epoch read before the count step advances it).
     const int* pull_done;
     const int* dispatch_epoch;
     int num_ranks;
     RecordFormat rec;
     int record_stride;
+    // This dispatch's epoch (the count step's, known to the host), and the staged-chunk signalling:
+    // with signal_chunks the standalone stage releases staged[rank][chunk] = epoch in every
+    // receiver's control block as each chunk completes (stage warps of the pull always do).
+    int epoch;
+    int signal_chunks;
+    int rank;
+    PeerTable peers;
+    NormalLayout layout;
     KernelStatus st;
 };
-// Standalone stage (the fused dispatch + GEMM path runs it before the count exchange).
-void launch_dispatch_stage(const StageArgs& a, int num_sms, cudaStream_t stream);
+// Standalone stage: before the count exchange (fused dispatch + GEMM), or concurrently with the
+// count step with per-chunk signalling (normal dispatch). max_sms > 0 caps the SMs it occupies.
+void launch_dispatch_stage(const StageArgs& a, int max_sms, cudaStream_t stream);
 
 // Dispatch count step (multi-CTA): waits until every receiver has finished pulling the previous
 // dispatch, builds the ordered per-destination token lists and send_head from the routing alone
@@ -53,7 +62,6 @@ struct CountArgs {
     int cached;                      // 1: only wait for the previous pulls, reset, and exchange readiness
     int tokens_per_cta;              // multiple of the block size; grid = ceil(N / tokens_per_cta) <= kMaxCountCtas
     int expert_alignment;
-    int stage_chunks;                // staged-chunk counters to reset for this dispatch's stage
     PeerTable peers;
     NormalLayout layout;
     int* send_head;                  // [N][R]
@@ -92,8 +100,11 @@ struct PullArgs {
     int host_ticket;
     int chunk;                       // rows dealt to pipeline pairs in chunks of this size (0: contiguous)
     // Overlapped stage: with stage_warps > 0 the same launch also stages this rank's tokens (stage
-    // warps next to the pull pairs) and the pull waits per (source, chunk) for the staged flags.
+    // warps next to the pull pairs). With stage_warps > 0 or wait_staged (the stage ran as its own
+    // launch, concurrently with the count step) the pull waits per (source, chunk) for the staged
+    // flags and takes rows in wavefront order; its last block resets this rank's chunk counters.
     int stage_warps;
+    int wait_staged;
     StageArgs stage;
     KernelStatus st;
 };

@@ -141,8 +141,22 @@ __device__ __forceinline__ void stage_token_regs(const StageArgs& a, int t) {
     stage_record_meta(a, t, rec);
 }
 
-// Standalone stage kernel (before the count exchange, whose barrier then orders every peer's pull
-// after this rank's staging).
+// After a warp staged token t (its stores ordered before lane 0 by __syncwarp): count the token in
+// its chunk; the add that completes the chunk has acquired every earlier add of the chunk, so its
+// releases of staged[rank][chunk] = epoch into every receiver's control block cover the whole chunk.
+__device__ __forceinline__ void stage_signal_chunk(const StageArgs& a, int* chunk_done, int t) {
+    const int c = t / a.chunk;
+    const int target = min(a.chunk, a.num_tokens - c * a.chunk);
+    fence_proxy_async_global();  // receivers read the staging with TMA (async proxy)
+    if (atom_add_acq_rel_sys(&chunk_done[c], 1) == target - 1) {
+        for (int r = 0; r < a.num_ranks; ++r)
+            st_release_sys(&reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(a.peers.base[r]) + a.layout.ctrl_off)->staged[a.rank][c],
+                           a.epoch);
+    }
+}
+
+// Standalone stage kernel: either before the count exchange (whose barrier then orders every peer's
+// pull after this rank's staging), or concurrently with the count step with per-chunk signalling.
 __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
     // With tma_rows each warp owns one row buffer of dynamic shared memory: a single bulk copy brings
     // the whole bf16 row in (no registers held for loads in flight), the warp quantizes from there.
@@ -155,9 +169,11 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
     }
     if ((int)threadIdx.x < a.num_ranks && a.pull_done != nullptr) {
         // Receivers must have finished pulling the previous dispatch before the staging is rewritten.
-        const int prev_epoch = ld_volatile(a.dispatch_epoch);
+        const int prev_epoch = a.epoch > 0 ? a.epoch - 1 : ld_volatile(a.dispatch_epoch);
         if (prev_epoch > 0) wait_ge(&a.pull_done[threadIdx.x], prev_epoch, a.st, kErrTimeoutPullDone, threadIdx.x);
     }
+    int* chunk_done = a.signal_chunks ? reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(a.peers.base[a.rank]) + a.layout.ctrl_off)->stage_chunk_done
+                                      : nullptr;
     __syncthreads();
     if (threadIdx.x == 0) trace_end(a.st, kTraceWaitReceivers, t_start, a.num_tokens);
     if (aborted(a.st)) return;
@@ -169,6 +185,10 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
     for (int t = blockIdx.x * warps + warp_id(); t < a.num_tokens; t += total_warps) {
         if (!(a.quantize && a.tma_rows)) {
             stage_token_regs(a, t);
+            if (chunk_done != nullptr) {
+                __syncwarp();
+                if (lane == 0) stage_signal_chunk(a, chunk_done, t);
+            }
             continue;
         }
         uint8_t* rec = a.staging + (int64_t)t * a.record_stride;
@@ -188,6 +208,10 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
                                   reinterpret_cast<float*>(rec + a.rec.scale_off), a.hidden, a.round_scale != 0);
         __syncwarp();
         stage_record_meta(a, t, rec);
+        if (chunk_done != nullptr) {
+            __syncwarp();
+            if (lane == 0) stage_signal_chunk(a, chunk_done, t);
+        }
     }
     if (a.st.trace != nullptr) {
         __syncthreads();
@@ -195,8 +219,7 @@ __global__ void __launch_bounds__(256, 2) dispatch_stage_kernel(StageArgs a) {
     }
 }
 
-void launch_dispatch_stage(const StageArgs& a_in, int num_sms, cudaStream_t stream) {
-    (void)num_sms;
+void launch_dispatch_stage(const StageArgs& a_in, int max_sms, cudaStream_t stream) {
     StageArgs a = a_in;
     int blocks = (a.num_tokens + 7) / 8;
     if (blocks < 1) blocks = 1;
@@ -209,6 +232,7 @@ void launch_dispatch_stage(const StageArgs& a_in, int num_sms, cudaStream_t stre
         smem = 8 * row_bytes;
         int sm_count = 148, dev = 0;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (max_sms > 0 && max_sms < sm_count) sm_count = max_sms;
         if (blocks > 2 * sm_count) blocks = 2 * sm_count;  // grid-stride: every block resident
         cudaFuncSetAttribute(dispatch_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     }
@@ -394,7 +418,6 @@ __global__ void __launch_bounds__(kCountThreads) dispatch_count_kernel(CountArgs
             *c = 0;  // ready for the next dispatch
         }
     }
-    for (int i = tid; i < a.stage_chunks; i += nt) my_ctrl->stage_chunk_done[i] = 0;
     if (tid == 0) my_ctrl->count_done_ctas = 0;
     __syncthreads();
     const uint64_t t_wait = trace_begin(a.st);
@@ -541,21 +564,14 @@ constexpr int kStageWarps = 8;  // stage warps per pull block when the stage ove
 // staged[rank][chunk] = epoch in every receiver's control block. A warp's stores are ordered
 // before lane 0's acq_rel add by __syncwarp; the add that completes a chunk has acquired every
 // earlier add of that chunk, so its releases cover the whole chunk.
-__device__ __forceinline__ void stage_warps_run(const PullArgs& a, NormalCtrl* my_ctrl, int epoch) {
+__device__ __forceinline__ void stage_warps_run(const PullArgs& a, NormalCtrl* my_ctrl) {
     const StageArgs& sa = a.stage;
     const int lane = lane_id();
     const int gw = blockIdx.x * kStageWarps + (warp_id() - 2 * kPairs), GW = gridDim.x * kStageWarps;
     for (int t = gw; t < sa.num_tokens; t += GW) {
         stage_token_regs(sa, t);
         __syncwarp();
-        if (lane == 0) {
-            const int c = t / sa.chunk;
-            const int target = min(sa.chunk, sa.num_tokens - c * sa.chunk);
-            fence_proxy_async_global();  // receivers read the staging with TMA (async proxy)
-            if (atom_add_acq_rel_sys(&my_ctrl->stage_chunk_done[c], 1) == target - 1) {
-                for (int r = 0; r < a.num_ranks; ++r) st_release_sys(&ctrl_of(a.peers, a.layout, r)->staged[a.rank][c], epoch);
-            }
-        }
+        if (lane == 0) stage_signal_chunk(sa, my_ctrl->stage_chunk_done, t);
         if ((t & 63) == 0 && aborted(a.st)) break;
     }
 }
@@ -587,7 +603,7 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
     if (!pull_warp) {
         // Stage warps: they never wait for the pulls, so every rank's pulls make progress.
         const uint64_t t_stage = trace_begin(a.st);
-        if (a.stage_warps > 0 && !aborted(a.st)) stage_warps_run(a, my_ctrl, epoch);
+        if (a.stage_warps > 0 && !aborted(a.st)) stage_warps_run(a, my_ctrl);
         if (warp == 2 * kPairs && lane == 0 && a.stage_warps > 0) trace_end(a.st, kTraceStage, t_stage, a.stage.num_tokens);
     } else if (num_recv > a.num_out_rows) {
         if (threadIdx.x == 0 && blockIdx.x == 0) report_error(a.st, kErrCapacity, -1, num_recv);
@@ -618,11 +634,12 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
         // row of source (k + g) % R, so every pair walks every source's tokens in increasing order, at
         // the pace its stage warps release them, with the loads spread over all sources. Otherwise
         // rows are dealt in blocks (or chunks) of the receive order.
-        const bool wave = a.stage_warps > 0;
+        const bool staged_flags = (a.stage_warps > 0 || a.wait_staged) && a.stage.chunk > 0;
+        const bool wave = staged_flags;
         const int my_rows = wave ? wave_num_rows(g, P, s_prefix, R, num_recv) : pair_num_rows(g, P, num_recv, a.chunk);
         auto row_at = [&](int k) { return wave ? wave_row(g, P, k, s_prefix, R, num_recv) : pair_row(g, P, k, a.chunk, num_recv); };
         const int S = p.S;
-        const int chunk = a.stage_warps > 0 ? a.stage.chunk : 0;
+        const int chunk = staged_flags ? a.stage.chunk : 0;
 
         if (producer) {
             // After an expired wait lane 0 issues nothing more (the consumer stops at the first row that
@@ -728,6 +745,10 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
         const int old = atom_add_acq_rel_gpu(&my_ctrl->pull_finished_blocks, 1);
         if (old == (int)gridDim.x - 1) {
             my_ctrl->pull_finished_blocks = 0;
+            // every stage of this dispatch is done (stage warps of this launch, or the stage launch
+            // before it): its chunk counters start from zero for the next dispatch
+            if ((a.stage_warps > 0 || a.wait_staged) && a.stage.chunk > 0)
+                for (int c = 0; c * a.stage.chunk < a.stage.num_tokens; ++c) my_ctrl->stage_chunk_done[c] = 0;
             fence_sys();
             for (int s = 0; s < R; ++s) st_release_sys(&ctrl_of(a.peers, a.layout, s)->pull_done[a.rank], epoch);
         }

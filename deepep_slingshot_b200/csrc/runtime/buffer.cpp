@@ -217,7 +217,8 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
       low_latency_mode_(low_latency_mode),
       explicitly_destroy_(explicitly_destroy),
       enable_shrink_(enable_shrink),
-      comm_stream_(at::cuda::getStreamFromPool(true)) {
+      comm_stream_(at::cuda::getStreamFromPool(true)),
+      count_stream_(at::cuda::getStreamFromPool(true)) {
     if (num_ranks < 1 || num_ranks > kMaxRanks)
         throw std::runtime_error("B200 EP buffer: the group must be one NVLink domain of 1..8 ranks (got " +
                                  std::to_string(num_ranks) + "); internode RDMA is not available on a single box");
@@ -238,6 +239,11 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     poison_outputs_ = poison_env != nullptr && std::string(poison_env) == "1";
     const char* announce = std::getenv("DEEPEP_B200_COMBINE_ANNOUNCE");
     combine_announce_lagged_ = announce != nullptr && std::string(announce) == "lagged";
+    // Dispatch staging: "concurrent" (default) runs the stage as its own launch on the comm stream
+    // while the count step runs on a second stream, the pull after both; "warps" stages inside the
+    // pull launch (stage warps beside the pull pairs, after the count step).
+    const char* stage_mode = std::getenv("DEEPEP_B200_DISPATCH_STAGE");
+    stage_concurrent_ = stage_mode == nullptr || std::string(stage_mode) != "warps";
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
@@ -548,8 +554,7 @@ static int stage_chunk_tokens(int capacity) {
 
 // Count-step arguments shared by dispatch() and dispatch_gemm(); the caller fills the routing
 // inputs and the output tensors.
-CountArgs Buffer::count_args(const NormalLayout& L, int N, int K, int num_experts, bool cached, int expert_alignment,
-                             int stage_chunk) {
+CountArgs Buffer::count_args(const NormalLayout& L, int N, int K, int num_experts, bool cached, int expert_alignment) {
     CountArgs na{};
     na.num_tokens = N;
     na.num_topk = K;
@@ -562,7 +567,6 @@ CountArgs Buffer::count_args(const NormalLayout& L, int N, int K, int num_expert
     const int per_cta = (N + kMaxCountCtas - 1) / kMaxCountCtas;
     na.tokens_per_cta = std::max(1, (per_cta + 255) / 256) * 256;
     na.expert_alignment = std::max(1, expert_alignment);
-    na.stage_chunks = (N + stage_chunk - 1) / stage_chunk;
     na.peers = nvl_peers();
     na.layout = L;
     na.dev_num_recv = dev_workspace_ + 1;
@@ -645,7 +649,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
         num_recv_per_expert = torch::empty({E_l}, i32);
     }
     const int stage_chunk = stage_chunk_tokens(L.capacity);
-    CountArgs na = count_args(L, N, K, cached ? 0 : num_experts, cached, expert_alignment, stage_chunk);
+    CountArgs na = count_args(L, N, K, cached ? 0 : num_experts, cached, expert_alignment);
     na.topk_idx = (!cached && topk_idx.has_value()) ? topk_idx->data_ptr<int64_t>() : nullptr;
     na.is_token_in_rank = (!cached && is_token_in_rank.has_value()) ? is_token_in_rank->data_ptr<bool>() : nullptr;
     na.send_head = send_head.data_ptr<int>();
@@ -654,11 +658,8 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     na.recv_rank_prefix = cached ? nullptr : recv_rank_prefix.data_ptr<int>();
     na.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
     na.cumulative_stats = cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
-    prof_mark(stream, 0);
-    launch_dispatch_count(na, stream);
-    prof_mark(stream, 1);
-
-    // 2) the stage, run by stage warps of the pull launch (it overlaps the pulls chunk by chunk)
+    // 2) the stage: its own launch concurrent with the count step (default), or stage warps of the
+    //    pull launch; either way every chunk's completion is signalled to the receivers
     StageArgs sa{};
     sa.x = x.data_ptr();
     if (fp8_in) {
@@ -683,7 +684,33 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     sa.num_ranks = R;
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
+    sa.epoch = ticket;
+    sa.rank = rank_;
+    sa.peers = peers;
+    sa.layout = L;
     sa.st = st;
+    NormalCtrl* my_ctrl = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off);
+    sa.pull_done = my_ctrl->pull_done;
+    sa.dispatch_epoch = &my_ctrl->dispatch_epoch;
+    if (stage_concurrent_) {
+        // The count step starts on its own stream once every earlier comm-stream kernel is done (the
+        // flags it waits on for this GPU are then already set), launched first so that its CTAs take
+        // SMs before the stage's; the stage leaves a few SMs free for them. Neither waits on the
+        // other; the pull waits for both through the streams.
+        sa.signal_chunks = 1;
+        stream_wait(count_stream_, scope.comm);
+        prof_mark(count_stream_.stream(), 0);
+        launch_dispatch_count(na, count_stream_.stream());
+        prof_mark(count_stream_.stream(), 1);
+        int sm_count = 148;
+        EP_CUDA_CHECK(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device_id_));
+        launch_dispatch_stage(sa, std::max(1, sm_count - 8), stream);
+        stream_wait(scope.comm, count_stream_);
+    } else {
+        prof_mark(stream, 0);
+        launch_dispatch_count(na, stream);
+        prof_mark(stream, 1);
+    }
 
     // 3) receive size. Cached: known. Worst case (`num_worst_tokens`): no CPU sync at all. Otherwise
     //    the pull is launched at once into outputs sized for the largest possible receive
@@ -755,7 +782,8 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
     pa.host_ticket = ticket;
     pa.chunk = row_chunk_;
-    pa.stage_warps = 1;
+    pa.stage_warps = stage_concurrent_ ? 0 : 1;
+    pa.wait_staged = stage_concurrent_ ? 1 : 0;
     pa.stage = sa;
     pa.st = st;
     prof_mark(stream, 2);
@@ -853,8 +881,9 @@ Buffer::intranode_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& top
     sa.round_scale = round_scale ? 1 : 0;
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
+    sa.epoch = ticket;
     sa.st = st;
-    launch_dispatch_stage(sa, num_sms, stream);
+    launch_dispatch_stage(sa, 0, stream);
 
     // 2) count: lists, counts, 128-aligned per-expert rows, raw per-expert rows (statistics output)
     auto send_head = torch::empty({N, R}, i32);
@@ -862,7 +891,7 @@ Buffer::intranode_dispatch_gemm(const torch::Tensor& x, const torch::Tensor& top
     auto spm = torch::empty({R, R}, i32);
     auto recv_rank_prefix = torch::empty({R + 1}, i32);
     auto aligned_counts = torch::empty({E_l}, i32);
-    CountArgs na = count_args(L, N, K, num_experts, false, 128, stage_chunk_tokens(L.capacity));
+    CountArgs na = count_args(L, N, K, num_experts, false, 128);
     na.topk_idx = topk_idx.data_ptr<int64_t>();
     na.send_head = send_head.data_ptr<int>();
     na.rank_prefix_matrix = rpm.data_ptr<int>();

@@ -179,8 +179,7 @@ class Buffer {
     int num_ranks() const { return num_ranks_; }
 
    private:
-    CountArgs count_args(const NormalLayout& L, int N, int K, int num_experts, bool cached, int expert_alignment,
-                         int stage_chunk);
+    CountArgs count_args(const NormalLayout& L, int N, int K, int num_experts, bool cached, int expert_alignment);
     KernelStatus status() const;
     PeerTable nvl_peers() const;
     PeerTable ll_peers() const;
@@ -220,6 +219,8 @@ class Buffer {
     int64_t trace_capacity_ = 0;
 
     at::cuda::CUDAStream comm_stream_;
+    at::cuda::CUDAStream count_stream_;  // the dispatch count step, concurrent with the stage on comm_stream_
+    bool stage_concurrent_ = true;       // stage as its own launch next to the count step (else: stage warps of the pull)
     int dispatch_epoch_ = 0, combine_seq_ = 0, barrier_epoch_ = 0, ll_dispatch_seq_ = 0, ll_combine_seq_ = 0;
 };
 
