@@ -282,10 +282,16 @@ def main():
         return buf.dispatch(xin, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe,
                             topk_idx=ids, topk_weights=wts, config=cfg, **kw)
 
+    host_times = []  # DEEPEP_B200_BENCH_HOST_TIMES=1: host seconds spent in the dispatch and combine calls
+
     def step():
+        t0 = time.perf_counter()
         (rx, rs), ri, rw, lst, h, _ = layout_and_dispatch(x, idx, w)
+        t1 = time.perf_counter()
         state['mid'].record()
         out, out_w, _ = buf.combine(y_full[:rx.shape[0]], h, topk_weights=rw, config=cfg)
+        t2 = time.perf_counter()
+        host_times.append((t1 - t0, t2 - t1))
         state['num_recv'] = rx.shape[0]
         return out
 
@@ -665,6 +671,10 @@ def main():
         }
         if os.environ.get('DEEPEP_B200_PROFILE') == '1' and hasattr(buf, 'get_profile'):
             line['kernel_profile_rank0'] = buf.get_profile()
+        if os.environ.get('DEEPEP_B200_BENCH_HOST_TIMES') == '1':
+            timed = host_times[args.warmup:args.warmup + args.steps]
+            line['host_us_rank0'] = {'dispatch_call': 1e6 * sum(a for a, _ in timed) / len(timed),
+                                     'combine_call': 1e6 * sum(b for _, b in timed) / len(timed)}
         line.update(ll)
         line.update(moe)
         if e2e is not None:

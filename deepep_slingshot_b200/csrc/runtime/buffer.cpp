@@ -487,7 +487,9 @@ void Buffer::prof_mark(cudaStream_t stream, int point) {
 std::map<std::string, double> Buffer::get_profile() {
     std::map<std::string, double> out;
     cudaDeviceSynchronize();
-    const char* names[] = {"count", "outputs", "stage_pull", "dispatch_end", "combine", "combine_end"};
+    // count: the count step; count_to_pull: its end to the pull launch (the rest of the concurrent stage
+    // launch, or the output set-up); pull: the pull launch (with stage warps in the "warps" mode)
+    const char* names[] = {"count", "count_to_pull", "pull", "dispatch_end", "combine", "combine_end"};
     std::map<std::string, std::pair<double, int>> acc;
     for (size_t i = 0; i + 1 < prof_events_.size(); ++i) {
         const int a = prof_events_[i].first, b = prof_events_[i + 1].first;

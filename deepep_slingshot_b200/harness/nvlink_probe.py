@@ -85,7 +85,7 @@ def main() -> None:
     # the region past the control block must hold the largest copy plus its offset
     need = max(args.matrix_bytes, max(DEFAULT_SIZES) + max(DEFAULT_OFFSETS)) + (16 << 20)
     hint = max(Buffer.get_nvl_buffer_size_hint(4096, 7168, dist.get_world_size()), need)
-    buf = Buffer(dist.group.WORLD, num_nvl_bytes=hint, num_gpu_timeout_secs=10)
+    buf = Buffer(dist.group.WORLD, num_nvl_bytes=hint, num_gpu_timeout_secs=10, explicitly_destroy=True)
     report = {'world': buf.group_size,
               'flag_round_trip_ns': flag_latency(buf, args.iters),
               'store_sweep': copy_sweep(buf, store=True),

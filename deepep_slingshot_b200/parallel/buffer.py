@@ -191,7 +191,7 @@ class Buffer:
         self.runtime.clear_error()
 
     def get_profile(self) -> dict:
-        """Mean device milliseconds per phase (count / outputs / stage_pull / combine) since the last call,
+        """Mean device milliseconds per phase (count / count_to_pull / pull / combine) since the last call,
         recorded only when the process runs with DEEPEP_B200_PROFILE=1 (diagnostics; adds events)."""
         return dict(self.runtime.get_profile())
 

@@ -35,7 +35,8 @@ def _as_bytes(t: torch.Tensor) -> torch.Tensor:
 
 
 def _from_bytes(b: torch.Tensor, dtype: torch.dtype, cols: int) -> torch.Tensor:
-    return b.contiguous().view(dtype).reshape(b.shape[0], cols)
+    # a fresh copy: a one-row slice counts as contiguous but keeps the parent's row stride and offset
+    return torch.empty(b.shape, dtype=b.dtype, device=b.device).copy_(b).view(dtype).reshape(b.shape[0], cols)
 
 
 class ReferenceBuffer:

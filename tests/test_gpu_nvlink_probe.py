@@ -19,7 +19,7 @@ def _worlds():
 def _body(rank, world):
     from deepep_slingshot_b200 import Buffer
     from deepep_slingshot_b200.harness import nvlink_probe
-    buf = Buffer(dist.group.WORLD, num_nvl_bytes=64 << 20, num_gpu_timeout_secs=10)
+    buf = Buffer(dist.group.WORLD, num_nvl_bytes=64 << 20, num_gpu_timeout_secs=10, explicitly_destroy=True)
     lat = nvlink_probe.flag_latency(buf, iters=200)
     if rank == 0:
         assert all(0 < v < 1e6 for v in lat.values()), lat
