@@ -176,10 +176,14 @@ def build(args):
         quant.swiglu_backward(state['h'], state['h'][:, :n1 // 2].contiguous())
         permute.zero_group_padding([pm.x, pm.scales], pm.expert_offsets, pm.expert_counts)
 
+    probe_src = torch.randint(0, 256, ((32 << 20) + 64,), generator=g, dtype=torch.int32).to(torch.uint8).cuda()
+
     def transport_checks():
         buf.transport_selftest(64, 8, 16)
         require_ext().window_check(torch.tensor([[0, 1, 1], [5, 6, 10]], dtype=torch.int64, device='cuda'))
         buf.runtime.sample_clock()  # the trace clock alignment's %globaltimer read
+        buf.runtime.probe_flag_latency(0, 100)  # NVLink micro-probes against this GPU's own mapping
+        buf.runtime.probe_peer_copy(0, 32 << 20, 0, True, 1, 296, probe_src)
 
     def ll_clean():
         buf.clean_low_latency_buffer(T, H, E_ll)
