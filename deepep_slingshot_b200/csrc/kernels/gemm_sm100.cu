@@ -24,7 +24,9 @@
 // shared-memory feed; the two accumulators then fill all 512 TMEM columns and each epilogue thread
 // promotes 64 columns, 16 at a time.
 // Every mbarrier wait is bounded (a status is reported, the kernel returns).
+#include <algorithm>
 #include <cstdlib>
+#include <string>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -273,6 +275,233 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// CTA-pair variant (`cta_group::2`): a cluster of two CTAs computes a 256 x 256 tile with one MMA
+// of M = 256, N = 256 per 32-deep K step. Each CTA stages its own 128 rows of A and its own 128 of
+// the tile's 256 rows of B (32 KiB per K block instead of 48 KiB for a 128 x 256 tile on one CTA),
+// and the tensor cores read both CTAs' halves of B: per FLOP, half the L2 -> shared-memory traffic
+// of the 128 x 128 tile. Roles:
+//  * warp 0 of each CTA, one thread: waits for its own stage to be free, TMA-loads its halves with
+//    `cta_group::2` loads whose bytes complete on the leader CTA's full barrier (the leader expects
+//    the bytes of both CTAs);
+//  * warp 1 of the leader (cluster rank 0), one thread: four MMAs per K block into TMEM buffer
+//    g % 2 of both CTAs (each CTA's TMEM holds its 128 rows x 256 columns), then one commit to each
+//    CTA's empty barrier of the stage and one to each CTA's full barrier of the TMEM buffer;
+//  * warps 2..17 of each CTA: the per-K-block scale promotion of its own rows (as in the one-CTA
+//    kernel), then an arrive on the leader's TMEM-empty barrier (both CTAs' epilogues must drain a
+//    buffer before the next MMA writes it).
+// An expert's 128-row m-tiles are paired; the second CTA of an expert's last, odd pair computes
+// rows it does not store. Every wait is bounded; both CTAs meet in a cluster barrier before the
+// TMEM is freed and before either exits.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kPBN = 256;                    // tile columns per pair
+constexpr int kPStageBytes = (kBM + 128) * kBK;  // own A rows + own half of B (32 KiB)
+constexpr int kPCols = kPBN / 4;             // accumulator columns per epilogue thread
+
+struct PairTile {
+    int e, m0, n0, valid;  // expert, this CTA's first row, the pair's first column, rows to store
+};
+
+// Map tile index t to (expert, this CTA's m0, n0); `s_mp_prefix[e]` counts m-tile pairs.
+__device__ __forceinline__ bool pair_tile_of(int t, const int* s_mp_prefix, const int* s_mt, int E, int n_tiles,
+                                             const int* offsets, uint32_t rank, PairTile& ti) {
+    const int total = s_mp_prefix[E] * n_tiles;
+    if (t >= total) return false;
+    const int mp = t / n_tiles, nt = t % n_tiles;
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_mp_prefix[mid] <= mp) lo = mid;
+        else hi = mid - 1;
+    }
+    const int mt = 2 * (mp - s_mp_prefix[lo]) + (int)rank;
+    ti.e = lo;
+    ti.m0 = offsets[lo] + mt * kBM;
+    ti.n0 = nt * kPBN;
+    ti.valid = mt < s_mt[lo];
+    return true;
+}
+
+__device__ __forceinline__ void mma_f8_pair(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                          const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
+    __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_mp_prefix[kMaxGemmExperts + 1];
+    __shared__ int s_mt[kMaxGemmExperts];
+
+    const int warp = warp_id(), lane = lane_id();
+    const int S = a.stages;
+    const uint32_t rank = tc::cluster_ctarank();
+    const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int KB = a.k / kBK;
+    const int n_tiles = a.n / kPBN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&s_full[s], 1);   // leader: its own arrive.expect_tx (bytes of both CTAs)
+            mbar_init(&s_empty[s], 1);  // one commit from the leader's MMA thread
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_tfull[b], 1);
+            mbar_init(&s_tempty[b], 2 * kEpiWarps);  // leader: the epilogue warps of both CTAs
+        }
+        fence_mbar_init();
+        int acc = 0;
+        s_mp_prefix[0] = 0;
+        for (int e = 0; e < a.num_experts; ++e) {
+            const int rows = a.expert_counts != nullptr ? a.expert_counts[e] : a.offsets[e + 1] - a.offsets[e];
+            const int mt = (rows + kBM - 1) / kBM;
+            s_mt[e] = mt;
+            acc += (mt + 1) / 2;
+            s_mp_prefix[e + 1] = acc;
+        }
+    }
+    if (warp == 1) tc::tmem_alloc_pair(&s_tmem_base, 512);  // same warp in both CTAs
+    tc_fence_before();
+    __syncthreads();
+    tc::cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or load
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer (both CTAs)
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            PairTile ti;
+            for (int t = cluster; ok && pair_tile_of(t, s_mp_prefix, s_mt, a.num_experts, n_tiles, a.offsets, rank, ti);
+                 t += clusters) {
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int s = g % S;
+                    ok = wait_bar(&s_empty[s], ((g / S) & 1) ^ 1, a.st);
+                    if (!ok) break;
+                    uint8_t* sa_tile = smem + (size_t)s * kPStageBytes;
+                    uint8_t* sb_tile = sa_tile + kBM * kBK;
+                    if (rank == 0) mbar_arrive_expect_tx(&s_full[s], 2 * kPStageBytes);
+                    const uint32_t full_leader = tc::mapa_shared(smem_u32(&s_full[s]), 0);
+                    tc::tma_load_2d_pair(sa_tile, &map_a, kb * kBK, ti.m0, full_leader);
+                    tc::tma_load_2d_pair(sb_tile, &map_b, kb * kBK, ti.e * a.n + ti.n0 + 128 * (int)rank, full_leader);
+                }
+            }
+            // After an expired wait: the leader waits for the stages it expects before TMEM is freed.
+            if (!ok && rank == 0) ring_drain(s_full, S, (int)g, a.st, kErrTimeoutTma);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer (leader only)
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_e4m3_f32(2 * kBM, kPBN);
+            const uint32_t peer = 1;
+            uint32_t g = 0;
+            bool ok = true;
+            PairTile ti;
+            for (int t = cluster; ok && pair_tile_of(t, s_mp_prefix, s_mt, a.num_experts, n_tiles, a.offsets, 0, ti);
+                 t += clusters) {
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int s = g % S, b = g & 1;
+                    ok = wait_bar(&s_tempty[b], ((g >> 1) & 1) ^ 1, a.st) && wait_bar(&s_full[s], (g / S) & 1, a.st);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t sa_addr = smem_u32(smem + (size_t)s * kPStageBytes);
+                    const uint32_t sb_addr = sa_addr + kBM * kBK;
+                    const uint64_t da = smem_desc_sw128(sa_addr), db = smem_desc_sw128(sb_addr);
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(b * kPBN);
+#pragma unroll
+                    for (int k = 0; k < kBK / 32; ++k)
+                        mma_f8_pair(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, k > 0 ? 1u : 0u);
+                    tc::mma_commit_pair(smem_u32(&s_empty[s]));
+                    tc::mma_commit_pair(tc::mapa_shared(smem_u32(&s_empty[s]), peer));
+                    tc::mma_commit_pair(smem_u32(&s_tfull[b]));
+                    tc::mma_commit_pair(tc::mapa_shared(smem_u32(&s_tfull[b]), peer));
+                }
+            }
+            if (!ok && g > 0) wait_bar(&s_empty[(g - 1) % S], ((g - 1) / S) & 1, a.st);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue / promotion (both CTAs)
+        const int ew = warp - 2;
+        const int q = warp & 3;
+        const int h = ew >> 2;
+        const int row = 32 * q + lane;
+        uint32_t g = 0;
+        bool ok = true;
+        PairTile ti;
+        for (int t = cluster; ok && pair_tile_of(t, s_mp_prefix, s_mt, a.num_experts, n_tiles, a.offsets, rank, ti);
+             t += clusters) {
+            float acc[kPCols];
+#pragma unroll
+            for (int i = 0; i < kPCols; ++i) acc[i] = 0.f;
+            const int m = ti.m0 + row;
+            // rows past this expert's tiles (the second half of an odd pair) compute but are not stored
+            const float* sa_row = a.sa + (int64_t)min(m, a.rows - 1) * KB;
+            const float* sb_blk = a.sb + ((int64_t)ti.e * (a.n / 128) + (ti.n0 + kPCols * h) / 128) * KB;
+            float pa = sa_row[0], pb = sb_blk[0];
+            for (int kb = 0; kb < KB; ++kb) {
+                const int b = g & 1;
+                const float scale = pa * pb;
+                if (kb + 1 < KB) {
+                    pa = sa_row[kb + 1];
+                    pb = sb_blk[kb + 1];
+                }
+                int good = 1;
+                if (lane == 0) good = wait_bar(&s_tfull[b], (g >> 1) & 1, a.st) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, good, 0)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kPBN + kPCols * h);
+#pragma unroll
+                for (int c = 0; c < kPCols; c += 8) {  // 8 staged values: the register budget of 18 warps
+                    float v[8];
+                    tc::tmem_ld_8(taddr + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive_cluster(tc::mapa_shared(smem_u32(&s_tempty[b]), 0));
+                ++g;
+            }
+            if (!ok) break;
+            if (ti.valid && m < a.rows) {
+                __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + kPCols * h;
+#pragma unroll
+                for (int c = 0; c < kPCols; c += 8) {
+                    int4 o;
+                    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[c + 2 * i], acc[c + 2 * i + 1]);
+                    *reinterpret_cast<int4*>(d + c) = o;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc::cluster_sync();  // no CTA frees TMEM or exits while the other may still signal it
+    if (warp == 1) {
+        tc_fence_after();
+        tc::tmem_dealloc_pair(tmem_base, 512);
     }
 }
 
@@ -551,6 +780,42 @@ int launch_tiles(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+// CTA pairs: DEEPEP_B200_GEMM_PAIR=1 selects the cta_group::2 kernel (256 x 256 tiles) when n allows.
+bool use_pairs(int n) {
+    static const bool requested = [] {
+        const char* v = std::getenv("DEEPEP_B200_GEMM_PAIR");
+        return v != nullptr && std::string(v) == "1";
+    }();
+    return requested && n % kPBN == 0;
+}
+
+int launch_pairs(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
+    GemmArgs a = args_in;
+    CUtensorMap map_a, map_b;
+    if (!make_map_u8(&map_a, a.a, (uint64_t)a.rows, (uint64_t)a.k)) return 2;
+    if (!make_map_u8(&map_b, a.b, (uint64_t)a.num_experts * a.n, (uint64_t)a.k, 128)) return 2;
+    const int max_stages = (int)((218 * 1024 - 1024) / kPStageBytes);
+    if (a.stages <= 0) a.stages = 6;
+    if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
+    if (a.stages > max_stages) a.stages = max_stages;
+    const size_t smem = (size_t)a.stages * kPStageBytes + 1024;
+    if (cudaFuncSetAttribute(grouped_gemm_fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return 3;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::max(2, num_sms / 2 * 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, grouped_gemm_fp8_pair_kernel, map_a, map_b, a) == cudaSuccess ? 0 : 3;
+}
+
 }  // namespace
 
 int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
@@ -569,6 +834,7 @@ int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t s
         grouped_gemm_fp8_bs_kernel<<<num_sms, kBsThreads, smem, stream>>>(map_a, map_b, a);
         return cudaGetLastError() == cudaSuccess ? 0 : 3;
     }
+    if (use_pairs(args_in.n)) return launch_pairs(args_in, num_sms, stream);
     return tile_width(args_in.n) == 256 ? launch_tiles<256>(args_in, num_sms, stream)
                                         : launch_tiles<128>(args_in, num_sms, stream);
 }

@@ -37,6 +37,15 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// 8 consecutive fp32 columns of this warp's 32 TMEM lanes (one value per thread per column).
+__device__ __forceinline__ void tmem_ld_8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
 // 16 consecutive fp32 columns of this warp's 32 TMEM lanes (one value per thread per column).
 __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, float* v) {
     uint32_t r[16];
@@ -111,6 +120,57 @@ inline bool make_map_2d_box(CUtensorMap* map, CUtensorMapDataType type, int elem
 inline bool make_map_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base, uint64_t rows,
                         uint64_t cols, uint32_t box_cols) {
     return make_map_2d_box(map, type, elem_bytes, base, rows, cols, box_cols, 128);
+}
+
+}  // namespace tc
+}  // namespace ep
+
+// ------------------------------------------------------------------------------------------------
+// CTA pairs (`cta_group::2`): two CTAs of a cluster of two share one MMA of M = 256. Every shared
+// memory address below is a CTA-local offset, identical in both CTAs of the pair; `mapa` turns it
+// into the cluster address of the same object in the other CTA. No multicast form is used.
+// ------------------------------------------------------------------------------------------------
+namespace ep {
+namespace tc {
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Cluster address of the shared-memory object at CTA-local address `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2D tile into this CTA's shared memory; the bytes complete on the barrier at cluster address
+// `bar_cluster` (the pair's leader CTA holds the stage's full barrier).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+// Completion of this thread's earlier tcgen05 operations arrives once on the barrier at cluster
+// address `bar_cluster` (either CTA of the pair).
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Arrive (release, cluster scope) on the barrier at cluster address `bar_cluster`.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
 }
 
 }  // namespace tc
