@@ -72,6 +72,11 @@ struct CountArgs {
     int* dev_num_recv;               // [1]
     int* cumulative_stats;           // [E_l] optional
     int* expert_counts;              // scratch [E]: zero at entry, zero again at exit
+    // Host-mapped counts for the CPU (null: none): the last CTA writes the received-token count and
+    // the aligned per-expert counts, then `host_ticket`, as soon as the exchange is done, so a
+    // CPU-synced dispatch returns while the stage and the pull still run.
+    HostCounters* host;
+    int host_ticket;
     KernelStatus st;
 };
 void launch_dispatch_count(const CountArgs& a, cudaStream_t stream);

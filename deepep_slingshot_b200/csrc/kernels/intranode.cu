@@ -468,10 +468,16 @@ __global__ void __launch_bounds__(kCountThreads) dispatch_count_kernel(CountArgs
         if (a.cumulative_stats != nullptr) a.cumulative_stats[le] += c;
         const int al = a.expert_alignment > 1 ? (c + a.expert_alignment - 1) / a.expert_alignment * a.expert_alignment : c;
         a.num_recv_per_expert[le] = al;
+        if (a.host != nullptr) a.host->num_recv_tokens_per_expert[le] = al;
     }
     __syncthreads();
     if (tid == 0) {
         my_ctrl->dispatch_epoch = epoch;
+        if (a.host != nullptr) {
+            a.host->num_recv_tokens = *a.dev_num_recv;  // written by this thread above
+            __threadfence_system();  // the counts (every thread's, ordered by the barrier) before the ticket
+            *reinterpret_cast<volatile int*>(&a.host->ready_ticket) = a.host_ticket;
+        }
         trace_end(a.st, kTraceCount, t_start, 0);
     }
 }

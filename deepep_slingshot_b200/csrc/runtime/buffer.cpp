@@ -660,6 +660,9 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     na.recv_rank_prefix = cached ? nullptr : recv_rank_prefix.data_ptr<int>();
     na.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
     na.cumulative_stats = cumulative_local_expert_recv_stats.has_value() ? cumulative_local_expert_recv_stats->data_ptr<int>() : nullptr;
+    // the counts reach the CPU from the count step itself (a synced dispatch returns before the pull ends)
+    na.host = cached ? nullptr : host_counters_dev_;
+    na.host_ticket = ticket;
     // 2) the stage: its own launch concurrent with the count step (default), or stage warps of the
     //    pull launch; either way every chunk's completion is signalled to the receivers
     StageArgs sa{};
@@ -780,7 +783,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.recv_src_idx = cached ? nullptr : recv_src_idx.data_ptr<int>();
     pa.cached_src_idx = cached ? cached_recv_src_idx->data_ptr<int>() : nullptr;
     pa.stages = 0;
-    pa.host = cached ? nullptr : host_counters_dev_;
+    pa.host = nullptr;  // the count step wrote the host counters
     pa.num_recv_per_expert = cached ? nullptr : num_recv_per_expert->data_ptr<int>();
     pa.host_ticket = ticket;
     pa.chunk = row_chunk_;

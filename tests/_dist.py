@@ -20,7 +20,7 @@ def _worker(rank, world, port, backend, fn, args, errq):
     os.environ['MASTER_PORT'] = str(port)
     os.environ['NCCL_NVLS_ENABLE'] = os.environ.get('NCCL_NVLS_ENABLE', '0')
     try:
-        kw = dict(backend=backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        kw = dict(backend=backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
         if backend == 'nccl':
             torch.cuda.set_device(rank)
             kw['device_id'] = torch.device('cuda', rank)
