@@ -110,6 +110,10 @@ struct PullArgs {
     // flags and takes rows in wavefront order; its last block resets this rank's chunk counters.
     int stage_warps;
     int wait_staged;
+    // This dispatch's epoch when no count step ran before the pull (cached handle with the
+    // concurrent stage): the pull uses it and its last block records it as the dispatch epoch.
+    // 0: the count step set the dispatch epoch.
+    int epoch;
     StageArgs stage;
     KernelStatus st;
 };

@@ -592,7 +592,7 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
     const int R = a.num_ranks;
     const int slot_bytes = (a.rec.bytes + 127) / 128 * 128;
     NormalCtrl* my_ctrl = ctrl_of(a.peers, a.layout, a.rank);
-    const int epoch = ld_volatile(&my_ctrl->dispatch_epoch);
+    const int epoch = a.epoch > 0 ? a.epoch : ld_volatile(&my_ctrl->dispatch_epoch);
     const PipeSmem p = pipe_smem(smem, pull_warp ? pair : 0, a.stages, slot_bytes);
     if (pull_warp) pipe_init(p);
     if (threadIdx.x == 0) {
@@ -755,6 +755,7 @@ __global__ void __launch_bounds__(64 * kPairs + 32 * kStageWarps) dispatch_pull_
             // before it): its chunk counters start from zero for the next dispatch
             if ((a.stage_warps > 0 || a.wait_staged) && a.stage.chunk > 0)
                 for (int c = 0; c * a.stage.chunk < a.stage.num_tokens; ++c) my_ctrl->stage_chunk_done[c] = 0;
+            if (a.epoch > 0) my_ctrl->dispatch_epoch = a.epoch;  // no count step ran for this dispatch
             fence_sys();
             for (int s = 0; s < R; ++s) st_release_sys(&ctrl_of(a.peers, a.layout, s)->pull_done[a.rank], epoch);
         }

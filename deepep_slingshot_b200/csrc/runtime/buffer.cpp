@@ -697,7 +697,14 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     NormalCtrl* my_ctrl = reinterpret_cast<NormalCtrl*>(my_base + L.ctrl_off);
     sa.pull_done = my_ctrl->pull_done;
     sa.dispatch_epoch = &my_ctrl->dispatch_epoch;
-    if (stage_concurrent_) {
+    const bool skip_count = stage_concurrent_ && cached;
+    if (skip_count) {
+        // Cached handle: the counts and lists are known, so no count step runs. The stage waits for
+        // the receivers' previous pulls (staging reuse) and releases each chunk with this dispatch's
+        // epoch; the pull waits for every source's chunks and records the epoch when it ends.
+        sa.signal_chunks = 1;
+        launch_dispatch_stage(sa, 0, stream);
+    } else if (stage_concurrent_) {
         // The count step starts on its own stream once every earlier comm-stream kernel is done (the
         // flags it waits on for this GPU are then already set), launched first so that its CTAs take
         // SMs before the stage's; the stage leaves a few SMs free for them. Neither waits on the
@@ -789,6 +796,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     pa.chunk = row_chunk_;
     pa.stage_warps = stage_concurrent_ ? 0 : 1;
     pa.wait_staged = stage_concurrent_ ? 1 : 0;
+    pa.epoch = skip_count ? ticket : 0;
     pa.stage = sa;
     pa.st = st;
     prof_mark(stream, 2);
