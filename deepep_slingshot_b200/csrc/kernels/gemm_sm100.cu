@@ -19,10 +19,11 @@
 //  * warps 2..17: read the K-block partial with `tcgen05.ld` (four warps per TMEM lane quarter, one
 //    column quarter each), release the TMEM buffer, and accumulate sa*sb*partial in fp32 registers
 //    (the per-block scale promotion that fp32 scales need); after the last K block they write bf16 rows.
-// Tile width: 128 (default) or 256 columns (`DEEPEP_B200_GEMM_BN=256`, when N allows): a 256-wide
-// tile stages 48 KiB of A and B per 8.4 MFLOP instead of 32 KiB per 4.2 MFLOP, easing the L2 ->
-// shared-memory feed; the two accumulators then fill all 512 TMEM columns and each epilogue thread
-// promotes 64 columns, 16 at a time.
+// Tile width: 256 columns when N allows (default), else 128 (`DEEPEP_B200_GEMM_BN=128` forces it):
+// a 256-wide tile stages 48 KiB of A and B per 8.4 MFLOP instead of 32 KiB per 4.2 MFLOP and halves
+// the promotion round trips per FLOP (the promotion paces the MMA issuer); the two accumulators then
+// fill all 512 TMEM columns and each epilogue thread promotes 64 columns, 8 per TMEM load with the
+// next load in flight.
 // Every mbarrier wait is bounded (a status is reported, the kernel returns).
 #include <algorithm>
 #include <cstdlib>
@@ -241,18 +242,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                 }
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + kCols * h);
-                // TMEM -> registers kChunk columns per load (register budget at 576 threads: the kCols
-                // accumulators + kChunk staged values), then release the buffer to the MMA issuer.
-                constexpr int kChunk = kCols <= 32 ? 32 : 16;
-#pragma unroll
-                for (int c = 0; c < kCols; c += kChunk) {
-                    float v[kChunk];
-                    if constexpr (kChunk == 32) tmem_ld_32(taddr + c, v);
-                    else tmem_ld_16(taddr + c, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < kChunk; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
-                }
+                // TMEM -> registers 8 columns per load with the next load in flight (register budget at
+                // 576 threads: the kCols accumulators + 16 staged values), then release the buffer.
+                tc::tmem_promote<kCols>(taddr, scale, acc);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_tempty[b]);
@@ -473,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_pair_kernel(cons
                 for (int c = 0; c < kPCols; c += 8) {  // 8 staged values: the register budget of 18 warps
                     float v[8];
                     tc::tmem_ld_8(taddr + c, v);
-                    tmem_wait_ld();
+                    tc::tmem_wait_ld_8(v);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
                 }
@@ -753,11 +745,12 @@ bool make_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
     return tc::make_map_2d_box(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols, 128, box_rows);
 }
 
-// Tile width: 128 by default; DEEPEP_B200_GEMM_BN=256 selects 256-wide tiles when n allows.
+// Tile width: 256 when n allows (measured 187 vs 264 us on 4 x 1024 x 4096 x 7168: half the
+// promotion round trips per FLOP); DEEPEP_B200_GEMM_BN=128 forces 128-wide tiles.
 int tile_width(int n) {
     static const int requested = [] {
         const char* v = std::getenv("DEEPEP_B200_GEMM_BN");
-        return v != nullptr ? std::atoi(v) : 128;
+        return v != nullptr ? std::atoi(v) : 256;
     }();
     return requested == 256 && n % 256 == 0 ? 256 : 128;
 }

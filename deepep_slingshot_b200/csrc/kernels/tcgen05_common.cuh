@@ -46,6 +46,35 @@ __device__ __forceinline__ void tmem_ld_8(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+// Waits for this thread's outstanding tcgen05.ld and ties `v` (8 values loaded by tmem_ld_8) to the
+// wait, so no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld_8(float* v) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7])
+                 :
+                 : "memory");
+}
+// acc[0..kCols) += scale * (kCols fp32 TMEM columns from taddr), 8 columns per load with the next
+// load in flight while the current 8 are accumulated (one TMEM round trip exposed per call instead
+// of one per chunk).
+template <int kCols>
+__device__ __forceinline__ void tmem_promote(uint32_t taddr, float scale, float* acc) {
+    static_assert(kCols % 16 == 0, "pairs of 8-column chunks");
+    float va[8], vb[8];
+    tmem_ld_8(taddr, va);
+    tmem_wait_ld_8(va);
+#pragma unroll
+    for (int c = 0; c < kCols; c += 16) {
+        tmem_ld_8(taddr + c + 8, vb);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[c + i] = fmaf(scale, va[i], acc[c + i]);
+        tmem_wait_ld_8(vb);
+        if (c + 16 < kCols) tmem_ld_8(taddr + c + 16, va);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[c + 8 + i] = fmaf(scale, vb[i], acc[c + 8 + i]);
+        if (c + 16 < kCols) tmem_wait_ld_8(va);
+    }
+}
 // 16 consecutive fp32 columns of this warp's 32 TMEM lanes (one value per thread per column).
 __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, float* v) {
     uint32_t r[16];
