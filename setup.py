@@ -2,9 +2,17 @@
 
 Only Blackwell datacenter parts are targeted: every CUDA translation unit is compiled with
 `-gencode arch=compute_100a,code=sm_100a`, which also keeps torch from adding its own arch list.
-A kernel that spills registers fails the build (ptxas --warn-on-spills --warning-as-error).
+A kernel that spills registers fails the build (ptxas --warn-on-spills --warning-as-error), and
+every kernel entry's resource use (registers, shared memory, stack, spills per template instance)
+is recorded in `deepep_slingshot_b200/kernel_variants.json` (`utils/variants.py` reads it).
 """
+import json
 import os
+import re
+import subprocess
+import sys
+import tempfile
+
 from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
@@ -43,6 +51,82 @@ NVCC_FLAGS = [
 ]
 CXX_FLAGS = ["-O3", "-std=c++17", "-Wno-unused-function"]
 
+VARIANT_TABLE = os.path.join(ROOT, "deepep_slingshot_b200", "kernel_variants.json")
+
+
+def _variants_module():
+    """`deepep_slingshot_b200/utils/variants.py` loaded by path (the package itself imports the
+    extension that is being built)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_ep_variants", os.path.join(ROOT, "deepep_slingshot_b200", "utils", "variants.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def demangle(names):
+    try:
+        res = subprocess.run(["c++filt"], input="\n".join(names), capture_output=True, text=True, timeout=60)
+        lines = res.stdout.splitlines()
+        if res.returncode == 0 and len(lines) == len(names):
+            return lines
+    except (OSError, subprocess.TimeoutExpired):
+        pass
+    return list(names)
+
+
+def write_variant_table(log: str) -> None:
+    """Merge this build's per-kernel resource records into the package's kernel variant table (an
+    incremental build recompiles only some translation units; the others keep their records)."""
+    table = {}
+    if os.path.exists(VARIANT_TABLE):
+        with open(VARIANT_TABLE) as f:
+            table = json.load(f)
+    by_source = table.get("sources", {})
+    fresh = _variants_module().parse_ptxas(log, os.path.join(ROOT, CSRC))
+    for src, entries in fresh.items():
+        names = demangle([e["mangled"] for e in entries])
+        for e, n in zip(entries, names):
+            e["name"] = n
+        by_source[src] = entries
+    table = {"arch": "sm_100a", "nvcc_flags": NVCC_FLAGS, "sources": dict(sorted(by_source.items()))}
+    with open(VARIANT_TABLE, "w") as f:
+        json.dump(table, f, indent=1)
+
+
+class BuildWithVariantTable(BuildExtension):
+    """The extension build, with its compiler output captured and the ptxas resource lines of every
+    kernel entry written to `deepep_slingshot_b200/kernel_variants.json` (registers, shared memory,
+    stack and spills per template instance), then echoed."""
+
+    def build_extensions(self):
+        sys.stdout.flush()
+        sys.stderr.flush()
+        with tempfile.TemporaryFile() as log:
+            saved_out, saved_err = os.dup(1), os.dup(2)
+            os.dup2(log.fileno(), 1)
+            os.dup2(log.fileno(), 2)
+            failed = None
+            try:
+                super().build_extensions()
+            except BaseException as exc:  # re-raised after the output is restored
+                failed = exc
+            finally:
+                sys.stdout.flush()
+                sys.stderr.flush()
+                os.dup2(saved_out, 1)
+                os.dup2(saved_err, 2)
+                os.close(saved_out)
+                os.close(saved_err)
+            log.seek(0)
+            text = log.read().decode(errors="replace")
+        sys.stdout.write(text)
+        sys.stdout.flush()
+        if failed is not None:
+            raise failed
+        write_variant_table(text)
+
+
 setup(
     name="deepep_slingshot_b200",
     version="0.1.0",
@@ -55,5 +139,5 @@ setup(
             extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
         )
     ],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": BuildWithVariantTable.with_options(use_ninja=True)},
 )
