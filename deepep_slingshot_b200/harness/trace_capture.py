@@ -4,13 +4,16 @@
         --tokens 4096 --hidden 7168 --experts 256 --topk 8 --steps 3 --out trace_ep8
 
 Every rank runs warm-up steps, then `--steps` traced steps (layout + FP8 dispatch + combine, the
-benchmark's step) with the device trace ring on. Results are checked on the traced steps against the
+benchmark's step) with the device trace ring on and its host calls recorded as spans on the same
+clock (`host.step`, `host.dispatch_call`, `host.combine_call`), so the timeline shows when each
+rank's host issued and returned from its calls against its kernels and the peers'. Results are checked on the traced steps against the
 untraced ones. Rank 0 writes `trace.json` (Chrome / Perfetto timeline: one process per rank, kernel
 blocks as threads, all ranks on the host clock) and prints, per step and rank, when each phase
 started and ended relative to the step's first record on any rank, which shows inter-rank skew.
 Traced timings are for timelines only, never for benchmark numbers.
 """
 import argparse
+import contextlib
 import datetime
 import json
 import os
@@ -32,7 +35,7 @@ def main(argv=None):
     args = p.parse_args(argv)
     from .. import Buffer
     from ..utils import gate
-    from ..utils.trace import capture, gather_and_write
+    from ..utils.trace import HostSpans, capture, gather_and_write
     owns = not dist.is_initialized()
     if owns:
         local = int(os.environ.get('LOCAL_RANK', '0'))
@@ -51,12 +54,18 @@ def main(argv=None):
     y = torch.randn((N * world, H), generator=g).to(torch.bfloat16).cuda()
     outs = []
 
+    spans = HostSpans()
+    tracing = {'on': False}
+
     def step():
-        ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(idx, E)
-        (rx, rs), ri, rw, _, h, _ = buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
-                                                 num_tokens_per_expert=ntpe, topk_idx=idx, topk_weights=w,
-                                                 config=cfg, quantize_fp8=True)
-        out, _, _ = buf.combine(y[:rx.shape[0]], h, topk_weights=rw, config=cfg)
+        with (spans.span('host.step') if tracing['on'] else contextlib.nullcontext()):
+            with (spans.span('host.dispatch_call') if tracing['on'] else contextlib.nullcontext()):
+                ntpr, _, ntpe, itir, _ = buf.get_dispatch_layout(idx, E)
+                (rx, rs), ri, rw, _, h, _ = buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir,
+                                                         num_tokens_per_expert=ntpe, topk_idx=idx, topk_weights=w,
+                                                         config=cfg, quantize_fp8=True)
+            with (spans.span('host.combine_call') if tracing['on'] else contextlib.nullcontext()):
+                out, _, _ = buf.combine(y[:rx.shape[0]], h, topk_weights=rw, config=cfg)
         outs.append(out)
 
     for _ in range(args.warmup):
@@ -70,11 +79,14 @@ def main(argv=None):
         assert torch.equal(outs[-1], expected), 'traced step differs from the untraced result'
 
     dist.barrier()
+    tracing['on'] = True
     rec, offset = capture(buf, step, iterations=args.steps, group=dist.group.WORLD, check=check)
+    tracing['on'] = False
     os.makedirs(args.out, exist_ok=True)
-    trace = gather_and_write(rec, offset, os.path.join(args.out, 'trace.json'), dist.group.WORLD)
+    trace = gather_and_write(rec, offset, os.path.join(args.out, 'trace.json'), dist.group.WORLD, spans)
     if rank == 0:
-        # Phase windows per (step, rank): steps are split at each rank's stage records.
+        # Phase windows per (step, rank): steps are split at each rank's host step spans (the host
+        # clock, which the device records are aligned to).
         ev = trace['traceEvents']
         lines = []
         by_rank = {}
@@ -82,11 +94,10 @@ def main(argv=None):
             by_rank.setdefault(e['pid'], []).append(e)
         for r, es in sorted(by_rank.items()):
             es.sort(key=lambda e: e['ts'])
-            starts = sorted(e['ts'] for e in es if e['name'] == 'dispatch.stage.wait_receivers')
-            stage_starts = [t for i, t in enumerate(starts) if i == 0 or t - starts[i - 1] > 50.0]  # one per step
+            step_starts = sorted(e['ts'] for e in es if e['name'] == 'host.step')
             phases = {}
             for e in es:
-                s = sum(1 for t in stage_starts if t <= e['ts'] + 1e-6) - 1
+                s = sum(1 for t in step_starts if t <= e['ts'] + 1e-6) - 1
                 key = (s, e['name'])
                 lo, hi = phases.get(key, (1e30, -1e30))
                 phases[key] = (min(lo, e['ts']), max(hi, e['ts'] + e['dur']))

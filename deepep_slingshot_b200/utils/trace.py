@@ -7,10 +7,13 @@ compile-time pointer (backend/tests/device_trace.cuh:1-29) with host clock ping-
 overflow check that aborts the capture (backend/tests/trace_capture.py:17-69). Here the ranks of one
 box share CLOCK_MONOTONIC, so each rank maps its GPU clock onto the host clock with one bracketed
 sample (`Buffer.sample_clock`), and an overflowing ring raises instead of returning partial data.
-Traced runs are for timelines, never for timing numbers.
+Host calls can be recorded as spans on the same clock (`HostSpans`), which shows how a rank's host
+and its kernels interleave. Traced runs are for timelines, never for timing numbers.
 """
+import contextlib
 import json
-from typing import Callable, Dict, List, Optional
+import time
+from typing import Callable, Dict, List, Optional, Tuple
 
 import numpy as np
 import torch
@@ -80,9 +83,32 @@ def _union_us(starts: np.ndarray, ends: np.ndarray) -> float:
     return total / 1e3
 
 
-def to_chrome_trace(records_by_rank: Dict[int, np.ndarray], offsets_ns: Optional[Dict[int, int]] = None) -> dict:
+class HostSpans:
+    """Host-side intervals on CLOCK_MONOTONIC (the clock the device records are aligned to), so the
+    calls a rank's host makes appear on the same timeline as its kernels:
+
+        spans = HostSpans()
+        with spans.span('host.dispatch_call'):
+            buf.dispatch(...)
+    """
+
+    def __init__(self) -> None:
+        self.spans: List[Tuple[str, int, int]] = []
+
+    @contextlib.contextmanager
+    def span(self, name: str):
+        start = time.monotonic_ns()
+        try:
+            yield
+        finally:
+            self.spans.append((name, start, time.monotonic_ns()))
+
+
+def to_chrome_trace(records_by_rank: Dict[int, np.ndarray], offsets_ns: Optional[Dict[int, int]] = None,
+                    host_by_rank: Optional[Dict[int, List[Tuple[str, int, int]]]] = None) -> dict:
     """Chrome / Perfetto JSON: one process per rank, one thread per (event, block); times on the host
-    clock when `offsets_ns` (per-rank GPU-minus-host offsets) are given."""
+    clock when `offsets_ns` (per-rank GPU-minus-host offsets) are given. `host_by_rank` adds each
+    rank's host spans (host clock, thread `host`)."""
     events = []
     t0 = None
     for rank, rec in records_by_rank.items():
@@ -90,6 +116,13 @@ def to_chrome_trace(records_by_rank: Dict[int, np.ndarray], offsets_ns: Optional
         for r in rec:
             s = int(r['start_ns']) - off
             t0 = s if t0 is None else min(t0, s)
+    for rank, spans in (host_by_rank or {}).items():
+        for _, s, _ in spans:
+            t0 = s if t0 is None else min(t0, s)
+    for rank, spans in (host_by_rank or {}).items():
+        for name, s, e in spans:
+            events.append({'name': name, 'ph': 'X', 'pid': int(rank), 'tid': 'host', 'ts': (s - (t0 or 0)) / 1e3,
+                           'dur': max(e - s, 0) / 1e3, 'args': {}})
     for rank, rec in records_by_rank.items():
         off = (offsets_ns or {}).get(rank, 0)
         for r in rec:
@@ -124,14 +157,18 @@ def capture(buffer, fn: Callable[[], None], iterations: int = 1, capacity: int =
     return decode(raw), offset
 
 
-def gather_and_write(records: np.ndarray, offset_ns: int, path: Optional[str], group: dist.ProcessGroup) -> dict:
-    """All ranks: gather records + offsets to every rank; rank 0 writes the Chrome trace to `path`."""
+def gather_and_write(records: np.ndarray, offset_ns: int, path: Optional[str], group: dist.ProcessGroup,
+                     host_spans: Optional[HostSpans] = None) -> dict:
+    """All ranks: gather records, offsets and host spans to every rank; rank 0 writes the Chrome
+    trace to `path`."""
     world = group.size()
     objs: List = [None] * world
-    dist.all_gather_object(objs, (group.rank(), records.tobytes(), int(offset_ns)), group)
-    by_rank = {r: np.frombuffer(b, dtype=TRACE_DTYPE) for r, b, _ in objs}
-    offsets = {r: o for r, _, o in objs}
-    trace = to_chrome_trace(by_rank, offsets)
+    spans = host_spans.spans if host_spans is not None else []
+    dist.all_gather_object(objs, (group.rank(), records.tobytes(), int(offset_ns), spans), group)
+    by_rank = {r: np.frombuffer(b, dtype=TRACE_DTYPE) for r, b, _, _ in objs}
+    offsets = {r: o for r, _, o, _ in objs}
+    host = {r: sp for r, _, _, sp in objs if sp}
+    trace = to_chrome_trace(by_rank, offsets, host or None)
     if path and group.rank() == 0:
         with open(path, 'w') as f:
             json.dump(trace, f)

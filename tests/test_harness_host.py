@@ -341,3 +341,22 @@ def test_nccl_baseline_matches_oracle_gloo():
     the oracle returns (receive order, handle fields, combine sums), so its timings compare."""
     from tests._dist import run_ranks
     run_ranks(_nccl_baseline_body, 2, 'gloo')
+
+
+def test_host_spans_join_the_device_timeline():
+    """Host spans (host clock) and device records (GPU clock minus the rank's offset) land on one
+    timeline: a host call that starts 2 µs before a kernel appears 2 µs earlier."""
+    import time
+    from deepep_slingshot_b200.utils.trace import TRACE_DTYPE, HostSpans, to_chrome_trace
+    spans = HostSpans()
+    with spans.span('host.dispatch_call'):
+        time.sleep(0.001)
+    (name, hs, he), = spans.spans
+    assert name == 'host.dispatch_call' and he - hs >= 1_000_000
+    offset = 5_000_000_000  # GPU clock ahead of the host clock
+    rec = np.zeros(1, dtype=TRACE_DTYPE)
+    rec['start_ns'], rec['end_ns'], rec['event'] = hs + 2000 + offset, hs + 9000 + offset, 102
+    tr = to_chrome_trace({0: rec}, {0: offset}, {0: spans.spans})
+    by_name = {e['name']: e for e in tr['traceEvents']}
+    assert by_name['host.dispatch_call']['ts'] == 0.0 and by_name['host.dispatch_call']['tid'] == 'host'
+    assert by_name['dispatch.count']['ts'] == 2.0 and by_name['dispatch.count']['dur'] == 7.0
