@@ -41,6 +41,10 @@ struct StageArgs {
     // receiver's control block as each chunk completes (stage warps of the pull always do).
     int epoch;
     int signal_chunks;
+    // 1: the per-token chunk counter add is acquire-release at GPU scope (the counter is local); the
+    // release of the staged flag to the receivers stays at system scope and, by cumulativity,
+    // covers the writes of every warp whose add it observed. 0: system scope (default).
+    int signal_gpu_scope;
     int rank;
     PeerTable peers;
     NormalLayout layout;

@@ -148,7 +148,8 @@ __device__ __forceinline__ void stage_signal_chunk(const StageArgs& a, int* chun
     const int c = t / a.chunk;
     const int target = min(a.chunk, a.num_tokens - c * a.chunk);
     fence_proxy_async_global();  // receivers read the staging with TMA (async proxy)
-    if (atom_add_acq_rel_sys(&chunk_done[c], 1) == target - 1) {
+    const int before = a.signal_gpu_scope ? atom_add_acq_rel_gpu(&chunk_done[c], 1) : atom_add_acq_rel_sys(&chunk_done[c], 1);
+    if (before == target - 1) {
         for (int r = 0; r < a.num_ranks; ++r)
             st_release_sys(&reinterpret_cast<NormalCtrl*>(static_cast<uint8_t*>(a.peers.base[r]) + a.layout.ctrl_off)->staged[a.rank][c],
                            a.epoch);

@@ -244,6 +244,10 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     // pull launch (stage warps beside the pull pairs, after the count step).
     const char* stage_mode = std::getenv("DEEPEP_B200_DISPATCH_STAGE");
     stage_concurrent_ = stage_mode == nullptr || std::string(stage_mode) != "warps";
+    // Scope of the stage's per-token chunk-counter add: "sys" (default) or "gpu" (the flag release
+    // to the receivers stays at system scope either way).
+    const char* scope_env = std::getenv("DEEPEP_B200_STAGE_SIGNAL_SCOPE");
+    stage_signal_gpu_scope_ = scope_env != nullptr && std::string(scope_env) == "gpu";
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
@@ -690,6 +694,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     sa.rec = rec;
     sa.record_stride = L.record_bytes;
     sa.epoch = ticket;
+    sa.signal_gpu_scope = stage_signal_gpu_scope_ ? 1 : 0;
     sa.rank = rank_;
     sa.peers = peers;
     sa.layout = L;

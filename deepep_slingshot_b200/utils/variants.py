@@ -21,7 +21,7 @@ TABLE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SELECTION: Dict[str, str] = {
     'dispatch_layout_kernel': 'get_dispatch_layout',
     'dispatch_count_kernel': 'normal dispatch, fresh or cached handle (a cached handle with the concurrent stage skips it)',
-    'dispatch_stage_kernel': 'DEEPEP_B200_DISPATCH_STAGE=concurrent (default) and the fused dispatch + GEMM',
+    'dispatch_stage_kernel': 'DEEPEP_B200_DISPATCH_STAGE=concurrent (default) and the fused dispatch + GEMM; chunk counters at GPU scope with DEEPEP_B200_STAGE_SIGNAL_SCOPE=gpu',
     'dispatch_pull_kernel': 'normal dispatch; stage warps inside it with DEEPEP_B200_DISPATCH_STAGE=warps',
     'combine_kernel': '<false>: rows per received token; <true>: expanded rows (combine(..., row_map=...)), weighted on the sender',
     'barrier_kernel': 'Buffer.barrier',
