@@ -45,6 +45,9 @@ struct StageArgs {
     // release of the staged flag to the receivers stays at system scope and, by cumulativity,
     // covers the writes of every warp whose add it observed. 0: system scope (default).
     int signal_gpu_scope;
+    // 1 (default): the signalling lane orders the staged rows for the async proxy (fence.proxy.async)
+    // before it counts them; 0: only the receivers' fence after they acquire the flag does.
+    int writer_proxy_fence;
     int rank;
     PeerTable peers;
     NormalLayout layout;

@@ -147,7 +147,7 @@ __device__ __forceinline__ void stage_token_regs(const StageArgs& a, int t) {
 __device__ __forceinline__ void stage_signal_chunk(const StageArgs& a, int* chunk_done, int t) {
     const int c = t / a.chunk;
     const int target = min(a.chunk, a.num_tokens - c * a.chunk);
-    fence_proxy_async_global();  // receivers read the staging with TMA (async proxy)
+    if (a.writer_proxy_fence) fence_proxy_async_global();  // receivers read the staging with TMA (async proxy)
     const int before = a.signal_gpu_scope ? atom_add_acq_rel_gpu(&chunk_done[c], 1) : atom_add_acq_rel_sys(&chunk_done[c], 1);
     if (before == target - 1) {
         for (int r = 0; r < a.num_ranks; ++r)
