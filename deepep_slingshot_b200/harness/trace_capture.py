@@ -22,6 +22,26 @@ import torch
 import torch.distributed as dist
 
 
+def phase_table(events):
+    """Chrome-trace events -> one record per (rank, step, phase) with the phase's first start and last
+    end (µs, across the phase's blocks). A rank's steps are split at its `host.step` spans (host
+    clock, which the device records are aligned to); events before the first span get step -1."""
+    by_rank = {}
+    for e in events:
+        by_rank.setdefault(e['pid'], []).append(e)
+    lines = []
+    for r, es in sorted(by_rank.items()):
+        step_starts = sorted(e['ts'] for e in es if e['name'] == 'host.step')
+        phases = {}
+        for e in es:
+            s = sum(1 for t in step_starts if t <= e['ts'] + 1e-6) - 1
+            lo, hi = phases.get((s, e['name']), (1e30, -1e30))
+            phases[(s, e['name'])] = (min(lo, e['ts']), max(hi, e['ts'] + e['dur']))
+        for (s, name), (lo, hi) in sorted(phases.items()):
+            lines.append({'rank': r, 'step': s, 'phase': name, 'start_us': round(lo, 1), 'end_us': round(hi, 1)})
+    return lines
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument('--tokens', type=int, default=4096)
@@ -85,24 +105,7 @@ def main(argv=None):
     os.makedirs(args.out, exist_ok=True)
     trace = gather_and_write(rec, offset, os.path.join(args.out, 'trace.json'), dist.group.WORLD, spans)
     if rank == 0:
-        # Phase windows per (step, rank): steps are split at each rank's host step spans (the host
-        # clock, which the device records are aligned to).
-        ev = trace['traceEvents']
-        lines = []
-        by_rank = {}
-        for e in ev:
-            by_rank.setdefault(e['pid'], []).append(e)
-        for r, es in sorted(by_rank.items()):
-            es.sort(key=lambda e: e['ts'])
-            step_starts = sorted(e['ts'] for e in es if e['name'] == 'host.step')
-            phases = {}
-            for e in es:
-                s = sum(1 for t in step_starts if t <= e['ts'] + 1e-6) - 1
-                key = (s, e['name'])
-                lo, hi = phases.get(key, (1e30, -1e30))
-                phases[key] = (min(lo, e['ts']), max(hi, e['ts'] + e['dur']))
-            for (s, name), (lo, hi) in sorted(phases.items()):
-                lines.append({'rank': r, 'step': s, 'phase': name, 'start_us': round(lo, 1), 'end_us': round(hi, 1)})
+        lines = phase_table(trace['traceEvents'])
         with open(os.path.join(args.out, 'phases.jsonl'), 'w') as f:
             for l in lines:
                 f.write(json.dumps(l) + '\n')

@@ -360,3 +360,21 @@ def test_host_spans_join_the_device_timeline():
     by_name = {e['name']: e for e in tr['traceEvents']}
     assert by_name['host.dispatch_call']['ts'] == 0.0 and by_name['host.dispatch_call']['tid'] == 'host'
     assert by_name['dispatch.count']['ts'] == 2.0 and by_name['dispatch.count']['dur'] == 7.0
+
+
+def test_trace_phase_table_splits_steps_at_host_spans():
+    from deepep_slingshot_b200.harness.trace_capture import phase_table
+    ev = [
+        {'name': 'host.step', 'pid': 0, 'ts': 0.0, 'dur': 100.0},
+        {'name': 'dispatch.count', 'pid': 0, 'ts': 10.0, 'dur': 5.0},
+        {'name': 'dispatch.count', 'pid': 0, 'ts': 12.0, 'dur': 6.0},   # second block of the same phase
+        {'name': 'host.step', 'pid': 0, 'ts': 200.0, 'dur': 100.0},
+        {'name': 'dispatch.count', 'pid': 0, 'ts': 210.0, 'dur': 4.0},
+        {'name': 'host.step', 'pid': 1, 'ts': 1.0, 'dur': 100.0},
+        {'name': 'dispatch.pull', 'pid': 1, 'ts': 30.0, 'dur': 10.0},
+    ]
+    rows = {(l['rank'], l['step'], l['phase']): (l['start_us'], l['end_us']) for l in phase_table(ev)}
+    assert rows[(0, 0, 'dispatch.count')] == (10.0, 18.0)
+    assert rows[(0, 1, 'dispatch.count')] == (210.0, 214.0)
+    assert rows[(1, 0, 'dispatch.pull')] == (30.0, 40.0)
+    assert (0, 1, 'host.step') in rows and (1, 0, 'host.step') in rows
