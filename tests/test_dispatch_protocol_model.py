@@ -1,4 +1,5 @@
-"""CPU model of the normal-mode dispatch protocol across ranks, driven by random schedules.
+"""CPU models of the normal-mode dispatch and combine protocols across ranks, driven by random
+schedules.
 
 Each rank runs a sequence of dispatches, fresh (count step concurrent with the stage, then the pull)
 or with a cached handle (stage, then the pull; no count step), as the runtime launches them. The
@@ -13,6 +14,13 @@ The waits mirror the kernels': the stage and the count step wait until every rec
 pulling the previous dispatch; the count step exchanges readiness with every peer; the pull waits
 per (source, chunk) for the staged flag of its epoch; the pull's end releases `pull_done` to every
 source and, without a count step, records the epoch.
+
+The combine model runs back-to-back combines: each rank's pushers wait until the destination has
+finished its previous combine (`combine_ready`), store rows into its slots and announce them on the
+token's arrival counter; its reducers wait for the token's exact contribution count, read the rows
+and reset the counter; the rank's last block then records its sequence number and releases it to
+every rank. Checked: every reduced row is the current combine's, every counter ends at zero, no
+deadlock; a variant without the destination wait is caught.
 """
 import random
 
@@ -28,7 +36,6 @@ class Rank:
         self.notify = [0] * world             # written by peer s in its count step
         self.staged = [[0] * chunks for _ in range(world)]  # staged[s][c]: source s released chunk c at epoch
         self.staging = [0] * chunks           # version (epoch) of each chunk's rows in my staging
-        self.queue = []                       # pending actions in stream order (a list of concurrent groups)
 
 
 def build_ops(rank, plan, world, chunks):
@@ -160,3 +167,128 @@ def test_model_detects_a_missing_receiver_wait():
         assert bad > 0
     finally:
         stage_steps = original
+
+
+# ------------------------------------------------------------------------------------------------
+# Combine: push rows into the destination's slots, announce arrivals, reduce, release the slots.
+# ------------------------------------------------------------------------------------------------
+class CRank:
+    def __init__(self, world, tokens):
+        self.seq = 0                                    # combines this rank has completed
+        self.ready = [0] * world                        # ready[d]: d's completed combines (d writes)
+        self.arrival = [0] * tokens                     # per own token: contributions landed
+        self.slot = [[0] * tokens for _ in range(world)]  # slot[s][t]: version of source s's row for my token t
+
+
+def combine_push_steps(C, me, k, routes):
+    """Pushers of rank `me` for combine k: rows of the tokens it received, back to their source."""
+    start_seq = C[me].seq
+    for d, t in routes:
+        yield (lambda d=d: C[me].ready[d] >= start_seq), (lambda: None)
+
+        def store(d=d, t=t):
+            C[d].slot[me][t] = k
+        yield (lambda: True), store
+
+        def announce(d=d, t=t):
+            C[d].arrival[t] += 1
+        yield (lambda: True), announce
+
+
+def combine_reduce_steps(C, me, k, contributors, errors):
+    for t, srcs in enumerate(contributors):
+        if not srcs:
+            continue
+        yield (lambda t=t, n=len(srcs): C[me].arrival[t] == n), (lambda: None)
+
+        def reduce(t=t, srcs=srcs):
+            for s in srcs:
+                if C[me].slot[s][t] != k:
+                    errors.append((me, s, t, k, C[me].slot[s][t]))
+            C[me].arrival[t] = 0
+        yield (lambda: True), reduce
+
+
+def run_combines(world, tokens, n_combines, seed):
+    rng = random.Random(seed)
+    C = [CRank(world, tokens) for _ in range(world)]
+    errors = []
+    plans = []
+    for k in range(1, n_combines + 1):
+        # which ranks hold a row of each source token (at least its own rank in half the cases)
+        holders = [[sorted(rng.sample(range(world), rng.randint(0, world))) for _ in range(tokens)] for _ in range(world)]
+        plans.append(holders)
+    queue = [[k for k in range(1, n_combines + 1)] for _ in range(world)]
+    active = [[] for _ in range(world)]  # [generator, pending step] of the current combine's roles
+    ending = [None] * world
+    for step in range(400000):
+        for r in range(world):
+            if not active[r] and ending[r] is None and queue[r]:
+                k = queue[r].pop(0)
+                holders = plans[k - 1]
+                routes = [(d, t) for d in range(world) for t in range(tokens) if r in holders[d][t]]
+                rng.shuffle(routes)
+                gens = [combine_push_steps(C, r, k, routes),
+                        combine_reduce_steps(C, r, k, [holders[r][t] for t in range(tokens)], errors)]
+                active[r] = [[g, next(g, None)] for g in gens]
+                active[r] = [x for x in active[r] if x[1] is not None]
+                ending[r] = k
+        enabled = [(r, i) for r in range(world) for i, (g, st) in enumerate(active[r]) if st[0]()]
+        finishing = [r for r in range(world) if not active[r] and ending[r] is not None]
+        if not enabled and not finishing:
+            assert not any(queue), f'deadlock at step {step}'
+            return errors, C
+        pick = rng.randrange(len(enabled) + len(finishing))
+        if pick >= len(enabled):
+            r = finishing[pick - len(enabled)]
+            C[r].seq = ending[r]                  # the last block: seq, then release to every rank
+            for s in range(world):
+                C[s].ready[r] = ending[r]
+            ending[r] = None
+            continue
+        r, i = enabled[pick]
+        g, st = active[r][i]
+        st[1]()
+        nxt = next(g, None)
+        if nxt is None:
+            active[r].pop(i)
+        else:
+            active[r][i][1] = nxt
+    raise AssertionError('schedule did not finish')
+
+
+@pytest.mark.parametrize('seed', range(12))
+@pytest.mark.parametrize('world', [1, 2, 3])
+def test_combine_protocol_back_to_back(seed, world):
+    errors, C = run_combines(world, tokens=4, n_combines=5, seed=seed)
+    assert not errors, errors[:5]
+    assert all(c.seq == 5 for c in C) and all(a == 0 for c in C for a in c.arrival)
+
+
+def test_combine_model_detects_a_missing_ready_wait():
+    """Sanity check of the model: pushers that do not wait for the destination's previous combine
+    overwrite rows it has not reduced yet."""
+    global combine_push_steps
+    original = combine_push_steps
+
+    def no_wait(C, me, k, routes):
+        for d, t in routes:
+            def store(d=d, t=t):
+                C[d].slot[me][t] = k
+            yield (lambda: True), store
+
+            def announce(d=d, t=t):
+                C[d].arrival[t] += 1
+            yield (lambda: True), announce
+    combine_push_steps = no_wait
+    try:
+        bad = 0
+        for seed in range(40):
+            try:
+                errors, _ = run_combines(2, tokens=3, n_combines=4, seed=seed)
+            except AssertionError:
+                errors = ['deadlock']  # an early arrival can also leave a counter that never matches
+            bad += bool(errors)
+        assert bad > 0
+    finally:
+        combine_push_steps = original
