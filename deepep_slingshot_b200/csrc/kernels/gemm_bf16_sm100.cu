@@ -21,8 +21,10 @@
 //  * warp 1, one thread: four `tcgen05.mma.cta_group::1.kind::f16` (bf16 x bf16 -> fp32, M=128,
 //    N=128, K=16) per K block, accumulating the whole K range of a tile in one TMEM buffer; two
 //    buffers alternate between tiles so the epilogue of one tile overlaps the MMAs of the next;
-//  * warps 2..9: `tcgen05.ld` the finished accumulator, release it, write bf16 through a per-warp
-//    shared-memory buffer so the global stores are whole 128-byte row segments.
+//  * warps 2..9: `tcgen05.ld` the finished accumulator, release it, write the warp's 32 x 64 bf16
+//    block into its shared-memory buffer in the 128-byte swizzle pattern and hand it to one TMA 2D
+//    store (the tile leaves as bulk copies while the warp moves on; the buffer is rewritten only
+//    after the store has read it).
 // Every mbarrier wait is bounded (a status is reported, the kernel returns).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -140,6 +142,7 @@ constexpr uint64_t kStep = kMN ? (16 * 128) / 16 : 2;
 template <bool kAMN, bool kBMN>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                       const __grid_constant__ CUtensorMap map_b,
+                                                                      const __grid_constant__ CUtensorMap map_d,
                                                                       Bf16GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
@@ -268,10 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_tempty[b]);
             ++j;
-            // Each lane holds one row's 64 values; the stores go out row-contiguous instead: the warp's
-            // 32 x 64 block is written to its shared-memory buffer (16-byte chunk c of row l at chunk
-            // c ^ (l & 7), conflict-free both ways) and read back so that every store instruction
-            // writes four full 128-byte row segments, not 32 rows' 16-byte pieces.
+            // Each lane holds one row's 64 values. The warp's 32 x 64 block goes into its shared-memory
+            // buffer in the 128-byte swizzle pattern (16-byte chunk c of row l at chunk c ^ (l & 7),
+            // conflict-free), which the output tensor map also uses, and one TMA store writes it out.
+            if (lane == 0) bulk_wait_read<0>();  // the previous tile's store has read the buffer
+            __syncwarp();
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 int4 o;
@@ -280,17 +284,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_bf16_kernel(const __
                 for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(v[8 * c + 2 * i], v[8 * c + 2 * i + 1]);
                 *reinterpret_cast<int4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = o;
             }
+            fence_proxy_async_smem();  // each lane's generic writes before the async-proxy read
             __syncwarp();
-            __nv_bfloat16* d0 = static_cast<__nv_bfloat16*>(a.d) + (ti.d_row0 + 32 * q) * (int64_t)a.n + ti.n0 + 64 * h;
-#pragma unroll
-            for (int it = 0; it < 8; ++it) {
-                const int r = it * 4 + (lane >> 3), cc = lane & 7;
-                const int4 o = *reinterpret_cast<const int4*>(stg + r * 128 + ((cc ^ (r & 7)) << 4));
-                *reinterpret_cast<int4*>(d0 + (int64_t)r * a.n + cc * 8) = o;
+            if (lane == 0) {
+                tc::tma_store_2d(&map_d, ti.n0 + 64 * h, (int)(ti.d_row0 + 32 * q), stg);
+                bulk_commit();
             }
-            __syncwarp();  // the buffer is rewritten by the next tile
         }
     }
+    if (warp >= 2 && lane_id() == 0) bulk_wait<0>();  // every TMA store of this warp has completed
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -312,11 +314,11 @@ bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 }
 
 template <bool kAMN, bool kBMN>
-int launch_instance(const CUtensorMap& map_a, const CUtensorMap& map_b, const Bf16GemmArgs& a, int num_sms,
-                    cudaStream_t stream) {
+int launch_instance(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_d, const Bf16GemmArgs& a,
+                    int num_sms, cudaStream_t stream) {
     const size_t smem = (size_t)a.stages * kStageBytes + (size_t)kEpiWarps * kEpiStageBytes + 1024;
     cudaFuncSetAttribute(grouped_gemm_bf16_kernel<kAMN, kBMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    grouped_gemm_bf16_kernel<kAMN, kBMN><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
+    grouped_gemm_bf16_kernel<kAMN, kBMN><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, map_d, a);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -344,13 +346,18 @@ int launch_grouped_gemm_bf16(const Bf16GemmArgs& args_in, int num_sms, cudaStrea
                 : !make_map_bf16(&map_b, a.b, (uint64_t)a.n, (uint64_t)a.k))
             return 2;
     }
+    // Output map: D [rows, n] bf16 (mode 0) or [E * m, n] (mode 1), boxes of 32 rows x 64 columns
+    // (128 bytes, the 128-byte swizzle of the epilogue buffers).
+    CUtensorMap map_d;
+    const uint64_t d_rows = a.mode == 0 ? (uint64_t)a.rows : (uint64_t)a.num_experts * a.m;
+    if (!tc::make_map_2d_box(&map_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.d, d_rows, (uint64_t)a.n, 64, 32)) return 2;
     if (a.stages <= 0) a.stages = 5;  // 5 x 32 KiB ring + 32 KiB of epilogue store buffers
     if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
     if (a.stages > 5) a.stages = 5;
-    if (amn) return bmn ? launch_instance<true, true>(map_a, map_b, a, num_sms, stream)
-                        : launch_instance<true, false>(map_a, map_b, a, num_sms, stream);
-    return bmn ? launch_instance<false, true>(map_a, map_b, a, num_sms, stream)
-               : launch_instance<false, false>(map_a, map_b, a, num_sms, stream);
+    if (amn) return bmn ? launch_instance<true, true>(map_a, map_b, map_d, a, num_sms, stream)
+                        : launch_instance<true, false>(map_a, map_b, map_d, a, num_sms, stream);
+    return bmn ? launch_instance<false, true>(map_a, map_b, map_d, a, num_sms, stream)
+               : launch_instance<false, false>(map_a, map_b, map_d, a, num_sms, stream);
 }
 
 }  // namespace ep
