@@ -7,7 +7,9 @@ within `max_rel_diff` (the repeat runs the models in the opposite order, so drif
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m deepep_slingshot_b200.harness.ladder --out ladder_ep8
 
 State lives in `<out>/ladder_state.json`: a gate that passed is skipped on the next run; after a
-failure the ladder stops, and it runs again only with `--resume "<reason>"` (the reason is recorded).
+failure the ladder stops, and it runs again only with `--resume "<reason>"` (the reason is recorded)
+and only if a read-only GPU health check (`utils/gpu_health.py`: uncorrected ECC errors, pending
+page retirement or row remapping, hardware or thermal slowdown) finds nothing wrong.
 """
 import argparse
 import json
@@ -80,9 +82,12 @@ def save_state(path: str, state: dict) -> None:
 
 
 def run_ladder(out: str, run_gate: Callable[[dict, str], List[str]], gates: List[Dict] = GATES,
-               resume_reason: Optional[str] = None, is_leader: bool = True) -> bool:
+               resume_reason: Optional[str] = None, is_leader: bool = True,
+               health_check: Optional[Callable[[], List[str]]] = None) -> bool:
     """Run the gates in order. `run_gate(gate, gate_dir)` runs one gate and returns its validation
-    problems (empty = pass). Returns True when every gate passed."""
+    problems (empty = pass). A resume after a failed gate needs a reason and, when `health_check` is
+    given, a clean GPU health report (its problem lines, empty = healthy); both are recorded.
+    Returns True when every gate passed."""
     os.makedirs(out, exist_ok=True)
     state_path = os.path.join(out, 'ladder_state.json')
     state = load_state(state_path)
@@ -91,7 +96,13 @@ def run_ladder(out: str, run_gate: Callable[[dict, str], List[str]], gates: List
             if is_leader:
                 print(f"[ladder] gate {state['failed']} failed earlier; rerun with --resume \"<reason>\"", flush=True)
             return False
-        state['resumes'].append({'gate': state['failed'], 'reason': resume_reason, 'time': time.time()})
+        health = health_check() if health_check is not None else []
+        if health:
+            if is_leader:
+                print('[ladder] not resuming, GPU health check failed:\n  ' + '\n  '.join(health), flush=True)
+            return False
+        state['resumes'].append({'gate': state['failed'], 'reason': resume_reason, 'time': time.time(),
+                                 'health_checked': health_check is not None})
         state['failed'] = None
     for gate in gates:
         if gate['name'] in state['passed']:
@@ -142,7 +153,9 @@ def main(argv=None):
     torch.cuda.set_device(local)
     os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
     dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=torch.device('cuda', local))
-    ok = run_ladder(args.out, _run_gate_distributed, resume_reason=args.resume, is_leader=dist.get_rank() == 0)
+    from ..utils import gpu_health
+    ok = run_ladder(args.out, _run_gate_distributed, resume_reason=args.resume, is_leader=dist.get_rank() == 0,
+                    health_check=lambda: gpu_health.unhealthy(gpu_health.snapshot()))
     dist.destroy_process_group()
     return 0 if ok else 1
 
