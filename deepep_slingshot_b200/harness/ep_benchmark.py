@@ -281,6 +281,9 @@ def main(argv=None):
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--num-sms', type=int, default=0)
     p.add_argument('--out', default='ep_results')
+    p.add_argument('--spool', action='store_true',
+                   help='write the journals to local memory (/dev/shm) and let an independent copier process '
+                        'move them to --out, so written records survive a hung or killed run')
     p.add_argument('--impl', choices=['ours', 'nccl'], default='ours',
                    help="'nccl': the same cases through all_to_all_single over NCCL with torch FP8 casts (the "
                         "baseline; pair two result directories with harness.compare)")
@@ -307,7 +310,14 @@ def main(argv=None):
                                 device_id=torch.device('cuda', local))
     rank, world = dist.get_rank(), dist.get_world_size()
     os.makedirs(args.out, exist_ok=True)
-    logs = {k: _Jsonl(os.path.join(args.out, f'{k}-rank{rank}.jsonl')) for k in ('manifest', 'correctness', 'timings')}
+    copier = spool_dir = None
+    if args.spool:
+        from ..utils import result_spool
+        spool_dir = result_spool.default_spool_dir(f'{os.path.basename(os.path.abspath(args.out))}-rank{rank}-{os.getpid()}')
+        copier = result_spool.start_copier(spool_dir, args.out)
+        logs = {k: result_spool.SpoolWriter(spool_dir, f'{k}-rank{rank}.jsonl') for k in ('manifest', 'correctness', 'timings')}
+    else:
+        logs = {k: _Jsonl(os.path.join(args.out, f'{k}-rank{rank}.jsonl')) for k in ('manifest', 'correctness', 'timings')}
     logs['manifest'].write(manifest(args))
     max_tokens = max(args.tokens)
     max_hidden = max(MODELS[m][0] for m in args.models)
@@ -342,6 +352,9 @@ def main(argv=None):
                             if rank == 0:
                                 print(f'[ep_benchmark] {model} {dtype} {routing} seed {seed}: FAILED: {e}', flush=True)
     torch.cuda.synchronize()
+    if copier is not None:  # every record reaches --out before the summary reads it
+        result_spool.finish(spool_dir)
+        copier.wait(timeout=120)
     dist.barrier()
     if rank == 0:
         summarize_dir(args.out)
