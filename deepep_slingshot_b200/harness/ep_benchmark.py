@@ -199,7 +199,8 @@ def run_case(buf, ref, model, tokens, dtype, routing, seed, args, logs):
         rmax_us = rank_max(local_us)
         host_max = rank_max([max(host[args.warmup:] or [0.0])])[0]
         bytes_max = rank_max([float(nbytes)])[0]
-        rec = {'kind': 'timing', **case, 'op': op, 'bytes': nbytes, 'local_us': local_us, 'rank_max_us': rmax_us,
+        rec = {'kind': 'timing', 'rank': dist.get_rank(), **case, 'op': op, 'bytes': nbytes, 'local_us': local_us,
+               'rank_max_us': rmax_us,
                'max_host_us_per_iteration': host_max, 'bytes_rank_max': bytes_max}
         logs['timings'].write(rec)
         result[op] = rec
