@@ -1,6 +1,9 @@
-"""Fail-closed validation of an `ep_benchmark` results directory.
+"""Fail-closed validation of an `ep_benchmark` results directory (and, with `--kind`, of a
+`bench.py` line or an `nvlink_probe` report).
 
     python -m deepep_slingshot_b200.harness.validate ep_results [--max-cv 0.1] [--ranks 8]
+    python -m deepep_slingshot_b200.harness.validate bench.log --kind bench
+    python -m deepep_slingshot_b200.harness.validate probe.json --kind probe
 
 Passes (exit 0) only when:
   * every rank wrote a manifest, and all manifests agree on the world size and the source hashes
@@ -104,13 +107,89 @@ def validate(out_dir: str, max_cv: float = 0.1, ranks: int = 0) -> List[str]:
     return problems
 
 
+# The benchmark line's contract: the keys every `bench.py` JSON line carries for its driver.
+BENCH_KEYS = ('metric', 'value', 'unit', 'n_gpus', 'steps', 'warmup', 'ms_per_step', 'higher_is_better', 'scaling',
+              'vs_baseline', 'dtype', 'data', 'config', 'clocks', 'gpu_launches')
+BENCH_CONFIG_KEYS = ('model', 'global_batch', 'seq_len', 'parallelism', 'l2')
+THROTTLE_REASONS = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown')
+
+
+def validate_bench_line(line: dict) -> List[str]:
+    """Fail-closed check of one `bench.py` line (this library's arm): contract keys, sane values,
+    an end-to-end number with its host transfer bytes, kernels launched, and no thermal or hardware
+    slowdown during the timed steps."""
+    if line.get('impl') == 'reference' and 'unavailable' in line:
+        return []  # the reference arm's documented unavailability line
+    problems = [f'missing key {k}' for k in BENCH_KEYS if k not in line]
+    cfg = line.get('config') or {}
+    problems += [f'missing config.{k}' for k in BENCH_CONFIG_KEYS if k not in cfg]
+    if problems:
+        return problems
+    if not (isinstance(line['value'], (int, float)) and line['value'] > 0):
+        problems.append(f"value {line['value']!r} is not a positive number")
+    if line['warmup'] < 3:
+        problems.append(f"warmup {line['warmup']} < 3")
+    if line['scaling'] not in ('weak', 'strong'):
+        problems.append(f"scaling {line['scaling']!r}")
+    if line.get('impl', 'ours') == 'ours':
+        if not line['gpu_launches']:
+            problems.append('gpu_launches is 0: no kernel of this library ran in the timed region')
+        e2e = line.get('e2e')
+        if e2e is not None:
+            for k in ('value', 'unit', 'h2d_bytes_per_step', 'd2h_bytes_per_step'):
+                if k not in e2e:
+                    problems.append(f'missing e2e.{k}')
+            if e2e.get('h2d_bytes_per_step', 0) <= 0:
+                problems.append('e2e copies no inputs from the host')
+    reasons = set((line['clocks'] or {}).get('reasons', []))
+    bad = sorted(reasons & set(THROTTLE_REASONS))
+    if bad:
+        problems.append(f"clock slowdown during the timed steps: {', '.join(bad)}")
+    return problems
+
+
+def validate_probe(report: dict) -> List[str]:
+    """Fail-closed check of an `nvlink_probe` report: a positive finite round trip per peer, a
+    positive bandwidth in every sweep row, a complete per-pair matrix."""
+    problems = []
+    world = report.get('world')
+    if not isinstance(world, int) or world < 1:
+        return ['missing or bad world size']
+    lat = report.get('flag_round_trip_ns') or {}
+    if len(lat) != max(1, world - 1):
+        problems.append(f'round trips for {len(lat)} peers, expected {max(1, world - 1)}')
+    problems += [f'round trip to {k}: {v!r}' for k, v in lat.items() if not (isinstance(v, (int, float)) and 0 < v < 1e7)]
+    for kind in ('store_sweep', 'load_sweep'):
+        rows = report.get(kind)
+        if not rows:
+            problems.append(f'missing {kind}')
+            continue
+        problems += [f"{kind}: {r.get('bytes')} B at offset {r.get('offset')}: {r.get('gbps')!r} GB/s"
+                     for r in rows if not (r.get('gbps') or 0) > 0]
+    for kind in ('store_matrix_gbps', 'load_matrix_gbps'):
+        m = report.get(kind)
+        if not m or len(m) != world or any(len(row) != world or min(row) <= 0 for row in m):
+            problems.append(f'{kind} is not a complete {world} x {world} matrix of positive rates')
+    return problems
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument('out_dir')
+    p.add_argument('out_dir', help='ep_benchmark results directory, bench.py output file (--kind bench) or '
+                                   'nvlink_probe report (--kind probe)')
+    p.add_argument('--kind', choices=['ep', 'bench', 'probe'], default='ep')
     p.add_argument('--max-cv', type=float, default=0.1)
     p.add_argument('--ranks', type=int, default=0)
     args = p.parse_args(argv)
-    problems = validate(args.out_dir, args.max_cv, args.ranks)
+    if args.kind == 'bench':
+        with open(args.out_dir) as f:
+            lines = [json.loads(l) for l in f if l.strip().startswith('{')]
+        problems = ['no JSON line'] if not lines else [x for l in lines for x in validate_bench_line(l)]
+    elif args.kind == 'probe':
+        with open(args.out_dir) as f:
+            problems = validate_probe(json.load(f))
+    else:
+        problems = validate(args.out_dir, args.max_cv, args.ranks)
     for x in problems:
         print('FAIL', x)
     print('VALID' if not problems else f'INVALID ({len(problems)} problems)')
