@@ -81,6 +81,9 @@ def parse():
     p.add_argument('--moe-steps', type=int, default=3)
     p.add_argument('--moe-fused-dispatch', action='store_true',
                    help='MoE forward with the dispatch receive fused into the gate/up GEMM (Buffer.dispatch_gemm)')
+    p.add_argument('--moe-fused-combine', action='store_true',
+                   help='MoE forward with the down projection sending its rows into the combine slots '
+                        '(parallel.gemm_combine) instead of grouped GEMM -> combine')
     p.add_argument('--ll-moe', action='store_true',
                    help='also time the decode MoE layer (MoEFFN.forward_low_latency) at the low-latency shape')
     p.add_argument('--check', action='store_true', help='verify against the torch oracle before timing')
@@ -462,6 +465,7 @@ def main():
         from deepep_slingshot_b200.models import moe as _moe_mod
         inter = 2048
         _moe_mod._FUSED_DISPATCH['enabled'] = args.moe_fused_dispatch
+        _moe_mod._FUSED_COMBINE['enabled'] = args.moe_fused_combine
         gm = torch.Generator().manual_seed(4321)
         layer = MoEFFN(buf, H, inter, E, K, config=cfg, init_std=0.02, generator=gm)
         mx = torch.randn((N, H), generator=gm).to(torch.bfloat16).cuda().requires_grad_(True)
@@ -513,6 +517,8 @@ def main():
                               'routing': 'zipf s=1.1', 'grads': 'set to None before every step (zero_grad(set_to_none=True))',
                               'forward': 'fp8 block-scaled tcgen05 grouped GEMMs' +
                               (', dispatch receive fused into the gate/up GEMM' if args.moe_fused_dispatch else '') +
+                              (', down projection sends its rows into the combine slots (fused combine)'
+                               if args.moe_fused_combine and not args.moe_fused_dispatch else '') +
                               (', power-of-two (UE8M0) scales applied by the MMA' if _moe_mod._UE8M0['enabled'] else
                                ', fp32 scales promoted per 128-deep K block'),
                               'backward': {'tcgen05_mn': 'bf16 tcgen05 grouped GEMMs on MN-major operands (no transposes), '
@@ -524,6 +530,7 @@ def main():
                               'roofline': ('slowest rank of max(its fp8 fwd at 2x bf16 peak + bf16 bwd at measured '
                                            '1650 TFLOP/s over its expert rows, its NVLink bytes per direction at 770 GB/s, '
                                            '8 bytes per local weight element per step at measured 6558 GB/s HBM)')}}
+        layer.release()
         del layer
         torch.cuda.empty_cache()
 

@@ -243,6 +243,11 @@ struct alignas(128) SymCtrl {
     int barrier_signal[kMaxRanks];                    // written by peer r: barrier epoch
     int agrs_session_signal[kMaxRanks];               // written by peer r: AGRS session it finished
     int agrs_recv_signal[kMaxAgrsSlots][kMaxRanks];   // written by peer r: its copy of slot s arrived (value = session)
+    // Down projection with the combine send as its epilogue (one region per layer, epochs from the host).
+    int gc_done[kMaxRanks];   // written by peer r: last epoch whose rows r stored into my slots
+    int gc_free[kMaxRanks];   // written by peer r: last epoch r finished reducing (its slots are free)
+    int gc_send_blocks;       // local: GEMM CTAs that finished the send (reset by the last one)
+    int gc_reduce_blocks;     // local: reduce blocks that finished (reset by the last one)
 };
 static_assert(sizeof(SymCtrl) <= kSymCtrlBytes, "SymCtrl must fit in the control block");
 

@@ -22,11 +22,46 @@ struct GemmArgs {
     int rows, n, k, num_experts;
     int stages;
     int block_scaled;         // 1: scales are powers of two, applied by the block-scaled MMA (UE8M0)
+    // Combine send as the epilogue (row_dest != null; fp32-scale kernel only): row m also goes, bf16,
+    // to slot gc_slot_of(row_dest[m]) of rank gc_rank_of(row_dest[m]) (negative: nowhere) in the
+    // slot area of that rank's GEMM-combine region, and `d` may be null (rows not kept locally).
+    // Before its first store every CTA waits until each rank released its slots of epoch
+    // gc_epoch - 1; the last CTA to finish publishes gc_epoch in gc_done[gc_rank] of every rank.
+    const int* row_dest;      // [rows]
+    PeerTable gc_regions;     // region bases ([SymCtrl | slots]) of every rank
+    int gc_rank, gc_num_ranks, gc_epoch;
+    int64_t gc_slots;         // slots per rank
     KernelStatus st;
 };
 
 // Returns 0 on success, 1 bad shapes, 2 tensor-map encode failure, 3 launch failure.
 int launch_grouped_gemm_fp8(const GemmArgs& a, int num_sms, cudaStream_t stream);
+
+// Down projection -> combine (gemm_combine.cu), the two steps around the sending GEMM:
+// the destination word of every operand row from the dispatch handle and the permute's row map,
+// and the source rank's reduction of its slots once every rank's rows have landed.
+struct GcRowDestArgs {
+    const int* row_map;             // [num_recv][num_topk] operand row of (received token, k), -1 none
+    const int* recv_src_idx;        // [num_recv] token index on its source rank
+    const int* rank_prefix_matrix;  // [R][R] from the dispatch
+    int* row_dest;                  // [rows] out, preset to -1
+    int num_recv, num_topk, rows, rank, num_ranks;
+    int64_t slots;                  // slots per rank
+    KernelStatus st;
+};
+void launch_gc_row_dest(const GcRowDestArgs& a, cudaStream_t stream);
+
+struct GcReduceArgs {
+    PeerTable regions;              // region bases of every rank (flags are released into them)
+    int rank, num_ranks, epoch;
+    const int64_t* topk_idx;        // [num_tokens][num_topk] this rank's own routing (-1: none)
+    const float* topk_weights;      // [num_tokens][num_topk] (null: weight 1)
+    void* out;                      // [num_tokens][hidden] bf16
+    int num_tokens, num_topk, hidden;
+    int64_t slots;
+    KernelStatus st;
+};
+void launch_gc_reduce(const GcReduceArgs& a, int num_sms, cudaStream_t stream);
 
 // bf16 grouped GEMMs with both operands K-major (gemm_bf16_sm100.cu).
 //   mode 0 (M-grouped): a [rows][k], b [E*n][k], d [rows][n]; rows of expert e at offsets[e], 128-aligned

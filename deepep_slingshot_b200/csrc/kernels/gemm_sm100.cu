@@ -33,6 +33,7 @@
 #include <cuda_bf16.h>
 
 #include "../include/ep/device.cuh"
+#include "../include/ep/gemm_combine.cuh"
 #include "gemm.h"
 #include "tcgen05_common.cuh"
 
@@ -109,7 +110,8 @@ __device__ __forceinline__ bool tile_of(int t, const int* s_mt_prefix, int E, in
 
 }  // namespace
 
-template <int kBN>
+// kSend: the combine send is the epilogue (GemmArgs::row_dest); the plain instance is unchanged.
+template <int kBN, bool kSend>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                      const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
     constexpr int kStageBytes = kStageBytesT<kBN>;
@@ -121,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
     __shared__ __align__(8) uint64_t s_tfull[kAcc], s_tempty[kAcc];
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_mt_prefix[kMaxGemmExperts + 1];
+    __shared__ int s_send_ok;
 
     const int warp = warp_id(), lane = lane_id();
     const int S = a.stages;
@@ -144,6 +147,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
             const int rows = a.expert_counts != nullptr ? a.expert_counts[e] : a.offsets[e + 1] - a.offsets[e];
             acc += (rows + kBM - 1) / kBM;
             s_mt_prefix[e + 1] = acc;
+        }
+        if constexpr (kSend) {
+            // Every destination's slots must be free: it finished reducing the previous epoch (the
+            // wait is normally satisfied at once; the GEMM's own work does not depend on it).
+            s_send_ok = 1;
+            const SymCtrl* mine = static_cast<const SymCtrl*>(a.gc_regions.base[a.gc_rank]);
+            for (int r = 0; r < a.gc_num_ranks; ++r)
+                if (!wait_ge(&mine->gc_free[r], a.gc_epoch - 1, a.st, kErrTimeoutCombineReady, r)) {
+                    s_send_ok = 0;
+                    break;
+                }
         }
     }
     if (warp == 1) {  // TMEM allocation: one warp, power-of-two columns
@@ -251,14 +265,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
                 ++g;
             }
             if (!ok) break;
-            __nv_bfloat16* d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + kCols * h;
+            __nv_bfloat16* d = nullptr;
+            if (!kSend || a.d != nullptr) d = static_cast<__nv_bfloat16*>(a.d) + (int64_t)m * a.n + ti.n0 + kCols * h;
+            __nv_bfloat16* peer = nullptr;  // the row's combine slot on its source rank (kSend)
+            if constexpr (kSend) {
+                const int dest = (s_send_ok && m < a.rows) ? a.row_dest[m] : -1;
+                if (dest >= 0) {
+                    const int r = gc_rank_of(dest), slot = gc_slot_of(dest);
+                    if (r < a.gc_num_ranks && slot < a.gc_slots)
+                        peer = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(a.gc_regions.base[r]) + kSymCtrlBytes) +
+                               (int64_t)slot * a.n + ti.n0 + kCols * h;
+                    else
+                        report_error(a.st, kErrBounds, r, slot);
+                }
+            }
 #pragma unroll
             for (int c = 0; c < kCols; c += 8) {
                 int4 o;
                 __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(acc[c + 2 * i], acc[c + 2 * i + 1]);
-                *reinterpret_cast<int4*>(d + c) = o;
+                if constexpr (!kSend) {
+                    *reinterpret_cast<int4*>(d + c) = o;
+                } else {
+                    if (d != nullptr) *reinterpret_cast<int4*>(d + c) = o;
+                    if (peer != nullptr) *reinterpret_cast<int4*>(peer + c) = o;
+                }
             }
         }
     }
@@ -267,6 +299,23 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_kernel(const __g
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+    if constexpr (kSend) {
+        if (threadIdx.x == 0) {
+            // Every thread's slot stores precede the barrier above; the system fence orders them
+            // before the counter, and the last CTA publishes the epoch in every rank's gc_done. After
+            // an error nothing is published: the reducers' bounded waits then report it too.
+            SymCtrl* mine = static_cast<SymCtrl*>(a.gc_regions.base[a.gc_rank]);
+            fence_sys();
+            const int old = atom_add_acq_rel_gpu(&mine->gc_send_blocks, 1);
+            if (old == (int)gridDim.x - 1) {
+                mine->gc_send_blocks = 0;
+                fence_sys();
+                if (!aborted(a.st))
+                    for (int r = 0; r < a.gc_num_ranks; ++r)
+                        st_release_sys(&static_cast<SymCtrl*>(a.gc_regions.base[r])->gc_done[a.gc_rank], a.gc_epoch);
+            }
+        }
     }
 }
 
@@ -755,7 +804,7 @@ int tile_width(int n) {
     return requested == 256 && n % 256 == 0 ? 256 : 128;
 }
 
-template <int kBN>
+template <int kBN, bool kSend>
 int launch_tiles(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     constexpr int kStageBytes = kStageBytesT<kBN>;
     GemmArgs a = args_in;
@@ -768,8 +817,8 @@ int launch_tiles(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
     if (a.stages > max_stages) a.stages = max_stages;
     const size_t smem = (size_t)a.stages * kStageBytes + 1024;
-    cudaFuncSetAttribute(grouped_gemm_fp8_kernel<kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    grouped_gemm_fp8_kernel<kBN><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
+    cudaFuncSetAttribute(grouped_gemm_fp8_kernel<kBN, kSend>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    grouped_gemm_fp8_kernel<kBN, kSend><<<num_sms, kThreads, smem, stream>>>(map_a, map_b, a);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -813,6 +862,14 @@ int launch_pairs(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
 
 int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     if (args_in.k % kBK != 0 || args_in.n % 128 != 0 || args_in.num_experts > kMaxGemmExperts || args_in.rows <= 0) return 1;
+    if (args_in.row_dest != nullptr) {
+        // Combine send epilogue: the one-CTA fp32-scale kernel only.
+        const GemmArgs& a = args_in;
+        if (a.block_scaled || a.gc_num_ranks <= 0 || a.gc_num_ranks > kMaxRanks || a.gc_rank < 0 ||
+            a.gc_rank >= a.gc_num_ranks || a.gc_slots <= 0 || a.gc_slots > kGcMaxSlots || a.gc_epoch <= 0)
+            return 1;
+        return tile_width(a.n) == 256 ? launch_tiles<256, true>(a, num_sms, stream) : launch_tiles<128, true>(a, num_sms, stream);
+    }
     if (args_in.block_scaled) {
         GemmArgs a = args_in;
         CUtensorMap map_a, map_b;
@@ -828,8 +885,8 @@ int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t s
         return cudaGetLastError() == cudaSuccess ? 0 : 3;
     }
     if (use_pairs(args_in.n)) return launch_pairs(args_in, num_sms, stream);
-    return tile_width(args_in.n) == 256 ? launch_tiles<256>(args_in, num_sms, stream)
-                                        : launch_tiles<128>(args_in, num_sms, stream);
+    return tile_width(args_in.n) == 256 ? launch_tiles<256, false>(args_in, num_sms, stream)
+                                        : launch_tiles<128, false>(args_in, num_sms, stream);
 }
 
 }  // namespace ep

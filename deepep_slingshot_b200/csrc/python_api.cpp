@@ -145,7 +145,9 @@ PYBIND11_MODULE(_C, m) {
         .def("agrs_get_inplace_tensor", &ep::SymmetricRegion::agrs_get_inplace_tensor)
         .def("all_gather", &ep::SymmetricRegion::all_gather)
         .def("engram_write", &ep::SymmetricRegion::engram_write)
-        .def("engram_fetch", &ep::SymmetricRegion::engram_fetch);
+        .def("engram_fetch", &ep::SymmetricRegion::engram_fetch)
+        .def("gemm_combine_send", &ep::SymmetricRegion::gemm_combine_send)
+        .def("gemm_combine_reduce", &ep::SymmetricRegion::gemm_combine_reduce);
 
     ep::register_ops(m);
 }

@@ -12,6 +12,8 @@
 #include <string>
 
 #include "../include/ep/schedule.cuh"
+#include "../kernels/gemm.h"
+#include "../include/ep/gemm_combine.cuh"
 #include "../kernels/symmetric_ops.h"
 #include "buffer.hpp"
 
@@ -378,6 +380,131 @@ std::function<torch::Tensor()> SymmetricRegion::engram_fetch(const torch::Tensor
         done->block(at::cuda::getCurrentCUDAStream());
         return out;
     };
+}
+
+// =================================================================================================
+// Down projection -> combine
+// =================================================================================================
+torch::Tensor SymmetricRegion::gemm_combine_send(const torch::Tensor& a, const torch::Tensor& sa, const torch::Tensor& b,
+                                                 const torch::Tensor& sb, const torch::Tensor& offsets,
+                                                 const std::optional<torch::Tensor>& counts, const torch::Tensor& row_map,
+                                                 const torch::Tensor& recv_src_idx, const torch::Tensor& rank_prefix_matrix,
+                                                 bool keep_local, int num_sms) {
+    require_available();
+    check_error();
+    TORCH_CHECK(!gc_pending_, "gemm_combine_send: the previous send has not been reduced (call gemm_combine_reduce)");
+    TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.is_contiguous() && a.scalar_type() == torch::kFloat8_e4m3fn,
+                "a must be a contiguous [rows, k] e4m3 CUDA tensor");
+    TORCH_CHECK(b.is_cuda() && b.dim() == 3 && b.is_contiguous() && b.scalar_type() == torch::kFloat8_e4m3fn,
+                "b must be a contiguous [experts, n, k] e4m3 CUDA tensor");
+    const int rows = (int)a.size(0), k = (int)a.size(1), E = (int)b.size(0), n = (int)b.size(1);
+    TORCH_CHECK(rows > 0 && b.size(2) == k && k % 128 == 0 && n % 128 == 0, "k and n must be multiples of 128");
+    TORCH_CHECK(sa.scalar_type() == torch::kFloat32 && sa.is_contiguous() && sa.dim() == 2 && sa.size(0) == rows &&
+                    sa.size(1) == k / 128,
+                "sa must be contiguous [rows, k/128] fp32");
+    TORCH_CHECK(sb.scalar_type() == torch::kFloat32 && sb.is_contiguous() && sb.dim() == 3 && sb.size(0) == E &&
+                    sb.size(1) == n / 128 && sb.size(2) == k / 128,
+                "sb must be contiguous [experts, n/128, k/128] fp32");
+    TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.is_contiguous() && offsets.numel() == E + 1,
+                "offsets must be [experts + 1] int32");
+    if (counts.has_value())
+        TORCH_CHECK(counts->scalar_type() == torch::kInt32 && counts->is_contiguous() && counts->numel() == E,
+                    "counts must be [experts] int32");
+    TORCH_CHECK(row_map.is_cuda() && row_map.scalar_type() == torch::kInt32 && row_map.dim() == 2 && row_map.is_contiguous(),
+                "row_map must be the permute's contiguous [received tokens, top-k] int32 map");
+    const int num_recv = (int)row_map.size(0), K = (int)row_map.size(1);
+    TORCH_CHECK(K >= 1 && K <= 32, "top-k must be 1..32");
+    TORCH_CHECK(recv_src_idx.scalar_type() == torch::kInt32 && recv_src_idx.is_contiguous() && recv_src_idx.numel() == num_recv,
+                "recv_src_idx must be the dispatch handle's [received tokens] int32 source indices");
+    TORCH_CHECK(rank_prefix_matrix.scalar_type() == torch::kInt32 && rank_prefix_matrix.is_contiguous() &&
+                    rank_prefix_matrix.numel() == (int64_t)num_ranks_ * num_ranks_,
+                "rank_prefix_matrix must be the dispatch handle's [ranks, ranks] int32 matrix");
+    const int64_t slots = std::min<int64_t>(data_bytes_ / ((int64_t)n * 2), kGcMaxSlots);
+    TORCH_CHECK(slots > 0, "the region holds no row of this hidden size");
+    if (num_sms <= 0) EP_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device_id_));
+
+    auto stream = at::cuda::getCurrentCUDAStream();
+    auto i32 = torch::dtype(torch::kInt32).device(torch::kCUDA, device_id_);
+    auto row_dest = torch::full({rows}, -1, i32);
+    GcRowDestArgs ra{};
+    ra.row_map = row_map.data_ptr<int>();
+    ra.recv_src_idx = recv_src_idx.data_ptr<int>();
+    ra.rank_prefix_matrix = rank_prefix_matrix.data_ptr<int>();
+    ra.row_dest = row_dest.data_ptr<int>();
+    ra.num_recv = num_recv;
+    ra.num_topk = K;
+    ra.rows = rows;
+    ra.rank = rank_;
+    ra.num_ranks = num_ranks_;
+    ra.slots = slots;
+    ra.st = status();
+    launch_gc_row_dest(ra, stream);
+    EP_CUDA_CHECK(cudaGetLastError());
+
+    torch::Tensor y = keep_local ? torch::empty({rows, n}, a.options().dtype(torch::kBFloat16))
+                                 : torch::empty({0, n}, a.options().dtype(torch::kBFloat16));
+    GemmArgs g{};
+    g.a = a.data_ptr();
+    g.sa = sa.data_ptr<float>();
+    g.b = b.data_ptr();
+    g.sb = sb.data_ptr<float>();
+    g.offsets = offsets.data_ptr<int>();
+    g.expert_counts = counts.has_value() ? counts->data_ptr<int>() : nullptr;
+    g.d = keep_local ? y.data_ptr() : nullptr;
+    g.rows = rows;
+    g.n = n;
+    g.k = k;
+    g.num_experts = E;
+    g.row_dest = row_dest.data_ptr<int>();
+    for (int r = 0; r < num_ranks_; ++r) g.gc_regions.base[r] = peer_[r];
+    g.gc_rank = rank_;
+    g.gc_num_ranks = num_ranks_;
+    g.gc_epoch = gc_epoch_ + 1;
+    g.gc_slots = slots;
+    g.st = status();
+    const int rc = launch_grouped_gemm_fp8(g, num_sms, stream);
+    TORCH_CHECK(rc == 0, "gemm_combine_send: GEMM launch failed (code " + std::to_string(rc) + ")");
+    ++gc_epoch_;
+    gc_hidden_ = n;
+    gc_topk_ = K;
+    gc_pending_ = true;
+    return y;
+}
+
+torch::Tensor SymmetricRegion::gemm_combine_reduce(const torch::Tensor& topk_idx, const std::optional<torch::Tensor>& topk_weights,
+                                                   int num_sms) {
+    require_available();
+    check_error();
+    TORCH_CHECK(gc_pending_, "gemm_combine_reduce: no gemm_combine_send to reduce");
+    TORCH_CHECK(topk_idx.is_cuda() && topk_idx.dim() == 2 && topk_idx.is_contiguous() && topk_idx.scalar_type() == torch::kInt64,
+                "topk_idx must be this rank's contiguous [tokens, top-k] int64 routing");
+    const int N = (int)topk_idx.size(0), K = (int)topk_idx.size(1);
+    TORCH_CHECK(K == gc_topk_, "top-k differs from the send's row map");
+    if (topk_weights.has_value())
+        TORCH_CHECK(topk_weights->scalar_type() == torch::kFloat32 && topk_weights->is_contiguous() && topk_weights->dim() == 2 &&
+                        topk_weights->size(0) == N && topk_weights->size(1) == K,
+                    "topk_weights must be contiguous [tokens, top-k] fp32");
+    const int64_t slots = std::min<int64_t>(data_bytes_ / ((int64_t)gc_hidden_ * 2), kGcMaxSlots);
+    TORCH_CHECK((int64_t)N * K <= slots, "more tokens x top-k than the region's slots");
+    if (num_sms <= 0) EP_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device_id_));
+    auto out = torch::empty({N, gc_hidden_}, torch::dtype(torch::kBFloat16).device(torch::kCUDA, device_id_));
+    GcReduceArgs r{};
+    for (int q = 0; q < num_ranks_; ++q) r.regions.base[q] = peer_[q];
+    r.rank = rank_;
+    r.num_ranks = num_ranks_;
+    r.epoch = gc_epoch_;
+    r.topk_idx = topk_idx.data_ptr<int64_t>();
+    r.topk_weights = topk_weights.has_value() ? topk_weights->data_ptr<float>() : nullptr;
+    r.out = out.data_ptr();
+    r.num_tokens = N;
+    r.num_topk = K;
+    r.hidden = gc_hidden_;
+    r.slots = slots;
+    r.st = status();
+    launch_gc_reduce(r, num_sms, at::cuda::getCurrentCUDAStream());
+    EP_CUDA_CHECK(cudaGetLastError());
+    gc_pending_ = false;
+    return out;
 }
 
 }  // namespace ep

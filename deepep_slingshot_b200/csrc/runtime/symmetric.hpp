@@ -64,6 +64,21 @@ public:
     void engram_write(const torch::Tensor& storage);
     std::function<torch::Tensor()> engram_fetch(const torch::Tensor& indices, int num_sms);
 
+    // ---- down projection with the combine send as its epilogue (normal-mode MoE layer)
+    // Receiver side: the grouped FP8 GEMM y = a b_e^T (fp32 block scales) whose epilogue stores every
+    // row of (received token j, k) into slot (recv_src_idx[j], k) of j's source rank over NVLink.
+    // Returns y when `keep_local` (an empty tensor otherwise). Collective: every rank sends, then
+    // every rank reduces, in the same order (epochs are host counters, so not graph-replayable).
+    torch::Tensor gemm_combine_send(const torch::Tensor& a, const torch::Tensor& sa, const torch::Tensor& b,
+                                    const torch::Tensor& sb, const torch::Tensor& offsets,
+                                    const std::optional<torch::Tensor>& counts, const torch::Tensor& row_map,
+                                    const torch::Tensor& recv_src_idx, const torch::Tensor& rank_prefix_matrix,
+                                    bool keep_local, int num_sms);
+    // Source side: out [tokens, hidden] bf16 = sum over k with topk_idx >= 0 of weight * slot (t, k),
+    // in fp32, once every rank's rows of the last send have landed.
+    torch::Tensor gemm_combine_reduce(const torch::Tensor& topk_idx, const std::optional<torch::Tensor>& topk_weights,
+                                      int num_sms);
+
 private:
     KernelStatus status() const;
     SymCtrl* ctrl_of(int r) const { return static_cast<SymCtrl*>(peer_[r]); }
@@ -83,6 +98,8 @@ private:
     int* abort_flag_ = nullptr;
     at::cuda::CUDAStream copy_stream_;
     int barrier_epoch_ = 0;
+    int gc_epoch_ = 0, gc_hidden_ = 0, gc_topk_ = 0;
+    bool gc_pending_ = false;  // a send awaits its reduce
 
     // pipeline
     int64_t pp_max_bytes_ = 0;

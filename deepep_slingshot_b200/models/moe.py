@@ -40,6 +40,11 @@ _BWD = {'mode': os.environ.get('DEEPEP_B200_MOE_BWD', 'tcgen05_mn')}
 # output) is a power of two, and the grouped GEMMs let the tensor core apply the scales
 # (`grouped_gemm_fp8(..., ue8m0=True)`, kind::mxf8f6f4.block_scale) instead of promoting every K block.
 _UE8M0 = {'enabled': os.environ.get('DEEPEP_B200_MOE_UE8M0', '0') == '1'}
+# DEEPEP_B200_MOE_FUSED_COMBINE=1: the down projection's epilogue sends every row into its token's
+# combine slot on the source rank and the source reduces its slots (parallel.gemm_combine) instead of
+# grouped GEMM -> weighted expanded combine. fp32-scale GEMMs after the plain dispatch only (not with
+# UE8M0 or the fused dispatch, whose handle rows past the received count are not row-mapped).
+_FUSED_COMBINE = {'enabled': os.environ.get('DEEPEP_B200_MOE_FUSED_COMBINE', '0') == '1'}
 
 
 def _aligned_rows(per_expert, alignment: int = 128) -> int:
@@ -97,7 +102,7 @@ def _expert_grads(g_y, a, h, xf, offsets, counts, w1, w2, inter):
 class _MoEFunction(torch.autograd.Function):
 
     @staticmethod
-    def forward(ctx, x, topk_idx, topk_weights, w1, w2, buffer, num_experts, config):
+    def forward(ctx, x, topk_idx, topk_weights, w1, w2, buffer, num_experts, config, gemm_combine=None):
         E_l = w1.shape[0]
         inter = w1.shape[1] // 2
         ue8m0 = _UE8M0['enabled'] and not _FUSED_DISPATCH['enabled']
@@ -123,9 +128,16 @@ class _MoEFunction(torch.autograd.Function):
             h = grouped_gemm_fp8(p.x, p.scales, w1q, w1s.contiguous(), p.expert_offsets, p.expert_counts, ue8m0=ue8m0)
         a, aq, as_ = require_ext().swiglu_quant(h, ue8m0)
         w2q, w2s = quantize_weights_fp8(w2.detach(), round_scale=ue8m0)
-        y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts, ue8m0=ue8m0)
-        # Top-k weighted reduction of the grouped rows, bf16 cast and exchange in one kernel.
-        out, _, _ = buffer.combine(y, handle, config=config, row_map=p.row_map, row_weights=rw)
+        if gemm_combine is not None and not ue8m0 and not _FUSED_DISPATCH['enabled']:
+            # The down projection's epilogue sends each row to its token's slot on the source rank;
+            # the source sums its slots with its own top-k weights. y stays local for the backward.
+            y = gemm_combine.send(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts, p.row_map, handle,
+                                  keep_local=True)
+            out = gemm_combine.reduce(topk_idx, topk_weights)
+        else:
+            y = grouped_gemm_fp8(aq, as_, w2q, w2s.contiguous(), p.expert_offsets, p.expert_counts, ue8m0=ue8m0)
+            # Top-k weighted reduction of the grouped rows, bf16 cast and exchange in one kernel.
+            out, _, _ = buffer.combine(y, handle, config=config, row_map=p.row_map, row_weights=rw)
         ctx.buffer, ctx.config, ctx.inter, ctx.rows = buffer, config, inter, rows
         ctx.handle = handle
         ctx.save_for_backward(p.x, p.scales, p.row_map, p.expert_offsets, p.expert_counts, rw, h, a, y, w1, w2)
@@ -145,7 +157,7 @@ class _MoEFunction(torch.autograd.Function):
         g_xp, g_w1, g_w2 = _expert_grads(g_y, a[:R], h[:R], xf, offsets, counts, w1, w2, inter)
         # permute^T (sum of each received token's rows) fused with dispatch^T = combine (sum over ranks)
         g_x, g_topk_w, _ = buffer.combine(g_xp, ctx.handle, topk_weights=g_rw, config=config, row_map=row_map)
-        return g_x, None, g_topk_w, g_w1, g_w2, None, None, None
+        return g_x, None, g_topk_w, g_w1, g_w2, None, None, None, None
 
 
 class MoEFFN(torch.nn.Module):
@@ -171,7 +183,26 @@ class MoEFFN(torch.nn.Module):
 
     def forward(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
         return _MoEFunction.apply(x, topk_idx, topk_weights, self.w1, self.w2, self.buffer, self.num_experts,
-                                  self.config)
+                                  self.config, self._gemm_combine(topk_idx))
+
+    def _gemm_combine(self, topk_idx: torch.Tensor):
+        """The layer's GEMM-combine region when DEEPEP_B200_MOE_FUSED_COMBINE=1 (created at the first
+        forward, a collective call; its slots hold the buffer's token capacity on every rank)."""
+        if not _FUSED_COMBINE['enabled'] or _UE8M0['enabled'] or _FUSED_DISPATCH['enabled']:
+            return None
+        gc = getattr(self, '_gc', None)
+        if gc is None:
+            from ..parallel.gemm_combine import GemmCombine
+            gc = GemmCombine(self.buffer.group, self.buffer.get_capacity(self.hidden), topk_idx.shape[1], self.hidden)
+            self._gc = gc
+        return gc
+
+    def release(self) -> None:
+        """Free the layer's GEMM-combine region (collective: every rank calls it)."""
+        gc = getattr(self, '_gc', None)
+        if gc is not None:
+            gc.destroy()
+            self._gc = None
 
     def quantized_weights(self):
         """FP8 weights with 128x128 scales (w1q, w1s, w2q, w2s), re-quantized only after the bf16

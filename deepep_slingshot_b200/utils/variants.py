@@ -33,7 +33,10 @@ SELECTION: Dict[str, str] = {
     'per_token_cast_back_kernel': 'ops.quant.per_token_cast_back',
     'quantize_weights_fp8_kernel': 'ops.gemm.quantize_weights_fp8',
     'swiglu_quant_kernel': 'ops.quant.swiglu_quant',
-    'grouped_gemm_fp8_kernel': '<256>: N % 256 == 0 (default), <128>: otherwise or DEEPEP_B200_GEMM_BN=128',
+    'grouped_gemm_fp8_kernel': '<256, *>: N % 256 == 0 (default), <128, *>: otherwise or DEEPEP_B200_GEMM_BN=128; '
+                               '<*, true>: GemmCombine.send (the combine send as the epilogue)',
+    'gc_row_dest_kernel': 'GemmCombine.send (destination of every operand row)',
+    'gc_reduce_kernel': 'GemmCombine.reduce (source-side top-k weighted sum of the combine slots)',
     'grouped_gemm_fp8_bs_kernel': 'grouped_gemm_fp8(..., ue8m0=True) (power-of-two scales, block-scaled MMA)',
     'grouped_gemm_fp8_pair_kernel': 'DEEPEP_B200_GEMM_PAIR=1 and N % 256 == 0 (CTA pairs, cta_group::2)',
     'grouped_gemm_bf16_kernel': '<A MN-major, B MN-major>: operand layouts of grouped_gemm_bf16 / _wgrad_rows',

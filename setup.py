@@ -32,6 +32,7 @@ SOURCES = [
     os.path.join(CSRC, "kernels", "gemm_sm100.cu"),
     os.path.join(CSRC, "kernels", "gemm_bf16_sm100.cu"),
     os.path.join(CSRC, "kernels", "gemm_masked_sm100.cu"),
+    os.path.join(CSRC, "kernels", "gemm_combine.cu"),
     os.path.join(CSRC, "kernels", "fused_dispatch_gemm.cu"),
     os.path.join(CSRC, "kernels", "symmetric_ops.cu"),
     os.path.join(CSRC, "kernels", "transport_checks.cu"),

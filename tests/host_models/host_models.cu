@@ -7,7 +7,10 @@
 //      order, never overwrites an unconsumed slot and never deadlocks, under random interleavings;
 //   3. LogFMT-10 packing round-trips and the code -> value mapping stays within its error bound;
 //   4. the masked grouped GEMM's tile order covers every tile once and balances decode batches;
-//   5. the fused dispatch -> GEMM tile order covers every live tile once, level by level.
+//   5. the fused dispatch -> GEMM tile order covers every live tile once, level by level;
+//   6. the down projection -> combine index rules (csrc/include/ep/gemm_combine.cuh): over random
+//      routings of 1..8 ranks, every expert row lands in exactly one slot of its token's source rank,
+//      and the source's reduction over its own routing equals the direct top-k weighted sum.
 // Prints "ALL OK" and exits 0 on success.
 #include <algorithm>
 #include <cmath>
@@ -17,6 +20,7 @@
 #include <random>
 #include <vector>
 
+#include "../../deepep_slingshot_b200/csrc/include/ep/gemm_combine.cuh"
 #include "../../deepep_slingshot_b200/csrc/include/ep/logfmt.cuh"
 #include "../../deepep_slingshot_b200/csrc/include/ep/schedule.cuh"
 
@@ -271,11 +275,129 @@ static void check_fused_tiles(std::mt19937& rng) {
     CHECK(ep::fused_gemm_levels(too_many, 2, order, prefix, 3, hist) == -1, "overflow not reported");
 }
 
+// Down projection -> combine. Dispatch semantics as the library's: receiver r gets, in source-rank
+// order and token order, every token with at least one expert on r; its routing row keeps the k
+// positions (local expert id, -1 elsewhere); the permute gives each (received token, k) with a local
+// expert one operand row of that expert's 128-aligned block. The receiver's GEMM output for a row is
+// modelled by a value that names (source, token, global expert); the row goes to the slot that the
+// same destination-word rule as the row-destination kernel gives.
+static double expert_value(int s, int t, int e) { return 1000.0 * s + t + 0.001 * e; }
+
+static void check_gemm_combine(std::mt19937& rng) {
+    for (int trial = 0; trial < 1500; ++trial) {
+        const int R = 1 + rng() % 8, E_l = 1 + rng() % 6, E = R * E_l, K = 1 + rng() % std::min(8, E);
+        std::vector<int> N(R);
+        std::vector<std::vector<int>> topk(R);      // [t * K + k] global expert or -1
+        std::vector<std::vector<double>> w(R);
+        for (int s = 0; s < R; ++s) {
+            N[s] = rng() % 4 == 0 ? 0 : (int)(rng() % 40);
+            topk[s].assign((size_t)N[s] * K, -1);
+            w[s].resize((size_t)N[s] * K);
+            for (int t = 0; t < N[s]; ++t) {
+                std::vector<int> perm(E);
+                for (int e = 0; e < E; ++e) perm[e] = e;
+                std::shuffle(perm.begin(), perm.end(), rng);
+                for (int k = 0; k < K; ++k) {
+                    topk[s][(size_t)t * K + k] = rng() % 5 == 0 ? -1 : perm[k];
+                    w[s][(size_t)t * K + k] = (double)(rng() % 1000) / 997.0;
+                }
+            }
+        }
+        // send[s][r] = tokens s sends to r; rank_prefix_matrix[s][r] = sum over s' <= s
+        std::vector<int> rpm((size_t)R * R, 0);
+        for (int r = 0; r < R; ++r) {
+            int acc = 0;
+            for (int s = 0; s < R; ++s) {
+                for (int t = 0; t < N[s]; ++t) {
+                    bool to_r = false;
+                    for (int k = 0; k < K; ++k) to_r |= topk[s][(size_t)t * K + k] >= 0 && topk[s][(size_t)t * K + k] / E_l == r;
+                    acc += to_r;
+                }
+                rpm[(size_t)s * R + r] = acc;
+            }
+        }
+        std::vector<std::vector<double>> slots(R);
+        std::vector<std::vector<int>> written(R);
+        for (int s = 0; s < R; ++s) {
+            slots[s].assign((size_t)N[s] * K, 0.0);
+            written[s].assign((size_t)N[s] * K, 0);
+        }
+        for (int r = 0; r < R; ++r) {
+            std::vector<int> src_idx, recv_topk;  // received tokens
+            for (int s = 0; s < R; ++s)
+                for (int t = 0; t < N[s]; ++t) {
+                    bool to_r = false;
+                    for (int k = 0; k < K; ++k) to_r |= topk[s][(size_t)t * K + k] >= 0 && topk[s][(size_t)t * K + k] / E_l == r;
+                    if (!to_r) continue;
+                    src_idx.push_back(t);
+                    for (int k = 0; k < K; ++k) {
+                        const int e = topk[s][(size_t)t * K + k];
+                        recv_topk.push_back(e >= 0 && e / E_l == r ? e % E_l : -1);
+                    }
+                }
+            const int num_recv = (int)src_idx.size();
+            CHECK(num_recv == rpm[(size_t)(R - 1) * R + r], "receive count");
+            // permute: 128-aligned blocks per local expert, rows in (token, k) order
+            std::vector<int> count(E_l, 0), offset(E_l + 1, 0);
+            for (int x : recv_topk)
+                if (x >= 0) ++count[x];
+            for (int e = 0; e < E_l; ++e) offset[e + 1] = offset[e] + (count[e] + 127) / 128 * 128;
+            const int rows = std::max(offset[E_l], 1);
+            std::vector<int> row_map((size_t)num_recv * K, -1), fill(E_l, 0);
+            for (int j = 0; j < num_recv; ++j)
+                for (int k = 0; k < K; ++k) {
+                    const int e = recv_topk[(size_t)j * K + k];
+                    if (e >= 0) row_map[(size_t)j * K + k] = offset[e] + fill[e]++;
+                }
+            // destination words (the row-destination kernel's rule) and the GEMM's rows
+            std::vector<int> prefix(R + 1, 0);
+            for (int s = 0; s < R; ++s) prefix[s + 1] = rpm[(size_t)s * R + r];
+            std::vector<int> dest(rows, -1);
+            std::vector<double> y(rows, 0.0);
+            for (int j = 0; j < num_recv; ++j)
+                for (int k = 0; k < K; ++k) {
+                    const int row = row_map[(size_t)j * K + k];
+                    if (row < 0) continue;
+                    const int s = ep::gc_source_of(prefix.data(), R, j);
+                    const int t = src_idx[j];
+                    dest[row] = ep::gc_encode(s, t, k, K);
+                    y[row] = expert_value(s, t, r * E_l + recv_topk[(size_t)j * K + k]);
+                }
+            // the epilogue: rows with a destination go to that slot, padding rows nowhere
+            for (int row = 0; row < rows; ++row) {
+                if (dest[row] < 0) continue;
+                const int s = ep::gc_rank_of(dest[row]), slot = ep::gc_slot_of(dest[row]);
+                CHECK(s >= 0 && s < R && slot >= 0 && slot < N[s] * K, "destination out of range");
+                CHECK(++written[s][slot] == 1, "slot written twice");
+                slots[s][slot] = y[row];
+            }
+        }
+        // source reduction over its own routing == direct top-k weighted sum
+        for (int s = 0; s < R; ++s)
+            for (int t = 0; t < N[s]; ++t) {
+                double got = 0.0, want = 0.0;
+                for (int k = 0; k < K; ++k) {
+                    const int e = topk[s][(size_t)t * K + k];
+                    const bool valid = e >= 0;
+                    CHECK(written[s][(size_t)t * K + k] == (valid ? 1 : 0), "slot (%d, %d) of rank %d written %d times",
+                          t, k, s, written[s][(size_t)t * K + k]);
+                    if (!valid) continue;
+                    got += w[s][(size_t)t * K + k] * slots[s][(size_t)t * K + k];
+                    want += w[s][(size_t)t * K + k] * expert_value(s, t, e);
+                }
+                CHECK(std::fabs(got - want) <= 1e-9 * (1.0 + std::fabs(want)), "reduction mismatch");
+            }
+    }
+    CHECK(ep::gc_rank_of(ep::gc_encode(7, (1 << 21) - 1, 7, 8)) == 7 && ep::gc_slot_of(ep::gc_encode(7, (1 << 21) - 1, 7, 8)) == (1 << 24) - 1,
+          "largest destination word");
+}
+
 int main() {
     std::mt19937 rng(12345);
     check_dealing(rng);
     check_masked_tiles(rng);
     check_fused_tiles(rng);
+    check_gemm_combine(rng);
     check_pp_ring(rng);
     check_logfmt(rng);
     std::printf("ALL OK\n");
