@@ -21,6 +21,12 @@ token's arrival counter; its reducers wait for the token's exact contribution co
 and reset the counter; the rank's last block then records its sequence number and releases it to
 every rank. Checked: every reduced row is the current combine's, every counter ends at zero, no
 deadlock; a variant without the destination wait is caught.
+
+The GEMM-combine model (the down projection whose epilogue stores into the sources' slots) runs
+epochs of send then reduce on every rank: the GEMM waits per destination for the release of the
+previous epoch, stores its rows and publishes its epoch; the source waits for every rank's epoch,
+reads its slots and releases them. Checked: every slot read holds the current epoch's row, no
+deadlock; a GEMM without the release wait is caught.
 """
 import random
 
@@ -292,3 +298,122 @@ def test_combine_model_detects_a_missing_ready_wait():
         assert bad > 0
     finally:
         combine_push_steps = original
+
+
+# ------------------------------------------------------------------------------------------------
+# Down projection -> combine (parallel/gemm_combine.py): every rank's GEMM stores rows into the
+# slots of the tokens' source ranks and publishes its epoch (gc_done); each source waits for every
+# rank's epoch, reduces its slots and releases them (gc_free); the next epoch's GEMM waits, per
+# destination, until that destination released the previous epoch.
+# ------------------------------------------------------------------------------------------------
+class GRank:
+    def __init__(self, world, tokens):
+        self.done = [0] * world       # done[s]: last epoch whose rows s stored into my slots (s writes)
+        self.free = [0] * world       # free[d]: last epoch d finished reducing (d writes)
+        self.slot = [[0] * tokens for _ in range(world)]  # slot[s][t]: epoch of the row s stored for my token t
+
+
+def gc_send_steps(G, me, e, routes):
+    """The GEMM of epoch e on rank `me`: waits for every destination's release of epoch e - 1, stores
+    its rows (destination, token) in any order, then the last CTA publishes e to every rank."""
+    world = len(G)
+    for d in range(world):
+        yield (lambda d=d: G[me].free[d] >= e - 1), (lambda: None)
+    for d, t in routes:
+        def store(d=d, t=t):
+            G[d].slot[me][t] = e
+        yield (lambda: True), store
+
+    def publish():
+        for d in range(world):
+            G[d].done[me] = e
+    yield (lambda: True), publish
+
+
+def gc_reduce_steps(G, me, e, expected, errors):
+    """The reduce of epoch e on rank `me`: waits for every rank's epoch, reads each expected slot,
+    then releases its slots to every rank."""
+    world = len(G)
+    for s in range(world):
+        yield (lambda s=s: G[me].done[s] >= e), (lambda: None)
+    for s, t in expected:
+        def read(s=s, t=t):
+            if G[me].slot[s][t] != e:
+                errors.append((me, s, t, e, G[me].slot[s][t]))
+        yield (lambda: True), read
+
+    def release():
+        for d in range(world):
+            G[d].free[me] = e
+    yield (lambda: True), release
+
+
+def run_gemm_combine(world, tokens, epochs, seed, send_steps=None):
+    send_steps = send_steps or gc_send_steps
+    rng = random.Random(seed)
+    G = [GRank(world, tokens) for _ in range(world)]
+    errors = []
+    plans = []  # plans[e-1][r]: (destination, token) rows rank r sends at epoch e
+    for _ in range(epochs):
+        routes = [[] for _ in range(world)]
+        for s in range(world):
+            for t in range(tokens):
+                for r in rng.sample(range(world), rng.randint(0, world)):
+                    routes[r].append((s, t))
+        for r in range(world):
+            rng.shuffle(routes[r])
+        plans.append(routes)
+    # per rank: a stream of operations send(1), reduce(1), send(2), ... each a generator
+    queues = []
+    for r in range(world):
+        q = []
+        for e in range(1, epochs + 1):
+            expected = [(s, t) for s in range(world) for (d, t) in plans[e - 1][s] if d == r]
+            q.append(('send', e, plans[e - 1][r]))
+            q.append(('reduce', e, expected))
+        queues.append(q)
+    current = [None] * world
+    for step in range(500000):
+        for r in range(world):
+            if current[r] is None and queues[r]:
+                kind, e, arg = queues[r].pop(0)
+                g = send_steps(G, r, e, arg) if kind == 'send' else gc_reduce_steps(G, r, e, arg, errors)
+                current[r] = [g, next(g)]
+        enabled = [r for r in range(world) if current[r] is not None and current[r][1][0]()]
+        if not enabled:
+            assert all(c is None for c in current) and not any(queues), f'deadlock at step {step}'
+            return errors, G
+        r = rng.choice(enabled)
+        g, st = current[r]
+        st[1]()
+        nxt = next(g, None)
+        current[r] = None if nxt is None else [g, nxt]
+    raise AssertionError('schedule did not finish')
+
+
+@pytest.mark.parametrize('seed', range(12))
+@pytest.mark.parametrize('world', [1, 2, 3, 4])
+def test_gemm_combine_protocol_epochs(seed, world):
+    errors, G = run_gemm_combine(world, tokens=3, epochs=5, seed=seed)
+    assert not errors, errors[:5]
+    assert all(x == 5 for g in G for x in g.done) and all(x == 5 for g in G for x in g.free)
+
+
+def test_gemm_combine_model_detects_a_missing_release_wait():
+    """Sanity check of the model: a GEMM that does not wait for the destinations' release of the
+    previous epoch overwrites slots a slow source has not reduced yet."""
+    def no_wait(G, me, e, routes):
+        for d, t in routes:
+            def store(d=d, t=t):
+                G[d].slot[me][t] = e
+            yield (lambda: True), store
+
+        def publish():
+            for d in range(len(G)):
+                G[d].done[me] = e
+        yield (lambda: True), publish
+    bad = 0
+    for seed in range(60):
+        errors, _ = run_gemm_combine(2, tokens=3, epochs=4, seed=seed, send_steps=no_wait)
+        bad += bool(errors)
+    assert bad > 0
