@@ -4,19 +4,22 @@
 // [DE]csrc/kernels/legacy/intranode.cu:25-1117, v2 [DE]deep_ep/include/deep_ep/impls/dispatch.cuh,
 // combine.cuh, combine_reduce_epilogue.cuh), re-designed for B200:
 //
-//  dispatch = count -> (stage || pull), two launches
+//  dispatch = (count || stage) -> pull: the count step on a second stream concurrent with the
+//  stage launch (default), or count -> pull with stage warps inside the pull launch
+//  (DEEPEP_B200_DISPATCH_STAGE=warps); a cached handle with the concurrent stage runs no count step
 //    * count  (up to 128 CTAs): waits until every receiver finished pulling the previous dispatch,
 //               then builds the ordered per-destination token lists and `send_head` from the routing
 //               alone (each CTA adds the per-destination counts its predecessors published) and the
 //               per-expert counts; its last CTA pushes the count row and the per-expert counts into
 //               every peer's control block, releases a flag, waits for every peer's flag and
 //               computes the receive layout (prefix matrices, aligned per-expert counts).
-//    * stage  (stage warps of the pull launch): each source writes one 16-byte-aligned RECORD per
-//               token into its own staging area (the row: bf16, or FP8 e4m3 with the 1x128
-//               quantization fused here; its fp32 block scales; its top-k ids/weights), in token
-//               order, and releases a staged flag per chunk of tokens in every receiver's control
-//               block. The quantization is thereby off the critical path: it overlaps the pulls.
-//    * pull   (pull pairs of the same launch): every receiver pulls the records it needs straight
+//    * stage  (its own launch, or stage warps of the pull launch): each source writes one
+//               16-byte-aligned RECORD per token into its own staging area (the row: bf16, or FP8
+//               e4m3 with the 1x128 quantization fused here; its fp32 block scales; its top-k
+//               ids/weights), in token order, and releases a staged flag per chunk of tokens in
+//               every receiver's control block. The quantization is thereby off the count step's
+//               critical path, and the pulls start on the first staged chunks.
+//    * pull   (pull pairs): every receiver pulls the records it needs straight
 //               out of the sources' staging with TMA bulk loads over NVLink (no multicast) into a
 //               shared-memory ring, in the wavefront order (at step k pair g takes the next row of
 //               source (k + g) % R, so all pairs walk every source's tokens in the order they are
@@ -243,7 +246,7 @@ void launch_dispatch_stage(const StageArgs& a_in, int max_sms, cudaStream_t stre
 // =================================================================================================
 // count: ordered per-destination lists + send_head + per-expert counts (all CTAs), then the count
 // exchange and the receive layout (last CTA). Only the routing is read, so this step does not wait
-// for the quantization; the staging itself overlaps the pulls (stage warps of the pull launch).
+// for the quantization; the staging runs concurrently (its own launch) or overlaps the pulls.
 // =================================================================================================
 __device__ __forceinline__ uint32_t token_rank_mask(const CountArgs& a, int t) {
     uint32_t m = 0;
