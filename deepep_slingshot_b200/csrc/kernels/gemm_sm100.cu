@@ -342,7 +342,12 @@ namespace {
 
 constexpr int kPBN = 256;                    // tile columns per pair
 constexpr int kPStageBytes = (kBM + 128) * kBK;  // own A rows + own half of B (32 KiB)
-constexpr int kPCols = kPBN / 4;             // accumulator columns per epilogue thread
+// Epilogue warps per CTA: 16 (a quarter of the columns each; the 18 warps put five on two SM
+// sub-partitions, a 96-register cap, so the promotion loads TMEM eight columns at a time and waits on
+// each) or 8 (half of the columns each; ten warps, at most three per sub-partition, a 168-register
+// cap that holds the pipelined promotion with the next load in flight).
+template <int kEpi>
+constexpr int kPColsT = kPBN / (kEpi / 4);  // accumulator columns per epilogue thread
 
 struct PairTile {
     int e, m0, n0, valid;  // expert, this CTA's first row, the pair's first column, rows to store
@@ -379,8 +384,12 @@ __device__ __forceinline__ void mma_f8_pair(uint32_t tmem_d, uint64_t a_desc, ui
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap map_a,
-                                                                          const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+template <int kEpi>
+__global__ void __launch_bounds__((2 + kEpi) * 32, 1) grouped_gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                                const __grid_constant__ CUtensorMap map_b,
+                                                                                GemmArgs a) {
+    static_assert(kEpi == 8 || kEpi == 16, "8 or 16 epilogue warps");
+    constexpr int kPCols = kPColsT<kEpi>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t s_full[kMaxGemmStages], s_empty[kMaxGemmStages];
     __shared__ __align__(8) uint64_t s_tfull[2], s_tempty[2];
@@ -403,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_pair_kernel(cons
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_tfull[b], 1);
-            mbar_init(&s_tempty[b], 2 * kEpiWarps);  // leader: the epilogue warps of both CTAs
+            mbar_init(&s_tempty[b], 2 * kEpi);  // leader: the epilogue warps of both CTAs
         }
         fence_mbar_init();
         int acc = 0;
@@ -510,13 +519,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_fp8_pair_kernel(cons
                 }
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kPBN + kPCols * h);
+                if constexpr (kEpi == 16) {
 #pragma unroll
-                for (int c = 0; c < kPCols; c += 8) {  // 8 staged values: the register budget of 18 warps
-                    float v[8];
-                    tc::tmem_ld_8(taddr + c, v);
-                    tc::tmem_wait_ld_8(v);
+                    for (int c = 0; c < kPCols; c += 8) {  // 8 staged values: the register budget of 18 warps
+                        float v[8];
+                        tc::tmem_ld_8(taddr + c, v);
+                        tc::tmem_wait_ld_8(v);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
+                        for (int i = 0; i < 8; ++i) acc[c + i] = fmaf(scale, v[i], acc[c + i]);
+                    }
+                } else {
+                    tc::tmem_promote<kPCols>(taddr, scale, acc);  // the next 8 columns in flight
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -822,15 +835,19 @@ int launch_tiles(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
-// CTA pairs: DEEPEP_B200_GEMM_PAIR=1 selects the cta_group::2 kernel (256 x 256 tiles) when n allows.
-bool use_pairs(int n) {
-    static const bool requested = [] {
+// CTA pairs: DEEPEP_B200_GEMM_PAIR=1 selects the cta_group::2 kernel (256 x 256 tiles) with 16
+// epilogue warps, =2 the one with 8 epilogue warps and the pipelined promotion, when n allows.
+int pair_epilogue_warps(int n) {
+    static const int requested = [] {
         const char* v = std::getenv("DEEPEP_B200_GEMM_PAIR");
-        return v != nullptr && std::string(v) == "1";
+        if (v == nullptr) return 0;
+        const std::string s(v);
+        return s == "1" ? 16 : s == "2" ? 8 : 0;
     }();
-    return requested && n % kPBN == 0;
+    return n % kPBN == 0 ? requested : 0;
 }
 
+template <int kEpi>
 int launch_pairs(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     GemmArgs a = args_in;
     CUtensorMap map_a, map_b;
@@ -841,11 +858,12 @@ int launch_pairs(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     if (a.stages > kMaxGemmStages) a.stages = kMaxGemmStages;
     if (a.stages > max_stages) a.stages = max_stages;
     const size_t smem = (size_t)a.stages * kPStageBytes + 1024;
-    if (cudaFuncSetAttribute(grouped_gemm_fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(grouped_gemm_fp8_pair_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
         return 3;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)std::max(2, num_sms / 2 * 2));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3((2 + kEpi) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -855,7 +873,7 @@ int launch_pairs(const GemmArgs& args_in, int num_sms, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, grouped_gemm_fp8_pair_kernel, map_a, map_b, a) == cudaSuccess ? 0 : 3;
+    return cudaLaunchKernelEx(&cfg, grouped_gemm_fp8_pair_kernel<kEpi>, map_a, map_b, a) == cudaSuccess ? 0 : 3;
 }
 
 }  // namespace
@@ -884,7 +902,9 @@ int launch_grouped_gemm_fp8(const GemmArgs& args_in, int num_sms, cudaStream_t s
         grouped_gemm_fp8_bs_kernel<<<num_sms, kBsThreads, smem, stream>>>(map_a, map_b, a);
         return cudaGetLastError() == cudaSuccess ? 0 : 3;
     }
-    if (use_pairs(args_in.n)) return launch_pairs(args_in, num_sms, stream);
+    const int pair_epi = pair_epilogue_warps(args_in.n);
+    if (pair_epi == 16) return launch_pairs<16>(args_in, num_sms, stream);
+    if (pair_epi == 8) return launch_pairs<8>(args_in, num_sms, stream);
     return tile_width(args_in.n) == 256 ? launch_tiles<256, false>(args_in, num_sms, stream)
                                         : launch_tiles<128, false>(args_in, num_sms, stream);
 }

@@ -38,7 +38,8 @@ SELECTION: Dict[str, str] = {
     'gc_row_dest_kernel': 'GemmCombine.send (destination of every operand row)',
     'gc_reduce_kernel': 'GemmCombine.reduce (source-side top-k weighted sum of the combine slots)',
     'grouped_gemm_fp8_bs_kernel': 'grouped_gemm_fp8(..., ue8m0=True) (power-of-two scales, block-scaled MMA)',
-    'grouped_gemm_fp8_pair_kernel': 'DEEPEP_B200_GEMM_PAIR=1 and N % 256 == 0 (CTA pairs, cta_group::2)',
+    'grouped_gemm_fp8_pair_kernel': 'N % 256 == 0 (CTA pairs, cta_group::2) and DEEPEP_B200_GEMM_PAIR=1 (<16>: 16 epilogue '
+                                    'warps) or =2 (<8>: 8 epilogue warps, pipelined promotion)',
     'grouped_gemm_bf16_kernel': '<A MN-major, B MN-major>: operand layouts of grouped_gemm_bf16 / _wgrad_rows',
     'masked_gemm_fp8_kernel': 'ops.gemm.masked_grouped_gemm_fp8, low_latency_dispatch_gemm, low_latency_gemm_combine',
     'fused_dispatch_gemm_kernel': 'Buffer.dispatch_gemm (DEEPEP_B200_MOE_FUSED_DISPATCH=1 in the MoE layer)',
