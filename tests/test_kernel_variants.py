@@ -46,7 +46,8 @@ def _global_kernels():
     names = set()
     for path in glob.glob(os.path.join(CSRC, '**', '*.cu'), recursive=True):
         src = open(path).read()
-        for m in re.finditer(r'__global__\s+(?:void\s+)?(?:__launch_bounds__\([^)]*\)\s+)?(?:void\s+)?(\w+)\s*\(', src):
+        # launch bounds may hold one level of parentheses: __launch_bounds__((2 + kEpi) * 32, 1)
+        for m in re.finditer(r'__global__\s+(?:void\s+)?(?:__launch_bounds__\((?:[^()]|\([^()]*\))*\)\s+)?(?:void\s+)?(\w+)\s*\(', src):
             names.add(m.group(1))
     return names
 
