@@ -41,8 +41,8 @@ def _body(rank, world, N, H, E, K):
     buf = Buffer(group, num_nvl_bytes=Buffer.get_nvl_buffer_size_hint(N, H, world), num_gpu_timeout_secs=20)
     gc = GemmCombine(group, N, K, H, timeout_secs=20)
     E_l = E // world
-    gw = torch.Generator().manual_seed(99 + rank)
-    wq, ws = quantize_weights_fp8((torch.randn((E_l, H, H), generator=gw) * 0.05).to(torch.bfloat16).cuda())
+    gw = torch.Generator(device='cuda').manual_seed(99 + rank)
+    wq, ws = quantize_weights_fp8((torch.randn((E_l, H, H), generator=gw, device='cuda') * 0.05).to(torch.bfloat16))
     ws = ws.contiguous()
     with pytest.raises(RuntimeError):
         gc.reduce(torch.zeros((4, K), dtype=torch.int64, device='cuda'))  # no send to reduce
@@ -87,8 +87,8 @@ def test_gemm_combine_matches_the_unfused_path(world):
 
 @pytest.mark.parametrize('world', _worlds())
 def test_gemm_combine_deepseek_shape(world):
-    """hidden 7168, 256 experts, top-8."""
-    run_ranks(_body, world, backend='nccl', args=(512, 7168, 256, 8))
+    """hidden 7168, top-8 (32 experts keep the square [experts, hidden, hidden] test weights small)."""
+    run_ranks(_body, world, backend='nccl', args=(512, 7168, 32, 8))
 
 
 def _moe_body(rank, world, N, H, I, E, K):
