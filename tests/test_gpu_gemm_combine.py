@@ -8,22 +8,16 @@ Compared, at every world size the box offers and over three back-to-back epochs 
   * the MoE layer forward and backward with `DEEPEP_B200_MOE_FUSED_COMBINE` against the unfused layer.
 The host-side ordering rules (reduce without a send, two sends without a reduce) raise on the host.
 
-These kernels have not run on a B200 yet: the file is collected and skipped until
-`DEEPEP_B200_TEST_NEW_KERNELS=1` is set for their first run.
+All of them passed at world 1 on their first B200 run; the multi-rank parametrisations need a box
+with more GPUs.
 """
-import os
-
 import pytest
 import torch
 import torch.distributed as dist
 
 from tests._dist import run_ranks
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get('DEEPEP_B200_TEST_NEW_KERNELS', '0') != '1',
-                       reason='first B200 run pending (set DEEPEP_B200_TEST_NEW_KERNELS=1)'),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _worlds():

@@ -3,8 +3,7 @@ DEEPEP_B200_GEMM_PAIR=1), against the fp32 oracle of `tests/test_gpu_gemm.py`: e
 number of 128-row m-tiles (the second CTA of the last pair computes rows it must not store), empty
 experts, partial tiles, and the DeepSeek-V3 shapes. The switch is read once per process, so the
 cases run in a child process. DEEPEP_B200_GEMM_PAIR=2 selects the variant with eight epilogue warps
-and the pipelined promotion; it has not run on a B200 yet, so its case is skipped until
-DEEPEP_B200_TEST_NEW_KERNELS=1.
+and the pipelined promotion.
 """
 import os
 import subprocess
@@ -27,11 +26,7 @@ print("PAIR OK")
 '''
 
 
-@pytest.mark.parametrize('variant', [
-    '1',
-    pytest.param('2', marks=pytest.mark.skipif(os.environ.get('DEEPEP_B200_TEST_NEW_KERNELS', '0') != '1',
-                                               reason='first B200 run pending (set DEEPEP_B200_TEST_NEW_KERNELS=1)')),
-])
+@pytest.mark.parametrize('variant', ['1', '2'])
 def test_grouped_gemm_fp8_cta_pairs(variant):
     env = dict(os.environ, DEEPEP_B200_GEMM_PAIR=variant, PYTHONPATH=ROOT)
     out = subprocess.run([sys.executable, '-c', _CHILD], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
