@@ -8,6 +8,7 @@
 
 #include "kernels/api.h"
 #include "runtime/buffer.hpp"
+#include "runtime/host_segment.hpp"
 #include "runtime/ops.hpp"
 #include "runtime/symmetric.hpp"
 
@@ -148,6 +149,16 @@ PYBIND11_MODULE(_C, m) {
         .def("engram_fetch", &ep::SymmetricRegion::engram_fetch)
         .def("gemm_combine_send", &ep::SymmetricRegion::gemm_combine_send)
         .def("gemm_combine_reduce", &ep::SymmetricRegion::gemm_combine_reduce);
+
+    py::class_<ep::HostSegment>(m, "HostSegment")
+        .def(py::init<const std::string&, int64_t, bool>())
+        .def("name", &ep::HostSegment::name)
+        .def("bytes", &ep::HostSegment::bytes)
+        .def("is_owner", &ep::HostSegment::is_owner)
+        .def("host_ptr", &ep::HostSegment::host_ptr)
+        .def("device_ptr", &ep::HostSegment::device_ptr)
+        .def("host_view", &ep::HostSegment::host_view)
+        .def("destroy", &ep::HostSegment::destroy);
 
     ep::register_ops(m);
 }

@@ -9,6 +9,7 @@
 #include "../kernels/api.h"
 #include "../kernels/permute.h"
 #include "../kernels/gemm.h"
+#include "../kernels/symmetric_ops.h"
 
 namespace ep {
 
@@ -360,9 +361,44 @@ void zero_group_padding(const std::vector<torch::Tensor>& tensors, const torch::
     launch_zero_group_padding(a, (int)counts.numel(), at::cuda::getCurrentCUDAStream());
 }
 
+// Engram rows from storage that lies at caller-given device addresses, one per rank (the elastic
+// API's hybrid mode: host segments registered with CUDA): out[t] = row (idx % entries_per_rank) of
+// rank idx / entries_per_rank; a bad index gives a zero row and reports kErrBounds. Same kernel as
+// the symmetric region's fetch.
+torch::Tensor engram_fetch_rows(const torch::Tensor& indices, const std::vector<int64_t>& bases, int64_t entries_per_rank,
+                                int64_t hidden, int num_sms, double timeout_s) {
+    TORCH_CHECK(indices.is_cuda() && indices.is_contiguous() && indices.dim() == 1 && indices.scalar_type() == torch::kInt32,
+                "engram indices: contiguous [num_tokens] int32 CUDA tensor");
+    TORCH_CHECK(!bases.empty() && (int)bases.size() <= kMaxRanks, "one storage address per rank (1..8)");
+    TORCH_CHECK(entries_per_rank > 0 && entries_per_rank * (int64_t)bases.size() < ((int64_t)1 << 31), "entries per rank");
+    TORCH_CHECK(hidden > 0 && (hidden * 2) % 16 == 0, "engram hidden * 2 bytes must be a multiple of 16");
+    for (int64_t b : bases) TORCH_CHECK(b != 0 && b % 16 == 0, "storage addresses must be 16-byte aligned");
+    auto out = torch::empty({indices.size(0), hidden}, indices.options().dtype(torch::kBFloat16));
+    EngramFetchArgs a{};
+    for (size_t r = 0; r < bases.size(); ++r) a.storage.base[r] = reinterpret_cast<void*>(bases[r]);
+    a.indices = indices.data_ptr<int>();
+    a.out = static_cast<uint8_t*>(out.data_ptr());
+    a.num_tokens = (int)indices.size(0);
+    a.entries_per_rank = (int)entries_per_rank;
+    a.row_bytes = (int)(hidden * 2);
+    a.num_ranks = (int)bases.size();
+    a.st = op_status(timeout_s);
+    if (num_sms <= 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    launch_engram_fetch(a, num_sms, at::cuda::getCurrentCUDAStream());
+    TORCH_CHECK(cudaGetLastError() == cudaSuccess, "engram_fetch_rows launch failed");
+    return out;
+}
+
 }  // namespace
 
 void register_ops(pybind11::module_& m) {
+    m.def("engram_fetch_rows", &engram_fetch_rows, pybind11::arg("indices"), pybind11::arg("bases"),
+          pybind11::arg("entries_per_rank"), pybind11::arg("hidden"), pybind11::arg("num_sms") = 0,
+          pybind11::arg("timeout_s") = 10.0);
     m.def("unpermute_backward", &unpermute_backward);
     m.def("swiglu_backward", &swiglu_backward);
     m.def("zero_group_padding", &zero_group_padding);

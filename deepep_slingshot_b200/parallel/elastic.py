@@ -106,6 +106,15 @@ class ElasticBuffer:
         self.explicitly_destroy = explicitly_destroy
         self._buffer = Buffer(group, num_nvl_bytes=num_bytes, num_rdma_bytes=0, explicitly_destroy=explicitly_destroy,
                               num_gpu_timeout_secs=num_gpu_timeout_secs)
+        # Hybrid CPU memory: one shared host segment per rank, mapped by every rank (Engram storage).
+        self.num_cpu_bytes = int(num_cpu_bytes) if allow_hybrid_mode else 0
+        self.num_gpu_timeout_secs = num_gpu_timeout_secs
+        self._host = None
+        if self.num_cpu_bytes > 0:
+            if self.num_cpu_bytes % self.get_elastic_buffer_alignment():
+                raise ValueError('num_cpu_bytes must be a multiple of get_elastic_buffer_alignment() (2 MiB)')
+            from .host_memory import HostSegments
+            self._host = HostSegments(group, self.num_cpu_bytes)
         self.runtime = self._buffer.runtime
         self.num_scaleout_ranks, self.num_scaleup_ranks = 1, self.num_ranks
         self.scaleout_rank_idx, self.scaleup_rank_idx = 0, self.rank_idx
@@ -118,6 +127,9 @@ class ElasticBuffer:
         for region in self.__dict__.get('_side_regions', {}).values():
             region.destroy()
         self.__dict__['_side_regions'] = {}
+        if getattr(self, '_host', None) is not None:
+            self._host.destroy()
+            self._host = None
         if self._buffer is not None:
             self._buffer.destroy()
             self._buffer = None
@@ -139,7 +151,8 @@ class ElasticBuffer:
     def get_engram_storage_size_hint(num_entries: int, hidden: int, num_max_tokens_per_rank: int,
                                      dtype: torch.dtype = torch.bfloat16) -> Tuple[int, int]:
         """(fetch receive bytes, storage bytes), each 2 MiB aligned. Rows are bf16 here; the fetched
-        rows land in a fresh tensor, the storage lives in GPU memory."""
+        rows land in a fresh tensor. The storage lives in a GPU region, or, with `num_cpu_bytes` set
+        to the storage bytes (hybrid mode), in each rank's shared host segment."""
         row = align(hidden * dtype.itemsize, 32)
         a = ElasticBuffer.get_elastic_buffer_alignment()
         return align(row * num_max_tokens_per_rank, a), align(64 * 1024 + row * num_entries, a)
@@ -347,17 +360,38 @@ class ElasticBuffer:
 
     def engram_write(self, storage: torch.Tensor) -> None:
         """(Experimental) Publish this rank's Engram storage `[num_entries, hidden]` bf16 (collective;
-        barriers before and after). Entry `i` of the group lives on rank `i // num_entries`."""
+        barriers before and after). Entry `i` of the group lives on rank `i // num_entries`. With
+        `num_cpu_bytes` (hybrid mode) the storage lives in this rank's shared host segment, as in
+        the reference; otherwise in a GPU region."""
         assert storage.dtype == torch.bfloat16 and storage.dim() == 2
         shapes = [None] * self.num_ranks
         dist.all_gather_object(shapes, tuple(storage.shape), self.group)
         assert all(s == shapes[0] for s in shapes), 'every rank must hold the same number of Engram entries'
+        if self._host is not None:
+            nbytes = storage.numel() * storage.element_size()
+            if nbytes > self.num_cpu_bytes:
+                raise ValueError(f'Engram storage of {nbytes} bytes exceeds num_cpu_bytes ({self.num_cpu_bytes})')
+            if (storage.shape[1] * 2) % 16:
+                raise ValueError('Engram hidden * 2 bytes must be a multiple of 16')
+            torch.cuda.synchronize()
+            dist.barrier(self.group)  # earlier fetches by peers have finished reading the old storage
+            self._host.view(self.rank_idx)[:nbytes].copy_(storage.contiguous().view(torch.uint8).flatten())
+            dist.barrier(self.group)  # every rank's storage is in place
+            self._engram_host = (int(storage.shape[0]), int(storage.shape[1]))
+            return
         self._engram = self._side_region('engram', storage.numel() * storage.element_size())
         self._engram.engram_write(storage.contiguous())
 
     def engram_fetch(self, indices: torch.Tensor, num_qps: int = 0):
-        """(Experimental) Fetch rows by global entry index (int32 `[num_tokens]`). The peer reads run on
-        the region's copy stream; the returned hook joins it and returns `[num_tokens, hidden]` bf16."""
+        """(Experimental) Fetch rows by global entry index (int32 `[num_tokens]`). GPU storage: the
+        peer reads run on the region's copy stream and the returned hook joins it. Host storage
+        (hybrid mode): the kernel reads the ranks' host segments on the current stream. The hook
+        returns `[num_tokens, hidden]` bf16."""
+        if getattr(self, '_engram_host', None) is not None:
+            entries, hidden = self._engram_host
+            out = require_ext().engram_fetch_rows(indices.to(torch.int32).contiguous(), self._host.device_ptrs(), entries,
+                                                  hidden, 0, float(self.num_gpu_timeout_secs))
+            return lambda: out
         assert getattr(self, '_engram', None) is not None, 'call engram_write first'
         return self._engram.engram_fetch(indices.to(torch.int32).contiguous(), 0)
 

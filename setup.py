@@ -24,6 +24,7 @@ SOURCES = [
     os.path.join(CSRC, "runtime", "buffer.cpp"),
     os.path.join(CSRC, "runtime", "ops.cpp"),
     os.path.join(CSRC, "runtime", "symmetric.cpp"),
+    os.path.join(CSRC, "runtime", "host_segment.cpp"),
     os.path.join(CSRC, "kernels", "intranode.cu"),
     os.path.join(CSRC, "kernels", "low_latency.cu"),
     os.path.join(CSRC, "kernels", "quant.cu"),
@@ -138,6 +139,7 @@ setup(
             sources=SOURCES,
             include_dirs=[os.path.join(ROOT, CSRC)],
             extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+            extra_link_args=["-lrt"],  # shm_open / shm_unlink (host segments)
         )
     ],
     cmdclass={"build_ext": BuildWithVariantTable.with_options(use_ninja=True)},
