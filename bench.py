@@ -391,8 +391,24 @@ def main():
         torch.cuda.synchronize()
         t_ns = max_over_ranks([a.elapsed_time(b) for a, b in t_ns])
         ms_ns = sum(t_ns) / len(t_ns)
+        # The CPU-synced dispatch timed the same way (dispatches back to back, no combine between
+        # them): against the step's dispatch interval it separates the host round trip itself from
+        # the coupling of the ranks' host loops through the combine.
+        dist.barrier()
+        t_sa = []
+        for i in range(args.steps):
+            flush.zero_()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            buf.dispatch(x, num_tokens_per_rank=ntpr, is_token_in_rank=itir, num_tokens_per_expert=ntpe, topk_idx=idx,
+                         topk_weights=w, config=cfg, quantize_fp8=True)
+            s1.record()
+            t_sa.append((s0, s1))
+        torch.cuda.synchronize()
+        t_sa = max_over_ranks([a.elapsed_time(b) for a, b in t_sa])
         nosync = {'dispatch_nosync_ms': ms_ns, 'dispatch_nosync_gbps_per_rank': disp_bytes / (ms_ns * 1e-3) / 1e9,
-                  'dispatch_nosync_note': 'num_worst_tokens = tokens x ranks: no CPU sync on the received counts'}
+                  'dispatch_nosync_note': 'num_worst_tokens = tokens x ranks: no CPU sync on the received counts',
+                  'dispatch_synced_alone_ms': sum(t_sa) / len(t_sa)}
 
     # ---------------------------------------------------------------- low-latency
     ll = {}
