@@ -28,6 +28,7 @@ struct StageArgs {
     int quantize;                // 1: fuse bf16 -> fp8 e4m3 1x128 quantization
     int round_scale;             // 1: power-of-two scales
     int tma_rows;                // 1 (set by the launcher): rows are TMA-loaded into shared memory before quantizing
+    int regs_rows;               // 1: the standalone stage quantizes rows through registers (no TMA row loads)
     int chunk;                   // overlapped stage: tokens per staged-chunk flag (same on every rank)
     // Standalone stage only: wait until every receiver pulled the previous dispatch (pull_done[r] >=
     // epoch - 1; with epoch 0, >= *dispatch_epoch read before the count step advances it).

@@ -230,7 +230,7 @@ void launch_dispatch_stage(const StageArgs& a_in, int max_sms, cudaStream_t stre
     size_t smem = 0;
     const size_t row_bytes = (size_t)a.hidden * 2;
     // TMA row loads: 8 row buffers per block (two blocks per SM up to hidden 7168), 16-byte aligned rows.
-    a.tma_rows = a.quantize && row_bytes % 16 == 0 && 8 * row_bytes <= 112 * 1024 &&
+    a.tma_rows = !a.regs_rows && a.quantize && row_bytes % 16 == 0 && 8 * row_bytes <= 112 * 1024 &&
                  reinterpret_cast<uintptr_t>(a.x) % 16 == 0;
     if (a.tma_rows) {
         smem = 8 * row_bytes;

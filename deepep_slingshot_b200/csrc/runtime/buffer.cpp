@@ -250,6 +250,10 @@ Buffer::Buffer(int rank, int num_ranks, int64_t num_nvl_bytes, int64_t num_rdma_
     stage_signal_gpu_scope_ = scope_env != nullptr && std::string(scope_env) == "gpu";
     const char* fence_env = std::getenv("DEEPEP_B200_STAGE_WRITER_FENCE");
     stage_writer_fence_ = fence_env == nullptr || std::string(fence_env) != "0";
+    // Row path of the standalone stage: "tma" (default: each warp TMA-loads a whole row into shared
+    // memory, then quantizes it) or "regs" (rows through registers, six column groups in flight).
+    const char* rows_env = std::getenv("DEEPEP_B200_STAGE_ROWS");
+    stage_regs_rows_ = rows_env != nullptr && std::string(rows_env) == "regs";
 
     num_nvl_bytes_ = align_up(num_nvl_bytes_, 2 << 20);
     EP_CUDA_CHECK(cudaMalloc(&nvl_base_, num_nvl_bytes_));
@@ -697,6 +701,7 @@ Buffer::intranode_dispatch(const torch::Tensor& x, const std::optional<torch::Te
     sa.record_stride = L.record_bytes;
     sa.epoch = ticket;
     sa.signal_gpu_scope = stage_signal_gpu_scope_ ? 1 : 0;
+    sa.regs_rows = stage_regs_rows_ ? 1 : 0;
     sa.writer_proxy_fence = stage_writer_fence_ ? 1 : 0;
     sa.rank = rank_;
     sa.peers = peers;

@@ -223,6 +223,7 @@ class Buffer {
     bool stage_concurrent_ = true;       // stage as its own launch next to the count step (else: stage warps of the pull)
     bool stage_signal_gpu_scope_ = false;  // chunk counters at GPU scope (DEEPEP_B200_STAGE_SIGNAL_SCOPE=gpu)
     bool stage_writer_fence_ = true;       // writer-side async-proxy fence (DEEPEP_B200_STAGE_WRITER_FENCE=0 drops it)
+    bool stage_regs_rows_ = false;         // stage rows through registers (DEEPEP_B200_STAGE_ROWS=regs)
     int dispatch_epoch_ = 0, combine_seq_ = 0, barrier_epoch_ = 0, ll_dispatch_seq_ = 0, ll_combine_seq_ = 0;
 };
 
