@@ -76,3 +76,17 @@ def test_fused_entry_points_exist():
     assert callable(MoEFFN.forward_low_latency) and callable(MoEFFN.quantized_weights)
     assert callable(gemm.masked_grouped_gemm_fp8) and callable(gemm.grouped_gemm_bf16_wgrad_rows)
     assert callable(quant.swiglu_quant)
+
+
+def test_gemm_combine_and_host_memory_entry_points():
+    from deepep_slingshot_b200._ext import require_ext
+    from deepep_slingshot_b200.models import MoEFFN
+    from deepep_slingshot_b200.parallel.gemm_combine import GemmCombine
+    from deepep_slingshot_b200.parallel.host_memory import HostSegments
+    _C = require_ext()
+    for name in ('gemm_combine_send', 'gemm_combine_reduce'):
+        assert callable(getattr(_C.SymmetricRegion, name))
+    assert callable(_C.engram_fetch_rows) and hasattr(_C, 'HostSegment')
+    assert callable(GemmCombine.send) and callable(GemmCombine.reduce) and callable(HostSegments.device_ptrs)
+    assert callable(MoEFFN.release)
+    assert GemmCombine.size_hint(4096, 8, 7168) == 4096 * 8 * 7168 * 2
