@@ -55,6 +55,12 @@ def summarize(rec: dict, peaks: Optional[dict] = None) -> List[str]:
             rows.append(f"| {k} per rank | {_fmt(v)} GB/s ({_fmt(rec.get(f'{k}_ms', 0) * 1e3)} µs) | "
                         f"{v / PUBLISHED[f'{k}_gbps_per_rank']:.2f} of published {PUBLISHED[f'{k}_gbps_per_rank']:.0f}; "
                         f"{v / NVLINK_GBPS:.2f} of the {NVLINK_GBPS:.0f} GB/s peer copy |")
+    if rec.get('dispatch_nosync_ms') is not None:
+        alone = rec.get('dispatch_synced_alone_ms')
+        rows.append(f"| dispatch host sync | step interval {_fmt(rec.get('dispatch_ms', 0) * 1e3)} µs"
+                    + (f", synced alone {_fmt(alone * 1e3)} µs" if alone is not None else '')
+                    + f", without the CPU sync {_fmt(rec['dispatch_nosync_ms'] * 1e3)} µs | "
+                    "the synced dispatch's host round trip and the coupling of the ranks' host loops |")
     for k in ('ll_dispatch_us', 'll_combine_us'):
         v = rec.get(k)
         if v is not None:

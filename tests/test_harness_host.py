@@ -267,6 +267,9 @@ def test_bench_report(tmp_path):
     assert 'HBM 13.7' in text and 'serial 39.8' in text and 'reasons: none' in text
     assert 'unavailable' in report.summarize(recs[2])[0]
     assert 'rank 2: 41932 expert rows' in '\n'.join(report.summarize(recs[1]))
+    sync = '\n'.join(report.summarize(dict(line1, n_gpus=2, dispatch_ms=0.694, dispatch_nosync_ms=0.149,
+                                            dispatch_synced_alone_ms=0.2)))
+    assert 'step interval 694.0 µs, synced alone 200.0 µs, without the CPU sync 149.0 µs' in sync
     sc = '\n'.join(report.scaling(recs))
     assert '| 8 | 4091.0 | 511.4 | 1.03 |' in sc
     assert report.main([str(f), '--peaks', str(tmp_path / 'missing.json')]) == 0
