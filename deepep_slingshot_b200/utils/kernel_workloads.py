@@ -13,7 +13,8 @@ grouped_gemm, grouped_gemm_ue8m0 (power-of-two scales, block-scaled MMA), swiglu
 bf16_gemm, bf16_mn, bf16_wgrad, fused_dispatch_gemm (standalone stage + count + fused receive/GEMM),
 moe_backward_ops (needs dispatch and grouped_gemm), transport_checks, ll_clean, side_features (PP,
 AGRS, Engram), gemm_combine (down projection whose epilogue sends into the combine slots, and the
-source-side reduce).
+source-side reduce), gemm_then_combine (the same down projection unfused: grouped GEMM, then the
+weighted expanded combine).
 The default set is every workload.
 
 Sizes default to inputs larger than L2 for the bandwidth-bound kernels while keeping the whole
@@ -126,7 +127,7 @@ def build(args):
 
     # down projection with the combine send as its epilogue, then the source-side reduce (its own
     # FP8 dispatch over 8 experts: square [8, hidden, hidden] weights stay under a GB)
-    def gemm_combine():
+    def gc_setup():
         if 'gc' not in state:
             from ..parallel.gemm_combine import GemmCombine
             e2 = 8
@@ -136,10 +137,19 @@ def build(args):
                                                           quantize_fp8=True)
             p2 = permute.permute(rx2, ri2, e2, alignment=128, probs=rw2, x_scales=rs2, zero_padding=True)
             wd, wds = gemm.quantize_weights_fp8((torch.randn((e2, H, H), device='cuda') * 0.02).to(torch.bfloat16))
-            state['gc'] = (GemmCombine(dist.group.WORLD, N, K, H), p2, wd, wds.contiguous(), h2, idx2, w2)
-        gc, p2, wd, wds, h2, idx2, w2 = state['gc']
+            state['gc'] = (GemmCombine(dist.group.WORLD, N, K, H), p2, wd, wds.contiguous(), h2, idx2, w2, rw2)
+        return state['gc']
+
+    def gemm_combine():
+        gc, p2, wd, wds, h2, idx2, w2, _ = gc_setup()
         gc.send(p2.x, p2.scales, wd, wds, p2.expert_offsets, p2.expert_counts, p2.row_map, h2, keep_local=False)
         gc.reduce(idx2, w2)
+
+    # the same down projection unfused: grouped GEMM, then the weighted expanded combine
+    def gemm_then_combine():
+        _, p2, wd, wds, h2, _, _, rw2 = gc_setup()
+        y2 = gemm.grouped_gemm_fp8(p2.x, p2.scales, wd, wds, p2.expert_offsets, p2.expert_counts)
+        buf.combine(y2, h2, row_map=p2.row_map, row_weights=rw2)
 
     def ll_logfmt():
         recv, cnt, hh, _, hook = buf.low_latency_dispatch(lx, lidx, T, E_ll, use_fp8=True, return_recv_hook=True)
@@ -232,7 +242,8 @@ def build(args):
                  'masked_gemm': masked_gemm, 'll_dispatch_gemm': ll_dispatch_gemm, 'bf16_gemm': bf16_gemm,
                  'bf16_mn': bf16_mn, 'bf16_wgrad': bf16_wgrad, 'fused_dispatch_gemm': fused_dispatch_gemm,
                  'moe_backward_ops': moe_backward_ops, 'transport_checks': transport_checks, 'll_clean': ll_clean,
-                 'side_features': side_features, 'gemm_combine': gemm_combine})
+                 'side_features': side_features, 'gemm_combine': gemm_combine,
+                 'gemm_then_combine': gemm_then_combine})
     return work
 
 
